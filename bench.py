@@ -1,0 +1,316 @@
+"""Benchmark of the WKV-7 + ROSA hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of the hot path over one batch of synthetic input.  The
+headline workload is the isolated WKV-7 scan op of benchmark config 2
+(B=8, T=2048, H=16, N=40, fp32, zero initial state, seeded N(0,1) inputs):
+each rank scans its own batch (weak scaling, no collective on the data path;
+NCCL only for the start/stop barrier and the max-over-ranks time).
+
+* ``value``   tokens/s over all ranks, inputs resident in HBM (device-timed).
+* ``e2e``     the same metric through the public API (``cuda_ops.rwkv7_cuda``)
+              with pinned HOST buffers: every step copies the inputs to the
+              device and y + final state back.
+* ``roofline``  the scan kernel's algorithmic bytes (6 inputs + y per (b,t,h):
+              7*N*4 B; plus the final state N*N*4 per (b,h)) over its measured
+              time, against the measured HBM copy bandwidth.
+* ``cpu_baseline``  the C restatement of the reference recurrence
+              (oracle/scans_ref.c, OpenMP over (b,h)) on this host's cores.
+
+``--impl reference`` times the reference algorithm's CPU implementation
+(the same C port; the reference itself is PyTorch CPU code that cannot be
+shipped to the GPU box) on rank 0 and prints its own line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B, T, H, N = 8, 2048, 16, 40
+TOKENS = B * T
+ALGO_BYTES = B * T * H * 7 * N * 4 + B * H * N * N * 4
+METRIC = "wkv7_scan_prefill_tokens_per_s"
+UNIT = "tokens/s"
+WORKLOAD = "config2_wkv7_scan_op_B8_T2048_H16_N40_fp32"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    return p.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the scan kernel from the committed ncu summary."""
+    f = ROOT / "profiles" / "wkv7_scan_config2.txt"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+def cpu_oracle_run(n_batch, seconds, threads=None):
+    from oracle import cref
+    from yufmusicgen_b200.workloads import wkv_op_inputs
+
+    ins = wkv_op_inputs(n_batch, T, H, N, seed=0)
+    args = [ins[k] for k in "rwkvab"]
+    cref.wkv7_scan(*args, n_threads=threads)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        cref.wkv7_scan(*args, n_threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return n_batch * T * reps / el, reps, el
+
+
+def run_reference(args):
+    rank, _, world = env_rank()
+    if rank != 0:
+        return
+    from oracle import cref
+
+    threads = cref.threads_default()
+    sample_b = 2
+    from yufmusicgen_b200.workloads import wkv_op_inputs
+
+    ins = wkv_op_inputs(sample_b, T, H, N, seed=0)
+    a = [ins[k] for k in "rwkvab"]
+    for _ in range(args.warmup):
+        cref.wkv7_scan(*a, n_threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cref.wkv7_scan(*a, n_threads=threads)
+    el = time.perf_counter() - t0
+    value = sample_b * T * args.steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "sample": f"B{sample_b} of B{B} per step"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample_b} of {B} sequences x T{T} x H{H} per step; C port of "
+                                   "RWKV7TimeMix._torch_recurrence, OpenMP over (b,h)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _time(fn, n, dev, stream, warm=3):
+    import torch
+
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / n
+
+
+def measure_extras(dev, stream, args):
+    """Secondary kernels of the hot path, timed on rank 0 (not the headline)."""
+    import torch
+
+    from yufmusicgen_b200 import cuda_ops, rosa_cuda
+    from yufmusicgen_b200.workloads import rosa_op_inputs, wkv_op_inputs
+
+    peak, _ = peaks()
+    out = {}
+    n = max(5, min(args.steps, 50))
+    # the sequential kernel on the headline workload, for comparison
+    ins = wkv_op_inputs(B, T, H, N, seed=0)
+    d = {k: torch.from_numpy(ins[k]).to(dev) for k in "rwkvab"}
+    y = torch.empty_like(d["r"])
+    s = torch.empty(B, H, N, N, device=dev)
+    ms = _time(lambda: cuda_ops.wkv7_forward(*(d[k] for k in "rwkvab"), None, out=y, state_out=s,
+                                             algo=cuda_ops.ALGO_SEQUENTIAL), n, dev, stream)
+    out["wkv7_sequential_config2"] = {"ms": ms, "GBps": ALGO_BYTES / ms / 1e6}
+    del d, y, s
+    # batched decode step: config-4 state shape (256 seqs x 16 heads x N40), T = 1
+    Bd = 256
+    di = wkv_op_inputs(Bd, 1, H, N, seed=1, with_state=True)
+    dd = {k: torch.from_numpy(di[k]).to(dev) for k in "rwkvab"}
+    st = torch.from_numpy(di["s0"]).to(dev)
+    yd = torch.empty_like(dd["r"])
+    ms = _time(lambda: cuda_ops.wkv7_forward(*(dd[k] for k in "rwkvab"), st, out=yd, state_out=st,
+                                             algo=cuda_ops.ALGO_SEQUENTIAL), n, dev, stream)
+    dbytes = 2 * Bd * H * N * N * 4 + 7 * Bd * H * N * 4
+    out["wkv7_decode_step_B256_H16_N40"] = {"ms": ms, "GBps": dbytes / ms / 1e6,
+                                            "frac_of_hbm": dbytes / ms / 1e6 / peak,
+                                            "bytes": dbytes}
+    # ROSA scan at the 0.1B model's shape (B2, T2048, R128), gated
+    ri = rosa_op_inputs(2, T, 128, seed=2)
+    keys = ("cand", "write", "read_gate", "decay", "direction", "m0")
+    rd = [torch.from_numpy(ri[k]).to(dev) for k in keys]
+    ro = torch.empty_like(rd[0])
+    mo = torch.empty_like(rd[5])
+    ms = _time(lambda: rosa_cuda.rosa_scan(*rd, gated=True, out=ro, memory_out=mo), n, dev, stream)
+    rbytes = 4 * 2 * T * 128 * 4
+    out["rosa_scan_B2_T2048_R128"] = {"ms": ms, "GBps": rbytes / ms / 1e6,
+                                      "tokens_per_s": 2 * T / (ms * 1e-3)}
+    return out
+
+
+def run_ours(args):
+    import torch
+
+    rank, local, world = env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = world > 1
+    if dist:
+        import datetime
+
+        import torch.distributed as tdist
+
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                 device_id=dev)
+    from yufmusicgen_b200 import cuda_ops
+    from yufmusicgen_b200.telemetry import ClockSampler
+    from yufmusicgen_b200.workloads import wkv_op_inputs
+
+    def barrier():
+        if dist:
+            torch.distributed.barrier()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    ins = wkv_op_inputs(B, T, H, N, seed=rank)
+    host = {k: torch.from_numpy(ins[k]).pin_memory() for k in "rwkvab"}
+    d = {k: host[k].to(dev) for k in "rwkvab"}
+    y = torch.empty_like(d["r"])
+    s = torch.empty(B, H, N, N, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        cuda_ops.wkv7_forward(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], None, out=y, state_out=s)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = max_over_ranks(ms)
+    value = world * TOKENS / (ms_max * 1e-3)
+
+    # End to end through the public API with pinned host buffers.
+    y_h = torch.empty(B, T, H, N).pin_memory()
+    s_h = torch.empty(B, H, N, N).pin_memory()
+
+    def e2e_step():
+        dd = [host[k].to(dev, non_blocking=True) for k in "rwkvab"]
+        yy, ss = cuda_ops.rwkv7_cuda(*dd)
+        y_h.copy_(yy, non_blocking=True)
+        s_h.copy_(ss, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 50))
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    h2d = sum(host[k].numel() * 4 for k in "rwkvab")
+    d2h = (y_h.numel() + s_h.numel()) * 4
+
+    extra = measure_extras(dev, stream, args) if rank == 0 else {}
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        achieved = ALGO_BYTES / (ms * 1e-3) / 1e9
+        traffic = profiled_traffic()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "per_gpu_batch": B, "seq_len": T, "heads": H,
+                       "head_size": N, "parallelism": f"batch-sharded x{world}, no collectives",
+                       "l2": "inputs larger than L2 (294 MB touched per step)"},
+            "e2e": {"value": world * TOKENS / (e2e_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "wkv7_scan_kernel<40>",
+                         "algorithmic_bytes_per_launch": ALGO_BYTES},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "extra": extra,
+        }
+        if world == 1:
+            v, reps, el = cpu_oracle_run(B, seconds=3.0)
+            from oracle import cref
+
+            line["cpu_baseline"] = {
+                "value": v, "unit": UNIT, "cores": cref.threads_default(), "kind": "port",
+                "sample": f"full config-2 workload x{reps} ({el:.1f} s); C port of the reference "
+                          "recurrence, OpenMP over (b,h)"}
+        print(json.dumps(line), flush=True)
+    if dist:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+"""Generate the golden fixtures from the reference implementation itself.
+
+Run in a container that holds the reference source tree (it is imported, not
+copied):
+
+    YUF_REFERENCE=/path/to/YufMusicGen python tests/golden/make_golden.py
+
+Every fixture is produced by the reference's own PyTorch fp32 CPU code:
+
+* ``RWKV7TimeMix._torch_recurrence``   (yufmusicgen/model.py:145-165)
+* ``ROSAMemory._reference_recurrence`` (yufmusicgen/model.py:260-288)
+* ``YufMusicGen.forward`` / ``.step``  (yufmusicgen/model.py:406-431) built with
+  ``use_cuda_kernel=False, use_rosa_scan=False`` and loaded with the seeded
+  weights of ``yufmusicgen_b200.weights.init_weights``.
+
+The fixtures are small ``.npz`` files; the GPU box never needs the reference.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO))
+REF = os.environ.get("YUF_REFERENCE")
+if not REF:
+    raise SystemExit("set YUF_REFERENCE to the reference source tree")
+sys.path.insert(0, REF)
+sys.dont_write_bytecode = True
+
+import torch  # noqa: E402
+from yufmusicgen.config import ModelConfig as RefConfig  # noqa: E402
+from yufmusicgen.model import ROSAMemory, RWKV7TimeMix, YufMusicGen  # noqa: E402
+
+from yufmusicgen_b200 import config as C  # noqa: E402
+from yufmusicgen_b200.weights import init_weights  # noqa: E402
+from yufmusicgen_b200.workloads import rosa_op_inputs, tiny_ids, wkv_op_inputs, zipf_ids  # noqa: E402
+
+torch.set_num_threads(max(1, os.cpu_count() or 1))
+
+
+def t(x):
+    return torch.from_numpy(np.ascontiguousarray(x))
+
+
+def wkv_cases():
+    out = {}
+    cases = [
+        ("n40_state", 2, 37, 3, 40, 11, True),
+        ("n32_zero", 1, 16, 2, 32, 12, False),
+        ("n64_state", 2, 9, 2, 64, 13, True),
+        ("n16_state", 3, 21, 2, 16, 14, True),
+        ("n40_t1", 4, 1, 5, 40, 15, True),
+    ]
+    for name, B, T, H, N, seed, st in cases:
+        ins = wkv_op_inputs(B, T, H, N, seed=seed, with_state=st)
+        s0 = ins["s0"] if st else np.zeros((B, H, N, N), np.float32)
+        y, sT = RWKV7TimeMix._torch_recurrence(
+            t(ins["r"]), t(ins["w"]), t(ins["k"]), t(ins["v"]), t(ins["a"]), t(ins["b"]), t(s0)
+        )
+        for k in ("r", "w", "k", "v", "a", "b"):
+            out[f"{name}.{k}"] = ins[k]
+        out[f"{name}.s0"] = s0
+        out[f"{name}.y"] = y.numpy()
+        out[f"{name}.sT"] = sT.numpy()
+    np.savez_compressed(HERE / "wkv7_cases.npz", **out)
+
+
+def rosa_cases():
+    out = {}
+    cases = [
+        ("r32_state", 2, 29, 32, 21, True),
+        ("r128_zero", 2, 33, 128, 22, False),
+        ("r256_state", 1, 17, 256, 23, True),
+        ("r12_state", 3, 7, 12, 24, True),
+        ("r128_t1", 5, 1, 128, 25, True),
+    ]
+    for name, B, T, R, seed, st in cases:
+        ins = rosa_op_inputs(B, T, R, seed=seed, with_state=st)
+        read, mT = ROSAMemory._reference_recurrence(
+            t(ins["cand"]), t(ins["write"]), t(ins["read_gate"]), t(ins["decay"]),
+            t(ins["direction"]), t(ins["m0"]),
+        )
+        for k, v in ins.items():
+            out[f"{name}.{k}"] = v
+        out[f"{name}.read"] = read.numpy()
+        out[f"{name}.mT"] = mT.numpy()
+    np.savez_compressed(HERE / "rosa_cases.npz", **out)
+
+
+def ref_model(cfg_kwargs, weights):
+    cfg = RefConfig(**cfg_kwargs, use_cuda_kernel=False, use_rosa_scan=False)
+    model = YufMusicGen(cfg).eval()
+    model.load_state_dict({k: t(v) for k, v in weights.items()}, strict=True)
+    return model
+
+
+def greedy(model, prompt, n):
+    with torch.no_grad():
+        logits, st = model(t(prompt))
+        last = logits[:, -1]
+        toks, logs = [], []
+        for _ in range(n):
+            tok = torch.argmax(last, dim=-1)
+            toks.append(tok)
+            last, st = model.step(tok, st)
+            logs.append(last)
+    return torch.stack(toks, 1).numpy(), torch.stack(logs, 1).numpy()
+
+
+def model_case(name, cfg_kwargs, seed, recipe, ids, n_greedy, keep_positions=None, regions_T=0):
+    cfg = C.ModelConfig(**cfg_kwargs)
+    weights = init_weights(cfg, seed, recipe)
+    model = ref_model(cfg_kwargs, weights)
+    out = {"ids": ids}
+    with torch.no_grad():
+        logits, _ = model(t(ids))
+    logits = logits.numpy()
+    if keep_positions is None:
+        out["logits"] = logits
+    else:
+        out["positions"] = np.asarray(keep_positions, np.int64)
+        out["logits"] = logits[:, keep_positions]
+    if n_greedy:
+        toks, logs = greedy(model, ids, n_greedy)
+        out["greedy_tokens"] = toks
+        out["greedy_logits"] = logs
+    if regions_T:
+        # Per-layer regions of a short prefill, the region names of
+        # vulkan/scripts/dump_reference_step.py:186-322.
+        short = ids[:, :regions_T]
+        caps = {}
+        hooks = []
+        for li, blk in enumerate(model.blocks):
+            def tm_hook(mod, inp, outp, li=li):
+                caps[f"L{li}.tm_out"] = outp[0].detach().numpy()
+                caps[f"L{li}.S"] = outp[1].memory.detach().numpy()
+                caps[f"L{li}.prev"] = outp[1].previous.detach().numpy()
+            def ro_hook(mod, inp, outp, li=li):
+                caps[f"L{li}.rosa_out"] = outp[0].detach().numpy()
+                caps[f"L{li}.m"] = outp[1].detach().numpy()
+            def blk_hook(mod, inp, outp, li=li):
+                caps[f"L{li}.h3"] = outp[0].detach().numpy()
+            hooks.append(blk.time_mix.register_forward_hook(tm_hook))
+            hooks.append(blk.rosa.register_forward_hook(ro_hook))
+            hooks.append(blk.register_forward_hook(blk_hook))
+        with torch.no_grad():
+            lg, _ = model(t(short))
+        for h in hooks:
+            h.remove()
+        caps["logits"] = lg.numpy()
+        for k, v in caps.items():
+            out[f"regions.{k}"] = v
+        out["regions_T"] = np.int64(regions_T)
+    meta = dict(seed=seed, recipe=recipe, **cfg_kwargs)
+    out["meta_keys"] = np.array(list(meta.keys()))
+    out["meta_vals"] = np.array([str(v) for v in meta.values()])
+    np.savez_compressed(HERE / f"model_{name}.npz", **out)
+
+
+def state_test_case():
+    """The reference's own sequence-vs-step test (tests/test_model_state.py:9-28),
+    with the reference recurrence selected (use_rosa_scan=False)."""
+    torch.manual_seed(7)
+    cfg = RefConfig(**C.STATE_TEST, use_cuda_kernel=False, use_rosa_scan=False)
+    model = YufMusicGen(cfg).eval()
+    tokens = torch.randint(0, cfg.vocab_size, (1, 6))
+    with torch.no_grad():
+        full, _ = model(tokens)
+        st = None
+        steps = []
+        for i in range(tokens.shape[1]):
+            lg, st = model.step(tokens[:, i], st)
+            steps.append(lg)
+    sd = {k: v.numpy() for k, v in model.state_dict().items()}
+    np.savez_compressed(
+        HERE / "model_state_test.npz",
+        ids=tokens.numpy(), logits=full.numpy(), stepped=torch.stack(steps, 1).numpy(),
+        **{f"w.{k}": v for k, v in sd.items()},
+    )
+
+
+def main():
+    wkv_cases()
+    rosa_cases()
+    state_test_case()
+    model_case("tiny", C.TINY, seed=0, recipe="perturbed", ids=tiny_ids(2, 256, seed=0),
+               n_greedy=64, regions_T=16)
+    model_case("tiny_baseline", C.TINY, seed=0, recipe="baseline", ids=tiny_ids(2, 64, seed=3),
+               n_greedy=16)
+    ids3 = zipf_ids(1, 24, seed=1, vocab=20000, byte_prefix=8)
+    model_case("base0p1b", C.BASE_0P1B, seed=1, recipe="baseline", ids=ids3, n_greedy=8,
+               keep_positions=[0, 7, 8, 23])
+    c5 = dict(C.LONG_1K, n_layers=2)
+    ids5 = zipf_ids(1, 12, seed=2, vocab=20000, byte_prefix=0)
+    model_case("long1k_2l", c5, seed=2, recipe="perturbed", ids=ids5, n_greedy=4,
+               keep_positions=[0, 11])
+    print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,130 @@
+"""Pin the CPU oracle to the reference's own outputs (tests/golden/*.npz).
+
+The fixtures were produced by the reference's PyTorch fp32 CPU path
+(tests/golden/make_golden.py).  The oracle restates that path in numpy, so it
+must agree to float32 rounding (1e-5 here; the engine is held to 1e-3 / 1e-4
+against the oracle).
+"""
+
+import numpy as np
+import pytest
+
+from oracle.model import OracleModel
+from oracle.scans import rosa_scan, rosa_scan_ungated, wkv7_scan
+from yufmusicgen_b200 import config as C
+from yufmusicgen_b200.weights import init_weights
+
+WKV = ["n40_state", "n32_zero", "n64_state", "n16_state", "n40_t1"]
+ROSA = ["r32_state", "r128_zero", "r256_state", "r12_state", "r128_t1"]
+
+
+@pytest.mark.parametrize("case", WKV)
+def test_wkv7_oracle_matches_reference(golden, case):
+    g = golden("wkv7_cases.npz")
+    ins = [g[f"{case}.{k}"] for k in ("r", "w", "k", "v", "a", "b")]
+    y, sT = wkv7_scan(*ins, g[f"{case}.s0"])
+    np.testing.assert_allclose(y, g[f"{case}.y"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(sT, g[f"{case}.sT"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("case", ROSA)
+def test_rosa_oracle_matches_reference(golden, case):
+    g = golden("rosa_cases.npz")
+    args = [g[f"{case}.{k}"] for k in ("cand", "write", "read_gate", "decay", "direction", "m0")]
+    read, mT = rosa_scan(*args)
+    np.testing.assert_allclose(read, g[f"{case}.read"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(mT, g[f"{case}.mT"], rtol=1e-5, atol=1e-6)
+    # The CUDA-op contract returns the ungated read (rosa_householder.cu:89-91).
+    ung, mT2 = rosa_scan_ungated(*args)
+    gate = 1.0 / (1.0 + np.exp(-g[f"{case}.read_gate"]))
+    np.testing.assert_allclose(ung * gate, g[f"{case}.read"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_array_equal(mT2, mT)
+
+
+def _model_from_golden(g, name_cfg, seed, recipe):
+    cfg = C.ModelConfig(**name_cfg)
+    return cfg, OracleModel(cfg, init_weights(cfg, seed, recipe))
+
+
+def _meta(g):
+    return dict(zip(g["meta_keys"].tolist(), g["meta_vals"].tolist()))
+
+
+@pytest.mark.parametrize(
+    "fixture,cfgd,seed,recipe",
+    [
+        ("model_tiny.npz", C.TINY, 0, "perturbed"),
+        ("model_tiny_baseline.npz", C.TINY, 0, "baseline"),
+        ("model_base0p1b.npz", C.BASE_0P1B, 1, "baseline"),
+        ("model_long1k_2l.npz", dict(C.LONG_1K, n_layers=2), 2, "perturbed"),
+    ],
+)
+def test_model_oracle_matches_reference(golden, fixture, cfgd, seed, recipe):
+    g = golden(fixture)
+    meta = _meta(g)
+    assert meta["recipe"] == recipe and int(meta["seed"]) == seed
+    cfg, om = _model_from_golden(g, cfgd, seed, recipe)
+    logits, _ = om.forward(g["ids"])
+    if "positions" in g:
+        logits = logits[:, g["positions"]]
+    np.testing.assert_allclose(logits, g["logits"], rtol=1e-4, atol=2e-5)
+    if "greedy_tokens" in g:
+        n = g["greedy_tokens"].shape[1]
+        toks, logs = om.greedy(g["ids"], n)
+        np.testing.assert_array_equal(toks, g["greedy_tokens"])
+        np.testing.assert_allclose(logs, g["greedy_logits"], rtol=1e-4, atol=2e-5)
+
+
+def test_model_regions_match_reference(golden):
+    g = golden("model_tiny.npz")
+    cfg, om = _model_from_golden(g, C.TINY, 0, "perturbed")
+    T = int(g["regions_T"])
+    regions = {}
+    logits, st = om.forward(g["ids"][:, :T], regions=regions)
+    np.testing.assert_allclose(logits, g["regions.logits"], rtol=1e-4, atol=2e-5)
+    for li in range(cfg.n_layers):
+        R = regions[li]
+        np.testing.assert_allclose(R["h3"], g[f"regions.L{li}.h3"], rtol=1e-4, atol=2e-5)
+        np.testing.assert_allclose(R["o"], g[f"regions.L{li}.tm_out"], rtol=1e-4, atol=2e-5)
+        np.testing.assert_allclose(st[li]["S"], g[f"regions.L{li}.S"], rtol=1e-4, atol=2e-5)
+        np.testing.assert_allclose(st[li]["prev"], g[f"regions.L{li}.prev"], rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(st[li]["m"], g[f"regions.L{li}.m"], rtol=1e-4, atol=2e-5)
+
+
+def test_reference_state_test_sequence_equals_step(golden):
+    """tests/test_model_state.py:9-28 of the reference, on its own weights."""
+    g = golden("model_state_test.npz")
+    cfg = C.ModelConfig(**C.STATE_TEST)
+    w = {k[2:]: v for k, v in g.items() if k.startswith("w.")}
+    om = OracleModel(cfg, w)
+    full, _ = om.forward(g["ids"])
+    np.testing.assert_allclose(full, g["logits"], rtol=1e-5, atol=1e-5)
+    st = None
+    steps = []
+    for i in range(g["ids"].shape[1]):
+        lg, st = om.step(g["ids"][:, i], st if st is not None else om.initial_state(1))
+        steps.append(lg)
+    np.testing.assert_allclose(np.stack(steps, 1), g["stepped"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(np.stack(steps, 1), full, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("case", WKV)
+def test_c_oracle_wkv7_matches_reference(golden, case):
+    from oracle import cref
+
+    g = golden("wkv7_cases.npz")
+    ins = [g[f"{case}.{k}"] for k in ("r", "w", "k", "v", "a", "b")]
+    y, sT = cref.wkv7_scan(*ins, g[f"{case}.s0"])
+    np.testing.assert_allclose(y, g[f"{case}.y"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(sT, g[f"{case}.sT"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("case", ROSA)
+def test_c_oracle_rosa_matches_reference(golden, case):
+    from oracle import cref
+
+    g = golden("rosa_cases.npz")
+    args = [g[f"{case}.{k}"] for k in ("cand", "write", "read_gate", "decay", "direction", "m0")]
+    read, mT = cref.rosa_scan(*args)
+    np.testing.assert_allclose(read, g[f"{case}.read"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(mT, g[f"{case}.mT"], rtol=1e-5, atol=1e-6)

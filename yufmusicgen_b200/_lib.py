@@ -1,0 +1,80 @@
+"""ctypes binding of ``libyufb200.so`` (the C ABI in ``include/yufb200.h``).
+
+The library is built in-tree by ``yufmusicgen_b200.build``.  There is no CPU
+fallback: if the library is missing or a call fails, the error is raised.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libyufb200.so"
+
+_lock = threading.Lock()
+_lib = None
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+
+# name -> argtypes (restype is always int: yuf_status_t)
+SIGNATURES = {
+    "yuf_wkv7_forward": [P] * 9 + [I] * 4 + [P],
+    "yuf_wkv7_forward_ex": [P] * 9 + [I] * 5 + [P],
+    "yuf_wkv7_forward_compat": [P] * 9 + [I] * 4 + [P],
+    "yuf_rosa_forward": [P] * 8 + [I] * 4 + [P],
+    "yuf_rosa_forward_compat": [P] * 14 + [I] * 3 + [P],
+}
+
+
+class YufError(RuntimeError):
+    """A C-ABI call returned a non-OK status."""
+
+    def __init__(self, func: str, status: int, message: str):
+        self.status = status
+        super().__init__(f"{func} failed with {status_name(status)}: {message}")
+
+
+def load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m yufmusicgen_b200.build` "
+                "(this package has no CPU fallback)"
+            )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        lib.yuf_status_string.restype = ctypes.c_char_p
+        lib.yuf_status_string.argtypes = [I]
+        lib.yuf_last_error.restype = ctypes.c_char_p
+        lib.yuf_last_error.argtypes = []
+        lib.yuf_abi_version.restype = I
+        for name, args in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = I
+        _lib = lib
+        return lib
+
+
+def status_name(status: int) -> str:
+    return load().yuf_status_string(status).decode()
+
+
+def call(name: str, *args) -> None:
+    lib = load()
+    st = getattr(lib, name)(*args)
+    if st != 0:
+        raise YufError(name, st, lib.yuf_last_error().decode())
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a torch tensor (None for None)."""
+    if t is None:
+        return None
+    return t.data_ptr()

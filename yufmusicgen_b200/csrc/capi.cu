@@ -1,0 +1,167 @@
+// C ABI of the scan kernels: host-side validation, then dispatch on the
+// caller's stream.  No entry point throws; failures return a status and leave
+// a message for yuf_last_error().
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace yuf {
+
+static thread_local char g_err[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+yuf_status_t check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s: launch failed: %s", what, cudaGetErrorString(e));
+    return YUF_ERR_CUDA;
+  }
+  return YUF_OK;
+}
+
+yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const float* v,
+                           const float* a, const float* b, const float* s0, float* y, float* s_out,
+                           float* ckpt, float* sa, int B, int T, int H, int N, bool compat,
+                           cudaStream_t stream);
+yuf_status_t wkv7_chunk_dispatch(const float* r, const float* w, const float* k, const float* v,
+                                 const float* a, const float* b, const float* s0, float* y,
+                                 float* s_out, int B, int T, int H, int N, cudaStream_t stream);
+yuf_status_t rosa_dispatch(const float* cand, const float* write, const float* gate,
+                           const float* decay, const float* dir, const float* m0, float* read,
+                           float* m_out, int B, int T, int R, bool gated, cudaStream_t stream);
+yuf_status_t rosa_compat_dispatch(const float* cand, const float* write, const float* gate,
+                                  const float* decay, const float* dir, const float* m0, float* read,
+                                  float* m_out, float* cs, float* ws, float* rs, float* gs, float* ds,
+                                  float* ms, int B, int T, int R, cudaStream_t stream);
+
+static bool aligned(const void* p, size_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+#define REQUIRE(cond, ...)                  \
+  do {                                      \
+    if (!(cond)) {                          \
+      set_error(__VA_ARGS__);               \
+      return YUF_ERR_INVALID_ARGUMENT;      \
+    }                                       \
+  } while (0)
+
+static yuf_status_t check_wkv_args(const float* const* in, int n_in, int B, int T, int H, int N) {
+  REQUIRE(B >= 0 && T >= 0 && H >= 0 && N > 0, "wkv7: negative or zero size (B=%d T=%d H=%d N=%d)",
+          B, T, H, N);
+  const long long elems = (long long)B * T * H * N;
+  REQUIRE(elems < (1LL << 40), "wkv7: tensor too large");
+  for (int i = 0; i < n_in; ++i) {
+    REQUIRE(elems == 0 || in[i] != nullptr, "wkv7: input %d is NULL", i);
+    REQUIRE(aligned(in[i], 16), "wkv7: input %d is not 16-byte aligned", i);
+  }
+  return YUF_OK;
+}
+
+}  // namespace yuf
+
+using namespace yuf;
+
+extern "C" {
+
+const char* yuf_status_string(yuf_status_t s) {
+  switch (s) {
+    case YUF_OK: return "YUF_OK";
+    case YUF_ERR_INVALID_ARGUMENT: return "YUF_ERR_INVALID_ARGUMENT";
+    case YUF_ERR_UNSUPPORTED: return "YUF_ERR_UNSUPPORTED";
+    case YUF_ERR_CUDA: return "YUF_ERR_CUDA";
+    case YUF_ERR_OUT_OF_MEMORY: return "YUF_ERR_OUT_OF_MEMORY";
+    case YUF_ERR_IO: return "YUF_ERR_IO";
+    case YUF_ERR_TIMEOUT: return "YUF_ERR_TIMEOUT";
+  }
+  return "YUF_ERR_UNKNOWN";
+}
+
+const char* yuf_last_error(void) { return g_err; }
+
+int yuf_abi_version(void) { return 1; }
+
+yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k, const float* v,
+                                 const float* a, const float* b, const float* s0, float* y,
+                                 float* s_out, int B, int T, int H, int N, int algo,
+                                 void* stream) {
+  g_err[0] = 0;
+  const float* in[7] = {r, w, k, v, a, b, y};
+  yuf_status_t st = check_wkv_args(in, 7, B, T, H, N);
+  if (st != YUF_OK) return st;
+  REQUIRE(aligned(s0, 8) && aligned(s_out, 8), "wkv7: state buffers must be 8-byte aligned");
+  REQUIRE(algo >= YUF_WKV_AUTO && algo <= YUF_WKV_CHUNKED, "wkv7: unknown algorithm %d", algo);
+  if (B == 0 || H == 0) return YUF_OK;
+  const bool chunked = algo == YUF_WKV_CHUNKED || (algo == YUF_WKV_AUTO && T >= 16);
+  if (chunked)
+    return wkv7_chunk_dispatch(r, w, k, v, a, b, s0, y, s_out, B, T, H, N,
+                               static_cast<cudaStream_t>(stream));
+  return wkv7_dispatch(r, w, k, v, a, b, s0, y, s_out, nullptr, nullptr, B, T, H, N, false,
+                       static_cast<cudaStream_t>(stream));
+}
+
+yuf_status_t yuf_wkv7_forward(const float* r, const float* w, const float* k, const float* v,
+                              const float* a, const float* b, const float* s0, float* y,
+                              float* s_out, int B, int T, int H, int N, void* stream) {
+  return yuf_wkv7_forward_ex(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, YUF_WKV_AUTO, stream);
+}
+
+yuf_status_t yuf_wkv7_forward_compat(const float* r, const float* w, const float* k,
+                                     const float* v, const float* a, const float* b, float* y,
+                                     float* states, float* sa, int B, int T, int H, int N,
+                                     void* stream) {
+  g_err[0] = 0;
+  const float* in[7] = {r, w, k, v, a, b, y};
+  yuf_status_t st = check_wkv_args(in, 7, B, T, H, N);
+  if (st != YUF_OK) return st;
+  REQUIRE(T % 16 == 0, "wkv7 compat: T=%d must be a multiple of 16 (pad as cuda_ops.py does)", T);
+  REQUIRE(((long long)B * T * H * N == 0) || (states != nullptr && sa != nullptr),
+          "wkv7 compat: states and sa are required");
+  if (B == 0 || H == 0) return YUF_OK;
+  return wkv7_dispatch(r, w, k, v, a, b, nullptr, y, nullptr, states, sa, B, T, H, N, true,
+                       static_cast<cudaStream_t>(stream));
+}
+
+yuf_status_t yuf_rosa_forward(const float* cand, const float* write, const float* gate,
+                              const float* decay, const float* direction, const float* m0,
+                              float* read, float* m_out, int B, int T, int R, int gated,
+                              void* stream) {
+  g_err[0] = 0;
+  REQUIRE(B >= 0 && T >= 0, "rosa: negative size (B=%d T=%d)", B, T);
+  REQUIRE(R >= 1 && R <= 1024, "rosa: R=%d outside 1..1024", R);
+  REQUIRE(decay && direction && m0, "rosa: decay, direction and m0 are required");
+  REQUIRE((long long)B * T == 0 || (cand && write && read), "rosa: cand, write, read are required");
+  REQUIRE(!gated || (long long)B * T == 0 || gate, "rosa: gate is required when gated");
+  if (B == 0) return YUF_OK;
+  return rosa_dispatch(cand, write, gate, decay, direction, m0, read, m_out, B, T, R, gated != 0,
+                       static_cast<cudaStream_t>(stream));
+}
+
+yuf_status_t yuf_rosa_forward_compat(const float* cand, const float* write, const float* read_raw,
+                                     const float* decay, const float* direction,
+                                     const float* memory, float* read_out, float* memory_out,
+                                     float* cand_saved, float* write_saved, float* read_saved,
+                                     float* gate_saved, float* decay_saved, float* mem_saved,
+                                     int B, int T, int R, void* stream) {
+  g_err[0] = 0;
+  REQUIRE(B >= 0 && T >= 0, "rosa compat: negative size (B=%d T=%d)", B, T);
+  REQUIRE(R == 16 || R == 32 || R == 64 || R == 128 || R == 256,
+          "ROSA CUDA kernel supports D in {16, 32, 64, 128, 256}");
+  REQUIRE(decay && direction && memory && memory_out && mem_saved,
+          "rosa compat: decay, direction, memory, memory_out, mem_saved are required");
+  REQUIRE((long long)B * T == 0 || (cand && write && read_raw && read_out && cand_saved &&
+                                    write_saved && read_saved && gate_saved && decay_saved),
+          "rosa compat: a per-step tensor is NULL");
+  if (B == 0) return YUF_OK;
+  return rosa_compat_dispatch(cand, write, read_raw, decay, direction, memory, read_out, memory_out,
+                              cand_saved, write_saved, read_saved, gate_saved, decay_saved,
+                              mem_saved, B, T, R, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

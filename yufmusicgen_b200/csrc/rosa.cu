@@ -1,0 +1,218 @@
+// ROSA Householder-memory scan for sm_100a.
+//
+// Math (yufmusicgen/model.py:260-288; rosa_householder.cu:30-101), per batch
+// row, memory m in R^R, unit direction d, post-sigmoid decay D = diag(decay):
+//   p_t    = d . m_{t-1}
+//   m_t    = D (m_{t-1} - 2 p_t d) + u_t,        u_t = sigmoid(write_t) * tanh(cand_t)
+//   read_t = m_t - 2 (d . m_t) d  (= m_t - 2 p_{t+1} d), optionally * sigmoid(gate_t)
+//
+// The only coupling between channels is the scalar p_t.  Split m_t = e_t - 2 g_t
+// with the plain per-channel EMA e_t = D e_{t-1} + u_t (e_0 = m_0) and the
+// correction g_t = D (g_{t-1} + p_t d) (g_0 = 0).  Then
+//   p_t = d . e_{t-1} - 2 sum_{tau<t} c_{t-tau} p_tau,   c_k = sum_j d_j^2 decay_j^k,
+// a lower-triangular Toeplitz system whose matrix (I + 2C) is the same for every
+// chunk of L tokens, because D and d do not depend on the token.  Its inverse is
+// lower-triangular Toeplitz too (coefficients q_n, computed once per launch), so
+// within a chunk:
+//   1. each thread (one channel) runs its EMA over the chunk: no communication;
+//   2. ONE block reduction yields all L+1 dot products s_t = d . e_t at once;
+//   3. p_{t+1} = sum_tau q_{t-tau} s_tau (every thread, from shared memory);
+//   4. each thread forms g_t, m_t and read_t.
+// That replaces the reference's two block-wide O(R) dot products per token with
+// one batched reduction per 16 tokens.  One CTA per batch row, one thread per
+// channel; the next chunk's inputs are loaded into registers while the current
+// one is processed.
+
+#include "common.cuh"
+
+namespace yuf {
+
+constexpr int ROSA_L = 16;
+
+// Sum each of V per-thread values over the block; every thread receives all V
+// sums in out[] (shared).  scratch holds nwarps * V floats.
+template <int V>
+YUF_DEVICE void block_sum_array(const float (&x)[V], float* scratch, float* out, int nwarps) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    float s = x[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) scratch[warp * V + i] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < V) {
+    float s = 0.f;
+    for (int wi = 0; wi < nwarps; ++wi) s += scratch[wi * V + threadIdx.x];
+    out[threadIdx.x] = s;
+  }
+  __syncthreads();
+}
+
+template <bool GATED, bool COMPAT, int MAXT>
+__global__ void __launch_bounds__(MAXT)
+    rosa_scan_kernel(const float* __restrict__ cand, const float* __restrict__ write,
+                     const float* __restrict__ gate, const float* __restrict__ decay,
+                     const float* __restrict__ dir, const float* m0, float* __restrict__ read,
+                     float* m_out, float* __restrict__ cand_saved, float* __restrict__ write_saved,
+                     float* __restrict__ read_saved, float* __restrict__ gate_saved,
+                     float* __restrict__ decay_saved, float* __restrict__ mem_saved, int T, int R) {
+  constexpr int L = ROSA_L;
+  __shared__ float scratch[32 * (L + 1)];
+  __shared__ float s_sum[L + 1];
+  __shared__ float q[L + 1];
+  __shared__ float c_sum[L + 1];
+
+  const int bb = blockIdx.x;
+  const int j = threadIdx.x;
+  const int nwarps = blockDim.x >> 5;
+  const bool act = j < R;
+  const float d = act ? dir[j] : 0.f;
+  const float dec = act ? decay[j] : 0.f;
+
+  // c_k = sum_j d_j^2 decay_j^k, k = 1..L (index 0 unused).
+  {
+    float x[L + 1];
+    float pw = d * d;
+    x[0] = 0.f;
+#pragma unroll
+    for (int kk = 1; kk <= L; ++kk) {
+      pw *= dec;
+      x[kk] = pw;
+    }
+    block_sum_array<L + 1>(x, scratch, c_sum, nwarps);
+  }
+  // Inverse of the unit lower-triangular Toeplitz (I + 2C): q_0 = 1,
+  // q_n = -2 sum_{k=1..n} c_k q_{n-k}.
+  if (j == 0) {
+    q[0] = 1.f;
+    for (int n = 1; n <= L; ++n) {
+      float acc = 0.f;
+      for (int kk = 1; kk <= n; ++kk) acc += c_sum[kk] * q[n - kk];
+      q[n] = -2.f * acc;
+    }
+  }
+  __syncthreads();
+
+  float m = act ? m0[(size_t)bb * R + j] : 0.f;
+  const size_t base = (size_t)bb * T * R + j;
+  if (COMPAT && act) mem_saved[(size_t)bb * (T + 1) * R + j] = m;
+
+  float cc[L], ww[L], gg[L];
+  auto load = [&](int t0, float (&c_)[L], float (&w_)[L], float (&g_)[L]) {
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      const bool ok = act && (t0 + t < T);
+      const size_t o = base + (size_t)(t0 + t) * R;
+      c_[t] = ok ? cand[o] : 0.f;
+      w_[t] = ok ? write[o] : 0.f;
+      g_[t] = (ok && (GATED || COMPAT)) ? gate[o] : 0.f;
+    }
+  };
+  if (T > 0) load(0, cc, ww, gg);
+
+  for (int t0 = 0; t0 < T; t0 += L) {
+    const int Lc = min(L, T - t0);
+    float u[L];
+#pragma unroll
+    for (int t = 0; t < L; ++t) u[t] = sigmoidf_fast(ww[t]) * tanhf(cc[t]);
+    float gcur[L];
+#pragma unroll
+    for (int t = 0; t < L; ++t) gcur[t] = gg[t];
+    float ccur[L], wcur[L];
+    if constexpr (COMPAT) {
+#pragma unroll
+      for (int t = 0; t < L; ++t) {
+        ccur[t] = cc[t];
+        wcur[t] = ww[t];
+      }
+    }
+    if (t0 + L < T) load(t0 + L, cc, ww, gg);  // prefetch the next chunk
+
+    // 1. per-channel EMA from the true chunk-start memory.
+    float e[L + 1], x[L + 1];
+    e[0] = m;
+    x[0] = d * m;
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      e[t + 1] = (t < Lc) ? fmaf(dec, e[t], u[t]) : e[t];
+      x[t + 1] = d * e[t + 1];
+    }
+    // 2. all L+1 projections s_t = d . e_t in one block reduction.
+    block_sum_array<L + 1>(x, scratch, s_sum, nwarps);
+    // 3. p_{t+1} = sum_{tau <= t} q_{t-tau} s_tau  (p index shifted by one).
+    float p[L + 1];
+#pragma unroll
+    for (int t = 0; t <= L; ++t) {
+      float acc = 0.f;
+#pragma unroll
+      for (int tau = 0; tau <= t; ++tau) acc = fmaf(q[t - tau], s_sum[tau], acc);
+      p[t] = acc;
+    }
+    // 4. correction, memory and read.
+    float gc = 0.f;
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      if (t < Lc) {
+        gc = dec * fmaf(p[t], d, gc);
+        const float mt = fmaf(-2.f, gc, e[t + 1]);
+        const float rd = fmaf(-2.f * p[t + 1], d, mt);
+        if (act) {
+          const size_t o = base + (size_t)(t0 + t) * R;
+          if constexpr (COMPAT) {
+            read[o] = rd;
+            read_saved[o] = rd;
+            cand_saved[o] = tanhf(ccur[t]);
+            write_saved[o] = sigmoidf_fast(wcur[t]);
+            gate_saved[o] = sigmoidf_fast(gcur[t]);
+            decay_saved[o] = dec;
+            mem_saved[(size_t)bb * (T + 1) * R + (size_t)(t0 + t + 1) * R + j] = mt;
+          } else if constexpr (GATED) {
+            read[o] = rd * sigmoidf_fast(gcur[t]);
+          } else {
+            read[o] = rd;
+          }
+        }
+        if (t == Lc - 1) m = mt;
+      }
+    }
+    __syncthreads();  // s_sum / scratch are rewritten by the next chunk
+  }
+  if (act && m_out != nullptr) m_out[(size_t)bb * R + j] = m;
+}
+
+template <bool GATED, bool COMPAT>
+static yuf_status_t launch_rosa(const float* cand, const float* write, const float* gate,
+                                const float* decay, const float* dir, const float* m0, float* read,
+                                float* m_out, float* cs, float* ws, float* rs, float* gs, float* ds,
+                                float* ms, int B, int T, int R, cudaStream_t stream) {
+  const int threads = ((R + 31) / 32) * 32;
+  if (threads <= 256)
+    rosa_scan_kernel<GATED, COMPAT, 256><<<B, threads, 0, stream>>>(
+        cand, write, gate, decay, dir, m0, read, m_out, cs, ws, rs, gs, ds, ms, T, R);
+  else
+    rosa_scan_kernel<GATED, COMPAT, 1024><<<B, threads, 0, stream>>>(
+        cand, write, gate, decay, dir, m0, read, m_out, cs, ws, rs, gs, ds, ms, T, R);
+  return check_launch("rosa_scan_kernel");
+}
+
+yuf_status_t rosa_dispatch(const float* cand, const float* write, const float* gate,
+                           const float* decay, const float* dir, const float* m0, float* read,
+                           float* m_out, int B, int T, int R, bool gated, cudaStream_t stream) {
+  if (gated)
+    return launch_rosa<true, false>(cand, write, gate, decay, dir, m0, read, m_out, nullptr, nullptr,
+                                    nullptr, nullptr, nullptr, nullptr, B, T, R, stream);
+  return launch_rosa<false, false>(cand, write, gate, decay, dir, m0, read, m_out, nullptr, nullptr,
+                                   nullptr, nullptr, nullptr, nullptr, B, T, R, stream);
+}
+
+yuf_status_t rosa_compat_dispatch(const float* cand, const float* write, const float* gate,
+                                  const float* decay, const float* dir, const float* m0, float* read,
+                                  float* m_out, float* cs, float* ws, float* rs, float* gs, float* ds,
+                                  float* ms, int B, int T, int R, cudaStream_t stream) {
+  return launch_rosa<false, true>(cand, write, gate, decay, dir, m0, read, m_out, cs, ws, rs, gs, ds,
+                                  ms, B, T, R, stream);
+}
+
+}  // namespace yuf
