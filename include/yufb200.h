@@ -58,7 +58,7 @@ yuf_status_t yuf_wkv7_forward(const float* r, const float* w, const float* k, co
 
 /* Algorithm choice for yuf_wkv7_forward_ex. */
 enum {
-  YUF_WKV_AUTO = 0,       /* chunked for T >= 16, sequential below          */
+  YUF_WKV_AUTO = 0,       /* single-token kernel for T == 1, else sequential */
   YUF_WKV_SEQUENTIAL = 1, /* token-by-token (the decode step)                */
   YUF_WKV_CHUNKED = 2     /* 16-token chunks, no per-token reduction chain   */
 };
@@ -105,6 +105,70 @@ yuf_status_t yuf_rosa_forward_compat(const float* cand, const float* write, cons
                                      float* cand_saved, float* write_saved, float* read_saved,
                                      float* gate_saved, float* decay_saved, float* mem_saved,
                                      int B, int T, int R, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Model engine: the YufMusicGen block stack (yufmusicgen/model.py:345-445) on
+ * the GPU with device-resident recurrent state, the batched counterpart of the
+ * Vulkan engine's Model::new / Model::step / Model::reset_state
+ * (vulkan/src/compute/model.rs:24-65).
+ * ------------------------------------------------------------------------ */
+
+typedef struct yuf_model yuf_model; /* opaque */
+
+typedef struct yuf_model_config {
+  int vocab_size, d_model, n_layers, n_heads, head_size, rosa_size;
+  int low_rank; /* 0 = the reference rule max(32, round(2.5 sqrt(d) / 32) * 32), model.py:59 */
+} yuf_model_config;
+
+enum {
+  YUF_PRECISION_FP32 = 0,        /* fp32 weights; GEMMs with fp32 accuracy (BF16x9 emulation) */
+  YUF_PRECISION_BF16_WEIGHTS = 1 /* bf16 weights and GEMM inputs, fp32 accumulate and state */
+};
+
+/* Build a model on `device` from host fp32 tensors named as in the reference
+ * state_dict (e.g. "blocks.3.time_mix.key.weight"); `lm_head.weight` may be
+ * absent (tied to token_embedding.weight, model.py:389-391).  Every tensor the
+ * architecture needs must be present with its exact element count. */
+yuf_status_t yuf_model_create(const yuf_model_config* cfg, int precision, int device, int n_tensors,
+                              const char* const* names, const float* const* host_data,
+                              const int64_t* numels, yuf_model** out);
+/* Build a model from a .yuf checkpoint (vulkan/scripts/export_checkpoint.py). */
+yuf_status_t yuf_model_create_from_yuf(const char* path, int precision, int device, yuf_model** out);
+yuf_status_t yuf_model_destroy(yuf_model* model);
+yuf_status_t yuf_model_get_config(const yuf_model* model, yuf_model_config* out);
+
+/* Allocate `n_slots` recurrent-state slots (per layer: prev [d], S [H,N,N],
+ * m [R]) and zero them.  Replaces any previous slots. */
+yuf_status_t yuf_state_alloc(yuf_model* model, int n_slots);
+/* Zero slots [slot0, slot0 + n) on `stream` (Model::reset_state, model.rs:62-65). */
+yuf_status_t yuf_state_reset(yuf_model* model, int slot0, int n, void* stream);
+/* Copy slots [slot0, slot0 + n) of one layer to/from caller device buffers in
+ * the reference layout: prev [n,d], S [n,H,N,N] (row = value, col = key), m [n,R]. */
+yuf_status_t yuf_state_export(yuf_model* model, int layer, int slot0, int n, float* prev, float* S,
+                              float* m, void* stream);
+yuf_status_t yuf_state_import(yuf_model* model, int layer, int slot0, int n, const float* prev,
+                              const float* S, const float* m, void* stream);
+
+/* Prefill: run B sequences of T tokens (device int32 ids [B,T]) through the model
+ * starting from the state in slots [slot0, slot0 + B) and leave the final
+ * state there (YufMusicGen.forward(ids, state), model.py:406-422).
+ * logits_last [B,V] and/or logits_all [B,T,V] (device, either may be NULL). */
+yuf_status_t yuf_prefill(yuf_model* model, const int32_t* ids, int B, int T, int slot0,
+                         float* logits_last, float* logits_all, void* stream);
+/* Decode step: one token per sequence (device int32 ids [B]), slots
+ * [slot0, slot0 + B), logits [B,V] (YufMusicGen.step, model.py:424-431). */
+yuf_status_t yuf_step(yuf_model* model, const int32_t* ids, int B, int slot0, float* logits,
+                      void* stream);
+/* Synchronise `stream` and report device-side input errors of earlier calls
+ * (token id outside [0, vocab)). */
+yuf_status_t yuf_model_sync_check(yuf_model* model, void* stream);
+
+/* Parity dumps (the regions of vulkan/scripts/dump_reference_step.py:186-322).
+ * When enabled, every prefill/step keeps per-layer copies of: ln0, r, w, k, v,
+ * a, b, g, y, h1, read, h2, h3 and (layer -1) logits of the last call. */
+yuf_status_t yuf_model_set_debug(yuf_model* model, int enabled);
+yuf_status_t yuf_debug_dump(yuf_model* model, const char* region, int layer, float* host_out,
+                            size_t capacity, size_t* n_written);
 
 #ifdef __cplusplus
 }

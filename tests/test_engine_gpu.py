@@ -1,0 +1,189 @@
+"""Model engine parity on the GPU (prefill, batched decode, state, .yuf).
+
+fp32 tolerance: |got - want| <= 1e-3 + 1e-4 |want| (max-abs 1e-3 / rel 1e-4)
+against the reference's own outputs (tests/golden) or the numpy oracle.
+bf16-weight mode: |got - want| <= 0.15 + 0.05 |want| on the logits (stated
+tolerance for bf16 weights and GEMM inputs with fp32 accumulation and state).
+"""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+from oracle.model import OracleModel  # noqa: E402
+from yufmusicgen_b200 import config as C  # noqa: E402
+from yufmusicgen_b200.engine import Engine, Model  # noqa: E402
+from yufmusicgen_b200.weights import init_weights  # noqa: E402
+from yufmusicgen_b200.workloads import tiny_ids, zipf_ids  # noqa: E402
+from yufmusicgen_b200.yuf_format import write_yuf  # noqa: E402
+
+RTOL, ATOL = 1e-4, 1e-3
+BF_RTOL, BF_ATOL = 5e-2, 0.15
+
+
+def close(got, want, rtol=RTOL, atol=ATOL):
+    g = got.detach().cpu().numpy() if hasattr(got, "detach") else np.asarray(got)
+    np.testing.assert_allclose(g, want, rtol=rtol, atol=atol)
+
+
+def make(cfgd, seed, recipe, precision="fp32", n_slots=4):
+    cfg = C.ModelConfig(**cfgd)
+    w = init_weights(cfg, seed, recipe)
+    return cfg, w, Engine(cfg, w, precision=precision, n_slots=n_slots)
+
+
+def greedy(eng, prompt, n, slot0=0):
+    ids = torch.as_tensor(prompt, dtype=torch.int32, device="cuda")
+    last = eng.prefill(ids, slot0=slot0)
+    toks, logs = [], []
+    for _ in range(n):
+        tok = torch.argmax(last, dim=-1).to(torch.int32)
+        toks.append(tok)
+        last = eng.step(tok, slot0=slot0)
+        logs.append(last.clone())
+    return torch.stack(toks, 1).cpu().numpy(), torch.stack(logs, 1)
+
+
+@pytest.mark.parametrize("fixture,cfgd,seed,recipe", [
+    ("model_tiny.npz", C.TINY, 0, "perturbed"),
+    ("model_tiny_baseline.npz", C.TINY, 0, "baseline"),
+    ("model_base0p1b.npz", C.BASE_0P1B, 1, "baseline"),
+    ("model_long1k_2l.npz", dict(C.LONG_1K, n_layers=2), 2, "perturbed"),
+])
+def test_prefill_and_greedy_match_reference(golden, fixture, cfgd, seed, recipe):
+    g = golden(fixture)
+    cfg, w, eng = make(cfgd, seed, recipe)
+    ids = g["ids"]
+    _, allv = eng.prefill(torch.as_tensor(ids, dtype=torch.int32, device="cuda"), all_logits=True)
+    got = allv.cpu().numpy()
+    if "positions" in g:
+        got = got[:, g["positions"]]
+    close(got, g["logits"])
+    if "greedy_tokens" in g:
+        eng.reset_state()
+        n = g["greedy_tokens"].shape[1]
+        toks, logs = greedy(eng, ids, n)
+        np.testing.assert_array_equal(toks, g["greedy_tokens"])
+        close(logs, g["greedy_logits"])
+    eng.sync_check()
+    eng.close()
+
+
+def test_tiny_per_layer_regions_match_reference(golden):
+    g = golden("model_tiny.npz")
+    cfg, w, eng = make(C.TINY, 0, "perturbed")
+    T = int(g["regions_T"])
+    eng.set_debug(True)
+    logits = eng.prefill(torch.as_tensor(g["ids"][:, :T], dtype=torch.int32, device="cuda"))
+    close(logits, g["regions.logits"][:, -1])
+    B = g["ids"].shape[0]
+    for li in range(cfg.n_layers):
+        close(eng.debug_dump("h3", li).reshape(B, T, -1), g[f"regions.L{li}.h3"])
+        st = eng.export_state(li, 0, B)
+        close(st["S"], g[f"regions.L{li}.S"])
+        close(st["prev"], g[f"regions.L{li}.prev"])
+        close(st["m"], g[f"regions.L{li}.m"])
+    eng.close()
+
+
+def test_reference_state_test_sequence_equals_step(golden):
+    """tests/test_model_state.py:9-28 of the reference on the engine."""
+    g = golden("model_state_test.npz")
+    cfg = C.ModelConfig(**C.STATE_TEST)
+    w = {k[2:]: v for k, v in g.items() if k.startswith("w.")}
+    eng = Engine(cfg, w, n_slots=2)
+    ids = torch.as_tensor(g["ids"], dtype=torch.int32, device="cuda")
+    _, full = eng.prefill(ids, slot0=0, all_logits=True)
+    close(full, g["logits"])
+    steps = [eng.step(ids[:, i], slot0=1) for i in range(ids.shape[1])]
+    close(torch.stack(steps, 1), g["stepped"])
+    close(torch.stack(steps, 1), full.cpu().numpy(), rtol=1e-5, atol=1e-5)
+    eng.close()
+
+
+def test_batched_slots_are_independent():
+    cfg, w, eng = make(C.TINY, 0, "perturbed", n_slots=6)
+    ids = tiny_ids(2, 40, seed=7)
+    t = torch.as_tensor(ids, dtype=torch.int32, device="cuda")
+    both = eng.prefill(t, slot0=0)
+    a = eng.prefill(t[:1], slot0=2)
+    b = eng.prefill(t[1:], slot0=3)
+    close(both[0], a[0].cpu().numpy(), rtol=1e-6, atol=1e-6)
+    close(both[1], b[0].cpu().numpy(), rtol=1e-6, atol=1e-6)
+    # decode continues each slot from its own state
+    tok = torch.tensor([5, 300], dtype=torch.int32, device="cuda")
+    s2 = eng.step(tok, slot0=0)
+    sa = eng.step(tok[:1], slot0=2)
+    close(s2[0], sa[0].cpu().numpy(), rtol=1e-6, atol=1e-6)
+    eng.close()
+
+
+def test_chunked_prefill_equals_single_prefill():
+    """Prefill 100 tokens then 60 more == one 160-token prefill (state carried)."""
+    cfg, w, eng = make(C.TINY, 0, "perturbed", n_slots=2)
+    ids = torch.as_tensor(tiny_ids(1, 160, seed=9), dtype=torch.int32, device="cuda")
+    one = eng.prefill(ids, slot0=0)
+    eng.prefill(ids[:, :100], slot0=1)
+    two = eng.prefill(ids[:, 100:], slot0=1)
+    close(two, one.cpu().numpy(), rtol=1e-5, atol=1e-5)
+    eng.close()
+
+
+def test_base0p1b_longer_prefill_vs_oracle():
+    cfg = C.ModelConfig(**C.BASE_0P1B)
+    w = init_weights(cfg, 1, "baseline")
+    ids = zipf_ids(1, 80, seed=11, vocab=cfg.vocab_size, byte_prefix=16)
+    want, _ = OracleModel(cfg, w).forward(ids)
+    eng = Engine(cfg, w)
+    _, allv = eng.prefill(torch.as_tensor(ids, dtype=torch.int32, device="cuda"), all_logits=True)
+    close(allv, want)
+    eng.close()
+
+
+@pytest.mark.parametrize("fixture,cfgd,seed,recipe", [
+    ("model_tiny.npz", C.TINY, 0, "perturbed"),
+    ("model_base0p1b.npz", C.BASE_0P1B, 1, "baseline"),
+])
+def test_bf16_weights_within_stated_tolerance(golden, fixture, cfgd, seed, recipe):
+    g = golden(fixture)
+    cfg, w, eng = make(cfgd, seed, recipe, precision="bf16")
+    _, allv = eng.prefill(torch.as_tensor(g["ids"], dtype=torch.int32, device="cuda"), all_logits=True)
+    got = allv.cpu().numpy()
+    if "positions" in g:
+        got = got[:, g["positions"]]
+    close(got, g["logits"], rtol=BF_RTOL, atol=BF_ATOL)
+    eng.close()
+
+
+def test_yuf_checkpoint_roundtrip(tmp_path):
+    cfg, w, eng = make(C.TINY, 0, "perturbed")
+    path = tmp_path / "tiny.yuf"
+    write_yuf(path, cfg, w)
+    ids = torch.as_tensor(tiny_ids(2, 33, seed=4), dtype=torch.int32, device="cuda")
+    want = eng.prefill(ids).cpu().numpy()
+    m = Model.from_yuf(str(path))
+    assert m.config.d_model == cfg.d_model and m.engine.low_rank == cfg.low_rank
+    got = m.engine.prefill(ids[:1])
+    close(got[0], want[0], rtol=1e-6, atol=1e-6)
+    # Vulkan-style single-token API: step / reset_state
+    m.reset_state()
+    row = None
+    for tok in ids[0].tolist():
+        row = m.step(tok)
+    close(np.asarray(row), want[0], rtol=1e-5, atol=1e-5)
+    eng.close()
+    m.engine.close()
+
+
+def test_out_of_range_token_is_reported():
+    from yufmusicgen_b200._lib import YufError
+
+    cfg, w, eng = make(C.TINY, 0, "perturbed")
+    eng.step(torch.tensor([cfg.vocab_size + 5], dtype=torch.int32, device="cuda"))
+    with pytest.raises(YufError):
+        eng.sync_check()
+    eng.sync_check()  # cleared
+    eng.close()

@@ -25,7 +25,27 @@ SIGNATURES = {
     "yuf_wkv7_forward_compat": [P] * 9 + [I] * 4 + [P],
     "yuf_rosa_forward": [P] * 8 + [I] * 4 + [P],
     "yuf_rosa_forward_compat": [P] * 14 + [I] * 3 + [P],
+    "yuf_model_create": [P, I, I, I, P, P, P, P],
+    "yuf_model_create_from_yuf": [ctypes.c_char_p, I, I, P],
+    "yuf_model_destroy": [P],
+    "yuf_model_get_config": [P, P],
+    "yuf_state_alloc": [P, I],
+    "yuf_state_reset": [P, I, I, P],
+    "yuf_state_export": [P, I, I, I, P, P, P, P],
+    "yuf_state_import": [P, I, I, I, P, P, P, P],
+    "yuf_prefill": [P, P, I, I, I, P, P, P],
+    "yuf_step": [P, P, I, I, P, P],
+    "yuf_model_sync_check": [P, P],
+    "yuf_model_set_debug": [P, I],
+    "yuf_debug_dump": [P, ctypes.c_char_p, I, P, ctypes.c_size_t, P],
 }
+
+
+class ModelConfigC(ctypes.Structure):
+    """``yuf_model_config`` of include/yufb200.h."""
+
+    _fields_ = [(n, ctypes.c_int) for n in ("vocab_size", "d_model", "n_layers", "n_heads",
+                                             "head_size", "rosa_size", "low_rank")]
 
 
 class YufError(RuntimeError):

@@ -34,6 +34,9 @@ yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const
 yuf_status_t wkv7_chunk_dispatch(const float* r, const float* w, const float* k, const float* v,
                                  const float* a, const float* b, const float* s0, float* y,
                                  float* s_out, int B, int T, int H, int N, cudaStream_t stream);
+yuf_status_t wkv7_decode_dispatch(const float* r, const float* w, const float* k, const float* v,
+                                  const float* a, const float* b, const float* s0, float* y,
+                                  float* s_out, int BH, int N, cudaStream_t stream);
 yuf_status_t rosa_dispatch(const float* cand, const float* write, const float* gate,
                            const float* decay, const float* dir, const float* m0, float* read,
                            float* m_out, int B, int T, int R, bool gated, cudaStream_t stream);
@@ -98,7 +101,10 @@ yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k,
   REQUIRE(aligned(s0, 8) && aligned(s_out, 8), "wkv7: state buffers must be 8-byte aligned");
   REQUIRE(algo >= YUF_WKV_AUTO && algo <= YUF_WKV_CHUNKED, "wkv7: unknown algorithm %d", algo);
   if (B == 0 || H == 0) return YUF_OK;
-  const bool chunked = algo == YUF_WKV_CHUNKED || (algo == YUF_WKV_AUTO && T >= 16);
+  if (T == 1 && algo != YUF_WKV_CHUNKED)
+    return wkv7_decode_dispatch(r, w, k, v, a, b, s0, y, s_out, B * H, N,
+                                static_cast<cudaStream_t>(stream));
+  const bool chunked = algo == YUF_WKV_CHUNKED;
   if (chunked)
     return wkv7_chunk_dispatch(r, w, k, v, a, b, s0, y, s_out, B, T, H, N,
                                static_cast<cudaStream_t>(stream));

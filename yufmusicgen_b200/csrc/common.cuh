@@ -61,3 +61,20 @@ YUF_DEVICE float lane_group_sum(float v, int lane) {
   }
 }
 }  // namespace yuf
+
+namespace yuf {
+// Smallest lane stride >= C, a multiple of 4 floats (LDS.128), for which the G
+// lanes' 16-byte windows at the same offset land on distinct banks.
+constexpr int conflict_free_stride(int C, int G) {
+  for (int cs = (C + 3) / 4 * 4;; cs += 4) {
+    bool ok = true;
+    for (int g1 = 0; g1 < G && ok; ++g1)
+      for (int g2 = g1 + 1; g2 < G && ok; ++g2) {
+        const int d = ((g2 - g1) * cs) % 32;
+        ok = d >= 4 && d <= 28;
+      }
+    if (ok) return cs;
+  }
+}
+
+}  // namespace yuf

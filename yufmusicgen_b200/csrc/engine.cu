@@ -1,0 +1,648 @@
+// Model engine: the YufMusicGen block stack on one B200 with device-resident
+// recurrent state slots (C ABI in include/yufb200.h).
+//
+// Forward of one block (yufmusicgen/model.py:365-378), rows = tokens:
+//   xt  = LN_time(x)                                   layernorm_kernel
+//   6 token-shift mixes of xt (prev = state)           mix_kernel
+//   r,k,v = x_{r,k,v} W^T                              one strided-batched GEMM
+//   lr1 = x_{w,a,g} L1 ; tanh on the w part ; lr2 = lr1 L2   two batched GEMMs
+//   w_raw, k_adj, a_op, b_op, g                        timemix_post_kernel
+//   y, S  = WKV-7 scan (state slot in/out)             wkv7 kernels
+//   x    += W_o (LN_out(y) * g)                        layernorm(+gate) + GEMM (beta = 1)
+//   [cand|write|gate] = LN_rosa(x) W^T                 one GEMM ([3R, d] weight)
+//   read, m = ROSA scan (+ bias, gated, state slot)    rosa scan kernel
+//   x    += read W_out^T                               GEMM (beta = 1)
+//   x    += W_out(silu(x_f W_in^T) * (x_f W_g^T))      GEMM [8d, d], silu_mul, GEMM (beta = 1)
+// then logits = LN_final(x) E^T (tied head, model.py:389-391, 421).
+//
+// GEMMs go to cuBLAS: fp32 mode uses its BF16x9 FP32 emulation (fp32-accurate
+// products on the tensor cores), bf16 mode stores the weights in bf16 and feeds
+// bf16 activations with fp32 accumulation.  Everything else (scans, norms,
+// activations, state) stays fp32.
+
+#include <cublas_v2.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "model_kernels.cuh"
+
+namespace yuf {
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  ~DevBuf() { if (p) cudaFree(p); }
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+};
+
+static int reference_low_rank(int d) {
+  // max(32, int(round(2.5 * sqrt(d) / 32) * 32)), Python round-half-even (model.py:59)
+  const double x = 2.5 * std::sqrt((double)d) / 32.0;
+  double r = std::nearbyint(x);  // default rounding mode: half to even
+  return std::max(32, (int)r * 32);
+}
+
+}  // namespace yuf
+
+using namespace yuf;
+
+struct LayerW {
+  float *ln_t_w, *ln_t_b, *mix, *w0, *a0, *k_k, *k_a;
+  void *W_rkv, *W_lr1, *W_lr2, *W_o;
+  float *ln_o_w, *ln_o_b, *ln_r_w, *ln_r_b, *householder, *decay, *b_rosa;
+  void *W_rosa_in, *W_rosa_out;
+  float *ln_f_w, *ln_f_b;
+  void *W_ffn_in, *W_ffn_out;
+};
+
+struct yuf_model {
+  yuf_model_config cfg{};
+  int precision = 0;
+  int device = 0;
+  cublasHandle_t blas = nullptr;
+  bool emulated_fp32 = false;
+  std::vector<std::unique_ptr<DevBuf>> owned;
+  float* emb = nullptr;        // [V, d] fp32
+  void* emb_gemm = nullptr;    // LM head operand (fp32 or bf16 copy)
+  float *fin_w = nullptr, *fin_b = nullptr;
+  std::vector<LayerW> L;
+  // state slots
+  int n_slots = 0;
+  float *st_prev = nullptr, *st_S = nullptr, *st_m = nullptr;
+  // workspace
+  size_t ws_rows = 0;
+  std::unique_ptr<DevBuf> ws;
+  std::unique_ptr<DevBuf> blas_ws;
+  int* d_err = nullptr;
+  // debug dumps: region -> per layer host copies of the last call
+  bool debug = false;
+  std::map<std::string, std::vector<std::vector<float>>> dumps;
+
+  void* alloc(size_t bytes) {
+    auto b = std::make_unique<DevBuf>();
+    if (cudaMalloc(&b->p, bytes) != cudaSuccess) return nullptr;
+    b->bytes = bytes;
+    void* p = b->p;
+    owned.push_back(std::move(b));
+    return p;
+  }
+  int d() const { return cfg.d_model; }
+  int H() const { return cfg.n_heads; }
+  int N() const { return cfg.head_size; }
+  int R() const { return cfg.rosa_size; }
+  int lr() const { return cfg.low_rank; }
+  int V() const { return cfg.vocab_size; }
+  size_t wsz() const { return precision == YUF_PRECISION_BF16_WEIGHTS ? 2 : 4; }
+  size_t slot_prev() const { return (size_t)d(); }
+  size_t slot_S() const { return (size_t)H() * N() * N(); }
+  size_t slot_m() const { return (size_t)R(); }
+};
+
+namespace yuf {
+#define Y_REQUIRE(cond, ...)                 \
+  do {                                       \
+    if (!(cond)) {                           \
+      set_error(__VA_ARGS__);                \
+      return YUF_ERR_INVALID_ARGUMENT;       \
+    }                                        \
+  } while (0)
+#define Y_CUDA(call)                                                          \
+  do {                                                                        \
+    cudaError_t e_ = (call);                                                  \
+    if (e_ != cudaSuccess) {                                                  \
+      set_error("%s failed: %s", #call, cudaGetErrorString(e_));              \
+      return e_ == cudaErrorMemoryAllocation ? YUF_ERR_OUT_OF_MEMORY : YUF_ERR_CUDA; \
+    }                                                                         \
+  } while (0)
+#define Y_BLAS(call)                                                          \
+  do {                                                                        \
+    cublasStatus_t s_ = (call);                                               \
+    if (s_ != CUBLAS_STATUS_SUCCESS) {                                        \
+      set_error("%s failed: cuBLAS status %d", #call, (int)s_);               \
+      return YUF_ERR_CUDA;                                                    \
+    }                                                                         \
+  } while (0)
+#define Y_TRY(call)                    \
+  do {                                 \
+    yuf_status_t st_ = (call);         \
+    if (st_ != YUF_OK) return st_;     \
+  } while (0)
+
+// Row-major C[M,N] (ldc) = A[M,K] (lda) . W[N,K]^T + beta C, batched with strides.
+static yuf_status_t gemm(yuf_model* m, const void* A, int lda, long long sA, const void* W,
+                         long long sW, float* C, int ldc, long long sC, int M, int N, int K,
+                         float beta, int batch, cudaStream_t s) {
+  const float alpha = 1.f;
+  const bool bf = m->precision == YUF_PRECISION_BF16_WEIGHTS;
+  const cudaDataType ty = bf ? CUDA_R_16BF : CUDA_R_32F;
+  // fp32: the handle's math mode (CUBLAS_FP32_EMULATED_BF16X9_MATH) lets cuBLAS run
+  // the fp32 products as BF16x9 on the tensor cores with fp32-level accuracy.
+  const cublasComputeType_t ct = CUBLAS_COMPUTE_32F;
+  Y_BLAS(cublasSetStream(m->blas, s));
+  if (batch == 1) {
+    Y_BLAS(cublasGemmEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, &alpha, W, ty, K, A, ty, lda,
+                        &beta, C, CUDA_R_32F, ldc, ct, CUBLAS_GEMM_DEFAULT));
+  } else {
+    Y_BLAS(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, &alpha, W, ty, K, sW,
+                                      A, ty, lda, sA, &beta, C, CUDA_R_32F, ldc, sC, batch, ct,
+                                      CUBLAS_GEMM_DEFAULT));
+  }
+  return YUF_OK;
+}
+
+// Workspace for `rows` token rows (grown on demand; never shrinks).
+struct WS {
+  float *x, *xt, *mixed, *rkv, *lr1, *lr2, *w_raw, *k_adj, *a_op, *b_op, *g, *y, *tmp, *rosa, *read,
+      *ig, *h;
+  __nv_bfloat16* bf;  // bf16 staging of a GEMM input (largest: [rows, 4d] or [6][rows][d])
+};
+
+static size_t ws_floats_per_row(const yuf_model* m) {
+  const size_t d = m->d(), lr = m->lr(), R = m->R();
+  return d /*x*/ + d /*xt*/ + 6 * d /*mixed*/ + 3 * d /*rkv*/ + 3 * lr /*lr1*/ + 3 * d /*lr2*/ +
+         5 * d /*w_raw,k_adj,a_op,b_op,g*/ + d /*y*/ + d /*tmp*/ + 3 * R /*rosa*/ + R /*read*/ +
+         8 * d /*ig*/ + 4 * d /*h*/;
+}
+
+static yuf_status_t ensure_ws(yuf_model* m, size_t rows) {
+  if (rows <= m->ws_rows) return YUF_OK;
+  const size_t per = ws_floats_per_row(m);
+  const size_t bf_elems = rows * (size_t)std::max(6 * m->d(), m->R());
+  auto b = std::make_unique<DevBuf>();
+  const size_t bytes = rows * per * sizeof(float) + bf_elems * sizeof(__nv_bfloat16) + 256;
+  Y_CUDA(cudaMalloc(&b->p, bytes));
+  b->bytes = bytes;
+  m->ws = std::move(b);
+  m->ws_rows = rows;
+  return YUF_OK;
+}
+
+static WS carve(yuf_model* m, size_t rows) {
+  float* p = static_cast<float*>(m->ws->p);
+  const size_t d = m->d(), lr = m->lr(), R = m->R();
+  WS w;
+  auto take = [&](size_t n) { float* q = p; p += n; return q; };
+  w.x = take(rows * d);
+  w.xt = take(rows * d);
+  w.mixed = take(6 * rows * d);
+  w.rkv = take(3 * rows * d);
+  w.lr1 = take(3 * rows * lr);
+  w.lr2 = take(3 * rows * d);
+  w.w_raw = take(rows * d);
+  w.k_adj = take(rows * d);
+  w.a_op = take(rows * d);
+  w.b_op = take(rows * d);
+  w.g = take(rows * d);
+  w.y = take(rows * d);
+  w.tmp = take(rows * d);
+  w.rosa = take(rows * 3 * R);
+  w.read = take(rows * R);
+  w.ig = take(rows * 8 * d);
+  w.h = take(rows * 4 * d);
+  uintptr_t u = reinterpret_cast<uintptr_t>(p);
+  u = (u + 255) & ~uintptr_t(255);
+  w.bf = reinterpret_cast<__nv_bfloat16*>(u);
+  return w;
+}
+
+// GEMM input operand: fp32 as is, or converted to bf16 in the staging buffer.
+static const void* gemm_input(yuf_model* m, WS& w, const float* x, size_t n, cudaStream_t s) {
+  if (m->precision != YUF_PRECISION_BF16_WEIGHTS) return x;
+  launch_to_bf16(x, w.bf, n, s);
+  return w.bf;
+}
+
+static void dump(yuf_model* m, const char* region, int layer, const float* dev, size_t n,
+                 cudaStream_t s) {
+  if (!m->debug) return;
+  auto& v = m->dumps[region];
+  if ((int)v.size() <= layer + 1) v.resize(layer + 2);
+  auto& h = v[layer + 1];
+  h.resize(n);
+  cudaMemcpyAsync(h.data(), dev, n * sizeof(float), cudaMemcpyDeviceToHost, s);
+  cudaStreamSynchronize(s);
+}
+
+// One forward over B sequences x T tokens (rows = B*T), state slots [slot0, slot0+B).
+static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int slot0,
+                            float* logits_last, float* logits_all, cudaStream_t s) {
+  const size_t rows = (size_t)B * T;
+  const int d = m->d(), H = m->H(), N = m->N(), R = m->R(), lr = m->lr(), V = m->V();
+  Y_TRY(ensure_ws(m, rows));
+  WS w = carve(m, rows);
+  launch_embed(ids, m->emb, w.x, (int)rows, d, V, m->d_err, s);
+  const size_t RD = rows * d;
+  for (int li = 0; li < m->cfg.n_layers; ++li) {
+    const LayerW& Lw = m->L[li];
+    float* prev = m->st_prev + ((size_t)li * m->n_slots + slot0) * m->slot_prev();
+    float* S = m->st_S + ((size_t)li * m->n_slots + slot0) * m->slot_S();
+    float* mem = m->st_m + ((size_t)li * m->n_slots + slot0) * m->slot_m();
+    // --- TimeMix
+    launch_layernorm<float>(w.x, Lw.ln_t_w, Lw.ln_t_b, nullptr, w.xt, (int)rows, d, s);
+    launch_mix<float>(w.xt, prev, Lw.mix, w.mixed, B, T, d, s);
+    Y_CUDA(cudaMemcpy2DAsync(prev, d * sizeof(float), w.xt + (size_t)(T - 1) * d,
+                             (size_t)T * d * sizeof(float), d * sizeof(float), B,
+                             cudaMemcpyDeviceToDevice, s));
+    const void* mixed = gemm_input(m, w, w.mixed, 6 * RD, s);
+    const size_t esz = m->precision == YUF_PRECISION_BF16_WEIGHTS ? 2 : 4;
+    const char* mixed_hi = static_cast<const char*>(mixed) + 3 * RD * esz;  // w, a, g mixes
+    Y_TRY(gemm(m, mixed, d, RD, Lw.W_rkv, (long long)d * d, w.rkv, d, RD, (int)rows, d, d, 0.f, 3, s));
+    Y_TRY(gemm(m, mixed_hi, d, RD, Lw.W_lr1, (long long)lr * d, w.lr1, lr, rows * lr, (int)rows, lr, d,
+               0.f, 3, s));
+    launch_tanh<float>(w.lr1, w.lr1, rows * lr, s);  // w branch: tanh(xw W1)
+    const void* lr1 = gemm_input(m, w, w.lr1, 3 * rows * lr, s);
+    Y_TRY(gemm(m, lr1, lr, rows * lr, Lw.W_lr2, (long long)d * lr, w.lr2, d, RD, (int)rows, d, lr, 0.f,
+               3, s));
+    launch_timemix_post(w.rkv + RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD, Lw.w0, Lw.a0, Lw.k_k, Lw.k_a,
+                        w.w_raw, w.k_adj, w.a_op, w.b_op, w.g, (int)rows, H, N, s);
+    if (T == 1)
+      Y_TRY(wkv7_decode_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S,
+                                 B * H, N, s));
+    else
+      Y_TRY(wkv7_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, nullptr,
+                          nullptr, B, T, H, N, false, s));
+    launch_layernorm<float>(w.y, Lw.ln_o_w, Lw.ln_o_b, w.g, w.tmp, (int)rows, d, s);
+    if (m->debug) {
+      dump(m, "ln0", li, w.xt, RD, s);
+      dump(m, "r", li, w.rkv, RD, s);
+      dump(m, "w", li, w.w_raw, RD, s);
+      dump(m, "k", li, w.k_adj, RD, s);
+      dump(m, "v", li, w.rkv + 2 * RD, RD, s);
+      dump(m, "a", li, w.a_op, RD, s);
+      dump(m, "b", li, w.b_op, RD, s);
+      dump(m, "g", li, w.g, RD, s);
+      dump(m, "y", li, w.y, RD, s);
+    }
+    Y_TRY(gemm(m, gemm_input(m, w, w.tmp, RD, s), d, 0, Lw.W_o, 0, w.x, d, 0, (int)rows, d, d, 1.f, 1, s));
+    if (m->debug) dump(m, "h1", li, w.x, RD, s);
+    // --- ROSA
+    launch_layernorm<float>(w.x, Lw.ln_r_w, Lw.ln_r_b, nullptr, w.tmp, (int)rows, d, s);
+    Y_TRY(gemm(m, gemm_input(m, w, w.tmp, RD, s), d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0, (int)rows,
+               3 * R, d, 0.f, 1, s));
+    Y_TRY(rosa_engine_dispatch(w.rosa, w.rosa + R, w.rosa + 2 * R, Lw.b_rosa, Lw.b_rosa + R,
+                               Lw.b_rosa + 2 * R, 3 * R, Lw.decay, Lw.householder, mem, w.read, mem, B,
+                               T, R, s));
+    if (m->debug) dump(m, "read", li, w.read, rows * R, s);
+    Y_TRY(gemm(m, gemm_input(m, w, w.read, rows * R, s), R, 0, Lw.W_rosa_out, 0, w.x, d, 0, (int)rows, d,
+               R, 1.f, 1, s));
+    if (m->debug) dump(m, "h2", li, w.x, RD, s);
+    // --- FFN
+    launch_layernorm<float>(w.x, Lw.ln_f_w, Lw.ln_f_b, nullptr, w.tmp, (int)rows, d, s);
+    Y_TRY(gemm(m, gemm_input(m, w, w.tmp, RD, s), d, 0, Lw.W_ffn_in, 0, w.ig, 8 * d, 0, (int)rows,
+               8 * d, d, 0.f, 1, s));
+    launch_silu_mul<float>(w.ig, w.h, (int)rows, 4 * d, s);
+    Y_TRY(gemm(m, gemm_input(m, w, w.h, rows * 4 * d, s), 4 * d, 0, Lw.W_ffn_out, 0, w.x, d, 0,
+               (int)rows, d, 4 * d, 1.f, 1, s));
+    if (m->debug) dump(m, "h3", li, w.x, RD, s);
+  }
+  // final norm + tied LM head
+  launch_layernorm<float>(w.x, m->fin_w, m->fin_b, nullptr, w.tmp, (int)rows, d, s);
+  const void* hn = gemm_input(m, w, w.tmp, RD, s);
+  const size_t esz = m->precision == YUF_PRECISION_BF16_WEIGHTS ? 2 : 4;
+  if (logits_all)
+    Y_TRY(gemm(m, hn, d, 0, m->emb_gemm, 0, logits_all, V, 0, (int)rows, V, d, 0.f, 1, s));
+  if (logits_last) {
+    const void* last = static_cast<const char*>(hn) + (size_t)(T - 1) * d * esz;
+    Y_TRY(gemm(m, last, T * d, 0, m->emb_gemm, 0, logits_last, V, 0, B, V, d, 0.f, 1, s));
+    if (m->debug) dump(m, "logits", -1, logits_last, (size_t)B * V, s);
+  }
+  return check_launch("model forward");
+}
+
+// ---------------------------------------------------------------- loading
+struct HostTensor {
+  const float* p;
+  int64_t n;
+};
+
+static yuf_status_t upload(yuf_model* m, const std::unordered_map<std::string, HostTensor>& t,
+                           const std::string& name, int64_t n, float** out) {
+  auto it = t.find(name);
+  Y_REQUIRE(it != t.end(), "model: missing tensor %s", name.c_str());
+  Y_REQUIRE(it->second.n == n, "model: tensor %s has %lld elements, expected %lld", name.c_str(),
+            (long long)it->second.n, (long long)n);
+  float* d = static_cast<float*>(m->alloc(n * sizeof(float)));
+  if (!d) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+  Y_CUDA(cudaMemcpy(d, it->second.p, n * sizeof(float), cudaMemcpyHostToDevice));
+  *out = d;
+  return YUF_OK;
+}
+
+// Pack host fp32 matrices (each [rows_i, K], row-major) into one GEMM weight in
+// the model precision.  transpose: the source is [K, rows] (a Parameter used as
+// x @ P, model.py:108-112) and is transposed to [rows, K].
+static yuf_status_t pack_weight(yuf_model* m, const std::unordered_map<std::string, HostTensor>& t,
+                                const std::vector<std::string>& names, const std::vector<int>& rows,
+                                int K, bool transpose, void** out) {
+  size_t total = 0;
+  for (int r : rows) total += (size_t)r * K;
+  std::vector<float> host(total);
+  size_t off = 0;
+  for (size_t i = 0; i < names.size(); ++i) {
+    auto it = t.find(names[i]);
+    Y_REQUIRE(it != t.end(), "model: missing tensor %s", names[i].c_str());
+    Y_REQUIRE(it->second.n == (int64_t)rows[i] * K, "model: tensor %s has %lld elements, expected %lld",
+              names[i].c_str(), (long long)it->second.n, (long long)rows[i] * K);
+    const float* src = it->second.p;
+    if (!transpose) {
+      std::memcpy(host.data() + off, src, (size_t)rows[i] * K * sizeof(float));
+    } else {
+      for (int r = 0; r < rows[i]; ++r)
+        for (int k = 0; k < K; ++k) host[off + (size_t)r * K + k] = src[(size_t)k * rows[i] + r];
+    }
+    off += (size_t)rows[i] * K;
+  }
+  if (m->precision == YUF_PRECISION_BF16_WEIGHTS) {
+    std::vector<__nv_bfloat16> hb(total);
+    for (size_t i = 0; i < total; ++i) hb[i] = __float2bfloat16_rn(host[i]);
+    void* d = m->alloc(total * 2);
+    if (!d) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+    Y_CUDA(cudaMemcpy(d, hb.data(), total * 2, cudaMemcpyHostToDevice));
+    *out = d;
+  } else {
+    void* d = m->alloc(total * 4);
+    if (!d) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+    Y_CUDA(cudaMemcpy(d, host.data(), total * 4, cudaMemcpyHostToDevice));
+    *out = d;
+  }
+  return YUF_OK;
+}
+
+static yuf_status_t load_weights(yuf_model* m, const std::unordered_map<std::string, HostTensor>& t) {
+  const int d = m->d(), R = m->R(), lr = m->lr(), V = m->V(), F = 4 * d;
+  Y_TRY(upload(m, t, "token_embedding.weight", (int64_t)V * d, &m->emb));
+  Y_TRY(upload(m, t, "final_norm.weight", d, &m->fin_w));
+  Y_TRY(upload(m, t, "final_norm.bias", d, &m->fin_b));
+  auto lm = t.find("lm_head.weight");
+  if (lm != t.end() && lm->second.p != t.at("token_embedding.weight").p) {
+    // A separate head is only meaningful untied; the reference ties them.
+    Y_REQUIRE(std::memcmp(lm->second.p, t.at("token_embedding.weight").p, (size_t)V * d * 4) == 0,
+              "model: lm_head.weight differs from token_embedding.weight (untied heads unsupported)");
+  }
+  Y_TRY(pack_weight(m, t, {"token_embedding.weight"}, {V}, d, false, &m->emb_gemm));
+  m->L.resize(m->cfg.n_layers);
+  for (int i = 0; i < m->cfg.n_layers; ++i) {
+    LayerW& Lw = m->L[i];
+    const std::string p = "blocks." + std::to_string(i) + ".";
+    const std::string tm = p + "time_mix.", ro = p + "rosa.";
+    Y_TRY(upload(m, t, p + "norm_time.weight", d, &Lw.ln_t_w));
+    Y_TRY(upload(m, t, p + "norm_time.bias", d, &Lw.ln_t_b));
+    {  // mix rows in the reference order r, w, k, v, a, g
+      std::vector<float> mix(6 * (size_t)d);
+      const char* names[6] = {"mix_r", "mix_w", "mix_k", "mix_v", "mix_a", "mix_g"};
+      for (int c = 0; c < 6; ++c) {
+        auto it = t.find(tm + names[c]);
+        Y_REQUIRE(it != t.end() && it->second.n == d, "model: bad tensor %s%s", tm.c_str(), names[c]);
+        std::memcpy(mix.data() + (size_t)c * d, it->second.p, d * 4);
+      }
+      Lw.mix = static_cast<float*>(m->alloc(mix.size() * 4));
+      if (!Lw.mix) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+      Y_CUDA(cudaMemcpy(Lw.mix, mix.data(), mix.size() * 4, cudaMemcpyHostToDevice));
+    }
+    Y_TRY(upload(m, t, tm + "w0", d, &Lw.w0));
+    Y_TRY(upload(m, t, tm + "a0", d, &Lw.a0));
+    Y_TRY(upload(m, t, tm + "k_k", d, &Lw.k_k));
+    Y_TRY(upload(m, t, tm + "k_a", d, &Lw.k_a));
+    Y_TRY(pack_weight(m, t, {tm + "receptance.weight", tm + "key.weight", tm + "value.weight"},
+                      {d, d, d}, d, false, &Lw.W_rkv));
+    Y_TRY(pack_weight(m, t, {tm + "w1", tm + "a1", tm + "g1"}, {lr, lr, lr}, d, true, &Lw.W_lr1));
+    Y_TRY(pack_weight(m, t, {tm + "w2", tm + "a2", tm + "g2"}, {d, d, d}, lr, true, &Lw.W_lr2));
+    Y_TRY(pack_weight(m, t, {tm + "output.weight"}, {d}, d, false, &Lw.W_o));
+    Y_TRY(upload(m, t, tm + "out_norm.weight", d, &Lw.ln_o_w));
+    Y_TRY(upload(m, t, tm + "out_norm.bias", d, &Lw.ln_o_b));
+    Y_TRY(upload(m, t, p + "norm_rosa.weight", d, &Lw.ln_r_w));
+    Y_TRY(upload(m, t, p + "norm_rosa.bias", d, &Lw.ln_r_b));
+    Y_TRY(upload(m, t, ro + "householder", R, &Lw.householder));
+    Y_TRY(upload(m, t, ro + "decay", R, &Lw.decay));
+    Y_TRY(pack_weight(m, t, {ro + "input.weight", ro + "write_gate.weight", ro + "read_gate.weight"},
+                      {R, R, R}, d, false, &Lw.W_rosa_in));
+    {
+      std::vector<float> bias(3 * (size_t)R);
+      const char* names[3] = {"input.bias", "write_gate.bias", "read_gate.bias"};
+      for (int c = 0; c < 3; ++c) {
+        auto it = t.find(ro + names[c]);
+        Y_REQUIRE(it != t.end() && it->second.n == R, "model: bad tensor %s%s", ro.c_str(), names[c]);
+        std::memcpy(bias.data() + (size_t)c * R, it->second.p, R * 4);
+      }
+      Lw.b_rosa = static_cast<float*>(m->alloc(bias.size() * 4));
+      if (!Lw.b_rosa) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+      Y_CUDA(cudaMemcpy(Lw.b_rosa, bias.data(), bias.size() * 4, cudaMemcpyHostToDevice));
+    }
+    Y_TRY(pack_weight(m, t, {ro + "output.weight"}, {d}, R, false, &Lw.W_rosa_out));
+    Y_TRY(upload(m, t, p + "norm_ffn.weight", d, &Lw.ln_f_w));
+    Y_TRY(upload(m, t, p + "norm_ffn.bias", d, &Lw.ln_f_b));
+    Y_TRY(pack_weight(m, t, {p + "ffn_in.weight", p + "ffn_gate.weight"}, {F, F}, d, false, &Lw.W_ffn_in));
+    Y_TRY(pack_weight(m, t, {p + "ffn_out.weight"}, {d}, F, false, &Lw.W_ffn_out));
+  }
+  return YUF_OK;
+}
+
+static yuf_status_t validate_cfg(yuf_model_config* c) {
+  Y_REQUIRE(c->d_model == c->n_heads * c->head_size, "model: d_model must equal n_heads * head_size");
+  Y_REQUIRE(c->d_model >= 32 && c->n_layers >= 1, "model: model is too small to be useful");
+  Y_REQUIRE(c->d_model % 8 == 0, "model: d_model must be a multiple of 8");
+  Y_REQUIRE(c->vocab_size > 0 && c->rosa_size >= 1 && c->rosa_size <= 1024, "model: bad vocab/rosa size");
+  if (c->low_rank <= 0) c->low_rank = reference_low_rank(c->d_model);
+  return YUF_OK;
+}
+
+yuf_status_t model_create_from_map(const yuf_model_config* cfg, int precision, int device,
+                                   const std::unordered_map<std::string, HostTensor>& t,
+                                   yuf_model** out) {
+  Y_REQUIRE(cfg && out, "model: null argument");
+  Y_REQUIRE(precision == YUF_PRECISION_FP32 || precision == YUF_PRECISION_BF16_WEIGHTS,
+            "model: unknown precision %d", precision);
+  yuf_model_config c = *cfg;
+  Y_TRY(validate_cfg(&c));
+  switch (c.head_size) {
+    case 16: case 32: case 40: case 48: case 64: case 96: case 128: break;
+    default: set_error("model: head_size %d has no kernel", c.head_size); return YUF_ERR_UNSUPPORTED;
+  }
+  Y_CUDA(cudaSetDevice(device));
+  auto m = std::make_unique<yuf_model>();
+  m->cfg = c;
+  m->precision = precision;
+  m->device = device;
+  Y_BLAS(cublasCreate(&m->blas));
+  // fp32: prefer cuBLAS's BF16x9 emulation (fp32-accurate on the tensor cores,
+  // cuBLAS >= 12.9); an older cuBLAS already loaded into the process (e.g. the
+  // one a framework ships) rejects the mode, and plain fp32 GEMMs are used.
+  m->emulated_fp32 = precision == YUF_PRECISION_FP32 &&
+                     cublasSetMathMode(m->blas, CUBLAS_FP32_EMULATED_BF16X9_MATH) == CUBLAS_STATUS_SUCCESS;
+  if (!m->emulated_fp32) Y_BLAS(cublasSetMathMode(m->blas, CUBLAS_DEFAULT_MATH));
+  m->blas_ws = std::make_unique<DevBuf>();
+  m->blas_ws->bytes = 64u << 20;
+  Y_CUDA(cudaMalloc(&m->blas_ws->p, m->blas_ws->bytes));
+  Y_BLAS(cublasSetWorkspace(m->blas, m->blas_ws->p, m->blas_ws->bytes));
+  m->d_err = static_cast<int*>(m->alloc(sizeof(int)));
+  if (!m->d_err) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+  Y_CUDA(cudaMemset(m->d_err, 0, sizeof(int)));
+  yuf_status_t st = load_weights(m.get(), t);
+  if (st != YUF_OK) {
+    cublasDestroy(m->blas);
+    return st;
+  }
+  *out = m.release();
+  return YUF_OK;
+}
+
+}  // namespace yuf
+
+extern "C" {
+
+yuf_status_t yuf_model_create(const yuf_model_config* cfg, int precision, int device, int n_tensors,
+                              const char* const* names, const float* const* host_data,
+                              const int64_t* numels, yuf_model** out) {
+  Y_REQUIRE(n_tensors >= 0 && (n_tensors == 0 || (names && host_data && numels)), "model: bad tensor list");
+  std::unordered_map<std::string, HostTensor> t;
+  for (int i = 0; i < n_tensors; ++i) {
+    Y_REQUIRE(names[i] && host_data[i], "model: tensor %d has a null name or pointer", i);
+    t[names[i]] = HostTensor{host_data[i], numels[i]};
+  }
+  return model_create_from_map(cfg, precision, device, t, out);
+}
+
+yuf_status_t yuf_model_destroy(yuf_model* m) {
+  if (!m) return YUF_OK;
+  cudaSetDevice(m->device);
+  if (m->blas) cublasDestroy(m->blas);
+  delete m;
+  return YUF_OK;
+}
+
+yuf_status_t yuf_model_get_config(const yuf_model* m, yuf_model_config* out) {
+  Y_REQUIRE(m && out, "model: null argument");
+  *out = m->cfg;
+  return YUF_OK;
+}
+
+yuf_status_t yuf_state_alloc(yuf_model* m, int n_slots) {
+  Y_REQUIRE(m && n_slots >= 1, "state: need at least one slot");
+  Y_CUDA(cudaSetDevice(m->device));
+  const size_t Lr = m->cfg.n_layers, n = n_slots;
+  float* p = static_cast<float*>(m->alloc(Lr * n * m->slot_prev() * 4));
+  float* S = static_cast<float*>(m->alloc(Lr * n * m->slot_S() * 4));
+  float* mm = static_cast<float*>(m->alloc(Lr * n * m->slot_m() * 4));
+  if (!p || !S || !mm) { set_error("state: out of device memory for %d slots", n_slots); return YUF_ERR_OUT_OF_MEMORY; }
+  Y_CUDA(cudaMemset(p, 0, Lr * n * m->slot_prev() * 4));
+  Y_CUDA(cudaMemset(S, 0, Lr * n * m->slot_S() * 4));
+  Y_CUDA(cudaMemset(mm, 0, Lr * n * m->slot_m() * 4));
+  m->st_prev = p;
+  m->st_S = S;
+  m->st_m = mm;
+  m->n_slots = n_slots;
+  return YUF_OK;
+}
+
+yuf_status_t yuf_state_reset(yuf_model* m, int slot0, int n, void* stream) {
+  Y_REQUIRE(m && m->n_slots > 0, "state: no slots allocated");
+  Y_REQUIRE(slot0 >= 0 && n >= 0 && slot0 + n <= m->n_slots, "state: slots [%d, %d) out of range", slot0, slot0 + n);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int li = 0; li < m->cfg.n_layers; ++li) {
+    const size_t base = (size_t)li * m->n_slots + slot0;
+    Y_CUDA(cudaMemsetAsync(m->st_prev + base * m->slot_prev(), 0, n * m->slot_prev() * 4, s));
+    Y_CUDA(cudaMemsetAsync(m->st_S + base * m->slot_S(), 0, n * m->slot_S() * 4, s));
+    Y_CUDA(cudaMemsetAsync(m->st_m + base * m->slot_m(), 0, n * m->slot_m() * 4, s));
+  }
+  return YUF_OK;
+}
+
+static yuf_status_t state_copy(yuf_model* m, int layer, int slot0, int n, float* prev, float* S,
+                               float* mm, bool to_model, cudaStream_t s) {
+  Y_REQUIRE(m && m->n_slots > 0, "state: no slots allocated");
+  Y_REQUIRE(layer >= 0 && layer < m->cfg.n_layers, "state: layer %d out of range", layer);
+  Y_REQUIRE(slot0 >= 0 && n >= 0 && slot0 + n <= m->n_slots, "state: slots out of range");
+  const size_t base = (size_t)layer * m->n_slots + slot0;
+  struct { float* mine; float* theirs; size_t per; } parts[3] = {
+      {m->st_prev + base * m->slot_prev(), prev, m->slot_prev()},
+      {m->st_S + base * m->slot_S(), S, m->slot_S()},
+      {m->st_m + base * m->slot_m(), mm, m->slot_m()}};
+  for (auto& pt : parts) {
+    if (!pt.theirs) continue;
+    if (to_model)
+      Y_CUDA(cudaMemcpyAsync(pt.mine, pt.theirs, n * pt.per * 4, cudaMemcpyDeviceToDevice, s));
+    else
+      Y_CUDA(cudaMemcpyAsync(pt.theirs, pt.mine, n * pt.per * 4, cudaMemcpyDeviceToDevice, s));
+  }
+  return YUF_OK;
+}
+
+yuf_status_t yuf_state_export(yuf_model* m, int layer, int slot0, int n, float* prev, float* S,
+                              float* mm, void* stream) {
+  return state_copy(m, layer, slot0, n, prev, S, mm, false, static_cast<cudaStream_t>(stream));
+}
+
+yuf_status_t yuf_state_import(yuf_model* m, int layer, int slot0, int n, const float* prev,
+                              const float* S, const float* mm, void* stream) {
+  return state_copy(m, layer, slot0, n, const_cast<float*>(prev), const_cast<float*>(S),
+                    const_cast<float*>(mm), true, static_cast<cudaStream_t>(stream));
+}
+
+yuf_status_t yuf_prefill(yuf_model* m, const int32_t* ids, int B, int T, int slot0,
+                         float* logits_last, float* logits_all, void* stream) {
+  Y_REQUIRE(m, "prefill: null model");
+  Y_REQUIRE(m->n_slots > 0, "prefill: call yuf_state_alloc first");
+  Y_REQUIRE(B >= 1 && T >= 1 && ids, "prefill: need B >= 1, T >= 1 and ids");
+  Y_REQUIRE(slot0 >= 0 && slot0 + B <= m->n_slots, "prefill: slots [%d, %d) out of range (%d slots)",
+            slot0, slot0 + B, m->n_slots);
+  Y_CUDA(cudaSetDevice(m->device));
+  return forward(m, ids, B, T, slot0, logits_last, logits_all, static_cast<cudaStream_t>(stream));
+}
+
+yuf_status_t yuf_step(yuf_model* m, const int32_t* ids, int B, int slot0, float* logits, void* stream) {
+  Y_REQUIRE(m, "step: null model");
+  Y_REQUIRE(m->n_slots > 0, "step: call yuf_state_alloc first");
+  Y_REQUIRE(B >= 1 && ids && logits, "step: need B >= 1, ids and logits");
+  Y_REQUIRE(slot0 >= 0 && slot0 + B <= m->n_slots, "step: slots [%d, %d) out of range (%d slots)",
+            slot0, slot0 + B, m->n_slots);
+  Y_CUDA(cudaSetDevice(m->device));
+  return forward(m, ids, B, 1, slot0, logits, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+yuf_status_t yuf_model_sync_check(yuf_model* m, void* stream) {
+  Y_REQUIRE(m, "null model");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Y_CUDA(cudaStreamSynchronize(s));
+  int err = 0;
+  Y_CUDA(cudaMemcpy(&err, m->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) {
+    Y_CUDA(cudaMemset(m->d_err, 0, sizeof(int)));
+    set_error("model: a token id was outside [0, %d)", m->cfg.vocab_size);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  return YUF_OK;
+}
+
+yuf_status_t yuf_model_set_debug(yuf_model* m, int enabled) {
+  Y_REQUIRE(m, "null model");
+  m->debug = enabled != 0;
+  if (!m->debug) m->dumps.clear();
+  return YUF_OK;
+}
+
+yuf_status_t yuf_debug_dump(yuf_model* m, const char* region, int layer, float* host_out,
+                            size_t capacity, size_t* n_written) {
+  Y_REQUIRE(m && region, "null argument");
+  auto it = m->dumps.find(region);
+  Y_REQUIRE(it != m->dumps.end(), "debug: region %s was not recorded (enable debug first)", region);
+  Y_REQUIRE(layer + 1 >= 0 && layer + 1 < (int)it->second.size() && !it->second[layer + 1].empty(),
+            "debug: region %s has no layer %d", region, layer);
+  const auto& v = it->second[layer + 1];
+  if (n_written) *n_written = v.size();
+  if (host_out) {
+    Y_REQUIRE(capacity >= v.size(), "debug: buffer holds %zu floats, region needs %zu", capacity, v.size());
+    std::memcpy(host_out, v.data(), v.size() * 4);
+  }
+  return YUF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,219 @@
+// Elementwise / row kernels of the YufMusicGen block on sm_100a.
+//
+// Every kernel follows one formula of the reference block
+// (yufmusicgen/model.py:97-131, 195-197, 290-342, 365-422) and fuses what the
+// reference runs as separate ATen passes: the six token-shift mixes in one
+// pass over the LayerNorm output (model.py:98-105), the w/a/g activations with
+// the per-head kk normalisation and the key adjustment (model.py:108-122), the
+// output LayerNorm with the gate multiply (model.py:196), SiLU(in)*gate
+// (model.py:377).  Rows are tokens; one warp per row for the d-wide reductions.
+
+#include "model_kernels.cuh"
+
+namespace yuf {
+
+YUF_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+YUF_DEVICE void store_out(float* p, size_t i, float v) { p[i] = v; }
+YUF_DEVICE void store_out(__nv_bfloat16* p, size_t i, float v) { p[i] = __float2bfloat16_rn(v); }
+
+// x[row, :] = E[ids[row], :]  (nn.Embedding, model.py:411)
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ E,
+                             float* __restrict__ x, int rows, int d, int vocab, int* __restrict__ err) {
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  int id = ids[row];
+  if (id < 0 || id >= vocab) {  // out-of-range ids are reported, never read
+    if (threadIdx.x == 0) atomicExch(err, 1);
+    id = 0;
+  }
+  const float4* src = reinterpret_cast<const float4*>(E + (size_t)id * d);
+  float4* dst = reinterpret_cast<float4*>(x + (size_t)row * d);
+  for (int i = threadIdx.x; i < d / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+// LayerNorm over d (eps 1e-5, biased variance: nn.LayerNorm).  One warp per row.
+// Optionally multiplies by gate[row, :] after the affine (out_norm(y) * g).
+template <typename OUT>
+__global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                 const float* __restrict__ b, const float* __restrict__ gate,
+                                 OUT* __restrict__ out, int rows, int d) {
+  const int warps = blockDim.x >> 5;
+  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* xr = x + (size_t)row * d;
+  float s = 0.f;
+  for (int i = lane; i < d; i += 32) s += xr[i];
+  const float mean = warp_sum(s) / d;
+  float q = 0.f;
+  for (int i = lane; i < d; i += 32) {
+    const float c = xr[i] - mean;
+    q = fmaf(c, c, q);
+  }
+  const float rstd = rsqrtf(warp_sum(q) / d + 1e-5f);
+  for (int i = lane; i < d; i += 32) {
+    float v = (xr[i] - mean) * rstd * w[i] + b[i];
+    if (gate) v *= gate[(size_t)row * d + i];
+    store_out(out, (size_t)row * d + i, v);
+  }
+}
+
+// Token shift + the six lerps (model.py:98-105):
+//   delta = xt - shifted, x_c = xt + delta * mix_c, shifted = [prev, xt[:-1]]
+// out layout [6][rows][d] in the order r, k, v, w, a, g (the order the batched
+// projections consume).  The caller copies the new `prev` (xt of each
+// sequence's last token, model.py:197) after this kernel, so `prev` is only read.
+template <typename OUT>
+__global__ void mix_kernel(const float* __restrict__ xt, const float* __restrict__ prev,
+                           const float* __restrict__ mix, OUT* __restrict__ out, int B, int T, int d) {
+  const size_t rows = (size_t)B * T;
+  const size_t total = rows * d;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t row = i / d;
+    const int c = (int)(i - row * d);
+    const int t = (int)(row % T);
+    const int bb = (int)(row / T);
+    const float x = xt[i];
+    const float sh = t == 0 ? prev[(size_t)bb * d + c] : xt[i - d];
+    const float delta = x - sh;
+    // mix rows in the reference order r, w, k, v, a, g; outputs in r, k, v, w, a, g
+    store_out(out, 0 * total + i, x + delta * mix[0 * d + c]);
+    store_out(out, 3 * total + i, x + delta * mix[1 * d + c]);
+    store_out(out, 1 * total + i, x + delta * mix[2 * d + c]);
+    store_out(out, 2 * total + i, x + delta * mix[3 * d + c]);
+    store_out(out, 4 * total + i, x + delta * mix[4 * d + c]);
+    store_out(out, 5 * total + i, x + delta * mix[5 * d + c]);
+  }
+}
+
+template <typename OUT>
+__global__ void tanh_kernel(const float* __restrict__ x, OUT* __restrict__ out, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    store_out(out, i, tanhf(x[i]));
+}
+
+// w/a/g activations, kk normalisation and key adjustment (model.py:108-122).
+// Inputs (row-major [rows, d]): k (key proj), lw = tanh(xw W1) W2, la = (xa A1) A2,
+// lg = (xg G1) G2.  Outputs: w_raw = w0 + lw, a_op = -kk, b_op = kk * a,
+// k_adj = k * (1 + (a - 1) * k_a), g = sigmoid(lg).  One warp per (row, head).
+__global__ void timemix_post_kernel(const float* __restrict__ k, const float* __restrict__ lw,
+                                    const float* __restrict__ la, const float* __restrict__ lg,
+                                    const float* __restrict__ w0, const float* __restrict__ a0,
+                                    const float* __restrict__ k_k, const float* __restrict__ k_a,
+                                    float* __restrict__ w_raw, float* __restrict__ k_adj,
+                                    float* __restrict__ a_op, float* __restrict__ b_op,
+                                    float* __restrict__ g_out, int rows, int H, int N) {
+  const int warps = blockDim.x >> 5;
+  const size_t item = (size_t)blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (item >= (size_t)rows * H) return;
+  const size_t row = item / H;
+  const int h = (int)(item - row * H);
+  const int d = H * N;
+  const size_t base = row * d + (size_t)h * N;
+  float ss = 0.f;
+  for (int j = lane; j < N; j += 32) {
+    const float kv = k[base + j] * k_k[h * N + j];
+    ss = fmaf(kv, kv, ss);
+  }
+  const float nrm = sqrtf(warp_sum(ss));
+  const float inv = 1.f / fmaxf(nrm, 1e-12f);  // F.normalize eps (model.py:116)
+  for (int j = lane; j < N; j += 32) {
+    const int c = h * N + j;
+    const size_t i = base + j;
+    const float kv = k[i];
+    const float a = 1.f / (1.f + expf(-(a0[c] + la[i])));
+    const float kk = kv * k_k[c] * inv;
+    w_raw[i] = w0[c] + lw[i];
+    a_op[i] = -kk;
+    b_op[i] = kk * a;
+    k_adj[i] = kv * (1.f + (a - 1.f) * k_a[c]);
+    g_out[i] = 1.f / (1.f + expf(-lg[i]));
+  }
+}
+
+// SiLU(in) * gate over the fused [rows, 2F] projection (in | gate halves).
+template <typename OUT>
+__global__ void silu_mul_kernel(const float* __restrict__ ig, OUT* __restrict__ out, int rows,
+                                int F) {
+  const size_t total = (size_t)rows * F;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t row = i / F;
+    const int c = (int)(i - row * F);
+    const float h = ig[row * 2 * F + c];
+    const float gv = ig[row * 2 * F + F + c];
+    store_out(out, i, h / (1.f + expf(-h)) * gv);
+  }
+}
+
+// float -> bfloat16 copy (activations feeding a bf16-weight GEMM)
+__global__ void to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    y[i] = __float2bfloat16_rn(x[i]);
+}
+
+// ---- host launchers ----
+static int grid_for(size_t n, int threads) {
+  size_t g = (n + threads - 1) / threads;
+  return (int)(g > 148 * 32 ? 148 * 32 : (g == 0 ? 1 : g));
+}
+
+void launch_embed(const int32_t* ids, const float* E, float* x, int rows, int d, int vocab, int* err,
+                  cudaStream_t s) {
+  embed_kernel<<<rows, 128, 0, s>>>(ids, E, x, rows, d, vocab, err);
+}
+template <typename OUT>
+void launch_layernorm(const float* x, const float* w, const float* b, const float* gate, OUT* out,
+                      int rows, int d, cudaStream_t s) {
+  const int warps = 8;
+  layernorm_kernel<OUT><<<(rows + warps - 1) / warps, 32 * warps, 0, s>>>(x, w, b, gate, out, rows, d);
+}
+template <typename OUT>
+void launch_mix(const float* xt, const float* prev, const float* mix, OUT* out, int B, int T, int d,
+                cudaStream_t s) {
+  mix_kernel<OUT><<<grid_for((size_t)B * T * d, 256), 256, 0, s>>>(xt, prev, mix, out, B, T, d);
+}
+template <typename OUT>
+void launch_tanh(const float* x, OUT* out, size_t n, cudaStream_t s) {
+  tanh_kernel<OUT><<<grid_for(n, 256), 256, 0, s>>>(x, out, n);
+}
+void launch_timemix_post(const float* k, const float* lw, const float* la, const float* lg,
+                         const float* w0, const float* a0, const float* k_k, const float* k_a,
+                         float* w_raw, float* k_adj, float* a_op, float* b_op, float* g, int rows,
+                         int H, int N, cudaStream_t s) {
+  const int warps = 8;
+  const size_t items = (size_t)rows * H;
+  timemix_post_kernel<<<(unsigned)((items + warps - 1) / warps), 32 * warps, 0, s>>>(
+      k, lw, la, lg, w0, a0, k_k, k_a, w_raw, k_adj, a_op, b_op, g, rows, H, N);
+}
+template <typename OUT>
+void launch_silu_mul(const float* ig, OUT* out, int rows, int F, cudaStream_t s) {
+  silu_mul_kernel<OUT><<<grid_for((size_t)rows * F, 256), 256, 0, s>>>(ig, out, rows, F);
+}
+void launch_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) {
+  to_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
+}
+
+template void launch_layernorm<float>(const float*, const float*, const float*, const float*, float*,
+                                      int, int, cudaStream_t);
+template void launch_layernorm<__nv_bfloat16>(const float*, const float*, const float*, const float*,
+                                              __nv_bfloat16*, int, int, cudaStream_t);
+template void launch_mix<float>(const float*, const float*, const float*, float*, int, int, int,
+                                cudaStream_t);
+template void launch_mix<__nv_bfloat16>(const float*, const float*, const float*, __nv_bfloat16*,
+                                        int, int, int, cudaStream_t);
+template void launch_tanh<float>(const float*, float*, size_t, cudaStream_t);
+template void launch_tanh<__nv_bfloat16>(const float*, __nv_bfloat16*, size_t, cudaStream_t);
+template void launch_silu_mul<float>(const float*, float*, int, int, cudaStream_t);
+template void launch_silu_mul<__nv_bfloat16>(const float*, __nv_bfloat16*, int, int, cudaStream_t);
+
+}  // namespace yuf

@@ -1,0 +1,43 @@
+// Declarations of the block kernels (model_kernels.cu) and the scan
+// dispatchers used by the model engine.
+#pragma once
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+
+namespace yuf {
+
+void launch_embed(const int32_t* ids, const float* E, float* x, int rows, int d, int vocab, int* err,
+                  cudaStream_t s);
+template <typename OUT>
+void launch_layernorm(const float* x, const float* w, const float* b, const float* gate, OUT* out,
+                      int rows, int d, cudaStream_t s);
+template <typename OUT>
+void launch_mix(const float* xt, const float* prev, const float* mix, OUT* out, int B, int T, int d,
+                cudaStream_t s);
+template <typename OUT>
+void launch_tanh(const float* x, OUT* out, size_t n, cudaStream_t s);
+void launch_timemix_post(const float* k, const float* lw, const float* la, const float* lg,
+                         const float* w0, const float* a0, const float* k_k, const float* k_a,
+                         float* w_raw, float* k_adj, float* a_op, float* b_op, float* g, int rows,
+                         int H, int N, cudaStream_t s);
+template <typename OUT>
+void launch_silu_mul(const float* ig, OUT* out, int rows, int F, cudaStream_t s);
+void launch_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s);
+
+yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const float* v,
+                           const float* a, const float* b, const float* s0, float* y, float* s_out,
+                           float* ckpt, float* sa, int B, int T, int H, int N, bool compat,
+                           cudaStream_t stream);
+yuf_status_t wkv7_decode_dispatch(const float* r, const float* w, const float* k, const float* v,
+                                  const float* a, const float* b, const float* s0, float* y,
+                                  float* s_out, int BH, int N, cudaStream_t stream);
+// ROSA scan over inputs with row stride `ld` (elements between tokens) and
+// optional per-channel biases added to cand/write/gate before the activations.
+yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const float* gate,
+                                  const float* bias_c, const float* bias_w, const float* bias_g,
+                                  int ld, const float* decay_raw, const float* dir_raw,
+                                  const float* m0, float* read, float* m_out, int B, int T, int R,
+                                  cudaStream_t stream);
+
+}  // namespace yuf

@@ -57,7 +57,9 @@ __global__ void __launch_bounds__(MAXT)
                      const float* __restrict__ dir, const float* m0, float* __restrict__ read,
                      float* m_out, float* __restrict__ cand_saved, float* __restrict__ write_saved,
                      float* __restrict__ read_saved, float* __restrict__ gate_saved,
-                     float* __restrict__ decay_saved, float* __restrict__ mem_saved, int T, int R) {
+                     float* __restrict__ decay_saved, float* __restrict__ mem_saved, int T, int R,
+                     int ld, const float* __restrict__ bias_c, const float* __restrict__ bias_w,
+                     const float* __restrict__ bias_g, int raw_params) {
   constexpr int L = ROSA_L;
   __shared__ float scratch[32 * (L + 1)];
   __shared__ float s_sum[L + 1];
@@ -68,8 +70,19 @@ __global__ void __launch_bounds__(MAXT)
   const int j = threadIdx.x;
   const int nwarps = blockDim.x >> 5;
   const bool act = j < R;
-  const float d = act ? dir[j] : 0.f;
-  const float dec = act ? decay[j] : 0.f;
+  float d = act ? dir[j] : 0.f;
+  float dec = act ? decay[j] : 0.f;
+  if (raw_params) {
+    // engine path: decay = sigmoid(decay_param), d = normalize(householder)
+    // (yufmusicgen/model.py:300-301)
+    dec = act ? 1.f / (1.f + expf(-dec)) : 0.f;
+    float x1[1] = {d * d};
+    block_sum_array<1>(x1, scratch, c_sum, nwarps);
+    d = d / fmaxf(sqrtf(c_sum[0]), 1e-12f);
+  }
+  const float bc = (act && bias_c) ? bias_c[j] : 0.f;
+  const float bw = (act && bias_w) ? bias_w[j] : 0.f;
+  const float bg = (act && bias_g) ? bias_g[j] : 0.f;
 
   // c_k = sum_j d_j^2 decay_j^k, k = 1..L (index 0 unused).
   {
@@ -94,9 +107,13 @@ __global__ void __launch_bounds__(MAXT)
     }
   }
   __syncthreads();
+  float qr[L + 1];
+#pragma unroll
+  for (int n = 0; n <= L; ++n) qr[n] = q[n];
 
   float m = act ? m0[(size_t)bb * R + j] : 0.f;
-  const size_t base = (size_t)bb * T * R + j;
+  const size_t base = (size_t)bb * T * R + j;            // output [B, T, R]
+  const size_t base_in = (size_t)bb * T * ld + j;        // inputs: row stride ld
   if (COMPAT && act) mem_saved[(size_t)bb * (T + 1) * R + j] = m;
 
   float cc[L], ww[L], gg[L];
@@ -104,10 +121,10 @@ __global__ void __launch_bounds__(MAXT)
 #pragma unroll
     for (int t = 0; t < L; ++t) {
       const bool ok = act && (t0 + t < T);
-      const size_t o = base + (size_t)(t0 + t) * R;
-      c_[t] = ok ? cand[o] : 0.f;
-      w_[t] = ok ? write[o] : 0.f;
-      g_[t] = (ok && (GATED || COMPAT)) ? gate[o] : 0.f;
+      const size_t o = base_in + (size_t)(t0 + t) * ld;
+      c_[t] = ok ? cand[o] + bc : 0.f;
+      w_[t] = ok ? write[o] + bw : 0.f;
+      g_[t] = (ok && (GATED || COMPAT)) ? gate[o] + bg : 0.f;
     }
   };
   if (T > 0) load(0, cc, ww, gg);
@@ -142,12 +159,14 @@ __global__ void __launch_bounds__(MAXT)
     // 2. all L+1 projections s_t = d . e_t in one block reduction.
     block_sum_array<L + 1>(x, scratch, s_sum, nwarps);
     // 3. p_{t+1} = sum_{tau <= t} q_{t-tau} s_tau  (p index shifted by one).
-    float p[L + 1];
+    float p[L + 1], sv[L + 1];
+#pragma unroll
+    for (int t = 0; t <= L; ++t) sv[t] = s_sum[t];
 #pragma unroll
     for (int t = 0; t <= L; ++t) {
       float acc = 0.f;
 #pragma unroll
-      for (int tau = 0; tau <= t; ++tau) acc = fmaf(q[t - tau], s_sum[tau], acc);
+      for (int tau = 0; tau <= t; ++tau) acc = fmaf(qr[t - tau], sv[tau], acc);
       p[t] = acc;
     }
     // 4. correction, memory and read.
@@ -190,10 +209,12 @@ static yuf_status_t launch_rosa(const float* cand, const float* write, const flo
   const int threads = ((R + 31) / 32) * 32;
   if (threads <= 256)
     rosa_scan_kernel<GATED, COMPAT, 256><<<B, threads, 0, stream>>>(
-        cand, write, gate, decay, dir, m0, read, m_out, cs, ws, rs, gs, ds, ms, T, R);
+        cand, write, gate, decay, dir, m0, read, m_out, cs, ws, rs, gs, ds, ms, T, R, R, nullptr,
+        nullptr, nullptr, 0);
   else
     rosa_scan_kernel<GATED, COMPAT, 1024><<<B, threads, 0, stream>>>(
-        cand, write, gate, decay, dir, m0, read, m_out, cs, ws, rs, gs, ds, ms, T, R);
+        cand, write, gate, decay, dir, m0, read, m_out, cs, ws, rs, gs, ds, ms, T, R, R, nullptr,
+        nullptr, nullptr, 0);
   return check_launch("rosa_scan_kernel");
 }
 
@@ -213,6 +234,23 @@ yuf_status_t rosa_compat_dispatch(const float* cand, const float* write, const f
                                   float* ms, int B, int T, int R, cudaStream_t stream) {
   return launch_rosa<false, true>(cand, write, gate, decay, dir, m0, read, m_out, cs, ws, rs, gs, ds,
                                   ms, B, T, R, stream);
+}
+
+yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const float* gate,
+                                  const float* bias_c, const float* bias_w, const float* bias_g,
+                                  int ld, const float* decay_raw, const float* dir_raw,
+                                  const float* m0, float* read, float* m_out, int B, int T, int R,
+                                  cudaStream_t stream) {
+  const int threads = ((R + 31) / 32) * 32;
+  if (threads <= 256)
+    rosa_scan_kernel<true, false, 256><<<B, threads, 0, stream>>>(
+        cand, write, gate, decay_raw, dir_raw, m0, read, m_out, nullptr, nullptr, nullptr, nullptr,
+        nullptr, nullptr, T, R, ld, bias_c, bias_w, bias_g, 1);
+  else
+    rosa_scan_kernel<true, false, 1024><<<B, threads, 0, stream>>>(
+        cand, write, gate, decay_raw, dir_raw, m0, read, m_out, nullptr, nullptr, nullptr, nullptr,
+        nullptr, nullptr, T, R, ld, bias_c, bias_w, bias_g, 1);
+  return check_launch("rosa_scan_kernel");
 }
 
 }  // namespace yuf

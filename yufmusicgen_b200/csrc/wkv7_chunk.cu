@@ -39,7 +39,7 @@ struct ChunkCfg {
   static constexpr int G = (N == 40) ? 3 : (N == 16 ? 2 : 4);
   static constexpr int C0 = (N + G - 1) / G;
   static constexpr int C = (C0 + 1) / 2 * 2;   // columns per lane (even: float2 math)
-  static constexpr int CS = (C + 3) / 4 * 4;   // lane stride in shared memory (float4 loads)
+  static constexpr int CS = conflict_free_stride(C, G);  // lane stride in shared memory
   static constexpr int VP = G * CS;            // padded vector length
   static constexpr int RPW = 32 / G;           // rows per warp
   static constexpr int NWARPS = (N + RPW - 1) / RPW;

@@ -52,7 +52,8 @@ def wkv7_forward(r, w, k, v, a, b, state=None, out=None, state_out=None, algo=AL
 
     ``state`` is the [B,H,N,N] initial state or None (zeros).  ``state_out``
     may be ``state`` itself (updated in place).  ``algo`` picks the sequential
-    (decode) or chunked (prefill) kernel; AUTO uses chunked for T >= 16."""
+    (token by token) or chunked kernel; AUTO uses the single-token decode
+    kernel for T == 1 and the sequential kernel otherwise."""
     _validate((r, w, k, v, a, b))
     B, T, H, N = r.shape
     if state is not None:
