@@ -148,6 +148,9 @@ static yuf_status_t gemm(yuf_model* m, const void* A, int lda, long long sA, con
   // the fp32 products as BF16x9 on the tensor cores with fp32-level accuracy.
   const cublasComputeType_t ct = CUBLAS_COMPUTE_32F;
   Y_BLAS(cublasSetStream(m->blas, s));
+  // cublasSetStream resets the handle to cuBLAS's own workspace pool; point it
+  // back at the model's preallocated workspace so no GEMM allocates.
+  Y_BLAS(cublasSetWorkspace(m->blas, m->blas_ws->p, m->blas_ws->bytes));
   if (batch == 1) {
     Y_BLAS(cublasGemmEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, &alpha, W, ty, K, A, ty, lda,
                         &beta, C, CUDA_R_32F, ldc, ct, CUBLAS_GEMM_DEFAULT));
