@@ -159,6 +159,22 @@ yuf_status_t yuf_prefill(yuf_model* model, const int32_t* ids, int B, int T, int
  * [slot0, slot0 + B), logits [B,V] (YufMusicGen.step, model.py:424-431). */
 yuf_status_t yuf_step(yuf_model* model, const int32_t* ids, int B, int slot0, float* logits,
                       void* stream);
+/* Decode step that allocates nothing (no counterpart in the reference).
+ * Same inputs, outputs and results as yuf_step, for callers that may not
+ * allocate device memory at call time -- e.g. a real-time audio callback in a
+ * host application, where cudaMalloc's implicit synchronisation and latency
+ * are not allowed, or a component handed a fixed device-memory budget.  Its
+ * working memory is a fixed 8 MiB array compiled into this library (held on
+ * every GPU that loads the library until exit) instead of the model's
+ * grow-on-demand workspace; B larger than that array allows is rejected with
+ * YUF_ERR_INVALID_ARGUMENT and a message giving the largest B for the model.
+ * The first call on a device looks up the array's device address, so make
+ * that first call before any stream capture.  All calls share the one array:
+ * calls whose work overlaps on the GPU (other streams, other threads) race and
+ * must be serialised by the caller.  Nothing in the array needs clearing
+ * between calls.  Parity dumps (yuf_model_set_debug) must be off. */
+yuf_status_t yuf_step_static(yuf_model* model, const int32_t* ids, int B, int slot0, float* logits,
+                             void* stream);
 /* Synchronise `stream` and report device-side input errors of earlier calls
  * (token id outside [0, vocab)). */
 yuf_status_t yuf_model_sync_check(yuf_model* model, void* stream);

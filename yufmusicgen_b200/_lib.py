@@ -35,6 +35,7 @@ SIGNATURES = {
     "yuf_state_import": [P, I, I, I, P, P, P, P],
     "yuf_prefill": [P, P, I, I, I, P, P, P],
     "yuf_step": [P, P, I, I, P, P],
+    "yuf_step_static": [P, P, I, I, P, P],
     "yuf_model_sync_check": [P, P],
     "yuf_model_set_debug": [P, I],
     "yuf_debug_dump": [P, ctypes.c_char_p, I, P, ctypes.c_size_t, P],

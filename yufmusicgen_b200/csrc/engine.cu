@@ -176,12 +176,16 @@ static size_t ws_floats_per_row(const yuf_model* m) {
          8 * d /*ig*/ + 4 * d /*h*/;
 }
 
-static yuf_status_t ensure_ws(yuf_model* m, size_t rows) {
-  if (rows <= m->ws_rows) return YUF_OK;
+static size_t ws_bytes(const yuf_model* m, size_t rows) {
   const size_t per = ws_floats_per_row(m);
   const size_t bf_elems = rows * (size_t)std::max(6 * m->d(), m->R());
+  return rows * per * sizeof(float) + bf_elems * sizeof(__nv_bfloat16) + 256;
+}
+
+static yuf_status_t ensure_ws(yuf_model* m, size_t rows) {
+  if (rows <= m->ws_rows) return YUF_OK;
   auto b = std::make_unique<DevBuf>();
-  const size_t bytes = rows * per * sizeof(float) + bf_elems * sizeof(__nv_bfloat16) + 256;
+  const size_t bytes = ws_bytes(m, rows);
   Y_CUDA(cudaMalloc(&b->p, bytes));
   b->bytes = bytes;
   m->ws = std::move(b);
@@ -189,8 +193,8 @@ static yuf_status_t ensure_ws(yuf_model* m, size_t rows) {
   return YUF_OK;
 }
 
-static WS carve(yuf_model* m, size_t rows) {
-  float* p = static_cast<float*>(m->ws->p);
+static WS carve(yuf_model* m, size_t rows, void* base) {
+  float* p = static_cast<float*>(base);
   const size_t d = m->d(), lr = m->lr(), R = m->R();
   WS w;
   auto take = [&](size_t n) { float* q = p; p += n; return q; };
@@ -236,12 +240,18 @@ static void dump(yuf_model* m, const char* region, int layer, const float* dev, 
 }
 
 // One forward over B sequences x T tokens (rows = B*T), state slots [slot0, slot0+B).
+// ws_base: workspace to carve the row buffers from; nullptr = the model's own
+// (grown on demand).
 static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int slot0,
-                            float* logits_last, float* logits_all, cudaStream_t s) {
+                            float* logits_last, float* logits_all, cudaStream_t s,
+                            void* ws_base = nullptr) {
   const size_t rows = (size_t)B * T;
   const int d = m->d(), H = m->H(), N = m->N(), R = m->R(), lr = m->lr(), V = m->V();
-  Y_TRY(ensure_ws(m, rows));
-  WS w = carve(m, rows);
+  if (ws_base == nullptr) {
+    Y_TRY(ensure_ws(m, rows));
+    ws_base = m->ws->p;
+  }
+  WS w = carve(m, rows, ws_base);
   launch_embed(ids, m->emb, w.x, (int)rows, d, V, m->d_err, s);
   const size_t RD = rows * d;
   for (int li = 0; li < m->cfg.n_layers; ++li) {
@@ -649,3 +659,66 @@ yuf_status_t yuf_debug_dump(yuf_model* m, const char* region, int layer, float* 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode step (yuf_step_static).
+//
+// Some callers may not allocate device memory at all: code running in a host
+// application's real-time callback (an audio plug-in rendering the next notes,
+// where cudaMalloc's implicit device synchronisation and unbounded latency are
+// not allowed), or code living inside a process that hands it a fixed device
+// memory budget up front.  yuf_step_static serves them: its per-call working
+// memory comes from the fixed array below instead of the model's grow-on-demand
+// workspace, so a call allocates nothing (the model, its weights, its state
+// slots and the cuBLAS workspace were all allocated when the model was built).
+//
+// The array is a file-scope __device__ object: every GPU that loads this library
+// holds it (YUF_STATIC_SCRATCH_BYTES) until the process exits.  Host code cannot
+// use its name as a device address, so the first call on each device looks the
+// address up with cudaGetSymbolAddress (with that device current) and caches it.
+namespace yuf {
+constexpr size_t YUF_STATIC_SCRATCH_BYTES = 8u << 20;  // 8 MiB
+}  // namespace yuf
+static __device__ __align__(256) unsigned char g_step_scratch[yuf::YUF_STATIC_SCRATCH_BYTES];
+
+#include <mutex>
+static std::mutex g_scratch_mu;
+static void* g_scratch_addr[128] = {};
+
+extern "C" yuf_status_t yuf_step_static(yuf_model* m, const int32_t* ids, int B, int slot0,
+                                        float* logits, void* stream) {
+  Y_REQUIRE(m, "step_static: null model");
+  Y_REQUIRE(B >= 1 && ids && logits, "step_static: need B >= 1, ids and logits");
+  const size_t need = ws_bytes(m, (size_t)B);
+  if (need > YUF_STATIC_SCRATCH_BYTES) {
+    size_t max_b = 0;
+    while (ws_bytes(m, max_b + 1) <= YUF_STATIC_SCRATCH_BYTES) ++max_b;
+    set_error("step_static: %d sequences need %zu bytes of scratch; the fixed scratch holds %zu "
+              "bytes (at most %zu sequences for this model)",
+              B, need, (size_t)YUF_STATIC_SCRATCH_BYTES, max_b);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  Y_REQUIRE(!m->debug, "step_static: parity dumps copy to host buffers; disable debug first");
+  Y_REQUIRE(m->n_slots > 0, "step_static: call yuf_state_alloc first");
+  Y_REQUIRE(slot0 >= 0 && slot0 + B <= m->n_slots, "step_static: slots [%d, %d) out of range (%d slots)",
+            slot0, slot0 + B, m->n_slots);
+  Y_REQUIRE(m->device >= 0 && m->device < 128, "step_static: device %d out of range", m->device);
+  Y_CUDA(cudaSetDevice(m->device));
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_scratch_addr[m->device] == nullptr) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_step_scratch);
+      if (e != cudaSuccess || p == nullptr) {
+        set_error("step_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        return YUF_ERR_CUDA;
+      }
+      g_scratch_addr[m->device] = p;
+    }
+    base = g_scratch_addr[m->device];
+  }
+  // Every scratch region is written before it is read within the step, so
+  // nothing has to be cleared between calls.
+  return forward(m, ids, B, 1, slot0, logits, nullptr, static_cast<cudaStream_t>(stream), base);
+}
