@@ -160,6 +160,9 @@ def measure_extras(dev, stream, args):
     ms = _time(lambda: cuda_ops.wkv7_forward(*(d[k] for k in "rwkvab"), None, out=y, state_out=s,
                                              algo=cuda_ops.ALGO_SEQUENTIAL), n, dev, stream)
     out["wkv7_sequential_config2"] = {"ms": ms, "GBps": ALGO_BYTES / ms / 1e6}
+    ms = _time(lambda: cuda_ops.wkv7_forward(*(d[k] for k in "rwkvab"), None, out=y, state_out=s,
+                                             algo=cuda_ops.ALGO_CHUNKED), n, dev, stream)
+    out["wkv7_chunked16_config2"] = {"ms": ms, "GBps": ALGO_BYTES / ms / 1e6}
     del d, y, s
     # batched decode step: config-4 state shape (256 seqs x 16 heads x N40), T = 1
     Bd = 256
@@ -183,7 +186,59 @@ def measure_extras(dev, stream, args):
     rbytes = 4 * 2 * T * 128 * 4
     out["rosa_scan_B2_T2048_R128"] = {"ms": ms, "GBps": rbytes / ms / 1e6,
                                       "tokens_per_s": 2 * T / (ms * 1e-3)}
+    del rd, ro, mo
+    out.update(measure_model(dev, stream))
     return out
+
+
+def measure_model(dev, stream):
+    """The 0.1B model (benchmark config 3/4 shapes) through the engine:
+    prefill tokens/s (B2 x T2048) in fp32 and bf16-weight mode, and batched
+    greedy decode tokens/s (256 sequences, 64-token prompts, config 4's batch)."""
+    import torch
+
+    from yufmusicgen_b200 import config as C
+    from yufmusicgen_b200.engine import Engine
+    from yufmusicgen_b200.weights import init_weights
+    from yufmusicgen_b200.workloads import zipf_ids
+
+    cfg = C.ModelConfig(**C.BASE_0P1B)
+    w = init_weights(cfg, 1, "baseline")
+    res = {}
+    ids = torch.as_tensor(zipf_ids(2, 2048, seed=1, vocab=cfg.vocab_size), dtype=torch.int32, device=dev)
+    for prec in ("fp32", "bf16"):
+        eng = Engine(cfg, w, precision=prec, device=dev.index, n_slots=2)
+        last = torch.empty(2, cfg.vocab_size, device=dev)
+
+        def pf():
+            eng.reset_state(0, 2)
+            eng.prefill(ids, slot0=0, out_last=last)
+
+        ms = _time(pf, 3, dev, stream, warm=1)
+        res[f"prefill_0p1b_B2_T2048_{prec}"] = {"ms": ms, "tokens_per_s": 2 * 2048 / (ms * 1e-3)}
+        eng.close()
+        del eng
+    # batched decode, config 4 shape: 256 sequences, 64-token byte prompts
+    Bd, steps = 256, 32
+    for prec in ("fp32", "bf16"):
+        eng = Engine(cfg, w, precision=prec, device=dev.index, n_slots=Bd)
+        prompt = torch.as_tensor(zipf_ids(Bd, 64, seed=4, vocab=cfg.vocab_size), dtype=torch.int32,
+                                 device=dev)
+        logits = eng.prefill(prompt)
+        tok = torch.argmax(logits, dim=-1).to(torch.int32)
+        out_l = torch.empty(Bd, cfg.vocab_size, device=dev)
+
+        def dec():
+            nonlocal tok
+            eng.step(tok, out=out_l)
+            tok = torch.argmax(out_l, dim=-1).to(torch.int32)
+
+        ms = _time(dec, steps, dev, stream, warm=2)
+        res[f"decode_0p1b_B256_{prec}"] = {"ms_per_step": ms, "tokens_per_s": Bd / (ms * 1e-3),
+                                           "sampler": "greedy argmax on device"}
+        eng.close()
+        del eng
+    return res
 
 
 def run_ours(args):
@@ -285,7 +340,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "wkv7_scan_kernel<40>",
+                         "kernel": "wkv7_scan_kernel<40,0,false> (sequential; AUTO for B*H = 128)",
                          "algorithmic_bytes_per_launch": ALGO_BYTES},
             "gpu_launches": args.steps,
             "clocks": clocks.summary(),

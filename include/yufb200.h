@@ -58,9 +58,13 @@ yuf_status_t yuf_wkv7_forward(const float* r, const float* w, const float* k, co
 
 /* Algorithm choice for yuf_wkv7_forward_ex. */
 enum {
-  YUF_WKV_AUTO = 0,       /* single-token kernel for T == 1, else sequential */
-  YUF_WKV_SEQUENTIAL = 1, /* token-by-token (the decode step)                */
-  YUF_WKV_CHUNKED = 2     /* 16-token chunks, no per-token reduction chain   */
+  YUF_WKV_AUTO = 0,       /* T == 1: single-token kernel; T >= 256 and B*H <= 96: time-parallel;
+                             else sequential                                                    */
+  YUF_WKV_SEQUENTIAL = 1, /* token by token, one CTA per (sequence, head)                         */
+  YUF_WKV_CHUNKED = 2,    /* 16-token chunks, no per-token reduction chain                        */
+  YUF_WKV_PARALLEL = 3    /* 128-token chunks scanned in parallel, states carried between them;
+                             allocates stream-ordered scratch (cudaMallocAsync) for the chunk
+                             transitions; T >= 256                                                 */
 };
 /* yuf_wkv7_forward with an explicit algorithm (same results to fp32 rounding). */
 yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k, const float* v,

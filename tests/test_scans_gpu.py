@@ -222,3 +222,40 @@ def test_torch_op_drop_in_rosa_forward():
     _, m_half = np_rosa(*(ins[k][:, :20] if ins[k].ndim == 3 else ins[k]
                           for k in ("cand", "write", "read_gate", "decay", "direction", "m0")))
     close(mem_saved[:, 20], m_half)
+
+
+@pytest.mark.parametrize("T", [256, 300, 1000])
+@pytest.mark.parametrize("N", [16, 40, 64, 128])
+def test_wkv7_time_parallel_matches_oracle(T, N):
+    """128-token chunks scanned in parallel with carried states (incl. a tail)."""
+    ins = wkv_op_inputs(2, T, 3, N, seed=500 + T + N, with_state=True)
+    y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=cu(ins["s0"]),
+                                 algo=cuda_ops.ALGO_PARALLEL)
+    yr, sr = cref.wkv7_scan(*(ins[k] for k in "rwkvab"), ins["s0"])
+    close(y, yr)
+    close(s, sr)
+
+
+def test_wkv7_time_parallel_full_config2_and_inplace_state():
+    ins = wkv_op_inputs(8, 2048, 16, 40, seed=0, with_state=True)
+    st = cu(ins["s0"])
+    y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=st, state_out=st,
+                                 algo=cuda_ops.ALGO_PARALLEL)
+    yr, sr = cref.wkv7_scan(*(ins[k] for k in "rwkvab"), ins["s0"])
+    close(y, yr)
+    close(st, sr)
+
+
+@pytest.mark.parametrize("B,T,R", [(1, 1024, 128), (2, 2048, 128), (3, 512, 100), (4, 256, 32), (2, 384, 12)])
+def test_rosa_time_parallel_matches_oracle(B, T, R):
+    ins = rosa_op_inputs(B, T, R, seed=B * 1000 + T + R, with_state=True)
+    if R == 128:
+        ins["decay"][:8] = 0.9999  # slow channels stress the carried state
+    args = [cu(ins[k]) for k in ("cand", "write", "read_gate", "decay", "direction", "m0")]
+    read, m = rosa_cuda.rosa_scan(*args, gated=True)
+    rr, mr = cref.rosa_scan(*(ins[k] for k in ("cand", "write", "read_gate", "decay", "direction", "m0")))
+    close(read, rr)
+    close(m, mr)
+    ung, _ = rosa_cuda.rosa_householder_scan(*args)
+    ur, _ = rosa_scan_ungated(*(ins[k] for k in ("cand", "write", "read_gate", "decay", "direction", "m0")))
+    close(ung, ur)

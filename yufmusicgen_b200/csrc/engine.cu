@@ -165,7 +165,7 @@ static yuf_status_t gemm(yuf_model* m, const void* A, int lda, long long sA, con
 // Workspace for `rows` token rows (grown on demand; never shrinks).
 struct WS {
   float *x, *xt, *mixed, *rkv, *lr1, *lr2, *w_raw, *k_adj, *a_op, *b_op, *g, *y, *tmp, *rosa, *read,
-      *ig, *h;
+      *ig, *h, *scan;  // scan: scratch of the time-parallel scans
   __nv_bfloat16* bf;  // bf16 staging of a GEMM input (largest: [rows, 4d] or [6][rows][d])
 };
 
@@ -176,10 +176,26 @@ static size_t ws_floats_per_row(const yuf_model* m) {
          8 * d /*ig*/ + 4 * d /*h*/;
 }
 
+// Scratch of the time-parallel scans for a forward over `rows` token rows.
+static size_t scan_rosa_floats(const yuf_model* m, size_t rows) {
+  const size_t R = m->R();
+  return (R * R + 2 * (rows / 32 + 1) * R + 3) / 4 * 4;  // keep the WKV part 16-byte aligned
+}
+
+static size_t scan_scratch_floats(const yuf_model* m, size_t rows) {
+  const size_t R = m->R(), HNN = (size_t)m->H() * m->N() * m->N();
+  // ROSA: A^K + chunk end/start states (32-token chunks).  WKV: U, P, chunk
+  // start states per 128-token chunk plus one state per sequence; the time-
+  // parallel path runs only for T >= 256, so sequences <= rows / 256.
+  (void)R;
+  return scan_rosa_floats(m, rows) + (3 * (rows / 128) + rows / 256 + 1) * HNN + 16;
+}
+
 static size_t ws_bytes(const yuf_model* m, size_t rows) {
   const size_t per = ws_floats_per_row(m);
   const size_t bf_elems = rows * (size_t)std::max(6 * m->d(), m->R());
-  return rows * per * sizeof(float) + bf_elems * sizeof(__nv_bfloat16) + 256;
+  return (rows * per + scan_scratch_floats(m, rows)) * sizeof(float) +
+         bf_elems * sizeof(__nv_bfloat16) + 512;
 }
 
 static yuf_status_t ensure_ws(yuf_model* m, size_t rows) {
@@ -215,6 +231,11 @@ static WS carve(yuf_model* m, size_t rows, void* base) {
   w.read = take(rows * R);
   w.ig = take(rows * 8 * d);
   w.h = take(rows * 4 * d);
+  {  // 16-byte alignment for the scans' cp.async / float4 accesses
+    uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    p = reinterpret_cast<float*>((a + 15) & ~uintptr_t(15));
+  }
+  w.scan = take(scan_scratch_floats(m, rows));
   uintptr_t u = reinterpret_cast<uintptr_t>(p);
   u = (u + 255) & ~uintptr_t(255);
   w.bf = reinterpret_cast<__nv_bfloat16*>(u);
@@ -280,6 +301,9 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     if (T == 1)
       Y_TRY(wkv7_decode_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S,
                                  B * H, N, s));
+    else if (wkv7_parallel_applies(B, T, H))
+      Y_TRY(wkv7_parallel(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, B, T, H,
+                          N, w.scan + scan_rosa_floats(m, rows), s));
     else
       Y_TRY(wkv7_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, nullptr,
                           nullptr, B, T, H, N, false, s));
@@ -303,7 +327,7 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
                3 * R, d, 0.f, 1, s));
     Y_TRY(rosa_engine_dispatch(w.rosa, w.rosa + R, w.rosa + 2 * R, Lw.b_rosa, Lw.b_rosa + R,
                                Lw.b_rosa + 2 * R, 3 * R, Lw.decay, Lw.householder, mem, w.read, mem, B,
-                               T, R, s));
+                               T, R, w.scan, s));
     if (m->debug) dump(m, "read", li, w.read, rows * R, s);
     Y_TRY(gemm(m, gemm_input(m, w, w.read, rows * R, s), R, 0, Lw.W_rosa_out, 0, w.x, d, 0, (int)rows, d,
                R, 1.f, 1, s));

@@ -38,6 +38,19 @@ yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const f
                                   const float* bias_c, const float* bias_w, const float* bias_g,
                                   int ld, const float* decay_raw, const float* dir_raw,
                                   const float* m0, float* read, float* m_out, int B, int T, int R,
-                                  cudaStream_t stream);
+                                  float* scratch, cudaStream_t stream);
+// floats of scratch the time-parallel ROSA scan needs (0 if it does not apply)
+size_t rosa_parallel_scratch_floats(int B, int T, int R);
+bool rosa_parallel_applies(int B, int T, int R);
 
+}  // namespace yuf
+
+namespace yuf {
+// Time-parallel WKV-7 prefill (wkv7_parallel.cu): applies for T >= 256; scratch
+// holds wkv7_parallel_scratch_floats() floats, 16-byte aligned.
+bool wkv7_parallel_applies(int B, int T, int H);
+size_t wkv7_parallel_scratch_floats(int B, int T, int H, int N);
+yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const float* v,
+                           const float* a, const float* b, const float* s0, float* y, float* s_out,
+                           int B, int T, int H, int N, float* scratch, cudaStream_t st);
 }  // namespace yuf

@@ -29,6 +29,13 @@ namespace yuf {
 
 constexpr int ROSA_L = 16;
 
+bool rosa_parallel_applies(int B, int T, int R);
+yuf_status_t rosa_parallel(const float* cand, const float* write, const float* gate,
+                           const float* bias_c, const float* bias_w, const float* bias_g, int ld,
+                           const float* decay, const float* dir, int raw, const float* m0,
+                           float* read, float* m_out, int B, int T, int R, bool gated,
+                           float* scratch, cudaStream_t s);
+
 // Sum each of V per-thread values over the block; every thread receives all V
 // sums in out[] (shared).  scratch holds nwarps * V floats.
 template <int V>
@@ -50,7 +57,11 @@ YUF_DEVICE void block_sum_array(const float (&x)[V], float* scratch, float* out,
   __syncthreads();
 }
 
-template <bool GATED, bool COMPAT, int MAXT>
+// MODE 0: the scan.  MODE 1: end state only, from a zero initial state (no read
+// output).  MODE 2: transition -- batch row bb starts from the unit vector e_bb
+// with zero input for T steps, so m_out row bb = A^T e_bb, i.e. column bb of
+// A^T (A the one-step transition, A^T its T-th power).
+template <bool GATED, bool COMPAT, int MAXT, int MODE = 0>
 __global__ void __launch_bounds__(MAXT)
     rosa_scan_kernel(const float* __restrict__ cand, const float* __restrict__ write,
                      const float* __restrict__ gate, const float* __restrict__ decay,
@@ -111,7 +122,8 @@ __global__ void __launch_bounds__(MAXT)
 #pragma unroll
   for (int n = 0; n <= L; ++n) qr[n] = q[n];
 
-  float m = act ? m0[(size_t)bb * R + j] : 0.f;
+  float m = (MODE == 2) ? ((act && j == bb) ? 1.f : 0.f)
+                        : ((MODE == 1 || !act) ? 0.f : m0[(size_t)bb * R + j]);
   const size_t base = (size_t)bb * T * R + j;            // output [B, T, R]
   const size_t base_in = (size_t)bb * T * ld + j;        // inputs: row stride ld
   if (COMPAT && act) mem_saved[(size_t)bb * (T + 1) * R + j] = m;
@@ -120,7 +132,7 @@ __global__ void __launch_bounds__(MAXT)
   auto load = [&](int t0, float (&c_)[L], float (&w_)[L], float (&g_)[L]) {
 #pragma unroll
     for (int t = 0; t < L; ++t) {
-      const bool ok = act && (t0 + t < T);
+      const bool ok = act && (t0 + t < T) && MODE != 2;
       const size_t o = base_in + (size_t)(t0 + t) * ld;
       c_[t] = ok ? cand[o] + bc : 0.f;
       w_[t] = ok ? write[o] + bw : 0.f;
@@ -177,7 +189,7 @@ __global__ void __launch_bounds__(MAXT)
         gc = dec * fmaf(p[t], d, gc);
         const float mt = fmaf(-2.f, gc, e[t + 1]);
         const float rd = fmaf(-2.f * p[t + 1], d, mt);
-        if (act) {
+        if (act && MODE == 0) {
           const size_t o = base + (size_t)(t0 + t) * R;
           if constexpr (COMPAT) {
             read[o] = rd;
@@ -218,9 +230,25 @@ static yuf_status_t launch_rosa(const float* cand, const float* write, const flo
   return check_launch("rosa_scan_kernel");
 }
 
+size_t rosa_parallel_scratch_floats(int B, int T, int R);
+
 yuf_status_t rosa_dispatch(const float* cand, const float* write, const float* gate,
                            const float* decay, const float* dir, const float* m0, float* read,
                            float* m_out, int B, int T, int R, bool gated, cudaStream_t stream) {
+  if (rosa_parallel_applies(B, T, R)) {
+    // stream-ordered scratch: freed on the stream right after use
+    float* scratch = nullptr;
+    const size_t bytes = rosa_parallel_scratch_floats(B, T, R) * sizeof(float);
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, stream);
+    if (e != cudaSuccess) {
+      set_error("rosa: scratch allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+      return YUF_ERR_OUT_OF_MEMORY;
+    }
+    yuf_status_t st = rosa_parallel(cand, write, gate, nullptr, nullptr, nullptr, R, decay, dir, 0, m0,
+                                    read, m_out, B, T, R, gated, scratch, stream);
+    cudaFreeAsync(scratch, stream);
+    return st;
+  }
   if (gated)
     return launch_rosa<true, false>(cand, write, gate, decay, dir, m0, read, m_out, nullptr, nullptr,
                                     nullptr, nullptr, nullptr, nullptr, B, T, R, stream);
@@ -240,7 +268,10 @@ yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const f
                                   const float* bias_c, const float* bias_w, const float* bias_g,
                                   int ld, const float* decay_raw, const float* dir_raw,
                                   const float* m0, float* read, float* m_out, int B, int T, int R,
-                                  cudaStream_t stream) {
+                                  float* scratch, cudaStream_t stream) {
+  if (scratch && rosa_parallel_applies(B, T, R))
+    return rosa_parallel(cand, write, gate, bias_c, bias_w, bias_g, ld, decay_raw, dir_raw, 1, m0,
+                         read, m_out, B, T, R, true, scratch, stream);
   const int threads = ((R + 31) / 32) * 32;
   if (threads <= 256)
     rosa_scan_kernel<true, false, 256><<<B, threads, 0, stream>>>(
@@ -251,6 +282,117 @@ yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const f
         cand, write, gate, decay_raw, dir_raw, m0, read, m_out, nullptr, nullptr, nullptr, nullptr,
         nullptr, nullptr, T, R, ld, bias_c, bias_w, bias_g, 1);
   return check_launch("rosa_scan_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Time-parallel ROSA scan.  With few sequences (the 0.1B prefill has B = 2) the
+// one-CTA-per-sequence scan leaves the GPU idle, so the T axis is cut into
+// chunks of K tokens.  The transition A = diag(decay)(I - 2 d d^T) does not
+// depend on the token, hence:
+//   1. A^K: scan R unit vectors for K steps with zero input (MODE 2);
+//   2. every chunk, as its own "sequence", is scanned from a zero state (MODE 1)
+//      giving its end state z_c -- chunks of one sequence are contiguous in
+//      [B, T, R], so the chunk batch is the same tensor viewed as [B*T/K, K, R];
+//   3. per sequence, m_c = A^K m_{c-1} + z_c over the chunks (rosa_carry_kernel);
+//   4. every chunk is scanned again from its true start state (MODE 0).
+// Exact in exact arithmetic (linearity of the recurrence in m).
+constexpr int ROSA_PAR_K = 32;
+
+// One CTA per sequence; A^K (stored transposed: AKt[j][i] = (A^K)[i][j]) in
+// shared memory.
+__global__ void __launch_bounds__(128)
+    rosa_carry_kernel(const float* __restrict__ AKt, const float* __restrict__ z,
+                      const float* m0, float* __restrict__ m_start, float* m_out, int C, int R) {
+  extern __shared__ float sh[];
+  float* A = sh;          // [R][R]
+  float* mv = sh + R * R; // [R]
+  const int b = blockIdx.x, i = threadIdx.x;
+  for (int q = i; q < R * R; q += blockDim.x) A[q] = AKt[q];
+  float m = (i < R && m0) ? m0[(size_t)b * R + i] : 0.f;
+  for (int c = 0; c < C; ++c) {
+    const size_t row = ((size_t)b * C + c) * R;
+    if (i < R) {
+      m_start[row + i] = m;
+      mv[i] = m;
+    }
+    __syncthreads();
+    if (i < R) {
+      float a0 = z[row + i], a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      int j = 0;
+      for (; j + 4 <= R; j += 4) {
+        a0 = fmaf(A[(j + 0) * R + i], mv[j + 0], a0);
+        a1 = fmaf(A[(j + 1) * R + i], mv[j + 1], a1);
+        a2 = fmaf(A[(j + 2) * R + i], mv[j + 2], a2);
+        a3 = fmaf(A[(j + 3) * R + i], mv[j + 3], a3);
+      }
+      for (; j < R; ++j) a0 = fmaf(A[j * R + i], mv[j], a0);
+      m = (a0 + a1) + (a2 + a3);
+    }
+    __syncthreads();
+  }
+  if (i < R && m_out) m_out[(size_t)b * R + i] = m;
+}
+
+template <bool GATED, int MODE>
+static void launch_mode(const float* cand, const float* write, const float* gate,
+                        const float* bias_c, const float* bias_w, const float* bias_g, int ld,
+                        const float* decay, const float* dir, int raw, const float* m0, float* read,
+                        float* m_out, int B, int T, int R, cudaStream_t s) {
+  const int threads = ((R + 31) / 32) * 32;
+  rosa_scan_kernel<GATED, false, 256, MODE><<<B, threads, 0, s>>>(
+      cand, write, gate, decay, dir, m0, read, m_out, nullptr, nullptr, nullptr, nullptr, nullptr,
+      nullptr, T, R, ld, bias_c, bias_w, bias_g, raw);
+}
+
+size_t rosa_parallel_scratch_floats(int B, int T, int R) {
+  const size_t C = (size_t)T / ROSA_PAR_K;
+  return (size_t)R * R + 2 * (size_t)B * C * R;
+}
+
+bool rosa_parallel_applies(int B, int T, int R) {
+  // shared-memory A^K (R <= 128), whole chunks, and enough of them to be worth
+  // the extra passes
+  return R <= 128 && T % ROSA_PAR_K == 0 && T >= 4 * ROSA_PAR_K &&
+         (long long)B * (T / ROSA_PAR_K) >= 16;
+}
+
+// The caller guarantees rosa_parallel_applies(); scratch holds
+// rosa_parallel_scratch_floats() floats.
+yuf_status_t rosa_parallel(const float* cand, const float* write, const float* gate,
+                           const float* bias_c, const float* bias_w, const float* bias_g, int ld,
+                           const float* decay, const float* dir, int raw, const float* m0,
+                           float* read, float* m_out, int B, int T, int R, bool gated,
+                           float* scratch, cudaStream_t s) {
+  constexpr int K = ROSA_PAR_K;
+  const int C = T / K;
+  float* AKt = scratch;
+  float* z = AKt + (size_t)R * R;
+  float* m_start = z + (size_t)B * C * R;
+  // 1. A^K from R unit vectors (inputs unused in MODE 2)
+  launch_mode<false, 2>(cand, write, gate, nullptr, nullptr, nullptr, ld, decay, dir, raw, nullptr,
+                        nullptr, AKt, R, K, R, s);
+  // 2. chunk end states from zero: chunks are the batch, K tokens each
+  launch_mode<false, 1>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, nullptr,
+                        nullptr, z, B * C, K, R, s);
+  // 3. carry across chunks
+  const int threads = ((R + 31) / 32) * 32;
+  const size_t sm = ((size_t)R * R + R) * sizeof(float);
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(rosa_carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) {
+      set_error("rosa: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+      return YUF_ERR_CUDA;
+    }
+  }
+  rosa_carry_kernel<<<B, threads, sm, s>>>(AKt, z, m0, m_start, m_out, C, R);
+  // 4. rescan every chunk from its true start state
+  if (gated)
+    launch_mode<true, 0>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, m_start, read,
+                         nullptr, B * C, K, R, s);
+  else
+    launch_mode<false, 0>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, m_start, read,
+                          nullptr, B * C, K, R, s);
+  return check_launch("rosa parallel scan");
 }
 
 }  // namespace yuf
