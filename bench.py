@@ -199,6 +199,7 @@ def measure_model(dev, stream):
 
     from yufmusicgen_b200 import config as C
     from yufmusicgen_b200.engine import Engine
+    from yufmusicgen_b200.sampler import sample
     from yufmusicgen_b200.weights import init_weights
     from yufmusicgen_b200.workloads import zipf_ids
 
@@ -220,22 +221,28 @@ def measure_model(dev, stream):
         del eng
     # batched decode, config 4 shape: 256 sequences, 64-token byte prompts
     Bd, steps = 256, 32
+    side = torch.cuda.Stream(dev)
     for prec in ("fp32", "bf16"):
+      with torch.cuda.stream(side):
         eng = Engine(cfg, w, precision=prec, device=dev.index, n_slots=Bd)
+        eng.set_decode_graphs(True)
         prompt = torch.as_tensor(zipf_ids(Bd, 64, seed=4, vocab=cfg.vocab_size), dtype=torch.int32,
                                  device=dev)
         logits = eng.prefill(prompt)
         tok = torch.argmax(logits, dim=-1).to(torch.int32)
         out_l = torch.empty(Bd, cfg.vocab_size, device=dev)
 
-        def dec():
-            nonlocal tok
-            eng.step(tok, out=out_l)
-            tok = torch.argmax(out_l, dim=-1).to(torch.int32)
+        step_no = [0]
 
-        ms = _time(dec, steps, dev, stream, warm=2)
+        def dec():
+            eng.step(tok, out=out_l)  # same buffers every step -> one captured graph
+            sample(out_l, seed=1234, step=step_no[0], temperature=1.0, top_k=32, out=tok)
+            step_no[0] += 1
+
+        ms = _time(dec, steps, dev, side, warm=2)
         res[f"decode_0p1b_B256_{prec}"] = {"ms_per_step": ms, "tokens_per_s": Bd / (ms * 1e-3),
-                                           "sampler": "greedy argmax on device"}
+                                           "sampler": "top-k 32, T=1.0, Philox4x32-10 on device",
+                                           "cuda_graph": True}
         eng.close()
         del eng
     return res

@@ -179,6 +179,30 @@ yuf_status_t yuf_step(yuf_model* model, const int32_t* ids, int B, int slot0, fl
  * between calls.  Parity dumps (yuf_model_set_debug) must be off. */
 yuf_status_t yuf_step_static(yuf_model* model, const int32_t* ids, int B, int slot0, float* logits,
                              void* stream);
+/* On-device sampling of one token per sequence from logits [B,V] (device) into
+ * out_ids [B] (device int32), replacing the host-side sample_token of
+ * yufmusicgen/cli/generate.py:45-56 and its masking (generate.py:142-149):
+ * ids below `mask_below` are excluded except `eos_id` when allow_eos != 0;
+ * logits are divided by `temperature` (<= 0: greedy argmax); the `top_k`
+ * (1..1024) most likely tokens are kept, then the top-p cut inside them (a token
+ * is dropped when the mass before it exceeds top_p), then one draw with the
+ * uniform Philox4x32-10(key = seed, counter = (step, seq0 + b, 0)), so results
+ * do not depend on batch layout.  out_uniform [B] (nullable) receives the
+ * uniforms used.  V <= 51200. */
+yuf_status_t yuf_sample(const float* logits, int B, int V, float temperature, int top_k,
+                        float top_p, uint64_t seed, uint64_t step, int seq0, int mask_below,
+                        int eos_id, int allow_eos, int32_t* out_ids, float* out_uniform,
+                        void* stream);
+/* The sampler's uniforms for sequences seq0 .. seq0 + n - 1 at (seed, step). */
+yuf_status_t yuf_philox_uniform(uint64_t seed, uint64_t step, int seq0, int n, float* out,
+                                void* stream);
+
+/* Replay yuf_step as a CUDA graph: the first call for a given (B, slot0, ids,
+ * logits) captures the whole step on the caller's stream, later calls with the
+ * same arguments launch the graph (one launch instead of ~25 per layer).  Only
+ * on a non-NULL stream and with debug dumps off; growing the workspace (a
+ * bigger prefill) drops the captured graphs.  Off by default. */
+yuf_status_t yuf_model_set_decode_graphs(yuf_model* model, int enabled);
 /* Synchronise `stream` and report device-side input errors of earlier calls
  * (token id outside [0, vocab)). */
 yuf_status_t yuf_model_sync_check(yuf_model* model, void* stream);

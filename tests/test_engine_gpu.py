@@ -187,3 +187,30 @@ def test_out_of_range_token_is_reported():
         eng.sync_check()
     eng.sync_check()  # cleared
     eng.close()
+
+
+def test_decode_graph_replay_equals_eager():
+    cfg, w, eng = make(C.TINY, 0, "perturbed", n_slots=4)
+    prompt = torch.as_tensor(tiny_ids(2, 24, seed=8), dtype=torch.int32, device="cuda")
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        eng.prefill(prompt, slot0=0)
+        eng.prefill(prompt, slot0=2)
+        eng.set_decode_graphs(True)
+        ids = torch.tensor([3, 300], dtype=torch.int32, device="cuda")
+        out = torch.empty(2, cfg.vocab_size, device="cuda")
+        got = []
+        for _ in range(5):  # capture once, replay four times (same buffers)
+            eng.step(ids, slot0=0, out=out)
+            got.append(out.clone())
+            ids.copy_(torch.argmax(out, dim=-1).to(torch.int32))
+        eng.set_decode_graphs(False)
+        ids2 = torch.tensor([3, 300], dtype=torch.int32, device="cuda")
+        want = []
+        for _ in range(5):
+            o = eng.step(ids2, slot0=2)
+            want.append(o.clone())
+            ids2 = torch.argmax(o, dim=-1).to(torch.int32)
+    side.synchronize()
+    close(torch.stack(got), torch.stack(want).cpu().numpy(), rtol=1e-6, atol=1e-6)
+    eng.close()

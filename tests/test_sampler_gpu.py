@@ -1,0 +1,73 @@
+"""On-device sampler (yuf_sample): Philox stream, masking, greedy, top-k/top-p
+distribution, batch-layout independence."""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+from oracle.philox import uniform  # noqa: E402
+from yufmusicgen_b200.sampler import philox_uniform, sample, sample_music  # noqa: E402
+
+
+@pytest.mark.parametrize("seed,step,seq0", [(0, 0, 0), (1234567, 3, 10), (2**40 + 17, 2**33 + 5, 100)])
+def test_philox_matches_restatement(seed, step, seq0):
+    got = philox_uniform(seed, step, seq0, 64).cpu().numpy()
+    want = np.array([uniform(seed, step, seq0 + i) for i in range(64)], np.float32)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_greedy_and_topk1_are_argmax_with_mask():
+    g = torch.Generator().manual_seed(0)
+    logits = torch.randn(16, 700, generator=g).cuda()
+    ids = sample(logits, seed=1, step=0, temperature=0.0, mask_below=260, eos_id=2, allow_eos=False)
+    want = torch.argmax(logits[:, 260:], dim=-1) + 260
+    assert torch.equal(ids.long(), want)
+    ids = sample(logits, seed=1, step=0, temperature=1.0, top_k=1)
+    assert torch.equal(ids.long(), torch.argmax(logits, dim=-1))
+
+
+def test_music_mask_and_eos_rule():
+    logits = torch.zeros(4, 600, device="cuda")
+    logits[:, 2] = 50.0  # EOS dominates when allowed
+    logits[:, 5] = 40.0  # a byte token: always masked
+    ids = sample_music(logits, seed=3, step=0, generated=0, top_k=8)
+    assert (ids >= 260).all()
+    ids = sample_music(logits, seed=3, step=0, generated=16, top_k=8)
+    assert (ids == 2).all()
+
+
+def test_topk_topp_distribution():
+    p = np.array([0.4, 0.3, 0.15, 0.1, 0.05], np.float64)
+    base = np.full(64, -30.0, np.float32)
+    base[:5] = np.log(p)
+    rows = torch.from_numpy(np.tile(base, (4000, 1))).cuda()
+    counts = np.zeros(64)
+    for step in range(5):
+        ids = sample(rows, seed=99, step=step, top_k=4, top_p=1.0, seq0=0).cpu().numpy()
+        counts += np.bincount(ids, minlength=64)
+    freq = counts / counts.sum()
+    want = np.zeros(64)
+    want[:4] = p[:4] / p[:4].sum()  # top-k 4, renormalised
+    assert np.abs(freq - want).max() < 0.015
+    # top-p 0.6: keep tokens whose preceding mass <= 0.6 -> {0, 1} (0.4, then 0.7 > 0.6 stops)
+    counts[:] = 0
+    for step in range(5):
+        ids = sample(rows, seed=7, step=step, top_k=5, top_p=0.6).cpu().numpy()
+        counts += np.bincount(ids, minlength=64)
+    freq = counts / counts.sum()
+    want = np.zeros(64)
+    want[:2] = np.array([0.4, 0.3]) / 0.7
+    assert np.abs(freq - want).max() < 0.015
+
+
+def test_draws_depend_on_sequence_id_not_batch_position():
+    g = torch.Generator().manual_seed(5)
+    logits = torch.randn(8, 512, generator=g).cuda()
+    full = sample(logits, seed=11, step=4, top_k=32, seq0=100)
+    part = sample(logits[5:], seed=11, step=4, top_k=32, seq0=105)
+    assert torch.equal(full[5:], part)
+    again = sample(logits, seed=11, step=4, top_k=32, seq0=100)
+    assert torch.equal(full, again)

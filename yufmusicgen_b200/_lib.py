@@ -36,6 +36,10 @@ SIGNATURES = {
     "yuf_prefill": [P, P, I, I, I, P, P, P],
     "yuf_step": [P, P, I, I, P, P],
     "yuf_step_static": [P, P, I, I, P, P],
+    "yuf_model_set_decode_graphs": [P, I],
+    "yuf_sample": [P, I, I, ctypes.c_float, I, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64, I, I,
+                   I, I, P, P, P],
+    "yuf_philox_uniform": [ctypes.c_uint64, ctypes.c_uint64, I, I, P, P],
     "yuf_model_sync_check": [P, P],
     "yuf_model_set_debug": [P, I],
     "yuf_debug_dump": [P, ctypes.c_char_p, I, P, ctypes.c_size_t, P],

@@ -83,6 +83,22 @@ struct yuf_model {
   std::unique_ptr<DevBuf> ws;
   std::unique_ptr<DevBuf> blas_ws;
   int* d_err = nullptr;
+  // decode-step CUDA graphs, keyed by (B, slot0, ids, logits); a workspace
+  // reallocation bumps ws_gen and invalidates them
+  struct DecodeGraph {
+    int B, slot0;
+    const void* ids;
+    const void* logits;
+    size_t ws_gen;
+    cudaGraphExec_t exec;
+  };
+  bool decode_graphs = false;
+  size_t ws_gen = 0;
+  std::vector<DecodeGraph> graphs;
+  void drop_graphs() {
+    for (auto& g : graphs) cudaGraphExecDestroy(g.exec);
+    graphs.clear();
+  }
   // debug dumps: region -> per layer host copies of the last call
   bool debug = false;
   std::map<std::string, std::vector<std::vector<float>>> dumps;
@@ -206,6 +222,8 @@ static yuf_status_t ensure_ws(yuf_model* m, size_t rows) {
   b->bytes = bytes;
   m->ws = std::move(b);
   m->ws_rows = rows;
+  ++m->ws_gen;
+  m->drop_graphs();  // captured graphs point into the old workspace
   return YUF_OK;
 }
 
@@ -551,6 +569,7 @@ yuf_status_t yuf_model_create(const yuf_model_config* cfg, int precision, int de
 yuf_status_t yuf_model_destroy(yuf_model* m) {
   if (!m) return YUF_OK;
   cudaSetDevice(m->device);
+  m->drop_graphs();
   if (m->blas) cublasDestroy(m->blas);
   delete m;
   return YUF_OK;
@@ -642,7 +661,45 @@ yuf_status_t yuf_step(yuf_model* m, const int32_t* ids, int B, int slot0, float*
   Y_REQUIRE(slot0 >= 0 && slot0 + B <= m->n_slots, "step: slots [%d, %d) out of range (%d slots)",
             slot0, slot0 + B, m->n_slots);
   Y_CUDA(cudaSetDevice(m->device));
-  return forward(m, ids, B, 1, slot0, logits, nullptr, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!m->decode_graphs || s == nullptr || m->debug) return forward(m, ids, B, 1, slot0, logits, nullptr, s);
+  // Replay a captured graph of this exact step (same batch, slots and buffers).
+  Y_TRY(ensure_ws(m, (size_t)B));
+  for (auto& g : m->graphs)
+    if (g.B == B && g.slot0 == slot0 && g.ids == ids && g.logits == logits && g.ws_gen == m->ws_gen) {
+      Y_CUDA(cudaGraphLaunch(g.exec, s));
+      return YUF_OK;
+    }
+  cudaGraph_t graph = nullptr;
+  Y_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  yuf_status_t st = forward(m, ids, B, 1, slot0, logits, nullptr, s);
+  cudaError_t e = cudaStreamEndCapture(s, &graph);
+  if (st != YUF_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return st;
+  }
+  if (e != cudaSuccess) {
+    set_error("step: graph capture failed: %s", cudaGetErrorString(e));
+    return YUF_ERR_CUDA;
+  }
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    set_error("step: graph instantiation failed: %s", cudaGetErrorString(e));
+    return YUF_ERR_CUDA;
+  }
+  if (m->graphs.size() >= 64) m->drop_graphs();
+  m->graphs.push_back({B, slot0, ids, logits, m->ws_gen, exec});
+  Y_CUDA(cudaGraphLaunch(exec, s));
+  return YUF_OK;
+}
+
+yuf_status_t yuf_model_set_decode_graphs(yuf_model* m, int enabled) {
+  Y_REQUIRE(m, "null model");
+  m->decode_graphs = enabled != 0;
+  if (!m->decode_graphs) m->drop_graphs();
+  return YUF_OK;
 }
 
 yuf_status_t yuf_model_sync_check(yuf_model* m, void* stream) {

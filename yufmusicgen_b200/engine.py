@@ -136,6 +136,10 @@ class Engine:
             _lib.call("yuf_step", self._h, ids.data_ptr(), B, slot0, logits.data_ptr(), self._stream())
         return logits
 
+    def set_decode_graphs(self, enabled: bool = True):
+        """Replay decode steps as CUDA graphs (needs a non-default stream)."""
+        _lib.call("yuf_model_set_decode_graphs", self._h, 1 if enabled else 0)
+
     def sync_check(self):
         with torch.cuda.device(self.device):
             _lib.call("yuf_model_sync_check", self._h, self._stream())
