@@ -163,6 +163,9 @@ def measure_extras(dev, stream, args):
     ms = _time(lambda: cuda_ops.wkv7_forward(*(d[k] for k in "rwkvab"), None, out=y, state_out=s,
                                              algo=cuda_ops.ALGO_CHUNKED), n, dev, stream)
     out["wkv7_chunked16_config2"] = {"ms": ms, "GBps": ALGO_BYTES / ms / 1e6}
+    ms = _time(lambda: cuda_ops.wkv7_forward(*(d[k] for k in "rwkvab"), None, out=y, state_out=s,
+                                             algo=cuda_ops.ALGO_PARALLEL), n, dev, stream)
+    out["wkv7_time_parallel_config2"] = {"ms": ms, "GBps": ALGO_BYTES / ms / 1e6}
     del d, y, s
     # batched decode step: config-4 state shape (256 seqs x 16 heads x N40), T = 1
     Bd = 256

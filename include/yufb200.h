@@ -58,13 +58,15 @@ yuf_status_t yuf_wkv7_forward(const float* r, const float* w, const float* k, co
 
 /* Algorithm choice for yuf_wkv7_forward_ex. */
 enum {
-  YUF_WKV_AUTO = 0,       /* T == 1: single-token kernel; T >= 256 and B*H <= 96: time-parallel;
+  YUF_WKV_AUTO = 0,       /* T == 1: single-token kernel; T >= 256 and few (sequence, head)
+                             chains (N <= 40: B*H <= a third of the resident pair blocks,
+                             592 on a 148-SM B200; larger N: B*H <= 64): time-parallel;
                              else sequential                                                    */
   YUF_WKV_SEQUENTIAL = 1, /* token by token, one CTA per (sequence, head)                         */
   YUF_WKV_CHUNKED = 2,    /* 16-token chunks, no per-token reduction chain                        */
-  YUF_WKV_PARALLEL = 3    /* 128-token chunks scanned in parallel, states carried between them;
-                             allocates stream-ordered scratch (cudaMallocAsync) for the chunk
-                             transitions; T >= 256                                                 */
+  YUF_WKV_PARALLEL = 3    /* chunks scanned in parallel (about one wave of blocks), states
+                             carried between them; takes stream-ordered scratch for the chunk
+                             transitions from a library-owned pool that keeps its pages; T >= 256 */
 };
 /* yuf_wkv7_forward with an explicit algorithm (same results to fp32 rounding). */
 yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k, const float* v,

@@ -227,11 +227,29 @@ def test_torch_op_drop_in_rosa_forward():
 @pytest.mark.parametrize("T", [256, 300, 1000])
 @pytest.mark.parametrize("N", [16, 40, 64, 128])
 def test_wkv7_time_parallel_matches_oracle(T, N):
-    """128-token chunks scanned in parallel with carried states (incl. a tail)."""
+    """Chunks scanned in parallel with carried states (the last chunk ragged)."""
     ins = wkv_op_inputs(2, T, 3, N, seed=500 + T + N, with_state=True)
     y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=cu(ins["s0"]),
                                  algo=cuda_ops.ALGO_PARALLEL)
     yr, sr = cref.wkv7_scan(*(ins[k] for k in "rwkvab"), ins["s0"])
+    close(y, yr)
+    close(s, sr)
+
+
+@pytest.mark.parametrize("B,T,H,N,with_state", [
+    (2, 257, 3, 40, False),   # zero start: chunk 0 skips the correction; short last chunk
+    (1, 520, 2, 32, True),
+    (4, 300, 2, 48, False),
+    (2, 1000, 2, 96, True),
+    (1, 777, 1, 16, True),
+    (40, 256, 16, 40, True),  # many chains: two chunks per sequence
+])
+def test_wkv7_time_parallel_shapes(B, T, H, N, with_state):
+    ins = wkv_op_inputs(B, T, H, N, seed=900 + B + T + N, with_state=with_state)
+    s0 = cu(ins["s0"]) if with_state else None
+    y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=s0,
+                                 algo=cuda_ops.ALGO_PARALLEL)
+    yr, sr = cref.wkv7_scan(*(ins[k] for k in "rwkvab"), ins["s0"] if with_state else None)
     close(y, yr)
     close(s, sr)
 

@@ -4,6 +4,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 
 #include "model_kernels.cuh"
 
@@ -25,6 +26,41 @@ yuf_status_t check_launch(const char* what) {
     return YUF_ERR_CUDA;
   }
   return YUF_OK;
+}
+
+// Scratch of the raw ops comes from a memory pool of this library's own, one
+// per device, that keeps freed blocks (release threshold = max): a call that
+// needs the same size as the previous one reuses its pages instead of mapping
+// new ones, and the process's default pool keeps its own settings.
+static std::mutex g_pool_mu;
+static cudaMemPool_t g_pools[64] = {};
+
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  cudaMemPool_t pool;
+  {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if (!g_pools[dev]) {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      e = cudaMemPoolCreate(&g_pools[dev], &props);
+      if (e != cudaSuccess) return e;
+      uint64_t keep = ~0ull;
+      e = cudaMemPoolSetAttribute(g_pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+      if (e != cudaSuccess) return e;
+    }
+    pool = g_pools[dev];
+  }
+  return cudaMallocFromPoolAsync(p, bytes, pool, st);
+}
+
+void scratch_free(void* p, cudaStream_t st) {
+  if (p) cudaFreeAsync(p, st);
 }
 
 yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const float* v,
@@ -106,18 +142,18 @@ yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k,
   if (T == 1 && algo != YUF_WKV_CHUNKED)
     return wkv7_decode_dispatch(r, w, k, v, a, b, s0, y, s_out, B * H, N, st_);
   if (algo == YUF_WKV_CHUNKED) return wkv7_chunk_dispatch(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, st_);
-  if (algo == YUF_WKV_PARALLEL || (algo == YUF_WKV_AUTO && wkv7_parallel_applies(B, T, H))) {
+  if (algo == YUF_WKV_PARALLEL || (algo == YUF_WKV_AUTO && wkv7_parallel_applies(B, T, H, N))) {
     // stream-ordered scratch for the chunk transitions, released right after use
     const size_t bytes = wkv7_parallel_scratch_floats(B, T, H, N) * sizeof(float);
     void* scratch = nullptr;
-    cudaError_t e = cudaMallocAsync(&scratch, bytes, st_);
+    cudaError_t e = scratch_alloc(&scratch, bytes, st_);
     if (e != cudaSuccess) {
       set_error("wkv7: scratch allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
       return YUF_ERR_OUT_OF_MEMORY;
     }
     yuf_status_t rc = wkv7_parallel(r, w, k, v, a, b, s0, y, s_out, B, T, H, N,
                                     static_cast<float*>(scratch), st_);
-    cudaFreeAsync(scratch, st_);
+    scratch_free(scratch, st_);
     return rc;
   }
   return wkv7_dispatch(r, w, k, v, a, b, s0, y, s_out, nullptr, nullptr, B, T, H, N, false,

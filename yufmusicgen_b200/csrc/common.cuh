@@ -42,6 +42,9 @@ YUF_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"
 namespace yuf {
 void set_error(const char* fmt, ...);
 yuf_status_t check_launch(const char* what);
+// stream-ordered scratch for the raw ops (a per-device pool that keeps its pages)
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st);
+void scratch_free(void* p, cudaStream_t st);
 }  // namespace yuf
 
 namespace yuf {

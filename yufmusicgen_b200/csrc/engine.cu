@@ -199,12 +199,9 @@ static size_t scan_rosa_floats(const yuf_model* m, size_t rows) {
 }
 
 static size_t scan_scratch_floats(const yuf_model* m, size_t rows) {
-  const size_t R = m->R(), HNN = (size_t)m->H() * m->N() * m->N();
-  // ROSA: A^K + chunk end/start states (32-token chunks).  WKV: U, P, chunk
-  // start states per 128-token chunk plus one state per sequence; the time-
-  // parallel path runs only for T >= 256, so sequences <= rows / 256.
-  (void)R;
-  return scan_rosa_floats(m, rows) + (3 * (rows / 128) + rows / 256 + 1) * HNN + 16;
+  // ROSA: A^K + chunk end/start states (32-token chunks); WKV: the time-parallel
+  // scan's bound for any batch of at most `rows` tokens
+  return scan_rosa_floats(m, rows) + wkv7_parallel_scratch_bound(rows, m->H(), m->N());
 }
 
 static size_t ws_bytes(const yuf_model* m, size_t rows) {
@@ -319,7 +316,7 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     if (T == 1)
       Y_TRY(wkv7_decode_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S,
                                  B * H, N, s));
-    else if (wkv7_parallel_applies(B, T, H))
+    else if (wkv7_parallel_applies(B, T, H, N))
       Y_TRY(wkv7_parallel(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, B, T, H,
                           N, w.scan + scan_rosa_floats(m, rows), s));
     else

@@ -46,10 +46,12 @@ bool rosa_parallel_applies(int B, int T, int R);
 }  // namespace yuf
 
 namespace yuf {
-// Time-parallel WKV-7 prefill (wkv7_parallel.cu): applies for T >= 256; scratch
+// Time-parallel WKV-7 prefill (wkv7_parallel.cu): runs for T >= 256; scratch
 // holds wkv7_parallel_scratch_floats() floats, 16-byte aligned.
-bool wkv7_parallel_applies(int B, int T, int H);
+// wkv7_parallel_scratch_bound(rows, H, N) covers every B, T with B*T <= rows.
+bool wkv7_parallel_applies(int B, int T, int H, int N);
 size_t wkv7_parallel_scratch_floats(int B, int T, int H, int N);
+size_t wkv7_parallel_scratch_bound(size_t rows, int H, int N);
 yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
                            int B, int T, int H, int N, float* scratch, cudaStream_t st);

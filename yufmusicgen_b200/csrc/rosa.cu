@@ -239,14 +239,14 @@ yuf_status_t rosa_dispatch(const float* cand, const float* write, const float* g
     // stream-ordered scratch: freed on the stream right after use
     float* scratch = nullptr;
     const size_t bytes = rosa_parallel_scratch_floats(B, T, R) * sizeof(float);
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), bytes, stream);
+    cudaError_t e = scratch_alloc(reinterpret_cast<void**>(&scratch), bytes, stream);
     if (e != cudaSuccess) {
       set_error("rosa: scratch allocation of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
       return YUF_ERR_OUT_OF_MEMORY;
     }
     yuf_status_t st = rosa_parallel(cand, write, gate, nullptr, nullptr, nullptr, R, decay, dir, 0, m0,
                                     read, m_out, B, T, R, gated, scratch, stream);
-    cudaFreeAsync(scratch, stream);
+    scratch_free(scratch, stream);
     return st;
   }
   if (gated)

@@ -1,0 +1,637 @@
+// Single-pass chunk summary and output correction for the time-parallel
+// WKV-7 prefill (wkv7_parallel.cu).
+//
+// For a chunk of tokens with start state S_0:
+//   S_t = S_0 P_t + U_t,   P_t = G_1 ... G_t,   U_t = scan from a zero state,
+//   y_t = S_t r_t = (U_t r_t) + S_0 (P_t r_t) = yU_t + S_0 q_t.
+// The pair kernels run, for every state row i, the zero-start row (U) and the
+// identity-start row (P, no value input) in the SAME lane, so every per-token
+// vector loaded from shared memory serves both rows, and write
+//   yU_t (into y), q_t = P_t r_t (row t of Q, [K, N] per chunk and head,
+//   token-major like y), U = U_end and P = P_end.
+// After the carry (S_0 of every chunk), wkv7_correct_kernel adds S_0 q_t to y:
+// a [len x N] x [N x N] product per (chunk, head) instead of a second scan.
+//
+// Work item bb = s * Cper + c is chunk c of sequence s: tokens
+// [c*K, min(c*K + K, Tstride)) -- the last chunk of a sequence may be shorter.
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace yuf {
+
+YUF_DEVICE size_t item_head_off(int bb, int hh, int K, int H, int N, int Tstride, int Cper) {
+  return (((size_t)(bb / Cper) * Tstride + (size_t)(bb % Cper) * K) * H + hh) * N;
+}
+YUF_DEVICE int item_len(int bb, int K, int Tstride, int Cper) {
+  return min(K, Tstride - (bb % Cper) * K);
+}
+
+constexpr int PAIR_TS = 16;
+
+// Multi-warp form for N >= 48: G lanes per state row; RP row pairs per lane
+// (each loaded column value then feeds 2*RP rows).
+template <int N>
+struct PairCfg {
+  static constexpr int G = (N == 16) ? 2 : 4;
+  static constexpr int C0 = (N + G - 1) / G;
+  static constexpr int C = (C0 + 1) / 2 * 2;
+  static constexpr int RP = C <= 12 ? 2 : 1;
+  static constexpr int CS = conflict_free_stride(C, G);
+  static constexpr int VP = G * CS;
+  static constexpr int RPW = 32 / G;  // row groups per warp (RP pairs each)
+  static constexpr int NWARPS = (N + RPW * RP - 1) / (RPW * RP);
+  static constexpr int NT = 32 * NWARPS;
+  static constexpr int TS = PAIR_TS;
+  static constexpr int RAW = 0;
+  static constexpr int PAD = RAW + 2 * 6 * TS * N;
+  static constexpr int TOTAL = PAD + 5 * TS * VP;
+  static constexpr size_t BYTES = (size_t)TOTAL * sizeof(float);
+};
+
+template <int N>
+__global__ void __launch_bounds__(PairCfg<N>::NT, 1)
+    wkv7_pair_kernel(const float* __restrict__ r, const float* __restrict__ w,
+                     const float* __restrict__ k, const float* __restrict__ v,
+                     const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y,
+                     float* __restrict__ Q, float* __restrict__ U_out, float* __restrict__ P_out,
+                     int K_, int H, int Tstride, int Cper) {
+  using K = PairCfg<N>;
+  constexpr int G = K::G, C = K::C, C2 = C / 2, CS = K::CS, VP = K::VP, NT = K::NT;
+  constexpr int RPW = K::RPW, TS = K::TS, RP = K::RP;
+  extern __shared__ float4 smem_f4[];
+  float* sm = reinterpret_cast<float*>(smem_f4);
+
+  const int bh = blockIdx.x;
+  const int bb = bh / H, hh = bh - bb * H;
+  const int T = item_len(bb, K_, Tstride, Cper);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int lrow = lane / G;
+  const bool lane_ok = lrow < RPW;
+  const int rgrp = warp * RPW + (lane_ok ? lrow : 0);
+  const int g = lane_ok ? lane - lrow * G : 0;
+  const int j0 = g * C;
+  int row[RP];
+  bool row_ok[RP];
+#pragma unroll
+  for (int p = 0; p < RP; ++p) {
+    const int rr = rgrp * RP + p;
+    row_ok[p] = lane_ok && rr < N;
+    row[p] = row_ok[p] ? rr : 0;
+  }
+
+  const int t_used = min(TS, T);
+  for (int i = tid; i < 5 * TS * VP; i += NT)
+    if ((i / VP) % TS < t_used) sm[K::PAD + i] = 0.f;
+
+  float2 SU[RP][C2], SP[RP][C2];
+#pragma unroll
+  for (int p = 0; p < RP; ++p)
+#pragma unroll
+    for (int c = 0; c < C2; ++c) {
+      const int j = j0 + 2 * c;
+      SU[p][c] = make_float2(0.f, 0.f);
+      SP[p][c] = make_float2(j == row[p] ? 1.f : 0.f, j + 1 == row[p] ? 1.f : 0.f);
+    }
+
+  const size_t tok_stride = (size_t)H * N;
+  const size_t head_off = item_head_off(bb, hh, K_, H, N, Tstride, Cper);
+  float* Qh = Q + (size_t)bh * K_ * N;  // Q[bb][hh][t][row]
+  const float* src[6] = {r + head_off, w + head_off, k + head_off,
+                         v + head_off, a + head_off, b + head_off};
+  auto stage = [&](int buf, int t0, int Tc) {
+    constexpr int Q4 = N / 4;
+    const int per_arr = Tc * Q4;
+#pragma unroll
+    for (int arr = 0; arr < 6; ++arr) {
+      for (int idx = tid; idx < per_arr; idx += NT) {
+        const int t = idx / Q4, q = idx - t * Q4;
+        cp_async_16(sm + K::RAW + ((buf * 6 + arr) * TS + t) * N + 4 * q,
+                    src[arr] + (size_t)(t0 + t) * tok_stride + 4 * q);
+      }
+    }
+    cp_async_commit();
+  };
+  const int nchunks = (T + TS - 1) / TS;
+  if (nchunks > 0) stage(0, 0, min(TS, T));
+  __syncthreads();
+  const float* Pw = sm + K::PAD + 0 * TS * VP + g * CS;
+  const float* Pk = sm + K::PAD + 1 * TS * VP + g * CS;
+  const float* Pa = sm + K::PAD + 2 * TS * VP + g * CS;
+  const float* Pb = sm + K::PAD + 3 * TS * VP + g * CS;
+  const float* Pr = sm + K::PAD + 4 * TS * VP + g * CS;
+
+  for (int c = 0; c < nchunks; ++c) {
+    const int buf = c & 1;
+    const int t0 = c * TS;
+    const int Tc = min(TS, T - t0);
+    if (c + 1 < nchunks) {
+      stage(buf ^ 1, t0 + TS, min(TS, T - t0 - TS));
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* raw = sm + K::RAW + buf * 6 * TS * N;
+    const float* rawv = raw + 3 * TS * N;
+    for (int idx = tid; idx < Tc * N; idx += NT) {
+      const int t = idx / N, j = idx - t * N;
+      const int pj = K::PAD + t * VP + (j / C) * CS + (j % C);
+      sm[pj + 0 * TS * VP] = __expf(W_SCALE * sigmoidf_fast(raw[1 * TS * N + idx]));
+      sm[pj + 1 * TS * VP] = raw[2 * TS * N + idx];
+      sm[pj + 2 * TS * VP] = raw[4 * TS * N + idx];
+      sm[pj + 3 * TS * VP] = raw[5 * TS * N + idx];
+      sm[pj + 4 * TS * VP] = raw[0 * TS * N + idx];
+    }
+    __syncthreads();
+    constexpr int CQ = (C + 3) / 4;
+#define YUF_H2(arr, c2) ((c2 & 1) ? make_float2(arr[c2 >> 1].z, arr[c2 >> 1].w) \
+                                  : make_float2(arr[c2 >> 1].x, arr[c2 >> 1].y))
+#pragma unroll
+    for (int t = 0; t < TS; ++t) {
+      if (t < Tc) {
+        const int o = t * VP;
+        float4 qA[CQ], qK[CQ], qB[CQ], qW[CQ], qR[CQ];
+#pragma unroll
+        for (int q = 0; q < CQ; ++q) {
+          qA[q] = *reinterpret_cast<const float4*>(Pa + o + 4 * q);
+          qK[q] = *reinterpret_cast<const float4*>(Pk + o + 4 * q);
+          qB[q] = *reinterpret_cast<const float4*>(Pb + o + 4 * q);
+          qW[q] = *reinterpret_cast<const float4*>(Pw + o + 4 * q);
+          qR[q] = *reinterpret_cast<const float4*>(Pr + o + 4 * q);
+        }
+#pragma unroll
+        for (int p = 0; p < RP; ++p) {
+          const float cv = rawv[t * N + row[p]];
+          float2 u0 = make_float2(0.f, 0.f), u1 = u0, p0 = u0, p1 = u0;
+#pragma unroll
+          for (int c2 = 0; c2 < C2; ++c2) {
+            const float2 av = YUF_H2(qA, c2);
+            if (c2 & 1) { u1 = ffma2(SU[p][c2], av, u1); p1 = ffma2(SP[p][c2], av, p1); }
+            else        { u0 = ffma2(SU[p][c2], av, u0); p0 = ffma2(SP[p][c2], av, p0); }
+          }
+          const float saU = lane_group_sum<G>((u0.x + u1.x) + (u0.y + u1.y), lane);
+          const float saP = lane_group_sum<G>((p0.x + p1.x) + (p0.y + p1.y), lane);
+          float2 yu0 = make_float2(0.f, 0.f), yu1 = yu0, yp0 = yu0, yp1 = yu0;
+#pragma unroll
+          for (int c2 = 0; c2 < C2; ++c2) {
+            const float2 wv = YUF_H2(qW, c2), bv = YUF_H2(qB, c2), rv = YUF_H2(qR, c2);
+            SU[p][c2] = ffma2(SU[p][c2], wv, ffma2(f2(saU), bv, fmul2(f2(cv), YUF_H2(qK, c2))));
+            SP[p][c2] = ffma2(SP[p][c2], wv, fmul2(f2(saP), bv));
+            if (c2 & 1) { yu1 = ffma2(SU[p][c2], rv, yu1); yp1 = ffma2(SP[p][c2], rv, yp1); }
+            else        { yu0 = ffma2(SU[p][c2], rv, yu0); yp0 = ffma2(SP[p][c2], rv, yp0); }
+          }
+          const float yU = lane_group_sum<G>((yu0.x + yu1.x) + (yu0.y + yu1.y), lane);
+          const float qv = lane_group_sum<G>((yp0.x + yp1.x) + (yp0.y + yp1.y), lane);
+          if (g == 0 && row_ok[p]) {
+            y[head_off + (size_t)(t0 + t) * tok_stride + row[p]] = yU;
+            Qh[(size_t)(t0 + t) * N + row[p]] = qv;
+          }
+        }
+      }
+    }
+#undef YUF_H2
+    __syncthreads();
+  }
+#pragma unroll
+  for (int p = 0; p < RP; ++p) {
+    if (!row_ok[p]) continue;
+    const size_t srow = (size_t)bh * N * N + (size_t)row[p] * N;
+#pragma unroll
+    for (int c = 0; c < C2; ++c) {
+      const int j = j0 + 2 * c;
+      if (j < N) {
+        *reinterpret_cast<float2*>(U_out + srow + j) = SU[p][c];
+        *reinterpret_cast<float2*>(P_out + srow + j) = SP[p][c];
+      }
+    }
+  }
+}
+
+// One warp per (chunk, head) for N = 16, 32, 40.  Lane (rg, g),
+// rg = lane / 4, g = lane % 4, owns the R = N / 8 state rows rg*R .. rg*R+R-1 --
+// each as a zero-start row and an identity-start row -- over the C = N / 4
+// columns g*C .. g*C+C-1.  Every per-token column value a lane reads from shared
+// memory then feeds 2R rows, so the kernel is bound by the FMA pipe rather than
+// by shared-memory delivery (the multi-warp kernel above feeds 4 rows per read).
+// Per token: the two row dot products with a (all-reduced over the 4 lanes of a
+// row group), the update, and the two dot products with r, reduce-scattered so
+// that each lane finishes a few of the 2N outputs and stores them directly (a
+// warp's stores of one token cover one contiguous row of y and of Q).
+// Staging per group of TS tokens: cp.async brings the raw rows, one pass turns
+// them into the lane layout (and the decay into exp(-0.6065 sigmoid(w))), then
+// the next group's copy starts while this group is scanned; single buffers keep
+// the block at 16.6 KB of shared memory (N = 40), 12 resident warps per SM.
+template <int N>
+struct PairWCfg {
+  static constexpr int G = 4;       // lanes per row group
+  static constexpr int R = N / 8;   // rows per lane (8 row groups per warp)
+  static constexpr int C = N / G;   // columns per lane
+  static constexpr int C2 = C / 2;
+  static constexpr int CS = conflict_free_stride(C, G);
+  static constexpr int VP = G * CS;
+  static constexpr int TS = 8;                    // tokens per staged group
+  static constexpr int RAW = 0;                   // [6][TS][N] raw rows r, w, k, v, a, b
+  static constexpr int PAD = RAW + 6 * TS * N;    // [5][TS][VP] ret, k, a, b, r in lane layout
+  static constexpr int VV = PAD + 5 * TS * VP;    // [TS][N] values
+  static constexpr int TOTAL = VV + TS * N;
+  static constexpr size_t BYTES = (size_t)TOTAL * sizeof(float);
+  static_assert(N % 8 == 0 && C % 2 == 0 && N <= 40, "one-warp pair kernel: N in {16, 32, 40}");
+};
+
+// C floats of one padded vector as float2 pairs (C/4 LDS.128 and one LDS.64).
+template <int C>
+YUF_DEVICE void load_cols(float2 (&dst)[C / 2], const float* p) {
+#pragma unroll
+  for (int q = 0; q < C / 4; ++q) {
+    const float4 x = *reinterpret_cast<const float4*>(p + 4 * q);
+    dst[2 * q] = make_float2(x.x, x.y);
+    dst[2 * q + 1] = make_float2(x.z, x.w);
+  }
+  if constexpr (C % 4 != 0) dst[C / 2 - 1] = *reinterpret_cast<const float2*>(p + C - 2);
+}
+
+template <int N>
+__global__ void __launch_bounds__(32)
+    wkv7_pairw_kernel(const float* __restrict__ r, const float* __restrict__ w,
+                      const float* __restrict__ k, const float* __restrict__ v,
+                      const float* __restrict__ a, const float* __restrict__ b,
+                      float* __restrict__ y, float* __restrict__ Q, float* __restrict__ U_out,
+                      float* __restrict__ P_out, int K_, int H, int Tstride, int Cper) {
+  using K = PairWCfg<N>;
+  constexpr int R = K::R, C = K::C, C2 = K::C2, CS = K::CS, VP = K::VP, TS = K::TS;
+  constexpr int RH = (R + 1) / 2;  // outputs kept by the even lane of a pair after reduce-scatter
+  extern __shared__ float4 smem_f4[];
+  float* sm = reinterpret_cast<float*>(smem_f4);
+
+  const int bh = blockIdx.x;
+  const int bb = bh / H, hh = bh - bb * H;
+  const int T = item_len(bb, K_, Tstride, Cper);
+  const int lane = threadIdx.x;
+  const int rg = lane >> 2, g = lane & 3;
+  const int i0 = rg * R, j0 = g * C;
+
+  float2 SU[R][C2], SP[R][C2];
+#pragma unroll
+  for (int p = 0; p < R; ++p)
+#pragma unroll
+    for (int c = 0; c < C2; ++c) {
+      const int j = j0 + 2 * c, i = i0 + p;
+      SU[p][c] = make_float2(0.f, 0.f);
+      SP[p][c] = make_float2(j == i ? 1.f : 0.f, j + 1 == i ? 1.f : 0.f);
+    }
+
+  const size_t tok_stride = (size_t)H * N;
+  const size_t head_off = item_head_off(bb, hh, K_, H, N, Tstride, Cper);
+  float* Qh = Q + (size_t)bh * K_ * N;  // Q[bb][hh][t][row]
+  const float* src[6] = {r + head_off, w + head_off, k + head_off,
+                         v + head_off, a + head_off, b + head_off};
+  auto stage = [&](int t0, int Tc) {
+    constexpr int Q4 = N / 4;
+#pragma unroll
+    for (int arr = 0; arr < 6; ++arr)
+      for (int idx = lane; idx < Tc * Q4; idx += 32) {
+        const int t = idx / Q4, q = idx - t * Q4;
+        cp_async_16(sm + K::RAW + (arr * TS + t) * N + 4 * q,
+                    src[arr] + (size_t)(t0 + t) * tok_stride + 4 * q);
+      }
+    cp_async_commit();
+  };
+
+  const int ngroups = (T + TS - 1) / TS;
+  if (ngroups > 0) stage(0, min(TS, T));
+  const float* Pw = sm + K::PAD + 0 * TS * VP + g * CS;
+  const float* Pk = sm + K::PAD + 1 * TS * VP + g * CS;
+  const float* Pa = sm + K::PAD + 2 * TS * VP + g * CS;
+  const float* Pb = sm + K::PAD + 3 * TS * VP + g * CS;
+  const float* Pr = sm + K::PAD + 4 * TS * VP + g * CS;
+  const float* vv = sm + K::VV;
+  const int h = (lane >> 1) & 1, e = lane & 1;  // reduce-scatter roles inside the row group
+  const int rbase = i0 + (e ? RH : 0);
+  const int nk = e ? R - RH : RH;
+  float* obase = h ? Qh + rbase : y + head_off + rbase;
+  const size_t ostride = h ? (size_t)N : tok_stride;
+
+  for (int gi = 0; gi < ngroups; ++gi) {
+    const int t0 = gi * TS;
+    const int Tc = min(TS, T - t0);
+    cp_async_wait<0>();
+    __syncwarp();
+    // lane layout, two columns at a time (C is even, so a pair never straddles lanes)
+    for (int idx = lane; idx < Tc * N / 2; idx += 32) {
+      const int t = idx / (N / 2), j = 2 * (idx - t * (N / 2));
+      const int pj = K::PAD + t * VP + (j / C) * CS + (j % C);
+      const int rj = t * N + j;
+      const float2 wr = *reinterpret_cast<const float2*>(sm + K::RAW + 1 * TS * N + rj);
+      *reinterpret_cast<float2*>(sm + pj + 0 * TS * VP) =
+          make_float2(__expf(W_SCALE * sigmoidf_fast(wr.x)), __expf(W_SCALE * sigmoidf_fast(wr.y)));
+      *reinterpret_cast<float2*>(sm + pj + 1 * TS * VP) =
+          *reinterpret_cast<const float2*>(sm + K::RAW + 2 * TS * N + rj);
+      *reinterpret_cast<float2*>(sm + pj + 2 * TS * VP) =
+          *reinterpret_cast<const float2*>(sm + K::RAW + 4 * TS * N + rj);
+      *reinterpret_cast<float2*>(sm + pj + 3 * TS * VP) =
+          *reinterpret_cast<const float2*>(sm + K::RAW + 5 * TS * N + rj);
+      *reinterpret_cast<float2*>(sm + pj + 4 * TS * VP) =
+          *reinterpret_cast<const float2*>(sm + K::RAW + 0 * TS * N + rj);
+      *reinterpret_cast<float2*>(sm + K::VV + rj) =
+          *reinterpret_cast<const float2*>(sm + K::RAW + 3 * TS * N + rj);
+    }
+    __syncwarp();
+    if (gi + 1 < ngroups) stage(t0 + TS, min(TS, T - t0 - TS));  // raw buffer is free again
+
+#pragma unroll
+    for (int t = 0; t < TS; ++t) {
+      if (t < Tc) {
+        const int o = t * VP;
+        float2 av[C2];
+        load_cols<C>(av, Pa + o);
+        float sU[R], sP[R];
+#pragma unroll
+        for (int p = 0; p < R; ++p) {
+          float2 u = make_float2(0.f, 0.f), q = u;
+#pragma unroll
+          for (int c = 0; c < C2; ++c) {
+            u = ffma2(SU[p][c], av[c], u);
+            q = ffma2(SP[p][c], av[c], q);
+          }
+          sU[p] = u.x + u.y;
+          sP[p] = q.x + q.y;
+        }
+#pragma unroll
+        for (int p = 0; p < R; ++p) {
+          sU[p] += __shfl_xor_sync(0xffffffffu, sU[p], 1);
+          sP[p] += __shfl_xor_sync(0xffffffffu, sP[p], 1);
+        }
+#pragma unroll
+        for (int p = 0; p < R; ++p) {
+          sU[p] += __shfl_xor_sync(0xffffffffu, sU[p], 2);
+          sP[p] += __shfl_xor_sync(0xffffffffu, sP[p], 2);
+        }
+        float2 wv[C2], bv[C2], kv[C2];
+        load_cols<C>(wv, Pw + o);
+        load_cols<C>(bv, Pb + o);
+        load_cols<C>(kv, Pk + o);
+        float vr[R];
+#pragma unroll
+        for (int p = 0; p < R; ++p) vr[p] = vv[t * N + i0 + p];
+#pragma unroll
+        for (int p = 0; p < R; ++p)
+#pragma unroll
+          for (int c = 0; c < C2; ++c) {
+            SU[p][c] = ffma2(SU[p][c], wv[c], ffma2(f2(sU[p]), bv[c], fmul2(f2(vr[p]), kv[c])));
+            SP[p][c] = ffma2(SP[p][c], wv[c], fmul2(f2(sP[p]), bv[c]));
+          }
+        float2 rv[C2];
+        load_cols<C>(rv, Pr + o);
+        float yo[2 * R];  // [0, R): zero-start outputs, [R, 2R): q
+#pragma unroll
+        for (int p = 0; p < R; ++p) {
+          float2 u = make_float2(0.f, 0.f), q = u;
+#pragma unroll
+          for (int c = 0; c < C2; ++c) {
+            u = ffma2(SU[p][c], rv[c], u);
+            q = ffma2(SP[p][c], rv[c], q);
+          }
+          yo[p] = u.x + u.y;
+          yo[R + p] = q.x + q.y;
+        }
+        // reduce-scatter over the row group: lanes with h = 0 keep the zero-start
+        // outputs, h = 1 the q values; then e = 0 keeps rows [0, RH), e = 1 the rest
+        float kept[R];
+#pragma unroll
+        for (int p = 0; p < R; ++p) {
+          const float send = h ? yo[p] : yo[R + p];
+          kept[p] = (h ? yo[R + p] : yo[p]) + __shfl_xor_sync(0xffffffffu, send, 2);
+        }
+        float* orow = obase + (size_t)(t0 + t) * ostride;
+#pragma unroll
+        for (int p = 0; p < RH; ++p) {
+          const float hi = (RH + p < R) ? kept[RH + p] : 0.f;
+          const float send = e ? kept[p] : hi;
+          const float fin = (e ? hi : kept[p]) + __shfl_xor_sync(0xffffffffu, send, 1);
+          if (p < nk) orow[p] = fin;
+        }
+      }
+    }
+    __syncwarp();  // the next group's transform overwrites the lane layout
+  }
+#pragma unroll
+  for (int p = 0; p < R; ++p) {
+    const size_t srow = (size_t)bh * N * N + (size_t)(i0 + p) * N;
+#pragma unroll
+    for (int c = 0; c < C2; ++c) {
+      *reinterpret_cast<float2*>(U_out + srow + j0 + 2 * c) = SU[p][c];
+      *reinterpret_cast<float2*>(P_out + srow + j0 + 2 * c) = SP[p][c];
+    }
+  }
+}
+
+// y[t][i] += sum_j S0[i][j] q_t[j] over one (chunk, head).  Thread (tq, ig)
+// owns tokens 4tq .. 4tq+3 and the RI consecutive rows ig*RI ..; its y values
+// are loaded into registers before the product so their latency overlaps it.
+// S0 and the chunk's Q sit in shared memory with rows padded to N + 1 floats
+// (conflict-free reads across the token groups of a warp).
+template <int N>
+struct CorrCfg {
+  static constexpr int RI = N / 4 < 16 ? N / 4 : 16;  // rows per thread
+  static constexpr int IG = N / RI;                   // row groups
+  static constexpr int NP = N + 1;
+};
+
+template <int N>
+__global__ void __launch_bounds__(256)
+    wkv7_correct_kernel(const float* __restrict__ S0, const float* __restrict__ Q,
+                        float* __restrict__ y, int K_, int H, int Tstride, int Cper, int skip_first) {
+  constexpr int RI = CorrCfg<N>::RI, IG = CorrCfg<N>::IG, NP = CorrCfg<N>::NP;
+  extern __shared__ float4 corr_sm[];
+  float* Ss = reinterpret_cast<float*>(corr_sm);  // [N][NP]
+  float* Qs = Ss + N * NP;                        // [K][NP]
+  const int bh = blockIdx.x;
+  const int bb = bh / H, hh = bh - bb * H;
+  if (skip_first && bb % Cper == 0) return;  // chunk 0 starts from the zero state
+  const int T = item_len(bb, K_, Tstride, Cper);
+  const int tid = threadIdx.x, nt = blockDim.x;  // nt is a multiple of IG
+  const float* S0h = S0 + (size_t)bh * N * N;
+  const float* Qg = Q + (size_t)bh * K_ * N;
+  for (int q = tid; q < N * N / 4; q += nt) {
+    const float4 x = reinterpret_cast<const float4*>(S0h)[q];
+    const int i = (4 * q) / N, j = 4 * q - i * N;
+    float* d = Ss + i * NP + j;
+    d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+  }
+  for (int q = tid; q < T * N / 4; q += nt) {
+    const float4 x = reinterpret_cast<const float4*>(Qg)[q];
+    const int t = (4 * q) / N, j = 4 * q - t * N;
+    float* d = Qs + t * NP + j;
+    d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+  }
+  const size_t tok_stride = (size_t)H * N;
+  const size_t head_off = item_head_off(bb, hh, K_, H, N, Tstride, Cper);
+  const int ig = tid % IG, i0 = ig * RI;
+  const int tstep = 4 * (nt / IG);
+  float yv[4][RI];
+  auto load_y = [&](int t0) {
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt) {
+      if (t0 + tt < T) {
+        const float* yr = y + head_off + (size_t)(t0 + tt) * tok_stride + i0;
+#pragma unroll
+        for (int q = 0; q < RI; q += 2) {
+          const float2 x = *reinterpret_cast<const float2*>(yr + q);
+          yv[tt][q] = x.x;
+          yv[tt][q + 1] = x.y;
+        }
+      }
+    }
+  };
+  const int t_first = (tid / IG) * 4;
+  load_y(t_first);  // issued before the barrier: overlaps the staging above
+  __syncthreads();  // S0 and Q staged
+  for (int t0 = t_first; t0 < T; t0 += tstep) {
+    if (t0 != t_first) load_y(t0);
+    float acc[4][RI];
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt)
+#pragma unroll
+      for (int q = 0; q < RI; ++q) acc[tt][q] = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < N; ++j) {
+      float qv[4];
+#pragma unroll
+      for (int tt = 0; tt < 4; ++tt) qv[tt] = Qs[(t0 + tt) * NP + j];  // rows past T: unused
+#pragma unroll
+      for (int q = 0; q < RI; ++q) {
+        const float sv = Ss[(i0 + q) * NP + j];
+#pragma unroll
+        for (int tt = 0; tt < 4; ++tt) acc[tt][q] = fmaf(sv, qv[tt], acc[tt][q]);
+      }
+    }
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt) {
+      if (t0 + tt < T) {
+        float* yr = y + head_off + (size_t)(t0 + tt) * tok_stride + i0;
+#pragma unroll
+        for (int q = 0; q < RI; q += 2)
+          *reinterpret_cast<float2*>(yr + q) =
+              make_float2(yv[tt][q] + acc[tt][q], yv[tt][q + 1] + acc[tt][q + 1]);
+      }
+    }
+  }
+}
+
+// Resident pair blocks per device for head size N (blocks per SM x SMs),
+// queried once per (device, N).
+int wkv7_pair_slots(int N) {
+  static int cache[64][8] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  const int ni = N == 16 ? 0 : N == 32 ? 1 : N == 40 ? 2 : N == 48 ? 3 : N == 64 ? 4 : N == 96 ? 5 : 6;
+  if (cache[dev][ni] > 0) return cache[dev][ni];
+  int sms = 148, per_sm = 1;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t e = cudaSuccess;
+  switch (N) {
+#define SLOTW(NN)                                                                                \
+  case NN: {                                                                                     \
+    auto kern = wkv7_pairw_kernel<NN>;                                                           \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PairWCfg<NN>::BYTES); \
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32, PairWCfg<NN>::BYTES);   \
+    break;                                                                                       \
+  }
+#define SLOT(NN)                                                                                 \
+  case NN: {                                                                                     \
+    auto kern = wkv7_pair_kernel<NN>;                                                            \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PairCfg<NN>::BYTES); \
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, PairCfg<NN>::NT, PairCfg<NN>::BYTES); \
+    break;                                                                                       \
+  }
+    SLOTW(16) SLOTW(32) SLOTW(40) SLOT(48) SLOT(64) SLOT(96) SLOT(128)
+#undef SLOTW
+#undef SLOT
+    default:
+      break;
+  }
+  if (e != cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  cache[dev][ni] = std::max(1, per_sm * sms);
+  return cache[dev][ni];
+}
+
+// Largest chunk the correction kernel can stage for head size N (multiple of 8).
+int wkv7_correct_max_chunk(int N) {
+  const int floats = 200 * 1024 / 4;
+  const int kmax = floats / (N + 1) - N;
+  return kmax / 8 * 8;
+}
+
+yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, const float* v,
+                                const float* a, const float* b, float* y, float* Q, float* U, float* P,
+                                int items, int K, int H, int N, int Tstride, int Cper, cudaStream_t st) {
+  switch (N) {
+#define CASEW(NN)                                                                                \
+  case NN: {                                                                                     \
+    using Kc = PairWCfg<NN>;                                                                     \
+    auto kern = wkv7_pairw_kernel<NN>;                                                           \
+    if (Kc::BYTES > 48 * 1024 &&                                                                 \
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Kc::BYTES) != \
+            cudaSuccess) {                                                                       \
+      set_error("wkv7 pair: cudaFuncSetAttribute failed");                                      \
+      return YUF_ERR_CUDA;                                                                       \
+    }                                                                                            \
+    kern<<<items * H, 32, Kc::BYTES, st>>>(r, w, k, v, a, b, y, Q, U, P, K, H, Tstride, Cper);   \
+    return check_launch("wkv7_pairw_kernel");                                                    \
+  }
+#define CASE(NN)                                                                                 \
+  case NN: {                                                                                     \
+    using Kc = PairCfg<NN>;                                                                      \
+    auto kern = wkv7_pair_kernel<NN>;                                                            \
+    if (Kc::BYTES > 48 * 1024 &&                                                                 \
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Kc::BYTES) != \
+            cudaSuccess) {                                                                       \
+      set_error("wkv7 pair: cudaFuncSetAttribute failed");                                      \
+      return YUF_ERR_CUDA;                                                                       \
+    }                                                                                            \
+    kern<<<items * H, Kc::NT, Kc::BYTES, st>>>(r, w, k, v, a, b, y, Q, U, P, K, H, Tstride, Cper); \
+    return check_launch("wkv7_pair_kernel");                                                     \
+  }
+    CASEW(16) CASEW(32) CASEW(40) CASE(48) CASE(64) CASE(96) CASE(128)
+#undef CASEW
+#undef CASE
+    default:
+      set_error("wkv7: head size N=%d has no kernel", N);
+      return YUF_ERR_UNSUPPORTED;
+  }
+}
+
+yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, int items, int K, int H,
+                                   int N, int Tstride, int Cper, bool skip_first, cudaStream_t st) {
+  const size_t bytes = ((size_t)N * (N + 1) + (size_t)K * (N + 1)) * sizeof(float);
+  switch (N) {
+#define CASE(NN)                                                                                   \
+  case NN: {                                                                                       \
+    auto kern = wkv7_correct_kernel<NN>;                                                           \
+    if (bytes > 48 * 1024 &&                                                                       \
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=     \
+            cudaSuccess) {                                                                         \
+      set_error("wkv7 correct: cudaFuncSetAttribute failed");                                     \
+      return YUF_ERR_CUDA;                                                                         \
+    }                                                                                              \
+    constexpr int IG = CorrCfg<NN>::IG;                                                            \
+    int nt = ((K + 3) / 4) * IG;                                                                   \
+    nt = std::min(256, (nt + 31) / 32 * 32);                                                       \
+    nt = std::max(nt, 32) / IG * IG;                                                               \
+    kern<<<items * H, nt, bytes, st>>>(S0, Q, y, K, H, Tstride, Cper, skip_first ? 1 : 0);         \
+    return check_launch("wkv7_correct_kernel");                                                    \
+  }
+    CASE(16) CASE(32) CASE(40) CASE(48) CASE(64) CASE(96) CASE(128)
+#undef CASE
+    default:
+      set_error("wkv7: head size N=%d has no kernel", N);
+      return YUF_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace yuf

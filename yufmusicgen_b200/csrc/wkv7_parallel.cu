@@ -2,35 +2,41 @@
 //
 // The sequential scan (wkv7.cu) gives one CTA to each (sequence, head) and walks
 // all T tokens; with few sequences (the 0.1B prefill: B = 2, H = 16, 32 CTAs for
-// 148 SMs) most of the GPU idles.  The recurrence is linear in the state,
+// 148 SMs) most of the GPU idles, and even at B*H = 128 one chain per SM is bound
+// by that SM's shared-memory delivery.  The recurrence is linear in the state,
 //   S_t = S_{t-1} G_t + v_t k_t^T,   G_t = diag(w_t) + a_t b_t^T,
-// so over a chunk of K tokens  S_end = S_start P + U  with the chunk's
-// transition P = G_1 ... G_K and its own contribution U (the end state from a
-// zero start).  Three passes:
-//   1. every (sequence, chunk, head) computes U and P (wkv7.cu MODE 1: N rows
-//      from zero with the value input, N identity rows without it);
+// so over a chunk of tokens  S_end = S_start P + U  with the chunk's transition
+// P = G_1 ... G_K and its own contribution U (the end state from a zero start).
+// Three passes:
+//   1. every (sequence, chunk, head) scans its tokens once with, per state row,
+//      the zero-start row and the identity-start row in the same lane
+//      (wkv7_pair.cu): y from a zero start, q_t = P_t r_t, U and P;
 //   2. per (sequence, head) the chunk start states S_c = S_{c-1} P_c + U_c
-//      (wkv7_carry_kernel, an N x N x N product per chunk, P_c/U_c prefetched
-//      with cp.async while the previous product runs);
-//   3. every (sequence, chunk, head) rescans its tokens from S_{c-1} and writes y
-//      (wkv7.cu MODE 0 over the chunks as batch entries).
-// Tokens past the last whole chunk are scanned from the carried state by the
-// sequential kernel.  Exact in exact arithmetic; the fp32 rounding differs from
-// the sequential order only by the product association of pass 2.
+//      (wkv7_carry_kernel, an N x N x N product per chunk, P_c and U_c
+//      prefetched with cp.async while the previous product runs);
+//   3. every (sequence, chunk, head) adds S_{c-1} q_t to its y
+//      (wkv7_correct_kernel, since y_t = yU_t + S_{c-1} q_t).
+// The chunk count is chosen so that pass 1 fills the GPU in one wave: about
+// (resident pair blocks) / (B*H) chunks per sequence, chunk length a multiple
+// of 8, the last chunk of a sequence possibly shorter.  Exact in exact
+// arithmetic; the fp32 rounding differs from the sequential order only by the
+// product association of passes 2 and 3.
+
+#include <algorithm>
 
 #include "common.cuh"
 
 namespace yuf {
 
-constexpr int WKV_PAR_K = 128;  // tokens per chunk
+constexpr int WKV_PAR_CMAX = 48;  // the carry is sequential over chunks
 
-yuf_status_t wkv7_dispatch_strided(const float* r, const float* w, const float* k, const float* v,
-                                   const float* a, const float* b, const float* s0, float* y,
-                                   float* s_out, float* ckpt, float* sa, int B, int T, int H, int N,
-                                   bool compat, int Tstride, int Cper, cudaStream_t stream);
-yuf_status_t wkv7_summary_dispatch(const float* w, const float* k, const float* v, const float* a,
-                                   const float* b, float* U, float* P, int B, int T, int H, int N,
-                                   int Tstride, int Cper, cudaStream_t stream);
+yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, const float* v,
+                                const float* a, const float* b, float* y, float* Q, float* U, float* P,
+                                int items, int K, int H, int N, int Tstride, int Cper, cudaStream_t st);
+yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, int items, int K, int H,
+                                   int N, int Tstride, int Cper, bool skip_first, cudaStream_t st);
+int wkv7_pair_slots(int N);
+int wkv7_correct_max_chunk(int N);
 
 // One CTA per (sequence, head); thread (ib, jb) owns a RB x 4 block of S.
 template <int N, int RB>
@@ -39,9 +45,11 @@ __global__ void __launch_bounds__(N * N / (RB * 4))
                       float* __restrict__ S_start, float* s_out, int C, int H) {
   constexpr int NT = N * N / (RB * 4);
   constexpr int NN = N * N;
+  constexpr bool PREU = N <= 64;                     // U prefetched too when it fits
   extern __shared__ float4 carry_sm[];
   float* Ss = reinterpret_cast<float*>(carry_sm);   // [N][N] running state
   float* Pb0 = Ss + NN;                              // [2][N][N] transitions, double buffered
+  float* Ub0 = Pb0 + 2 * NN;                         // [2][N][N] contributions (PREU only)
   const int bh = blockIdx.x;
   const int s = bh / H, h = bh - s * H;
   const int tid = threadIdx.x;
@@ -51,7 +59,10 @@ __global__ void __launch_bounds__(N * N / (RB * 4))
   for (int q = tid; q < NN; q += NT) Ss[q] = s0p ? s0p[q] : 0.f;
   auto fetch = [&](int c, int buf) {
     const size_t off = (((size_t)s * C + c) * H + h) * NN;
-    for (int q = tid; q < NN / 4; q += NT) cp_async_16(Pb0 + buf * NN + 4 * q, P + off + 4 * q);
+    for (int q = tid; q < NN / 4; q += NT) {
+      cp_async_16(Pb0 + buf * NN + 4 * q, P + off + 4 * q);
+      if (PREU) cp_async_16(Ub0 + buf * NN + 4 * q, U + off + 4 * q);
+    }
     cp_async_commit();
   };
   if (C > 0) fetch(0, 0);
@@ -71,7 +82,7 @@ __global__ void __launch_bounds__(N * N / (RB * 4))
     }
     __syncthreads();
     float acc[RB][4];
-    const float* Uc = U + (((size_t)s * C + c) * H + h) * NN;
+    const float* Uc = PREU ? Ub0 + buf * NN : U + (((size_t)s * C + c) * H + h) * NN;
 #pragma unroll
     for (int r = 0; r < RB; ++r) {
       const float4 u = *reinterpret_cast<const float4*>(Uc + (i0 + r) * N + j0);
@@ -105,7 +116,7 @@ template <int N>
 static yuf_status_t launch_carry(const float* U, const float* P, const float* s0, float* S_start,
                                  float* s_out, int B, int C, int H, cudaStream_t st) {
   constexpr int RB = N >= 96 ? 4 : 2;
-  const size_t bytes = 3 * (size_t)N * N * sizeof(float);
+  const size_t bytes = (N <= 64 ? 5 : 3) * (size_t)N * N * sizeof(float);
   auto kern = wkv7_carry_kernel<N, RB>;
   if (bytes > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
@@ -118,35 +129,65 @@ static yuf_status_t launch_carry(const float* U, const float* P, const float* s0
   return check_launch("wkv7_carry_kernel");
 }
 
-// The parallel path does about 3x the sequential work (the N transition rows of
-// pass 1 and the rescan); it wins when the sequential scan would leave SMs idle,
-// i.e. when there are fewer (sequence, head) chains than about 2/3 of the 148 SMs
-// (measured: B*H = 32 -> 6x faster per layer, B*H = 128 -> 1.3x slower).
-bool wkv7_parallel_applies(int B, int T, int H) {
-  return T >= 2 * WKV_PAR_K && (long long)B * H <= 96;
+// Chunks per sequence and chunk length for B sequences of T tokens.
+void wkv7_parallel_plan(int B, int T, int H, int N, int* C_out, int* K_out) {
+  const long long BH = std::max(1LL, (long long)B * H);
+  long long C = wkv7_pair_slots(N) / BH;
+  C = std::max(2LL, std::min<long long>(C, WKV_PAR_CMAX));
+  C = std::min<long long>(C, std::max(1, T / 16));
+  int K = (int)((T + C - 1) / C);
+  K = (K + 7) / 8 * 8;
+  K = std::min(K, wkv7_correct_max_chunk(N));
+  *K_out = K;
+  *C_out = (T + K - 1) / K;
+}
+
+// The parallel path does about twice the sequential work (the N transition rows
+// of pass 1); it wins while the sequential scan, one chain per CTA, would leave
+// SMs idle or be bound by one SM's shared-memory delivery.  Measured on B200 at
+// T = 2048, N = 40: 3.8x faster at B*H = 32, 2.0x at 128, 1.2x at 512 (a third
+// of the 1776 resident pair blocks).  Head sizes above 40 use the multi-warp
+// pair kernel: 3.6x at B*H = 32 for N = 64, slower than sequential at 128.
+bool wkv7_parallel_applies(int B, int T, int H, int N) {
+  const long long BH = (long long)B * H;
+  if (T < 256) return false;
+  return N <= 40 ? 3 * BH <= wkv7_pair_slots(N) : BH <= 64;
 }
 
 size_t wkv7_parallel_scratch_floats(int B, int T, int H, int N) {
-  const size_t C = (size_t)T / WKV_PAR_K;
-  return 3 * (size_t)B * C * H * N * N + (size_t)B * H * N * N;
+  int C = 0, K = 0;
+  wkv7_parallel_plan(B, T, H, N, &C, &K);
+  // U, P and the chunk start states; Q ([K, N] per chunk and head)
+  return 3 * (size_t)B * C * H * N * N + (size_t)B * C * H * K * N;
+}
+
+// Scratch for any B, T with B*T <= rows and T >= 256 (the engine's workspace):
+// B*C*H <= max(slots, 2*B*H) + B*H*ceil(T / Kmax) and B*C*H*K <= 2*B*H*T.
+size_t wkv7_parallel_scratch_bound(size_t rows, int H, int N) {
+  if (rows < 256) return 0;  // no sequence of 256 tokens fits
+  const size_t bh = (rows / 256) * (size_t)H;
+  const size_t items = std::max<size_t>((size_t)wkv7_pair_slots(N), 2 * bh) +
+                       (size_t)H * (rows / (size_t)wkv7_correct_max_chunk(N) + rows / 256 + 1);
+  return 3 * items * N * N + 2 * rows * (size_t)H * N + 16;
 }
 
 yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
                            int B, int T, int H, int N, float* scratch, cudaStream_t st) {
-  constexpr int K = WKV_PAR_K;
-  const int C = T / K, Tm = C * K;
+  int C = 0, K = 0;
+  wkv7_parallel_plan(B, T, H, N, &C, &K);
   const size_t per = (size_t)B * C * H * N * N;
   float* U = scratch;
   float* P = U + per;
   float* S_start = P + per;
-  float* S_mid = S_start + per;  // state after the whole chunks when a tail follows
-  const bool tail = Tm < T;
-  yuf_status_t rc = wkv7_summary_dispatch(w, k, v, a, b, U, P, B * C, K, H, N, T, C, st);
+  float* Qm = S_start + per;  // [B*C, H, K, N]
+  // 1. one pass: y from a zero start (into y), Q, U, P
+  yuf_status_t rc = wkv7_pair_dispatch(r, w, k, v, a, b, y, Qm, U, P, B * C, K, H, N, T, C, st);
   if (rc != YUF_OK) return rc;
+  // 2. chunk start states and the final state
   switch (N) {
 #define CASE(NN) \
-  case NN: rc = launch_carry<NN>(U, P, s0, S_start, tail ? S_mid : s_out, B, C, H, st); break;
+  case NN: rc = launch_carry<NN>(U, P, s0, S_start, s_out, B, C, H, st); break;
     CASE(16) CASE(32) CASE(40) CASE(48) CASE(64) CASE(96) CASE(128)
 #undef CASE
     default:
@@ -154,12 +195,8 @@ yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const
       return YUF_ERR_UNSUPPORTED;
   }
   if (rc != YUF_OK) return rc;
-  rc = wkv7_dispatch_strided(r, w, k, v, a, b, S_start, y, nullptr, nullptr, nullptr, B * C, K, H, N,
-                             false, T, C, st);
-  if (rc != YUF_OK || !tail) return rc;
-  const size_t off = (size_t)Tm * H * N;
-  return wkv7_dispatch_strided(r + off, w + off, k + off, v + off, a + off, b + off, S_mid, y + off,
-                               s_out, nullptr, nullptr, B, T - Tm, H, N, false, T, 1, st);
+  // 3. y += S_start q_t per (chunk, head); chunk 0 of a zero start needs none
+  return wkv7_correct_dispatch(S_start, Qm, y, B * C, K, H, N, T, C, s0 == nullptr, st);
 }
 
 }  // namespace yuf
