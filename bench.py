@@ -12,9 +12,12 @@ NCCL only for the start/stop barrier and the max-over-ranks time).
 * ``e2e``     the same metric through the public API (``cuda_ops.rwkv7_cuda``)
               with pinned HOST buffers: every step copies the inputs to the
               device and y + final state back.
-* ``roofline``  the scan kernel's algorithmic bytes (6 inputs + y per (b,t,h):
-              7*N*4 B; plus the final state N*N*4 per (b,h)) over its measured
-              time, against the measured HBM copy bandwidth.
+* ``roofline``  the scan's algorithmic bytes (6 inputs + y per (b,t,h):
+              7*N*4 B; plus the final state N*N*4 per (b,h)) over the measured
+              time of one step, against the measured HBM copy bandwidth.  At
+              this shape the step is the time-parallel scan: two launches,
+              wkv7_pairw_kernel<40> (chunk summaries) and
+              wkv7_carry_correct_kernel<40> (carried states, output correction).
 * ``cpu_baseline``  the C restatement of the reference recurrence
               (oracle/scans_ref.c, OpenMP over (b,h)) on this host's cores.
 
@@ -43,6 +46,7 @@ ALGO_BYTES = B * T * H * 7 * N * 4 + B * H * N * N * 4
 METRIC = "wkv7_scan_prefill_tokens_per_s"
 UNIT = "tokens/s"
 WORKLOAD = "config2_wkv7_scan_op_B8_T2048_H16_N40_fp32"
+LAUNCHES_PER_STEP = 2  # time-parallel scan: chunk summaries + carry/correction
 
 
 def parse():
@@ -68,12 +72,13 @@ def peaks():
 
 
 def profiled_traffic():
-    """dram bytes per launch of the scan kernel from the committed ncu summary."""
-    f = ROOT / "profiles" / "wkv7_scan_config2.txt"
+    """DRAM bytes of one headline step (all of its kernels) from the committed
+    ncu summary of the time-parallel scan on the config-2 workload."""
+    f = ROOT / "profiles" / "wkv7_time_parallel_config2.txt"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
-        if line.startswith("dram_bytes_per_launch:"):
+        if line.startswith("dram_bytes_per_step:"):
             return float(line.split(":", 1)[1])
     return None
 
@@ -350,9 +355,10 @@ def run_ours(args):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "wkv7_scan_kernel<40,0,false> (sequential; AUTO for B*H = 128)",
-                         "algorithmic_bytes_per_launch": ALGO_BYTES},
-            "gpu_launches": args.steps,
+                         "kernel": "wkv7 time-parallel scan (AUTO at B*H = 128): "
+                                   "wkv7_pairw_kernel<40> + wkv7_carry_correct_kernel<40>",
+                         "algorithmic_bytes_per_step": ALGO_BYTES},
+            "gpu_launches": LAUNCHES_PER_STEP * args.steps,
             "clocks": clocks.summary(),
             "extra": extra,
         }

@@ -215,14 +215,30 @@ __global__ void __launch_bounds__(PairCfg<N>::NT, 1)
 // columns g*C .. g*C+C-1.  Every per-token column value a lane reads from shared
 // memory then feeds 2R rows, so the kernel is bound by the FMA pipe rather than
 // by shared-memory delivery (the multi-warp kernel above feeds 4 rows per read).
+//
+// Decay-scaled state.  Inside a group of TS tokens the lanes carry
+// S'_t = S_t / gamma_t (column-wise, gamma_t = w_1 ... w_t since the group
+// started), for which the update loses its decay product:
+//   S'_t = S'_{t-1} + sa_t (b_t / gamma_t)^T + v_t (k_t / gamma_t)^T,
+//   sa_t = S'_{t-1} (gamma_{t-1} a_t),   y_t = S'_t (gamma_t r_t)
+// -- two FMAs per zero-start element and one per identity-start element
+// instead of three and two.  The scaled vectors are made once per token and
+// column when the group is staged; at the group end S = S' gamma_end, so
+// gamma stays >= 0.545^TS (no underflow, 1/gamma <= 128 for TS = 8).
+//
 // Per token: the two row dot products with a (all-reduced over the 4 lanes of a
 // row group), the update, and the two dot products with r, reduce-scattered so
 // that each lane finishes a few of the 2N outputs and stores them directly (a
 // warp's stores of one token cover one contiguous row of y and of Q).
-// Staging per group of TS tokens: cp.async brings the raw rows, one pass turns
-// them into the lane layout (and the decay into exp(-0.6065 sigmoid(w))), then
-// the next group's copy starts while this group is scanned; single buffers keep
-// the block at 16.6 KB of shared memory (N = 40), 12 resident warps per SM.
+// Staging per group: cp.async brings the raw rows, one pass (a lane per column
+// pair, sequential over the group's tokens) makes the scaled vectors in the
+// lane layout, then the next group's copy starts while this group is scanned;
+// single buffers keep the block small (15 KB at N = 40, 12 warps per SM).
+#ifndef YUF_PAIRW_UNROLL
+#define YUF_PAIRW_UNROLL 4
+#endif
+constexpr int PAIRW_UNROLL = YUF_PAIRW_UNROLL;  // token loop unroll: code size vs. scheduling
+
 template <int N>
 struct PairWCfg {
   static constexpr int G = 4;       // lanes per row group
@@ -233,8 +249,9 @@ struct PairWCfg {
   static constexpr int VP = G * CS;
   static constexpr int TS = 8;                    // tokens per staged group
   static constexpr int RAW = 0;                   // [6][TS][N] raw rows r, w, k, v, a, b
-  static constexpr int PAD = RAW + 6 * TS * N;    // [5][TS][VP] ret, k, a, b, r in lane layout
-  static constexpr int VV = PAD + 5 * TS * VP;    // [TS][N] values
+  static constexpr int PAD = RAW + 6 * TS * N;    // [4][TS][VP] scaled a, b, k, r in lane layout
+  static constexpr int GEND = PAD + 4 * TS * VP;  // [VP] gamma at the group end
+  static constexpr int VV = GEND + VP;            // [TS][N] values
   static constexpr int TOTAL = VV + TS * N;
   static constexpr size_t BYTES = (size_t)TOTAL * sizeof(float);
   static_assert(N % 8 == 0 && C % 2 == 0 && N <= 40, "one-warp pair kernel: N in {16, 32, 40}");
@@ -301,11 +318,11 @@ __global__ void __launch_bounds__(32)
 
   const int ngroups = (T + TS - 1) / TS;
   if (ngroups > 0) stage(0, min(TS, T));
-  const float* Pw = sm + K::PAD + 0 * TS * VP + g * CS;
-  const float* Pk = sm + K::PAD + 1 * TS * VP + g * CS;
-  const float* Pa = sm + K::PAD + 2 * TS * VP + g * CS;
-  const float* Pb = sm + K::PAD + 3 * TS * VP + g * CS;
-  const float* Pr = sm + K::PAD + 4 * TS * VP + g * CS;
+  const float* Pa = sm + K::PAD + 0 * TS * VP + g * CS;
+  const float* Pb = sm + K::PAD + 1 * TS * VP + g * CS;
+  const float* Pk = sm + K::PAD + 2 * TS * VP + g * CS;
+  const float* Pr = sm + K::PAD + 3 * TS * VP + g * CS;
+  const float* Pg = sm + K::GEND + g * CS;
   const float* vv = sm + K::VV;
   const int h = (lane >> 1) & 1, e = lane & 1;  // reduce-scatter roles inside the row group
   const int rbase = i0 + (e ? RH : 0);
@@ -318,91 +335,113 @@ __global__ void __launch_bounds__(32)
     const int Tc = min(TS, T - t0);
     cp_async_wait<0>();
     __syncwarp();
-    // lane layout, two columns at a time (C is even, so a pair never straddles lanes)
-    for (int idx = lane; idx < Tc * N / 2; idx += 32) {
-      const int t = idx / (N / 2), j = 2 * (idx - t * (N / 2));
-      const int pj = K::PAD + t * VP + (j / C) * CS + (j % C);
-      const int rj = t * N + j;
-      const float2 wr = *reinterpret_cast<const float2*>(sm + K::RAW + 1 * TS * N + rj);
-      *reinterpret_cast<float2*>(sm + pj + 0 * TS * VP) =
-          make_float2(__expf(W_SCALE * sigmoidf_fast(wr.x)), __expf(W_SCALE * sigmoidf_fast(wr.y)));
-      *reinterpret_cast<float2*>(sm + pj + 1 * TS * VP) =
-          *reinterpret_cast<const float2*>(sm + K::RAW + 2 * TS * N + rj);
-      *reinterpret_cast<float2*>(sm + pj + 2 * TS * VP) =
-          *reinterpret_cast<const float2*>(sm + K::RAW + 4 * TS * N + rj);
-      *reinterpret_cast<float2*>(sm + pj + 3 * TS * VP) =
-          *reinterpret_cast<const float2*>(sm + K::RAW + 5 * TS * N + rj);
-      *reinterpret_cast<float2*>(sm + pj + 4 * TS * VP) =
-          *reinterpret_cast<const float2*>(sm + K::RAW + 0 * TS * N + rj);
-      *reinterpret_cast<float2*>(sm + K::VV + rj) =
-          *reinterpret_cast<const float2*>(sm + K::RAW + 3 * TS * N + rj);
+    // scaled vectors: a lane per column pair, running gamma over the group's tokens
+    if (lane < N / 2) {
+      const int j = 2 * lane;
+      const int pj = (j / C) * CS + (j % C);  // lane-layout offset of the pair
+      float2 gam = make_float2(1.f, 1.f), ginv = gam;
+      for (int t = 0; t < Tc; ++t) {
+        const int rj = t * N + j;
+        const float2 wr = *reinterpret_cast<const float2*>(sm + K::RAW + 1 * TS * N + rj);
+        const float sx = W_SCALE * sigmoidf_fast(wr.x), sy = W_SCALE * sigmoidf_fast(wr.y);
+        const float2 av = *reinterpret_cast<const float2*>(sm + K::RAW + 4 * TS * N + rj);
+        const float2 bv = *reinterpret_cast<const float2*>(sm + K::RAW + 5 * TS * N + rj);
+        const float2 kv = *reinterpret_cast<const float2*>(sm + K::RAW + 2 * TS * N + rj);
+        const float2 rv = *reinterpret_cast<const float2*>(sm + K::RAW + 0 * TS * N + rj);
+        float* d = sm + K::PAD + t * VP + pj;
+        *reinterpret_cast<float2*>(d + 0 * TS * VP) = fmul2(av, gam);  // gamma_{t-1} a_t
+        gam = fmul2(gam, make_float2(__expf(sx), __expf(sy)));
+        ginv = fmul2(ginv, make_float2(__expf(-sx), __expf(-sy)));
+        *reinterpret_cast<float2*>(d + 1 * TS * VP) = fmul2(bv, ginv);  // b_t / gamma_t
+        *reinterpret_cast<float2*>(d + 2 * TS * VP) = fmul2(kv, ginv);  // k_t / gamma_t
+        *reinterpret_cast<float2*>(d + 3 * TS * VP) = fmul2(rv, gam);   // gamma_t r_t
+        *reinterpret_cast<float2*>(sm + K::VV + rj) =
+            *reinterpret_cast<const float2*>(sm + K::RAW + 3 * TS * N + rj);
+      }
+      *reinterpret_cast<float2*>(sm + K::GEND + pj) = gam;
     }
     __syncwarp();
     if (gi + 1 < ngroups) stage(t0 + TS, min(TS, T - t0 - TS));  // raw buffer is free again
 
+    // sa of the group's first token; every later token's sa comes out of the
+    // previous token's pass over the state together with that token's outputs
+    float sU[R], sP[R];
+    {
+      float2 av[C2];
+      load_cols<C>(av, Pa);
 #pragma unroll
+      for (int p = 0; p < R; ++p) {
+        float2 u = make_float2(0.f, 0.f), q = u;
+#pragma unroll
+        for (int c = 0; c < C2; ++c) {
+          u = ffma2(SU[p][c], av[c], u);
+          q = ffma2(SP[p][c], av[c], q);
+        }
+        sU[p] = u.x + u.y;
+        sP[p] = q.x + q.y;
+      }
+#pragma unroll
+      for (int p = 0; p < R; ++p) {
+        sU[p] += __shfl_xor_sync(0xffffffffu, sU[p], 1);
+        sP[p] += __shfl_xor_sync(0xffffffffu, sP[p], 1);
+      }
+#pragma unroll
+      for (int p = 0; p < R; ++p) {
+        sU[p] += __shfl_xor_sync(0xffffffffu, sU[p], 2);
+        sP[p] += __shfl_xor_sync(0xffffffffu, sP[p], 2);
+      }
+    }
+#pragma unroll PAIRW_UNROLL
     for (int t = 0; t < TS; ++t) {
       if (t < Tc) {
         const int o = t * VP;
-        float2 av[C2];
-        load_cols<C>(av, Pa + o);
-        float sU[R], sP[R];
+        {
+          float2 bv[C2], kv[C2];
+          load_cols<C>(bv, Pb + o);
+          load_cols<C>(kv, Pk + o);
+          float vr[R];
 #pragma unroll
-        for (int p = 0; p < R; ++p) {
-          float2 u = make_float2(0.f, 0.f), q = u;
+          for (int p = 0; p < R; ++p) vr[p] = vv[t * N + i0 + p];
 #pragma unroll
-          for (int c = 0; c < C2; ++c) {
-            u = ffma2(SU[p][c], av[c], u);
-            q = ffma2(SP[p][c], av[c], q);
-          }
-          sU[p] = u.x + u.y;
-          sP[p] = q.x + q.y;
+          for (int p = 0; p < R; ++p)
+#pragma unroll
+            for (int c = 0; c < C2; ++c) {
+              SU[p][c] = ffma2(f2(sU[p]), bv[c], ffma2(f2(vr[p]), kv[c], SU[p][c]));
+              SP[p][c] = ffma2(f2(sP[p]), bv[c], SP[p][c]);
+            }
         }
-#pragma unroll
-        for (int p = 0; p < R; ++p) {
-          sU[p] += __shfl_xor_sync(0xffffffffu, sU[p], 1);
-          sP[p] += __shfl_xor_sync(0xffffffffu, sP[p], 1);
-        }
-#pragma unroll
-        for (int p = 0; p < R; ++p) {
-          sU[p] += __shfl_xor_sync(0xffffffffu, sU[p], 2);
-          sP[p] += __shfl_xor_sync(0xffffffffu, sP[p], 2);
-        }
-        float2 wv[C2], bv[C2], kv[C2];
-        load_cols<C>(wv, Pw + o);
-        load_cols<C>(bv, Pb + o);
-        load_cols<C>(kv, Pk + o);
-        float vr[R];
-#pragma unroll
-        for (int p = 0; p < R; ++p) vr[p] = vv[t * N + i0 + p];
-#pragma unroll
-        for (int p = 0; p < R; ++p)
-#pragma unroll
-          for (int c = 0; c < C2; ++c) {
-            SU[p][c] = ffma2(SU[p][c], wv[c], ffma2(f2(sU[p]), bv[c], fmul2(f2(vr[p]), kv[c])));
-            SP[p][c] = ffma2(SP[p][c], wv[c], fmul2(f2(sP[p]), bv[c]));
-          }
-        float2 rv[C2];
+        // one pass over the updated state: outputs of token t and sa of token
+        // t + 1 (for the group's last token the a row read is not a token's and
+        // its sa is dropped)
+        float2 rv[C2], av[C2];
         load_cols<C>(rv, Pr + o);
+        load_cols<C>(av, Pa + o + VP);
         float yo[2 * R];  // [0, R): zero-start outputs, [R, 2R): q
 #pragma unroll
         for (int p = 0; p < R; ++p) {
-          float2 u = make_float2(0.f, 0.f), q = u;
+          float2 u = make_float2(0.f, 0.f), q = u, ua = u, qa = u;
 #pragma unroll
           for (int c = 0; c < C2; ++c) {
             u = ffma2(SU[p][c], rv[c], u);
             q = ffma2(SP[p][c], rv[c], q);
+            ua = ffma2(SU[p][c], av[c], ua);
+            qa = ffma2(SP[p][c], av[c], qa);
           }
           yo[p] = u.x + u.y;
           yo[R + p] = q.x + q.y;
+          sU[p] = ua.x + ua.y;
+          sP[p] = qa.x + qa.y;
         }
-        // reduce-scatter over the row group: lanes with h = 0 keep the zero-start
-        // outputs, h = 1 the q values; then e = 0 keeps rows [0, RH), e = 1 the rest
+        // reduce-scatter of the outputs over the row group (lanes with h = 0 keep
+        // the zero-start outputs, h = 1 the q values; then e = 0 keeps rows
+        // [0, RH), e = 1 the rest), interleaved with the all-reduce of sa
         float kept[R];
 #pragma unroll
         for (int p = 0; p < R; ++p) {
           const float send = h ? yo[p] : yo[R + p];
           kept[p] = (h ? yo[R + p] : yo[p]) + __shfl_xor_sync(0xffffffffu, send, 2);
+          sU[p] += __shfl_xor_sync(0xffffffffu, sU[p], 1);
+          sP[p] += __shfl_xor_sync(0xffffffffu, sP[p], 1);
         }
         float* orow = obase + (size_t)(t0 + t) * ostride;
 #pragma unroll
@@ -412,9 +451,26 @@ __global__ void __launch_bounds__(32)
           const float fin = (e ? hi : kept[p]) + __shfl_xor_sync(0xffffffffu, send, 1);
           if (p < nk) orow[p] = fin;
         }
+#pragma unroll
+        for (int p = 0; p < R; ++p) {
+          sU[p] += __shfl_xor_sync(0xffffffffu, sU[p], 2);
+          sP[p] += __shfl_xor_sync(0xffffffffu, sP[p], 2);
+        }
       }
     }
-    __syncwarp();  // the next group's transform overwrites the lane layout
+    // back to the unscaled state: S = S' gamma_end
+    {
+      float2 ge[C2];
+      load_cols<C>(ge, Pg);
+#pragma unroll
+      for (int p = 0; p < R; ++p)
+#pragma unroll
+        for (int c = 0; c < C2; ++c) {
+          SU[p][c] = fmul2(SU[p][c], ge[c]);
+          SP[p][c] = fmul2(SP[p][c], ge[c]);
+        }
+    }
+    __syncwarp();  // the next group's staging pass overwrites the lane layout
   }
 #pragma unroll
   for (int p = 0; p < R; ++p) {
@@ -427,23 +483,25 @@ __global__ void __launch_bounds__(32)
   }
 }
 
-// y[t][i] += sum_j S0[i][j] q_t[j] over one (chunk, head).  Thread (tq, ig)
-// owns tokens 4tq .. 4tq+3 and the RI consecutive rows ig*RI ..; its y values
-// are loaded into registers before the product so their latency overlaps it.
-// S0 and the chunk's Q sit in shared memory with rows padded to N + 1 floats
-// (conflict-free reads across the token groups of a warp).
+// y[t][i] += sum_j S0[i][j] q_t[j] over one (chunk, head).  cp.async stages S0
+// and the chunk's Q in shared memory (rows padded to N + 4 floats: 16-byte rows,
+// and the token rows a warp reads at once land on distinct banks).  Thread
+// (tq, ig) owns the tokens tq, tq + ntq, tq + 2 ntq, tq + 3 ntq of a pass and the
+// RI consecutive rows ig*RI ..; its y values are loaded into registers before the
+// product so their latency overlaps the staging and the product.
 template <int N>
 struct CorrCfg {
-  static constexpr int RI = N / 4 < 16 ? N / 4 : 16;  // rows per thread
+  static constexpr int RI = N / 8 < 16 ? N / 8 : 16;  // rows per thread
   static constexpr int IG = N / RI;                   // row groups
-  static constexpr int NP = N + 1;
+  static constexpr int NP = N + 4;
+  static constexpr int MAXT = N <= 64 ? 512 : 256;    // threads per block at most
 };
 
 template <int N>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(CorrCfg<N>::MAXT)
     wkv7_correct_kernel(const float* __restrict__ S0, const float* __restrict__ Q,
                         float* __restrict__ y, int K_, int H, int Tstride, int Cper, int skip_first) {
-  constexpr int RI = CorrCfg<N>::RI, IG = CorrCfg<N>::IG, NP = CorrCfg<N>::NP;
+  constexpr int RI = CorrCfg<N>::RI, IG = CorrCfg<N>::IG, NP = CorrCfg<N>::NP, Q4 = N / 4;
   extern __shared__ float4 corr_sm[];
   float* Ss = reinterpret_cast<float*>(corr_sm);  // [N][NP]
   float* Qs = Ss + N * NP;                        // [K][NP]
@@ -454,52 +512,49 @@ __global__ void __launch_bounds__(256)
   const int tid = threadIdx.x, nt = blockDim.x;  // nt is a multiple of IG
   const float* S0h = S0 + (size_t)bh * N * N;
   const float* Qg = Q + (size_t)bh * K_ * N;
-  for (int q = tid; q < N * N / 4; q += nt) {
-    const float4 x = reinterpret_cast<const float4*>(S0h)[q];
-    const int i = (4 * q) / N, j = 4 * q - i * N;
-    float* d = Ss + i * NP + j;
-    d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+  for (int q = tid; q < N * Q4; q += nt) {
+    const int i = q / Q4, c = q - i * Q4;
+    cp_async_16(Ss + i * NP + 4 * c, S0h + i * N + 4 * c);
   }
-  for (int q = tid; q < T * N / 4; q += nt) {
-    const float4 x = reinterpret_cast<const float4*>(Qg)[q];
-    const int t = (4 * q) / N, j = 4 * q - t * N;
-    float* d = Qs + t * NP + j;
-    d[0] = x.x; d[1] = x.y; d[2] = x.z; d[3] = x.w;
+  for (int q = tid; q < T * Q4; q += nt) {
+    const int t = q / Q4, c = q - t * Q4;
+    cp_async_16(Qs + t * NP + 4 * c, Qg + t * N + 4 * c);
   }
+  cp_async_commit();
   const size_t tok_stride = (size_t)H * N;
   const size_t head_off = item_head_off(bb, hh, K_, H, N, Tstride, Cper);
   const int ig = tid % IG, i0 = ig * RI;
-  const int tstep = 4 * (nt / IG);
+  const int tq = tid / IG, ntq = nt / IG;
   float yv[4][RI];
   auto load_y = [&](int t0) {
 #pragma unroll
     for (int tt = 0; tt < 4; ++tt) {
-      if (t0 + tt < T) {
-        const float* yr = y + head_off + (size_t)(t0 + tt) * tok_stride + i0;
+      const int t = t0 + tt * ntq;
+      if (t < T) {
+        const float* yr = y + head_off + (size_t)t * tok_stride + i0;
 #pragma unroll
-        for (int q = 0; q < RI; q += 2) {
-          const float2 x = *reinterpret_cast<const float2*>(yr + q);
-          yv[tt][q] = x.x;
-          yv[tt][q + 1] = x.y;
-        }
+        for (int q = 0; q < RI; ++q) yv[tt][q] = yr[q];
       }
     }
   };
-  const int t_first = (tid / IG) * 4;
-  load_y(t_first);  // issued before the barrier: overlaps the staging above
+  load_y(tq);  // issued before the barrier: overlaps the staging
+  cp_async_wait<0>();
   __syncthreads();  // S0 and Q staged
-  for (int t0 = t_first; t0 < T; t0 += tstep) {
-    if (t0 != t_first) load_y(t0);
+  for (int t0 = tq; t0 < T; t0 += 4 * ntq) {
+    if (t0 != tq) load_y(t0);
+    int trow[4];
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt) trow[tt] = min(t0 + tt * ntq, T - 1) * NP;  // rows past T: unused
     float acc[4][RI];
 #pragma unroll
     for (int tt = 0; tt < 4; ++tt)
 #pragma unroll
       for (int q = 0; q < RI; ++q) acc[tt][q] = 0.f;
-#pragma unroll 4
+#pragma unroll 2
     for (int j = 0; j < N; ++j) {
       float qv[4];
 #pragma unroll
-      for (int tt = 0; tt < 4; ++tt) qv[tt] = Qs[(t0 + tt) * NP + j];  // rows past T: unused
+      for (int tt = 0; tt < 4; ++tt) qv[tt] = Qs[trow[tt] + j];
 #pragma unroll
       for (int q = 0; q < RI; ++q) {
         const float sv = Ss[(i0 + q) * NP + j];
@@ -509,12 +564,11 @@ __global__ void __launch_bounds__(256)
     }
 #pragma unroll
     for (int tt = 0; tt < 4; ++tt) {
-      if (t0 + tt < T) {
-        float* yr = y + head_off + (size_t)(t0 + tt) * tok_stride + i0;
+      const int t = t0 + tt * ntq;
+      if (t < T) {
+        float* yr = y + head_off + (size_t)t * tok_stride + i0;
 #pragma unroll
-        for (int q = 0; q < RI; q += 2)
-          *reinterpret_cast<float2*>(yr + q) =
-              make_float2(yv[tt][q] + acc[tt][q], yv[tt][q + 1] + acc[tt][q + 1]);
+        for (int q = 0; q < RI; ++q) yr[q] = yv[tt][q] + acc[tt][q];
       }
     }
   }
@@ -563,7 +617,7 @@ int wkv7_pair_slots(int N) {
 // Largest chunk the correction kernel can stage for head size N (multiple of 8).
 int wkv7_correct_max_chunk(int N) {
   const int floats = 200 * 1024 / 4;
-  const int kmax = floats / (N + 1) - N;
+  const int kmax = floats / (N + 4) - N;
   return kmax / 8 * 8;
 }
 
@@ -608,7 +662,7 @@ yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, 
 
 yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, int items, int K, int H,
                                    int N, int Tstride, int Cper, bool skip_first, cudaStream_t st) {
-  const size_t bytes = ((size_t)N * (N + 1) + (size_t)K * (N + 1)) * sizeof(float);
+  const size_t bytes = ((size_t)N + K) * (N + 4) * sizeof(float);
   switch (N) {
 #define CASE(NN)                                                                                   \
   case NN: {                                                                                       \
@@ -621,7 +675,7 @@ yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, in
     }                                                                                              \
     constexpr int IG = CorrCfg<NN>::IG;                                                            \
     int nt = ((K + 3) / 4) * IG;                                                                   \
-    nt = std::min(256, (nt + 31) / 32 * 32);                                                       \
+    nt = std::min(CorrCfg<NN>::MAXT, (nt + 31) / 32 * 32);                                         \
     nt = std::max(nt, 32) / IG * IG;                                                               \
     kern<<<items * H, nt, bytes, st>>>(S0, Q, y, K, H, Tstride, Cper, skip_first ? 1 : 0);         \
     return check_launch("wkv7_correct_kernel");                                                    \

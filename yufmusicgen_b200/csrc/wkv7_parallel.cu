@@ -28,7 +28,7 @@
 
 namespace yuf {
 
-constexpr int WKV_PAR_CMAX = 48;  // the carry is sequential over chunks
+constexpr int WKV_PAR_CMAX = 32;  // the carry is sequential over chunks
 
 yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, const float* v,
                                 const float* a, const float* b, float* y, float* Q, float* U, float* P,
@@ -38,95 +38,133 @@ yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, in
 int wkv7_pair_slots(int N);
 int wkv7_correct_max_chunk(int N);
 
-// One CTA per (sequence, head); thread (ib, jb) owns a RB x 4 block of S.
-template <int N, int RB>
-__global__ void __launch_bounds__(N * N / (RB * 4))
+// Pass 2: per (sequence, head) the chunk start states S_c = S_{c-1} P_c + U_c.
+// State rows are independent recurrences, so each (sequence, head) is split
+// into RS row blocks of NR = N/RS rows, one CTA each (RS = 4, 2 or 1: the most
+// that fit in one wave of resident blocks, since a CTA walks every chunk of its
+// sequence).  Thread = 1 row x 4 columns of the block.  P_c and the block's rows
+// of U_c come in through a cp.async ring of up to 4 stages: every chunk's inputs are
+// already in memory when the kernel starts, so the chain of chunks waits on the
+// memory latency only once.
+template <int N, int RS>
+struct CarryCfg {
+  static constexpr int NR = N / RS;
+  static constexpr int NT = NR * N / 4;
+  static constexpr int STAGE = N * N + NR * N;  // P_c and the block's rows of U_c
+  static constexpr int FIT = (200 * 1024 / 4 - NR * N) / STAGE;
+  static constexpr int DEPTH = FIT < 2 ? 2 : (FIT > 4 ? 4 : FIT);  // ring stages
+  static constexpr int FLOATS = NR * N + DEPTH * STAGE;
+  static constexpr size_t BYTES = (size_t)FLOATS * sizeof(float);
+};
+
+template <int N, int RS>
+__global__ void __launch_bounds__(CarryCfg<N, RS>::NT)
     wkv7_carry_kernel(const float* __restrict__ U, const float* __restrict__ P, const float* s0,
                       float* __restrict__ S_start, float* s_out, int C, int H) {
-  constexpr int NT = N * N / (RB * 4);
-  constexpr int NN = N * N;
-  constexpr bool PREU = N <= 64;                     // U prefetched too when it fits
+  constexpr int NR = CarryCfg<N, RS>::NR, NT = CarryCfg<N, RS>::NT, NN = N * N;
+  constexpr int STAGE = CarryCfg<N, RS>::STAGE, D = CarryCfg<N, RS>::DEPTH;
   extern __shared__ float4 carry_sm[];
-  float* Ss = reinterpret_cast<float*>(carry_sm);   // [N][N] running state
-  float* Pb0 = Ss + NN;                              // [2][N][N] transitions, double buffered
-  float* Ub0 = Pb0 + 2 * NN;                         // [2][N][N] contributions (PREU only)
-  const int bh = blockIdx.x;
+  float* Ss = reinterpret_cast<float*>(carry_sm);  // [NR][N] rows of the running state
+  float* ring = Ss + NR * N;                        // [D][N*N + NR*N]: P_c, then rows of U_c
+  const int bh = blockIdx.x / RS, rb = blockIdx.x - bh * RS;
+  const int r0 = rb * NR;
   const int s = bh / H, h = bh - s * H;
   const int tid = threadIdx.x;
-  const int ib = tid / (N / 4), jb = tid - ib * (N / 4);
-  const int i0 = ib * RB, j0 = jb * 4;
-  const float* s0p = s0 ? s0 + (size_t)bh * NN : nullptr;
-  for (int q = tid; q < NN; q += NT) Ss[q] = s0p ? s0p[q] : 0.f;
-  auto fetch = [&](int c, int buf) {
-    const size_t off = (((size_t)s * C + c) * H + h) * NN;
-    for (int q = tid; q < NN / 4; q += NT) {
-      cp_async_16(Pb0 + buf * NN + 4 * q, P + off + 4 * q);
-      if (PREU) cp_async_16(Ub0 + buf * NN + 4 * q, U + off + 4 * q);
+  const int i = tid / (N / 4), j0 = (tid % (N / 4)) * 4;
+  const size_t row_off = (size_t)r0 * N;
+  const float* s0p = s0 ? s0 + (size_t)bh * NN + row_off : nullptr;
+  for (int q = tid; q < NR * N; q += NT) Ss[q] = s0p ? s0p[q] : 0.f;
+  auto fetch = [&](int c) {  // always commits a group (empty past the last chunk)
+    if (c < C) {
+      float* dst = ring + (c % D) * STAGE;
+      const size_t off = (((size_t)s * C + c) * H + h) * NN;
+      for (int q = tid; q < NN / 4; q += NT) cp_async_16(dst + 4 * q, P + off + 4 * q);
+      for (int q = tid; q < NR * N / 4; q += NT)
+        cp_async_16(dst + NN + 4 * q, U + off + row_off + 4 * q);
     }
     cp_async_commit();
   };
-  if (C > 0) fetch(0, 0);
+#pragma unroll
+  for (int c = 0; c < D - 1; ++c) fetch(c);
   for (int c = 0; c < C; ++c) {
-    const int buf = c & 1;
-    __syncthreads();  // Ss final for this chunk; buffer buf^1 free
+    __syncthreads();  // Ss final for this chunk; stage (c - 1) % D free
+    fetch(c + D - 1);
     {
-      float* dst = S_start + (((size_t)s * C + c) * H + h) * NN;
-      for (int q = tid; q < NN / 4; q += NT)
+      float* dst = S_start + (((size_t)s * C + c) * H + h) * NN + row_off;
+      for (int q = tid; q < NR * N / 4; q += NT)
         reinterpret_cast<float4*>(dst)[q] = reinterpret_cast<const float4*>(Ss)[q];
     }
-    if (c + 1 < C) {
-      fetch(c + 1, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    cp_async_wait<D - 1>();  // chunk c's group landed
     __syncthreads();
-    float acc[RB][4];
-    const float* Uc = PREU ? Ub0 + buf * NN : U + (((size_t)s * C + c) * H + h) * NN;
-#pragma unroll
-    for (int r = 0; r < RB; ++r) {
-      const float4 u = *reinterpret_cast<const float4*>(Uc + (i0 + r) * N + j0);
-      acc[r][0] = u.x; acc[r][1] = u.y; acc[r][2] = u.z; acc[r][3] = u.w;
-    }
-    const float* Pc = Pb0 + buf * NN;
-#pragma unroll 4
-    for (int l = 0; l < N; ++l) {
-      const float4 p = *reinterpret_cast<const float4*>(Pc + l * N + j0);
-#pragma unroll
-      for (int r = 0; r < RB; ++r) {
-        const float sv = Ss[(i0 + r) * N + l];
-        acc[r][0] = fmaf(sv, p.x, acc[r][0]);
-        acc[r][1] = fmaf(sv, p.y, acc[r][1]);
-        acc[r][2] = fmaf(sv, p.z, acc[r][2]);
-        acc[r][3] = fmaf(sv, p.w, acc[r][3]);
-      }
+    const float* Pc = ring + (c % D) * STAGE;
+    float4 acc = *reinterpret_cast<const float4*>(Pc + NN + i * N + j0);
+    float4 acc2 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int l = 0; l < N; l += 2) {
+      const float4 p0 = *reinterpret_cast<const float4*>(Pc + l * N + j0);
+      const float4 p1 = *reinterpret_cast<const float4*>(Pc + (l + 1) * N + j0);
+      const float2 sv = *reinterpret_cast<const float2*>(Ss + i * N + l);
+      acc.x = fmaf(sv.x, p0.x, acc.x); acc.y = fmaf(sv.x, p0.y, acc.y);
+      acc.z = fmaf(sv.x, p0.z, acc.z); acc.w = fmaf(sv.x, p0.w, acc.w);
+      acc2.x = fmaf(sv.y, p1.x, acc2.x); acc2.y = fmaf(sv.y, p1.y, acc2.y);
+      acc2.z = fmaf(sv.y, p1.z, acc2.z); acc2.w = fmaf(sv.y, p1.w, acc2.w);
     }
     __syncthreads();  // every read of Ss done
-#pragma unroll
-    for (int r = 0; r < RB; ++r)
-      *reinterpret_cast<float4*>(&Ss[(i0 + r) * N + j0]) =
-          make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+    *reinterpret_cast<float4*>(Ss + i * N + j0) =
+        make_float4(acc.x + acc2.x, acc.y + acc2.y, acc.z + acc2.z, acc.w + acc2.w);
   }
+  cp_async_wait<0>();
   __syncthreads();
   if (s_out)
-    for (int q = tid; q < NN; q += NT) s_out[(size_t)bh * NN + q] = Ss[q];
+    for (int q = tid; q < NR * N; q += NT) s_out[(size_t)bh * NN + row_off + q] = Ss[q];
 }
 
-template <int N>
-static yuf_status_t launch_carry(const float* U, const float* P, const float* s0, float* S_start,
-                                 float* s_out, int B, int C, int H, cudaStream_t st) {
-  constexpr int RB = N >= 96 ? 4 : 2;
-  const size_t bytes = (N <= 64 ? 5 : 3) * (size_t)N * N * sizeof(float);
-  auto kern = wkv7_carry_kernel<N, RB>;
-  if (bytes > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+template <int N, int RS>
+static yuf_status_t launch_carry_rs(const float* U, const float* P, const float* s0, float* S_start,
+                                    float* s_out, int B, int C, int H, cudaStream_t st) {
+  using Cf = CarryCfg<N, RS>;
+  auto kern = wkv7_carry_kernel<N, RS>;
+  if (Cf::BYTES > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::BYTES);
     if (e != cudaSuccess) {
       set_error("wkv7 carry: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
       return YUF_ERR_CUDA;
     }
   }
-  kern<<<B * H, N * N / (RB * 4), bytes, st>>>(U, P, s0, S_start, s_out, C, H);
+  kern<<<B * H * RS, Cf::NT, Cf::BYTES, st>>>(U, P, s0, S_start, s_out, C, H);
   return check_launch("wkv7_carry_kernel");
+}
+
+// Resident blocks of a kernel per device (blocks per SM x SMs), 1 when unknown.
+template <typename Kern>
+static long long resident_blocks(Kern kern, int threads, size_t bytes) {
+  int dev = 0, sms = 148, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (bytes > 48 * 1024)
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
+  return (long long)std::max(1, per_sm) * sms;
+}
+
+template <int N>
+static yuf_status_t launch_carry(const float* U, const float* P, const float* s0, float* S_start,
+                                 float* s_out, int B, int C, int H, cudaStream_t st) {
+  // RS = 4 always has a legal block size; 2 and 1 only while N*N/8 resp. N*N/4
+  // threads fit in a block
+  const long long BH = (long long)B * H;
+  if (4 * BH <= resident_blocks(wkv7_carry_kernel<N, 4>, CarryCfg<N, 4>::NT, CarryCfg<N, 4>::BYTES))
+    return launch_carry_rs<N, 4>(U, P, s0, S_start, s_out, B, C, H, st);
+  if constexpr (CarryCfg<N, 2>::NT <= 1024) {
+    if (2 * BH <= resident_blocks(wkv7_carry_kernel<N, 2>, CarryCfg<N, 2>::NT, CarryCfg<N, 2>::BYTES))
+      return launch_carry_rs<N, 2>(U, P, s0, S_start, s_out, B, C, H, st);
+    if constexpr (CarryCfg<N, 1>::NT <= 1024)
+      return launch_carry_rs<N, 1>(U, P, s0, S_start, s_out, B, C, H, st);
+  }
+  return launch_carry_rs<N, 4>(U, P, s0, S_start, s_out, B, C, H, st);  // more than one wave
 }
 
 // Chunks per sequence and chunk length for B sequences of T tokens.
