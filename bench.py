@@ -15,9 +15,9 @@ NCCL only for the start/stop barrier and the max-over-ranks time).
 * ``roofline``  the scan's algorithmic bytes (6 inputs + y per (b,t,h):
               7*N*4 B; plus the final state N*N*4 per (b,h)) over the measured
               time of one step, against the measured HBM copy bandwidth.  At
-              this shape the step is the time-parallel scan: two launches,
-              wkv7_pairw_kernel<40> (chunk summaries) and
-              wkv7_carry_correct_kernel<40> (carried states, output correction).
+              this shape the step is the time-parallel scan: three launches,
+              wkv7_pairw_kernel<40> (chunk summaries), wkv7_carry_kernel<40>
+              (carried states) and wkv7_correct_kernel<40> (output correction).
 * ``cpu_baseline``  the C restatement of the reference recurrence
               (oracle/scans_ref.c, OpenMP over (b,h)) on this host's cores.
 
@@ -46,7 +46,7 @@ ALGO_BYTES = B * T * H * 7 * N * 4 + B * H * N * N * 4
 METRIC = "wkv7_scan_prefill_tokens_per_s"
 UNIT = "tokens/s"
 WORKLOAD = "config2_wkv7_scan_op_B8_T2048_H16_N40_fp32"
-LAUNCHES_PER_STEP = 2  # time-parallel scan: chunk summaries + carry/correction
+LAUNCHES_PER_STEP = 3  # time-parallel scan: chunk summaries, carry, output correction
 
 
 def parse():
@@ -356,7 +356,8 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "wkv7 time-parallel scan (AUTO at B*H = 128): "
-                                   "wkv7_pairw_kernel<40> + wkv7_carry_correct_kernel<40>",
+                                   "wkv7_pairw_kernel<40> + wkv7_carry_kernel<40> + "
+                                   "wkv7_correct_kernel<40>",
                          "algorithmic_bytes_per_step": ALGO_BYTES},
             "gpu_launches": LAUNCHES_PER_STEP * args.steps,
             "clocks": clocks.summary(),

@@ -81,3 +81,63 @@ constexpr int conflict_free_stride(int C, int G) {
 }
 
 }  // namespace yuf
+
+namespace yuf {
+// Tensor-core fp32 products with near-fp32 accuracy ("3xTF32"): each operand x
+// is split into hi = x with its 13 low mantissa bits cleared (a tf32 value) and
+// lo = x - hi (exact in fp32; the tensor core reads its top 19 bits), and
+// a*b = ah*bh + ah*bl + al*bh, with al*bl (~2^-20 relative) dropped.  The split
+// is one logic op and one subtraction, no conversion instruction.
+YUF_DEVICE void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = __float_as_uint(x) & 0xffffe000u;
+  lo = __float_as_uint(x - __uint_as_float(hi));
+}
+// D += A B for one m16n8k8 tile (A row-major 16x8, B 8x8 given by columns).
+YUF_DEVICE void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+// Fragment values (lane = 4g + q): a = {A[g][q], A[g+8][q], A[g][q+4], A[g+8][q+4]},
+// b = {B[q][g], B[q+4][g]}, d = {D[g][2q], D[g][2q+1], D[g+8][2q], D[g+8][2q+1]}.
+// The three products go to three accumulators (main, and the two cross terms)
+// so that consecutive k-steps form three short dependency chains; the caller
+// sums them once at the end (small terms first).
+struct Acc3 {
+  float d[4], e1[4], e2[4];
+};
+YUF_DEVICE void acc3_init(Acc3& x, float v0, float v1, float v2, float v3) {
+  x.d[0] = v0; x.d[1] = v1; x.d[2] = v2; x.d[3] = v3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x.e1[i] = x.e2[i] = 0.f;
+}
+YUF_DEVICE void mma_3xtf32(Acc3& x, const float (&a)[4], const float (&b)[2]) {
+  uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) split_tf32(a[i], ah[i], al[i]);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) split_tf32(b[i], bh[i], bl[i]);
+  mma_tf32(x.e1, al, bh);
+  mma_tf32(x.e2, ah, bl);
+  mma_tf32(x.d, ah, bh);
+}
+YUF_DEVICE float acc3_get(const Acc3& x, int i) { return x.d[i] + (x.e1[i] + x.e2[i]); }
+YUF_DEVICE void acc_init(Acc3& x, float v0, float v1, float v2, float v3) { acc3_init(x, v0, v1, v2, v3); }
+YUF_DEVICE void acc_init(float (&x)[4], float v0, float v1, float v2, float v3) {
+  x[0] = v0; x[1] = v1; x[2] = v2; x[3] = v3;
+}
+YUF_DEVICE float acc_get(const Acc3& x, int i) { return acc3_get(x, i); }
+YUF_DEVICE float acc_get(const float (&x)[4], int i) { return x[i]; }
+// The same products into one accumulator (for register-tight callers).
+YUF_DEVICE void mma_3xtf32(float (&d)[4], const float (&a)[4], const float (&b)[2]) {
+  uint32_t ah[4], al[4], bh[2], bl[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) split_tf32(a[i], ah[i], al[i]);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) split_tf32(b[i], bh[i], bl[i]);
+  mma_tf32(d, al, bh);
+  mma_tf32(d, ah, bl);
+  mma_tf32(d, ah, bh);
+}
+}  // namespace yuf

@@ -483,93 +483,122 @@ __global__ void __launch_bounds__(32)
   }
 }
 
-// y[t][i] += sum_j S0[i][j] q_t[j] over one (chunk, head).  cp.async stages S0
-// and the chunk's Q in shared memory (rows padded to N + 4 floats: 16-byte rows,
-// and the token rows a warp reads at once land on distinct banks).  Thread
-// (tq, ig) owns the tokens tq, tq + ntq, tq + 2 ntq, tq + 3 ntq of a pass and the
-// RI consecutive rows ig*RI ..; its y values are loaded into registers before the
-// product so their latency overlaps the staging and the product.
+// y[t][i] += sum_j S0[i][j] q_t[j] over one (chunk, head): a [len x N] x
+// [N x N]^T product on the tensor cores (mma.sync m16n8k8, 3xTF32 for near-fp32
+// accuracy).  cp.async stages the chunk's Q (rows padded to N + 4 floats, which
+// makes the A-fragment loads bank-conflict free; rows past len zero-filled up
+// to the 16-row tile); S0 is split once into its tf32 high and low parts in
+// shared memory.  Each warp takes 16-token row tiles across all N/8 column
+// tiles, so an A fragment is loaded and split once per k-step for N/8 products;
+// the accumulators start from y (loaded before the staging completes).  A block
+// covers TW = 80 tokens of a chunk (one tile per warp), so a chunk spreads over
+// several blocks and each block waits on memory once.
 template <int N>
 struct CorrCfg {
-  static constexpr int RI = N / 8 < 16 ? N / 8 : 16;  // rows per thread
-  static constexpr int IG = N / RI;                   // row groups
   static constexpr int NP = N + 4;
-  static constexpr int MAXT = N <= 64 ? 512 : 256;    // threads per block at most
+  static constexpr int WARPS = 5;
+  static constexpr int NT = 32 * WARPS;
+  static constexpr int TW = 16 * WARPS;  // tokens per block: one 16-token tile per warp
 };
 
 template <int N>
-__global__ void __launch_bounds__(CorrCfg<N>::MAXT)
+__global__ void __launch_bounds__(256)
     wkv7_correct_kernel(const float* __restrict__ S0, const float* __restrict__ Q,
-                        float* __restrict__ y, int K_, int H, int Tstride, int Cper, int skip_first) {
-  constexpr int RI = CorrCfg<N>::RI, IG = CorrCfg<N>::IG, NP = CorrCfg<N>::NP, Q4 = N / 4;
+                        float* __restrict__ y, int K_, int H, int Tstride, int Cper, int skip_first,
+                        int parts) {
+  constexpr int NP = CorrCfg<N>::NP, NT = CorrCfg<N>::NT, WARPS = CorrCfg<N>::WARPS, Q4 = N / 4;
+  constexpr int NTL = N / 8, TW = CorrCfg<N>::TW;
   extern __shared__ float4 corr_sm[];
-  float* Ss = reinterpret_cast<float*>(corr_sm);  // [N][NP]
-  float* Qs = Ss + N * NP;                        // [K][NP]
-  const int bh = blockIdx.x;
+  uint32_t* Sh = reinterpret_cast<uint32_t*>(corr_sm);  // [N][NP] tf32 high parts of S0
+  uint32_t* Sl = Sh + N * NP;                            // [N][NP] low parts
+  float* Qs = reinterpret_cast<float*>(Sl + N * NP);     // [TW][NP]
+  const int bh = blockIdx.x / parts, part = blockIdx.x - bh * parts;
   const int bb = bh / H, hh = bh - bb * H;
   if (skip_first && bb % Cper == 0) return;  // chunk 0 starts from the zero state
-  const int T = item_len(bb, K_, Tstride, Cper);
-  const int tid = threadIdx.x, nt = blockDim.x;  // nt is a multiple of IG
+  const int tb = part * TW;                  // first token of this block in the chunk
+  const int T = min(TW, item_len(bb, K_, Tstride, Cper) - tb);
+  if (T <= 0) return;
+  const int T16 = (T + 15) / 16 * 16;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
   const float* S0h = S0 + (size_t)bh * N * N;
-  const float* Qg = Q + (size_t)bh * K_ * N;
-  for (int q = tid; q < N * Q4; q += nt) {
-    const int i = q / Q4, c = q - i * Q4;
-    cp_async_16(Ss + i * NP + 4 * c, S0h + i * N + 4 * c);
-  }
-  for (int q = tid; q < T * Q4; q += nt) {
-    const int t = q / Q4, c = q - t * Q4;
+  const float* Qg = Q + ((size_t)bh * K_ + tb) * N;
+  for (int x = tid; x < T * Q4; x += NT) {
+    const int t = x / Q4, c = x - t * Q4;
     cp_async_16(Qs + t * NP + 4 * c, Qg + t * N + 4 * c);
   }
+  for (int x = tid; x < N * Q4; x += NT) {  // S0 rows, split in place below
+    const int i = x / Q4, c = x - i * Q4;
+    cp_async_16(Sh + i * NP + 4 * c, S0h + i * N + 4 * c);
+  }
   cp_async_commit();
+  for (int x = T * NP + tid; x < T16 * NP; x += NT) Qs[x] = 0.f;
   const size_t tok_stride = (size_t)H * N;
-  const size_t head_off = item_head_off(bb, hh, K_, H, N, Tstride, Cper);
-  const int ig = tid % IG, i0 = ig * RI;
-  const int tq = tid / IG, ntq = nt / IG;
-  float yv[4][RI];
-  auto load_y = [&](int t0) {
+  const size_t head_off = item_head_off(bb, hh, K_, H, N, Tstride, Cper) + (size_t)tb * tok_stride;
+  const int mtiles = T16 / 16;
+  float2 yv[NTL][2];
+  auto load_y = [&](int mt) {
+    const int t_lo = mt * 16 + g, t_hi = t_lo + 8;
 #pragma unroll
-    for (int tt = 0; tt < 4; ++tt) {
-      const int t = t0 + tt * ntq;
-      if (t < T) {
-        const float* yr = y + head_off + (size_t)t * tok_stride + i0;
-#pragma unroll
-        for (int q = 0; q < RI; ++q) yv[tt][q] = yr[q];
-      }
+    for (int nt = 0; nt < NTL; ++nt) {
+      const int col = nt * 8 + 2 * q;
+      yv[nt][0] = yv[nt][1] = make_float2(0.f, 0.f);
+      if (t_lo < T) yv[nt][0] = *reinterpret_cast<const float2*>(y + head_off + (size_t)t_lo * tok_stride + col);
+      if (t_hi < T) yv[nt][1] = *reinterpret_cast<const float2*>(y + head_off + (size_t)t_hi * tok_stride + col);
     }
   };
-  load_y(tq);  // issued before the barrier: overlaps the staging
+  if (warp < mtiles) load_y(warp);  // in flight while the staging completes
   cp_async_wait<0>();
-  __syncthreads();  // S0 and Q staged
-  for (int t0 = tq; t0 < T; t0 += 4 * ntq) {
-    if (t0 != tq) load_y(t0);
-    int trow[4];
+  __syncthreads();
+  for (int x = tid; x < N * N; x += NT) {
+    const int o = (x / N) * NP + x % N;
+    uint32_t hi, lo;
+    split_tf32(__uint_as_float(Sh[o]), hi, lo);
+    Sh[o] = hi;
+    Sl[o] = lo;
+  }
+  __syncthreads();
+  for (int mt = warp; mt < mtiles; mt += WARPS) {
+    if (mt != warp) load_y(mt);
+    const int t_lo = mt * 16 + g, t_hi = t_lo + 8;
+    // an opaque zero keeps the S fragment loads inside the loop (hoisting all
+    // of them would take N*N/8 registers per thread and cut the occupancy)
+    int z;
+    asm volatile("mov.u32 %0, 0;" : "=r"(z));
+    const uint32_t* ShI = Sh + z;
+    const uint32_t* SlI = Sl + z;
+    float acc[NTL][4];
 #pragma unroll
-    for (int tt = 0; tt < 4; ++tt) trow[tt] = min(t0 + tt * ntq, T - 1) * NP;  // rows past T: unused
-    float acc[4][RI];
+    for (int nt = 0; nt < NTL; ++nt) {
+      acc[nt][0] = yv[nt][0].x; acc[nt][1] = yv[nt][0].y;
+      acc[nt][2] = yv[nt][1].x; acc[nt][3] = yv[nt][1].y;
+    }
 #pragma unroll
-    for (int tt = 0; tt < 4; ++tt)
+    for (int k0 = 0; k0 < N; k0 += 8) {
+      const float a[4] = {Qs[t_lo * NP + k0 + q], Qs[t_hi * NP + k0 + q],
+                          Qs[t_lo * NP + k0 + q + 4], Qs[t_hi * NP + k0 + q + 4]};
+      uint32_t ah[4], al[4];
 #pragma unroll
-      for (int q = 0; q < RI; ++q) acc[tt][q] = 0.f;
-#pragma unroll 2
-    for (int j = 0; j < N; ++j) {
-      float qv[4];
+      for (int r = 0; r < 4; ++r) split_tf32(a[r], ah[r], al[r]);
 #pragma unroll
-      for (int tt = 0; tt < 4; ++tt) qv[tt] = Qs[trow[tt] + j];
-#pragma unroll
-      for (int q = 0; q < RI; ++q) {
-        const float sv = Ss[(i0 + q) * NP + j];
-#pragma unroll
-        for (int tt = 0; tt < 4; ++tt) acc[tt][q] = fmaf(sv, qv[tt], acc[tt][q]);
+      for (int nt = 0; nt < NTL; ++nt) {
+        const int srow = (nt * 8 + g) * NP + k0 + q;
+        const uint32_t bh_[2] = {ShI[srow], ShI[srow + 4]};
+        const uint32_t bl_[2] = {SlI[srow], SlI[srow + 4]};
+        mma_tf32(acc[nt], al, bh_);
+        mma_tf32(acc[nt], ah, bl_);
+        mma_tf32(acc[nt], ah, bh_);
       }
     }
 #pragma unroll
-    for (int tt = 0; tt < 4; ++tt) {
-      const int t = t0 + tt * ntq;
-      if (t < T) {
-        float* yr = y + head_off + (size_t)t * tok_stride + i0;
-#pragma unroll
-        for (int q = 0; q < RI; ++q) yr[q] = yv[tt][q] + acc[tt][q];
-      }
+    for (int nt = 0; nt < NTL; ++nt) {
+      const int col = nt * 8 + 2 * q;
+      if (t_lo < T)
+        *reinterpret_cast<float2*>(y + head_off + (size_t)t_lo * tok_stride + col) =
+            make_float2(acc[nt][0], acc[nt][1]);
+      if (t_hi < T)
+        *reinterpret_cast<float2*>(y + head_off + (size_t)t_hi * tok_stride + col) =
+            make_float2(acc[nt][2], acc[nt][3]);
     }
   }
 }
@@ -616,9 +645,8 @@ int wkv7_pair_slots(int N) {
 
 // Largest chunk the correction kernel can stage for head size N (multiple of 8).
 int wkv7_correct_max_chunk(int N) {
-  const int floats = 200 * 1024 / 4;
-  const int kmax = floats / (N + 4) - N;
-  return kmax / 8 * 8;
+  (void)N;  // the correction walks a chunk 80 tokens per block: no staging limit
+  return 1 << 20;
 }
 
 yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, const float* v,
@@ -662,7 +690,7 @@ yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, 
 
 yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, int items, int K, int H,
                                    int N, int Tstride, int Cper, bool skip_first, cudaStream_t st) {
-  const size_t bytes = ((size_t)N + K) * (N + 4) * sizeof(float);
+  const size_t bytes = ((size_t)2 * N + 80) * (N + 4) * sizeof(float);
   switch (N) {
 #define CASE(NN)                                                                                   \
   case NN: {                                                                                       \
@@ -673,11 +701,9 @@ yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, in
       set_error("wkv7 correct: cudaFuncSetAttribute failed");                                     \
       return YUF_ERR_CUDA;                                                                         \
     }                                                                                              \
-    constexpr int IG = CorrCfg<NN>::IG;                                                            \
-    int nt = ((K + 3) / 4) * IG;                                                                   \
-    nt = std::min(CorrCfg<NN>::MAXT, (nt + 31) / 32 * 32);                                         \
-    nt = std::max(nt, 32) / IG * IG;                                                               \
-    kern<<<items * H, nt, bytes, st>>>(S0, Q, y, K, H, Tstride, Cper, skip_first ? 1 : 0);         \
+    const int parts = (K + CorrCfg<NN>::TW - 1) / CorrCfg<NN>::TW;                                 \
+    kern<<<items * H * parts, CorrCfg<NN>::NT, bytes, st>>>(S0, Q, y, K, H, Tstride, Cper,          \
+                                                            skip_first ? 1 : 0, parts);            \
     return check_launch("wkv7_correct_kernel");                                                    \
   }
     CASE(16) CASE(32) CASE(40) CASE(48) CASE(64) CASE(96) CASE(128)

@@ -12,8 +12,8 @@
 //      the zero-start row and the identity-start row in the same lane
 //      (wkv7_pair.cu): y from a zero start, q_t = P_t r_t, U and P;
 //   2. per (sequence, head) the chunk start states S_c = S_{c-1} P_c + U_c
-//      (wkv7_carry_kernel, an N x N x N product per chunk, P_c and U_c
-//      prefetched with cp.async while the previous product runs);
+//      (wkv7_carry_kernel, an N x N x N product per chunk on the tensor cores,
+//      P_c and U_c streamed in ahead through a cp.async ring);
 //   3. every (sequence, chunk, head) adds S_{c-1} q_t to its y
 //      (wkv7_correct_kernel, since y_t = yU_t + S_{c-1} q_t).
 // The chunk count is chosen so that pass 1 fills the GPU in one wave: about
@@ -23,6 +23,7 @@
 // product association of passes 2 and 3.
 
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -38,92 +39,138 @@ yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, in
 int wkv7_pair_slots(int N);
 int wkv7_correct_max_chunk(int N);
 
-// Pass 2: per (sequence, head) the chunk start states S_c = S_{c-1} P_c + U_c.
-// State rows are independent recurrences, so each (sequence, head) is split
-// into RS row blocks of NR = N/RS rows, one CTA each (RS = 4, 2 or 1: the most
-// that fit in one wave of resident blocks, since a CTA walks every chunk of its
-// sequence).  Thread = 1 row x 4 columns of the block.  P_c and the block's rows
-// of U_c come in through a cp.async ring of up to 4 stages: every chunk's inputs are
-// already in memory when the kernel starts, so the chain of chunks waits on the
-// memory latency only once.
-template <int N, int RS>
+// Pass 2: per (sequence, head) the chunk start states S_c = S_{c-1} P_c + U_c,
+// one CTA per (sequence, head) walking its chunks.  The N x N x N product runs
+// on the tensor cores (mma.sync m16n8k8, 3xTF32 for fp32-level accuracy): one
+// warp per 16 x 8 output tile (up to 32 warps), A = rows of S from shared memory
+// (rows past N read as zero), B = P_c, accumulators initialised with U_c.  P_c
+// and U_c come in through a cp.async ring: every chunk's inputs are in memory
+// when the kernel starts, so the chain of chunks waits on memory only once.
+// Row strides: S and U pad to N + 4 floats and P to the next width = 8 mod 32,
+// which makes the A and B fragment loads bank-conflict free.
+template <int N>
 struct CarryCfg {
-  static constexpr int NR = N / RS;
-  static constexpr int NT = NR * N / 4;
-  static constexpr int STAGE = N * N + NR * N;  // P_c and the block's rows of U_c
-  static constexpr int FIT = (200 * 1024 / 4 - NR * N) / STAGE;
-  static constexpr int DEPTH = FIT < 2 ? 2 : (FIT > 4 ? 4 : FIT);  // ring stages
-  static constexpr int FLOATS = NR * N + DEPTH * STAGE;
+  static constexpr int MT = (N + 15) / 16;               // 16-row tiles (rows >= N are zero)
+  static constexpr int NTL = N / 8;                      // 8-column tiles
+  static constexpr int TILES = MT * NTL;
+  static constexpr int WARPS = TILES < 32 ? TILES : 32;
+  static constexpr int TPW = (TILES + WARPS - 1) / WARPS;  // tiles per warp
+  static constexpr int NT = 32 * WARPS;
+  static constexpr int NP = N + 4;
+  static constexpr int PP = N + (40 - N % 32) % 32;
+  static constexpr bool UIN = N <= 96;                   // U staged in the ring
+  static constexpr int STAGE = N * PP + (UIN ? N * NP : 0);
+  static constexpr int SROWS = MT * 16;
+  static constexpr int FIT = (200 * 1024 / 4 - SROWS * NP) / STAGE;
+  static constexpr int DEPTH = FIT < 2 ? 2 : (FIT > 4 ? 4 : FIT);
+  static constexpr int FLOATS = SROWS * NP + DEPTH * STAGE;
   static constexpr size_t BYTES = (size_t)FLOATS * sizeof(float);
 };
 
-template <int N, int RS>
-__global__ void __launch_bounds__(CarryCfg<N, RS>::NT)
+template <int N>
+__global__ void __launch_bounds__(CarryCfg<N>::NT)
     wkv7_carry_kernel(const float* __restrict__ U, const float* __restrict__ P, const float* s0,
                       float* __restrict__ S_start, float* s_out, int C, int H) {
-  constexpr int NR = CarryCfg<N, RS>::NR, NT = CarryCfg<N, RS>::NT, NN = N * N;
-  constexpr int STAGE = CarryCfg<N, RS>::STAGE, D = CarryCfg<N, RS>::DEPTH;
+  using Cf = CarryCfg<N>;
+  constexpr int NT = Cf::NT, NP = Cf::NP, PP = Cf::PP, NTL = Cf::NTL, TILES = Cf::TILES;
+  constexpr int WARPS = Cf::WARPS, TPW = Cf::TPW, STAGE = Cf::STAGE, D = Cf::DEPTH, NN = N * N;
+  constexpr int Q4 = N / 4;
   extern __shared__ float4 carry_sm[];
-  float* Ss = reinterpret_cast<float*>(carry_sm);  // [NR][N] rows of the running state
-  float* ring = Ss + NR * N;                        // [D][N*N + NR*N]: P_c, then rows of U_c
-  const int bh = blockIdx.x / RS, rb = blockIdx.x - bh * RS;
-  const int r0 = rb * NR;
+  float* Ss = reinterpret_cast<float*>(carry_sm);  // [SROWS][NP] running state
+  float* ring = Ss + Cf::SROWS * NP;                // [D][N*PP (+ N*NP)]: P_c, U_c
+  const int bh = blockIdx.x;
   const int s = bh / H, h = bh - s * H;
-  const int tid = threadIdx.x;
-  const int i = tid / (N / 4), j0 = (tid % (N / 4)) * 4;
-  const size_t row_off = (size_t)r0 * N;
-  const float* s0p = s0 ? s0 + (size_t)bh * NN + row_off : nullptr;
-  for (int q = tid; q < NR * N; q += NT) Ss[q] = s0p ? s0p[q] : 0.f;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  const float* s0p = s0 ? s0 + (size_t)bh * NN : nullptr;
+  for (int x = tid; x < Cf::SROWS * NP; x += NT) {
+    const int i = x / NP, j = x - i * NP;
+    Ss[x] = (s0p && i < N && j < N) ? s0p[i * N + j] : 0.f;
+  }
   auto fetch = [&](int c) {  // always commits a group (empty past the last chunk)
     if (c < C) {
       float* dst = ring + (c % D) * STAGE;
       const size_t off = (((size_t)s * C + c) * H + h) * NN;
-      for (int q = tid; q < NN / 4; q += NT) cp_async_16(dst + 4 * q, P + off + 4 * q);
-      for (int q = tid; q < NR * N / 4; q += NT)
-        cp_async_16(dst + NN + 4 * q, U + off + row_off + 4 * q);
+      for (int x = tid; x < N * Q4; x += NT) {
+        const int i = x / Q4, j4 = x - i * Q4;
+        cp_async_16(dst + i * PP + 4 * j4, P + off + (size_t)i * N + 4 * j4);
+        if (Cf::UIN) cp_async_16(dst + N * PP + i * NP + 4 * j4, U + off + (size_t)i * N + 4 * j4);
+      }
     }
     cp_async_commit();
   };
 #pragma unroll
   for (int c = 0; c < D - 1; ++c) fetch(c);
   for (int c = 0; c < C; ++c) {
-    __syncthreads();  // Ss final for this chunk; stage (c - 1) % D free
+    __syncthreads();  // Ss = S_{c-1}; stage (c - 1) % D free
     fetch(c + D - 1);
     {
-      float* dst = S_start + (((size_t)s * C + c) * H + h) * NN + row_off;
-      for (int q = tid; q < NR * N / 4; q += NT)
-        reinterpret_cast<float4*>(dst)[q] = reinterpret_cast<const float4*>(Ss)[q];
+      float* dst = S_start + (((size_t)s * C + c) * H + h) * NN;
+      for (int x = tid; x < N * Q4; x += NT) {
+        const int i = x / Q4, j4 = x - i * Q4;
+        *reinterpret_cast<float4*>(dst + i * N + 4 * j4) =
+            *reinterpret_cast<const float4*>(Ss + i * NP + 4 * j4);
+      }
     }
     cp_async_wait<D - 1>();  // chunk c's group landed
     __syncthreads();
     const float* Pc = ring + (c % D) * STAGE;
-    float4 acc = *reinterpret_cast<const float4*>(Pc + NN + i * N + j0);
-    float4 acc2 = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int l = 0; l < N; l += 2) {
-      const float4 p0 = *reinterpret_cast<const float4*>(Pc + l * N + j0);
-      const float4 p1 = *reinterpret_cast<const float4*>(Pc + (l + 1) * N + j0);
-      const float2 sv = *reinterpret_cast<const float2*>(Ss + i * N + l);
-      acc.x = fmaf(sv.x, p0.x, acc.x); acc.y = fmaf(sv.x, p0.y, acc.y);
-      acc.z = fmaf(sv.x, p0.z, acc.z); acc.w = fmaf(sv.x, p0.w, acc.w);
-      acc2.x = fmaf(sv.y, p1.x, acc2.x); acc2.y = fmaf(sv.y, p1.y, acc2.y);
-      acc2.z = fmaf(sv.y, p1.z, acc2.z); acc2.w = fmaf(sv.y, p1.w, acc2.w);
+    const float* Uc = Pc + N * PP;
+    const float* Ug = U + (((size_t)s * C + c) * H + h) * NN;
+    // three accumulator chains per tile while registers allow (N <= 64), one beyond
+    using AccT = typename std::conditional<(TPW <= 1), Acc3, float[4]>::type;
+    AccT acc[TPW];
+#pragma unroll
+    for (int tp = 0; tp < TPW; ++tp) {
+      const int tile = warp + tp * WARPS;
+      if (tile < TILES) {
+        const int m0 = (tile / NTL) * 16, n0 = (tile % NTL) * 8;
+        const int r_lo = m0 + g, r_hi = m0 + g + 8, col = n0 + 2 * q;
+        float2 u_lo = make_float2(0.f, 0.f), u_hi = u_lo;
+        if (Cf::UIN) {
+          if (r_lo < N) u_lo = *reinterpret_cast<const float2*>(Uc + r_lo * NP + col);
+          if (r_hi < N) u_hi = *reinterpret_cast<const float2*>(Uc + r_hi * NP + col);
+        } else {
+          if (r_lo < N) u_lo = *reinterpret_cast<const float2*>(Ug + (size_t)r_lo * N + col);
+          if (r_hi < N) u_hi = *reinterpret_cast<const float2*>(Ug + (size_t)r_hi * N + col);
+        }
+        acc_init(acc[tp], u_lo.x, u_lo.y, u_hi.x, u_hi.y);
+#pragma unroll
+        for (int k0 = 0; k0 < N; k0 += 8) {
+          const float a[4] = {Ss[r_lo * NP + k0 + q], Ss[r_hi * NP + k0 + q],
+                              Ss[r_lo * NP + k0 + q + 4], Ss[r_hi * NP + k0 + q + 4]};
+          const float b[2] = {Pc[(k0 + q) * PP + n0 + g], Pc[(k0 + q + 4) * PP + n0 + g]};
+          mma_3xtf32(acc[tp], a, b);
+        }
+      }
     }
     __syncthreads();  // every read of Ss done
-    *reinterpret_cast<float4*>(Ss + i * N + j0) =
-        make_float4(acc.x + acc2.x, acc.y + acc2.y, acc.z + acc2.z, acc.w + acc2.w);
+#pragma unroll
+    for (int tp = 0; tp < TPW; ++tp) {
+      const int tile = warp + tp * WARPS;
+      if (tile < TILES) {
+        const int m0 = (tile / NTL) * 16, n0 = (tile % NTL) * 8;
+        const int r_lo = m0 + g, r_hi = m0 + g + 8, col = n0 + 2 * q;
+        if (r_lo < N)
+          *reinterpret_cast<float2*>(Ss + r_lo * NP + col) =
+              make_float2(acc_get(acc[tp], 0), acc_get(acc[tp], 1));
+        if (r_hi < N)
+          *reinterpret_cast<float2*>(Ss + r_hi * NP + col) =
+              make_float2(acc_get(acc[tp], 2), acc_get(acc[tp], 3));
+      }
+    }
   }
   cp_async_wait<0>();
   __syncthreads();
   if (s_out)
-    for (int q = tid; q < NR * N; q += NT) s_out[(size_t)bh * NN + row_off + q] = Ss[q];
+    for (int x = tid; x < NN; x += NT) s_out[(size_t)bh * NN + x] = Ss[(x / N) * NP + x % N];
 }
 
-template <int N, int RS>
-static yuf_status_t launch_carry_rs(const float* U, const float* P, const float* s0, float* S_start,
-                                    float* s_out, int B, int C, int H, cudaStream_t st) {
-  using Cf = CarryCfg<N, RS>;
-  auto kern = wkv7_carry_kernel<N, RS>;
+template <int N>
+static yuf_status_t launch_carry(const float* U, const float* P, const float* s0, float* S_start,
+                                 float* s_out, int B, int C, int H, cudaStream_t st) {
+  using Cf = CarryCfg<N>;
+  auto kern = wkv7_carry_kernel<N>;
   if (Cf::BYTES > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cf::BYTES);
     if (e != cudaSuccess) {
@@ -131,40 +178,8 @@ static yuf_status_t launch_carry_rs(const float* U, const float* P, const float*
       return YUF_ERR_CUDA;
     }
   }
-  kern<<<B * H * RS, Cf::NT, Cf::BYTES, st>>>(U, P, s0, S_start, s_out, C, H);
+  kern<<<B * H, Cf::NT, Cf::BYTES, st>>>(U, P, s0, S_start, s_out, C, H);
   return check_launch("wkv7_carry_kernel");
-}
-
-// Resident blocks of a kernel per device (blocks per SM x SMs), 1 when unknown.
-template <typename Kern>
-static long long resident_blocks(Kern kern, int threads, size_t bytes) {
-  int dev = 0, sms = 148, per_sm = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (bytes > 48 * 1024)
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, bytes) != cudaSuccess) {
-    cudaGetLastError();
-    per_sm = 1;
-  }
-  return (long long)std::max(1, per_sm) * sms;
-}
-
-template <int N>
-static yuf_status_t launch_carry(const float* U, const float* P, const float* s0, float* S_start,
-                                 float* s_out, int B, int C, int H, cudaStream_t st) {
-  // RS = 4 always has a legal block size; 2 and 1 only while N*N/8 resp. N*N/4
-  // threads fit in a block
-  const long long BH = (long long)B * H;
-  if (4 * BH <= resident_blocks(wkv7_carry_kernel<N, 4>, CarryCfg<N, 4>::NT, CarryCfg<N, 4>::BYTES))
-    return launch_carry_rs<N, 4>(U, P, s0, S_start, s_out, B, C, H, st);
-  if constexpr (CarryCfg<N, 2>::NT <= 1024) {
-    if (2 * BH <= resident_blocks(wkv7_carry_kernel<N, 2>, CarryCfg<N, 2>::NT, CarryCfg<N, 2>::BYTES))
-      return launch_carry_rs<N, 2>(U, P, s0, S_start, s_out, B, C, H, st);
-    if constexpr (CarryCfg<N, 1>::NT <= 1024)
-      return launch_carry_rs<N, 1>(U, P, s0, S_start, s_out, B, C, H, st);
-  }
-  return launch_carry_rs<N, 4>(U, P, s0, S_start, s_out, B, C, H, st);  // more than one wave
 }
 
 // Chunks per sequence and chunk length for B sequences of T tokens.
