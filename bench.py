@@ -196,7 +196,38 @@ def measure_extras(dev, stream, args):
                                       "tokens_per_s": 2 * T / (ms * 1e-3)}
     del rd, ro, mo
     out.update(measure_model(dev, stream))
+    out.update(measure_long(dev, stream))
     return out
+
+
+def measure_long(dev, stream):
+    """Benchmark config 5's per-GPU share (8 of its 64 sequences) through the
+    engine: 24 layers, d1024, H16 x 64, ROSA 256, bf16 weights, fp32 state,
+    B8 x T8192 Zipf(1.1) ids, zero initial state; prefill tokens/s."""
+    import torch
+
+    from yufmusicgen_b200 import config as C
+    from yufmusicgen_b200.engine import Engine
+    from yufmusicgen_b200.weights import init_weights
+    from yufmusicgen_b200.workloads import zipf_ids
+
+    cfg = C.ModelConfig(**C.LONG_1K)
+    w = init_weights(cfg, 2, "baseline")
+    Bl, Tl = 8, 8192
+    ids = torch.as_tensor(zipf_ids(Bl, Tl, seed=2, vocab=cfg.vocab_size), dtype=torch.int32, device=dev)
+    eng = Engine(cfg, w, precision="bf16", device=dev.index, n_slots=Bl)
+    last = torch.empty(Bl, cfg.vocab_size, device=dev)
+
+    def pf():
+        eng.reset_state(0, Bl)
+        eng.prefill(ids, slot0=0, out_last=last)
+
+    ms = _time(pf, 2, dev, stream, warm=1)
+    eng.close()
+    del eng
+    flop = 915e6 * Bl * Tl  # about 2 x linear parameters + LM head per token
+    return {"prefill_c5_B8_T8192_bf16": {"ms": ms, "tokens_per_s": Bl * Tl / (ms * 1e-3),
+                                         "TFLOPs": flop / (ms * 1e-3) / 1e12}}
 
 
 def measure_model(dev, stream):

@@ -295,8 +295,10 @@ yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const f
 //      [B, T, R], so the chunk batch is the same tensor viewed as [B*T/K, K, R];
 //   3. per sequence, m_c = A^K m_{c-1} + z_c over the chunks (rosa_carry_kernel);
 //   4. every chunk is scanned again from its true start state (MODE 0).
-// Exact in exact arithmetic (linearity of the recurrence in m).
-constexpr int ROSA_PAR_K = 32;
+// Exact in exact arithmetic (linearity of the recurrence in m).  K = 32 for
+// R <= 128 (A^K in shared memory); K = 64 above, where A^K (R x R, 256 KB at
+// R = 256) is streamed from L2 in every carry step, so fewer, longer chunks.
+static int rosa_par_k(int R) { return R <= 128 ? 32 : 64; }
 
 // One CTA per sequence; A^K (stored transposed: AKt[j][i] = (A^K)[i][j]) in
 // shared memory.
@@ -333,6 +335,38 @@ __global__ void __launch_bounds__(128)
   if (i < R && m_out) m_out[(size_t)b * R + i] = m;
 }
 
+// R > 128: A^K stays in global memory (L2-resident, read coalesced: AKt[j][i]
+// over the threads i), 32 rows of it in flight per thread.
+__global__ void __launch_bounds__(256)
+    rosa_carry_global_kernel(const float* __restrict__ AKt, const float* __restrict__ z,
+                             const float* m0, float* __restrict__ m_start, float* m_out, int C, int R) {
+  extern __shared__ float sh[];
+  float* mv = sh;  // [R]
+  const int b = blockIdx.x, i = threadIdx.x;
+  const bool on = i < R;
+  const int ic = on ? i : 0;
+  float m = (on && m0) ? m0[(size_t)b * R + i] : 0.f;
+  for (int c = 0; c < C; ++c) {
+    const size_t row = ((size_t)b * C + c) * R;
+    if (on) {
+      m_start[row + i] = m;
+      mv[i] = m;
+    }
+    __syncthreads();
+    float a[8] = {on ? z[row + i] : 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int j = 0;
+#pragma unroll 4
+    for (; j + 8 <= R; j += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) a[u] = fmaf(__ldg(AKt + (size_t)(j + u) * R + ic), mv[j + u], a[u]);
+    }
+    for (; j < R; ++j) a[0] = fmaf(__ldg(AKt + (size_t)j * R + ic), mv[j], a[0]);
+    m = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+    __syncthreads();
+  }
+  if (on && m_out) m_out[(size_t)b * R + i] = m;
+}
+
 template <bool GATED, int MODE>
 static void launch_mode(const float* cand, const float* write, const float* gate,
                         const float* bias_c, const float* bias_w, const float* bias_g, int ld,
@@ -345,15 +379,15 @@ static void launch_mode(const float* cand, const float* write, const float* gate
 }
 
 size_t rosa_parallel_scratch_floats(int B, int T, int R) {
-  const size_t C = (size_t)T / ROSA_PAR_K;
+  const size_t C = (size_t)T / rosa_par_k(R);
   return (size_t)R * R + 2 * (size_t)B * C * R;
 }
 
 bool rosa_parallel_applies(int B, int T, int R) {
-  // shared-memory A^K (R <= 128), whole chunks, and enough of them to be worth
-  // the extra passes
-  return R <= 128 && T % ROSA_PAR_K == 0 && T >= 4 * ROSA_PAR_K &&
-         (long long)B * (T / ROSA_PAR_K) >= 16;
+  // R within the 256-thread scan kernel, whole chunks, and enough of them to be
+  // worth the extra passes
+  const int K = rosa_par_k(R);
+  return R <= 256 && T % K == 0 && T >= 4 * K && (long long)B * (T / K) >= 16;
 }
 
 // The caller guarantees rosa_parallel_applies(); scratch holds
@@ -363,7 +397,7 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
                            const float* decay, const float* dir, int raw, const float* m0,
                            float* read, float* m_out, int B, int T, int R, bool gated,
                            float* scratch, cudaStream_t s) {
-  constexpr int K = ROSA_PAR_K;
+  const int K = rosa_par_k(R);
   const int C = T / K;
   float* AKt = scratch;
   float* z = AKt + (size_t)R * R;
@@ -376,15 +410,19 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
                         nullptr, z, B * C, K, R, s);
   // 3. carry across chunks
   const int threads = ((R + 31) / 32) * 32;
-  const size_t sm = ((size_t)R * R + R) * sizeof(float);
-  if (sm > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(rosa_carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    if (e != cudaSuccess) {
-      set_error("rosa: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
-      return YUF_ERR_CUDA;
+  if (R <= 128) {
+    const size_t sm = ((size_t)R * R + R) * sizeof(float);
+    if (sm > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(rosa_carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      if (e != cudaSuccess) {
+        set_error("rosa: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        return YUF_ERR_CUDA;
+      }
     }
+    rosa_carry_kernel<<<B, threads, sm, s>>>(AKt, z, m0, m_start, m_out, C, R);
+  } else {
+    rosa_carry_global_kernel<<<B, threads, R * sizeof(float), s>>>(AKt, z, m0, m_start, m_out, C, R);
   }
-  rosa_carry_kernel<<<B, threads, sm, s>>>(AKt, z, m0, m_start, m_out, C, R);
   // 4. rescan every chunk from its true start state
   if (gated)
     launch_mode<true, 0>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, m_start, read,

@@ -269,8 +269,11 @@ YUF_DEVICE void load_cols(float2 (&dst)[C / 2], const float* p) {
   if constexpr (C % 4 != 0) dst[C / 2 - 1] = *reinterpret_cast<const float2*>(p + C - 2);
 }
 
+#ifndef YUF_PAIRW_MINB
+#define YUF_PAIRW_MINB 1
+#endif
 template <int N>
-__global__ void __launch_bounds__(32)
+__global__ void __launch_bounds__(32, YUF_PAIRW_MINB)
     wkv7_pairw_kernel(const float* __restrict__ r, const float* __restrict__ w,
                       const float* __restrict__ k, const float* __restrict__ v,
                       const float* __restrict__ a, const float* __restrict__ b,
