@@ -59,8 +59,9 @@ yuf_status_t yuf_wkv7_forward(const float* r, const float* w, const float* k, co
 /* Algorithm choice for yuf_wkv7_forward_ex. */
 enum {
   YUF_WKV_AUTO = 0,       /* T == 1: single-token kernel; T >= 256 and few (sequence, head)
-                             chains (N <= 40: B*H <= a third of the resident pair blocks,
-                             592 on a 148-SM B200; larger N: B*H <= 64): time-parallel;
+                             chains (N <= 64: B*H <= half the resident pair blocks, 888 at
+                             N = 40 and 370 at N = 64 on a 148-SM B200; larger N:
+                             B*H <= 64): time-parallel;
                              else sequential                                                    */
   YUF_WKV_SEQUENTIAL = 1, /* token by token, one CTA per (sequence, head)                         */
   YUF_WKV_CHUNKED = 2,    /* 16-token chunks, no per-token reduction chain                        */

@@ -209,10 +209,11 @@ __global__ void __launch_bounds__(PairCfg<N>::NT, 1)
   }
 }
 
-// One warp per (chunk, head) for N = 16, 32, 40.  Lane (rg, g),
-// rg = lane / 4, g = lane % 4, owns the R = N / 8 state rows rg*R .. rg*R+R-1 --
-// each as a zero-start row and an identity-start row -- over the C = N / 4
-// columns g*C .. g*C+C-1.  Every per-token column value a lane reads from shared
+// One block per (chunk, head) for N <= 64: NW warps (1 for N <= 40, 2 for 48
+// and 64), each of 8 row groups of 4 lanes.  Lane (rg, g) of warp wp,
+// rg = lane / 4, g = lane % 4, owns the R state rows i0 .. i0+R-1,
+// i0 = (8 wp + rg) R (R = 5 at N = 40, 4 at N = 64) -- each as a zero-start row
+// and an identity-start row -- over the C = N / 4 columns g*C .. g*C+C-1.  Every per-token column value a lane reads from shared
 // memory then feeds 2R rows, so the kernel is bound by the FMA pipe rather than
 // by shared-memory delivery (the multi-warp kernel above feeds 4 rows per read).
 //
@@ -241,9 +242,11 @@ constexpr int PAIRW_UNROLL = YUF_PAIRW_UNROLL;  // token loop unroll: code size 
 
 template <int N>
 struct PairWCfg {
-  static constexpr int G = 4;       // lanes per row group
-  static constexpr int R = N / 8;   // rows per lane (8 row groups per warp)
-  static constexpr int C = N / G;   // columns per lane
+  static constexpr int G = 4;                                   // lanes per row group
+  static constexpr int R = N == 48 ? 3 : (N == 64 ? 4 : N / 8);  // rows per lane
+  static constexpr int NW = N / (8 * R);                        // warps (8 row groups each)
+  static constexpr int NT = 32 * NW;
+  static constexpr int C = N / G;                               // columns per lane
   static constexpr int C2 = C / 2;
   static constexpr int CS = conflict_free_stride(C, G);
   static constexpr int VP = G * CS;
@@ -254,8 +257,16 @@ struct PairWCfg {
   static constexpr int VV = GEND + VP;            // [TS][N] values
   static constexpr int TOTAL = VV + TS * N;
   static constexpr size_t BYTES = (size_t)TOTAL * sizeof(float);
-  static_assert(N % 8 == 0 && C % 2 == 0 && N <= 40, "one-warp pair kernel: N in {16, 32, 40}");
+  static_assert(N % 8 == 0 && C % 2 == 0 && N <= 64 && NW * 8 * R == N,
+                "warp pair kernel: N in {16, 32, 40, 48, 64}");
 };
+
+// Barrier over the block's warps (a warp barrier when the block is one warp).
+template <int NW>
+YUF_DEVICE void block_sync() {
+  if constexpr (NW == 1) __syncwarp();
+  else __syncthreads();
+}
 
 // C floats of one padded vector as float2 pairs (C/4 LDS.128 and one LDS.64).
 template <int C>
@@ -269,11 +280,8 @@ YUF_DEVICE void load_cols(float2 (&dst)[C / 2], const float* p) {
   if constexpr (C % 4 != 0) dst[C / 2 - 1] = *reinterpret_cast<const float2*>(p + C - 2);
 }
 
-#ifndef YUF_PAIRW_MINB
-#define YUF_PAIRW_MINB 1
-#endif
 template <int N>
-__global__ void __launch_bounds__(32, YUF_PAIRW_MINB)
+__global__ void __launch_bounds__(PairWCfg<N>::NT)
     wkv7_pairw_kernel(const float* __restrict__ r, const float* __restrict__ w,
                       const float* __restrict__ k, const float* __restrict__ v,
                       const float* __restrict__ a, const float* __restrict__ b,
@@ -288,9 +296,11 @@ __global__ void __launch_bounds__(32, YUF_PAIRW_MINB)
   const int bh = blockIdx.x;
   const int bb = bh / H, hh = bh - bb * H;
   const int T = item_len(bb, K_, Tstride, Cper);
-  const int lane = threadIdx.x;
+  constexpr int NT = K::NT;
+  const int tid = threadIdx.x;
+  const int lane = K::NW == 1 ? tid : (tid & 31), wp = K::NW == 1 ? 0 : tid >> 5;
   const int rg = lane >> 2, g = lane & 3;
-  const int i0 = rg * R, j0 = g * C;
+  const int i0 = (wp * 8 + rg) * R, j0 = g * C;
 
   float2 SU[R][C2], SP[R][C2];
 #pragma unroll
@@ -311,7 +321,7 @@ __global__ void __launch_bounds__(32, YUF_PAIRW_MINB)
     constexpr int Q4 = N / 4;
 #pragma unroll
     for (int arr = 0; arr < 6; ++arr)
-      for (int idx = lane; idx < Tc * Q4; idx += 32) {
+      for (int idx = tid; idx < Tc * Q4; idx += NT) {
         const int t = idx / Q4, q = idx - t * Q4;
         cp_async_16(sm + K::RAW + (arr * TS + t) * N + 4 * q,
                     src[arr] + (size_t)(t0 + t) * tok_stride + 4 * q);
@@ -337,10 +347,10 @@ __global__ void __launch_bounds__(32, YUF_PAIRW_MINB)
     const int t0 = gi * TS;
     const int Tc = min(TS, T - t0);
     cp_async_wait<0>();
-    __syncwarp();
-    // scaled vectors: a lane per column pair, running gamma over the group's tokens
-    if (lane < N / 2) {
-      const int j = 2 * lane;
+    block_sync<K::NW>();
+    // scaled vectors: a thread per column pair, running gamma over the group's tokens
+    if (tid < N / 2) {
+      const int j = 2 * tid;
       const int pj = (j / C) * CS + (j % C);  // lane-layout offset of the pair
       float2 gam = make_float2(1.f, 1.f), ginv = gam;
       for (int t = 0; t < Tc; ++t) {
@@ -363,7 +373,7 @@ __global__ void __launch_bounds__(32, YUF_PAIRW_MINB)
       }
       *reinterpret_cast<float2*>(sm + K::GEND + pj) = gam;
     }
-    __syncwarp();
+    block_sync<K::NW>();
     if (gi + 1 < ngroups) stage(t0 + TS, min(TS, T - t0 - TS));  // raw buffer is free again
 
     // sa of the group's first token; every later token's sa comes out of the
@@ -473,7 +483,7 @@ __global__ void __launch_bounds__(32, YUF_PAIRW_MINB)
           SP[p][c] = fmul2(SP[p][c], ge[c]);
         }
     }
-    __syncwarp();  // the next group's staging pass overwrites the lane layout
+    block_sync<K::NW>();  // the next group's staging pass overwrites the lane layout
   }
 #pragma unroll
   for (int p = 0; p < R; ++p) {
@@ -622,7 +632,8 @@ int wkv7_pair_slots(int N) {
   case NN: {                                                                                     \
     auto kern = wkv7_pairw_kernel<NN>;                                                           \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PairWCfg<NN>::BYTES); \
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32, PairWCfg<NN>::BYTES);   \
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, PairWCfg<NN>::NT,           \
+                                                      PairWCfg<NN>::BYTES);                        \
     break;                                                                                       \
   }
 #define SLOT(NN)                                                                                 \
@@ -632,7 +643,7 @@ int wkv7_pair_slots(int N) {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, PairCfg<NN>::NT, PairCfg<NN>::BYTES); \
     break;                                                                                       \
   }
-    SLOTW(16) SLOTW(32) SLOTW(40) SLOT(48) SLOT(64) SLOT(96) SLOT(128)
+    SLOTW(16) SLOTW(32) SLOTW(40) SLOTW(48) SLOTW(64) SLOT(96) SLOT(128)
 #undef SLOTW
 #undef SLOT
     default:
@@ -666,7 +677,7 @@ yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, 
       set_error("wkv7 pair: cudaFuncSetAttribute failed");                                      \
       return YUF_ERR_CUDA;                                                                       \
     }                                                                                            \
-    kern<<<items * H, 32, Kc::BYTES, st>>>(r, w, k, v, a, b, y, Q, U, P, K, H, Tstride, Cper);   \
+    kern<<<items * H, Kc::NT, Kc::BYTES, st>>>(r, w, k, v, a, b, y, Q, U, P, K, H, Tstride, Cper); \
     return check_launch("wkv7_pairw_kernel");                                                    \
   }
 #define CASE(NN)                                                                                 \
@@ -682,7 +693,7 @@ yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, 
     kern<<<items * H, Kc::NT, Kc::BYTES, st>>>(r, w, k, v, a, b, y, Q, U, P, K, H, Tstride, Cper); \
     return check_launch("wkv7_pair_kernel");                                                     \
   }
-    CASEW(16) CASEW(32) CASEW(40) CASE(48) CASE(64) CASE(96) CASE(128)
+    CASEW(16) CASEW(32) CASEW(40) CASEW(48) CASEW(64) CASE(96) CASE(128)
 #undef CASEW
 #undef CASE
     default:

@@ -197,14 +197,16 @@ void wkv7_parallel_plan(int B, int T, int H, int N, int* C_out, int* K_out) {
 
 // The parallel path does about twice the sequential work (the N transition rows
 // of pass 1); it wins while the sequential scan, one chain per CTA, would leave
-// SMs idle or be bound by one SM's shared-memory delivery.  Measured on B200 at
-// T = 2048, N = 40: 3.8x faster at B*H = 32, 2.0x at 128, 1.2x at 512 (a third
-// of the 1776 resident pair blocks).  Head sizes above 40 use the multi-warp
-// pair kernel: 3.6x at B*H = 32 for N = 64, slower than sequential at 128.
+// SMs idle or be bound by one SM's shared-memory delivery.  Measured on B200,
+// T = 2048: N = 40 3.8x faster at B*H = 32, 2.4x at 128, 1.2x at 512; N = 64
+// 4.9x at 32, 1.7x at 128, 1.4x at 256 (1.8x at 128 for T = 8192).  Taken while
+// B*H is at most half the resident pair blocks (888 at N = 40, 370 at N = 64 on
+// a 148-SM B200); head sizes above 64 use the multi-warp pair kernel, which
+// wins only for few chains.
 bool wkv7_parallel_applies(int B, int T, int H, int N) {
   const long long BH = (long long)B * H;
   if (T < 256) return false;
-  return N <= 40 ? 3 * BH <= wkv7_pair_slots(N) : BH <= 64;
+  return N <= 64 ? 2 * BH <= wkv7_pair_slots(N) : BH <= 64;
 }
 
 size_t wkv7_parallel_scratch_floats(int B, int T, int H, int N) {
