@@ -290,6 +290,17 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
   WS w = carve(m, rows, ws_base);
   launch_embed(ids, m->emb, w.x, (int)rows, d, V, m->d_err, s);
   const size_t RD = rows * d;
+  // bf16-weight mode: the producers of GEMM inputs (mixes, layer norms, the FFN
+  // gate) write bf16 straight into the staging buffer instead of fp32 plus a copy
+  const bool bf = m->precision == YUF_PRECISION_BF16_WEIGHTS;
+  auto ln_in = [&](const float* x, const float* lw, const float* lb, const float* gate) -> const void* {
+    if (bf) {
+      launch_layernorm<__nv_bfloat16>(x, lw, lb, gate, w.bf, (int)rows, d, s);
+      return w.bf;
+    }
+    launch_layernorm<float>(x, lw, lb, gate, w.tmp, (int)rows, d, s);
+    return w.tmp;
+  };
   for (int li = 0; li < m->cfg.n_layers; ++li) {
     const LayerW& Lw = m->L[li];
     float* prev = m->st_prev + ((size_t)li * m->n_slots + slot0) * m->slot_prev();
@@ -297,11 +308,16 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     float* mem = m->st_m + ((size_t)li * m->n_slots + slot0) * m->slot_m();
     // --- TimeMix
     launch_layernorm<float>(w.x, Lw.ln_t_w, Lw.ln_t_b, nullptr, w.xt, (int)rows, d, s);
-    launch_mix<float>(w.xt, prev, Lw.mix, w.mixed, B, T, d, s);
+    const void* mixed = w.mixed;
+    if (bf) {
+      launch_mix<__nv_bfloat16>(w.xt, prev, Lw.mix, w.bf, B, T, d, s);
+      mixed = w.bf;
+    } else {
+      launch_mix<float>(w.xt, prev, Lw.mix, w.mixed, B, T, d, s);
+    }
     Y_CUDA(cudaMemcpy2DAsync(prev, d * sizeof(float), w.xt + (size_t)(T - 1) * d,
                              (size_t)T * d * sizeof(float), d * sizeof(float), B,
                              cudaMemcpyDeviceToDevice, s));
-    const void* mixed = gemm_input(m, w, w.mixed, 6 * RD, s);
     const size_t esz = m->precision == YUF_PRECISION_BF16_WEIGHTS ? 2 : 4;
     const char* mixed_hi = static_cast<const char*>(mixed) + 3 * RD * esz;  // w, a, g mixes
     Y_TRY(gemm(m, mixed, d, RD, Lw.W_rkv, (long long)d * d, w.rkv, d, RD, (int)rows, d, d, 0.f, 3, s));
@@ -322,7 +338,7 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     else
       Y_TRY(wkv7_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, nullptr,
                           nullptr, B, T, H, N, false, s));
-    launch_layernorm<float>(w.y, Lw.ln_o_w, Lw.ln_o_b, w.g, w.tmp, (int)rows, d, s);
+    const void* att = ln_in(w.y, Lw.ln_o_w, Lw.ln_o_b, w.g);
     if (m->debug) {
       dump(m, "ln0", li, w.xt, RD, s);
       dump(m, "r", li, w.rkv, RD, s);
@@ -334,12 +350,11 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
       dump(m, "g", li, w.g, RD, s);
       dump(m, "y", li, w.y, RD, s);
     }
-    Y_TRY(gemm(m, gemm_input(m, w, w.tmp, RD, s), d, 0, Lw.W_o, 0, w.x, d, 0, (int)rows, d, d, 1.f, 1, s));
+    Y_TRY(gemm(m, att, d, 0, Lw.W_o, 0, w.x, d, 0, (int)rows, d, d, 1.f, 1, s));
     if (m->debug) dump(m, "h1", li, w.x, RD, s);
     // --- ROSA
-    launch_layernorm<float>(w.x, Lw.ln_r_w, Lw.ln_r_b, nullptr, w.tmp, (int)rows, d, s);
-    Y_TRY(gemm(m, gemm_input(m, w, w.tmp, RD, s), d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0, (int)rows,
-               3 * R, d, 0.f, 1, s));
+    Y_TRY(gemm(m, ln_in(w.x, Lw.ln_r_w, Lw.ln_r_b, nullptr), d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0,
+               (int)rows, 3 * R, d, 0.f, 1, s));
     Y_TRY(rosa_engine_dispatch(w.rosa, w.rosa + R, w.rosa + 2 * R, Lw.b_rosa, Lw.b_rosa + R,
                                Lw.b_rosa + 2 * R, 3 * R, Lw.decay, Lw.householder, mem, w.read, mem, B,
                                T, R, w.scan, s));
@@ -348,18 +363,21 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
                R, 1.f, 1, s));
     if (m->debug) dump(m, "h2", li, w.x, RD, s);
     // --- FFN
-    launch_layernorm<float>(w.x, Lw.ln_f_w, Lw.ln_f_b, nullptr, w.tmp, (int)rows, d, s);
-    Y_TRY(gemm(m, gemm_input(m, w, w.tmp, RD, s), d, 0, Lw.W_ffn_in, 0, w.ig, 8 * d, 0, (int)rows,
-               8 * d, d, 0.f, 1, s));
-    launch_silu_mul<float>(w.ig, w.h, (int)rows, 4 * d, s);
-    Y_TRY(gemm(m, gemm_input(m, w, w.h, rows * 4 * d, s), 4 * d, 0, Lw.W_ffn_out, 0, w.x, d, 0,
-               (int)rows, d, 4 * d, 1.f, 1, s));
+    Y_TRY(gemm(m, ln_in(w.x, Lw.ln_f_w, Lw.ln_f_b, nullptr), d, 0, Lw.W_ffn_in, 0, w.ig, 8 * d, 0,
+               (int)rows, 8 * d, d, 0.f, 1, s));
+    const void* hid = w.h;
+    if (bf) {
+      launch_silu_mul<__nv_bfloat16>(w.ig, w.bf, (int)rows, 4 * d, s);
+      hid = w.bf;
+    } else {
+      launch_silu_mul<float>(w.ig, w.h, (int)rows, 4 * d, s);
+    }
+    Y_TRY(gemm(m, hid, 4 * d, 0, Lw.W_ffn_out, 0, w.x, d, 0, (int)rows, d, 4 * d, 1.f, 1, s));
     if (m->debug) dump(m, "h3", li, w.x, RD, s);
   }
   // final norm + tied LM head
-  launch_layernorm<float>(w.x, m->fin_w, m->fin_b, nullptr, w.tmp, (int)rows, d, s);
-  const void* hn = gemm_input(m, w, w.tmp, RD, s);
-  const size_t esz = m->precision == YUF_PRECISION_BF16_WEIGHTS ? 2 : 4;
+  const void* hn = ln_in(w.x, m->fin_w, m->fin_b, nullptr);
+  const size_t esz = bf ? 2 : 4;
   if (logits_all)
     Y_TRY(gemm(m, hn, d, 0, m->emb_gemm, 0, logits_all, V, 0, (int)rows, V, d, 0.f, 1, s));
   if (logits_last) {
