@@ -296,8 +296,8 @@ yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const f
 //   3. per sequence, m_c = A^K m_{c-1} + z_c over the chunks (rosa_carry_kernel);
 //   4. every chunk is scanned again from its true start state (MODE 0).
 // Exact in exact arithmetic (linearity of the recurrence in m).  K = 32 for
-// R <= 128 (A^K in shared memory); K = 64 above, where A^K (R x R, 256 KB at
-// R = 256) is streamed from L2 in every carry step, so fewer, longer chunks.
+// R <= 128 (A^K in shared memory); K = 64 above, where the carry applies A^K in
+// its diagonal-plus-rank-K form (rosa_lowrank_kernel).
 static int rosa_par_k(int R) { return R <= 128 ? 32 : 64; }
 
 // One CTA per sequence; A^K (stored transposed: AKt[j][i] = (A^K)[i][j]) in
@@ -335,16 +335,69 @@ __global__ void __launch_bounds__(128)
   if (i < R && m_out) m_out[(size_t)b * R + i] = m;
 }
 
-// R > 128: A^K stays in global memory (L2-resident, read coalesced: AKt[j][i]
-// over the threads i), 32 rows of it in flight per thread.
+// R > 128: A^K (R x R) does not fit in shared memory, but it is a diagonal plus
+// a rank-K matrix.  With A = D (I - 2 d d^T):
+//   A^K x = D^K x - 2 sum_{s=1..K} p_s D^{K-s+1} d,   p_s = d^T A^{s-1} x,
+// i.e. A^K = D^K - 2 W M with W[:, s] = D^{K-s+1} d and M[s, :] = d^T A^{s-1}.
+// rosa_lowrank_kernel (one CTA) builds W (as Wt[s][i]), M (as Mt[j][s]) and D^K
+// once per launch; the carry then costs 2 K R products per chunk instead of R^2.
 __global__ void __launch_bounds__(256)
-    rosa_carry_global_kernel(const float* __restrict__ AKt, const float* __restrict__ z,
-                             const float* m0, float* __restrict__ m_start, float* m_out, int C, int R) {
+    rosa_lowrank_kernel(const float* __restrict__ decay, const float* __restrict__ dir, int raw,
+                        float* __restrict__ Wt, float* __restrict__ Mt, float* __restrict__ DK, int K,
+                        int R) {
+  __shared__ float scratch[32];
+  __shared__ float red[1];
+  const int j = threadIdx.x, nwarps = blockDim.x >> 5;
+  const bool act = j < R;
+  float d = act ? dir[j] : 0.f;
+  float dec = act ? decay[j] : 0.f;
+  if (raw) {  // as in rosa_scan_kernel: decay = sigmoid(param), d = normalize(householder)
+    dec = act ? 1.f / (1.f + expf(-dec)) : 0.f;
+    float x1[1] = {d * d};
+    block_sum_array<1>(x1, scratch, red, nwarps);
+    d = d / fmaxf(sqrtf(red[0]), 1e-12f);
+  }
+  // W columns: D^{K-s+1} d, s = 1..K  (Wt[s-1][j])
+  {
+    float pw = dec;  // dec^1 for s = K
+    for (int s = K; s >= 1; --s) {
+      if (act) Wt[(size_t)(s - 1) * R + j] = pw * d;
+      pw *= dec;
+    }
+  }
+  {
+    float pk = 1.f;
+    for (int s = 0; s < K; ++s) pk *= dec;
+    if (act) DK[j] = pk;
+  }
+  // M rows: x_1 = d, x_{s+1} = x_s A = (x_s D) - 2 ((x_s D) . d) d   (Mt[j][s-1])
+  float x = d;
+  for (int s = 1; s <= K; ++s) {
+    if (act) Mt[(size_t)j * K + (s - 1)] = x;
+    const float xd = x * dec;
+    float x1[1] = {xd * d};
+    block_sum_array<1>(x1, scratch, red, nwarps);
+    x = xd - 2.f * red[0] * d;
+  }
+}
+
+// One CTA per sequence; Wt [K][R] and Mt [R][K+1] (padded) in shared memory.
+__global__ void __launch_bounds__(256)
+    rosa_carry_lowrank_kernel(const float* __restrict__ Wt, const float* __restrict__ Mt,
+                              const float* __restrict__ DK, const float* __restrict__ z,
+                              const float* m0, float* __restrict__ m_start, float* m_out, int C, int K,
+                              int R) {
   extern __shared__ float sh[];
-  float* mv = sh;  // [R]
+  const int KP = K + 1;
+  float* Ws = sh;             // [K][R]
+  float* Ms = Ws + K * R;     // [R][K+1]
+  float* mv = Ms + R * KP;    // [R]
+  float* pv = mv + R;         // [K]
   const int b = blockIdx.x, i = threadIdx.x;
   const bool on = i < R;
-  const int ic = on ? i : 0;
+  for (int q = i; q < K * R; q += blockDim.x) Ws[q] = Wt[q];
+  for (int q = i; q < K * R; q += blockDim.x) Ms[(q / K) * KP + q % K] = Mt[q];
+  const float dk = on ? DK[i] : 0.f;
   float m = (on && m0) ? m0[(size_t)b * R + i] : 0.f;
   for (int c = 0; c < C; ++c) {
     const size_t row = ((size_t)b * C + c) * R;
@@ -353,15 +406,29 @@ __global__ void __launch_bounds__(256)
       mv[i] = m;
     }
     __syncthreads();
-    float a[8] = {on ? z[row + i] : 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    int j = 0;
-#pragma unroll 4
-    for (; j + 8 <= R; j += 8) {
-#pragma unroll
-      for (int u = 0; u < 8; ++u) a[u] = fmaf(__ldg(AKt + (size_t)(j + u) * R + ic), mv[j + u], a[u]);
+    if (i < K) {  // p_s = M[s, :] . m
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      int jj = 0;
+      for (; jj + 4 <= R; jj += 4) {
+        a0 = fmaf(Ms[(jj + 0) * KP + i], mv[jj + 0], a0);
+        a1 = fmaf(Ms[(jj + 1) * KP + i], mv[jj + 1], a1);
+        a2 = fmaf(Ms[(jj + 2) * KP + i], mv[jj + 2], a2);
+        a3 = fmaf(Ms[(jj + 3) * KP + i], mv[jj + 3], a3);
+      }
+      for (; jj < R; ++jj) a0 = fmaf(Ms[jj * KP + i], mv[jj], a0);
+      pv[i] = (a0 + a1) + (a2 + a3);
     }
-    for (; j < R; ++j) a[0] = fmaf(__ldg(AKt + (size_t)j * R + ic), mv[j], a[0]);
-    m = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+    __syncthreads();
+    if (on) {  // A^K m + z = D^K m - 2 W p + z
+      float a0 = 0.f, a1 = 0.f;
+      int s = 0;
+      for (; s + 2 <= K; s += 2) {
+        a0 = fmaf(Ws[s * R + i], pv[s], a0);
+        a1 = fmaf(Ws[(s + 1) * R + i], pv[s + 1], a1);
+      }
+      for (; s < K; ++s) a0 = fmaf(Ws[s * R + i], pv[s], a0);
+      m = fmaf(dk, m, z[row + i]) - 2.f * (a0 + a1);
+    }
     __syncthreads();
   }
   if (on && m_out) m_out[(size_t)b * R + i] = m;
@@ -379,6 +446,8 @@ static void launch_mode(const float* cand, const float* write, const float* gate
 }
 
 size_t rosa_parallel_scratch_floats(int B, int T, int R) {
+  // A^K (R <= 128) or its low-rank factors W, M and D^K (2 K R + R <= R^2 for
+  // R > 128, K = 64), then chunk end states and chunk start states
   const size_t C = (size_t)T / rosa_par_k(R);
   return (size_t)R * R + 2 * (size_t)B * C * R;
 }
@@ -402,9 +471,11 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
   float* AKt = scratch;
   float* z = AKt + (size_t)R * R;
   float* m_start = z + (size_t)B * C * R;
-  // 1. A^K from R unit vectors (inputs unused in MODE 2)
-  launch_mode<false, 2>(cand, write, gate, nullptr, nullptr, nullptr, ld, decay, dir, raw, nullptr,
-                        nullptr, AKt, R, K, R, s);
+  // 1. A^K from R unit vectors (inputs unused in MODE 2); its low-rank form
+  //    for R > 128 is built in step 3
+  if (R <= 128)
+    launch_mode<false, 2>(cand, write, gate, nullptr, nullptr, nullptr, ld, decay, dir, raw, nullptr,
+                          nullptr, AKt, R, K, R, s);
   // 2. chunk end states from zero: chunks are the batch, K tokens each
   launch_mode<false, 1>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, nullptr,
                         nullptr, z, B * C, K, R, s);
@@ -421,7 +492,18 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
     }
     rosa_carry_kernel<<<B, threads, sm, s>>>(AKt, z, m0, m_start, m_out, C, R);
   } else {
-    rosa_carry_global_kernel<<<B, threads, R * sizeof(float), s>>>(AKt, z, m0, m_start, m_out, C, R);
+    float* Wt = AKt;                   // [K][R]
+    float* Mt = Wt + (size_t)K * R;    // [R][K]
+    float* DK = Mt + (size_t)R * K;    // [R]
+    rosa_lowrank_kernel<<<1, threads, 0, s>>>(decay, dir, raw, Wt, Mt, DK, K, R);
+    const size_t sm = ((size_t)K * R + (size_t)R * (K + 1) + R + K) * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(rosa_carry_lowrank_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) {
+      set_error("rosa: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+      return YUF_ERR_CUDA;
+    }
+    rosa_carry_lowrank_kernel<<<B, threads, sm, s>>>(Wt, Mt, DK, z, m0, m_start, m_out, C, K, R);
   }
   // 4. rescan every chunk from its true start state
   if (gated)
