@@ -118,39 +118,55 @@ __global__ void timemix_post_kernel(const float* __restrict__ k, const float* __
   const int h = (int)(item - row * H);
   const int d = H * N;
   const size_t base = row * d + (size_t)h * N;
+  // two columns per lane (N is even): 8-byte loads and stores
   float ss = 0.f;
-  for (int j = lane; j < N; j += 32) {
-    const float kv = k[base + j] * k_k[h * N + j];
-    ss = fmaf(kv, kv, ss);
+  for (int j = 2 * lane; j < N; j += 64) {
+    const float2 kv = *reinterpret_cast<const float2*>(k + base + j);
+    const float2 kk = *reinterpret_cast<const float2*>(k_k + h * N + j);
+    ss = fmaf(kv.x * kk.x, kv.x * kk.x, ss);
+    ss = fmaf(kv.y * kk.y, kv.y * kk.y, ss);
   }
   const float nrm = sqrtf(warp_sum(ss));
   const float inv = 1.f / fmaxf(nrm, 1e-12f);  // F.normalize eps (model.py:116)
-  for (int j = lane; j < N; j += 32) {
+  for (int j = 2 * lane; j < N; j += 64) {
     const int c = h * N + j;
     const size_t i = base + j;
-    const float kv = k[i];
-    const float a = 1.f / (1.f + expf(-(a0[c] + la[i])));
-    const float kk = kv * k_k[c] * inv;
-    w_raw[i] = w0[c] + lw[i];
-    a_op[i] = -kk;
-    b_op[i] = kk * a;
-    k_adj[i] = kv * (1.f + (a - 1.f) * k_a[c]);
-    g_out[i] = 1.f / (1.f + expf(-lg[i]));
+    const float2 kv = *reinterpret_cast<const float2*>(k + i);
+    const float2 kkp = *reinterpret_cast<const float2*>(k_k + c);
+    const float2 kap = *reinterpret_cast<const float2*>(k_a + c);
+    const float2 a0p = *reinterpret_cast<const float2*>(a0 + c);
+    const float2 w0p = *reinterpret_cast<const float2*>(w0 + c);
+    const float2 lwv = *reinterpret_cast<const float2*>(lw + i);
+    const float2 lav = *reinterpret_cast<const float2*>(la + i);
+    const float2 lgv = *reinterpret_cast<const float2*>(lg + i);
+    const float ax = 1.f / (1.f + expf(-(a0p.x + lav.x))), ay = 1.f / (1.f + expf(-(a0p.y + lav.y)));
+    const float kkx = kv.x * kkp.x * inv, kky = kv.y * kkp.y * inv;
+    *reinterpret_cast<float2*>(w_raw + i) = make_float2(w0p.x + lwv.x, w0p.y + lwv.y);
+    *reinterpret_cast<float2*>(a_op + i) = make_float2(-kkx, -kky);
+    *reinterpret_cast<float2*>(b_op + i) = make_float2(kkx * ax, kky * ay);
+    *reinterpret_cast<float2*>(k_adj + i) =
+        make_float2(kv.x * (1.f + (ax - 1.f) * kap.x), kv.y * (1.f + (ay - 1.f) * kap.y));
+    *reinterpret_cast<float2*>(g_out + i) =
+        make_float2(1.f / (1.f + expf(-lgv.x)), 1.f / (1.f + expf(-lgv.y)));
   }
 }
 
 // SiLU(in) * gate over the fused [rows, 2F] projection (in | gate halves).
+// One block per row (grid-strided over rows), four columns per thread (F % 4 == 0).
 template <typename OUT>
 __global__ void silu_mul_kernel(const float* __restrict__ ig, OUT* __restrict__ out, int rows,
                                 int F) {
-  const size_t total = (size_t)rows * F;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t row = i / F;
-    const int c = (int)(i - row * F);
-    const float h = ig[row * 2 * F + c];
-    const float gv = ig[row * 2 * F + F + c];
-    store_out(out, i, h / (1.f + expf(-h)) * gv);
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* in = ig + (size_t)row * 2 * F;
+    const size_t o = (size_t)row * F;
+    for (int c = 4 * threadIdx.x; c < F; c += 4 * blockDim.x) {
+      const float4 h = *reinterpret_cast<const float4*>(in + c);
+      const float4 gv = *reinterpret_cast<const float4*>(in + F + c);
+      store_out(out, o + c + 0, h.x / (1.f + expf(-h.x)) * gv.x);
+      store_out(out, o + c + 1, h.y / (1.f + expf(-h.y)) * gv.y);
+      store_out(out, o + c + 2, h.z / (1.f + expf(-h.z)) * gv.z);
+      store_out(out, o + c + 3, h.w / (1.f + expf(-h.w)) * gv.w);
+    }
   }
 }
 
@@ -197,7 +213,7 @@ void launch_timemix_post(const float* k, const float* lw, const float* la, const
 }
 template <typename OUT>
 void launch_silu_mul(const float* ig, OUT* out, int rows, int F, cudaStream_t s) {
-  silu_mul_kernel<OUT><<<grid_for((size_t)rows * F, 256), 256, 0, s>>>(ig, out, rows, F);
+  silu_mul_kernel<OUT><<<rows < 148 * 64 ? rows : 148 * 64, 256, 0, s>>>(ig, out, rows, F);
 }
 void launch_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) {
   to_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
