@@ -63,6 +63,59 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
   }
 }
 
+// The same, with the row held in registers: VPL float4 per lane (d <= 128 VPL),
+// one read of x (and of gate), two-pass mean/variance from registers.
+template <typename OUT, int VPL>
+__global__ void __launch_bounds__(128)
+    layernorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                         const float* __restrict__ b, const float* __restrict__ gate,
+                         OUT* __restrict__ out, int rows, int d) {
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int d4 = d >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * d);
+  float4 v[VPL];
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    const int i = lane + 32 * u;
+    v[u] = i < d4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[u].x + v[u].y) + (v[u].z + v[u].w);
+  }
+  const float mean = warp_sum(s) / d;
+  float q = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    if (lane + 32 * u < d4) {
+      const float cx = v[u].x - mean, cy = v[u].y - mean, cz = v[u].z - mean, cw = v[u].w - mean;
+      q = fmaf(cx, cx, fmaf(cy, cy, fmaf(cz, cz, fmaf(cw, cw, q))));
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / d + 1e-5f);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  const float4* g4 = gate ? reinterpret_cast<const float4*>(gate + (size_t)row * d) : nullptr;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    const int i = lane + 32 * u;
+    if (i < d4) {
+      const float4 ww = w4[i], bb = b4[i];
+      float4 o = make_float4((v[u].x - mean) * rstd * ww.x + bb.x, (v[u].y - mean) * rstd * ww.y + bb.y,
+                             (v[u].z - mean) * rstd * ww.z + bb.z, (v[u].w - mean) * rstd * ww.w + bb.w);
+      if (g4) {
+        const float4 gg = g4[i];
+        o.x *= gg.x; o.y *= gg.y; o.z *= gg.z; o.w *= gg.w;
+      }
+      const size_t base = (size_t)row * d + 4 * i;
+      store_out(out, base + 0, o.x);
+      store_out(out, base + 1, o.y);
+      store_out(out, base + 2, o.z);
+      store_out(out, base + 3, o.w);
+    }
+  }
+}
+
 // Token shift + the six lerps (model.py:98-105):
 //   delta = xt - shifted, x_c = xt + delta * mix_c, shifted = [prev, xt[:-1]]
 // out layout [6][rows][d] in the order r, k, v, w, a, g (the order the batched
@@ -190,6 +243,17 @@ void launch_embed(const int32_t* ids, const float* E, float* x, int rows, int d,
 template <typename OUT>
 void launch_layernorm(const float* x, const float* w, const float* b, const float* gate, OUT* out,
                       int rows, int d, cudaStream_t s) {
+  const int blocks4 = (rows + 3) / 4;
+  if (d % 4 == 0 && d <= 8 * 128) {  // row in registers (d <= 1024)
+    const int vpl = (d / 4 + 31) / 32;
+    switch (vpl) {
+#define CASE(V) \
+  case V: layernorm_reg_kernel<OUT, V><<<blocks4, 128, 0, s>>>(x, w, b, gate, out, rows, d); return;
+      CASE(1) CASE(2) CASE(3) CASE(4) CASE(5) CASE(6) CASE(7) CASE(8)
+#undef CASE
+      default: break;
+    }
+  }
   const int warps = 8;
   layernorm_kernel<OUT><<<(rows + warps - 1) / warps, 32 * warps, 0, s>>>(x, w, b, gate, out, rows, d);
 }
