@@ -42,6 +42,12 @@ const char* yuf_status_string(yuf_status_t status);
 const char* yuf_last_error(void);
 /* ABI version of this library (bumped on any incompatible change). */
 int yuf_abi_version(void);
+/* Number of bounded device-side waits (the time-parallel scan's staging barrier) that
+   expired on the current device since the previous call; the count is cleared.  0 in
+   a healthy run; a nonzero count means the outputs of the affected launches are void.
+   Synchronous (reads a device counter).  No reference counterpart: the reference
+   kernels have no bounded waits. */
+unsigned int yuf_wait_timeouts(void);
 
 /* WKV-7 forward scan with an optional initial state.
  * Replaces the forward launch behind torch.ops.yufmusicgen_rwkv7.forward

@@ -254,6 +254,15 @@ def test_wkv7_time_parallel_shapes(B, T, H, N, with_state):
     close(s, sr)
 
 
+def test_time_parallel_waits_never_expired():
+    """The pair kernel's staging barrier waits are bounded; none may have expired."""
+    from yufmusicgen_b200 import _lib
+    ins = wkv_op_inputs(2, 300, 3, 40, seed=11)
+    cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), algo=cuda_ops.ALGO_PARALLEL)
+    torch.cuda.synchronize()
+    assert _lib.wait_timeouts() == 0
+
+
 def test_wkv7_time_parallel_full_config2_and_inplace_state():
     ins = wkv_op_inputs(8, 2048, 16, 40, seed=0, with_state=True)
     st = cu(ins["s0"])

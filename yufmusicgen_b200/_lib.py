@@ -79,6 +79,8 @@ def load():
         lib.yuf_last_error.restype = ctypes.c_char_p
         lib.yuf_last_error.argtypes = []
         lib.yuf_abi_version.restype = I
+        lib.yuf_wait_timeouts.restype = ctypes.c_uint
+        lib.yuf_wait_timeouts.argtypes = []
         for name, args in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = args
@@ -96,6 +98,11 @@ def call(name: str, *args) -> None:
     st = getattr(lib, name)(*args)
     if st != 0:
         raise YufError(name, st, lib.yuf_last_error().decode())
+
+
+def wait_timeouts() -> int:
+    """Bounded device waits that expired since the last call (0 when healthy)."""
+    return int(load().yuf_wait_timeouts())
 
 
 def ptr(t) -> int | None:

@@ -63,6 +63,7 @@ void scratch_free(void* p, cudaStream_t st) {
   if (p) cudaFreeAsync(p, st);
 }
 
+unsigned int wkv7_pair_wait_timeouts();
 yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
                            float* ckpt, float* sa, int B, int T, int H, int N, bool compat,
@@ -108,6 +109,8 @@ static yuf_status_t check_wkv_args(const float* const* in, int n_in, int B, int 
 using namespace yuf;
 
 extern "C" {
+
+unsigned int yuf_wait_timeouts(void) { return yuf::wkv7_pair_wait_timeouts(); }
 
 const char* yuf_status_string(yuf_status_t s) {
   switch (s) {

@@ -15,11 +15,72 @@
 // Work item bb = s * Cper + c is chunk c of sequence s: tokens
 // [c*K, min(c*K + K, Tstride)) -- the last chunk of a sequence may be shorter.
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
 namespace yuf {
+
+// ---- TMA staging of the pair kernel ---------------------------------------
+// Each input [B*T, H*N] fp32 tensor is described by a 2-D tensor map (box = N
+// columns x 8 rows: one head's 8 tokens); one thread issues the six loads of an
+// 8-token group onto an mbarrier with the expected byte count, every thread
+// waits on the barrier's phase.  Waits are bounded: after WAIT_NS nanoseconds
+// (global timer) a thread counts a timeout in g_pair_wait_timeouts and leaves
+// the kernel.
+struct PairTmaps {
+  CUtensorMap m[6];  // r, w, k, v, a, b
+};
+
+__device__ unsigned int g_pair_wait_timeouts;
+constexpr unsigned long long WAIT_NS = 200ull * 1000 * 1000;  // 0.2 s
+
+YUF_DEVICE uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+YUF_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+YUF_DEVICE void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+YUF_DEVICE void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+YUF_DEVICE void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+YUF_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+YUF_DEVICE unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// true when the barrier's phase `parity` completed within WAIT_NS
+YUF_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  unsigned long long t0 = 0;
+  for (unsigned int it = 0;; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 63) == 0) {  // look at the clock every 64 polls
+      const unsigned long long now = global_ns();
+      if (it == 0) t0 = now;
+      else if (now - t0 > WAIT_NS) return false;
+    }
+  }
+}
 
 YUF_DEVICE size_t item_head_off(int bb, int hh, int K, int H, int N, int Tstride, int Cper) {
   return (((size_t)(bb / Cper) * Tstride + (size_t)(bb % Cper) * K) * H + hh) * N;
@@ -255,10 +316,13 @@ struct PairWCfg {
   static constexpr int PAD = RAW + 6 * TS * N;    // [4][TS][VP] scaled a, b, k, r in lane layout
   static constexpr int GEND = PAD + 4 * TS * VP;  // [VP] gamma at the group end
   static constexpr int VV = GEND + VP;            // [TS][N] values
-  static constexpr int TOTAL = VV + TS * N;
+  static constexpr int MBAR = (VV + TS * N + 1) / 2 * 2;  // one 8-byte mbarrier
+  static constexpr int TOTAL = MBAR + 2;
   static constexpr size_t BYTES = (size_t)TOTAL * sizeof(float);
+  static constexpr uint32_t TX_BYTES = 6u * TS * N * sizeof(float);  // six full boxes per group
   static_assert(N % 8 == 0 && C % 2 == 0 && N <= 64 && NW * 8 * R == N,
                 "warp pair kernel: N in {16, 32, 40, 48, 64}");
+  static_assert((TS * N * sizeof(float)) % 128 == 0, "TMA boxes land on 128-byte boundaries");
 };
 
 // Barrier over the block's warps (a warp barrier when the block is one warp).
@@ -286,12 +350,14 @@ __global__ void __launch_bounds__(PairWCfg<N>::NT)
                       const float* __restrict__ k, const float* __restrict__ v,
                       const float* __restrict__ a, const float* __restrict__ b,
                       float* __restrict__ y, float* __restrict__ Q, float* __restrict__ U_out,
-                      float* __restrict__ P_out, int K_, int H, int Tstride, int Cper) {
+                      float* __restrict__ P_out, int K_, int H, int Tstride, int Cper,
+                      const __grid_constant__ PairTmaps tm) {
   using K = PairWCfg<N>;
   constexpr int R = K::R, C = K::C, C2 = K::C2, CS = K::CS, VP = K::VP, TS = K::TS;
   constexpr int RH = (R + 1) / 2;  // outputs kept by the even lane of a pair after reduce-scatter
-  extern __shared__ float4 smem_f4[];
+  extern __shared__ __align__(128) float4 smem_f4[];
   float* sm = reinterpret_cast<float*>(smem_f4);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + K::MBAR);
 
   const int bh = blockIdx.x;
   const int bb = bh / H, hh = bh - bb * H;
@@ -315,22 +381,23 @@ __global__ void __launch_bounds__(PairWCfg<N>::NT)
   const size_t tok_stride = (size_t)H * N;
   const size_t head_off = item_head_off(bb, hh, K_, H, N, Tstride, Cper);
   float* Qh = Q + (size_t)bh * K_ * N;  // Q[bb][hh][t][row]
-  const float* src[6] = {r + head_off, w + head_off, k + head_off,
-                         v + head_off, a + head_off, b + head_off};
-  auto stage = [&](int t0, int Tc) {
-    constexpr int Q4 = N / 4;
+  // TMA coordinates of this item's first token: column hh*N, row s*Tstride + c*K
+  const int tx = hh * N;
+  const int ty = (bb / Cper) * Tstride + (bb % Cper) * K_;
+  auto stage = [&](int t0) {  // one thread: the six 8-token boxes of a group
+    mbar_expect_tx(bar, K::TX_BYTES);
 #pragma unroll
     for (int arr = 0; arr < 6; ++arr)
-      for (int idx = tid; idx < Tc * Q4; idx += NT) {
-        const int t = idx / Q4, q = idx - t * Q4;
-        cp_async_16(sm + K::RAW + (arr * TS + t) * N + 4 * q,
-                    src[arr] + (size_t)(t0 + t) * tok_stride + 4 * q);
-      }
-    cp_async_commit();
+      tma_load_2d(sm + K::RAW + arr * TS * N, &tm.m[arr], bar, tx, ty + t0);
   };
 
   const int ngroups = (T + TS - 1) / TS;
-  if (ngroups > 0) stage(0, min(TS, T));
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  block_sync<K::NW>();
+  if (tid == 0 && ngroups > 0) stage(0);
   const float* Pa = sm + K::PAD + 0 * TS * VP + g * CS;
   const float* Pb = sm + K::PAD + 1 * TS * VP + g * CS;
   const float* Pk = sm + K::PAD + 2 * TS * VP + g * CS;
@@ -346,8 +413,10 @@ __global__ void __launch_bounds__(PairWCfg<N>::NT)
   for (int gi = 0; gi < ngroups; ++gi) {
     const int t0 = gi * TS;
     const int Tc = min(TS, T - t0);
-    cp_async_wait<0>();
-    block_sync<K::NW>();
+    if (!mbar_wait(bar, gi & 1)) {  // every thread times out alike; the outputs are void
+      atomicAdd(&g_pair_wait_timeouts, 1u);
+      return;
+    }
     // scaled vectors: a thread per column pair, running gamma over the group's tokens
     if (tid < N / 2) {
       const int j = 2 * tid;
@@ -374,7 +443,10 @@ __global__ void __launch_bounds__(PairWCfg<N>::NT)
       *reinterpret_cast<float2*>(sm + K::GEND + pj) = gam;
     }
     block_sync<K::NW>();
-    if (gi + 1 < ngroups) stage(t0 + TS, min(TS, T - t0 - TS));  // raw buffer is free again
+    if (tid == 0 && gi + 1 < ngroups) {  // raw boxes are free again (all reads done)
+      fence_proxy_async();
+      stage(t0 + TS);
+    }
 
     // sa of the group's first token; every later token's sa comes out of the
     // previous token's pass over the state together with that token's outputs
@@ -663,9 +735,69 @@ int wkv7_correct_max_chunk(int N) {
   return 1 << 20;
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// Tensor maps of the six [rows, H*N] inputs, box = N columns x 8 rows.
+static yuf_status_t make_pair_tmaps(const float* const (&src)[6], long long rows, int H, int N,
+                                    PairTmaps* out) {
+  auto enc = tensor_map_encoder();
+  if (!enc) {
+    set_error("wkv7 pair: cuTensorMapEncodeTiled is unavailable");
+    return YUF_ERR_CUDA;
+  }
+  const cuuint64_t gdim[2] = {(cuuint64_t)H * N, (cuuint64_t)rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)H * N * sizeof(float)};
+  const cuuint32_t box[2] = {(cuuint32_t)N, 8u};
+  const cuuint32_t estride[2] = {1u, 1u};
+  for (int i = 0; i < 6; ++i) {
+    const CUresult rc = enc(&out->m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(src[i]),
+                            gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (rc != CUDA_SUCCESS) {
+      set_error("wkv7 pair: cuTensorMapEncodeTiled failed (%d) for input %d", (int)rc, i);
+      return YUF_ERR_CUDA;
+    }
+  }
+  return YUF_OK;
+}
+
+// Timeouts of the pair kernel's bounded barrier waits on the current device
+// since the last call (0 in a healthy run); clears the count.
+unsigned int wkv7_pair_wait_timeouts() {
+  unsigned int n = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&n, g_pair_wait_timeouts, sizeof(n)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_pair_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess) {
+    cudaGetLastError();
+    return ~0u;
+  }
+  return n;
+}
+
 yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, const float* v,
                                 const float* a, const float* b, float* y, float* Q, float* U, float* P,
                                 int items, int K, int H, int N, int Tstride, int Cper, cudaStream_t st) {
+  PairTmaps tm;
+  if (N <= 64) {
+    const float* const src[6] = {r, w, k, v, a, b};
+    const yuf_status_t rc = make_pair_tmaps(src, (long long)(items / Cper) * Tstride, H, N, &tm);
+    if (rc != YUF_OK) return rc;
+  }
   switch (N) {
 #define CASEW(NN)                                                                                \
   case NN: {                                                                                     \
@@ -677,7 +809,8 @@ yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, 
       set_error("wkv7 pair: cudaFuncSetAttribute failed");                                      \
       return YUF_ERR_CUDA;                                                                       \
     }                                                                                            \
-    kern<<<items * H, Kc::NT, Kc::BYTES, st>>>(r, w, k, v, a, b, y, Q, U, P, K, H, Tstride, Cper); \
+    kern<<<items * H, Kc::NT, Kc::BYTES, st>>>(r, w, k, v, a, b, y, Q, U, P, K, H, Tstride, Cper, \
+                                                tm);                                             \
     return check_launch("wkv7_pairw_kernel");                                                    \
   }
 #define CASE(NN)                                                                                 \
