@@ -305,21 +305,29 @@ static int rosa_par_k(int R) { return R <= 128 ? 32 : 64; }
 __global__ void __launch_bounds__(128)
     rosa_carry_kernel(const float* __restrict__ AKt, const float* __restrict__ z,
                       const float* m0, float* __restrict__ m_start, float* m_out, int C, int R) {
-  extern __shared__ float sh[];
-  float* A = sh;          // [R][R]
-  float* mv = sh + R * R; // [R]
+  extern __shared__ float4 sh4[];
+  float* A = reinterpret_cast<float*>(sh4);  // [R][R]
+  float* mv = A + R * R;                     // [R]
   const int b = blockIdx.x, i = threadIdx.x;
-  for (int q = i; q < R * R; q += blockDim.x) A[q] = AKt[q];
+  // A^K staged asynchronously (R*R is a multiple of 4: R % 4 == 0 here, or the
+  // scalar tail below)
+  for (int q = i; q < R * R / 4; q += blockDim.x) cp_async_16(A + 4 * q, AKt + 4 * q);
+  cp_async_commit();
+  for (int q = (R * R / 4) * 4 + i; q < R * R; q += blockDim.x) A[q] = AKt[q];
   float m = (i < R && m0) ? m0[(size_t)b * R + i] : 0.f;
+  float zc = (i < R && C > 0) ? z[(size_t)b * C * R + i] : 0.f;  // z of the current chunk
+  cp_async_wait<0>();
   for (int c = 0; c < C; ++c) {
     const size_t row = ((size_t)b * C + c) * R;
+    // next chunk's z is loaded now, so its latency hides behind this step
+    const float zn = (i < R && c + 1 < C) ? z[row + R + i] : 0.f;
     if (i < R) {
       m_start[row + i] = m;
       mv[i] = m;
     }
     __syncthreads();
     if (i < R) {
-      float a0 = z[row + i], a1 = 0.f, a2 = 0.f, a3 = 0.f;
+      float a0 = zc, a1 = 0.f, a2 = 0.f, a3 = 0.f;
       int j = 0;
       for (; j + 4 <= R; j += 4) {
         a0 = fmaf(A[(j + 0) * R + i], mv[j + 0], a0);
@@ -330,6 +338,7 @@ __global__ void __launch_bounds__(128)
       for (; j < R; ++j) a0 = fmaf(A[j * R + i], mv[j], a0);
       m = (a0 + a1) + (a2 + a3);
     }
+    zc = zn;
     __syncthreads();
   }
   if (i < R && m_out) m_out[(size_t)b * R + i] = m;
@@ -381,26 +390,33 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// One CTA per sequence; Wt [K][R] and Mt [R][K+1] (padded) in shared memory.
+// One CTA per sequence; Wt [K][R] and Mt [R][K] in shared memory.
 __global__ void __launch_bounds__(256)
     rosa_carry_lowrank_kernel(const float* __restrict__ Wt, const float* __restrict__ Mt,
                               const float* __restrict__ DK, const float* __restrict__ z,
                               const float* m0, float* __restrict__ m_start, float* m_out, int C, int K,
                               int R) {
-  extern __shared__ float sh[];
-  const int KP = K + 1;
-  float* Ws = sh;             // [K][R]
-  float* Ms = Ws + K * R;     // [R][K+1]
+  extern __shared__ float4 sh4[];
+  const int KP = K;           // Ms rows are read across the threads s: conflict-free unpadded
+  float* Ws = reinterpret_cast<float*>(sh4);  // [K][R]
+  float* Ms = Ws + K * R;     // [R][K]
   float* mv = Ms + R * KP;    // [R]
   float* pv = mv + R;         // [K]
   const int b = blockIdx.x, i = threadIdx.x;
   const bool on = i < R;
-  for (int q = i; q < K * R; q += blockDim.x) Ws[q] = Wt[q];
-  for (int q = i; q < K * R; q += blockDim.x) Ms[(q / K) * KP + q % K] = Mt[q];
+  // factors staged asynchronously (K*R is a multiple of 4: K = 64)
+  for (int q = i; q < K * R / 4; q += blockDim.x) {
+    cp_async_16(Ws + 4 * q, Wt + 4 * q);
+    cp_async_16(Ms + 4 * q, Mt + 4 * q);
+  }
+  cp_async_commit();
   const float dk = on ? DK[i] : 0.f;
   float m = (on && m0) ? m0[(size_t)b * R + i] : 0.f;
+  float zc = (on && C > 0) ? z[(size_t)b * C * R + i] : 0.f;  // z of the current chunk
+  cp_async_wait<0>();
   for (int c = 0; c < C; ++c) {
     const size_t row = ((size_t)b * C + c) * R;
+    const float zn = (on && c + 1 < C) ? z[row + R + i] : 0.f;  // next chunk's z, in flight
     if (on) {
       m_start[row + i] = m;
       mv[i] = m;
@@ -427,8 +443,9 @@ __global__ void __launch_bounds__(256)
         a1 = fmaf(Ws[(s + 1) * R + i], pv[s + 1], a1);
       }
       for (; s < K; ++s) a0 = fmaf(Ws[s * R + i], pv[s], a0);
-      m = fmaf(dk, m, z[row + i]) - 2.f * (a0 + a1);
+      m = fmaf(dk, m, zc) - 2.f * (a0 + a1);
     }
+    zc = zn;
     __syncthreads();
   }
   if (on && m_out) m_out[(size_t)b * R + i] = m;
@@ -496,7 +513,7 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
     float* Mt = Wt + (size_t)K * R;    // [R][K]
     float* DK = Mt + (size_t)R * K;    // [R]
     rosa_lowrank_kernel<<<1, threads, 0, s>>>(decay, dir, raw, Wt, Mt, DK, K, R);
-    const size_t sm = ((size_t)K * R + (size_t)R * (K + 1) + R + K) * sizeof(float);
+    const size_t sm = ((size_t)K * R + (size_t)R * K + R + K) * sizeof(float);
     cudaError_t e = cudaFuncSetAttribute(rosa_carry_lowrank_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) {

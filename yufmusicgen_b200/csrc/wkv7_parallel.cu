@@ -83,9 +83,15 @@ __global__ void __launch_bounds__(CarryCfg<N>::NT)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
   const float* s0p = s0 ? s0 + (size_t)bh * NN : nullptr;
-  for (int x = tid; x < Cf::SROWS * NP; x += NT) {
+  for (int x = tid; x < Cf::SROWS * NP; x += NT) {  // zero padding, and all of S without s0
     const int i = x / NP, j = x - i * NP;
-    Ss[x] = (s0p && i < N && j < N) ? s0p[i * N + j] : 0.f;
+    if (!s0p || i >= N || j >= N) Ss[x] = 0.f;
+  }
+  if (s0p) {  // s0 rows arrive with the first ring stage's group
+    for (int x = tid; x < N * Q4; x += NT) {
+      const int i = x / Q4, j4 = x - i * Q4;
+      cp_async_16(Ss + i * NP + 4 * j4, s0p + (size_t)i * N + 4 * j4);
+    }
   }
   auto fetch = [&](int c) {  // always commits a group (empty past the last chunk)
     if (c < C) {
@@ -104,6 +110,8 @@ __global__ void __launch_bounds__(CarryCfg<N>::NT)
   for (int c = 0; c < C; ++c) {
     __syncthreads();  // Ss = S_{c-1}; stage (c - 1) % D free
     fetch(c + D - 1);
+    cp_async_wait<D - 1>();  // chunk c's group landed (and, at c = 0, the s0 rows)
+    __syncthreads();
     {
       float* dst = S_start + (((size_t)s * C + c) * H + h) * NN;
       for (int x = tid; x < N * Q4; x += NT) {
@@ -112,8 +120,6 @@ __global__ void __launch_bounds__(CarryCfg<N>::NT)
             *reinterpret_cast<const float4*>(Ss + i * NP + 4 * j4);
       }
     }
-    cp_async_wait<D - 1>();  // chunk c's group landed
-    __syncthreads();
     const float* Pc = ring + (c % D) * STAGE;
     const float* Uc = Pc + N * PP;
     const float* Ug = U + (((size_t)s * C + c) * H + h) * NN;
