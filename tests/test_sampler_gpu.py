@@ -1,6 +1,8 @@
 """On-device sampler (yuf_sample): Philox stream, masking, greedy, top-k/top-p
 distribution, batch-layout independence."""
 
+import zlib
+
 import numpy as np
 import pytest
 
@@ -71,3 +73,66 @@ def test_draws_depend_on_sequence_id_not_batch_position():
     assert torch.equal(full[5:], part)
     again = sample(logits, seed=11, step=4, top_k=32, seq0=100)
     assert torch.equal(full, again)
+
+
+FLT_MAX = np.float32(np.finfo(np.float32).max)
+
+
+def _host_pick(row, u, temperature, top_k, top_p, mask_below, eos_id, allow_eos):
+    """The sampler restated on the host (float64 softmax): top_k by value
+    descending with ties to the smaller id, top-p cut, inverse CDF.  Returns the
+    pick and the distance of the draw from the nearest CDF boundary."""
+    V = row.size
+    ids = np.arange(V)
+    allowed = (ids >= mask_below) | (allow_eos & (ids == eos_id))
+    # the C ABI takes a float temperature and divides in fp32
+    inv_t = np.float32(1.0) / np.float32(temperature) if temperature > 0 else np.float32(1.0)
+    x = np.where(allowed, row.astype(np.float32) * inv_t, -FLT_MAX).astype(np.float32)
+    k = top_k if temperature > 0 else 1
+    order = np.lexsort((ids, -x.astype(np.float64)))[:k]
+    tv, ti = x[order].astype(np.float64), order
+    if k == 1:
+        return int(ti[0]), np.inf
+    valid = tv != -FLT_MAX
+    kk = int(np.argmin(valid)) if not valid.all() else k
+    p = np.exp(tv[:kk] - tv[0])
+    p /= p.sum()
+    cum, keep = 0.0, 0
+    while keep < kk and not cum > top_p:
+        cum += p[keep]
+        keep += 1
+    keep = max(keep, 1)
+    cdf = np.cumsum(p[:keep])
+    target = u * cdf[-1]
+    pos = min(int(np.searchsorted(cdf, target, side="right")), keep - 1)
+    return int(ti[pos]), float(np.min(np.abs(cdf - target)))
+
+
+@pytest.mark.parametrize("kind,top_k,top_p,mask_below", [
+    ("distinct", 32, 1.0, 0),
+    ("ties", 32, 1.0, 0),      # many logits equal to the k-th largest: id order decides
+    ("ties", 100, 0.9, 260),
+    ("distinct", 1, 1.0, 0),
+    ("ties", 1, 1.0, 0),       # argmax, first id among equal maxima
+    ("masked", 32, 1.0, 0),    # fewer allowed ids than top_k
+    ("distinct", 1024, 0.95, 0),
+])
+def test_topk_selection_matches_host_restatement(kind, top_k, top_p, mask_below):
+    g = np.random.default_rng(zlib.crc32(f"{kind}{top_k}".encode()))
+    B, V = 96, 20000
+    z = g.standard_normal((B, V)).astype(np.float32) * 2
+    if kind == "ties":
+        z = np.round(z * 2) / 2  # about 30 distinct values per row
+    if kind == "masked":
+        mask_below = V - 10
+    logits = torch.from_numpy(z).cuda()
+    ids, u = sample(logits, seed=21, step=3, temperature=0.8, top_k=top_k, top_p=top_p,
+                    mask_below=mask_below, eos_id=2, allow_eos=True, return_uniform=True)
+    ids, u = ids.cpu().numpy(), u.cpu().numpy()
+    for bi in range(B):
+        want, margin = _host_pick(z[bi], float(u[bi]), 0.8, top_k, top_p, mask_below, 2, True)
+        # the device sums __expf terms in fp32: a draw within 1e-4 of a CDF
+        # boundary may land on the neighbour
+        assert ids[bi] == want or margin < 1e-4, (bi, ids[bi], want, margin)
+    if kind == "masked":
+        assert ((ids >= mask_below) | (ids == 2)).all()

@@ -257,13 +257,6 @@ static WS carve(yuf_model* m, size_t rows, void* base) {
   return w;
 }
 
-// GEMM input operand: fp32 as is, or converted to bf16 in the staging buffer.
-static const void* gemm_input(yuf_model* m, WS& w, const float* x, size_t n, cudaStream_t s) {
-  if (m->precision != YUF_PRECISION_BF16_WEIGHTS) return x;
-  launch_to_bf16(x, w.bf, n, s);
-  return w.bf;
-}
-
 static void dump(yuf_model* m, const char* region, int layer, const float* dev, size_t n,
                  cudaStream_t s) {
   if (!m->debug) return;
@@ -307,24 +300,35 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     float* S = m->st_S + ((size_t)li * m->n_slots + slot0) * m->slot_S();
     float* mem = m->st_m + ((size_t)li * m->n_slots + slot0) * m->slot_m();
     // --- TimeMix
-    launch_layernorm<float>(w.x, Lw.ln_t_w, Lw.ln_t_b, nullptr, w.xt, (int)rows, d, s);
-    const void* mixed = w.mixed;
-    if (bf) {
-      launch_mix<__nv_bfloat16>(w.xt, prev, Lw.mix, w.bf, B, T, d, s);
-      mixed = w.bf;
-    } else {
-      launch_mix<float>(w.xt, prev, Lw.mix, w.mixed, B, T, d, s);
+    const void* mixed = bf ? static_cast<const void*>(w.bf) : w.mixed;
+    const bool fused_mix =
+        T == 1 && (bf ? launch_ln_mix_step<__nv_bfloat16>(w.x, Lw.ln_t_w, Lw.ln_t_b, w.xt, prev,
+                                                           Lw.mix, w.bf, B, d, s)
+                      : launch_ln_mix_step<float>(w.x, Lw.ln_t_w, Lw.ln_t_b, w.xt, prev, Lw.mix,
+                                                  w.mixed, B, d, s));
+    if (!fused_mix) {
+      launch_layernorm<float>(w.x, Lw.ln_t_w, Lw.ln_t_b, nullptr, w.xt, (int)rows, d, s);
+      if (bf)
+        launch_mix<__nv_bfloat16>(w.xt, prev, Lw.mix, w.bf, B, T, d, s);
+      else
+        launch_mix<float>(w.xt, prev, Lw.mix, w.mixed, B, T, d, s);
+      Y_CUDA(cudaMemcpy2DAsync(prev, d * sizeof(float), w.xt + (size_t)(T - 1) * d,
+                               (size_t)T * d * sizeof(float), d * sizeof(float), B,
+                               cudaMemcpyDeviceToDevice, s));
     }
-    Y_CUDA(cudaMemcpy2DAsync(prev, d * sizeof(float), w.xt + (size_t)(T - 1) * d,
-                             (size_t)T * d * sizeof(float), d * sizeof(float), B,
-                             cudaMemcpyDeviceToDevice, s));
     const size_t esz = m->precision == YUF_PRECISION_BF16_WEIGHTS ? 2 : 4;
     const char* mixed_hi = static_cast<const char*>(mixed) + 3 * RD * esz;  // w, a, g mixes
     Y_TRY(gemm(m, mixed, d, RD, Lw.W_rkv, (long long)d * d, w.rkv, d, RD, (int)rows, d, d, 0.f, 3, s));
     Y_TRY(gemm(m, mixed_hi, d, RD, Lw.W_lr1, (long long)lr * d, w.lr1, lr, rows * lr, (int)rows, lr, d,
                0.f, 3, s));
-    launch_tanh<float>(w.lr1, w.lr1, rows * lr, s);  // w branch: tanh(xw W1)
-    const void* lr1 = gemm_input(m, w, w.lr1, 3 * rows * lr, s);
+    // w branch: tanh(xw W1); in bf16 mode the same pass converts all three branches
+    const void* lr1 = w.lr1;
+    if (bf) {
+      launch_tanh<__nv_bfloat16>(w.lr1, w.bf, rows * lr, 3 * rows * lr, s);
+      lr1 = w.bf;
+    } else {
+      launch_tanh<float>(w.lr1, w.lr1, rows * lr, rows * lr, s);
+    }
     Y_TRY(gemm(m, lr1, lr, rows * lr, Lw.W_lr2, (long long)d * lr, w.lr2, d, RD, (int)rows, d, lr, 0.f,
                3, s));
     launch_timemix_post(w.rkv + RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD, Lw.w0, Lw.a0, Lw.k_k, Lw.k_a,
@@ -357,10 +361,10 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
                (int)rows, 3 * R, d, 0.f, 1, s));
     Y_TRY(rosa_engine_dispatch(w.rosa, w.rosa + R, w.rosa + 2 * R, Lw.b_rosa, Lw.b_rosa + R,
                                Lw.b_rosa + 2 * R, 3 * R, Lw.decay, Lw.householder, mem, w.read, mem, B,
-                               T, R, w.scan, s));
+                               T, R, w.scan, bf ? w.bf : nullptr, s));
     if (m->debug) dump(m, "read", li, w.read, rows * R, s);
-    Y_TRY(gemm(m, gemm_input(m, w, w.read, rows * R, s), R, 0, Lw.W_rosa_out, 0, w.x, d, 0, (int)rows, d,
-               R, 1.f, 1, s));
+    Y_TRY(gemm(m, bf ? static_cast<const void*>(w.bf) : w.read, R, 0, Lw.W_rosa_out, 0, w.x, d, 0,
+               (int)rows, d, R, 1.f, 1, s));
     if (m->debug) dump(m, "h2", li, w.x, RD, s);
     // --- FFN
     Y_TRY(gemm(m, ln_in(w.x, Lw.ln_f_w, Lw.ln_f_b, nullptr), d, 0, Lw.W_ffn_in, 0, w.ig, 8 * d, 0,

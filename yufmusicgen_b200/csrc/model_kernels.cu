@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(128)
     layernorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ w,
                          const float* __restrict__ b, const float* __restrict__ gate,
                          OUT* __restrict__ out, int rows, int d) {
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const int d4 = d >> 2;
@@ -121,6 +121,70 @@ __global__ void __launch_bounds__(128)
 // out layout [6][rows][d] in the order r, k, v, w, a, g (the order the batched
 // projections consume).  The caller copies the new `prev` (xt of each
 // sequence's last token, model.py:197) after this kernel, so `prev` is only read.
+// One token per sequence (decode): the TimeMix layer norm, the six lerps and the
+// token-shift update fused.  One warp per row, the row in registers (VPL float4
+// per lane): xt = LN(x) is written for the caller, prev is read and then
+// overwritten with xt by the same lane, the six mixes go to out [6][B][d].
+template <typename OUT, int VPL>
+__global__ void __launch_bounds__(128)
+    ln_mix_step_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                       const float* __restrict__ b, float* __restrict__ xt, float* prev,
+                       const float* __restrict__ mix, OUT* __restrict__ out, int B, int d) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= B) return;
+  const int d4 = d >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * d);
+  float4 v[VPL];
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    const int i = lane + 32 * u;
+    v[u] = i < d4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[u].x + v[u].y) + (v[u].z + v[u].w);
+  }
+  const float mean = warp_sum(s) / d;
+  float q = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    if (lane + 32 * u < d4) {
+      const float cx = v[u].x - mean, cy = v[u].y - mean, cz = v[u].z - mean, cw = v[u].w - mean;
+      q = fmaf(cx, cx, fmaf(cy, cy, fmaf(cz, cz, fmaf(cw, cw, q))));
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / d + 1e-5f);
+  const size_t total = (size_t)B * d;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  float4* p4 = reinterpret_cast<float4*>(prev + (size_t)row * d);
+  float4* t4 = reinterpret_cast<float4*>(xt + (size_t)row * d);
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    const int i = lane + 32 * u;
+    if (i < d4) {
+      const float4 ww = w4[i], bb = b4[i], pv = p4[i];
+      const float o[4] = {(v[u].x - mean) * rstd * ww.x + bb.x, (v[u].y - mean) * rstd * ww.y + bb.y,
+                          (v[u].z - mean) * rstd * ww.z + bb.z, (v[u].w - mean) * rstd * ww.w + bb.w};
+      const float pp[4] = {pv.x, pv.y, pv.z, pv.w};
+      t4[i] = make_float4(o[0], o[1], o[2], o[3]);
+      p4[i] = make_float4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = 4 * i + e;
+        const size_t oi = (size_t)row * d + c;
+        const float delta = o[e] - pp[e];
+        // mix rows in the reference order r, w, k, v, a, g; outputs in r, k, v, w, a, g
+        store_out(out, 0 * total + oi, o[e] + delta * mix[0 * d + c]);
+        store_out(out, 3 * total + oi, o[e] + delta * mix[1 * d + c]);
+        store_out(out, 1 * total + oi, o[e] + delta * mix[2 * d + c]);
+        store_out(out, 2 * total + oi, o[e] + delta * mix[3 * d + c]);
+        store_out(out, 4 * total + oi, o[e] + delta * mix[4 * d + c]);
+        store_out(out, 5 * total + oi, o[e] + delta * mix[5 * d + c]);
+      }
+    }
+  }
+}
+
 template <typename OUT>
 __global__ void mix_kernel(const float* __restrict__ xt, const float* __restrict__ prev,
                            const float* __restrict__ mix, OUT* __restrict__ out, int B, int T, int d) {
@@ -145,11 +209,14 @@ __global__ void mix_kernel(const float* __restrict__ xt, const float* __restrict
   }
 }
 
+// out[i] = tanh(x[i]) for i < n_tanh, x[i] for n_tanh <= i < n (the tail is
+// only a copy: the bf16 path converts the other low-rank branches in the same pass).
 template <typename OUT>
-__global__ void tanh_kernel(const float* __restrict__ x, OUT* __restrict__ out, size_t n) {
+__global__ void tanh_kernel(const float* __restrict__ x, OUT* __restrict__ out, size_t n_tanh,
+                            size_t n) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
-    store_out(out, i, tanhf(x[i]));
+    store_out(out, i, i < n_tanh ? tanhf(x[i]) : x[i]);
 }
 
 // w/a/g activations, kk normalisation and key adjustment (model.py:108-122).
@@ -243,12 +310,17 @@ void launch_embed(const int32_t* ids, const float* E, float* x, int rows, int d,
 template <typename OUT>
 void launch_layernorm(const float* x, const float* w, const float* b, const float* gate, OUT* out,
                       int rows, int d, cudaStream_t s) {
-  const int blocks4 = (rows + 3) / 4;
+  // one row per warp; four warps per block unless that leaves SMs idle
+  // (small decode batches), then one
+  const int wpb = rows >= 4 * 148 ? 4 : 1;
+  const int blocks = (rows + wpb - 1) / wpb;
   if (d % 4 == 0 && d <= 8 * 128) {  // row in registers (d <= 1024)
     const int vpl = (d / 4 + 31) / 32;
     switch (vpl) {
-#define CASE(V) \
-  case V: layernorm_reg_kernel<OUT, V><<<blocks4, 128, 0, s>>>(x, w, b, gate, out, rows, d); return;
+#define CASE(V)                                                                                  \
+  case V:                                                                                        \
+    layernorm_reg_kernel<OUT, V><<<blocks, 32 * wpb, 0, s>>>(x, w, b, gate, out, rows, d); \
+    return;
       CASE(1) CASE(2) CASE(3) CASE(4) CASE(5) CASE(6) CASE(7) CASE(8)
 #undef CASE
       default: break;
@@ -258,13 +330,29 @@ void launch_layernorm(const float* x, const float* w, const float* b, const floa
   layernorm_kernel<OUT><<<(rows + warps - 1) / warps, 32 * warps, 0, s>>>(x, w, b, gate, out, rows, d);
 }
 template <typename OUT>
+bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* xt, float* prev,
+                        const float* mix, OUT* out, int B, int d, cudaStream_t s) {
+  if (d % 4 != 0 || d > 8 * 128) return false;
+  const int wpb = B >= 4 * 148 ? 4 : 1;
+  const int blocks = (B + wpb - 1) / wpb;
+  switch ((d / 4 + 31) / 32) {
+#define CASE(V)                                                                                 \
+  case V:                                                                                       \
+    ln_mix_step_kernel<OUT, V><<<blocks, 32 * wpb, 0, s>>>(x, w, b, xt, prev, mix, out, B, d); \
+    return true;
+    CASE(1) CASE(2) CASE(3) CASE(4) CASE(5) CASE(6) CASE(7) CASE(8)
+#undef CASE
+    default: return false;
+  }
+}
+template <typename OUT>
 void launch_mix(const float* xt, const float* prev, const float* mix, OUT* out, int B, int T, int d,
                 cudaStream_t s) {
   mix_kernel<OUT><<<grid_for((size_t)B * T * d, 256), 256, 0, s>>>(xt, prev, mix, out, B, T, d);
 }
 template <typename OUT>
-void launch_tanh(const float* x, OUT* out, size_t n, cudaStream_t s) {
-  tanh_kernel<OUT><<<grid_for(n, 256), 256, 0, s>>>(x, out, n);
+void launch_tanh(const float* x, OUT* out, size_t n_tanh, size_t n, cudaStream_t s) {
+  tanh_kernel<OUT><<<grid_for(n, 256), 256, 0, s>>>(x, out, n_tanh, n);
 }
 void launch_timemix_post(const float* k, const float* lw, const float* la, const float* lg,
                          const float* w0, const float* a0, const float* k_k, const float* k_a,
@@ -287,12 +375,17 @@ template void launch_layernorm<float>(const float*, const float*, const float*, 
                                       int, int, cudaStream_t);
 template void launch_layernorm<__nv_bfloat16>(const float*, const float*, const float*, const float*,
                                               __nv_bfloat16*, int, int, cudaStream_t);
+template bool launch_ln_mix_step<float>(const float*, const float*, const float*, float*, float*,
+                                         const float*, float*, int, int, cudaStream_t);
+template bool launch_ln_mix_step<__nv_bfloat16>(const float*, const float*, const float*, float*,
+                                                float*, const float*, __nv_bfloat16*, int, int,
+                                                cudaStream_t);
 template void launch_mix<float>(const float*, const float*, const float*, float*, int, int, int,
                                 cudaStream_t);
 template void launch_mix<__nv_bfloat16>(const float*, const float*, const float*, __nv_bfloat16*,
                                         int, int, int, cudaStream_t);
-template void launch_tanh<float>(const float*, float*, size_t, cudaStream_t);
-template void launch_tanh<__nv_bfloat16>(const float*, __nv_bfloat16*, size_t, cudaStream_t);
+template void launch_tanh<float>(const float*, float*, size_t, size_t, cudaStream_t);
+template void launch_tanh<__nv_bfloat16>(const float*, __nv_bfloat16*, size_t, size_t, cudaStream_t);
 template void launch_silu_mul<float>(const float*, float*, int, int, cudaStream_t);
 template void launch_silu_mul<__nv_bfloat16>(const float*, __nv_bfloat16*, int, int, cudaStream_t);
 

@@ -15,8 +15,14 @@ void launch_layernorm(const float* x, const float* w, const float* b, const floa
 template <typename OUT>
 void launch_mix(const float* xt, const float* prev, const float* mix, OUT* out, int B, int T, int d,
                 cudaStream_t s);
+// one token per sequence: layer norm + six lerps + prev := xt in one launch;
+// false (nothing launched) when d is not a multiple of 4 or above 1024
 template <typename OUT>
-void launch_tanh(const float* x, OUT* out, size_t n, cudaStream_t s);
+bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* xt, float* prev,
+                        const float* mix, OUT* out, int B, int d, cudaStream_t s);
+// tanh of the first n_tanh elements, plain copy (conversion) of the rest up to n
+template <typename OUT>
+void launch_tanh(const float* x, OUT* out, size_t n_tanh, size_t n, cudaStream_t s);
 void launch_timemix_post(const float* k, const float* lw, const float* la, const float* lg,
                          const float* w0, const float* a0, const float* k_k, const float* k_a,
                          float* w_raw, float* k_adj, float* a_op, float* b_op, float* g, int rows,
@@ -38,7 +44,7 @@ yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const f
                                   const float* bias_c, const float* bias_w, const float* bias_g,
                                   int ld, const float* decay_raw, const float* dir_raw,
                                   const float* m0, float* read, float* m_out, int B, int T, int R,
-                                  float* scratch, cudaStream_t stream);
+                                  float* scratch, __nv_bfloat16* read_bf, cudaStream_t stream);
 // floats of scratch the time-parallel ROSA scan needs (0 if it does not apply)
 size_t rosa_parallel_scratch_floats(int B, int T, int R);
 bool rosa_parallel_applies(int B, int T, int R);

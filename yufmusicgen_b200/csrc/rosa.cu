@@ -24,6 +24,7 @@
 // one is processed.
 
 #include "common.cuh"
+#include "model_kernels.cuh"
 
 namespace yuf {
 
@@ -213,6 +214,57 @@ __global__ void __launch_bounds__(MAXT)
   if (act && m_out != nullptr) m_out[(size_t)bb * R + j] = m;
 }
 
+// One token (decode): per sequence two block reductions instead of the chunk
+// machinery (16 Toeplitz lags, their inverse and a 17-wide reduction):
+//   p = d . m,  m' = D (m - 2 p d) + u,  read = (m' - 2 (d . m') d) [* sigmoid(gate)].
+// With raw parameters (engine) d = householder / ||householder|| and the norm
+// is folded into the first reduction.  read_bf (optional) receives a bf16 copy
+// of read, the next projection's GEMM operand.
+template <bool GATED>
+__global__ void __launch_bounds__(1024)
+    rosa_step_kernel(const float* __restrict__ cand, const float* __restrict__ write,
+                     const float* __restrict__ gate, const float* __restrict__ decay,
+                     const float* __restrict__ dir, const float* m0, float* __restrict__ read,
+                     float* m_out, int R, int ld, const float* __restrict__ bias_c,
+                     const float* __restrict__ bias_w, const float* __restrict__ bias_g,
+                     int raw_params, __nv_bfloat16* __restrict__ read_bf) {
+  __shared__ float scratch[32 * 2];
+  __shared__ float red[2];
+  const int bb = blockIdx.x, j = threadIdx.x, nwarps = blockDim.x >> 5;
+  const bool act = j < R;
+  float d = act ? dir[j] : 0.f;
+  float dec = act ? decay[j] : 0.f;
+  if (raw_params) dec = act ? 1.f / (1.f + expf(-dec)) : 0.f;
+  const float m = act ? (m0 ? m0[(size_t)bb * R + j] : 0.f) : 0.f;
+  {
+    float x2[2] = {d * d, d * m};
+    block_sum_array<2>(x2, scratch, red, nwarps);
+  }
+  float p = red[1];
+  if (raw_params) {
+    const float inv = 1.f / fmaxf(sqrtf(red[0]), 1e-12f);
+    d *= inv;
+    p *= inv;
+  }
+  const size_t io = (size_t)bb * ld + j;
+  const float bc = (act && bias_c) ? bias_c[j] : 0.f;
+  const float bw = (act && bias_w) ? bias_w[j] : 0.f;
+  const float u = act ? sigmoidf_fast(write[io] + bw) * tanhf(cand[io] + bc) : 0.f;
+  const float mn = act ? fmaf(dec, fmaf(-2.f * p, d, m), u) : 0.f;
+  __syncthreads();  // red / scratch are reused
+  {
+    float x1[1] = {d * mn};
+    block_sum_array<1>(x1, scratch, red, nwarps);
+  }
+  if (act) {
+    float rd = fmaf(-2.f * red[0], d, mn);
+    if (GATED) rd *= sigmoidf_fast(gate[io] + ((bias_g) ? bias_g[j] : 0.f));
+    read[(size_t)bb * R + j] = rd;
+    if (read_bf) read_bf[(size_t)bb * R + j] = __float2bfloat16_rn(rd);
+    if (m_out) m_out[(size_t)bb * R + j] = mn;
+  }
+}
+
 template <bool GATED, bool COMPAT>
 static yuf_status_t launch_rosa(const float* cand, const float* write, const float* gate,
                                 const float* decay, const float* dir, const float* m0, float* read,
@@ -264,11 +316,39 @@ yuf_status_t rosa_compat_dispatch(const float* cand, const float* write, const f
                                   ms, B, T, R, stream);
 }
 
+static yuf_status_t rosa_engine_scan(const float* cand, const float* write, const float* gate,
+                                     const float* bias_c, const float* bias_w, const float* bias_g,
+                                     int ld, const float* decay_raw, const float* dir_raw,
+                                     const float* m0, float* read, float* m_out, int B, int T, int R,
+                                     float* scratch, cudaStream_t stream);
+
 yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const float* gate,
                                   const float* bias_c, const float* bias_w, const float* bias_g,
                                   int ld, const float* decay_raw, const float* dir_raw,
                                   const float* m0, float* read, float* m_out, int B, int T, int R,
-                                  float* scratch, cudaStream_t stream) {
+                                  float* scratch, __nv_bfloat16* read_bf, cudaStream_t stream) {
+  if (T == 1 && R <= 1024) {
+    rosa_step_kernel<true><<<B, ((R + 31) / 32) * 32, 0, stream>>>(
+        cand, write, gate, decay_raw, dir_raw, m0, read, m_out, R, ld, bias_c, bias_w, bias_g, 1,
+        read_bf);
+    return check_launch("rosa_step_kernel");
+  }
+  yuf_status_t st = rosa_engine_scan(cand, write, gate, bias_c, bias_w, bias_g, ld, decay_raw, dir_raw,
+                                     m0, read, m_out, B, T, R, scratch, stream);
+  if (st == YUF_OK && read_bf) {
+    launch_to_bf16(read, read_bf, (size_t)B * T * R, stream);
+    return check_launch("to_bf16_kernel");
+  }
+  return st;
+}
+
+// The engine's multi-token scan: time-parallel when it applies, else one CTA
+// per sequence.
+static yuf_status_t rosa_engine_scan(const float* cand, const float* write, const float* gate,
+                                     const float* bias_c, const float* bias_w, const float* bias_g,
+                                     int ld, const float* decay_raw, const float* dir_raw,
+                                     const float* m0, float* read, float* m_out, int B, int T, int R,
+                                     float* scratch, cudaStream_t stream) {
   if (scratch && rosa_parallel_applies(B, T, R))
     return rosa_parallel(cand, write, gate, bias_c, bias_w, bias_g, ld, decay_raw, dir_raw, 1, m0,
                          read, m_out, B, T, R, true, scratch, stream);

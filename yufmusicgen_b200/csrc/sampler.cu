@@ -6,8 +6,8 @@
 // whose mass reaches top_p, and draw with torch.multinomial -- one device->host
 // sync per token.  Here one CTA per sequence does the same on the GPU:
 //   1. masked, temperature-scaled logits of the row go to shared memory;
-//   2. the top_k largest are extracted in descending order by top_k rounds of a
-//      block-wide argmax (ties -> the smaller id);
+//   2. the top_k largest, in descending order with ties to the smaller id (a
+//      radix select for the k-th largest, then a rank sort of the k);
 //   3. softmax over those k, then the top-p cut inside them (a token is dropped
 //      when the mass before it already exceeds top_p, generate.py:52), then an
 //      inverse-CDF draw with a uniform from Philox4x32-10.
@@ -52,6 +52,18 @@ YUF_DEVICE float philox_uniform(uint64_t seed, uint64_t step, uint32_t seq) {
 constexpr int SAMPLER_THREADS = 512;
 constexpr int SAMPLER_MAX_K = 1024;
 
+// Order-preserving map float -> uint32 (larger float, larger key); -0 is
+// canonicalised to +0 by the caller so equal floats have equal keys.
+YUF_DEVICE uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Step 2 above as a radix select instead of top_k argmax rounds: four 8-bit
+// histogram passes (most significant digit first) find the key of the k-th
+// largest logit; every logit above it is a candidate, and of those equal to it
+// the smallest ids fill the remaining places (the same set, and after the rank
+// sort the same order, as descending extraction with ties to the smaller id).
 __global__ void __launch_bounds__(SAMPLER_THREADS)
     sample_kernel(const float* __restrict__ logits, int V, float inv_temp, int top_k, float top_p,
                   uint64_t seed, uint64_t step, int seq0, int mask_below, int eos_id, int allow_eos,
@@ -59,16 +71,22 @@ __global__ void __launch_bounds__(SAMPLER_THREADS)
   extern __shared__ float srow[];                 // [V] masked scaled logits
   __shared__ float top_v[SAMPLER_MAX_K];
   __shared__ int top_i[SAMPLER_MAX_K];
-  __shared__ float red_v[SAMPLER_THREADS / 32];
-  __shared__ int red_i[SAMPLER_THREADS / 32];
+  __shared__ float cand_v[SAMPLER_MAX_K];
+  __shared__ int cand_i[SAMPLER_MAX_K];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t sel[3];
+  __shared__ int wsum[SAMPLER_THREADS / 32];
+  __shared__ int n_above;
   const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const float* row = logits + (size_t)b * V;
   for (int i = tid; i < V; i += SAMPLER_THREADS) {
     const bool allowed = i >= mask_below || (allow_eos && i == eos_id);
-    srow[i] = allowed ? row[i] * inv_temp : -FLT_MAX;
+    srow[i] = allowed ? row[i] * inv_temp + 0.f : -FLT_MAX;
   }
-  __syncthreads();
-  for (int r = 0; r < top_k; ++r) {
+  if (tid == 0) n_above = 0;
+  if (top_k == 1) {
+    // greedy: one block-wide argmax (ties -> the smaller id)
+    __syncthreads();
     float bv = -FLT_MAX;
     int bi = 0x7fffffff;
     for (int i = tid; i < V; i += SAMPLER_THREADS) {
@@ -81,17 +99,114 @@ __global__ void __launch_bounds__(SAMPLER_THREADS)
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
-    if (lane == 0) { red_v[wid] = bv; red_i[wid] = bi; }
+    if (lane == 0) { cand_v[wid] = bv; cand_i[wid] = bi; }
     __syncthreads();
     if (tid == 0) {
       for (int q = 1; q < SAMPLER_THREADS / 32; ++q)
-        if (red_v[q] > bv || (red_v[q] == bv && red_i[q] < bi)) { bv = red_v[q]; bi = red_i[q]; }
-      top_v[r] = bv;
-      top_i[r] = bi;
-      if (bi >= 0 && bi < V) srow[bi] = -INFINITY;  // taken: never picked again
+        if (cand_v[q] > bv || (cand_v[q] == bv && cand_i[q] < bi)) { bv = cand_v[q]; bi = cand_i[q]; }
+      out_ids[b] = bi;
+      if (out_u) out_u[b] = philox_uniform(seed, step, (uint32_t)(seq0 + b));
+    }
+    return;
+  }
+  // radix select: after the passes, `prefix` is the k-th largest key and `need`
+  // the number of logits equal to it that belong to the top k
+  uint32_t prefix = 0, pmask = 0, need = (uint32_t)top_k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += SAMPLER_THREADS) hist[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < V; i += SAMPLER_THREADS) {
+      const uint32_t key = order_key(srow[i]);
+      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
     }
     __syncthreads();
+    if (wid == 0) {
+      // lane l owns bins 255-8l .. 248-8l (descending); find the bin where the
+      // count from the top reaches `need`
+      uint32_t c[8], tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[255 - 8 * lane - j];
+        tot += c[j];
+      }
+      uint32_t inc = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+      }
+      uint32_t acc = inc - tot;
+      if (acc < need && need <= inc) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (acc < need && need <= acc + c[j]) {
+            sel[0] = prefix | ((uint32_t)(255 - 8 * lane - j) << shift);
+            sel[1] = need - acc;
+            sel[2] = c[j];  // logits in the chosen bin
+          }
+          acc += c[j];
+        }
+      }
+    }
+    __syncthreads();
+    prefix = sel[0];
+    need = sel[1];
+    pmask |= 255u << shift;
   }
+  const uint32_t thr = prefix;
+  const int n_gt = top_k - (int)need;
+  // all logits equal to the threshold are taken (the usual case): they are
+  // gathered with those above it, the rank sort orders them by id
+  const bool take_all_eq = sel[2] == need;
+  // candidates above the threshold (any order; ranked below)
+  for (int i = tid; i < V; i += SAMPLER_THREADS) {
+    const float x = srow[i];
+    const uint32_t key = order_key(x);
+    if (key > thr || (take_all_eq && key == thr)) {
+      const int slot = atomicAdd(&n_above, 1);
+      cand_v[slot] = x;
+      cand_i[slot] = i;
+    }
+  }
+  // otherwise the logits equal to the threshold, smallest ids first: contiguous
+  // id ranges per thread and a block-wide exclusive scan of their counts
+  if (!take_all_eq) {
+    const int per = (V + SAMPLER_THREADS - 1) / SAMPLER_THREADS;
+    const int lo = min(V, tid * per), hi = min(V, lo + per);
+    int cnt = 0;
+    for (int i = lo; i < hi; ++i) cnt += order_key(srow[i]) == thr;
+    int inc = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    if (lane == 31) wsum[wid] = inc;
+    __syncthreads();
+    int rank = inc - cnt;
+    for (int q = 0; q < wid; ++q) rank += wsum[q];
+    for (int i = lo; i < hi && rank < (int)need; ++i) {
+      if (order_key(srow[i]) == thr) {
+        cand_v[n_gt + rank] = srow[i];
+        cand_i[n_gt + rank] = i;
+        ++rank;
+      }
+    }
+  }
+  __syncthreads();
+  // rank sort: value descending, ties by the smaller id
+  for (int t = tid; t < top_k; t += SAMPLER_THREADS) {
+    const float v = cand_v[t];
+    const int id = cand_i[t];
+    int r = 0;
+    for (int q = 0; q < top_k; ++q) {
+      const float w = cand_v[q];
+      r += (w > v) || (w == v && cand_i[q] < id);
+    }
+    top_v[r] = v;
+    top_i[r] = id;
+  }
+  __syncthreads();
   if (tid == 0) {
     const float u = philox_uniform(seed, step, (uint32_t)(seq0 + b));
     int pick = top_i[0];
