@@ -20,6 +20,32 @@ YUF_DEVICE float warp_sum(float v) {
 
 YUF_DEVICE void store_out(float* p, size_t i, float v) { p[i] = v; }
 YUF_DEVICE void store_out(__nv_bfloat16* p, size_t i, float v) { p[i] = __float2bfloat16_rn(v); }
+// four consecutive elements, i a multiple of 4 (one 16- or 8-byte store)
+YUF_DEVICE void store4(float* p, size_t i, float4 v) { *reinterpret_cast<float4*>(p + i) = v; }
+YUF_DEVICE void store4(__nv_bfloat16* p, size_t i, float4 v) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&lo);
+  u.y = *reinterpret_cast<const uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(p + i) = u;
+}
+YUF_DEVICE float4 f4_lerp(float4 x, float4 delta, float4 m) {
+  return make_float4(fmaf(delta.x, m.x, x.x), fmaf(delta.y, m.y, x.y), fmaf(delta.z, m.z, x.z),
+                     fmaf(delta.w, m.w, x.w));
+}
+
+// Sum over the block; every thread gets the total.  red: 32 floats of shared
+// memory, reusable by the next call.
+YUF_DEVICE float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();  // the previous call's readers are done with red
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int q = 0; q < nw; ++q) t += red[q];
+  return t;
+}
 
 // x[row, :] = E[ids[row], :]  (nn.Embedding, model.py:411)
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ E,
@@ -107,11 +133,7 @@ __global__ void __launch_bounds__(128)
         const float4 gg = g4[i];
         o.x *= gg.x; o.y *= gg.y; o.z *= gg.z; o.w *= gg.w;
       }
-      const size_t base = (size_t)row * d + 4 * i;
-      store_out(out, base + 0, o.x);
-      store_out(out, base + 1, o.y);
-      store_out(out, base + 2, o.z);
-      store_out(out, base + 3, o.w);
+      store4(out, (size_t)row * d + 4 * i, o);
     }
   }
 }
@@ -121,6 +143,51 @@ __global__ void __launch_bounds__(128)
 // out layout [6][rows][d] in the order r, k, v, w, a, g (the order the batched
 // projections consume).  The caller copies the new `prev` (xt of each
 // sequence's last token, model.py:197) after this kernel, so `prev` is only read.
+// Small row counts (decode batches): one CTA per row, one float4 per thread
+// (d <= 4096), so a batch of a few hundred rows covers every SM and each thread
+// has a single load in its dependency chain.  MIX: the TimeMix variant of
+// ln_mix_step_kernel (xt written, prev read then replaced by xt, six lerps to
+// out [6][rows][d]); otherwise LayerNorm, optional gate multiply, out [rows][d].
+template <typename OUT, bool MIX>
+__global__ void __launch_bounds__(1024)
+    ln_row_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                  const float* __restrict__ b, const float* __restrict__ gate, OUT* __restrict__ out,
+                  int rows, int d, float* __restrict__ xt, float* prev, const float* __restrict__ mix) {
+  __shared__ float red[32];
+  const int row = blockIdx.x, i = threadIdx.x, d4 = d >> 2;
+  const bool act = i < d4;
+  const size_t base = (size_t)row * d + 4 * (size_t)i;
+  const float4 v = act ? *reinterpret_cast<const float4*>(x + base) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 pv = make_float4(0.f, 0.f, 0.f, 0.f), gv = make_float4(1.f, 1.f, 1.f, 1.f);
+  if (act && MIX) pv = *reinterpret_cast<const float4*>(prev + base);
+  if (act && !MIX && gate) gv = *reinterpret_cast<const float4*>(gate + base);
+  const float mean = block_sum((v.x + v.y) + (v.z + v.w), red) / d;
+  const float cx = v.x - mean, cy = v.y - mean, cz = v.z - mean, cw = v.w - mean;
+  const float q = act ? fmaf(cx, cx, fmaf(cy, cy, fmaf(cz, cz, cw * cw))) : 0.f;
+  const float rstd = rsqrtf(block_sum(q, red) / d + 1e-5f);
+  if (!act) return;
+  const float4 ww = reinterpret_cast<const float4*>(w)[i], bb = reinterpret_cast<const float4*>(b)[i];
+  float4 o = make_float4(cx * rstd * ww.x + bb.x, cy * rstd * ww.y + bb.y, cz * rstd * ww.z + bb.z,
+                         cw * rstd * ww.w + bb.w);
+  if constexpr (MIX) {
+    *reinterpret_cast<float4*>(xt + base) = o;
+    *reinterpret_cast<float4*>(prev + base) = o;
+    const float4 delta = make_float4(o.x - pv.x, o.y - pv.y, o.z - pv.z, o.w - pv.w);
+    const size_t total = (size_t)rows * d;
+    const float4* m4 = reinterpret_cast<const float4*>(mix);
+    // mix rows in the reference order r, w, k, v, a, g; outputs in r, k, v, w, a, g
+    store4(out, 0 * total + base, f4_lerp(o, delta, m4[0 * d4 + i]));
+    store4(out, 3 * total + base, f4_lerp(o, delta, m4[1 * d4 + i]));
+    store4(out, 1 * total + base, f4_lerp(o, delta, m4[2 * d4 + i]));
+    store4(out, 2 * total + base, f4_lerp(o, delta, m4[3 * d4 + i]));
+    store4(out, 4 * total + base, f4_lerp(o, delta, m4[4 * d4 + i]));
+    store4(out, 5 * total + base, f4_lerp(o, delta, m4[5 * d4 + i]));
+  } else {
+    o = make_float4(o.x * gv.x, o.y * gv.y, o.z * gv.z, o.w * gv.w);
+    store4(out, base, o);
+  }
+}
+
 // One token per sequence (decode): the TimeMix layer norm, the six lerps and the
 // token-shift update fused.  One warp per row, the row in registers (VPL float4
 // per lane): xt = LN(x) is written for the caller, prev is read and then
@@ -158,29 +225,26 @@ __global__ void __launch_bounds__(128)
   const float4* b4 = reinterpret_cast<const float4*>(b);
   float4* p4 = reinterpret_cast<float4*>(prev + (size_t)row * d);
   float4* t4 = reinterpret_cast<float4*>(xt + (size_t)row * d);
+  const float4* m4 = reinterpret_cast<const float4*>(mix);
 #pragma unroll
   for (int u = 0; u < VPL; ++u) {
     const int i = lane + 32 * u;
     if (i < d4) {
       const float4 ww = w4[i], bb = b4[i], pv = p4[i];
-      const float o[4] = {(v[u].x - mean) * rstd * ww.x + bb.x, (v[u].y - mean) * rstd * ww.y + bb.y,
-                          (v[u].z - mean) * rstd * ww.z + bb.z, (v[u].w - mean) * rstd * ww.w + bb.w};
-      const float pp[4] = {pv.x, pv.y, pv.z, pv.w};
-      t4[i] = make_float4(o[0], o[1], o[2], o[3]);
-      p4[i] = make_float4(o[0], o[1], o[2], o[3]);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int c = 4 * i + e;
-        const size_t oi = (size_t)row * d + c;
-        const float delta = o[e] - pp[e];
-        // mix rows in the reference order r, w, k, v, a, g; outputs in r, k, v, w, a, g
-        store_out(out, 0 * total + oi, o[e] + delta * mix[0 * d + c]);
-        store_out(out, 3 * total + oi, o[e] + delta * mix[1 * d + c]);
-        store_out(out, 1 * total + oi, o[e] + delta * mix[2 * d + c]);
-        store_out(out, 2 * total + oi, o[e] + delta * mix[3 * d + c]);
-        store_out(out, 4 * total + oi, o[e] + delta * mix[4 * d + c]);
-        store_out(out, 5 * total + oi, o[e] + delta * mix[5 * d + c]);
-      }
+      const float4 o = make_float4(
+          (v[u].x - mean) * rstd * ww.x + bb.x, (v[u].y - mean) * rstd * ww.y + bb.y,
+          (v[u].z - mean) * rstd * ww.z + bb.z, (v[u].w - mean) * rstd * ww.w + bb.w);
+      t4[i] = o;
+      p4[i] = o;
+      const float4 delta = make_float4(o.x - pv.x, o.y - pv.y, o.z - pv.z, o.w - pv.w);
+      const size_t oi = (size_t)row * d + 4 * i;
+      // mix rows in the reference order r, w, k, v, a, g; outputs in r, k, v, w, a, g
+      store4(out, 0 * total + oi, f4_lerp(o, delta, m4[0 * d4 + i]));
+      store4(out, 3 * total + oi, f4_lerp(o, delta, m4[1 * d4 + i]));
+      store4(out, 1 * total + oi, f4_lerp(o, delta, m4[2 * d4 + i]));
+      store4(out, 2 * total + oi, f4_lerp(o, delta, m4[3 * d4 + i]));
+      store4(out, 4 * total + oi, f4_lerp(o, delta, m4[4 * d4 + i]));
+      store4(out, 5 * total + oi, f4_lerp(o, delta, m4[5 * d4 + i]));
     }
   }
 }
@@ -310,9 +374,13 @@ void launch_embed(const int32_t* ids, const float* E, float* x, int rows, int d,
 template <typename OUT>
 void launch_layernorm(const float* x, const float* w, const float* b, const float* gate, OUT* out,
                       int rows, int d, cudaStream_t s) {
-  // one row per warp; four warps per block unless that leaves SMs idle
-  // (small decode batches), then one
-  const int wpb = rows >= 4 * 148 ? 4 : 1;
+  if (rows < 4 * 148 && d % 4 == 0 && d <= 4096) {  // small batch: one CTA per row
+    ln_row_kernel<OUT, false><<<rows, ((d / 4 + 31) / 32) * 32, 0, s>>>(x, w, b, gate, out, rows, d,
+                                                                         nullptr, nullptr, nullptr);
+    return;
+  }
+  // one row per warp, four warps per block
+  const int wpb = 4;
   const int blocks = (rows + wpb - 1) / wpb;
   if (d % 4 == 0 && d <= 8 * 128) {  // row in registers (d <= 1024)
     const int vpl = (d / 4 + 31) / 32;
@@ -332,8 +400,14 @@ void launch_layernorm(const float* x, const float* w, const float* b, const floa
 template <typename OUT>
 bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* xt, float* prev,
                         const float* mix, OUT* out, int B, int d, cudaStream_t s) {
-  if (d % 4 != 0 || d > 8 * 128) return false;
-  const int wpb = B >= 4 * 148 ? 4 : 1;
+  if (d % 4 != 0) return false;
+  if (B < 4 * 148 && d <= 4096) {
+    ln_row_kernel<OUT, true><<<B, ((d / 4 + 31) / 32) * 32, 0, s>>>(x, w, b, nullptr, out, B, d, xt,
+                                                                     prev, mix);
+    return true;
+  }
+  if (d > 8 * 128) return false;
+  const int wpb = 4;
   const int blocks = (B + wpb - 1) / wpb;
   switch ((d / 4 + 31) / 32) {
 #define CASE(V)                                                                                 \
