@@ -263,6 +263,30 @@ def test_time_parallel_waits_never_expired():
     assert _lib.wait_timeouts() == 0
 
 
+@pytest.mark.parametrize("B,H,N", [(512, 16, 40), (128, 16, 64), (32, 16, 128), (64, 8, 96)])
+def test_wkv7_decode_many_heads_per_cta(B, H, N):
+    """Single-token steps with more heads than the decode ring's slots per CTA
+    (the slot refill path), in place, then the same step with the state at an
+    8-byte offset (the register-prefetch kernel); no bounded wait may expire."""
+    from yufmusicgen_b200 import _lib
+    ins = wkv_op_inputs(B, 1, H, N, seed=B + N, with_state=True)
+    yr, sr = cref.wkv7_scan(*(ins[k] for k in "rwkvab"), ins["s0"])
+    t = [cu(ins[k]) for k in "rwkvab"]
+    st = cu(ins["s0"])
+    y, _ = cuda_ops.wkv7_forward(*t, state=st, state_out=st)
+    close(y, yr)
+    close(st, sr)
+    n = st.numel()
+    buf = torch.zeros(n + 2, device=DEV)
+    off = buf[2:].view_as(st)  # 8 bytes past a 16-byte boundary
+    off.copy_(cu(ins["s0"]))
+    y2, _ = cuda_ops.wkv7_forward(*t, state=off, state_out=off)
+    close(y2, yr)
+    close(off, sr)
+    torch.cuda.synchronize()
+    assert _lib.wait_timeouts() == 0
+
+
 def test_wkv7_time_parallel_full_config2_and_inplace_state():
     ins = wkv_op_inputs(8, 2048, 16, 40, seed=0, with_state=True)
     st = cu(ins["s0"])

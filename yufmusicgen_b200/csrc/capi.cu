@@ -64,6 +64,7 @@ void scratch_free(void* p, cudaStream_t st) {
 }
 
 unsigned int wkv7_pair_wait_timeouts();
+unsigned int wkv7_decode_wait_timeouts();
 yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
                            float* ckpt, float* sa, int B, int T, int H, int N, bool compat,
@@ -110,7 +111,10 @@ using namespace yuf;
 
 extern "C" {
 
-unsigned int yuf_wait_timeouts(void) { return yuf::wkv7_pair_wait_timeouts(); }
+unsigned int yuf_wait_timeouts(void) {
+  const unsigned int p = yuf::wkv7_pair_wait_timeouts(), d = yuf::wkv7_decode_wait_timeouts();
+  return (p == ~0u || d == ~0u) ? ~0u : p + d;
+}
 
 const char* yuf_status_string(yuf_status_t s) {
   switch (s) {

@@ -718,6 +718,10 @@ yuf_status_t yuf_model_set_decode_graphs(yuf_model* m, int enabled) {
   Y_REQUIRE(m, "null model");
   m->decode_graphs = enabled != 0;
   if (!m->decode_graphs) m->drop_graphs();
+  if (m->decode_graphs) {
+    Y_CUDA(cudaSetDevice(m->device));
+    wkv7_decode_prepare(m->N());
+  }
   return YUF_OK;
 }
 

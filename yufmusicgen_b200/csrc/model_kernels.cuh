@@ -35,6 +35,8 @@ yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
                            float* ckpt, float* sa, int B, int T, int H, int N, bool compat,
                            cudaStream_t stream);
+// one-time setup of the decode kernels for head size N (outside graph capture)
+void wkv7_decode_prepare(int N);
 yuf_status_t wkv7_decode_dispatch(const float* r, const float* w, const float* k, const float* v,
                                   const float* a, const float* b, const float* s0, float* y,
                                   float* s_out, int BH, int N, cudaStream_t stream);

@@ -15,6 +15,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "mbarrier.cuh"
 
 namespace yuf {
 
@@ -99,6 +100,154 @@ __global__ void __launch_bounds__(N * 4)
   }
 }
 
+// ---- bulk-copy (TMA) ring variant --------------------------------------------
+// Each CTA owns a ring of STAGES shared-memory slots, one head per slot: the
+// head's N x N state (N*N*4 contiguous bytes) and its six token vectors
+// (r, w, k, v, a, b: N*4 bytes each) arrive by 1-D bulk copies on the slot's
+// mbarrier; the CTA updates the state in shared memory and one thread writes it
+// back with a bulk store.  STAGES-1 heads are in flight while one is computed,
+// and the copies move whole contiguous blocks, so the kernel streams at close
+// to copy bandwidth instead of waiting on per-thread load latency.
+template <int N>
+struct DecRing {
+  static constexpr int STATE_BYTES = N * N * 4;
+  static constexpr int VEC_BYTES = N * 4;
+  static constexpr int SLOT = STATE_BYTES + 6 * VEC_BYTES;  // state, r, w, k, v, a, b
+  static constexpr int STAGES = SLOT * 4 <= 96 * 1024 ? 4 : (SLOT * 3 <= 128 * 1024 ? 3 : 2);
+  static constexpr int SMEM = STAGES * SLOT + N * 4 + STAGES * 8;  // slots, retention, barriers
+  static_assert(SLOT % 16 == 0 && VEC_BYTES % 16 == 0, "bulk copies need 16-byte multiples");
+};
+
+__device__ unsigned int g_decode_wait_timeouts;
+
+template <int N>
+__global__ void __launch_bounds__(N * 4)
+    wkv7_decode_ring_kernel(const float* __restrict__ r, const float* __restrict__ w,
+                            const float* __restrict__ k, const float* __restrict__ v,
+                            const float* __restrict__ a, const float* __restrict__ b,
+                            const float* s0, float* __restrict__ y, float* s_out, int BH) {
+  using K = DecRing<N>;
+  constexpr int G = 4, C = N / G, C2 = C / 2;
+  extern __shared__ __align__(128) unsigned char dsm[];
+  float* ret = reinterpret_cast<float*>(dsm + K::STAGES * K::SLOT);
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + K::STAGES * K::SLOT + N * 4);
+  const int tid = threadIdx.x;
+  const int row = tid / G, g = tid - row * G, j0 = g * C;
+  const int first = blockIdx.x, stride = gridDim.x;
+  const int nheads = first < BH ? (BH - 1 - first) / stride + 1 : 0;
+  if (nheads == 0) return;
+
+  const float* vsrc[6] = {r, w, k, v, a, b};
+  auto issue = [&](int j) {  // thread 0: head j of this CTA into slot j % STAGES
+    const int sl = j % K::STAGES;
+    const size_t bh = (size_t)first + (size_t)j * stride;
+    unsigned char* slot = dsm + sl * K::SLOT;
+    mbar_expect_tx(&full[sl], K::SLOT);
+    bulk_load(slot, s0 + bh * N * N, K::STATE_BYTES, &full[sl]);
+#pragma unroll
+    for (int q = 0; q < 6; ++q)
+      bulk_load(slot + K::STATE_BYTES + q * K::VEC_BYTES, vsrc[q] + bh * N, K::VEC_BYTES, &full[sl]);
+  };
+  if (tid == 0) {
+    for (int sl = 0; sl < K::STAGES; ++sl) mbar_init(&full[sl], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int issued = 0;  // thread 0: heads whose copies were started
+  if (tid == 0)
+    for (; issued < min(nheads, K::STAGES); ++issued) issue(issued);
+
+  for (int j = 0; j < nheads; ++j) {
+    const int sl = j % K::STAGES;
+    const bool ok = mbar_wait(&full[sl], (uint32_t)(j / K::STAGES) & 1u);
+    if (__syncthreads_or(!ok)) {  // a copy never landed: record it, leave together
+      if (tid == 0) {
+        atomicAdd(&g_decode_wait_timeouts, 1u);
+        bulk_wait_all();
+        // give the loads still in flight into this CTA's slots a bounded chance to land
+        for (int h = j; h < issued; ++h) mbar_wait(&full[h % K::STAGES], (uint32_t)(h / K::STAGES) & 1u);
+      }
+      return;
+    }
+    float* St = reinterpret_cast<float*>(dsm + sl * K::SLOT);
+    const float* vec = St + N * N;  // r, w, k, v, a, b
+    if (tid < N) ret[tid] = __expf(W_SCALE * sigmoidf_fast(vec[N + tid]));
+    __syncthreads();
+    const float* W_ = ret + j0;
+    const float* K_ = vec + 2 * N + j0;
+    const float* A_ = vec + 4 * N + j0;
+    const float* B_ = vec + 5 * N + j0;
+    const float* R_ = vec + j0;
+    const float vi = vec[3 * N + row];
+    float* Srow = St + row * N + j0;
+    float2 S[C2];
+#pragma unroll
+    for (int c = 0; c < C2; ++c) S[c] = *reinterpret_cast<const float2*>(Srow + 2 * c);
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < C2; ++c) acc = ffma2(S[c], *reinterpret_cast<const float2*>(A_ + 2 * c), acc);
+    const float sa = group_sum<G>(acc.x + acc.y);
+    float2 yacc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < C2; ++c) {
+      const float2 upd = ffma2(f2(sa), *reinterpret_cast<const float2*>(B_ + 2 * c),
+                               fmul2(f2(vi), *reinterpret_cast<const float2*>(K_ + 2 * c)));
+      S[c] = ffma2(S[c], *reinterpret_cast<const float2*>(W_ + 2 * c), upd);
+      yacc = ffma2(S[c], *reinterpret_cast<const float2*>(R_ + 2 * c), yacc);
+      *reinterpret_cast<float2*>(Srow + 2 * c) = S[c];
+    }
+    const float yv = group_sum<G>(yacc.x + yacc.y);
+    const size_t bh = (size_t)first + (size_t)j * stride;
+    if (g == 0) y[bh * N + row] = yv;
+    fence_proxy_async();  // the state writes above feed the bulk store below
+    __syncthreads();
+    if (tid == 0) {
+      bulk_store(s_out + bh * N * N, St, K::STATE_BYTES);
+      bulk_commit();
+      // refill the previous head's slot once its store has read it
+      if (j >= 1 && j - 1 + K::STAGES < nheads) {
+        bulk_wait_read<1>();
+        issue(issued++);
+      }
+    }
+  }
+  if (tid == 0) bulk_wait_all();
+}
+
+// Timeouts of the ring kernel's bounded waits since the last call; clears them.
+unsigned int wkv7_decode_wait_timeouts() {
+  unsigned int n = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&n, g_decode_wait_timeouts, sizeof(n)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_decode_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess) {
+    cudaGetLastError();
+    return ~0u;
+  }
+  return n;
+}
+
+// Resident ring CTAs per SM for head size N on the current device (0: the ring
+// cannot run); sets the kernel's shared-memory limit on first use per device.
+template <int N>
+static int ring_blocks_per_sm() {
+  static int cache[64];  // per device: blocks + 1, 0 = not yet known
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (cache[dev]) return cache[dev] - 1;
+  int v = 0;
+  if (cudaFuncSetAttribute(wkv7_decode_ring_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           DecRing<N>::SMEM) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, wkv7_decode_ring_kernel<N>, N * 4,
+                                                    DecRing<N>::SMEM) != cudaSuccess) {
+    cudaGetLastError();
+    v = 0;
+  }
+  cache[dev] = v + 1;
+  return v;
+}
+
 // Resident CTAs per SM of the decode kernel for head size N (cached).
 template <int N>
 static int decode_blocks_per_sm() {
@@ -123,15 +272,43 @@ static int sm_count() {
   return n;
 }
 
+// Set the ring kernel's shared-memory limit and cache its occupancy for head
+// size N; the engine calls this before capturing decode graphs.
+void wkv7_decode_prepare(int N) {
+  switch (N) {
+    case 16: ring_blocks_per_sm<16>(); break;
+    case 32: ring_blocks_per_sm<32>(); break;
+    case 40: ring_blocks_per_sm<40>(); break;
+    case 48: ring_blocks_per_sm<48>(); break;
+    case 64: ring_blocks_per_sm<64>(); break;
+    case 96: ring_blocks_per_sm<96>(); break;
+    case 128: ring_blocks_per_sm<128>(); break;
+    default: break;
+  }
+  sm_count();
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 // Grid: one resident wave of CTAs, each looping over heads bh, bh + grid, ...
-// with the next head's loads issued before the current head's arithmetic.
+// The bulk-copy ring when the buffers allow it, else the register-prefetch loop.
 yuf_status_t wkv7_decode_dispatch(const float* r, const float* w, const float* k, const float* v,
                                   const float* a, const float* b, const float* s0, float* y,
                                   float* s_out, int BH, int N, cudaStream_t stream) {
   if (BH <= 0) return YUF_OK;
+  // the ring needs a state to read and write, all on 16-byte boundaries
+  const bool ring = s0 && s_out && aligned16(s0) && aligned16(s_out) && aligned16(r) &&
+                    aligned16(w) && aligned16(k) && aligned16(v) && aligned16(a) && aligned16(b);
   switch (N) {
 #define CASE(NN)                                                                                 \
   case NN: {                                                                                     \
+    const int per_sm = ring ? ring_blocks_per_sm<NN>() : 0;                                      \
+    if (per_sm > 0) {                                                                            \
+      const int grid = std::min(BH, per_sm * sm_count());                                        \
+      wkv7_decode_ring_kernel<NN><<<grid, NN * 4, DecRing<NN>::SMEM, stream>>>(                  \
+          r, w, k, v, a, b, s0, y, s_out, BH);                                                   \
+      return check_launch("wkv7_decode_ring_kernel");                                            \
+    }                                                                                            \
     const int grid = std::min(BH, decode_blocks_per_sm<NN>() * sm_count());                     \
     wkv7_decode_kernel<NN><<<grid, NN * 4, 0, stream>>>(r, w, k, v, a, b, s0, y, s_out, BH);    \
     return check_launch("wkv7_decode_kernel");                                                   \

@@ -22,6 +22,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "mbarrier.cuh"
 
 namespace yuf {
 
@@ -37,51 +38,13 @@ struct PairTmaps {
 };
 
 __device__ unsigned int g_pair_wait_timeouts;
-constexpr unsigned long long WAIT_NS = 200ull * 1000 * 1000;  // 0.2 s
 
-YUF_DEVICE uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-YUF_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-YUF_DEVICE void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-YUF_DEVICE void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-YUF_DEVICE void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
 YUF_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
-YUF_DEVICE unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// true when the barrier's phase `parity` completed within WAIT_NS
-YUF_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const uint32_t a = smem_u32(bar);
-  unsigned long long t0 = 0;
-  for (unsigned int it = 0;; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((it & 63) == 0) {  // look at the clock every 64 polls
-      const unsigned long long now = global_ns();
-      if (it == 0) t0 = now;
-      else if (now - t0 > WAIT_NS) return false;
-    }
-  }
-}
-
 YUF_DEVICE size_t item_head_off(int bb, int hh, int K, int H, int N, int Tstride, int Cper) {
   return (((size_t)(bb / Cper) * Tstride + (size_t)(bb % Cper) * K) * H + hh) * N;
 }
