@@ -177,14 +177,43 @@ def measure_extras(dev, stream, args):
     Bd = 256
     di = wkv_op_inputs(Bd, 1, H, N, seed=1, with_state=True)
     dd = {k: torch.from_numpy(di[k]).to(dev) for k in "rwkvab"}
-    st = torch.from_numpy(di["s0"]).to(dev)
     yd = torch.empty_like(dd["r"])
-    ms = _time(lambda: cuda_ops.wkv7_forward(*(dd[k] for k in "rwkvab"), st, out=yd, state_out=st,
-                                             algo=cuda_ops.ALGO_SEQUENTIAL), n, dev, stream)
+    # eight in-place states (8 x 26 MB > L2), one CUDA graph of eight steps so the
+    # number is the kernel's, not the Python call's
+    sts = [torch.from_numpy(di["s0"]).to(dev) for _ in range(8)]
+
+    def dec_all():
+        for st in sts:
+            cuda_ops.wkv7_forward(*(dd[k] for k in "rwkvab"), st, out=yd, state_out=st,
+                                  algo=cuda_ops.ALGO_SEQUENTIAL)
+
+    def floor_all():  # an in-place float update of the same states: the streaming floor
+        for st in sts:
+            st.mul_(1.0)
+
+    def graph_ms(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        t = _time(g.replay, n, dev, stream) / len(sts)
+        del g
+        return t
+
+    ms = graph_ms(dec_all)
+    ms_floor = graph_ms(floor_all)
     dbytes = 2 * Bd * H * N * N * 4 + 7 * Bd * H * N * 4
     out["wkv7_decode_step_B256_H16_N40"] = {"ms": ms, "GBps": dbytes / ms / 1e6,
                                             "frac_of_hbm": dbytes / ms / 1e6 / peak,
+                                            "inplace_update_floor_ms": ms_floor,
+                                            "frac_of_inplace_floor": ms_floor / ms,
                                             "bytes": dbytes}
+    del sts
     # ROSA scan at the 0.1B model's shape (B2, T2048, R128), gated
     ri = rosa_op_inputs(2, T, 128, seed=2)
     keys = ("cand", "write", "read_gate", "decay", "direction", "m0")

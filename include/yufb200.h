@@ -119,6 +119,43 @@ yuf_status_t yuf_rosa_forward_compat(const float* cand, const float* write, cons
                                      float* gate_saved, float* decay_saved, float* mem_saved,
                                      int B, int T, int R, void* stream);
 
+/* Training backward of the WKV-7 op: the reference's
+ * torch.ops.yufmusicgen_rwkv7.backward (rwkv7_clampw.cpp:40-63 ->
+ * rwkv7_clampw.cu:83-176), same buffers.  Inputs r..b [B,T,H,N] as given to
+ * yuf_wkv7_forward_compat, dy [B,T,H,N] = dL/dy, and that call's `states`
+ * [B,H,T/16,N,N] (transposed checkpoints) and `sa` [B,T,H,N].  Writes the
+ * gradients dr, dw (w.r.t. the raw w, through the retention clamp), dk, dv,
+ * da, db, each [B,T,H,N], for a zero initial state with no gradient on the
+ * final state.  T % 16 == 0; every pointer 16-byte aligned.  Scratch of
+ * 16*N*N floats per (b,h) comes from the library's stream-ordered pool.  The
+ * result is the exact gradient (fp32): the states are replayed from the
+ * checkpoints, where the reference divides by the retention to step back. */
+yuf_status_t yuf_wkv7_backward(const float* r, const float* w, const float* k, const float* v,
+                               const float* a, const float* b, const float* dy,
+                               const float* states, const float* sa, float* dr, float* dw,
+                               float* dk, float* dv, float* da, float* db, int B, int T, int H,
+                               int N, void* stream);
+
+/* Training backward of the ROSA op: the reference's
+ * torch.ops.yufmusicgen_rosa.backward (rosa_householder.cpp:52-83 ->
+ * rosa_householder.cu:103-285), same buffers.  Reads the saved tensors of
+ * yuf_rosa_forward_compat (cand_saved, write_saved, decay_saved, mem_saved;
+ * read_saved, gate_saved, final_memory and workspace are accepted and unused),
+ * direction [R] and d_read [B,T,R] = dL/d(ungated read).  Writes d_cand,
+ * d_write (w.r.t. the raw pre-activations), d_read_raw (zero: the ungated read
+ * does not depend on it), d_decay [B,T,R] (per step; the caller sums over B,T),
+ * d_direction_partial [B,R] (per sequence; the caller sums over B) and
+ * d_memory_out [B,R] = dL/dm_0.  The final memory carries no gradient.
+ * 1 <= R <= 1024. */
+yuf_status_t yuf_rosa_backward(const float* cand_saved, const float* write_saved,
+                               const float* read_saved, const float* gate_saved,
+                               const float* decay_saved, const float* mem_saved,
+                               const float* direction, const float* final_memory,
+                               const float* d_read, float* d_cand, float* d_write,
+                               float* d_read_raw, float* d_decay, float* d_direction_partial,
+                               float* d_memory_out, float* workspace, int B, int T, int R,
+                               void* stream);
+
 /* ------------------------------------------------------------------------ *
  * Model engine: the YufMusicGen block stack (yufmusicgen/model.py:345-445) on
  * the GPU with device-resident recurrent state, the batched counterpart of the

@@ -12,6 +12,10 @@ Every fixture is produced by the reference's own PyTorch fp32 CPU code:
 * ``YufMusicGen.forward`` / ``.step``  (yufmusicgen/model.py:406-431) built with
   ``use_cuda_kernel=False, use_rosa_scan=False`` and loaded with the seeded
   weights of ``yufmusicgen_b200.weights.init_weights``.
+* gradients of both recurrences by torch autograd through the reference's
+  CPU code (``grads_cases.npz``), the oracle of the training backward ops.
+
+``python tests/golden/make_golden.py grads`` writes only the gradient fixture.
 
 The fixtures are small ``.npz`` files; the GPU box never needs the reference.
 """
@@ -91,6 +95,46 @@ def rosa_cases():
         out[f"{name}.read"] = read.numpy()
         out[f"{name}.mT"] = mT.numpy()
     np.savez_compressed(HERE / "rosa_cases.npz", **out)
+
+
+def grad_cases():
+    """dL/d(inputs) for L = sum(out * seeded cotangent), through the reference's
+    own recurrences.  WKV: zero initial state (the reference op has none) and
+    only the outputs y carry gradient.  ROSA: the ungated read of the CUDA op is
+    the reference recurrence with sigmoid(read_gate) = 1 (read_gate = 80), and
+    only the reads carry gradient (the final memory is non-differentiable in
+    rosa_cuda.py:117)."""
+    out = {}
+    wcases = [("w_n40", 2, 32, 2, 40, 31), ("w_n16", 1, 48, 3, 16, 32), ("w_n64", 1, 16, 2, 64, 33),
+              ("w_n32_t20", 2, 20, 1, 32, 34)]
+    for name, B, T, H, N, seed in wcases:
+        ins = wkv_op_inputs(B, T, H, N, seed=seed)
+        dy = np.random.default_rng(seed + 1000).standard_normal((B, T, H, N), dtype=np.float32)
+        xs = [t(ins[k]).requires_grad_(True) for k in ("r", "w", "k", "v", "a", "b")]
+        y, _ = RWKV7TimeMix._torch_recurrence(*xs, torch.zeros(B, H, N, N))
+        gr = torch.autograd.grad((y * t(dy)).sum(), xs)
+        for k, g in zip(("r", "w", "k", "v", "a", "b"), gr):
+            out[f"{name}.{k}"] = ins[k]
+            out[f"{name}.d{k}"] = g.numpy()
+        out[f"{name}.dy"] = dy
+        out[f"{name}.y"] = y.detach().numpy()
+    rcases = [("r_r32", 2, 24, 32, 41, True), ("r_r128", 1, 40, 128, 42, False),
+              ("r_r12", 3, 9, 12, 43, True), ("r_r256", 1, 17, 256, 44, True)]
+    for name, B, T, R, seed, st in rcases:
+        ins = rosa_op_inputs(B, T, R, seed=seed, with_state=st)
+        dq = np.random.default_rng(seed + 1000).standard_normal((B, T, R), dtype=np.float32)
+        keys = ("cand", "write", "decay", "direction", "m0")
+        xs = {k: t(ins[k]).requires_grad_(True) for k in keys}
+        gate = torch.full((B, T, R), 80.0)
+        read, _ = ROSAMemory._reference_recurrence(xs["cand"], xs["write"], gate, xs["decay"],
+                                                   xs["direction"], xs["m0"])
+        gr = torch.autograd.grad((read * t(dq)).sum(), [xs[k] for k in keys])
+        for k, g in zip(keys, gr):
+            out[f"{name}.{k}"] = ins[k]
+            out[f"{name}.d{k}"] = g.numpy()
+        out[f"{name}.dq"] = dq
+        out[f"{name}.read"] = read.detach().numpy()
+    np.savez_compressed(HERE / "grads_cases.npz", **out)
 
 
 def ref_model(cfg_kwargs, weights):
@@ -204,4 +248,8 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["grads"]:
+        grad_cases()
+    else:
+        main()
+        grad_cases()

@@ -92,3 +92,19 @@ def test_empty_batch_is_a_noop_without_gpu():
     lib = _lib.load()
     assert _wkv(lib, B=0) == 0
     assert lib.yuf_rosa_forward(None, None, None, 16, 16, 16, None, None, 0, 4, 32, 1, None) == 0
+
+
+def test_backward_ops_validate_on_host():
+    lib = _lib.load()
+    wb = lib.yuf_wkv7_backward
+    assert wb(*([16] * 15), 1, 17, 1, 40, None) == 1                      # T not a multiple of 16
+    assert "multiple of 16" in lib.yuf_last_error().decode()
+    assert wb(*([16] * 6), None, *([16] * 8), 1, 16, 1, 40, None) == 1   # dy NULL
+    assert wb(*([16] * 15), 1, 16, 1, 24, None) == 2                      # no kernel for N=24
+    assert "N=24" in lib.yuf_last_error().decode()
+    assert wb(*([16] * 15), 0, 16, 1, 40, None) == 0                      # empty batch
+    rb = lib.yuf_rosa_backward
+    assert rb(*([16] * 16), 1, 4, 0, None) == 1                           # R = 0
+    assert rb(*([16] * 16), 1, 4, 2000, None) == 1                        # R too large
+    assert rb(*([16] * 8), None, *([16] * 7), 1, 4, 32, None) == 1       # d_read NULL
+    assert rb(*([None] * 16), 0, 4, 32, None) == 0                        # empty batch

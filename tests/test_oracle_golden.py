@@ -9,6 +9,7 @@ against the oracle).
 import numpy as np
 import pytest
 
+from oracle.grads import rosa_backward, wkv7_backward
 from oracle.model import OracleModel
 from oracle.scans import rosa_scan, rosa_scan_ungated, wkv7_scan
 from yufmusicgen_b200 import config as C
@@ -25,6 +26,31 @@ def test_wkv7_oracle_matches_reference(golden, case):
     y, sT = wkv7_scan(*ins, g[f"{case}.s0"])
     np.testing.assert_allclose(y, g[f"{case}.y"], rtol=1e-5, atol=1e-5)
     np.testing.assert_allclose(sT, g[f"{case}.sT"], rtol=1e-5, atol=1e-5)
+
+
+def _close_scaled(got, want, rel=1e-5):
+    """Gradients accumulate over T: compare against the largest magnitude."""
+    np.testing.assert_allclose(got, want, rtol=rel, atol=rel * float(np.abs(want).max()))
+
+
+@pytest.mark.parametrize("case", ["w_n40", "w_n16", "w_n64", "w_n32_t20"])
+def test_wkv7_backward_oracle_matches_reference_autograd(golden, case):
+    g = golden("grads_cases.npz")
+    ins = [g[f"{case}.{k}"] for k in "rwkvab"]
+    for k, got in zip("rwkvab", wkv7_backward(*ins, g[f"{case}.dy"])):
+        _close_scaled(got, g[f"{case}.d{k}"])
+
+
+@pytest.mark.parametrize("case", ["r_r32", "r_r128", "r_r12", "r_r256"])
+def test_rosa_backward_oracle_matches_reference_autograd(golden, case):
+    g = golden("grads_cases.npz")
+    ins = [g[f"{case}.{k}"] for k in ("cand", "write", "decay", "direction", "m0")]
+    dc, dw, dd, ddir, dm = rosa_backward(*ins, g[f"{case}.dq"])
+    _close_scaled(dc, g[f"{case}.dcand"])
+    _close_scaled(dw, g[f"{case}.dwrite"])
+    _close_scaled(dd.sum((0, 1)), g[f"{case}.ddecay"])
+    _close_scaled(ddir.sum(0), g[f"{case}.ddirection"])
+    _close_scaled(dm, g[f"{case}.dm0"])
 
 
 @pytest.mark.parametrize("case", ROSA)

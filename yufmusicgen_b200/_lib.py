@@ -25,6 +25,8 @@ SIGNATURES = {
     "yuf_wkv7_forward_compat": [P] * 9 + [I] * 4 + [P],
     "yuf_rosa_forward": [P] * 8 + [I] * 4 + [P],
     "yuf_rosa_forward_compat": [P] * 14 + [I] * 3 + [P],
+    "yuf_wkv7_backward": [P] * 15 + [I] * 4 + [P],
+    "yuf_rosa_backward": [P] * 16 + [I] * 3 + [P],
     "yuf_model_create": [P, I, I, I, P, P, P, P],
     "yuf_model_create_from_yuf": [ctypes.c_char_p, I, I, P],
     "yuf_model_destroy": [P],

@@ -83,6 +83,18 @@ yuf_status_t rosa_compat_dispatch(const float* cand, const float* write, const f
                                   float* m_out, float* cs, float* ws, float* rs, float* gs, float* ds,
                                   float* ms, int B, int T, int R, cudaStream_t stream);
 
+yuf_status_t wkv7_backward_dispatch(const float* r, const float* w, const float* k, const float* v,
+                                    const float* a, const float* b, const float* dy,
+                                    const float* states, const float* sa, float* dr, float* dw,
+                                    float* dk, float* dv, float* da, float* db, float* scratch,
+                                    int B, int T, int H, int N, cudaStream_t st);
+size_t wkv7_backward_scratch_floats(int B, int H, int N);
+yuf_status_t rosa_backward_dispatch(const float* cand_s, const float* write_s, const float* decay_s,
+                                    const float* mem_s, const float* direction, const float* d_read,
+                                    float* d_cand, float* d_write, float* d_read_raw, float* d_decay,
+                                    float* d_dir, float* d_mem, int B, int T, int R,
+                                    cudaStream_t st);
+
 static bool aligned(const void* p, size_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
 
 #define REQUIRE(cond, ...)                  \
@@ -223,6 +235,65 @@ yuf_status_t yuf_rosa_forward_compat(const float* cand, const float* write, cons
   return rosa_compat_dispatch(cand, write, read_raw, decay, direction, memory, read_out, memory_out,
                               cand_saved, write_saved, read_saved, gate_saved, decay_saved,
                               mem_saved, B, T, R, static_cast<cudaStream_t>(stream));
+}
+
+yuf_status_t yuf_wkv7_backward(const float* r, const float* w, const float* k, const float* v,
+                               const float* a, const float* b, const float* dy,
+                               const float* states, const float* sa, float* dr, float* dw,
+                               float* dk, float* dv, float* da, float* db, int B, int T, int H,
+                               int N, void* stream) {
+  g_err[0] = 0;
+  const float* in[13] = {r, w, k, v, a, b, dy, sa, dr, dw, dk, dv, da};
+  yuf_status_t st = check_wkv_args(in, 13, B, T, H, N);
+  if (st != YUF_OK) return st;
+  REQUIRE(T % 16 == 0, "wkv7 backward: T=%d must be a multiple of 16 (pad as cuda_ops.py does)", T);
+  REQUIRE((long long)B * T * H == 0 || (db && aligned(db, 16) && states && aligned(states, 16)),
+          "wkv7 backward: db and states must be non-NULL and 16-byte aligned");
+  if (!(N == 16 || N == 32 || N == 40 || N == 48 || N == 64 || N == 96 || N == 128)) {
+    set_error("wkv7 backward: head size N=%d has no kernel (supported: 16, 32, 40, 48, 64, 96, 128)",
+              N);
+    return YUF_ERR_UNSUPPORTED;
+  }
+  if ((long long)B * T * H == 0) return YUF_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* scratch = nullptr;
+  const size_t bytes = wkv7_backward_scratch_floats(B, H, N) * sizeof(float);
+  cudaError_t e = scratch_alloc(reinterpret_cast<void**>(&scratch), bytes, s);
+  if (e != cudaSuccess) {
+    set_error("wkv7 backward: scratch allocation of %zu bytes failed: %s", bytes,
+              cudaGetErrorString(e));
+    return YUF_ERR_OUT_OF_MEMORY;
+  }
+  st = wkv7_backward_dispatch(r, w, k, v, a, b, dy, states, sa, dr, dw, dk, dv, da, db, scratch, B,
+                              T, H, N, s);
+  scratch_free(scratch, s);
+  return st;
+}
+
+yuf_status_t yuf_rosa_backward(const float* cand_saved, const float* write_saved,
+                               const float* read_saved, const float* gate_saved,
+                               const float* decay_saved, const float* mem_saved,
+                               const float* direction, const float* final_memory,
+                               const float* d_read, float* d_cand, float* d_write,
+                               float* d_read_raw, float* d_decay, float* d_direction_partial,
+                               float* d_memory_out, float* workspace, int B, int T, int R,
+                               void* stream) {
+  (void)read_saved;
+  (void)gate_saved;
+  (void)final_memory;
+  (void)workspace;
+  g_err[0] = 0;
+  REQUIRE(B >= 0 && T >= 0, "rosa backward: negative size (B=%d T=%d)", B, T);
+  REQUIRE(R >= 1 && R <= 1024, "rosa backward: R=%d outside 1..1024", R);
+  REQUIRE(B == 0 || (direction && mem_saved && d_direction_partial && d_memory_out),
+          "rosa backward: direction, mem_saved, d_direction_partial, d_memory_out are required");
+  REQUIRE((long long)B * T == 0 || (cand_saved && write_saved && decay_saved && d_read && d_cand &&
+                                    d_write && d_read_raw && d_decay),
+          "rosa backward: a per-step tensor is NULL");
+  if (B == 0) return YUF_OK;
+  return rosa_backward_dispatch(cand_saved, write_saved, decay_saved, mem_saved, direction, d_read,
+                                d_cand, d_write, d_read_raw, d_decay, d_direction_partial,
+                                d_memory_out, B, T, R, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

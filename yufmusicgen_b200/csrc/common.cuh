@@ -140,4 +140,26 @@ YUF_DEVICE void mma_3xtf32(float (&d)[4], const float (&a)[4], const float (&b)[
   mma_tf32(d, ah, bl);
   mma_tf32(d, ah, bh);
 }
+
+// Sum each of V per-thread values over the block; every thread receives all V
+// sums in out[] (shared).  scratch holds nwarps * V floats.
+template <int V>
+YUF_DEVICE void block_sum_array(const float (&x)[V], float* scratch, float* out, int nwarps) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    float s = x[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) scratch[warp * V + i] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < V) {
+    float s = 0.f;
+    for (int wi = 0; wi < nwarps; ++wi) s += scratch[wi * V + threadIdx.x];
+    out[threadIdx.x] = s;
+  }
+  __syncthreads();
+}
+
 }  // namespace yuf

@@ -37,27 +37,6 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
                            float* read, float* m_out, int B, int T, int R, bool gated,
                            float* scratch, cudaStream_t s);
 
-// Sum each of V per-thread values over the block; every thread receives all V
-// sums in out[] (shared).  scratch holds nwarps * V floats.
-template <int V>
-YUF_DEVICE void block_sum_array(const float (&x)[V], float* scratch, float* out, int nwarps) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int i = 0; i < V; ++i) {
-    float s = x[i];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) scratch[warp * V + i] = s;
-  }
-  __syncthreads();
-  if (threadIdx.x < V) {
-    float s = 0.f;
-    for (int wi = 0; wi < nwarps; ++wi) s += scratch[wi * V + threadIdx.x];
-    out[threadIdx.x] = s;
-  }
-  __syncthreads();
-}
-
 // MODE 0: the scan.  MODE 1: end state only, from a zero initial state (no read
 // output).  MODE 2: transition -- batch row bb starts from the unit vector e_bb
 // with zero input for T steps, so m_out row bb = A^T e_bb, i.e. column bb of

@@ -11,8 +11,9 @@ Same public names and behaviour as the reference module:
 * ``cuda_kernel_enabled()`` / ``report_cuda_fallback(exc)`` (cuda_ops.py:269-283).
 * ``CHUNK_LENGTH = 16``.
 
-Forward only: the training backward of the reference (rwkv7_clampw.cu:83-176)
-is not part of this build, so differentiating through ``rwkv7_cuda`` raises.
+Training: with inputs that require grad, ``rwkv7_cuda`` runs the reference's
+op contract (T padded to 16, checkpoints and sa saved) and its backward runs
+``yuf_wkv7_backward`` (the reference's rwkv7_clampw.cu:83-176 contract).
 """
 
 from __future__ import annotations
@@ -71,25 +72,80 @@ def wkv7_forward(r, w, k, v, a, b, state=None, out=None, state_out=None, algo=AL
     return y, s_out
 
 
+def wkv7_forward_compat(r, w, k, v, a, b, y=None, states=None, sa=None):
+    """The reference op's forward contract (``yuf_wkv7_forward_compat``): zero
+    initial state, T % 16 == 0; returns ``(y, states [B,H,T/16,N,N] transposed
+    checkpoints, sa [B,T,H,N])``."""
+    _validate((r, w, k, v, a, b))
+    B, T, H, N = r.shape
+    y = torch.empty_like(r) if y is None else y
+    states = torch.empty(B, H, T // CHUNK_LENGTH, N, N, device=r.device) if states is None else states
+    sa = torch.empty_like(r) if sa is None else sa
+    with torch.cuda.device(r.device):
+        _lib.call("yuf_wkv7_forward_compat", *(_lib.ptr(x) for x in (r, w, k, v, a, b, y, states, sa)),
+                  B, T, H, N, torch.cuda.current_stream(r.device).cuda_stream)
+    return y, states, sa
+
+
+def wkv7_backward(r, w, k, v, a, b, dy, states, sa, grads=None):
+    """Gradients ``(dr, dw, dk, dv, da, db)`` of the compat forward
+    (``yuf_wkv7_backward``; rwkv7_clampw.cpp:40-63)."""
+    _validate((r, w, k, v, a, b, dy, sa))
+    B, T, H, N = r.shape
+    grads = [torch.empty_like(r) for _ in range(6)] if grads is None else grads
+    with torch.cuda.device(r.device):
+        _lib.call("yuf_wkv7_backward", *(_lib.ptr(x) for x in (r, w, k, v, a, b, dy, states, sa)),
+                  *(_lib.ptr(g) for g in grads), B, T, H, N,
+                  torch.cuda.current_stream(r.device).cuda_stream)
+    return tuple(grads)
+
+
+def _pad16(r, w, k, v, a, b):
+    """Pad T to a multiple of 16 as cuda_ops.py:159-186 does: zero r/k/v/a/b and
+    w_raw = -80 (retention 1), so the padded steps leave the state unchanged."""
+    T = r.shape[1]
+    extra = (-T) % CHUNK_LENGTH
+    if extra == 0:
+        return (r, w, k, v, a, b), T
+    def pad(x, value):
+        tail = torch.full((x.shape[0], extra, *x.shape[2:]), value, device=x.device, dtype=x.dtype)
+        return torch.cat((x, tail), dim=1).contiguous()
+    return (pad(r, 0.0), pad(w, -80.0), pad(k, 0.0), pad(v, 0.0), pad(a, 0.0), pad(b, 0.0)), T
+
+
 class _RWKV7Function(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, r, w, k, v, a, b, state):
-        y, s = wkv7_forward(r, w, k, v, a, b, state)
-        ctx.mark_non_differentiable(s)
-        return y, s
+    """Differentiable op: the compat forward saves the 16-token checkpoints and
+    sa, the backward kernel consumes them (the reference's _RWKV7CUDAFunction,
+    cuda_ops.py:189-253).  Zero initial state only, as in the reference."""
 
     @staticmethod
-    def backward(ctx, grad_y, grad_s):  # pragma: no cover - training is out of scope
-        raise NotImplementedError(
-            "yufmusicgen_b200 implements the WKV-7 forward only; the training backward "
-            "(rwkv7_clampw.cu:83-176) is not part of this build"
-        )
+    def forward(ctx, r, w, k, v, a, b):
+        (rp, wp, kp, vp, ap, bp), T = _pad16(r, w, k, v, a, b)
+        y, states, sa = wkv7_forward_compat(rp, wp, kp, vp, ap, bp)
+        ctx.save_for_backward(rp, wp, kp, vp, ap, bp, states, sa)
+        ctx.T = T
+        final_state = states[:, :, -1].transpose(-1, -2).contiguous()
+        ctx.mark_non_differentiable(final_state)
+        return y[:, :T].contiguous(), final_state
+
+    @staticmethod
+    def backward(ctx, grad_y, grad_s):
+        rp, wp, kp, vp, ap, bp, states, sa = ctx.saved_tensors
+        dy = torch.zeros_like(rp)
+        dy[:, :ctx.T] = grad_y
+        grads = wkv7_backward(rp, wp, kp, vp, ap, bp, dy, states, sa)
+        return tuple(g[:, :ctx.T].contiguous() for g in grads)
 
 
 def rwkv7_cuda(r, w, k, v, a, b, state=None):
-    """Run the fused RWKV-7 recurrence and return output plus final state."""
+    """Run the fused RWKV-7 recurrence and return output plus final state.
+    Differentiable (zero initial state) when an input requires grad."""
     if torch.is_grad_enabled() and any(x.requires_grad for x in (r, w, k, v, a, b)):
-        return _RWKV7Function.apply(r, w, k, v, a, b, state)
+        if state is not None:
+            raise NotImplementedError(
+                "rwkv7_cuda: gradients need a zero initial state (the reference op has no state input)")
+        _validate((r, w, k, v, a, b))
+        return _RWKV7Function.apply(r, w, k, v, a, b)
     return wkv7_forward(r, w, k, v, a, b, state)
 
 

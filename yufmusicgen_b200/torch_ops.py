@@ -12,10 +12,17 @@ reference's JIT-built extensions define them:
   memory, read_out, memory_out, cand_saved, write_saved, read_saved, gate_saved,
   decay_saved, mem_saved)`` (rosa_householder.cpp:24-50, 85-88).
 
-so ``yufmusicgen/cuda_ops.py`` and ``yufmusicgen/rosa_cuda.py`` run unchanged
-once their ``load(...)`` of the reference extension is replaced by importing
-this module.  Do not load the reference extensions in the same process: the op
-namespaces would collide.  The training ``backward`` ops are not provided.
+* ``torch.ops.yufmusicgen_rwkv7.backward(r, w, k, v, a, b, dy, state, sa, dr,
+  dw, dk, dv, da, db)`` (rwkv7_clampw.cpp:40-63) and
+  ``torch.ops.yufmusicgen_rosa.backward(cand_saved, write_saved, read_saved,
+  gate_saved, decay_saved, mem_saved, direction, final_memory, d_read, d_cand,
+  d_write, d_read_raw, d_decay, d_direction_partial, d_memory_out, workspace)``
+  (rosa_householder.cpp:52-83), gradients filled in place.
+
+so ``yufmusicgen/cuda_ops.py`` and ``yufmusicgen/rosa_cuda.py`` run unchanged,
+training included, once their ``load(...)`` of the reference extension is
+replaced by importing this module.  Do not load the reference extensions in the
+same process: the op namespaces would collide.
 """
 
 from __future__ import annotations
@@ -51,6 +58,24 @@ def _rosa_forward(cand, write, read_raw, decay, direction, memory, read_out, mem
             write_saved, read_saved, gate_saved, decay_saved, mem_saved)), B, T, R, _stream(cand))
 
 
+def _rwkv7_backward(r, w, k, v, a, b, dy, state, sa, dr, dw, dk, dv, da, db):
+    B, T, H, N = r.shape
+    with torch.cuda.device(r.device):
+        _lib.call("yuf_wkv7_backward", *(x.data_ptr() for x in (
+            r, w, k, v, a, b, dy, state, sa, dr, dw, dk, dv, da, db)), B, T, H, N, _stream(r))
+
+
+def _rosa_backward(cand_saved, write_saved, read_saved, gate_saved, decay_saved, mem_saved,
+                   direction, final_memory, d_read, d_cand, d_write, d_read_raw, d_decay,
+                   d_direction_partial, d_memory_out, workspace):
+    B, T, R = cand_saved.shape
+    with torch.cuda.device(cand_saved.device):
+        _lib.call("yuf_rosa_backward", *(x.data_ptr() for x in (
+            cand_saved, write_saved, read_saved, gate_saved, decay_saved, mem_saved, direction,
+            final_memory, d_read, d_cand, d_write, d_read_raw, d_decay, d_direction_partial,
+            d_memory_out, workspace)), B, T, R, _stream(cand_saved))
+
+
 def register() -> None:
     """Define and implement both ops (idempotent)."""
     if _libs:
@@ -61,6 +86,12 @@ def register() -> None:
         "Tensor(a!) y, Tensor(b!) state, Tensor(c!) sa) -> ()"
     )
     lib_r.impl("forward", _rwkv7_forward, "CUDA")
+    lib_r.define(
+        "backward(Tensor r, Tensor w, Tensor k, Tensor v, Tensor a, Tensor b, Tensor dy, "
+        "Tensor state, Tensor sa, Tensor(a!) dr, Tensor(b!) dw, Tensor(c!) dk, Tensor(d!) dv, "
+        "Tensor(e!) da, Tensor(f!) db) -> ()"
+    )
+    lib_r.impl("backward", _rwkv7_backward, "CUDA")
     lib_o = torch.library.Library(_ROSA_NS, "DEF")
     lib_o.define(
         "forward(Tensor cand, Tensor write, Tensor read_raw, Tensor decay, Tensor direction, "
@@ -69,6 +100,14 @@ def register() -> None:
         "Tensor(g!) decay_saved, Tensor(h!) mem_saved) -> ()"
     )
     lib_o.impl("forward", _rosa_forward, "CUDA")
+    lib_o.define(
+        "backward(Tensor cand_saved, Tensor write_saved, Tensor read_saved, Tensor gate_saved, "
+        "Tensor decay_saved, Tensor mem_saved, Tensor direction, Tensor final_memory, "
+        "Tensor d_read, Tensor(a!) d_cand, Tensor(b!) d_write, Tensor(c!) d_read_raw, "
+        "Tensor(d!) d_decay, Tensor(e!) d_direction_partial, Tensor(f!) d_memory_out, "
+        "Tensor(g!) workspace) -> ()"
+    )
+    lib_o.impl("backward", _rosa_backward, "CUDA")
     _libs.extend([lib_r, lib_o])
 
 
