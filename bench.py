@@ -225,6 +225,22 @@ def measure_extras(dev, stream, args):
     out["rosa_scan_B2_T2048_R128"] = {"ms": ms, "GBps": rbytes / ms / 1e6,
                                       "tokens_per_s": 2 * T / (ms * 1e-3)}
     del rd, ro, mo
+    # training backward at the config-2 and config-3 ROSA shapes (after the compat forward)
+    ins = wkv_op_inputs(B, T, H, N, seed=0)
+    d = [torch.from_numpy(ins[k]).to(dev) for k in "rwkvab"]
+    y, states, sa = cuda_ops.wkv7_forward_compat(*d)
+    dy = torch.randn_like(y)
+    grads = [torch.empty_like(y) for _ in range(6)]
+    ms = _time(lambda: cuda_ops.wkv7_backward(*d, dy, states, sa, grads), n, dev, stream)
+    out["wkv7_backward_config2"] = {"ms": ms, "tokens_per_s": B * T / (ms * 1e-3)}
+    del d, y, states, sa, dy, grads
+    ri = rosa_op_inputs(2, T, 128, seed=2, with_state=True)
+    rd = [torch.from_numpy(ri[k]).to(dev) for k in keys]
+    _, m_out, saved, mem_saved = rosa_cuda.rosa_forward_compat(*rd)
+    dq = torch.randn_like(rd[0])
+    ms = _time(lambda: rosa_cuda.rosa_backward(*saved, mem_saved, rd[4], m_out, dq), n, dev, stream)
+    out["rosa_backward_B2_T2048_R128"] = {"ms": ms, "tokens_per_s": 2 * T / (ms * 1e-3)}
+    del rd, saved, mem_saved, dq
     out.update(measure_model(dev, stream))
     out.update(measure_long(dev, stream))
     return out

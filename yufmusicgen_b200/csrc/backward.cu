@@ -18,9 +18,12 @@
 // is column j of S times ret_j plus sa b_j + v k_j, so a thread per column
 // replays the chunk without any reduction and writes the 16 states (transposed)
 // to a per-chain scratch.  The reference instead undoes each update by dividing
-// by ret, which loses accuracy over a chunk.  G lives in shared memory; thread
-// i owns row i for the row reductions (dv, dsa) and column i for the column
-// reductions and the update.
+// by ret, which loses accuracy over a chunk.  G lives in shared memory; eight
+// lanes serve row i for the row reductions (dv, dsa) and
+// column i for the column reductions and the update, each over a slice of the
+// other index, and combine their partial sums with shuffles.  A chunk's token
+// vectors are staged in shared memory in one pass and the state slices are
+// loaded one token ahead, so no global load sits on the per-token chain.
 //
 // ROSA (yufmusicgen/model.py:280-287, the CUDA op's ungated read,
 // rosa_householder.cu:89-91), per sequence, memory m [R], unit direction d:
@@ -43,13 +46,29 @@ constexpr int BWD_CHUNK = 16;
 
 template <int N>
 struct WkvBwd {
-  static constexpr int GP = N + 1;                 // padded row of G (conflict-free rows and columns)
-  static constexpr int NV = 10;                    // r, ret, sig, k, v, a, b, dy, sa, dsa
-  static constexpr int SMEM = (N * GP + NV * N) * 4;
+  static constexpr int L = 8;                      // lanes per row / column
+  static constexpr int C = N / L;                  // elements per lane
+  static constexpr int THREADS = N * L;
+  static constexpr int GP = N + 1;                 // padded row of G
+  static constexpr int NV = 9;                     // per token: r, ret, sig, k, v, a, b, dy, sa
+  static constexpr int SMEM = (N * GP + BWD_CHUNK * NV * N + N) * 4;  // G, chunk vectors, dsa
+  // load the state slices one token ahead (a third register slice; not at N = 128,
+  // whose 1024 threads have 64 registers each)
+  static constexpr bool PREFETCH = N < 128;
+  static_assert(N % L == 0, "lane slices");
 };
+enum { VR = 0, VRET, VSIG, VK, VV, VA, VB, VDY, VSA };
+
+// sum over the L lanes of a row group (consecutive lanes)
+template <int L>
+YUF_DEVICE float lane_sum(float x) {
+#pragma unroll
+  for (int o = 1; o < L; o <<= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
 
 template <int N>
-__global__ void __launch_bounds__(N)
+__global__ void __launch_bounds__(WkvBwd<N>::THREADS)
     wkv7_backward_kernel(const float* __restrict__ r, const float* __restrict__ w,
                          const float* __restrict__ k, const float* __restrict__ v,
                          const float* __restrict__ a, const float* __restrict__ b,
@@ -58,108 +77,146 @@ __global__ void __launch_bounds__(N)
                          float* __restrict__ dk, float* __restrict__ dv, float* __restrict__ da,
                          float* __restrict__ db, float* __restrict__ scratch, int T, int H) {
   using K = WkvBwd<N>;
+  constexpr int L = K::L, C = K::C, NV = K::NV;
   extern __shared__ __align__(16) float sm[];
   float* G = sm;
-  float* vr = sm + N * K::GP;
-  float *R_ = vr, *RET = vr + N, *SIG = vr + 2 * N, *K_ = vr + 3 * N, *V_ = vr + 4 * N,
-        *A_ = vr + 5 * N, *B_ = vr + 6 * N, *DY = vr + 7 * N, *SA = vr + 8 * N, *DSA = vr + 9 * N;
-  const int j = threadIdx.x;
+  float* VS = sm + N * K::GP;            // [16][NV][N]: the chunk's token vectors
+  float* DSA = VS + BWD_CHUNK * NV * N;  // [N]
+  const int tid = threadIdx.x;
+  const int x = tid / L, g = tid - x * L, i0 = g * C;  // x: the row / column this lane serves
   const int bh = blockIdx.x, bb = bh / H, hh = bh - bb * H;
   const int nc = T / BWD_CHUNK;
   const size_t NN = (size_t)N * N;
   float* scr = scratch + (size_t)bh * BWD_CHUNK * NN;  // [16][N][N]: S_t^T of the chunk's tokens
   const float* ckc = ck + (size_t)bh * nc * NN;        // [nc][N][N]: S^T after each chunk
-  for (int q = j; q < N * K::GP; q += N) G[q] = 0.f;
+  for (int q = tid; q < N * K::GP; q += K::THREADS) G[q] = 0.f;
+  auto slice = [&](const float* base, float (&o)[C]) {  // this lane's part of row x of S^T
+    if (base == nullptr) {
+#pragma unroll
+      for (int e = 0; e < C; ++e) o[e] = 0.f;
+    } else if constexpr (C % 2 == 0) {
+      const float2* p2 = reinterpret_cast<const float2*>(base + (size_t)x * N + i0);
+#pragma unroll
+      for (int e = 0; e < C / 2; ++e) {
+        const float2 q = p2[e];
+        o[2 * e] = q.x;
+        o[2 * e + 1] = q.y;
+      }
+    } else {
+      const float* p1 = base + (size_t)x * N + i0;
+#pragma unroll
+      for (int e = 0; e < C; ++e) o[e] = p1[e];
+    }
+  };
 
   for (int c = nc - 1; c >= 0; --c) {
-    // ---- replay the chunk: thread j carries column j of S
-    float col[N];
-    if (c == 0) {
+    const float* start = c > 0 ? ckc + (size_t)(c - 1) * NN : nullptr;  // S^T before the chunk
+    // ---- stage the chunk's vectors (one latency per chunk, not per token)
+    __syncthreads();  // the previous chunk is done with VS
+    for (int q = tid; q < BWD_CHUNK * NV * N; q += K::THREADS) {
+      const int tau = q / (NV * N), rem = q - tau * NV * N, vi = rem / N, e = rem - vi * N;
+      const size_t off = (((size_t)bb * T + c * BWD_CHUNK + tau) * H + hh) * N + e;
+      const float* sp = vi == VR ? r : vi <= VSIG ? w : vi == VK ? k : vi == VV ? v
+                      : vi == VA ? a : vi == VB ? b : vi == VDY ? dy : sa;
+      float val = sp[off];
+      if (vi == VSIG) val = sigmoidf_fast(val);
+      else if (vi == VRET) val = __expf(W_SCALE * sigmoidf_fast(val));
+      VS[q] = val;
+    }
+    __syncthreads();
+    // ---- replay: lane (x, g) carries rows i0 .. i0+C-1 of column x of S
+    {
+      float col[C];
+      slice(start, col);
+      for (int tau = 0; tau < BWD_CHUNK; ++tau) {
+        const float* vt = VS + tau * NV * N;
+        const float retx = vt[VRET * N + x], kx = vt[VK * N + x], bx = vt[VB * N + x];
+        float* o1 = scr + (size_t)tau * NN + (size_t)x * N + i0;
 #pragma unroll
-      for (int i = 0; i < N; ++i) col[i] = 0.f;
-    } else {
-      const float4* s4 = reinterpret_cast<const float4*>(ckc + (size_t)(c - 1) * NN + (size_t)j * N);
+        for (int e = 0; e < C; ++e)
+          col[e] = fmaf(col[e], retx, fmaf(vt[VSA * N + i0 + e], bx, vt[VV * N + i0 + e] * kx));
+        if constexpr (C % 2 == 0) {
 #pragma unroll
-      for (int i4 = 0; i4 < N / 4; ++i4) {
-        const float4 q = s4[i4];
-        col[4 * i4] = q.x; col[4 * i4 + 1] = q.y; col[4 * i4 + 2] = q.z; col[4 * i4 + 3] = q.w;
+          for (int e = 0; e < C / 2; ++e)
+            reinterpret_cast<float2*>(o1)[e] = make_float2(col[2 * e], col[2 * e + 1]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < C; ++e) o1[e] = col[e];
+        }
       }
     }
-    for (int tau = 0; tau < BWD_CHUNK; ++tau) {
-      const size_t off = (((size_t)bb * T + c * BWD_CHUNK + tau) * H + hh) * N;
-      __syncthreads();  // previous users of V_ / SA are done
-      V_[j] = v[off + j];
-      SA[j] = sa[off + j];
-      __syncthreads();
-      const float retj = __expf(W_SCALE * sigmoidf_fast(w[off + j]));
-      const float kj = k[off + j], bj = b[off + j];
+    // ---- reverse over the chunk's tokens; the state slices of the next token
+    // back are loaded one token ahead
+    float sn[C], so[C], nx[C];
+    slice(scr + (size_t)(BWD_CHUNK - 1) * NN, sn);
+    if constexpr (K::PREFETCH) slice(scr + (size_t)(BWD_CHUNK - 2) * NN, so);
+    // unrolled, so the slice rotation below is register renaming and the
+    // one-token-ahead loads are not waited for early
 #pragma unroll
-      for (int i = 0; i < N; ++i) col[i] = fmaf(col[i], retj, fmaf(SA[i], bj, V_[i] * kj));
-      float4* o4 = reinterpret_cast<float4*>(scr + (size_t)tau * NN + (size_t)j * N);
-#pragma unroll
-      for (int i4 = 0; i4 < N / 4; ++i4)
-        o4[i4] = make_float4(col[4 * i4], col[4 * i4 + 1], col[4 * i4 + 2], col[4 * i4 + 3]);
-    }
-    // ---- reverse over the chunk's tokens
     for (int tau = BWD_CHUNK - 1; tau >= 0; --tau) {
+      // so = S before token tau (the previous chunk's end, or zero, at tau = 0)
+      const float* prev = tau > 0 ? scr + (size_t)(tau - 1) * NN : start;
+      if constexpr (K::PREFETCH) {
+        if (tau >= 2) slice(scr + (size_t)(tau - 2) * NN, nx);
+        else if (tau == 1) slice(start, nx);
+      } else {
+        slice(prev, so);
+      }
       const size_t off = (((size_t)bb * T + c * BWD_CHUNK + tau) * H + hh) * N;
-      __syncthreads();  // the previous token's column pass is done with G and the vectors
-      R_[j] = r[off + j];
-      const float sg = sigmoidf_fast(w[off + j]);
-      SIG[j] = sg;
-      RET[j] = __expf(W_SCALE * sg);
-      K_[j] = k[off + j];
-      V_[j] = v[off + j];
-      A_[j] = a[off + j];
-      B_[j] = b[off + j];
-      DY[j] = dy[off + j];
-      SA[j] = sa[off + j];
-      __syncthreads();
-      {  // row pass, thread j = row i: G += dy r^T, dv = G k, dsa = G b
-        float* Gr = G + (size_t)j * K::GP;
-        const float dyi = DY[j];
+      const float* vt = VS + tau * NV * N;
+      __syncthreads();  // the previous token's column pass is done with G and DSA
+      {  // row pass, lane (x = row i, g): G += dy r^T, dv = G k, dsa = G b over its columns
+        float* Gr = G + (size_t)x * K::GP + i0;
+        const float dyi = vt[VDY * N + x];
         float dvi = 0.f, dsai = 0.f;
-#pragma unroll 8
-        for (int q = 0; q < N; ++q) {
-          const float g = fmaf(dyi, R_[q], Gr[q]);
-          Gr[q] = g;
-          dvi = fmaf(g, K_[q], dvi);
-          dsai = fmaf(g, B_[q], dsai);
+#pragma unroll
+        for (int q = 0; q < C; ++q) {
+          const float gv = fmaf(dyi, vt[VR * N + i0 + q], Gr[q]);
+          Gr[q] = gv;
+          dvi = fmaf(gv, vt[VK * N + i0 + q], dvi);
+          dsai = fmaf(gv, vt[VB * N + i0 + q], dsai);
         }
-        dv[off + j] = dvi;
-        DSA[j] = dsai;
+        dvi = lane_sum<L>(dvi);
+        dsai = lane_sum<L>(dsai);
+        if (g == 0) {
+          dv[off + x] = dvi;
+          DSA[x] = dsai;
+        }
       }
       __syncthreads();
-      {  // column pass, thread j = column j
-        const float* Snew = scr + (size_t)tau * NN + (size_t)j * N;
-        const float* Sold = tau > 0 ? scr + (size_t)(tau - 1) * NN + (size_t)j * N
-                                    : (c > 0 ? ckc + (size_t)(c - 1) * NN + (size_t)j * N : nullptr);
-        const float retj = RET[j], aj = A_[j];
+      {  // column pass, lane (x = column j, g) over rows i0 .. i0+C-1
+        const float retj = vt[VRET * N + x], aj = vt[VA * N + x];
         float drj = 0.f, dkj = 0.f, dbj = 0.f, dretj = 0.f, daj = 0.f;
-#pragma unroll 2
-        for (int i4 = 0; i4 < N / 4; ++i4) {
-          const float4 sn = reinterpret_cast<const float4*>(Snew)[i4];
-          const float4 so = Sold ? reinterpret_cast<const float4*>(Sold)[i4] : make_float4(0.f, 0.f, 0.f, 0.f);
-          const float snv[4] = {sn.x, sn.y, sn.z, sn.w}, sov[4] = {so.x, so.y, so.z, so.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i = 4 * i4 + e;
-            float* gp = G + (size_t)i * K::GP + j;
-            const float g = *gp;
-            drj = fmaf(snv[e], DY[i], drj);
-            dkj = fmaf(g, V_[i], dkj);
-            dbj = fmaf(g, SA[i], dbj);
-            dretj = fmaf(g, sov[e], dretj);
-            daj = fmaf(sov[e], DSA[i], daj);
-            *gp = fmaf(g, retj, DSA[i] * aj);
-          }
+        for (int e = 0; e < C; ++e) {
+          const int i = i0 + e;
+          float* gp = G + (size_t)i * K::GP + x;
+          const float gv = *gp;
+          drj = fmaf(sn[e], vt[VDY * N + i], drj);
+          dkj = fmaf(gv, vt[VV * N + i], dkj);
+          dbj = fmaf(gv, vt[VSA * N + i], dbj);
+          dretj = fmaf(gv, so[e], dretj);
+          daj = fmaf(so[e], DSA[i], daj);
+          *gp = fmaf(gv, retj, DSA[i] * aj);
         }
-        const float sg = SIG[j];
-        dr[off + j] = drj;
-        dk[off + j] = dkj;
-        db[off + j] = dbj;
-        da[off + j] = daj;
-        dw[off + j] = dretj * retj * W_SCALE * sg * (1.f - sg);
+        drj = lane_sum<L>(drj);
+        dkj = lane_sum<L>(dkj);
+        dbj = lane_sum<L>(dbj);
+        dretj = lane_sum<L>(dretj);
+        daj = lane_sum<L>(daj);
+        if (g == 0) {
+          const float sg = vt[VSIG * N + x];
+          dr[off + x] = drj;
+          dk[off + x] = dkj;
+          db[off + x] = dbj;
+          da[off + x] = daj;
+          dw[off + x] = dretj * retj * W_SCALE * sg * (1.f - sg);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < C; ++e) {
+        sn[e] = so[e];
+        if constexpr (K::PREFETCH) so[e] = nx[e];
       }
     }
   }
@@ -185,8 +242,8 @@ yuf_status_t wkv7_backward_dispatch(const float* r, const float* w, const float*
       set_error("wkv7 backward: cudaFuncSetAttribute failed");                                  \
       return YUF_ERR_CUDA;                                                                       \
     }                                                                                            \
-    kern<<<B * H, NN, WkvBwd<NN>::SMEM, st>>>(r, w, k, v, a, b, dy, states, sa, dr, dw, dk, dv,  \
-                                             da, db, scratch, T, H);                             \
+    kern<<<B * H, WkvBwd<NN>::THREADS, WkvBwd<NN>::SMEM, st>>>(                                \
+        r, w, k, v, a, b, dy, states, sa, dr, dw, dk, dv, da, db, scratch, T, H);                \
     return check_launch("wkv7_backward_kernel");                                                 \
   }
     CASE(16) CASE(32) CASE(40) CASE(48) CASE(64) CASE(96) CASE(128)
