@@ -242,14 +242,37 @@ def measure_extras(dev, stream, args):
     out["rosa_backward_B2_T2048_R128"] = {"ms": ms, "tokens_per_s": 2 * T / (ms * 1e-3)}
     del rd, saved, mem_saved, dq
     out.update(measure_model(dev, stream))
-    out.update(measure_long(dev, stream))
     return out
 
 
-def measure_long(dev, stream):
-    """Benchmark config 5's per-GPU share (8 of its 64 sequences) through the
-    engine: 24 layers, d1024, H16 x 64, ROSA 256, bf16 weights, fp32 state,
-    B8 x T8192 Zipf(1.1) ids, zero initial state; prefill tokens/s."""
+C4_SEQS, C4_PROMPT, C4_STEPS = 256, 64, 1024
+C5_SEQS_PER_GPU, C5_T = 8, 8192
+
+
+def model_bytes_per_step(cfg, wsz):
+    """Bytes a decode step must move for one model: every weight once (the tied
+    embedding as the LM head) and, per sequence, the recurrent state in and out
+    (per layer prev [d], S [H,N,N], m [R]) plus its logits row."""
+    d, lr, R, V = cfg.d_model, cfg.low_rank, cfg.rosa_size, cfg.vocab_size
+    per_layer = 4 * d * d + 6 * d * lr + 3 * R * d + R * d + 12 * d * d
+    weights = (cfg.n_layers * per_layer + V * d) * wsz
+    state = cfg.n_layers * 2 * 4 * (d + cfg.n_heads * cfg.head_size ** 2 + R) + 4 * V
+    return weights, state
+
+
+def measure_sharded(dev, rank, world, barrier, max_over_ranks):
+    """Benchmark configs 4 and 5 batch-sharded over the ranks (weak in the
+    sequences each GPU holds, no collective on the data path; time = max over
+    ranks of each rank's CUDA-event time).
+
+    * config 4: 256 sequences (256 / world per GPU), 64-token prompts
+      (Zipf(1.1) after a byte prefix), 1024 tokens generated per sequence with
+      temperature 1.0 and top-k 32 under Philox seed 2024 through
+      ``Engine.generate`` (yuf_generate: on-device sampling, CUDA-graph decode
+      steps); the time covers the prefill and all 1024 steps.
+    * config 5: 8 of the 64 sequences of T = 8192 per GPU through the 24-layer
+      d1024 model (bf16 weights, fp32 state): prefill tokens/s.
+    """
     import torch
 
     from yufmusicgen_b200 import config as C
@@ -257,23 +280,78 @@ def measure_long(dev, stream):
     from yufmusicgen_b200.weights import init_weights
     from yufmusicgen_b200.workloads import zipf_ids
 
+    peak, _ = peaks()
+    res = {}
+    side = torch.cuda.Stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cfg = C.ModelConfig(**C.BASE_0P1B)
+    w = init_weights(cfg, 1, "baseline")
+    per = C4_SEQS // world
+    prompt = torch.as_tensor(zipf_ids(C4_SEQS, C4_PROMPT, seed=4, vocab=cfg.vocab_size)[rank * per:(rank + 1) * per],
+                             dtype=torch.int32, device=dev)
+    gen = dict(temperature=1.0, top_k=32, seed=2024, seq0=rank * per)
+    for prec in ("bf16", "fp32"):
+        with torch.cuda.stream(side):
+            eng = Engine(cfg, w, precision=prec, device=dev.index, n_slots=per)
+            eng.set_decode_graphs(True)
+            toks = torch.empty(per, C4_STEPS, dtype=torch.int32, device=dev)
+            lens = torch.empty(per, dtype=torch.int32, device=dev)
+            eng.generate(prompt, 8, out_tokens=toks[:, :8].contiguous(), out_lengths=lens, **gen)
+            torch.cuda.synchronize(dev)
+            barrier()
+            torch.cuda.synchronize(dev)
+            e0.record(side)
+            eng.generate(prompt, C4_STEPS, out_tokens=toks, out_lengths=lens, **gen)
+            e1.record(side)
+            torch.cuda.synchronize(dev)
+            barrier()
+            ms = max_over_ranks(e0.elapsed_time(e1))
+            wbytes, sbytes = model_bytes_per_step(cfg, 2 if prec == "bf16" else 4)
+            step_ms = ms / C4_STEPS  # includes the prompt prefill: an upper bound
+            step_bytes = wbytes + per * sbytes
+            res[f"generate_c4_{prec}"] = {
+                "ms": ms, "tokens_per_s": C4_SEQS * C4_STEPS / (ms * 1e-3), "sequences": C4_SEQS,
+                "sequences_per_gpu": per, "prompt": C4_PROMPT, "steps": C4_STEPS,
+                "sampler": "temperature 1.0, top-k 32, Philox4x32-10 seed 2024 on device",
+                "step_bytes_per_gpu": step_bytes,
+                "hbm_frac_per_gpu": step_bytes / (step_ms * 1e-3) / 1e9 / peak}
+            eng.close()
+            del eng
+    del w
+    # config 5: this rank's 8 of the 64 sequences
     cfg = C.ModelConfig(**C.LONG_1K)
     w = init_weights(cfg, 2, "baseline")
-    Bl, Tl = 8, 8192
-    ids = torch.as_tensor(zipf_ids(Bl, Tl, seed=2, vocab=cfg.vocab_size), dtype=torch.int32, device=dev)
-    eng = Engine(cfg, w, precision="bf16", device=dev.index, n_slots=Bl)
-    last = torch.empty(Bl, cfg.vocab_size, device=dev)
+    ids = torch.as_tensor(zipf_ids(C5_SEQS_PER_GPU, C5_T, seed=100 + rank, vocab=cfg.vocab_size),
+                          dtype=torch.int32, device=dev)
+    eng = Engine(cfg, w, precision="bf16", device=dev.index, n_slots=C5_SEQS_PER_GPU)
+    del w
+    last = torch.empty(C5_SEQS_PER_GPU, cfg.vocab_size, device=dev)
+    stream = torch.cuda.current_stream(dev)
 
     def pf():
-        eng.reset_state(0, Bl)
+        eng.reset_state(0, C5_SEQS_PER_GPU)
         eng.prefill(ids, slot0=0, out_last=last)
 
-    ms = _time(pf, 2, dev, stream, warm=1)
+    pf()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    reps = 2
+    e0.record(stream)
+    for _ in range(reps):
+        pf()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / reps)
     eng.close()
     del eng
-    flop = 915e6 * Bl * Tl  # about 2 x linear parameters + LM head per token
-    return {"prefill_c5_B8_T8192_bf16": {"ms": ms, "tokens_per_s": Bl * Tl / (ms * 1e-3),
-                                         "TFLOPs": flop / (ms * 1e-3) / 1e12}}
+    tokens = world * C5_SEQS_PER_GPU * C5_T
+    flop = 915e6 * tokens  # about 2 x linear parameters + LM head per token
+    res["prefill_c5_bf16"] = {"ms": ms, "tokens_per_s": tokens / (ms * 1e-3),
+                              "sequences": world * C5_SEQS_PER_GPU, "seq_len": C5_T,
+                              "TFLOPs_per_gpu": flop / world / (ms * 1e-3) / 1e12}
+    return res
 
 
 def measure_model(dev, stream):
@@ -441,6 +519,7 @@ def run_ours(args):
     h2d = sum(host[k].numel() * 4 for k in "rwkvab")
     d2h = (y_h[0].numel() + s_h[0].numel()) * 4
 
+    sharded = measure_sharded(dev, rank, world, barrier, max_over_ranks)
     extra = measure_extras(dev, stream, args) if rank == 0 else {}
 
     if rank == 0:
@@ -464,6 +543,7 @@ def run_ours(args):
                          "algorithmic_bytes_per_step": ALGO_BYTES},
             "gpu_launches": LAUNCHES_PER_STEP * args.steps,
             "clocks": clocks.summary(),
+            "sharded": sharded,
             "extra": extra,
         }
         if world == 1:

@@ -243,6 +243,43 @@ yuf_status_t yuf_sample(const float* logits, int B, int V, float temperature, in
 yuf_status_t yuf_philox_uniform(uint64_t seed, uint64_t step, int seq0, int n, float* out,
                                 void* stream);
 
+/* Sampling rule of yuf_generate (the reference loop's knobs, cli/generate.py:34-56,
+ * 142-149, plus the top-k / Philox stream of benchmark config 4). */
+typedef struct yuf_generate_params {
+  float temperature;         /* <= 0: greedy argmax                                          */
+  int top_k;                 /* 1..1024                                                      */
+  float top_p;               /* nucleus cut inside the top-k (>= 1: off)                     */
+  uint64_t seed;             /* Philox4x32-10 key                                            */
+  int seq0;                  /* global index of the batch's first sequence (Philox counter)  */
+  int mask_below;            /* ids below are excluded, except EOS once allowed (reference:  */
+                             /* MIDI_OFFSET = 260; 0 = no mask)                              */
+  int eos_id;                /* end-of-sequence id (reference: EOS = 2), -1 = never end      */
+  int min_tokens_before_eos; /* EOS selectable once this many tokens were generated (16)     */
+} yuf_generate_params;
+
+/* Batched autoregressive generation on the device: the decode loop of the
+ * reference's run_generation (yufmusicgen/cli/generate.py:130-154; the Vulkan
+ * client's vulkan/src/generation.rs:176-214) for B sequences at once, with no
+ * host synchronisation per token.  Prefills prompt_ids [B,T] (device int32) from
+ * the state in slots [slot0, slot0 + B) -- zero them first (yuf_state_reset) for
+ * fresh sequences, as run_generation starts from no state -- then n_steps times:
+ * sample one token per sequence from the last logits (yuf_sample's rule with
+ * step = the step index and allow_eos = step >= min_tokens_before_eos), record
+ * it, and run one decode step with it (yuf_step; CUDA-graph replay when
+ * yuf_model_set_decode_graphs is on).  A sequence ends at its first EOS, which
+ * the reference does not emit (it breaks, generate.py:150-152):
+ *   tokens  [B, n_steps] (device int32): the generated ids; from a sequence's
+ *           end on, eos_id;
+ *   lengths [B]          (device int32): tokens generated before EOS (n_steps if
+ *           the sequence never ended).
+ * Ended sequences keep stepping (with EOS as input) until the batch finishes, so
+ * their slots' final state is not the reference's; the tokens are unaffected.
+ * Working buffers (the last logits, the sampled ids) are kept by the model and
+ * grow on demand. */
+yuf_status_t yuf_generate(yuf_model* model, const int32_t* prompt_ids, int B, int T, int slot0,
+                          int n_steps, const yuf_generate_params* params, int32_t* tokens,
+                          int32_t* lengths, void* stream);
+
 /* Replay yuf_step as a CUDA graph: the first call for a given (B, slot0, ids,
  * logits) captures the whole step on the caller's stream, later calls with the
  * same arguments launch the graph (one launch instead of ~25 per layer).  Only

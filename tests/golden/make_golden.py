@@ -15,7 +15,8 @@ Every fixture is produced by the reference's own PyTorch fp32 CPU code:
 * gradients of both recurrences by torch autograd through the reference's
   CPU code (``grads_cases.npz``), the oracle of the training backward ops.
 
-``python tests/golden/make_golden.py grads`` writes only the gradient fixture.
+``python tests/golden/make_golden.py grads`` writes only the gradient fixture,
+``... greedy256`` only the 256-step greedy decode of the 0.1B model.
 
 The fixtures are small ``.npz`` files; the GPU box never needs the reference.
 """
@@ -229,6 +230,35 @@ def state_test_case():
     )
 
 
+def greedy256_case():
+    """The north star's greedy bar on the 0.1B model (benchmark configs 3/4):
+    two 64-token config-4 prompts, 256 greedy decode steps through
+    ``YufMusicGen.forward`` + ``.step`` (yufmusicgen/model.py:406-431).  Stored:
+    the tokens, each step's top-1 minus top-2 logit margin (how far a step is
+    from a tie) and the full logits of the first and last step."""
+    cfg = C.ModelConfig(**C.BASE_0P1B)
+    weights = init_weights(cfg, 1, "baseline")
+    model = ref_model(C.BASE_0P1B, weights)
+    ids = zipf_ids(2, 64, seed=4, vocab=cfg.vocab_size)
+    n = 256
+    with torch.no_grad():
+        logits, st = model(t(ids))
+        last = logits[:, -1]
+        toks, gaps, keep = [], [], {}
+        for i in range(n):
+            top2 = torch.topk(last, 2, dim=-1).values
+            gaps.append(top2[:, 0] - top2[:, 1])
+            tok = torch.argmax(last, dim=-1)
+            toks.append(tok)
+            last, st = model.step(tok, st)
+            if i in (0, n - 1):
+                keep[i] = last.numpy().copy()
+    np.savez_compressed(
+        HERE / "greedy256_base0p1b.npz", ids=ids, tokens=torch.stack(toks, 1).numpy(),
+        margins=torch.stack(gaps, 1).numpy(), logits_step0=keep[0], logits_last=keep[n - 1],
+        meta_keys=np.array(["seed", "recipe", "steps"]), meta_vals=np.array(["1", "baseline", str(n)]))
+
+
 def main():
     wkv_cases()
     rosa_cases()
@@ -250,6 +280,9 @@ def main():
 if __name__ == "__main__":
     if sys.argv[1:] == ["grads"]:
         grad_cases()
+    elif sys.argv[1:] == ["greedy256"]:
+        greedy256_case()
     else:
         main()
         grad_cases()
+        greedy256_case()

@@ -108,3 +108,16 @@ def test_backward_ops_validate_on_host():
     assert rb(*([16] * 16), 1, 4, 2000, None) == 1                        # R too large
     assert rb(*([16] * 8), None, *([16] * 7), 1, 4, 32, None) == 1       # d_read NULL
     assert rb(*([None] * 16), 0, 4, 32, None) == 0                        # empty batch
+
+
+def test_generate_params_layout_and_host_validation():
+    """yuf_generate_params matches the C layout, and yuf_generate rejects a
+    missing model or params before any CUDA call."""
+    import ctypes as ct
+
+    assert ct.sizeof(_lib.GenerateParamsC) == 40
+    assert _lib.GenerateParamsC.seed.offset == 16
+    lib = _lib.load()
+    p = _lib.GenerateParamsC(1.0, 32, 1.0, 0, 0, 0, -1, 16)
+    assert lib.yuf_generate(None, 16, 1, 1, 0, 1, ct.byref(p), 16, 16, None) == 1
+    assert "null model" in lib.yuf_last_error().decode()

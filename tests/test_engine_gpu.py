@@ -72,6 +72,22 @@ def test_prefill_and_greedy_match_reference(golden, fixture, cfgd, seed, recipe)
     eng.close()
 
 
+def test_greedy_256_steps_identical_to_reference(golden):
+    """Greedy decode on the 0.1B model (config-4 prompts, fp32): the first 256
+    tokens equal the reference's, and the first and last step's logits are
+    within the fp32 tolerance.  The fixture's smallest top-1/top-2 margin is
+    about 1.2e-4, so a logit error above that would flip a token."""
+    g = golden("greedy256_base0p1b.npz")
+    cfg, w, eng = make(C.BASE_0P1B, 1, "baseline", n_slots=2)
+    toks, logs = greedy(eng, g["ids"], 256)
+    bad = np.argwhere(toks != g["tokens"])
+    assert bad.size == 0, f"first mismatch (seq, step) {bad[0].tolist()}, margin {g['margins'][tuple(bad[0])]}"
+    close(logs[:, 0], g["logits_step0"])
+    close(logs[:, -1], g["logits_last"])
+    eng.sync_check()
+    eng.close()
+
+
 def test_tiny_per_layer_regions_match_reference(golden):
     g = golden("model_tiny.npz")
     cfg, w, eng = make(C.TINY, 0, "perturbed")

@@ -154,3 +154,16 @@ def test_c_oracle_rosa_matches_reference(golden, case):
     read, mT = cref.rosa_scan(*args)
     np.testing.assert_allclose(read, g[f"{case}.read"], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(mT, g[f"{case}.mT"], rtol=1e-5, atol=1e-6)
+
+
+def test_greedy256_fixture_pinned_by_oracle(golden):
+    """The 256-step greedy fixture (reference CPU path, 0.1B model): the oracle
+    reproduces its prompt logits' argmax, its first greedy tokens and the logits
+    of the first step."""
+    g = golden("greedy256_base0p1b.npz")
+    cfg = C.ModelConfig(**C.BASE_0P1B)
+    om = OracleModel(cfg, init_weights(cfg, 1, "baseline"))
+    toks, logs = om.greedy(g["ids"], 4)
+    np.testing.assert_array_equal(toks, g["tokens"][:, :4])
+    np.testing.assert_allclose(logs[:, 0], g["logits_step0"], rtol=1e-4, atol=2e-5)
+    assert g["tokens"].shape == (2, 256) and g["margins"].min() > 0

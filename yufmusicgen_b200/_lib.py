@@ -42,6 +42,7 @@ SIGNATURES = {
     "yuf_sample": [P, I, I, ctypes.c_float, I, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64, I, I,
                    I, I, P, P, P],
     "yuf_philox_uniform": [ctypes.c_uint64, ctypes.c_uint64, I, I, P, P],
+    "yuf_generate": [P, P, I, I, I, I, P, P, P, P],
     "yuf_model_sync_check": [P, P],
     "yuf_model_set_debug": [P, I],
     "yuf_debug_dump": [P, ctypes.c_char_p, I, P, ctypes.c_size_t, P],
@@ -53,6 +54,14 @@ class ModelConfigC(ctypes.Structure):
 
     _fields_ = [(n, ctypes.c_int) for n in ("vocab_size", "d_model", "n_layers", "n_heads",
                                              "head_size", "rosa_size", "low_rank")]
+
+
+class GenerateParamsC(ctypes.Structure):
+    """``yuf_generate_params`` of include/yufb200.h."""
+
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_int), ("top_p", ctypes.c_float),
+                ("seed", ctypes.c_uint64), ("seq0", ctypes.c_int), ("mask_below", ctypes.c_int),
+                ("eos_id", ctypes.c_int), ("min_tokens_before_eos", ctypes.c_int)]
 
 
 class YufError(RuntimeError):

@@ -99,6 +99,9 @@ struct yuf_model {
     for (auto& g : graphs) cudaGraphExecDestroy(g.exec);
     graphs.clear();
   }
+  // yuf_generate's working buffers: the last logits [B, V] and the sampled ids
+  // [B], grown on demand (stable pointers, so its decode graphs replay)
+  std::unique_ptr<DevBuf> gen;
   // debug dumps: region -> per layer host copies of the last call
   bool debug = false;
   std::map<std::string, std::vector<std::vector<float>>> dumps;
@@ -711,6 +714,77 @@ yuf_status_t yuf_step(yuf_model* m, const int32_t* ids, int B, int slot0, float*
   if (m->graphs.size() >= 64) m->drop_graphs();
   m->graphs.push_back({B, slot0, ids, logits, m->ws_gen, exec});
   Y_CUDA(cudaGraphLaunch(exec, s));
+  return YUF_OK;
+}
+
+}  // extern "C"
+
+namespace yuf {
+// Step s of yuf_generate: record the sampled ids and end a sequence at its first
+// EOS.  lengths[b] == n_steps means "still running" (set at step 0); an ended
+// sequence records eos_id and is fed eos_id from then on.
+__global__ void gen_record_kernel(int32_t* __restrict__ ids, int32_t* __restrict__ tokens,
+                                  int32_t* __restrict__ lengths, int B, int n_steps, int s,
+                                  int eos_id) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  int len = s == 0 ? n_steps : lengths[b];
+  int tok = ids[b];
+  if (len != n_steps) tok = eos_id;                      // ended at an earlier step
+  else if (eos_id >= 0 && tok == eos_id) len = s;        // ends now
+  tokens[(size_t)b * n_steps + s] = len != n_steps ? eos_id : tok;
+  ids[b] = tok;
+  lengths[b] = len;
+}
+}  // namespace yuf
+
+extern "C" {
+
+yuf_status_t yuf_generate(yuf_model* m, const int32_t* prompt_ids, int B, int T, int slot0,
+                          int n_steps, const yuf_generate_params* p, int32_t* tokens,
+                          int32_t* lengths, void* stream) {
+  Y_REQUIRE(m && p, "generate: null model or params");
+  Y_REQUIRE(m->n_slots > 0, "generate: call yuf_state_alloc first");
+  Y_REQUIRE(B >= 1 && T >= 1 && n_steps >= 1, "generate: need B, T and n_steps >= 1 (got %d, %d, %d)",
+            B, T, n_steps);
+  Y_REQUIRE(prompt_ids && tokens && lengths, "generate: prompt_ids, tokens and lengths must be non-NULL");
+  Y_REQUIRE(slot0 >= 0 && slot0 + B <= m->n_slots, "generate: slots [%d, %d) out of range (%d slots)",
+            slot0, slot0 + B, m->n_slots);
+  Y_REQUIRE(p->top_k >= 1 && p->top_k <= 1024, "generate: top_k must be in [1, 1024] (got %d)", p->top_k);
+  Y_REQUIRE(std::isfinite(p->temperature) && std::isfinite(p->top_p) && p->top_p > 0.f,
+            "generate: temperature must be finite and top_p finite and > 0");
+  Y_REQUIRE(p->seq0 >= 0, "generate: seq0 must be >= 0");
+  Y_REQUIRE(p->mask_below >= 0 && p->mask_below < m->V(), "generate: mask_below must be in [0, %d)", m->V());
+  Y_REQUIRE(p->eos_id >= -1 && p->eos_id < m->V(), "generate: eos_id must be -1 or in [0, %d)", m->V());
+  Y_REQUIRE(p->min_tokens_before_eos >= 0, "generate: min_tokens_before_eos must be >= 0");
+  Y_CUDA(cudaSetDevice(m->device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t V = m->V();
+  const size_t logit_bytes = ((size_t)B * V * 4 + 255) / 256 * 256;
+  const size_t need = logit_bytes + (size_t)B * 4;
+  if (!m->gen || m->gen->bytes < need) {
+    if (m->gen) Y_CUDA(cudaStreamSynchronize(s));  // queued work may still read the old buffers
+    auto buf = std::make_unique<DevBuf>();
+    if (cudaMalloc(&buf->p, need) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("generate: out of device memory for %zu bytes of working buffers", need);
+      return YUF_ERR_OUT_OF_MEMORY;
+    }
+    buf->bytes = need;
+    m->gen = std::move(buf);
+  }
+  float* logits = static_cast<float*>(m->gen->p);
+  int32_t* ids = reinterpret_cast<int32_t*>(static_cast<char*>(m->gen->p) + logit_bytes);
+  Y_TRY(yuf_prefill(m, prompt_ids, B, T, slot0, logits, nullptr, stream));
+  const int eos_for_mask = p->eos_id >= 0 ? p->eos_id : 0;
+  for (int st = 0; st < n_steps; ++st) {
+    const int allow_eos = p->eos_id >= 0 && st >= p->min_tokens_before_eos;
+    Y_TRY(yuf_sample(logits, B, (int)V, p->temperature, p->top_k, p->top_p, p->seed, (uint64_t)st,
+                     p->seq0, p->mask_below, eos_for_mask, allow_eos, ids, nullptr, stream));
+    gen_record_kernel<<<(B + 127) / 128, 128, 0, s>>>(ids, tokens, lengths, B, n_steps, st, p->eos_id);
+    Y_CUDA(cudaGetLastError());
+    Y_TRY(yuf_step(m, ids, B, slot0, logits, stream));
+  }
   return YUF_OK;
 }
 

@@ -136,6 +136,37 @@ class Engine:
             _lib.call("yuf_step", self._h, ids.data_ptr(), B, slot0, logits.data_ptr(), self._stream())
         return logits
 
+    def generate(self, prompt_ids, n_steps: int, temperature: float = 1.0, top_k: int = 32,
+                 top_p: float = 1.0, seed: int = 0, seq0: int = 0, mask_below: int = 0,
+                 eos_id: int = -1, min_tokens_before_eos: int = 16, slot0: int = 0,
+                 reset: bool = True, out_tokens=None, out_lengths=None):
+        """Generate ``n_steps`` tokens per sequence on the device (C ABI
+        ``yuf_generate``): the batched decode loop of the reference's
+        ``run_generation`` (yufmusicgen/cli/generate.py:130-154).
+
+        ``prompt_ids`` [B, T] is prefilled into slots [slot0, slot0 + B), zeroed
+        first when ``reset`` (a fresh sequence, as the reference starts from no
+        state).  Returns (tokens [B, n_steps], lengths [B]) as device int32
+        tensors: a sequence ends at its first ``eos_id`` (not emitted; later
+        entries are ``eos_id``), ``lengths`` counts the tokens before it.  The
+        reference's own rule is ``mask_below=MIDI_OFFSET, eos_id=EOS,
+        min_tokens_before_eos=16`` (generate.py:142-147)."""
+        ids = self._ids(prompt_ids)
+        B, T = ids.shape
+        toks = out_tokens if out_tokens is not None else torch.empty(B, n_steps, dtype=torch.int32,
+                                                                     device=self.device)
+        lens = out_lengths if out_lengths is not None else torch.empty(B, dtype=torch.int32,
+                                                                       device=self.device)
+        p = _lib.GenerateParamsC(float(temperature), int(top_k), float(top_p),
+                                 int(seed) & (2**64 - 1), int(seq0), int(mask_below), int(eos_id),
+                                 int(min_tokens_before_eos))
+        if reset:
+            self.reset_state(slot0, B)
+        with torch.cuda.device(self.device):
+            _lib.call("yuf_generate", self._h, ids.data_ptr(), B, T, slot0, int(n_steps),
+                      ctypes.byref(p), toks.data_ptr(), lens.data_ptr(), self._stream())
+        return toks, lens
+
     def set_decode_graphs(self, enabled: bool = True):
         """Replay decode steps as CUDA graphs (needs a non-default stream)."""
         _lib.call("yuf_model_set_decode_graphs", self._h, 1 if enabled else 0)
