@@ -403,6 +403,56 @@ __global__ void __launch_bounds__(128)
   if (i < R && m_out) m_out[(size_t)b * R + i] = m;
 }
 
+// The same carry with A^K held in registers, for R in {32, 64, 128}: the thread
+// pair (2i, 2i + 1) owns row i of A^K, each thread half of its columns (R/2
+// registers), so a chunk step reads only m from shared memory (R/8 LDS.128 per
+// thread, every lane of a warp at the same address), sums its half row in eight
+// chains and combines the pair with one shuffle.  m is double buffered, so a
+// step needs one barrier: a buffer is written again only two steps later, after
+// every thread has passed the barrier that follows its reads.
+template <int R>
+__global__ void __launch_bounds__(2 * R)
+    rosa_carry_reg_kernel(const float* __restrict__ AKt, const float* __restrict__ z,
+                          const float* m0, float* __restrict__ m_start, float* m_out, int C) {
+  constexpr int HALF = R / 2;
+  static_assert(R % 32 == 0 && R <= 128, "register carry: R in {32, 64, 128}");
+  __shared__ __align__(16) float mv[2][R];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int i = tid >> 1, half = tid & 1, j0 = half * HALF;
+  float arow[HALF];
+#pragma unroll
+  for (int c = 0; c < HALF; ++c) arow[c] = AKt[(size_t)(j0 + c) * R + i];  // (A^K)[i][j0 + c]
+  float mi = m0 ? m0[(size_t)b * R + i] : 0.f;
+  float zc = C > 0 ? z[(size_t)b * C * R + i] : 0.f;  // z of the current chunk
+  for (int c = 0; c < C; ++c) {
+    const size_t row = ((size_t)b * C + c) * R;
+    const float zn = c + 1 < C ? z[row + R + i] : 0.f;  // next chunk's z, in flight
+    float* mb = mv[c & 1];
+    if (half == 0) {
+      m_start[row + i] = mi;
+      mb[i] = mi;
+    }
+    __syncthreads();
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+#pragma unroll
+    for (int q = 0; q < HALF / 4; ++q) {
+      const float4 mm = *reinterpret_cast<const float4*>(mb + j0 + 4 * q);
+      const int a = (2 * q) & 7;
+      acc[a] = fmaf(arow[4 * q + 0], mm.x, acc[a]);
+      acc[a + 1] = fmaf(arow[4 * q + 1], mm.y, acc[a + 1]);
+      acc[a] = fmaf(arow[4 * q + 2], mm.z, acc[a]);
+      acc[a + 1] = fmaf(arow[4 * q + 3], mm.w, acc[a + 1]);
+    }
+    float s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    mi = s + zc;
+    zc = zn;
+  }
+  if (half == 0 && m_out) m_out[(size_t)b * R + i] = mi;
+}
+
 // R > 128: A^K (R x R) does not fit in shared memory, but it is a diagonal plus
 // a rank-K matrix.  With A = D (I - 2 d d^T):
 //   A^K x = D^K x - 2 sum_{s=1..K} p_s D^{K-s+1} d,   p_s = d^T A^{s-1} x,
@@ -557,7 +607,11 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
                         nullptr, z, B * C, K, R, s);
   // 3. carry across chunks
   const int threads = ((R + 31) / 32) * 32;
-  if (R <= 128) {
+  if (R == 32 || R == 64 || R == 128) {
+    if (R == 32) rosa_carry_reg_kernel<32><<<B, 64, 0, s>>>(AKt, z, m0, m_start, m_out, C);
+    else if (R == 64) rosa_carry_reg_kernel<64><<<B, 128, 0, s>>>(AKt, z, m0, m_start, m_out, C);
+    else rosa_carry_reg_kernel<128><<<B, 256, 0, s>>>(AKt, z, m0, m_start, m_out, C);
+  } else if (R <= 128) {
     const size_t sm = ((size_t)R * R + R) * sizeof(float);
     if (sm > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(rosa_carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
