@@ -72,6 +72,15 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def bf16_peak():
+    """Measured bf16 dense TFLOP/s (sustained: the prefill is a long step)."""
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d.get("bf16_tflops_sustained", d["bf16_tflops"]))
+    return 1400.0
+
+
 def profiled_traffic():
     """DRAM bytes of one headline step (all of its kernels) from the committed
     ncu summary of the time-parallel scan on the config-2 workload."""
@@ -99,6 +108,41 @@ def cpu_oracle_run(n_batch, seconds, threads=None):
         if el >= seconds:
             break
     return n_batch * T * reps / el, reps, el
+
+
+def cpu_model_baseline():
+    """The whole model on the host cores: the numpy port of YufMusicGen.forward /
+    .step (oracle/model.py, the reference's use_rosa_scan=False CPU path) on
+    bounded samples of benchmark configs 3 (prefill) and 4 (decode)."""
+    from oracle.model import OracleModel
+    from yufmusicgen_b200 import config as C
+    from yufmusicgen_b200.weights import init_weights
+    from yufmusicgen_b200.workloads import zipf_ids
+
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((d.get("num_threads", 1) for d in threadpool_info()), default=1)
+    except Exception:  # pragma: no cover - threadpoolctl is optional
+        threads = os.cpu_count()
+    cfg = C.ModelConfig(**C.BASE_0P1B)
+    om = OracleModel(cfg, init_weights(cfg, 1, "baseline"))
+    ids = zipf_ids(1, 512, seed=1, vocab=cfg.vocab_size)
+    t0 = time.perf_counter()
+    om.forward(ids)
+    pf = 512 / (time.perf_counter() - t0)
+    seqs, steps = 32, 8
+    logits, st = om.forward(zipf_ids(seqs, C4_PROMPT, seed=4, vocab=cfg.vocab_size))
+    tok = np.argmax(logits[:, -1], axis=-1)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        last, st = om.step(tok, st)
+        tok = np.argmax(last, axis=-1)
+    dec = seqs * steps / (time.perf_counter() - t0)
+    return {"prefill_c3_tokens_per_s": pf, "decode_c4_tokens_per_s": dec, "unit": "tokens/s",
+            "cores": threads, "kind": "port",
+            "sample": "config-3 model (fp32): prefill of 1 x 512 tokens; greedy decode of 32 of "
+                      "config 4's sequences x 8 steps after their 64-token prompts; numpy port "
+                      "of the reference's CPU forward/step"}
 
 
 def run_reference(args):
@@ -348,9 +392,11 @@ def measure_sharded(dev, rank, world, barrier, max_over_ranks):
     del eng
     tokens = world * C5_SEQS_PER_GPU * C5_T
     flop = 915e6 * tokens  # about 2 x linear parameters + LM head per token
+    tflops = flop / world / (ms * 1e-3) / 1e12
     res["prefill_c5_bf16"] = {"ms": ms, "tokens_per_s": tokens / (ms * 1e-3),
                               "sequences": world * C5_SEQS_PER_GPU, "seq_len": C5_T,
-                              "TFLOPs_per_gpu": flop / world / (ms * 1e-3) / 1e12}
+                              "TFLOPs_per_gpu": tflops,
+                              "tensor_frac_per_gpu": tflops / bf16_peak()}
     return res
 
 
@@ -554,6 +600,7 @@ def run_ours(args):
                 "value": v, "unit": UNIT, "cores": cref.threads_default(), "kind": "port",
                 "sample": f"full config-2 workload x{reps} ({el:.1f} s); C port of the reference "
                           "recurrence, OpenMP over (b,h)"}
+            line["cpu_baseline_model"] = cpu_model_baseline()
         print(json.dumps(line), flush=True)
     if dist:
         torch.distributed.destroy_process_group()

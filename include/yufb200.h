@@ -71,9 +71,12 @@ enum {
                              else sequential                                                    */
   YUF_WKV_SEQUENTIAL = 1, /* token by token, one CTA per (sequence, head)                         */
   YUF_WKV_CHUNKED = 2,    /* 16-token chunks, no per-token reduction chain                        */
-  YUF_WKV_PARALLEL = 3    /* chunks scanned in parallel (about one wave of blocks), states
+  YUF_WKV_PARALLEL = 3,   /* chunks scanned in parallel (about one wave of blocks), states
                              carried between them; takes stream-ordered scratch for the chunk
                              transitions from a library-owned pool that keeps its pages; T >= 256 */
+  YUF_WKV_PARALLEL_TC = 4 /* YUF_WKV_PARALLEL with the output correction y += S0 q_t on the
+                             tcgen05 tensor cores (TMEM accumulators, 3xTF32) for N <= 64;
+                             today slower than the default mma.sync correction            */
 };
 /* yuf_wkv7_forward with an explicit algorithm (same results to fp32 rounding). */
 yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k, const float* v,

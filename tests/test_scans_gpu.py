@@ -224,13 +224,17 @@ def test_torch_op_drop_in_rosa_forward():
     close(mem_saved[:, 20], m_half)
 
 
+PAR_ALGOS = [cuda_ops.ALGO_PARALLEL, cuda_ops.ALGO_PARALLEL_TC]
+
+
+@pytest.mark.parametrize("algo", PAR_ALGOS)
 @pytest.mark.parametrize("T", [256, 300, 1000])
 @pytest.mark.parametrize("N", [16, 40, 64, 128])
-def test_wkv7_time_parallel_matches_oracle(T, N):
-    """Chunks scanned in parallel with carried states (the last chunk ragged)."""
+def test_wkv7_time_parallel_matches_oracle(T, N, algo):
+    """Chunks scanned in parallel with carried states (the last chunk ragged);
+    the output correction on mma.sync or on the tcgen05 tensor cores."""
     ins = wkv_op_inputs(2, T, 3, N, seed=500 + T + N, with_state=True)
-    y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=cu(ins["s0"]),
-                                 algo=cuda_ops.ALGO_PARALLEL)
+    y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=cu(ins["s0"]), algo=algo)
     yr, sr = cref.wkv7_scan(*(ins[k] for k in "rwkvab"), ins["s0"])
     close(y, yr)
     close(s, sr)
@@ -243,12 +247,14 @@ def test_wkv7_time_parallel_matches_oracle(T, N):
     (2, 1000, 2, 96, True),
     (1, 777, 1, 16, True),
     (40, 256, 16, 40, True),  # many chains: two chunks per sequence
+    (16, 1024, 4, 64, True),  # chunks of 208 tokens: two 128-token correction tiles each
+    (48, 600, 4, 16, False),  # chunks of 304 tokens: three tiles, the last one ragged
 ])
-def test_wkv7_time_parallel_shapes(B, T, H, N, with_state):
+@pytest.mark.parametrize("algo", PAR_ALGOS)
+def test_wkv7_time_parallel_shapes(B, T, H, N, with_state, algo):
     ins = wkv_op_inputs(B, T, H, N, seed=900 + B + T + N, with_state=with_state)
     s0 = cu(ins["s0"]) if with_state else None
-    y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=s0,
-                                 algo=cuda_ops.ALGO_PARALLEL)
+    y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=s0, algo=algo)
     yr, sr = cref.wkv7_scan(*(ins[k] for k in "rwkvab"), ins["s0"] if with_state else None)
     close(y, yr)
     close(s, sr)
@@ -287,11 +293,11 @@ def test_wkv7_decode_many_heads_per_cta(B, H, N):
     assert _lib.wait_timeouts() == 0
 
 
-def test_wkv7_time_parallel_full_config2_and_inplace_state():
+@pytest.mark.parametrize("algo", PAR_ALGOS)
+def test_wkv7_time_parallel_full_config2_and_inplace_state(algo):
     ins = wkv_op_inputs(8, 2048, 16, 40, seed=0, with_state=True)
     st = cu(ins["s0"])
-    y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=st, state_out=st,
-                                 algo=cuda_ops.ALGO_PARALLEL)
+    y, s = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), state=st, state_out=st, algo=algo)
     yr, sr = cref.wkv7_scan(*(ins[k] for k in "rwkvab"), ins["s0"])
     close(y, yr)
     close(st, sr)

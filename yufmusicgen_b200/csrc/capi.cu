@@ -154,14 +154,16 @@ yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k,
   yuf_status_t st = check_wkv_args(in, 7, B, T, H, N);
   if (st != YUF_OK) return st;
   REQUIRE(aligned(s0, 8) && aligned(s_out, 8), "wkv7: state buffers must be 8-byte aligned");
-  REQUIRE(algo >= YUF_WKV_AUTO && algo <= YUF_WKV_PARALLEL, "wkv7: unknown algorithm %d", algo);
-  REQUIRE(algo != YUF_WKV_PARALLEL || T >= 256, "wkv7: the time-parallel scan needs T >= 256 (T=%d)", T);
+  REQUIRE(algo >= YUF_WKV_AUTO && algo <= YUF_WKV_PARALLEL_TC, "wkv7: unknown algorithm %d", algo);
+  REQUIRE((algo != YUF_WKV_PARALLEL && algo != YUF_WKV_PARALLEL_TC) || T >= 256,
+          "wkv7: the time-parallel scan needs T >= 256 (T=%d)", T);
   if (B == 0 || H == 0) return YUF_OK;
   cudaStream_t st_ = static_cast<cudaStream_t>(stream);
   if (T == 1 && algo != YUF_WKV_CHUNKED)
     return wkv7_decode_dispatch(r, w, k, v, a, b, s0, y, s_out, B * H, N, st_);
   if (algo == YUF_WKV_CHUNKED) return wkv7_chunk_dispatch(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, st_);
-  if (algo == YUF_WKV_PARALLEL || (algo == YUF_WKV_AUTO && wkv7_parallel_applies(B, T, H, N))) {
+  if (algo == YUF_WKV_PARALLEL || algo == YUF_WKV_PARALLEL_TC ||
+      (algo == YUF_WKV_AUTO && wkv7_parallel_applies(B, T, H, N))) {
     // stream-ordered scratch for the chunk transitions, released right after use
     const size_t bytes = wkv7_parallel_scratch_floats(B, T, H, N) * sizeof(float);
     void* scratch = nullptr;
@@ -171,7 +173,7 @@ yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k,
       return YUF_ERR_OUT_OF_MEMORY;
     }
     yuf_status_t rc = wkv7_parallel(r, w, k, v, a, b, s0, y, s_out, B, T, H, N,
-                                    static_cast<float*>(scratch), st_);
+                                    static_cast<float*>(scratch), st_, algo == YUF_WKV_PARALLEL_TC);
     scratch_free(scratch, st_);
     return rc;
   }

@@ -62,5 +62,6 @@ size_t wkv7_parallel_scratch_floats(int B, int T, int H, int N);
 size_t wkv7_parallel_scratch_bound(size_t rows, int H, int N);
 yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
-                           int B, int T, int H, int N, float* scratch, cudaStream_t st);
+                           int B, int T, int H, int N, float* scratch, cudaStream_t st,
+                           bool tc_correct = false);
 }  // namespace yuf

@@ -1,0 +1,85 @@
+// 5th-generation tensor core (tcgen05) helpers for sm_100a kernels: tensor
+// memory (TMEM) allocation, UMMA shared-memory and instruction descriptors, the
+// kind::tf32 MMA, its commit to an mbarrier and the TMEM -> register load.
+// Layouts follow the PTX ISA's tcgen05 chapter; field positions match the
+// UMMA descriptors of CUTLASS's cute/arch/mma_sm100_desc.hpp.
+#pragma once
+#include <cstdint>
+
+#include "mbarrier.cuh"
+
+namespace yuf {
+
+// ---- tensor memory ---------------------------------------------------------
+// One full warp allocates `cols` columns (a power of two >= 32) for all 128
+// lanes and writes the TMEM address into shared memory at `slot`.
+YUF_DEVICE void tmem_alloc(uint32_t* slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(cols)
+               : "memory");
+}
+// Let other CTAs on this SM allocate (same warp as the allocation).
+YUF_DEVICE void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+YUF_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+// Order tcgen05 operations around a CTA barrier (before: issue side, after: wait side).
+YUF_DEVICE void tc_fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+YUF_DEVICE void tc_fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---- descriptors -----------------------------------------------------------
+// Shared-memory matrix descriptor, K-major operand without swizzle: the tile is
+// made of core matrices of 8 rows x 16 bytes (128 contiguous bytes); `lbo` is
+// the byte distance between core matrices adjacent in K, `sbo` between core
+// matrices adjacent in M/N (the next 8 rows).  Addresses and offsets are 16-byte
+// multiples; bits 46-47 hold the descriptor version (1 on sm_100).
+YUF_DEVICE uint64_t umma_desc_kmajor(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor of a dense kind::tf32 MMA with fp32 accumulators,
+// both operands K-major: D format f32 (bits 4-5 = 1), A and B tf32 (bits 7-9 and
+// 10-12 = 2), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
+constexpr uint32_t umma_idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---- MMA -------------------------------------------------------------------
+// D[tmem] (+)= A . B^T, issued by ONE thread; accumulate = 0 overwrites D.
+YUF_DEVICE void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+// Arrive on `bar` once every MMA this thread issued so far has completed.
+YUF_DEVICE void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// ---- TMEM -> registers -----------------------------------------------------
+// The warp's 32 lanes starting at the lane field of `taddr` (a warp may only
+// read its own quarter of the lanes: 32 * (warp % 4)), 8 consecutive 32-bit
+// columns each: thread t of the warp receives lane (base + t).  The load and its
+// completion wait (tcgen05.wait::ld) sit in one asm statement, so no instruction
+// can touch the destination registers before they are valid.
+YUF_DEVICE void tmem_ld_x8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace yuf

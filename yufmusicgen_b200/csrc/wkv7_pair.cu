@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "mbarrier.cuh"
+#include "tcgen05.cuh"
 
 namespace yuf {
 
@@ -260,7 +261,7 @@ __global__ void __launch_bounds__(PairCfg<N>::NT, 1)
 // lane layout, then the next group's copy starts while this group is scanned;
 // single buffers keep the block small (15 KB at N = 40, 12 warps per SM).
 #ifndef YUF_PAIRW_UNROLL
-#define YUF_PAIRW_UNROLL 4
+#define YUF_PAIRW_UNROLL 8
 #endif
 constexpr int PAIRW_UNROLL = YUF_PAIRW_UNROLL;  // token loop unroll: code size vs. scheduling
 
@@ -307,8 +308,11 @@ YUF_DEVICE void load_cols(float2 (&dst)[C / 2], const float* p) {
   if constexpr (C % 4 != 0) dst[C / 2 - 1] = *reinterpret_cast<const float2*>(p + C - 2);
 }
 
+#ifndef YUF_PAIRW_MINB
+#define YUF_PAIRW_MINB 1  // minimum resident blocks per SM the register budget is set for
+#endif
 template <int N>
-__global__ void __launch_bounds__(PairWCfg<N>::NT)
+__global__ void __launch_bounds__(PairWCfg<N>::NT, YUF_PAIRW_MINB)
     wkv7_pairw_kernel(const float* __restrict__ r, const float* __restrict__ w,
                       const float* __restrict__ k, const float* __restrict__ v,
                       const float* __restrict__ a, const float* __restrict__ b,
@@ -651,6 +655,165 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The same correction on the 5th-generation tensor cores (N <= 64): per block a
+// tile of up to 128 tokens of one (chunk, head) as one UMMA problem,
+//   D[128 x NM] = A[128 x N] . B[NM x N]^T,   A = the tile's q rows,
+//   B = S0 (rows past N zero; NM = N rounded up to 16),
+// accumulated in tensor memory (TMEM lane = token row, column = output i).
+// fp32 accuracy by 3xTF32: D = Alo Bhi + Ahi Blo + Ahi Bhi, three kind::tf32
+// MMAs per 8-wide k-step into the one accumulator.  Operands sit in shared memory
+// in the canonical K-major layout without swizzle (8-row x 16-byte core matrices;
+// the K-adjacent core matrix 128 bytes on, the next 8 rows N/4 * 128 bytes on),
+// written by the threads that load them (each thread one token row of A) after
+// the tf32 split.  One thread issues the MMAs and commits them to an mbarrier;
+// every warp then reads its 32 TMEM lanes and adds them to its tokens' y rows,
+// which were loaded while the operands were staged.  The wait is bounded
+// (WAIT_NS; an expiry is counted in g_pair_wait_timeouts, waited for once more
+// and the block's outputs are void), and the TMEM columns are always freed.
+// Measured on config 2 it is not yet faster than the mma.sync kernel (shared
+// memory holds it to 4 blocks per SM and each block runs load, split, MMA and
+// epilogue back to back), so it serves the explicit YUF_WKV_PARALLEL_TC choice.
+template <int N>
+struct CorrTcCfg {
+  static constexpr int M = 128;                  // tokens per tile = TMEM lanes
+  static constexpr int NM = (N + 15) / 16 * 16;  // MMA N: S0 rows, zero padded
+  static constexpr int KC = N / 4;               // 16-byte chunks per operand row
+  static constexpr uint32_t LBO = 128;           // next core matrix along K
+  static constexpr uint32_t SBO = KC * 128;      // next 8 rows
+  static constexpr int A_BYTES = M * N * 4;
+  static constexpr int B_BYTES = NM * N * 4;
+  static constexpr int OFF_AH = 0, OFF_AL = A_BYTES;
+  static constexpr int OFF_BH = 2 * A_BYTES, OFF_BL = 2 * A_BYTES + B_BYTES;
+  static constexpr int OFF_BAR = 2 * A_BYTES + 2 * B_BYTES;  // 16-byte multiple
+  static constexpr int OFF_SLOT = OFF_BAR + 8;
+  static constexpr size_t BYTES = OFF_SLOT + 8 + 128;        // + alignment slack of the base
+  static constexpr uint32_t TMEM_COLS = NM <= 32 ? 32 : 64;
+  static constexpr uint32_t IDESC = umma_idesc_tf32(M, NM);
+  static_assert(N % 8 == 0 && N <= 64, "tcgen05 correction: N in {16, 32, 40, 48, 64}");
+};
+
+// byte offset of the 16-byte chunk c (elements 4c .. 4c+3) of operand row r
+template <int N>
+YUF_DEVICE uint32_t corr_tc_off(int r, int c) {
+  return (uint32_t)((r & 7) * 16 + c * 128 + (r >> 3) * (int)CorrTcCfg<N>::SBO);
+}
+
+YUF_DEVICE void split4(const float4 x, uint4& hi, uint4& lo) {
+  split_tf32(x.x, hi.x, lo.x);
+  split_tf32(x.y, hi.y, lo.y);
+  split_tf32(x.z, hi.z, lo.z);
+  split_tf32(x.w, hi.w, lo.w);
+}
+
+template <int N>
+__global__ void __launch_bounds__(128)
+    wkv7_correct_tc_kernel(const float* __restrict__ S0, const float* __restrict__ Q,
+                           float* __restrict__ y, int K_, int H, int Tstride, int Cper, int skip_first,
+                           int parts) {
+  using Cf = CorrTcCfg<N>;
+  constexpr int KC = Cf::KC;
+  extern __shared__ __align__(128) unsigned char corr_tc_raw[];
+  unsigned char* sm = corr_tc_raw + ((128u - (smem_u32(corr_tc_raw) & 127u)) & 127u);
+  const int bh = blockIdx.x / parts, part = blockIdx.x - bh * parts;
+  const int bb = bh / H, hh = bh - bb * H;
+  if (skip_first && bb % Cper == 0) return;  // chunk 0 starts from the zero state
+  const int tb = part * Cf::M;               // first token of this tile in the chunk
+  const int T = min(Cf::M, item_len(bb, K_, Tstride, Cper) - tb);
+  if (T <= 0) return;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + Cf::OFF_BAR);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(sm + Cf::OFF_SLOT);
+
+  if (warp == 0) {
+    tmem_alloc(slot, Cf::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  // this thread's token row: its y row is loaded now and added after the MMAs
+  const int row = tid;
+  const bool live = row < T;
+  const size_t tok_stride = (size_t)H * N;
+  float* yrow = y + item_head_off(bb, hh, K_, H, N, Tstride, Cper) + (size_t)(tb + (live ? row : 0)) * tok_stride;
+  float4 yv[KC];
+#pragma unroll
+  for (int c = 0; c < KC; ++c)
+    yv[c] = live ? reinterpret_cast<const float4*>(yrow)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+  // A: the tile's q rows (rows past T zero), split into tf32 high and low parts
+  const float4* qrow = reinterpret_cast<const float4*>(Q + ((size_t)bh * K_ + tb + (live ? row : 0)) * N);
+#pragma unroll
+  for (int c = 0; c < KC; ++c) {
+    const float4 x = live ? qrow[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint4 hi, lo;
+    split4(x, hi, lo);
+    const uint32_t o = corr_tc_off<N>(row, c);
+    *reinterpret_cast<uint4*>(sm + Cf::OFF_AH + o) = hi;
+    *reinterpret_cast<uint4*>(sm + Cf::OFF_AL + o) = lo;
+  }
+  // B: S0 of this (chunk, head), rows N .. NM-1 zero
+  const float4* s0 = reinterpret_cast<const float4*>(S0 + (size_t)bh * N * N);
+  for (int x = tid; x < Cf::NM * KC; x += 128) {
+    const int i = x / KC, c = x - i * KC;
+    const float4 v = i < N ? s0[i * KC + c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint4 hi, lo;
+    split4(v, hi, lo);
+    const uint32_t o = corr_tc_off<N>(i, c);
+    *reinterpret_cast<uint4*>(sm + Cf::OFF_BH + o) = hi;
+    *reinterpret_cast<uint4*>(sm + Cf::OFF_BL + o) = lo;
+  }
+  fence_proxy_async();  // the operand stores become visible to the tensor core
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *slot;
+  if (tid == 0) {
+    const uint32_t ah = smem_u32(sm + Cf::OFF_AH), al = smem_u32(sm + Cf::OFF_AL);
+    const uint32_t bh_ = smem_u32(sm + Cf::OFF_BH), bl = smem_u32(sm + Cf::OFF_BL);
+#pragma unroll
+    for (int s = 0; s < N / 8; ++s) {
+      const uint32_t k = (uint32_t)s * 2 * Cf::LBO;  // two 16-byte chunks per k-step
+      umma_tf32(tmem, umma_desc_kmajor(al + k, Cf::LBO, Cf::SBO), umma_desc_kmajor(bh_ + k, Cf::LBO, Cf::SBO),
+                Cf::IDESC, s > 0 ? 1u : 0u);
+      umma_tf32(tmem, umma_desc_kmajor(ah + k, Cf::LBO, Cf::SBO), umma_desc_kmajor(bl + k, Cf::LBO, Cf::SBO),
+                Cf::IDESC, 1u);
+      umma_tf32(tmem, umma_desc_kmajor(ah + k, Cf::LBO, Cf::SBO), umma_desc_kmajor(bh_ + k, Cf::LBO, Cf::SBO),
+                Cf::IDESC, 1u);
+    }
+    umma_commit(bar);
+  }
+  __syncwarp();
+  bool done = mbar_wait(bar, 0);
+  done = __all_sync(0xffffffffu, done);
+  if (!done) {
+    if ((tid & 31) == 0) atomicAdd(&g_pair_wait_timeouts, 1u);
+    mbar_wait(bar, 0);  // once more, bounded, before the columns are freed
+  } else {
+    tc_fence_after_sync();
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll
+    for (int c8 = 0; c8 < N / 8; ++c8) {
+      float d[8];
+      tmem_ld_x8(lane_base + (uint32_t)(c8 * 8), d);
+      float4& y0 = yv[2 * c8];
+      float4& y1 = yv[2 * c8 + 1];
+      y0.x += d[0]; y0.y += d[1]; y0.z += d[2]; y0.w += d[3];
+      y1.x += d[4]; y1.y += d[5]; y1.z += d[6]; y1.w += d[7];
+    }
+    if (live) {
+#pragma unroll
+      for (int c = 0; c < KC; ++c) reinterpret_cast<float4*>(yrow)[c] = yv[c];
+    }
+  }
+  tc_fence_before_sync();
+  __syncthreads();  // every warp's TMEM reads are done
+  if (warp == 0) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, Cf::TMEM_COLS);
+  }
+}
+
 // Resident pair blocks per device for head size N (blocks per SM x SMs),
 // queried once per (device, N).
 int wkv7_pair_slots(int N) {
@@ -799,7 +962,28 @@ yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, 
 }
 
 yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, int items, int K, int H,
-                                   int N, int Tstride, int Cper, bool skip_first, cudaStream_t st) {
+                                   int N, int Tstride, int Cper, bool skip_first, bool tc, cudaStream_t st) {
+  if (tc) switch (N) {  // head sizes up to 64 on request: the tcgen05 kernel
+#define CASE_TC(NN)                                                                                \
+  case NN: {                                                                                       \
+    auto kern = wkv7_correct_tc_kernel<NN>;                                                        \
+    const size_t tb = CorrTcCfg<NN>::BYTES;                                                        \
+    if (tb > 48 * 1024 &&                                                                          \
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tb) !=        \
+            cudaSuccess) {                                                                         \
+      set_error("wkv7 correct: cudaFuncSetAttribute failed");                                     \
+      return YUF_ERR_CUDA;                                                                         \
+    }                                                                                              \
+    const int parts = (K + CorrTcCfg<NN>::M - 1) / CorrTcCfg<NN>::M;                               \
+    kern<<<items * H * parts, 128, tb, st>>>(S0, Q, y, K, H, Tstride, Cper, skip_first ? 1 : 0,    \
+                                             parts);                                               \
+    return check_launch("wkv7_correct_tc_kernel");                                                 \
+  }
+    CASE_TC(16) CASE_TC(32) CASE_TC(40) CASE_TC(48) CASE_TC(64)
+#undef CASE_TC
+    default:
+      break;
+  }
   const size_t bytes = ((size_t)2 * N + 80) * (N + 4) * sizeof(float);
   switch (N) {
 #define CASE(NN)                                                                                   \

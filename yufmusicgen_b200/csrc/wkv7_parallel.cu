@@ -35,7 +35,7 @@ yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, 
                                 const float* a, const float* b, float* y, float* Q, float* U, float* P,
                                 int items, int K, int H, int N, int Tstride, int Cper, cudaStream_t st);
 yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, int items, int K, int H,
-                                   int N, int Tstride, int Cper, bool skip_first, cudaStream_t st);
+                                   int N, int Tstride, int Cper, bool skip_first, bool tc, cudaStream_t st);
 int wkv7_pair_slots(int N);
 int wkv7_correct_max_chunk(int N);
 
@@ -234,7 +234,7 @@ size_t wkv7_parallel_scratch_bound(size_t rows, int H, int N) {
 
 yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
-                           int B, int T, int H, int N, float* scratch, cudaStream_t st) {
+                           int B, int T, int H, int N, float* scratch, cudaStream_t st, bool tc_correct) {
   int C = 0, K = 0;
   wkv7_parallel_plan(B, T, H, N, &C, &K);
   const size_t per = (size_t)B * C * H * N * N;
@@ -257,7 +257,7 @@ yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const
   }
   if (rc != YUF_OK) return rc;
   // 3. y += S_start q_t per (chunk, head); chunk 0 of a zero start needs none
-  return wkv7_correct_dispatch(S_start, Qm, y, B * C, K, H, N, T, C, s0 == nullptr, st);
+  return wkv7_correct_dispatch(S_start, Qm, y, B * C, K, H, N, T, C, s0 == nullptr, tc_correct, st);
 }
 
 }  // namespace yuf
