@@ -198,7 +198,9 @@ static size_t ws_floats_per_row(const yuf_model* m) {
 // Scratch of the time-parallel scans for a forward over `rows` token rows.
 static size_t scan_rosa_floats(const yuf_model* m, size_t rows) {
   const size_t R = m->R();
-  return (R * R + 2 * (rows / 32 + 1) * R + 3) / 4 * 4;  // keep the WKV part 16-byte aligned
+  // A^K, chunk end and start states, the layer's coefficient block (32 + 2R);
+  // rounded so the WKV part stays 16-byte aligned
+  return (R * R + 2 * (rows / 32 + 1) * R + 32 + 2 * R + 3) / 4 * 4;
 }
 
 static size_t scan_scratch_floats(const yuf_model* m, size_t rows) {

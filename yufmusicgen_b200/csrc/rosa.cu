@@ -37,6 +37,71 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
                            float* read, float* m_out, int B, int T, int R, bool gated,
                            float* scratch, cudaStream_t s);
 
+// Per-layer constants of the scan for channel j of a block of `nwarps` warps:
+// the unit direction d_j and post-sigmoid decay dec_j (from the raw parameters
+// when raw != 0: decay = sigmoid(decay_param), d = normalize(householder),
+// yufmusicgen/model.py:300-301) and the L+1 coefficients q_n of the inverse
+// Toeplitz matrix (I + 2C)^{-1}, c_k = sum_j d_j^2 dec_j^k:
+//   q_0 = 1,  q_n = -2 sum_{k=1..n} c_k q_{n-k}.
+// Every thread of the block calls it (it holds block reductions and barriers).
+constexpr int ROSA_COEF_D = 32;  // coefficient block: q [L+1] (padded to 32), d [R], dec [R]
+YUF_DEVICE void rosa_setup(int j, int R, int nwarps, const float* __restrict__ decay,
+                           const float* __restrict__ dir, int raw, float* scratch, float* c_sum,
+                           float* q, float& d, float& dec, float (&qr)[ROSA_L + 1]) {
+  constexpr int L = ROSA_L;
+  const bool act = j < R;
+  d = act ? dir[j] : 0.f;
+  dec = act ? decay[j] : 0.f;
+  if (raw) {
+    dec = act ? 1.f / (1.f + expf(-dec)) : 0.f;
+    float x1[1] = {d * d};
+    block_sum_array<1>(x1, scratch, c_sum, nwarps);
+    d = d / fmaxf(sqrtf(c_sum[0]), 1e-12f);
+  }
+  {  // c_k, k = 1..L (index 0 unused)
+    float x[L + 1];
+    float pw = d * d;
+    x[0] = 0.f;
+#pragma unroll
+    for (int kk = 1; kk <= L; ++kk) {
+      pw *= dec;
+      x[kk] = pw;
+    }
+    block_sum_array<L + 1>(x, scratch, c_sum, nwarps);
+  }
+  if (j == 0) {
+    q[0] = 1.f;
+    for (int n = 1; n <= L; ++n) {
+      float acc = 0.f;
+      for (int kk = 1; kk <= n; ++kk) acc += c_sum[kk] * q[n - kk];
+      q[n] = -2.f * acc;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int n = 0; n <= L; ++n) qr[n] = q[n];
+}
+
+// The setup once per launch of the time-parallel scan (one block of the scan
+// kernels' width, so the reductions add in the same order): coef = [q (padded
+// to ROSA_COEF_D), d (R), dec (R)], read by every chunk's block instead of
+// repeating two block reductions and the serial solve.
+__global__ void __launch_bounds__(1024)
+    rosa_coef_kernel(const float* __restrict__ decay, const float* __restrict__ dir, int raw, int R,
+                     float* __restrict__ coef) {
+  __shared__ float scratch[32 * (ROSA_L + 1)];
+  __shared__ float c_sum[ROSA_L + 1];
+  __shared__ float q[ROSA_L + 1];
+  const int j = threadIdx.x;
+  float d, dec, qr[ROSA_L + 1];
+  rosa_setup(j, R, blockDim.x >> 5, decay, dir, raw, scratch, c_sum, q, d, dec, qr);
+  if (j <= ROSA_L) coef[j] = qr[j];
+  if (j < R) {
+    coef[ROSA_COEF_D + j] = d;
+    coef[ROSA_COEF_D + R + j] = dec;
+  }
+}
+
 // MODE 0: the scan.  MODE 1: end state only, from a zero initial state (no read
 // output).  MODE 2: transition -- batch row bb starts from the unit vector e_bb
 // with zero input for T steps, so m_out row bb = A^T e_bb, i.e. column bb of
@@ -50,7 +115,8 @@ __global__ void __launch_bounds__(MAXT)
                      float* __restrict__ read_saved, float* __restrict__ gate_saved,
                      float* __restrict__ decay_saved, float* __restrict__ mem_saved, int T, int R,
                      int ld, const float* __restrict__ bias_c, const float* __restrict__ bias_w,
-                     const float* __restrict__ bias_g, int raw_params) {
+                     const float* __restrict__ bias_g, int raw_params,
+                     const float* __restrict__ coef = nullptr) {
   constexpr int L = ROSA_L;
   __shared__ float scratch[32 * (L + 1)];
   __shared__ float s_sum[L + 1];
@@ -61,46 +127,20 @@ __global__ void __launch_bounds__(MAXT)
   const int j = threadIdx.x;
   const int nwarps = blockDim.x >> 5;
   const bool act = j < R;
-  float d = act ? dir[j] : 0.f;
-  float dec = act ? decay[j] : 0.f;
-  if (raw_params) {
-    // engine path: decay = sigmoid(decay_param), d = normalize(householder)
-    // (yufmusicgen/model.py:300-301)
-    dec = act ? 1.f / (1.f + expf(-dec)) : 0.f;
-    float x1[1] = {d * d};
-    block_sum_array<1>(x1, scratch, c_sum, nwarps);
-    d = d / fmaxf(sqrtf(c_sum[0]), 1e-12f);
+  // direction, decay and the Toeplitz inverse: precomputed for the launch
+  // (rosa_coef_kernel, the time-parallel scan) or set up here
+  float d, dec, qr[L + 1];
+  if (coef != nullptr) {
+    d = act ? coef[ROSA_COEF_D + j] : 0.f;
+    dec = act ? coef[ROSA_COEF_D + R + j] : 0.f;
+#pragma unroll
+    for (int n = 0; n <= L; ++n) qr[n] = coef[n];
+  } else {
+    rosa_setup(j, R, nwarps, decay, dir, raw_params, scratch, c_sum, q, d, dec, qr);
   }
   const float bc = (act && bias_c) ? bias_c[j] : 0.f;
   const float bw = (act && bias_w) ? bias_w[j] : 0.f;
   const float bg = (act && bias_g) ? bias_g[j] : 0.f;
-
-  // c_k = sum_j d_j^2 decay_j^k, k = 1..L (index 0 unused).
-  {
-    float x[L + 1];
-    float pw = d * d;
-    x[0] = 0.f;
-#pragma unroll
-    for (int kk = 1; kk <= L; ++kk) {
-      pw *= dec;
-      x[kk] = pw;
-    }
-    block_sum_array<L + 1>(x, scratch, c_sum, nwarps);
-  }
-  // Inverse of the unit lower-triangular Toeplitz (I + 2C): q_0 = 1,
-  // q_n = -2 sum_{k=1..n} c_k q_{n-k}.
-  if (j == 0) {
-    q[0] = 1.f;
-    for (int n = 1; n <= L; ++n) {
-      float acc = 0.f;
-      for (int kk = 1; kk <= n; ++kk) acc += c_sum[kk] * q[n - kk];
-      q[n] = -2.f * acc;
-    }
-  }
-  __syncthreads();
-  float qr[L + 1];
-#pragma unroll
-  for (int n = 0; n <= L; ++n) qr[n] = q[n];
 
   float m = (MODE == 2) ? ((act && j == bb) ? 1.f : 0.f)
                         : ((MODE == 1 || !act) ? 0.f : m0[(size_t)bb * R + j]);
@@ -409,24 +449,43 @@ __global__ void __launch_bounds__(128)
 // thread, every lane of a warp at the same address), sums its half row in eight
 // chains and combines the pair with one shuffle.  m is double buffered, so a
 // step needs one barrier: a buffer is written again only two steps later, after
-// every thread has passed the barrier that follows its reads.
+// every thread has passed the barrier that follows its reads.  The chunk end
+// states z arrive by cp.async in blocks of ZB chunks, double buffered, so the
+// chain of steps never waits on a global load.
 template <int R>
 __global__ void __launch_bounds__(2 * R)
     rosa_carry_reg_kernel(const float* __restrict__ AKt, const float* __restrict__ z,
                           const float* m0, float* __restrict__ m_start, float* m_out, int C) {
-  constexpr int HALF = R / 2;
+  constexpr int HALF = R / 2, ZB = 16, NT = 2 * R;
   static_assert(R % 32 == 0 && R <= 128, "register carry: R in {32, 64, 128}");
   __shared__ __align__(16) float mv[2][R];
+  __shared__ __align__(16) float zs[2][ZB * R];
   const int b = blockIdx.x, tid = threadIdx.x;
   const int i = tid >> 1, half = tid & 1, j0 = half * HALF;
+  const int nblk = (C + ZB - 1) / ZB;
+  auto fetch = [&](int blk) {  // chunks [blk*ZB, blk*ZB + ZB) of this sequence; always commits
+    if (blk < nblk) {
+      const int c0 = blk * ZB, n4 = min(ZB, C - c0) * R / 4;
+      const float* src = z + ((size_t)b * C + c0) * R;
+      for (int x = tid; x < n4; x += NT) cp_async_16(&zs[blk & 1][4 * x], src + 4 * x);
+    }
+    cp_async_commit();
+  };
+  fetch(0);
   float arow[HALF];
 #pragma unroll
   for (int c = 0; c < HALF; ++c) arow[c] = AKt[(size_t)(j0 + c) * R + i];  // (A^K)[i][j0 + c]
   float mi = m0 ? m0[(size_t)b * R + i] : 0.f;
-  float zc = C > 0 ? z[(size_t)b * C * R + i] : 0.f;  // z of the current chunk
   for (int c = 0; c < C; ++c) {
     const size_t row = ((size_t)b * C + c) * R;
-    const float zn = c + 1 < C ? z[row + R + i] : 0.f;  // next chunk's z, in flight
+    const int blk = c / ZB, cc = c - blk * ZB;
+    if (cc == 0) {
+      __syncthreads();  // every read of the buffer refilled below is done
+      fetch(blk + 1);
+      cp_async_wait<1>();  // this block's chunks landed
+      __syncthreads();
+    }
+    const float zc = zs[blk & 1][cc * R + i];
     float* mb = mv[c & 1];
     if (half == 0) {
       m_start[row + i] = mi;
@@ -448,8 +507,8 @@ __global__ void __launch_bounds__(2 * R)
     float s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     mi = s + zc;
-    zc = zn;
   }
+  cp_async_wait<0>();
   if (half == 0 && m_out) m_out[(size_t)b * R + i] = mi;
 }
 
@@ -564,18 +623,18 @@ template <bool GATED, int MODE>
 static void launch_mode(const float* cand, const float* write, const float* gate,
                         const float* bias_c, const float* bias_w, const float* bias_g, int ld,
                         const float* decay, const float* dir, int raw, const float* m0, float* read,
-                        float* m_out, int B, int T, int R, cudaStream_t s) {
+                        float* m_out, int B, int T, int R, const float* coef, cudaStream_t s) {
   const int threads = ((R + 31) / 32) * 32;
   rosa_scan_kernel<GATED, false, 256, MODE><<<B, threads, 0, s>>>(
       cand, write, gate, decay, dir, m0, read, m_out, nullptr, nullptr, nullptr, nullptr, nullptr,
-      nullptr, T, R, ld, bias_c, bias_w, bias_g, raw);
+      nullptr, T, R, ld, bias_c, bias_w, bias_g, raw, coef);
 }
 
 size_t rosa_parallel_scratch_floats(int B, int T, int R) {
   // A^K (R <= 128) or its low-rank factors W, M and D^K (2 K R + R <= R^2 for
   // R > 128, K = 64), then chunk end states and chunk start states
   const size_t C = (size_t)T / rosa_par_k(R);
-  return (size_t)R * R + 2 * (size_t)B * C * R;
+  return (size_t)R * R + 2 * (size_t)B * C * R + ROSA_COEF_D + 2 * (size_t)R;
 }
 
 bool rosa_parallel_applies(int B, int T, int R) {
@@ -597,16 +656,18 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
   float* AKt = scratch;
   float* z = AKt + (size_t)R * R;
   float* m_start = z + (size_t)B * C * R;
+  float* coef = m_start + (size_t)B * C * R;  // q, d, dec of this layer
+  const int threads = ((R + 31) / 32) * 32;
+  rosa_coef_kernel<<<1, threads, 0, s>>>(decay, dir, raw, R, coef);
   // 1. A^K from R unit vectors (inputs unused in MODE 2); its low-rank form
   //    for R > 128 is built in step 3
   if (R <= 128)
     launch_mode<false, 2>(cand, write, gate, nullptr, nullptr, nullptr, ld, decay, dir, raw, nullptr,
-                          nullptr, AKt, R, K, R, s);
+                          nullptr, AKt, R, K, R, coef, s);
   // 2. chunk end states from zero: chunks are the batch, K tokens each
   launch_mode<false, 1>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, nullptr,
-                        nullptr, z, B * C, K, R, s);
+                        nullptr, z, B * C, K, R, coef, s);
   // 3. carry across chunks
-  const int threads = ((R + 31) / 32) * 32;
   if (R == 32 || R == 64 || R == 128) {
     if (R == 32) rosa_carry_reg_kernel<32><<<B, 64, 0, s>>>(AKt, z, m0, m_start, m_out, C);
     else if (R == 64) rosa_carry_reg_kernel<64><<<B, 128, 0, s>>>(AKt, z, m0, m_start, m_out, C);
@@ -638,10 +699,10 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
   // 4. rescan every chunk from its true start state
   if (gated)
     launch_mode<true, 0>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, m_start, read,
-                         nullptr, B * C, K, R, s);
+                         nullptr, B * C, K, R, coef, s);
   else
     launch_mode<false, 0>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, m_start, read,
-                          nullptr, B * C, K, R, s);
+                          nullptr, B * C, K, R, coef, s);
   return check_launch("rosa parallel scan");
 }
 

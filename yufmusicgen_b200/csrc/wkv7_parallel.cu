@@ -29,7 +29,10 @@
 
 namespace yuf {
 
-constexpr int WKV_PAR_CMAX = 32;  // the carry is sequential over chunks
+#ifndef YUF_WKV_PAR_CMAX
+#define YUF_WKV_PAR_CMAX 32
+#endif
+constexpr int WKV_PAR_CMAX = YUF_WKV_PAR_CMAX;  // the carry is sequential over chunks
 
 yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, const float* v,
                                 const float* a, const float* b, float* y, float* Q, float* U, float* P,
