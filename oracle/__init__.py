@@ -7,6 +7,9 @@ This package restates, in numpy (``model.py``, ``scans.py``) and plain C
 * ``ROSAMemory._reference_recurrence`` yufmusicgen/model.py:260-288
 * ``YufMusicGen.forward`` / ``.step``  yufmusicgen/model.py:345-431
 
+``wy.py`` restates the WKV-7 chunk summary in the chunked (WY) matrix form, as
+the checker for a tensor-core version of the time-parallel scan's first pass.
+
 It is the checker, never the product: only ``tests/``,
 ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` may
 import it.  The engine in ``yufmusicgen_b200`` never calls into this package

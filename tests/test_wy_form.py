@@ -1,0 +1,45 @@
+"""The chunked (WY) form of the WKV-7 chunk summary (oracle/wy.py) against the
+reference recurrence (oracle/scans.py, pinned to the reference's goldens): the
+four outputs the time-parallel scan's passes exchange (zero-start outputs, q
+rows, chunk contribution U and transition P) reproduce the token-by-token
+scan from any start state, for sub-chunks of 8 to 64 tokens, in float64 and
+in float32 (the precision a tensor-core kernel's 3xTF32 products approach).
+Tolerance: |got - want| <= 1e-3 + 1e-4 |want|."""
+
+import numpy as np
+import pytest
+
+from oracle.scans import wkv7_scan
+from oracle.wy import chunk_summary_wy
+from yufmusicgen_b200.workloads import wkv_op_inputs
+
+RTOL, ATOL = 1e-4, 1e-3
+
+
+def _case(T, N, seed):
+    ins = wkv_op_inputs(1, T, 1, N, seed=seed, with_state=True)
+    x = {k: ins[k][0, :, 0] for k in "rwkvab"}
+    s0 = ins["s0"][0, 0]
+    y, s = wkv7_scan(*(ins[k] for k in "rwkvab"), ins["s0"])
+    return x, s0, y[0, :, 0], s[0, 0]
+
+
+@pytest.mark.parametrize("sub", [8, 16, 32, 64])
+@pytest.mark.parametrize("dtype", [np.float64, np.float32])
+@pytest.mark.parametrize("T,N", [(160, 40), (100, 64), (37, 16)])
+def test_wy_chunk_summary_reproduces_the_recurrence(T, N, sub, dtype):
+    x, s0, y_ref, s_ref = _case(T, N, seed=T + N + sub)
+    yU, Q, U, P = chunk_summary_wy(*(x[k] for k in "rwkvab"), sub=sub, dtype=dtype)
+    y = Q @ s0.T.astype(dtype) + yU          # y_t = S_0 q_t + yU_t
+    s = s0.astype(dtype) @ P + U             # S_end = S_0 P + U
+    np.testing.assert_allclose(y, y_ref, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(s, s_ref, rtol=RTOL, atol=ATOL)
+
+
+def test_wy_zero_start_outputs_are_the_scan_from_zero():
+    x, _, _, _ = _case(160, 40, seed=7)
+    ins = {k: x[k][None, :, None] for k in "rwkvab"}
+    y0, s0 = wkv7_scan(*(ins[k] for k in "rwkvab"))
+    yU, _, U, _ = chunk_summary_wy(*(x[k] for k in "rwkvab"), sub=16)
+    np.testing.assert_allclose(yU, y0[0, :, 0], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(U, s0[0, 0], rtol=RTOL, atol=ATOL)
