@@ -20,7 +20,15 @@ NCCL only for the start/stop barrier and the max-over-ranks time).
               wkv7_pairw_kernel<40> (chunk summaries), wkv7_carry_kernel<40>
               (carried states) and wkv7_correct_kernel<40> (output correction).
 * ``cpu_baseline``  the C restatement of the reference recurrence
-              (oracle/scans_ref.c, OpenMP over (b,h)) on this host's cores.
+              (oracle/scans_ref.c, OpenMP over (b,h)) on this host's cores;
+              ``cpu_baseline_model`` the whole 0.1B model through the numpy port
+              of the reference's CPU forward/step on bounded samples (N = 1).
+* ``sharded``  benchmark configs 4 (256 sequences x 1024 generated tokens,
+              top-k 32, through Engine.generate) and 5 (8 sequences of 8192
+              tokens per GPU, bf16 weights) batch-sharded over all ranks, each
+              timed as the max over ranks: decode and prefill tokens/s at N GPUs.
+* ``extra``   rank 0's secondary kernel and model timings (sequential and
+              chunked scans, decode step, ROSA, backward, 0.1B prefill/decode).
 
 ``--impl reference`` times the reference algorithm's CPU implementation
 (the same C port; the reference itself is PyTorch CPU code that cannot be
