@@ -43,3 +43,19 @@ def test_wy_zero_start_outputs_are_the_scan_from_zero():
     yU, _, U, _ = chunk_summary_wy(*(x[k] for k in "rwkvab"), sub=16)
     np.testing.assert_allclose(yU, y0[0, :, 0], rtol=RTOL, atol=ATOL)
     np.testing.assert_allclose(U, s0[0, 0], rtol=RTOL, atol=ATOL)
+
+
+hypothesis = pytest.importorskip("hypothesis")
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+
+@settings(max_examples=30, deadline=None, derandomize=True)
+@given(T=st.integers(1, 96), N=st.sampled_from([8, 16, 24, 32, 40, 64]),
+       sub=st.sampled_from([1, 3, 8, 16, 48]), seed=st.integers(0, 10_000))
+def test_wy_form_property_any_shape(T, N, sub, seed):
+    """Any chunk length (ragged last sub-chunk included), head size and
+    sub-chunk size: the WY summary equals the token-by-token recurrence."""
+    x, s0, y_ref, s_ref = _case(T, N, seed)
+    yU, Q, U, P = chunk_summary_wy(*(x[k] for k in "rwkvab"), sub=sub)
+    np.testing.assert_allclose(Q @ s0.T + yU, y_ref, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(s0 @ P + U, s_ref, rtol=RTOL, atol=ATOL)
