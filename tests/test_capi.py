@@ -121,3 +121,14 @@ def test_generate_params_layout_and_host_validation():
     p = _lib.GenerateParamsC(1.0, 32, 1.0, 0, 0, 0, -1, 16)
     assert lib.yuf_generate(None, 16, 1, 1, 0, 1, ct.byref(p), 16, 16, None) == 1
     assert "null model" in lib.yuf_last_error().decode()
+
+
+def test_python_algorithm_constants_match_the_header():
+    """cuda_ops.ALGO_* carry the values of the header's YUF_WKV_* enum."""
+    from yufmusicgen_b200 import cuda_ops
+
+    text = HEADER.read_text()
+    enum = dict((m.group(1), int(m.group(2))) for m in re.finditer(r"YUF_WKV_([A-Z_]+) = (\d+)", text))
+    assert enum == {"AUTO": 0, "SEQUENTIAL": 1, "CHUNKED": 2, "PARALLEL": 3, "PARALLEL_TC": 4}
+    for name, value in enum.items():
+        assert getattr(cuda_ops, f"ALGO_{name}") == value
