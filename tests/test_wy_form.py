@@ -59,3 +59,26 @@ def test_wy_form_property_any_shape(T, N, sub, seed):
     yU, Q, U, P = chunk_summary_wy(*(x[k] for k in "rwkvab"), sub=sub)
     np.testing.assert_allclose(Q @ s0.T + yU, y_ref, rtol=RTOL, atol=ATOL)
     np.testing.assert_allclose(s0 @ P + U, s_ref, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("sub,blk", [(64, 16), (64, 8), (32, 16), (128, 16)])
+@pytest.mark.parametrize("T,N", [(160, 40), (128, 64), (70, 16)])
+def test_blocked_wy_with_3xtf32_products(T, N, sub, blk):
+    """The planned tensor-core schedule: float32 data, 64-token sub-chunks, the
+    triangular solve blocked into 16 x 16 diagonal blocks plus products, every
+    product a 3xTF32 tensor-core MMA (emulated) -- within the fp32 tolerance."""
+    from oracle.wy import chunk_summary_wy_blocked
+
+    x, s0, y_ref, s_ref = _case(T, N, seed=T * 7 + N + sub + blk)
+    yU, Q, U, P = chunk_summary_wy_blocked(*(x[k] for k in "rwkvab"), sub=sub, blk=blk)
+    np.testing.assert_allclose(Q @ s0.T + yU, y_ref, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(s0 @ P + U, s_ref, rtol=RTOL, atol=ATOL)
+
+
+def test_blocked_unit_lower_inverse():
+    from oracle.wy import mm_3xtf32, unit_lower_inverse_blocked
+
+    rng = np.random.default_rng(3)
+    A = np.eye(64, dtype=np.float32) - np.tril(rng.standard_normal((64, 64)).astype(np.float32) * 0.1, -1)
+    T = unit_lower_inverse_blocked(A, 16, mm_3xtf32)
+    np.testing.assert_allclose(T @ A, np.eye(64), atol=1e-5)
