@@ -293,6 +293,70 @@ yuf_status_t yuf_model_set_decode_graphs(yuf_model* model, int enabled);
  * (token id outside [0, vocab)). */
 yuf_status_t yuf_model_sync_check(yuf_model* model, void* stream);
 
+/* ------------------------------------------------------------------------ *
+ * REMI token codec and Standard MIDI File I/O (host only, no GPU): the
+ * generated token stream <-> notes <-> .mid bytes, the counterpart of the
+ * Vulkan client's RemiCodec (vulkan/src/remi.rs:26-312) and MIDI reader /
+ * writer (vulkan/src/midi.rs:58-434), i.e. MidiTok 3.0 REMI as YufMusicGen
+ * configures it: 8 ticks per quarter, 4/4 bars of 32 positions, a Program
+ * token before every note, velocities 3..127 in steps of 4, the vocabulary's
+ * Duration_<beat>.<position>.<resolution> values.
+ * Two-call convention for outputs of unknown size: pass NULL buffers to get
+ * the counts, then buffers of at least that size.
+ * ------------------------------------------------------------------------ */
+
+typedef struct yuf_note {
+  int32_t start, duration; /* ticks of the score's division */
+  int32_t pitch, velocity;
+} yuf_note;
+
+typedef struct yuf_track_desc {
+  int32_t program;       /* 0..127; -1 for the drum track of a decoded token stream */
+  int32_t is_drum;
+  const char* name;      /* may be NULL or "" */
+  const yuf_note* notes;
+  int64_t n_notes;
+} yuf_track_desc;
+
+typedef struct yuf_remi yuf_remi; /* opaque codec */
+
+/* Codec over a vocabulary (token id -> name, e.g. "Pitch_60", "Duration_0.2.8")
+ * (RemiCodec::new, remi.rs:35-62). */
+yuf_status_t yuf_remi_create(const char* const* vocab, int n_vocab, yuf_remi** out);
+yuf_status_t yuf_remi_destroy(yuf_remi* codec);
+/* Id of a token name, -1 when the vocabulary has none. */
+int32_t yuf_remi_token_id(const yuf_remi* codec, const char* name);
+/* Notes -> token ids (RemiCodec::encode, remi.rs:199-306): times scaled to 8 ticks
+ * per quarter (round half up, durations >= 1), tracks with the same (program,
+ * drum) merged, pitches outside 21..109 (drums 27..88) dropped, velocity and
+ * duration snapped to the nearest vocabulary value (ties to the larger).
+ * Fails when a token the score needs is not in the vocabulary. */
+yuf_status_t yuf_remi_encode(const yuf_remi* codec, int ticks_per_quarter,
+                             const yuf_track_desc* tracks, int n_tracks, int32_t* ids,
+                             int64_t capacity, int64_t* n_ids);
+/* Token ids -> notes at 8 ticks per quarter (RemiCodec::decode, remi.rs:74-180):
+ * one track per program in order of appearance (track_programs [n_tracks]);
+ * notes [n_notes] with their track index in note_track.  Malformed or unknown
+ * tokens are skipped, as the reference does. */
+yuf_status_t yuf_remi_decode(const yuf_remi* codec, const int32_t* ids, int64_t n_ids,
+                             int32_t* track_programs, int max_tracks, int* n_tracks,
+                             yuf_note* notes, int32_t* note_track, int64_t max_notes,
+                             int64_t* n_notes);
+/* Notes -> a format-1 Standard MIDI File (render_midi, midi.rs:351-402): per
+ * track a name, a program change (channel 9 for drums, else program % 16) and
+ * its notes as time-ordered note-on / note-off events.  Unlike the reference
+ * writer, which serialises a track's notes one after another, overlapping notes
+ * keep their times. */
+yuf_status_t yuf_midi_render(int ticks_per_quarter, const yuf_track_desc* tracks, int n_tracks,
+                             uint8_t* out, int64_t capacity, int64_t* n_bytes);
+/* Standard MIDI File -> notes (parse_midi, midi.rs:64-281): one track per
+ * (file track, channel) that has notes, channel 9 = drums, the channel's last
+ * program change, note-offs matched to the latest open note of that pitch. */
+yuf_status_t yuf_midi_parse(const uint8_t* bytes, int64_t n_bytes, int* ticks_per_quarter,
+                            int32_t* track_programs, int32_t* track_is_drum, int max_tracks,
+                            int* n_tracks, yuf_note* notes, int32_t* note_track,
+                            int64_t max_notes, int64_t* n_notes);
+
 /* Parity dumps (the regions of vulkan/scripts/dump_reference_step.py:186-322).
  * When enabled, every prefill/step keeps per-layer copies of: ln0, r, w, k, v,
  * a, b, g, y, h1, read, h2, h3 and (layer -1) logits of the last call. */

@@ -43,6 +43,13 @@ SIGNATURES = {
                    I, I, P, P, P],
     "yuf_philox_uniform": [ctypes.c_uint64, ctypes.c_uint64, I, I, P, P],
     "yuf_generate": [P, P, I, I, I, I, P, P, P, P],
+    "yuf_remi_create": [P, I, P],
+    "yuf_remi_destroy": [P],
+    "yuf_remi_token_id": [P, ctypes.c_char_p],
+    "yuf_remi_encode": [P, I, P, I, P, ctypes.c_int64, P],
+    "yuf_remi_decode": [P, P, ctypes.c_int64, P, I, P, P, P, ctypes.c_int64, P],
+    "yuf_midi_render": [I, P, I, P, ctypes.c_int64, P],
+    "yuf_midi_parse": [P, ctypes.c_int64, P, P, P, I, P, P, P, ctypes.c_int64, P],
     "yuf_model_sync_check": [P, P],
     "yuf_model_set_debug": [P, I],
     "yuf_debug_dump": [P, ctypes.c_char_p, I, P, ctypes.c_size_t, P],
