@@ -119,3 +119,20 @@ def test_generated_tokens_to_midi_ids(codec):
     model_tokens = [1, 4 + 65, *(t + MIDI_OFFSET for t in TOKENS), 2]  # BOS, a byte, the music, EOS
     assert midi_ids(model_tokens, vocab_size=MIDI_OFFSET + len(VOCAB)) == TOKENS
     assert len(codec.decode(midi_ids(model_tokens, MIDI_OFFSET + len(VOCAB))).tracks) == 2
+
+
+def test_codec_from_a_yuf_export(tmp_path):
+    """The exporter stores the MIDI vocabulary in the .yuf header
+    (vulkan/scripts/export_checkpoint.py:117-123); the codec reads it from there."""
+    from yufmusicgen_b200 import config as C
+    from yufmusicgen_b200.weights import init_weights
+    from yufmusicgen_b200.yuf_format import read_yuf, write_yuf
+
+    cfg = C.ModelConfig(**C.TINY)
+    path = tmp_path / "tiny.yuf"
+    write_yuf(path, cfg, init_weights(cfg, 0, "perturbed"),
+              midi={"tokenization": "REMI", "midi_offset": 260, "midi_vocab_size": len(VOCAB), "vocab": VOCAB})
+    header, _ = read_yuf(path)
+    c = RemiCodec(header["midi"]["vocab"])
+    assert c.encode(two_track_score()) == TOKENS
+    c.close()
