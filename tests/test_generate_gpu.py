@@ -109,3 +109,13 @@ def test_generate_is_independent_of_batch_layout():
     part, _ = eng.generate(prompt[4:], 24, seq0=4, **kw)
     np.testing.assert_array_equal(full[4:].cpu().numpy(), part.cpu().numpy())
     eng.close()
+
+
+def test_top_p_above_one_keeps_the_whole_top_k():
+    """top_p >= 1 turns the nucleus cut off (same tokens as top_p = 1)."""
+    cfg, eng = _tiny(2)
+    prompt = tiny_ids(2, 10, seed=8)
+    a, _ = eng.generate(prompt, 12, temperature=1.0, top_k=16, top_p=1.0, seed=4)
+    b, _ = eng.generate(prompt, 12, temperature=1.0, top_k=16, top_p=1.5, seed=4)
+    np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
+    eng.close()

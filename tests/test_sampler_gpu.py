@@ -136,3 +136,24 @@ def test_topk_selection_matches_host_restatement(kind, top_k, top_p, mask_below)
         assert ids[bi] == want or margin < 1e-4, (bi, ids[bi], want, margin)
     if kind == "masked":
         assert ((ids >= mask_below) | (ids == 2)).all()
+
+
+def test_sampled_ids_follow_the_restated_rule():
+    """Token for token against a CPU restatement of the sampling rule (masked
+    MIDI range + EOS, temperature, top-k, top-p, inverse CDF at the returned
+    Philox uniform); rows whose draw lies within 1e-5 of a boundary, where
+    float rounding decides, are left out."""
+    from oracle.sampler import sample_rule
+
+    g = torch.Generator().manual_seed(21)
+    logits = (torch.randn(512, 600, generator=g) * 2.0).cuda()
+    ids, u = sample(logits, seed=3, step=9, temperature=0.7, top_k=32, top_p=0.85, mask_below=260,
+                    eos_id=2, allow_eos=True, return_uniform=True)
+    ids, u, lg = ids.cpu().numpy(), u.cpu().numpy(), logits.cpu().numpy()
+    checked = 0
+    for row in range(lg.shape[0]):
+        want, margin = sample_rule(lg[row], float(u[row]), 0.7, 32, 0.85, mask_below=260, eos_id=2)
+        if margin > 1e-5:
+            assert ids[row] == want, row
+            checked += 1
+    assert checked >= 480

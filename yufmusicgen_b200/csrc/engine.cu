@@ -779,9 +779,10 @@ yuf_status_t yuf_generate(yuf_model* m, const int32_t* prompt_ids, int B, int T,
   int32_t* ids = reinterpret_cast<int32_t*>(static_cast<char*>(m->gen->p) + logit_bytes);
   Y_TRY(yuf_prefill(m, prompt_ids, B, T, slot0, logits, nullptr, stream));
   const int eos_for_mask = p->eos_id >= 0 ? p->eos_id : 0;
+  const float top_p = std::min(p->top_p, 1.f);  // >= 1 keeps the whole top-k
   for (int st = 0; st < n_steps; ++st) {
     const int allow_eos = p->eos_id >= 0 && st >= p->min_tokens_before_eos;
-    Y_TRY(yuf_sample(logits, B, (int)V, p->temperature, p->top_k, p->top_p, p->seed, (uint64_t)st,
+    Y_TRY(yuf_sample(logits, B, (int)V, p->temperature, p->top_k, top_p, p->seed, (uint64_t)st,
                      p->seq0, p->mask_below, eos_for_mask, allow_eos, ids, nullptr, stream));
     gen_record_kernel<<<(B + 127) / 128, 128, 0, s>>>(ids, tokens, lengths, B, n_steps, st, p->eos_id);
     Y_CUDA(cudaGetLastError());
