@@ -48,6 +48,16 @@ int yuf_abi_version(void);
    Synchronous (reads a device counter).  No reference counterpart: the reference
    kernels have no bounded waits. */
 unsigned int yuf_wait_timeouts(void);
+/* Synchronise `stream`, then report the bounded device waits that expired since the
+   last check (clearing the count): YUF_ERR_TIMEOUT when any did -- the outputs of the
+   launches involved are void -- else YUF_OK.  No reference counterpart (the reference
+   kernels have no bounded waits). */
+yuf_status_t yuf_sync_check(void* stream);
+/* Test hook of the bounded-wait path (no reference counterpart): launches one warp
+   that waits, with a bound of `limit_ns` nanoseconds (<= 2 s), on a barrier nothing
+   arrives at, and records the expiry as a scan kernel would; the next yuf_sync_check
+   then returns YUF_ERR_TIMEOUT.  Faults nothing; the context stays usable. */
+yuf_status_t yuf_debug_wait_selftest(unsigned long long limit_ns, void* stream);
 
 /* WKV-7 forward scan with an optional initial state.
  * Replaces the forward launch behind torch.ops.yufmusicgen_rwkv7.forward
@@ -221,8 +231,9 @@ yuf_status_t yuf_step(yuf_model* model, const int32_t* ids, int B, int slot0, fl
  * every GPU that loads the library until exit) instead of the model's
  * grow-on-demand workspace; B larger than that array allows is rejected with
  * YUF_ERR_INVALID_ARGUMENT and a message giving the largest B for the model.
- * The first call on a device looks up the array's device address, so make
- * that first call before any stream capture.  All calls share the one array:
+ * Every call looks up the array's device address (allocating nothing); the
+ * first call on a device may load the library's device code, so make that
+ * first call before any stream capture.  All calls share the one array:
  * calls whose work overlaps on the GPU (other streams, other threads) race and
  * must be serialised by the caller.  Nothing in the array needs clearing
  * between calls.  Parity dumps (yuf_model_set_debug) must be off. */
@@ -290,7 +301,8 @@ yuf_status_t yuf_generate(yuf_model* model, const int32_t* prompt_ids, int B, in
  * bigger prefill) drops the captured graphs.  Off by default. */
 yuf_status_t yuf_model_set_decode_graphs(yuf_model* model, int enabled);
 /* Synchronise `stream` and report device-side input errors of earlier calls
- * (token id outside [0, vocab)). */
+ * (token id outside [0, vocab): YUF_ERR_INVALID_ARGUMENT) and expired bounded
+ * waits (YUF_ERR_TIMEOUT, as yuf_sync_check). */
 yuf_status_t yuf_model_sync_check(yuf_model* model, void* stream);
 
 /* ------------------------------------------------------------------------ *
@@ -361,6 +373,12 @@ yuf_status_t yuf_midi_parse(const uint8_t* bytes, int64_t n_bytes, int* ticks_pe
  * When enabled, every prefill/step keeps per-layer copies of: ln0, r, w, k, v,
  * a, b, g, y, h1, read, h2, h3 and (layer -1) logits of the last call. */
 yuf_status_t yuf_model_set_debug(yuf_model* model, int enabled);
+/* Restrict the parity dumps to some regions and layers, as the Vulkan engine's
+ * debug_dump(&[&str]) names the regions it wants (vulkan/src/compute/model.rs):
+ * `regions` comma-separated (NULL or "" = all), `layers` [n_layers] (0 = all;
+ * the logits, layer -1, are kept whenever their region is). */
+yuf_status_t yuf_model_set_debug_filter(yuf_model* model, const char* regions, const int* layers,
+                                        int n_layers);
 yuf_status_t yuf_debug_dump(yuf_model* model, const char* region, int layer, float* host_out,
                             size_t capacity, size_t* n_written);
 

@@ -16,7 +16,8 @@ Every fixture is produced by the reference's own PyTorch fp32 CPU code:
   CPU code (``grads_cases.npz``), the oracle of the training backward ops.
 
 ``python tests/golden/make_golden.py grads`` writes only the gradient fixture,
-``... greedy256`` only the 256-step greedy decode of the 0.1B model.
+``... greedy256`` only the 256-step greedy decode of the 0.1B model, ``... long``
+only the benchmark-size prefills (config 3 in full, config-5 geometry).
 
 The fixtures are small ``.npz`` files; the GPU box never needs the reference.
 """
@@ -208,6 +209,80 @@ def model_case(name, cfg_kwargs, seed, recipe, ids, n_greedy, keep_positions=Non
     np.savez_compressed(HERE / f"model_{name}.npz", **out)
 
 
+def model_long_case(name, cfg_kwargs, seed, recipe, ids, positions, layers):
+    """A benchmark-size prefill (the shapes that take the time-parallel WKV-7 and
+    ROSA scans inside the model): the logits at a few positions and, for a few
+    layers, what the reference's two recurrences returned -- the WKV-7 output y
+    (at the kept positions) and final state S, the gated ROSA read (kept
+    positions) and final memory m -- plus the block output h3 (kept positions).
+    The recurrences are observed by wrapping the reference's own static methods
+    (RWKV7TimeMix._torch_recurrence, ROSAMemory._reference_recurrence), which
+    YufMusicGen.forward calls once per layer in layer order."""
+    cfg = C.ModelConfig(**cfg_kwargs)
+    weights = init_weights(cfg, seed, recipe)
+    model = ref_model(cfg_kwargs, weights)
+    pos = np.asarray(positions, np.int64)
+    caps, calls = {}, {"wkv": 0, "rosa": 0}
+    wkv_orig = RWKV7TimeMix._torch_recurrence
+    rosa_orig = ROSAMemory._reference_recurrence
+
+    def wkv(*a):
+        y, S = wkv_orig(*a)
+        li = calls["wkv"]
+        calls["wkv"] += 1
+        if li in layers:
+            caps[f"L{li}.y"] = y[:, pos].numpy()
+            caps[f"L{li}.S"] = S.numpy()
+        return y, S
+
+    def rosa(*a):
+        read, m = rosa_orig(*a)
+        li = calls["rosa"]
+        calls["rosa"] += 1
+        if li in layers:
+            caps[f"L{li}.read"] = read[:, pos].numpy()
+            caps[f"L{li}.m"] = m.numpy()
+        return read, m
+
+    hooks = []
+    for li, blk in enumerate(model.blocks):
+        if li in layers:
+            def blk_hook(mod, inp, outp, li=li):
+                caps[f"L{li}.h3"] = outp[0][:, pos].detach().numpy()
+            hooks.append(blk.register_forward_hook(blk_hook))
+    RWKV7TimeMix._torch_recurrence = staticmethod(wkv)
+    ROSAMemory._reference_recurrence = staticmethod(rosa)
+    try:
+        with torch.no_grad():
+            logits, _ = model(t(ids))
+    finally:
+        RWKV7TimeMix._torch_recurrence = staticmethod(wkv_orig)
+        ROSAMemory._reference_recurrence = staticmethod(rosa_orig)
+        for h in hooks:
+            h.remove()
+    assert calls["wkv"] == cfg.n_layers and calls["rosa"] == cfg.n_layers
+    out = {"ids": ids, "positions": pos, "layers": np.asarray(layers, np.int64),
+           "logits": logits[:, pos].numpy()}
+    for k, v in caps.items():
+        out[f"regions.{k}"] = v
+    meta = dict(seed=seed, recipe=recipe, **cfg_kwargs)
+    out["meta_keys"] = np.array(list(meta.keys()))
+    out["meta_vals"] = np.array([str(v) for v in meta.values()])
+    np.savez_compressed(HERE / f"model_{name}.npz", **out)
+
+
+def long_cases():
+    """Benchmark config 3 at its full size (0.1B model, B2 x T2048, the ids the
+    benchmark prefills) and the 24-layer config-5 geometry (d1024, N = 64,
+    R = 256) at B2 x T512."""
+    ids3 = zipf_ids(2, 2048, seed=1, vocab=20000)
+    model_long_case("c3_full", C.BASE_0P1B, seed=1, recipe="baseline", ids=ids3,
+                    positions=[0, 63, 64, 255, 1024, 2047], layers=[0, 7, 13])
+    ids5 = zipf_ids(2, 512, seed=5, vocab=20000)
+    model_long_case("c5_geometry", C.LONG_1K, seed=2, recipe="baseline", ids=ids5,
+                    positions=[0, 255, 256, 511], layers=[0, 12, 23])
+
+
 def state_test_case():
     """The reference's own sequence-vs-step test (tests/test_model_state.py:9-28),
     with the reference recurrence selected (use_rosa_scan=False)."""
@@ -280,9 +355,12 @@ def main():
 if __name__ == "__main__":
     if sys.argv[1:] == ["grads"]:
         grad_cases()
+    elif sys.argv[1:] == ["long"]:
+        long_cases()
     elif sys.argv[1:] == ["greedy256"]:
         greedy256_case()
     else:
         main()
         grad_cases()
         greedy256_case()
+        long_cases()

@@ -230,3 +230,70 @@ def test_decode_graph_replay_equals_eager():
     side.synchronize()
     close(torch.stack(got), torch.stack(want).cpu().numpy(), rtol=1e-6, atol=1e-6)
     eng.close()
+
+
+# Benchmark-size prefills against the reference (tests/golden/make_golden.py
+# long_cases): config 3 in full (0.1B model, B2 x T2048) and the 24-layer
+# config-5 geometry (d1024, N = 64, R = 256) at B2 x T512.  At these shapes the
+# engine takes the time-parallel WKV-7 scan (T >= 256, few (sequence, head)
+# chains) and the time-parallel ROSA scan (whole chunks, >= 16 of them), the
+# paths bench.py times; the small fixtures above only reach the sequential ones.
+LONG_FIXTURES = [("model_c3_full.npz", C.BASE_0P1B, 1), ("model_c5_geometry.npz", C.LONG_1K, 2)]
+
+# bf16-weight mode against the fp32 reference, per region: |got - want| <=
+# atol + rtol |want| (bf16 weights and GEMM inputs, fp32 accumulation and state).
+BF_REGION_TOL = {"y": (0.05, 0.05), "S": (0.05, 0.05), "read": (0.05, 0.05), "m": (0.05, 0.05),
+                 "h3": (0.15, 0.05), "logits": (BF_ATOL, BF_RTOL)}
+
+
+def _long_regions(eng, g):
+    """Engine regions at the fixture's layers and positions, shaped like the
+    fixture's: y [B,P,H,N], read [B,P,R], h3 [B,P,d], S [B,H,N,N], m [B,R]."""
+    B, T = g["ids"].shape
+    pos, c = g["positions"], eng.cfg
+    eng.set_debug(True, regions=["y", "read", "h3"], layers=g["layers"].tolist())
+    _, allv = eng.prefill(torch.as_tensor(g["ids"], dtype=torch.int32, device="cuda"), all_logits=True)
+    got = {"logits": allv[:, pos].cpu().numpy()}
+    del allv
+    for li in g["layers"].tolist():
+        got[f"L{li}.y"] = eng.debug_dump("y", li).reshape(B, T, c.n_heads, c.head_size)[:, pos]
+        got[f"L{li}.read"] = eng.debug_dump("read", li).reshape(B, T, c.rosa_size)[:, pos]
+        got[f"L{li}.h3"] = eng.debug_dump("h3", li).reshape(B, T, c.d_model)[:, pos]
+        st = eng.export_state(li, 0, B)
+        got[f"L{li}.S"] = st["S"].cpu().numpy()
+        got[f"L{li}.m"] = st["m"].cpu().numpy()
+    eng.set_debug(False)
+    return got
+
+
+@pytest.mark.parametrize("fixture,cfgd,seed", LONG_FIXTURES)
+def test_benchmark_size_prefill_matches_reference_per_layer(golden, fixture, cfgd, seed):
+    g = golden(fixture)
+    cfg, w, eng = make(cfgd, seed, "baseline", n_slots=g["ids"].shape[0])
+    got = _long_regions(eng, g)
+    close(got["logits"], g["logits"])
+    for key, val in got.items():
+        if key != "logits":
+            close(val, g[f"regions.{key}"])
+    eng.sync_check()
+    eng.close()
+
+
+@pytest.mark.parametrize("fixture,cfgd,seed", LONG_FIXTURES)
+def test_benchmark_size_prefill_bf16_weights_per_layer(golden, fixture, cfgd, seed):
+    """bf16-weight mode, reported per region against the fp32 reference; the
+    largest error relative to each region's tolerance is printed."""
+    g = golden(fixture)
+    cfg, w, eng = make(cfgd, seed, "baseline", precision="bf16", n_slots=g["ids"].shape[0])
+    got = _long_regions(eng, g)
+    worst = {}
+    for key, val in got.items():
+        want = g["logits"] if key == "logits" else g[f"regions.{key}"]
+        region = key.split(".")[-1]
+        atol, rtol = BF_REGION_TOL[region]
+        err = np.abs(val - want)
+        worst[key] = (float(err.max()), float((err / (atol + rtol * np.abs(want))).max()))
+    print(fixture, {k: f"max|d| {a:.3g} ({b:.2f} of tol)" for k, (a, b) in worst.items()})
+    bad = {k: v for k, v in worst.items() if v[1] > 1.0}
+    assert not bad, bad
+    eng.close()

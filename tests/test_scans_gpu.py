@@ -269,6 +269,28 @@ def test_time_parallel_waits_never_expired():
     assert _lib.wait_timeouts() == 0
 
 
+def test_expired_wait_is_reported_and_the_context_survives():
+    """The bounded-wait path end to end: a warp waits (2 ms bound) on a barrier
+    nothing arrives at, records the expiry as the scan kernels do, returns; the
+    synchronising check reports YUF_ERR_TIMEOUT once, then OK, and the next scan
+    on the same context is exact."""
+    from yufmusicgen_b200 import _lib
+    lib = _lib.load()
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.yuf_sync_check(s) == 0
+    assert lib.yuf_debug_wait_selftest(2_000_000, s) == 0
+    assert lib.yuf_sync_check(s) == 6  # YUF_ERR_TIMEOUT
+    assert "expired" in lib.yuf_last_error().decode()
+    assert lib.yuf_sync_check(s) == 0  # the count was cleared
+    assert lib.yuf_debug_wait_selftest(3_000_000_000, s) == 1  # above the 2 s cap: refused
+    ins = wkv_op_inputs(2, 300, 3, 40, seed=12)
+    y, st = cuda_ops.wkv7_forward(*(cu(ins[k]) for k in "rwkvab"), algo=cuda_ops.ALGO_PARALLEL)
+    yr, sr = cref.wkv7_scan(*(ins[k] for k in "rwkvab"), None)
+    close(y, yr)
+    close(st, sr)
+    assert lib.yuf_sync_check(s) == 0
+
+
 @pytest.mark.parametrize("B,H,N", [(512, 16, 40), (128, 16, 64), (32, 16, 128), (64, 8, 96)])
 def test_wkv7_decode_many_heads_per_cta(B, H, N):
     """Single-token steps with more heads than the decode ring's slots per CTA

@@ -51,7 +51,10 @@ SIGNATURES = {
     "yuf_midi_render": [I, P, I, P, ctypes.c_int64, P],
     "yuf_midi_parse": [P, ctypes.c_int64, P, P, P, I, P, P, P, ctypes.c_int64, P],
     "yuf_model_sync_check": [P, P],
+    "yuf_sync_check": [P],
+    "yuf_debug_wait_selftest": [ctypes.c_ulonglong, P],
     "yuf_model_set_debug": [P, I],
+    "yuf_model_set_debug_filter": [P, ctypes.c_char_p, P, I],
     "yuf_debug_dump": [P, ctypes.c_char_p, I, P, ctypes.c_size_t, P],
 }
 

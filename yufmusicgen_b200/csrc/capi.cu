@@ -65,6 +65,7 @@ void scratch_free(void* p, cudaStream_t st) {
 
 unsigned int wkv7_pair_wait_timeouts();
 unsigned int wkv7_decode_wait_timeouts();
+yuf_status_t wait_selftest(unsigned long long limit_ns, cudaStream_t st);
 yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
                            float* ckpt, float* sa, int B, int T, int H, int N, bool compat,
@@ -126,6 +127,31 @@ extern "C" {
 unsigned int yuf_wait_timeouts(void) {
   const unsigned int p = yuf::wkv7_pair_wait_timeouts(), d = yuf::wkv7_decode_wait_timeouts();
   return (p == ~0u || d == ~0u) ? ~0u : p + d;
+}
+
+yuf_status_t yuf_sync_check(void* stream) {
+  g_err[0] = 0;
+  const cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("sync_check: %s", cudaGetErrorString(e));
+    return YUF_ERR_CUDA;
+  }
+  const unsigned int n = yuf_wait_timeouts();
+  if (n == ~0u) {
+    set_error("sync_check: the wait-timeout counters could not be read");
+    return YUF_ERR_CUDA;
+  }
+  if (n != 0) {
+    set_error("%u bounded device wait(s) expired: the outputs of the affected launches are void", n);
+    return YUF_ERR_TIMEOUT;
+  }
+  return YUF_OK;
+}
+
+yuf_status_t yuf_debug_wait_selftest(unsigned long long limit_ns, void* stream) {
+  g_err[0] = 0;
+  REQUIRE(limit_ns <= 2000ull * 1000 * 1000, "wait selftest: limit %llu ns is above 2 s", limit_ns);
+  return wait_selftest(limit_ns, static_cast<cudaStream_t>(stream));
 }
 
 const char* yuf_status_string(yuf_status_t s) {

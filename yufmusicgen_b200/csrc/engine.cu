@@ -105,6 +105,8 @@ struct yuf_model {
   // debug dumps: region -> per layer host copies of the last call
   bool debug = false;
   std::map<std::string, std::vector<std::vector<float>>> dumps;
+  std::vector<std::string> debug_regions;  // empty: every region
+  std::vector<char> debug_layers;          // empty: every layer
 
   void* alloc(size_t bytes) {
     auto b = std::make_unique<DevBuf>();
@@ -209,11 +211,19 @@ static size_t scan_scratch_floats(const yuf_model* m, size_t rows) {
   return scan_rosa_floats(m, rows) + wkv7_parallel_scratch_bound(rows, m->H(), m->N());
 }
 
-static size_t ws_bytes(const yuf_model* m, size_t rows) {
+// bf16 staging elements per token row: the largest GEMM input written in bf16
+// (the six mixes [6][rows][d], the three low-rank activations [3][rows][lr], the
+// FFN hidden [rows][4d], the ROSA read [rows][R]).
+static size_t bf_elems_per_row(const yuf_model* m) {
+  return (size_t)std::max({6 * m->d(), 3 * m->lr(), m->R()});
+}
+
+// decode_only: a T = 1 step, which never touches the time-parallel scans' scratch
+static size_t ws_bytes(const yuf_model* m, size_t rows, bool decode_only = false) {
   const size_t per = ws_floats_per_row(m);
-  const size_t bf_elems = rows * (size_t)std::max(6 * m->d(), m->R());
-  return (rows * per + scan_scratch_floats(m, rows)) * sizeof(float) +
-         bf_elems * sizeof(__nv_bfloat16) + 512;
+  const size_t scan = decode_only ? 0 : scan_scratch_floats(m, rows);
+  return (rows * per + scan) * sizeof(float) + rows * bf_elems_per_row(m) * sizeof(__nv_bfloat16) +
+         512;
 }
 
 static yuf_status_t ensure_ws(yuf_model* m, size_t rows) {
@@ -229,7 +239,7 @@ static yuf_status_t ensure_ws(yuf_model* m, size_t rows) {
   return YUF_OK;
 }
 
-static WS carve(yuf_model* m, size_t rows, void* base) {
+static WS carve(yuf_model* m, size_t rows, void* base, bool decode_only = false) {
   float* p = static_cast<float*>(base);
   const size_t d = m->d(), lr = m->lr(), R = m->R();
   WS w;
@@ -255,7 +265,7 @@ static WS carve(yuf_model* m, size_t rows, void* base) {
     uintptr_t a = reinterpret_cast<uintptr_t>(p);
     p = reinterpret_cast<float*>((a + 15) & ~uintptr_t(15));
   }
-  w.scan = take(scan_scratch_floats(m, rows));
+  w.scan = decode_only ? nullptr : take(scan_scratch_floats(m, rows));
   uintptr_t u = reinterpret_cast<uintptr_t>(p);
   u = (u + 255) & ~uintptr_t(255);
   w.bf = reinterpret_cast<__nv_bfloat16*>(u);
@@ -265,6 +275,12 @@ static WS carve(yuf_model* m, size_t rows, void* base) {
 static void dump(yuf_model* m, const char* region, int layer, const float* dev, size_t n,
                  cudaStream_t s) {
   if (!m->debug) return;
+  if (!m->debug_regions.empty() &&
+      std::find(m->debug_regions.begin(), m->debug_regions.end(), region) == m->debug_regions.end())
+    return;
+  if (layer >= 0 && !m->debug_layers.empty() &&
+      (layer >= (int)m->debug_layers.size() || !m->debug_layers[layer]))
+    return;
   auto& v = m->dumps[region];
   if ((int)v.size() <= layer + 1) v.resize(layer + 2);
   auto& h = v[layer + 1];
@@ -281,11 +297,13 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
                             void* ws_base = nullptr) {
   const size_t rows = (size_t)B * T;
   const int d = m->d(), H = m->H(), N = m->N(), R = m->R(), lr = m->lr(), V = m->V();
-  if (ws_base == nullptr) {
+  // a caller-supplied workspace serves a decode step only (sized by ws_bytes(.., true))
+  const bool caller_ws = ws_base != nullptr;
+  if (!caller_ws) {
     Y_TRY(ensure_ws(m, rows));
     ws_base = m->ws->p;
   }
-  WS w = carve(m, rows, ws_base);
+  WS w = carve(m, rows, ws_base, caller_ws);
   launch_embed(ids, m->emb, w.x, (int)rows, d, V, m->d_err, s);
   const size_t RD = rows * d;
   // bf16-weight mode: the producers of GEMM inputs (mixes, layer norms, the FFN
@@ -531,6 +549,8 @@ static yuf_status_t validate_cfg(yuf_model_config* c) {
   Y_REQUIRE(c->d_model % 8 == 0, "model: d_model must be a multiple of 8");
   Y_REQUIRE(c->vocab_size > 0 && c->rosa_size >= 1 && c->rosa_size <= 1024, "model: bad vocab/rosa size");
   if (c->low_rank <= 0) c->low_rank = reference_low_rank(c->d_model);
+  Y_REQUIRE(c->low_rank <= 4 * c->d_model && c->low_rank % 8 == 0,
+            "model: low_rank %d must be a multiple of 8 and at most 4 * d_model", c->low_rank);
   return YUF_OK;
 }
 
@@ -813,13 +833,44 @@ yuf_status_t yuf_model_sync_check(yuf_model* m, void* stream) {
     set_error("model: a token id was outside [0, %d)", m->cfg.vocab_size);
     return YUF_ERR_INVALID_ARGUMENT;
   }
-  return YUF_OK;
+  // bounded device waits of the scan kernels (a nonzero count voids the outputs)
+  return yuf_sync_check(stream);
 }
 
 yuf_status_t yuf_model_set_debug(yuf_model* m, int enabled) {
   Y_REQUIRE(m, "null model");
   m->debug = enabled != 0;
   if (!m->debug) m->dumps.clear();
+  return YUF_OK;
+}
+
+yuf_status_t yuf_model_set_debug_filter(yuf_model* m, const char* regions, const int* layers,
+                                        int n_layers) {
+  Y_REQUIRE(m, "null model");
+  Y_REQUIRE(n_layers >= 0 && (n_layers == 0 || layers), "debug: bad layer list");
+  std::vector<std::string> names;
+  if (regions) {
+    std::string cur;
+    for (const char* c = regions;; ++c) {
+      if (*c == ',' || *c == 0) {
+        if (!cur.empty()) names.push_back(cur);
+        cur.clear();
+        if (*c == 0) break;
+      } else if (*c != ' ') {
+        cur.push_back(*c);
+      }
+    }
+  }
+  std::vector<char> mask;
+  if (n_layers > 0) {
+    mask.assign(m->cfg.n_layers, 0);
+    for (int i = 0; i < n_layers; ++i) {
+      Y_REQUIRE(layers[i] >= 0 && layers[i] < m->cfg.n_layers, "debug: layer %d out of range", layers[i]);
+      mask[layers[i]] = 1;
+    }
+  }
+  m->debug_regions = std::move(names);
+  m->debug_layers = std::move(mask);
   return YUF_OK;
 }
 
@@ -851,29 +902,28 @@ yuf_status_t yuf_debug_dump(yuf_model* m, const char* region, int layer, float* 
 // memory budget up front.  yuf_step_static serves them: its per-call working
 // memory comes from the fixed array below instead of the model's grow-on-demand
 // workspace, so a call allocates nothing (the model, its weights, its state
-// slots and the cuBLAS workspace were all allocated when the model was built).
+// slots and the GEMM workspace were all allocated when the model was built).
 //
 // The array is a file-scope __device__ object: every GPU that loads this library
 // holds it (YUF_STATIC_SCRATCH_BYTES) until the process exits.  Host code cannot
-// use its name as a device address, so the first call on each device looks the
-// address up with cudaGetSymbolAddress (with that device current) and caches it.
+// use its name as a device address, so every call looks the address up with
+// cudaGetSymbolAddress, with the model's device current (a lookup allocates
+// nothing; the first one on a device may load the library's device code, so
+// that first call belongs before any stream capture).  The step's scratch is
+// sized for one token per sequence (no time-parallel scan scratch).
 namespace yuf {
 constexpr size_t YUF_STATIC_SCRATCH_BYTES = 8u << 20;  // 8 MiB
 }  // namespace yuf
 static __device__ __align__(256) unsigned char g_step_scratch[yuf::YUF_STATIC_SCRATCH_BYTES];
 
-#include <mutex>
-static std::mutex g_scratch_mu;
-static void* g_scratch_addr[128] = {};
-
 extern "C" yuf_status_t yuf_step_static(yuf_model* m, const int32_t* ids, int B, int slot0,
                                         float* logits, void* stream) {
   Y_REQUIRE(m, "step_static: null model");
   Y_REQUIRE(B >= 1 && ids && logits, "step_static: need B >= 1, ids and logits");
-  const size_t need = ws_bytes(m, (size_t)B);
+  const size_t need = ws_bytes(m, (size_t)B, true);
   if (need > YUF_STATIC_SCRATCH_BYTES) {
     size_t max_b = 0;
-    while (ws_bytes(m, max_b + 1) <= YUF_STATIC_SCRATCH_BYTES) ++max_b;
+    while (ws_bytes(m, max_b + 1, true) <= YUF_STATIC_SCRATCH_BYTES) ++max_b;
     set_error("step_static: %d sequences need %zu bytes of scratch; the fixed scratch holds %zu "
               "bytes (at most %zu sequences for this model)",
               B, need, (size_t)YUF_STATIC_SCRATCH_BYTES, max_b);
@@ -883,21 +933,12 @@ extern "C" yuf_status_t yuf_step_static(yuf_model* m, const int32_t* ids, int B,
   Y_REQUIRE(m->n_slots > 0, "step_static: call yuf_state_alloc first");
   Y_REQUIRE(slot0 >= 0 && slot0 + B <= m->n_slots, "step_static: slots [%d, %d) out of range (%d slots)",
             slot0, slot0 + B, m->n_slots);
-  Y_REQUIRE(m->device >= 0 && m->device < 128, "step_static: device %d out of range", m->device);
   Y_CUDA(cudaSetDevice(m->device));
   void* base = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (g_scratch_addr[m->device] == nullptr) {
-      void* p = nullptr;
-      cudaError_t e = cudaGetSymbolAddress(&p, g_step_scratch);
-      if (e != cudaSuccess || p == nullptr) {
-        set_error("step_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-        return YUF_ERR_CUDA;
-      }
-      g_scratch_addr[m->device] = p;
-    }
-    base = g_scratch_addr[m->device];
+  const cudaError_t e = cudaGetSymbolAddress(&base, g_step_scratch);
+  if (e != cudaSuccess || base == nullptr) {
+    set_error("step_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    return YUF_ERR_CUDA;
   }
   // Every scratch region is written before it is read within the step, so
   // nothing has to be cleared between calls.

@@ -25,8 +25,9 @@ YUF_DEVICE unsigned long long global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// true when the barrier's phase `parity` completed within WAIT_NS
-YUF_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// true when the barrier's phase `parity` completed within `limit_ns` (WAIT_NS
+// unless a caller passes its own bound)
+YUF_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned long long limit_ns = WAIT_NS) {
   const uint32_t a = smem_u32(bar);
   unsigned long long t0 = 0;
   for (unsigned int it = 0;; ++it) {
@@ -42,7 +43,7 @@ YUF_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if ((it & 63) == 0) {  // look at the clock every 64 polls
       const unsigned long long now = global_ns();
       if (it == 0) t0 = now;
-      else if (now - t0 > WAIT_NS) return false;
+      else if (now - t0 > limit_ns) return false;
     }
   }
 }

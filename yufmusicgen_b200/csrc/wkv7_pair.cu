@@ -296,6 +296,13 @@ YUF_DEVICE void block_sync() {
   else __syncthreads();
 }
 
+// true on every thread when `p` holds on any thread of the block
+template <int NW>
+YUF_DEVICE bool block_any(bool p) {
+  if constexpr (NW == 1) return __any_sync(0xffffffffu, p);
+  else return __syncthreads_or(p) != 0;
+}
+
 // C floats of one padded vector as float2 pairs (C/4 LDS.128 and one LDS.64).
 template <int C>
 YUF_DEVICE void load_cols(float2 (&dst)[C / 2], const float* p) {
@@ -380,8 +387,14 @@ __global__ void __launch_bounds__(PairWCfg<N>::NT, YUF_PAIRW_MINB)
   for (int gi = 0; gi < ngroups; ++gi) {
     const int t0 = gi * TS;
     const int Tc = min(TS, T - t0);
-    if (!mbar_wait(bar, gi & 1)) {  // every thread times out alike; the outputs are void
-      atomicAdd(&g_pair_wait_timeouts, 1u);
+    // A group that never landed: the block votes, counts one timeout, lets the
+    // staging copy still in flight into its shared memory land (bounded) and
+    // leaves together; the outputs of the launch are void.
+    if (block_any<K::NW>(!mbar_wait(bar, gi & 1))) {
+      if (tid == 0) {
+        atomicAdd(&g_pair_wait_timeouts, 1u);
+        mbar_wait(bar, gi & 1);
+      }
       return;
     }
     // scaled vectors: a thread per column pair, running gamma over the group's tokens
@@ -901,6 +914,26 @@ static yuf_status_t make_pair_tmaps(const float* const (&src)[6], long long rows
     }
   }
   return YUF_OK;
+}
+
+// Self-test of the bounded-wait path: one warp waits on an mbarrier that nothing
+// ever arrives on, with the given bound, and records the expiry exactly as a
+// scan kernel does (the timeout count the host reads through yuf_wait_timeouts /
+// yuf_sync_check).  No copy is in flight, nothing faults, the context stays usable.
+__global__ void wait_selftest_kernel(unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar, 0, limit_ns));
+  if (!ok && threadIdx.x == 0) atomicAdd(&g_pair_wait_timeouts, 1u);
+}
+
+yuf_status_t wait_selftest(unsigned long long limit_ns, cudaStream_t st) {
+  wait_selftest_kernel<<<1, 32, 0, st>>>(limit_ns);
+  return check_launch("wait_selftest_kernel");
 }
 
 // Timeouts of the pair kernel's bounded barrier waits on the current device

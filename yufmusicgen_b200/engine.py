@@ -176,7 +176,13 @@ class Engine:
             _lib.call("yuf_model_sync_check", self._h, self._stream())
 
     # -- parity dumps ----------------------------------------------------
-    def set_debug(self, enabled: bool = True):
+    def set_debug(self, enabled: bool = True, regions=None, layers=None):
+        """Keep per-layer parity dumps of every call (all regions and layers, or
+        only the named ``regions`` of the given ``layers``)."""
+        names = ",".join(regions).encode() if regions else None
+        lay = list(layers) if layers else []
+        arr = (ctypes.c_int * max(1, len(lay)))(*lay)
+        _lib.call("yuf_model_set_debug_filter", self._h, names, arr if lay else None, len(lay))
         _lib.call("yuf_model_set_debug", self._h, 1 if enabled else 0)
 
     def debug_dump(self, region: str, layer: int = -1) -> np.ndarray:
