@@ -240,10 +240,11 @@ def test_decode_graph_replay_equals_eager():
 # paths bench.py times; the small fixtures above only reach the sequential ones.
 LONG_FIXTURES = [("model_c3_full.npz", C.BASE_0P1B, 1), ("model_c5_geometry.npz", C.LONG_1K, 2)]
 
-# bf16-weight mode against the fp32 reference, per region: |got - want| <=
-# atol + rtol |want| (bf16 weights and GEMM inputs, fp32 accumulation and state).
-BF_REGION_TOL = {"y": (0.05, 0.05), "S": (0.05, 0.05), "read": (0.05, 0.05), "m": (0.05, 0.05),
-                 "h3": (0.15, 0.05), "logits": (BF_ATOL, BF_RTOL)}
+# bf16-weight mode against the fp32 reference, per region (bf16 weights and GEMM
+# inputs, fp32 accumulation and state; the rounding drift grows with depth): the
+# largest error at most 15 % of the region's largest magnitude, and the RMS
+# error at most 5 % of the region's RMS.
+BF_REGION_MAX, BF_REGION_RMS = 0.15, 0.05
 
 
 def _long_regions(eng, g):
@@ -281,19 +282,19 @@ def test_benchmark_size_prefill_matches_reference_per_layer(golden, fixture, cfg
 
 @pytest.mark.parametrize("fixture,cfgd,seed", LONG_FIXTURES)
 def test_benchmark_size_prefill_bf16_weights_per_layer(golden, fixture, cfgd, seed):
-    """bf16-weight mode, reported per region against the fp32 reference; the
-    largest error relative to each region's tolerance is printed."""
+    """bf16-weight mode, reported per region against the fp32 reference: the
+    largest error relative to the region's largest magnitude, and the RMS error
+    relative to its RMS (printed for every region)."""
     g = golden(fixture)
     cfg, w, eng = make(cfgd, seed, "baseline", precision="bf16", n_slots=g["ids"].shape[0])
     got = _long_regions(eng, g)
-    worst = {}
+    rel = {}
     for key, val in got.items():
         want = g["logits"] if key == "logits" else g[f"regions.{key}"]
-        region = key.split(".")[-1]
-        atol, rtol = BF_REGION_TOL[region]
-        err = np.abs(val - want)
-        worst[key] = (float(err.max()), float((err / (atol + rtol * np.abs(want))).max()))
-    print(fixture, {k: f"max|d| {a:.3g} ({b:.2f} of tol)" for k, (a, b) in worst.items()})
-    bad = {k: v for k, v in worst.items() if v[1] > 1.0}
+        err = val.astype(np.float64) - want
+        rel[key] = (float(np.abs(err).max() / np.abs(want).max()),
+                    float(np.sqrt((err ** 2).mean() / (want.astype(np.float64) ** 2).mean())))
+    print(fixture, {k: f"max {a:.3f} rms {b:.4f}" for k, (a, b) in rel.items()})
+    bad = {k: v for k, v in rel.items() if v[0] > BF_REGION_MAX or v[1] > BF_REGION_RMS}
     assert not bad, bad
     eng.close()
