@@ -169,6 +169,35 @@ yuf_status_t yuf_rosa_backward(const float* cand_saved, const float* write_saved
                                float* d_memory_out, float* workspace, int B, int T, int R,
                                void* stream);
 
+/* Projection GEMM of the engine (bf16 operands, fp32 accumulation, tcgen05
+ * tensor cores), the nn.Linear products of yufmusicgen/model.py:107-112,
+ * 195-197, 297-311, 376-377, 421 for a host that drives the block itself:
+ *   C[z] = A[z] . W[z]^T  for z < batch,
+ * A [M, K] bf16 with row stride lda (batch z starts a_batch_rows rows on), W
+ * [N, K] bf16 contiguous (batch z starts w_batch_rows rows on), C with row
+ * stride ldc (batch z starts c_batch_stride elements on).  A and W rows
+ * 16-byte aligned (lda and K multiples of 8).  Epilogues:
+ *   YUF_GEMM_F32         C fp32 = acc, or C += acc with accumulate != 0
+ *                        (the block's residual adds);
+ *   YUF_GEMM_BF16        C bf16 = acc;
+ *   YUF_GEMM_BF16_TANH0  C bf16 = tanh(acc) for batch 0, acc for the others
+ *                        (the w branch of the low-rank projections);
+ *   YUF_GEMM_SILU_GATE   C bf16 [M, n_out] = SiLU(in) * gate, where W's rows
+ *                        come in groups of 128: 64 rows of ffn_in.weight, then
+ *                        the same 64 rows of ffn_gate.weight (model.py:376-377);
+ *                        output column 64g + j pairs W rows 128g + j and
+ *                        128g + 64 + j.  N % 128 == 0, n_out <= N / 2. */
+enum {
+  YUF_GEMM_F32 = 0,
+  YUF_GEMM_BF16 = 1,
+  YUF_GEMM_BF16_TANH0 = 2,
+  YUF_GEMM_SILU_GATE = 3
+};
+yuf_status_t yuf_gemm_bf16(const void* A, long long lda, long long a_batch_rows, const void* W,
+                           long long w_batch_rows, void* C, long long ldc, long long c_batch_stride,
+                           int M, int N, int K, int batch, int epilogue, int accumulate, int n_out,
+                           void* stream);
+
 /* ------------------------------------------------------------------------ *
  * Model engine: the YufMusicGen block stack (yufmusicgen/model.py:345-445) on
  * the GPU with device-resident recurrent state, the batched counterpart of the

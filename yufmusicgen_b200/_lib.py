@@ -54,6 +54,8 @@ SIGNATURES = {
     "yuf_sync_check": [P],
     "yuf_debug_wait_selftest": [ctypes.c_ulonglong, P],
     "yuf_model_set_debug": [P, I],
+    "yuf_gemm_bf16": [P, ctypes.c_longlong, ctypes.c_longlong, P, ctypes.c_longlong, P, ctypes.c_longlong,
+                      ctypes.c_longlong, I, I, I, I, I, I, I, P],
     "yuf_model_set_debug_filter": [P, ctypes.c_char_p, P, I],
     "yuf_debug_dump": [P, ctypes.c_char_p, I, P, ctypes.c_size_t, P],
 }

@@ -65,6 +65,7 @@ void scratch_free(void* p, cudaStream_t st) {
 
 unsigned int wkv7_pair_wait_timeouts();
 unsigned int wkv7_decode_wait_timeouts();
+unsigned int gemm_wait_timeouts();
 yuf_status_t wait_selftest(unsigned long long limit_ns, cudaStream_t st);
 yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
@@ -125,8 +126,9 @@ using namespace yuf;
 extern "C" {
 
 unsigned int yuf_wait_timeouts(void) {
-  const unsigned int p = yuf::wkv7_pair_wait_timeouts(), d = yuf::wkv7_decode_wait_timeouts();
-  return (p == ~0u || d == ~0u) ? ~0u : p + d;
+  const unsigned int p = yuf::wkv7_pair_wait_timeouts(), d = yuf::wkv7_decode_wait_timeouts(),
+                     g = yuf::gemm_wait_timeouts();
+  return (p == ~0u || d == ~0u || g == ~0u) ? ~0u : p + d + g;
 }
 
 yuf_status_t yuf_sync_check(void* stream) {

@@ -15,10 +15,15 @@
 //   x    += W_out(silu(x_f W_in^T) * (x_f W_g^T))      GEMM [8d, d], silu_mul, GEMM (beta = 1)
 // then logits = LN_final(x) E^T (tied head, model.py:389-391, 421).
 //
-// GEMMs go to cuBLAS: fp32 mode uses its BF16x9 FP32 emulation (fp32-accurate
-// products on the tensor cores), bf16 mode stores the weights in bf16 and feeds
-// bf16 activations with fp32 accumulation.  Everything else (scans, norms,
-// activations, state) stays fp32.
+// bf16-weight mode: every projection is the library's tcgen05 GEMM (gemm.cu)
+// on bf16 weights and bf16 activations with fp32 accumulation, with the work
+// around it folded into the epilogues: tanh of the w branch (lr1), the residual
+// adds of W_o / ROSA out / FFN out (accumulate into x), and SiLU(in) * gate of
+// the FFN (its weight packed in 64-row in/gate groups), so the FFN hidden
+// leaves the GEMM as bf16 and no [rows, 8d] intermediate exists.  fp32 mode
+// runs the products on cuBLAS's BF16x9 FP32 emulation (fp32-accurate products
+// on the tensor cores).  Everything else (scans, norms, activations, state)
+// stays fp32.
 
 #include <cublas_v2.h>
 
@@ -31,6 +36,7 @@
 #include <unordered_map>
 #include <vector>
 
+#include "gemm.cuh"
 #include "model_kernels.cuh"
 
 namespace yuf {
@@ -182,6 +188,39 @@ static yuf_status_t gemm(yuf_model* m, const void* A, int lda, long long sA, con
   }
   return YUF_OK;
 }
+
+// bf16-weight mode: C[z] = A[z] . W[z]^T on the tcgen05 GEMM (gemm.cu).
+// a_brows / w_brows: rows between batches in A / W; c_bstride: elements
+// between batches in C.
+static yuf_status_t proj_bf16(const void* A, long long lda, long long a_brows, const void* W,
+                              long long w_brows, void* C, long long ldc, long long c_bstride, int M,
+                              int N, int K, int batch, int epi, bool accumulate, cudaStream_t s,
+                              int n_out = 0, bool tanh_batch0 = false) {
+  GemmArgs g{};
+  g.A = A;
+  g.lda = lda;
+  g.a_brows = a_brows;
+  g.a_rows = (long long)(batch - 1) * a_brows + M;
+  g.W = W;
+  g.w_brows = w_brows;
+  g.w_rows = (long long)(batch - 1) * w_brows + N;
+  g.C = C;
+  g.ldc = ldc;
+  g.c_bstride = c_bstride;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.batch = batch;
+  g.epi = epi;
+  g.beta = accumulate ? 1.f : 0.f;
+  g.tanh_batch0 = tanh_batch0 ? 1 : 0;
+  g.n_out = n_out;
+  return gemm_bf16(g, s);
+}
+
+// Rows of the packed FFN in/gate weight of bf16 mode: 64-row groups of
+// ffn_in.weight and ffn_gate.weight alternating, the hidden width padded to 64.
+static int ffn_pad(int d) { return (4 * d + 63) / 64 * 64; }
 
 // Workspace for `rows` token rows (grown on demand; never shrinks).
 struct WS {
@@ -341,19 +380,24 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     }
     const size_t esz = m->precision == YUF_PRECISION_BF16_WEIGHTS ? 2 : 4;
     const char* mixed_hi = static_cast<const char*>(mixed) + 3 * RD * esz;  // w, a, g mixes
-    Y_TRY(gemm(m, mixed, d, RD, Lw.W_rkv, (long long)d * d, w.rkv, d, RD, (int)rows, d, d, 0.f, 3, s));
-    Y_TRY(gemm(m, mixed_hi, d, RD, Lw.W_lr1, (long long)lr * d, w.lr1, lr, rows * lr, (int)rows, lr, d,
-               0.f, 3, s));
-    // w branch: tanh(xw W1); in bf16 mode the same pass converts all three branches
-    const void* lr1 = w.lr1;
     if (bf) {
-      launch_tanh<__nv_bfloat16>(w.lr1, w.bf, rows * lr, 3 * rows * lr, s);
-      lr1 = w.bf;
+      // r, k, v; then x_{w,a,g} L1 with tanh on the w branch, written as bf16 into
+      // the lr1 buffer, which feeds L2
+      Y_TRY(proj_bf16(mixed, d, (long long)rows, Lw.W_rkv, d, w.rkv, d, RD, (int)rows, d, d, 3,
+                      GEMM_EPI_F32, false, s));
+      __nv_bfloat16* lr1b = reinterpret_cast<__nv_bfloat16*>(w.lr1);
+      Y_TRY(proj_bf16(mixed_hi, d, (long long)rows, Lw.W_lr1, lr, lr1b, lr, (long long)rows * lr,
+                      (int)rows, lr, d, 3, GEMM_EPI_BF16, false, s, 0, true));
+      Y_TRY(proj_bf16(lr1b, lr, (long long)rows, Lw.W_lr2, d, w.lr2, d, RD, (int)rows, d, lr, 3,
+                      GEMM_EPI_F32, false, s));
     } else {
-      launch_tanh<float>(w.lr1, w.lr1, rows * lr, rows * lr, s);
+      Y_TRY(gemm(m, mixed, d, RD, Lw.W_rkv, (long long)d * d, w.rkv, d, RD, (int)rows, d, d, 0.f, 3, s));
+      Y_TRY(gemm(m, mixed_hi, d, RD, Lw.W_lr1, (long long)lr * d, w.lr1, lr, rows * lr, (int)rows, lr, d,
+                 0.f, 3, s));
+      launch_tanh<float>(w.lr1, w.lr1, rows * lr, rows * lr, s);  // w branch: tanh(x_w W1)
+      Y_TRY(gemm(m, w.lr1, lr, rows * lr, Lw.W_lr2, (long long)d * lr, w.lr2, d, RD, (int)rows, d, lr,
+                 0.f, 3, s));
     }
-    Y_TRY(gemm(m, lr1, lr, rows * lr, Lw.W_lr2, (long long)d * lr, w.lr2, d, RD, (int)rows, d, lr, 0.f,
-               3, s));
     launch_timemix_post(w.rkv + RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD, Lw.w0, Lw.a0, Lw.k_k, Lw.k_a,
                         w.w_raw, w.k_adj, w.a_op, w.b_op, w.g, (int)rows, H, N, s);
     if (T == 1)
@@ -377,39 +421,60 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
       dump(m, "g", li, w.g, RD, s);
       dump(m, "y", li, w.y, RD, s);
     }
-    Y_TRY(gemm(m, att, d, 0, Lw.W_o, 0, w.x, d, 0, (int)rows, d, d, 1.f, 1, s));
+    // x += W_o (LN_out(y) * g)
+    if (bf)
+      Y_TRY(proj_bf16(att, d, 0, Lw.W_o, 0, w.x, d, 0, (int)rows, d, d, 1, GEMM_EPI_F32, true, s));
+    else
+      Y_TRY(gemm(m, att, d, 0, Lw.W_o, 0, w.x, d, 0, (int)rows, d, d, 1.f, 1, s));
     if (m->debug) dump(m, "h1", li, w.x, RD, s);
-    // --- ROSA
-    Y_TRY(gemm(m, ln_in(w.x, Lw.ln_r_w, Lw.ln_r_b, nullptr), d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0,
-               (int)rows, 3 * R, d, 0.f, 1, s));
+    // --- ROSA: [cand | write | gate] = LN_rosa(x) W^T, scan, x += read W_out^T
+    const void* xr = ln_in(w.x, Lw.ln_r_w, Lw.ln_r_b, nullptr);
+    if (bf)
+      Y_TRY(proj_bf16(xr, d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0, (int)rows, 3 * R, d, 1, GEMM_EPI_F32,
+                      false, s));
+    else
+      Y_TRY(gemm(m, xr, d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0, (int)rows, 3 * R, d, 0.f, 1, s));
     Y_TRY(rosa_engine_dispatch(w.rosa, w.rosa + R, w.rosa + 2 * R, Lw.b_rosa, Lw.b_rosa + R,
                                Lw.b_rosa + 2 * R, 3 * R, Lw.decay, Lw.householder, mem, w.read, mem, B,
                                T, R, w.scan, bf ? w.bf : nullptr, s));
     if (m->debug) dump(m, "read", li, w.read, rows * R, s);
-    Y_TRY(gemm(m, bf ? static_cast<const void*>(w.bf) : w.read, R, 0, Lw.W_rosa_out, 0, w.x, d, 0,
-               (int)rows, d, R, 1.f, 1, s));
+    if (bf)
+      Y_TRY(proj_bf16(w.bf, R, 0, Lw.W_rosa_out, 0, w.x, d, 0, (int)rows, d, R, 1, GEMM_EPI_F32, true, s));
+    else
+      Y_TRY(gemm(m, w.read, R, 0, Lw.W_rosa_out, 0, w.x, d, 0, (int)rows, d, R, 1.f, 1, s));
     if (m->debug) dump(m, "h2", li, w.x, RD, s);
-    // --- FFN
-    Y_TRY(gemm(m, ln_in(w.x, Lw.ln_f_w, Lw.ln_f_b, nullptr), d, 0, Lw.W_ffn_in, 0, w.ig, 8 * d, 0,
-               (int)rows, 8 * d, d, 0.f, 1, s));
-    const void* hid = w.h;
+    // --- FFN: x += W_out(SiLU(x_f W_in^T) * (x_f W_g^T))
+    const void* xf = ln_in(w.x, Lw.ln_f_w, Lw.ln_f_b, nullptr);
     if (bf) {
-      launch_silu_mul<__nv_bfloat16>(w.ig, w.bf, (int)rows, 4 * d, s);
-      hid = w.bf;
+      // the hidden leaves the GEMM as bf16 (SiLU-gate epilogue) into the h buffer
+      __nv_bfloat16* hid = reinterpret_cast<__nv_bfloat16*>(w.h);
+      Y_TRY(proj_bf16(xf, d, 0, Lw.W_ffn_in, 0, hid, 4 * d, 0, (int)rows, 2 * ffn_pad(d), d, 1,
+                      GEMM_EPI_SWIGLU, false, s, 4 * d));
+      Y_TRY(proj_bf16(hid, 4 * d, 0, Lw.W_ffn_out, 0, w.x, d, 0, (int)rows, d, 4 * d, 1, GEMM_EPI_F32, true,
+                      s));
     } else {
+      Y_TRY(gemm(m, xf, d, 0, Lw.W_ffn_in, 0, w.ig, 8 * d, 0, (int)rows, 8 * d, d, 0.f, 1, s));
       launch_silu_mul<float>(w.ig, w.h, (int)rows, 4 * d, s);
+      Y_TRY(gemm(m, w.h, 4 * d, 0, Lw.W_ffn_out, 0, w.x, d, 0, (int)rows, d, 4 * d, 1.f, 1, s));
     }
-    Y_TRY(gemm(m, hid, 4 * d, 0, Lw.W_ffn_out, 0, w.x, d, 0, (int)rows, d, 4 * d, 1.f, 1, s));
     if (m->debug) dump(m, "h3", li, w.x, RD, s);
   }
   // final norm + tied LM head
   const void* hn = ln_in(w.x, m->fin_w, m->fin_b, nullptr);
   const size_t esz = bf ? 2 : 4;
-  if (logits_all)
-    Y_TRY(gemm(m, hn, d, 0, m->emb_gemm, 0, logits_all, V, 0, (int)rows, V, d, 0.f, 1, s));
+  if (logits_all) {
+    if (bf)
+      Y_TRY(proj_bf16(hn, d, 0, m->emb_gemm, 0, logits_all, V, 0, (int)rows, V, d, 1, GEMM_EPI_F32, false, s));
+    else
+      Y_TRY(gemm(m, hn, d, 0, m->emb_gemm, 0, logits_all, V, 0, (int)rows, V, d, 0.f, 1, s));
+  }
   if (logits_last) {
     const void* last = static_cast<const char*>(hn) + (size_t)(T - 1) * d * esz;
-    Y_TRY(gemm(m, last, T * d, 0, m->emb_gemm, 0, logits_last, V, 0, B, V, d, 0.f, 1, s));
+    if (bf)
+      Y_TRY(proj_bf16(last, (long long)T * d, 0, m->emb_gemm, 0, logits_last, V, 0, B, V, d, 1, GEMM_EPI_F32,
+                      false, s));
+    else
+      Y_TRY(gemm(m, last, T * d, 0, m->emb_gemm, 0, logits_last, V, 0, B, V, d, 0.f, 1, s));
     if (m->debug) dump(m, "logits", -1, logits_last, (size_t)B * V, s);
   }
   return check_launch("model forward");
@@ -471,6 +536,33 @@ static yuf_status_t pack_weight(yuf_model* m, const std::unordered_map<std::stri
     Y_CUDA(cudaMemcpy(d, host.data(), total * 4, cudaMemcpyHostToDevice));
     *out = d;
   }
+  return YUF_OK;
+}
+
+// bf16 mode: ffn_in.weight and ffn_gate.weight ([F, d] each) interleaved in
+// 64-row groups -- rows 128g .. 128g+63 = ffn_in rows 64g .., rows 128g+64 ..
+// 128g+127 = the same ffn_gate rows -- with F padded to a multiple of 64 by zero
+// rows, the layout the GEMM's SiLU-gate epilogue pairs columns in.
+static yuf_status_t pack_ffn_in_bf16(yuf_model* m, const std::unordered_map<std::string, HostTensor>& t,
+                                     const std::string& in_name, const std::string& gate_name, void** out) {
+  const int d = m->d(), F = 4 * d, Fp = ffn_pad(d);
+  auto in = t.find(in_name), gate = t.find(gate_name);
+  Y_REQUIRE(in != t.end() && gate != t.end(), "model: missing tensor %s or %s", in_name.c_str(),
+            gate_name.c_str());
+  Y_REQUIRE(in->second.n == (int64_t)F * d && gate->second.n == (int64_t)F * d,
+            "model: %s / %s must hold %lld elements", in_name.c_str(), gate_name.c_str(), (long long)F * d);
+  std::vector<__nv_bfloat16> hb((size_t)2 * Fp * d, __float2bfloat16_rn(0.f));
+  for (int r = 0; r < F; ++r) {
+    const size_t dst_in = ((size_t)(r / 64) * 128 + r % 64) * d, dst_gate = dst_in + (size_t)64 * d;
+    for (int k = 0; k < d; ++k) {
+      hb[dst_in + k] = __float2bfloat16_rn(in->second.p[(size_t)r * d + k]);
+      hb[dst_gate + k] = __float2bfloat16_rn(gate->second.p[(size_t)r * d + k]);
+    }
+  }
+  void* dptr = m->alloc(hb.size() * 2);
+  if (!dptr) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+  Y_CUDA(cudaMemcpy(dptr, hb.data(), hb.size() * 2, cudaMemcpyHostToDevice));
+  *out = dptr;
   return YUF_OK;
 }
 
@@ -537,7 +629,10 @@ static yuf_status_t load_weights(yuf_model* m, const std::unordered_map<std::str
     Y_TRY(pack_weight(m, t, {ro + "output.weight"}, {d}, R, false, &Lw.W_rosa_out));
     Y_TRY(upload(m, t, p + "norm_ffn.weight", d, &Lw.ln_f_w));
     Y_TRY(upload(m, t, p + "norm_ffn.bias", d, &Lw.ln_f_b));
-    Y_TRY(pack_weight(m, t, {p + "ffn_in.weight", p + "ffn_gate.weight"}, {F, F}, d, false, &Lw.W_ffn_in));
+    if (m->precision == YUF_PRECISION_BF16_WEIGHTS)
+      Y_TRY(pack_ffn_in_bf16(m, t, p + "ffn_in.weight", p + "ffn_gate.weight", &Lw.W_ffn_in));
+    else
+      Y_TRY(pack_weight(m, t, {p + "ffn_in.weight", p + "ffn_gate.weight"}, {F, F}, d, false, &Lw.W_ffn_in));
     Y_TRY(pack_weight(m, t, {p + "ffn_out.weight"}, {d}, F, false, &Lw.W_ffn_out));
   }
   return YUF_OK;
@@ -562,6 +657,11 @@ yuf_status_t model_create_from_map(const yuf_model_config* cfg, int precision, i
             "model: unknown precision %d", precision);
   yuf_model_config c = *cfg;
   Y_TRY(validate_cfg(&c));
+  if (precision == YUF_PRECISION_BF16_WEIGHTS && c.rosa_size % 8 != 0) {
+    set_error("model: bf16-weight mode needs rosa_size %% 8 == 0 (16-byte rows for the tensor-core "
+              "GEMM), got %d", c.rosa_size);
+    return YUF_ERR_UNSUPPORTED;
+  }
   switch (c.head_size) {
     case 16: case 32: case 40: case 48: case 64: case 96: case 128: break;
     default: set_error("model: head_size %d has no kernel", c.head_size); return YUF_ERR_UNSUPPORTED;

@@ -1,0 +1,462 @@
+// Dense projections of the block on the 5th-generation tensor cores:
+//   C[z][M, N] = A[z][M, K] . W[z][N, K]^T       (bf16 operands, fp32 accumulate)
+// for the R/K/V, low-rank, output, ROSA, FFN and LM-head projections of
+// yufmusicgen/model.py:107-112, 195-197, 297-311, 376-377, 421.
+//
+// One persistent CTA per SM walks the output tiles (128 rows x BN columns) of
+// every batch z in a grouped order (8 row tiles x all column tiles per group,
+// so the rows and weights a wave of CTAs shares stay in L2).  Six warps with
+// fixed roles:
+//   warp 0   one thread issues the TMA loads: per 64-wide K block the A box
+//            (128 x 64) and the W box (BN x 64), 128-byte swizzled, into a ring
+//            of shared-memory stages guarded by full/empty mbarriers;
+//   warp 1   allocates 2*BN TMEM columns (two accumulators), and one thread
+//            issues the kind::f16 UMMAs (M = 128, N = BN, K = 16; four per
+//            stage), committing each stage back to its empty barrier and each
+//            finished tile to the accumulator's full barrier;
+//   warps 2-5  the epilogue: warp w reads TMEM lanes 32*(w % 4).., one output
+//            row per thread, 32 columns per tcgen05.ld, and writes the result
+//            (fp32 with an optional residual add, bf16 with an optional tanh, or
+//            SiLU(in) * gate for the FFN) straight to global memory, while the
+//            MMAs of the next tile run into the other accumulator.
+// Every mbarrier wait is bounded (WAIT_NS); a wait that expires raises the
+// CTA's abort flag, every role leaves its loop, the loads and MMAs still in
+// flight are waited for (bounded) before the TMEM is freed, and the expiry is
+// counted for yuf_wait_timeouts / yuf_sync_check.  No cluster multicast: each
+// CTA loads its own boxes.
+
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "mbarrier.cuh"
+#include "tcgen05.cuh"
+#include "tma.cuh"
+
+namespace yuf {
+
+__device__ unsigned int g_gemm_wait_timeouts;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128, BK = 64;           // BK bf16 = one 128-byte swizzle row
+  static constexpr int A_BYTES = BM * BK * 2;       // 16 KB
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;   // multiple of 1024
+  static constexpr int STAGES = std::min(8, (192 * 1024) / STAGE);
+  static constexpr uint32_t TMEM_COLS = 2 * BN;     // two fp32 accumulators of BN columns
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = STAGES * STAGE + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+  static constexpr int THREADS = 192;
+  static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
+  static_assert(STAGE % 1024 == 0, "stages stay 1024-byte aligned for the 128-byte swizzle");
+  static_assert(2 * STAGES * 8 + 4 * 8 + 8 + 8 <= BAR_BYTES, "barrier block");
+};
+
+// Tile t of the grouped walk -> (batch, row tile, column tile).
+YUF_DEVICE void gemm_tile(int t, int m_tiles, int n_tiles, int& z, int& mt, int& nt) {
+  constexpr int GM = 8;
+  const int per = m_tiles * n_tiles;
+  z = t / per;
+  const int r = t - z * per;
+  const int group = r / (GM * n_tiles);
+  const int first = group * GM;
+  const int gsz = min(GM, m_tiles - first);
+  const int rr = r - group * GM * n_tiles;
+  mt = first + rr % gsz;
+  nt = rr / gsz;
+}
+
+YUF_DEVICE float silu(float x) { return x / (1.f + expf(-x)); }
+
+// A bounded wait that gives up at once when another role already aborted.
+YUF_DEVICE bool gemm_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (*abort_flag) return false;
+  if (mbar_wait(bar, parity)) return true;
+  *abort_flag = 1;
+  return false;
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
+                     const GemmParams p) {
+  using G = GemmCfg<BN>;
+  extern __shared__ __align__(1024) unsigned char gemm_smem_raw[];
+  unsigned char* sm = gemm_smem_raw + ((1024u - (smem_u32(gemm_smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + G::STAGES * G::STAGE);
+  uint64_t* empty = full + G::STAGES;
+  uint64_t* tfull = empty + G::STAGES;   // [2] accumulator ready for the epilogue
+  uint64_t* tempty = tfull + 2;          // [2] accumulator drained by the epilogue
+  uint64_t* drain = tempty + 2;          // final commit of the MMA thread
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, G::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const int total = p.m_tiles * p.n_tiles * p.batch;
+  const int kblocks = (p.K + G::BK - 1) / G::BK;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---------------------------------------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        int z, mt, nt;
+        gemm_tile(t, p.m_tiles, p.n_tiles, z, mt, nt);
+        const int ay = (int)(z * p.a_brows) + mt * G::BM;
+        const int wy = (int)(z * p.w_brows) + nt * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!gemm_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          unsigned char* st = sm + stage * G::STAGE;
+          mbar_expect_tx(&full[stage], G::STAGE);
+          tma_load_2d(st, &ta, &full[stage], kb * G::BK, ay);
+          tma_load_2d(st + G::A_BYTES, &tw, &full[stage], kb * G::BK, wy);
+          ++issued;
+          if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+      if (*abort_flag) {  // let the loads still in flight into this CTA's stages land
+        for (int s = 0; s < G::STAGES; ++s) {
+          if (issued <= s) break;
+          mbar_wait(&full[s], s < stage ? phase : phase ^ 1u);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ------------------------------------------------- MMA issuer
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool any = false;
+      for (int t = blockIdx.x; t < total; t += gridDim.x) {
+        if (!gemm_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after_sync();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!gemm_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after_sync();
+          const uint32_t a0 = smem_u32(sm + stage * G::STAGE), b0 = a0 + G::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < G::BK / 16; ++kk)
+            umma_bf16(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), G::IDESC,
+                      (kb | kk) != 0 ? 1u : 0u);
+          any = true;
+          umma_commit(&empty[stage]);  // the stage is free once these MMAs have read it
+          if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);  // the tile's accumulator is complete
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (any) {  // every MMA issued has finished before the columns are freed
+        umma_commit(drain);
+        mbar_wait(drain, 0);
+      }
+    }
+  } else {  // ---------------------------------------------------- epilogue (warps 2-5)
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      int z, mt, nt;
+      gemm_tile(t, p.m_tiles, p.n_tiles, z, mt, nt);
+      bool ok = gemm_wait(&tfull[acc], acc_phase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after_sync();
+      const int row = mt * G::BM + q * 32 + lane;
+      const bool live = row < p.M;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      if constexpr (EPI == GEMM_EPI_SWIGLU) {
+        // tile columns per 128: [64 "in" rows | 64 "gate" rows] of the packed weight
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+#pragma unroll 1
+        for (int sb = 0; sb < BN / 128; ++sb)
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            float vi[32], vg[32];
+            tmem_ld_x32(tbase + sb * 128 + h * 32, vi);
+            tmem_ld_x32(tbase + sb * 128 + 64 + h * 32, vg);
+            const int col = nt * (BN / 2) + sb * 64 + h * 32;
+            if (live) {
+              if (p.vec && col + 32 <= p.n_out) {
+#pragma unroll
+                for (int c = 0; c < 32; c += 8) {
+                  uint4 pk;
+                  __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    b2[e] = __floats2bfloat162_rn(silu(vi[c + 2 * e]) * vg[c + 2 * e],
+                                                  silu(vi[c + 2 * e + 1]) * vg[c + 2 * e + 1]);
+                  *reinterpret_cast<uint4*>(out + col + c) = pk;
+                }
+              } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                  if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(silu(vi[c]) * vg[c]);
+              }
+            }
+          }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          float v[32];
+          tmem_ld_x32(tbase + c0, v);
+          const int col = nt * BN + c0;
+          if (!live || col >= p.N) continue;
+          if constexpr (EPI == GEMM_EPI_F32) {
+            float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
+            if (p.vec && col + 32 <= p.N) {
+#pragma unroll
+              for (int c = 0; c < 32; c += 4) {
+                float4 o = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+                if (p.beta != 0.f) {
+                  const float4 old = *reinterpret_cast<const float4*>(out + c);
+                  o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+                }
+                *reinterpret_cast<float4*>(out + c) = o;
+              }
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                if (col + c < p.N) out[c] = p.beta != 0.f ? v[c] + out[c] : v[c];
+            }
+          } else {  // GEMM_EPI_BF16
+            if (p.tanh_batch0 && z == 0) {
+#pragma unroll
+              for (int c = 0; c < 32; ++c) v[c] = tanhf(v[c]);
+            }
+            __nv_bfloat16* out =
+                static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
+            if (p.vec && col + 32 <= p.N) {
+#pragma unroll
+              for (int c = 0; c < 32; c += 8) {
+                uint4 pk;
+                __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) b2[e] = __floats2bfloat162_rn(v[c + 2 * e], v[c + 2 * e + 1]);
+                *reinterpret_cast<uint4*>(out + c) = pk;
+              }
+            } else {
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                if (col + c < p.N) out[c] = __float2bfloat16_rn(v[c]);
+            }
+          }
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicAdd(&g_gemm_wait_timeouts, 1u);
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, G::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------- host side
+static int sm_count() {
+  static int cache[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+static bool make_bf16_map(CUtensorMap* m, const void* base, long long inner, long long rows,
+                          long long ld, int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t gdim[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)ld * 2};
+  const cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  const cuuint32_t estride[2] = {1u, 1u};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box,
+             estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+static yuf_status_t launch_gemm(const GemmArgs& g, GemmParams p, cudaStream_t s) {
+  using G = GemmCfg<BN>;
+  static std::once_flag attr_once[128];
+  static cudaError_t attr_err[128];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 127;
+  std::call_once(attr_once[dev], [&] {
+    attr_err[dev] = cudaFuncSetAttribute(gemm_bf16_kernel<BN, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+  });
+  if (attr_err[dev] != cudaSuccess) {
+    set_error("gemm: cannot set %d bytes of shared memory: %s", G::SMEM, cudaGetErrorString(attr_err[dev]));
+    return YUF_ERR_CUDA;
+  }
+  CUtensorMap ta, tw;
+  if (!make_bf16_map(&ta, g.A, g.K, g.a_rows, g.lda, G::BM) ||
+      !make_bf16_map(&tw, g.W, g.K, g.w_rows, g.K, BN)) {
+    set_error("gemm: cuTensorMapEncodeTiled failed (A rows %lld, lda %lld, W rows %lld, K %d)", g.a_rows,
+              g.lda, g.w_rows, g.K);
+    return YUF_ERR_CUDA;
+  }
+  p.n_tiles = (p.N + BN - 1) / BN;
+  const long long total = (long long)p.m_tiles * p.n_tiles * p.batch;
+  const int grid = (int)std::min<long long>(total, sm_count());
+  gemm_bf16_kernel<BN, EPI><<<grid, G::THREADS, G::SMEM, s>>>(ta, tw, p);
+  return check_launch("gemm_bf16_kernel");
+}
+
+yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
+  if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return YUF_OK;
+  const bool a_ok = (reinterpret_cast<uintptr_t>(g.A) & 15) == 0 && g.lda % 8 == 0;
+  const bool w_ok = (reinterpret_cast<uintptr_t>(g.W) & 15) == 0;
+  if (!a_ok || !w_ok || g.K % 8 != 0 || g.K <= 0) {
+    set_error("gemm: operands need 16-byte aligned rows (A %p lda %lld, W %p, K %d)", g.A, g.lda, g.W, g.K);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  GemmParams p{};
+  p.C = g.C;
+  p.ldc = g.ldc;
+  p.c_bstride = g.c_bstride;
+  p.M = g.M;
+  p.N = g.N;
+  p.K = g.K;
+  p.batch = g.batch;
+  p.a_brows = g.a_brows;
+  p.w_brows = g.w_brows;
+  p.beta = g.beta;
+  p.tanh_batch0 = g.tanh_batch0;
+  p.n_out = g.epi == GEMM_EPI_SWIGLU ? g.n_out : g.N;
+  p.m_tiles = (g.M + 127) / 128;
+  const int esz = g.epi == GEMM_EPI_F32 ? 4 : 2;
+  const int vec_elems = 16 / esz;
+  p.vec = (reinterpret_cast<uintptr_t>(g.C) & 15) == 0 && g.ldc % vec_elems == 0 &&
+          g.c_bstride % vec_elems == 0;
+  const int sms = sm_count();
+  auto tiles = [&](int bn) { return (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch; };
+  if (g.epi == GEMM_EPI_SWIGLU) {
+    if (g.N % 128 != 0) {
+      set_error("gemm: the SiLU-gate weight must hold whole 128-row groups (N = %d)", g.N);
+      return YUF_ERR_INVALID_ARGUMENT;
+    }
+    return tiles(256) >= sms && g.N % 256 == 0 ? launch_gemm<256, GEMM_EPI_SWIGLU>(g, p, s)
+                                               : launch_gemm<128, GEMM_EPI_SWIGLU>(g, p, s);
+  }
+  int bn = 128;
+  if (g.N <= 64 || tiles(128) < sms) bn = 64;
+  else if (g.N % 256 == 0 || g.N >= 4096) bn = 256;
+  if (g.epi == GEMM_EPI_F32) {
+    if (bn == 64) return launch_gemm<64, GEMM_EPI_F32>(g, p, s);
+    if (bn == 128) return launch_gemm<128, GEMM_EPI_F32>(g, p, s);
+    return launch_gemm<256, GEMM_EPI_F32>(g, p, s);
+  }
+  if (bn == 64) return launch_gemm<64, GEMM_EPI_BF16>(g, p, s);
+  if (bn == 128) return launch_gemm<128, GEMM_EPI_BF16>(g, p, s);
+  return launch_gemm<256, GEMM_EPI_BF16>(g, p, s);
+}
+
+unsigned int gemm_wait_timeouts() {
+  unsigned int n = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&n, g_gemm_wait_timeouts, sizeof(n)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_gemm_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess) {
+    cudaGetLastError();
+    return ~0u;
+  }
+  return n;
+}
+
+}  // namespace yuf
+
+using namespace yuf;
+
+extern "C" yuf_status_t yuf_gemm_bf16(const void* A, long long lda, long long a_batch_rows, const void* W,
+                                      long long w_batch_rows, void* C, long long ldc,
+                                      long long c_batch_stride, int M, int N, int K, int batch,
+                                      int epilogue, int accumulate, int n_out, void* stream) {
+  if (!A || !W || !C || M < 0 || N < 0 || K <= 0 || batch < 0 || lda < K || ldc < 1) {
+    set_error("gemm: null operand or bad sizes (M=%d N=%d K=%d batch=%d lda=%lld ldc=%lld)", M, N, K, batch,
+              lda, ldc);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  if (epilogue < YUF_GEMM_F32 || epilogue > YUF_GEMM_SILU_GATE) {
+    set_error("gemm: unknown epilogue %d", epilogue);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  if (accumulate && epilogue != YUF_GEMM_F32) {
+    set_error("gemm: accumulate needs the fp32 epilogue");
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  if (epilogue == YUF_GEMM_SILU_GATE && (n_out <= 0 || 2 * (long long)n_out > N)) {
+    set_error("gemm: the SiLU-gate epilogue needs 0 < n_out <= N / 2 (n_out=%d N=%d)", n_out, N);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  if (batch > 1 && (a_batch_rows < M || w_batch_rows < N)) {
+    set_error("gemm: batches overlap (a_batch_rows %lld < M or w_batch_rows %lld < N)", a_batch_rows,
+              w_batch_rows);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  GemmArgs g{};
+  g.A = A;
+  g.lda = lda;
+  g.a_brows = batch > 1 ? a_batch_rows : 0;
+  g.a_rows = (long long)(batch > 1 ? batch - 1 : 0) * g.a_brows + M;
+  g.W = W;
+  g.w_brows = batch > 1 ? w_batch_rows : 0;
+  g.w_rows = (long long)(batch > 1 ? batch - 1 : 0) * g.w_brows + N;
+  g.C = C;
+  g.ldc = ldc;
+  g.c_bstride = c_batch_stride;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.batch = batch;
+  g.epi = epilogue == YUF_GEMM_F32 ? GEMM_EPI_F32
+                                   : (epilogue == YUF_GEMM_SILU_GATE ? GEMM_EPI_SWIGLU : GEMM_EPI_BF16);
+  g.beta = accumulate ? 1.f : 0.f;
+  g.tanh_batch0 = epilogue == YUF_GEMM_BF16_TANH0;
+  g.n_out = n_out;
+  return gemm_bf16(g, static_cast<cudaStream_t>(stream));
+}

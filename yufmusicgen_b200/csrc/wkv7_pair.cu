@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "mbarrier.cuh"
 #include "tcgen05.cuh"
+#include "tma.cuh"
 
 namespace yuf {
 
@@ -40,12 +41,6 @@ struct PairTmaps {
 
 __device__ unsigned int g_pair_wait_timeouts;
 
-YUF_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
 YUF_DEVICE size_t item_head_off(int bb, int hh, int K, int H, int N, int Tstride, int Cper) {
   return (((size_t)(bb / Cper) * Tstride + (size_t)(bb % Cper) * K) * H + hh) * N;
 }
@@ -875,7 +870,7 @@ int wkv7_correct_max_chunk(int N) {
 }
 
 // cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
-static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
