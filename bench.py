@@ -46,7 +46,8 @@ fallback (a Python loop of einsums per token), so they are stronger baselines.
 
 ``--only headline`` runs just the config-2 steps (the command the profiles'
 ncu captures use); ``--only model`` just one rank's config-3 prefill and
-config-4 decode step timings.
+config-4 decode step timings (fp32 and bf16 weights); ``--only prefill`` /
+``--only decode`` just the bf16-weight config-3 prefill / config-4 decode step.
 """
 
 from __future__ import annotations
@@ -78,7 +79,7 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--only", choices=["all", "headline", "model"], default="all")
+    p.add_argument("--only", choices=["all", "headline", "model", "prefill", "decode"], default="all")
     return p.parse_args()
 
 
@@ -481,7 +482,7 @@ def headline_keys(sh, world):
     }
 
 
-def measure_model(dev, stream):
+def measure_model(dev, stream, parts=("prefill", "decode"), precisions=("fp32", "bf16")):
     """The 0.1B model (benchmark config 3/4 shapes) through the engine:
     prefill tokens/s (B2 x T2048) in fp32 and bf16-weight mode, and batched
     greedy decode tokens/s (256 sequences, 64-token prompts, config 4's batch)."""
@@ -497,7 +498,7 @@ def measure_model(dev, stream):
     w = init_weights(cfg, 1, "baseline")
     res = {}
     ids = torch.as_tensor(zipf_ids(2, 2048, seed=1, vocab=cfg.vocab_size), dtype=torch.int32, device=dev)
-    for prec in ("fp32", "bf16"):
+    for prec in (precisions if "prefill" in parts else ()):
         eng = Engine(cfg, w, precision=prec, device=dev.index, n_slots=2)
         last = torch.empty(2, cfg.vocab_size, device=dev)
 
@@ -512,7 +513,7 @@ def measure_model(dev, stream):
     # batched decode, config 4 shape: 256 sequences, 64-token byte prompts
     Bd, steps = 256, 32
     side = torch.cuda.Stream(dev)
-    for prec in ("fp32", "bf16"):
+    for prec in (precisions if "decode" in parts else ()):
       with torch.cuda.stream(side):
         eng = Engine(cfg, w, precision=prec, device=dev.index, n_slots=Bd)
         eng.set_decode_graphs(True)
@@ -577,8 +578,10 @@ def run_ours(args):
     def step():
         cuda_ops.wkv7_forward(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], None, out=y, state_out=s)
 
-    if args.only == "model":
-        print(json.dumps({"only": "model", "model": measure_model(dev, stream)}), flush=True)
+    if args.only in ("model", "prefill", "decode"):
+        parts = ("prefill", "decode") if args.only == "model" else (args.only,)
+        precs = ("fp32", "bf16") if args.only == "model" else ("bf16",)
+        print(json.dumps({"only": args.only, "model": measure_model(dev, stream, parts, precs)}), flush=True)
         return
     for _ in range(max(3, args.warmup)):
         step()
