@@ -286,6 +286,29 @@ yuf_status_t yuf_sample(const float* logits, int B, int V, float temperature, in
 yuf_status_t yuf_philox_uniform(uint64_t seed, uint64_t step, int seq0, int n, float* out,
                                 void* stream);
 
+/* Host-side sampling with the reference's own random stream (no GPU): the
+ * sample_token rule of yufmusicgen/cli/generate.py:45-56 -- logits / temperature
+ * (<= 0: argmax), descending sort, softmax, drop an entry when the mass before
+ * it exceeds top_p, softmax again, torch.multinomial(p, 1) -- on a generator
+ * equal to torch's CPU generator after torch.manual_seed(seed) (MT19937; the
+ * bit-level reading of vulkan/src/sampler.rs:1-270).  A draw consumes one Exp(1)
+ * key per vocabulary entry, in sorted order, and takes argmax(p / key), as the
+ * CPU multinomial does for one sample; rows of a batch draw one after another
+ * (the order torch fills a [B, V] batch in).  Probabilities use the C library's
+ * expf, so a token can differ from torch's only where two keys tie to the last
+ * bit.  Not thread-safe per generator. */
+typedef struct yuf_mt19937 yuf_mt19937; /* opaque */
+yuf_status_t yuf_mt19937_create(uint64_t seed, yuf_mt19937** out);
+yuf_status_t yuf_mt19937_destroy(yuf_mt19937* rng);
+/* The next n raw 32-bit words of the generator. */
+yuf_status_t yuf_mt19937_next(yuf_mt19937* rng, uint32_t* out, int64_t n);
+/* The next n Exp(1) draws as torch's CPU Tensor.exponential_() makes them. */
+yuf_status_t yuf_mt19937_exponential(yuf_mt19937* rng, float* out, int64_t n);
+/* One token per row of host logits [B, V] (masked entries -inf) into host
+ * out_ids [B]. */
+yuf_status_t yuf_sample_host(const float* logits, int B, int V, float temperature, float top_p,
+                             yuf_mt19937* rng, int32_t* out_ids);
+
 /* Sampling rule of yuf_generate (the reference loop's knobs, cli/generate.py:34-56,
  * 142-149, plus the top-k / Philox stream of benchmark config 4). */
 typedef struct yuf_generate_params {

@@ -17,7 +17,8 @@ Every fixture is produced by the reference's own PyTorch fp32 CPU code:
 
 ``python tests/golden/make_golden.py grads`` writes only the gradient fixture,
 ``... greedy256`` only the 256-step greedy decode of the 0.1B model, ``... long``
-only the benchmark-size prefills (config 3 in full, config-5 geometry).
+only the benchmark-size prefills (config 3 in full, config-5 geometry), ``...
+sampler`` only the reference's sampled-decode draws.
 
 The fixtures are small ``.npz`` files; the GPU box never needs the reference.
 """
@@ -283,6 +284,97 @@ def long_cases():
                     positions=[0, 255, 256, 511], layers=[0, 12, 23])
 
 
+def sampler_cases():
+    """The reference's sampled decode rule, drawn by the reference itself:
+    ``sample_token`` of yufmusicgen/cli/generate.py:45-56 (temperature, sort,
+    top-p cut, ``torch.multinomial`` on the CPU MT19937 stream after
+    ``torch.manual_seed``), applied to rows masked as the reference's loop masks
+    them (generate.py:142-149: ids below MIDI_OFFSET = 260 excluded, EOS = 2
+    selectable from step MIN_MIDI_TOKENS_BEFORE_EOS = 16 on).  The CLI module
+    imports the MIDI codec packages (miditok, symusic), which are absent here
+    and unused by ``sample_token``; empty stand-ins let the import succeed.
+    Stored per case: the masked logits rows (in call order), the knobs, the seed
+    and the tokens (logits are float16-representable and stored as float16, so
+    the float32 rows are exact); plus raw Exp(1) draws of the generator (the
+    multinomial's per-element keys)."""
+    import types
+
+    class _Stub(types.ModuleType):
+        def __getattr__(self, name):
+            if name.startswith("__"):
+                raise AttributeError(name)
+            return type(name, (), {})
+
+    for name in ("miditok", "symusic", "miditok.classes", "symusic.core"):
+        sys.modules.setdefault(name, _Stub(name))
+    from yufmusicgen.cli.generate import MIN_MIDI_TOKENS_BEFORE_EOS, sample_token
+    from yufmusicgen.tokenizer import EOS, MIDI_OFFSET
+
+    out = {}
+    cases = [  # name, vocab, rows, temperature, top_p, seed, logit scale
+        ("v20000_t1_p095", 20000, 20, 1.0, 0.95, 1337, 3.0),
+        ("v20000_t08_p05", 20000, 12, 0.8, 0.5, 7, 4.0),
+        ("v673_t13_p1", 673, 48, 1.3, 1.0, 2024, 2.0),
+        ("v673_t1_p09_peaked", 673, 40, 1.0, 0.9, 5, 8.0),
+        ("v673_greedy", 673, 8, 0.0, 0.95, 11, 2.0),
+    ]
+    for name, V, rows, temp, top_p, seed, scale in cases:
+        g = torch.Generator().manual_seed(seed + 99)
+        # fp16-representable values, stored as float16 (exact as float32)
+        raw = (torch.randn(rows, V, generator=g) * scale).half().float()
+        masked = torch.full_like(raw, float("-inf"))
+        masked[:, MIDI_OFFSET:] = raw[:, MIDI_OFFSET:]
+        for i in range(rows):
+            if i >= MIN_MIDI_TOKENS_BEFORE_EOS:
+                masked[i, EOS] = raw[i, EOS]
+        torch.manual_seed(seed)
+        toks = [int(sample_token(masked[i:i + 1], temp, top_p).item()) for i in range(rows)]
+        out[f"{name}.logits"] = masked.numpy().astype(np.float16)
+        out[f"{name}.tokens"] = np.asarray(toks, np.int64)
+        out[f"{name}.knobs"] = np.asarray([temp, top_p], np.float64)
+        out[f"{name}.seed"] = np.int64(seed)
+    torch.manual_seed(1337)
+    out["exp_draws_seed1337"] = torch.empty(3000).exponential_().numpy()
+    # the reference's whole sampled loop on the 0.1B model (config-4 prompt,
+    # temperature 1.0, top-p 0.95, seed 1337), written out as run_generation
+    # runs it (generate.py:130-152) around the reference's own sample_token and
+    # YufMusicGen.forward / .step; per step also the margin of the draw: the
+    # winning key p/q over the runner-up's, minus 1 (keys replayed from the
+    # generator state before the draw)
+    cfg = C.ModelConfig(**C.BASE_0P1B)
+    model = ref_model(C.BASE_0P1B, init_weights(cfg, 1, "baseline"))
+    prompt = zipf_ids(1, 64, seed=4, vocab=cfg.vocab_size)
+    torch.manual_seed(1337)
+    toks, margins = [], []
+    with torch.no_grad():
+        logits, st = model(t(prompt))
+        logits = logits[:, -1]
+        for index in range(48):
+            allowed = torch.full_like(logits, float("-inf"))
+            allowed[:, MIDI_OFFSET:] = logits[:, MIDI_OFFSET:]
+            if index >= MIN_MIDI_TOKENS_BEFORE_EOS:
+                allowed[:, EOS] = logits[:, EOS]
+            state = torch.get_rng_state()
+            x = allowed / 1.0
+            sl, _ = torch.sort(x, descending=True, dim=-1)
+            pr = torch.softmax(sl, -1)
+            sl = sl.masked_fill(torch.cumsum(pr, -1) - pr > 0.95, float("-inf"))
+            keys = torch.softmax(sl, -1) / torch.empty_like(sl).exponential_()
+            top2 = torch.topk(keys[0], 2).values
+            margins.append(float(top2[0] / top2[1] - 1))
+            torch.set_rng_state(state)
+            token = sample_token(allowed, 1.0, 0.95)
+            if int(token.item()) == EOS:
+                break
+            toks.append(int(token.item()))
+            logits, st = model.step(token, st)
+    out["decode.prompt"] = prompt
+    out["decode.tokens"] = np.asarray(toks, np.int64)
+    out["decode.margins"] = np.asarray(margins, np.float64)
+    out["cases"] = np.array([c[0] for c in cases])
+    np.savez_compressed(HERE / "sampler_torch_cpu.npz", **out)
+
+
 def state_test_case():
     """The reference's own sequence-vs-step test (tests/test_model_state.py:9-28),
     with the reference recurrence selected (use_rosa_scan=False)."""
@@ -357,6 +449,8 @@ if __name__ == "__main__":
         grad_cases()
     elif sys.argv[1:] == ["long"]:
         long_cases()
+    elif sys.argv[1:] == ["sampler"]:
+        sampler_cases()
     elif sys.argv[1:] == ["greedy256"]:
         greedy256_case()
     else:
@@ -364,3 +458,4 @@ if __name__ == "__main__":
         grad_cases()
         greedy256_case()
         long_cases()
+        sampler_cases()

@@ -119,3 +119,19 @@ def test_top_p_above_one_keeps_the_whole_top_k():
     b, _ = eng.generate(prompt, 12, temperature=1.0, top_k=16, top_p=1.5, seed=4)
     np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
     eng.close()
+
+
+def test_sampled_decode_with_the_references_stream(golden):
+    """The reference's own sampled generation (tests/golden/sampler_torch_cpu.npz:
+    run_generation's loop on the 0.1B model, temperature 1, top-p 0.95,
+    torch.manual_seed(1337), 48 steps): the engine's loop with the host MT19937
+    sampler draws the same tokens.  fp32 logits within 1e-3 / 1e-4 of the
+    reference cannot flip a draw whose winning key leads by the fixture's
+    smallest margin (1.4e-3)."""
+    g = golden("sampler_torch_cpu.npz")
+    cfg = C.ModelConfig(**C.BASE_0P1B)
+    eng = Engine(cfg, init_weights(cfg, 1, "baseline"), n_slots=1)
+    toks = eng.generate_reference_stream(g["decode.prompt"], len(g["decode.tokens"]), temperature=1.0,
+                                         top_p=0.95, seed=1337)
+    np.testing.assert_array_equal(toks, g["decode.tokens"])
+    eng.close()

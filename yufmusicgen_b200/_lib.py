@@ -54,6 +54,11 @@ SIGNATURES = {
     "yuf_sync_check": [P],
     "yuf_debug_wait_selftest": [ctypes.c_ulonglong, P],
     "yuf_model_set_debug": [P, I],
+    "yuf_mt19937_create": [ctypes.c_uint64, P],
+    "yuf_mt19937_destroy": [P],
+    "yuf_mt19937_next": [P, P, ctypes.c_int64],
+    "yuf_mt19937_exponential": [P, P, ctypes.c_int64],
+    "yuf_sample_host": [P, I, I, ctypes.c_float, ctypes.c_float, P, P],
     "yuf_gemm_bf16": [P, ctypes.c_longlong, ctypes.c_longlong, P, ctypes.c_longlong, P, ctypes.c_longlong,
                       ctypes.c_longlong, I, I, I, I, I, I, I, P],
     "yuf_model_set_debug_filter": [P, ctypes.c_char_p, P, I],

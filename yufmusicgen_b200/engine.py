@@ -167,6 +167,44 @@ class Engine:
                       ctypes.byref(p), toks.data_ptr(), lens.data_ptr(), self._stream())
         return toks, lens
 
+    def generate_reference_stream(self, prompt_ids, n_steps: int, temperature: float = 1.0,
+                                  top_p: float = 0.95, seed: int = 1337, mask_below: int = 260,
+                                  eos_id: int = 2, min_tokens_before_eos: int = 16, slot0: int = 0):
+        """The reference's sampled decode with the reference's random stream:
+        the loop of run_generation (yufmusicgen/cli/generate.py:130-154) --
+        mask to MIDI ids (and EOS from step ``min_tokens_before_eos`` on),
+        ``sample_token``'s temperature / top-p rule, ``torch.multinomial`` on the
+        CPU generator after ``torch.manual_seed(seed)`` (host MT19937,
+        ``yuf_sample_host``), stop at EOS -- so a fixed seed yields the tokens
+        the reference's CPU loop draws.  Each step copies the logits to the host
+        (the reference synchronises per token too).  One sequence per call, as
+        the reference generates; returns the generated ids (EOS not included)."""
+        import numpy as np
+
+        from .sampler import TorchCpuGenerator, mask_like_reference
+
+        ids = self._ids(prompt_ids)
+        if ids.shape[0] != 1:
+            raise ValueError("the reference's loop generates one sequence at a time")
+        gen = TorchCpuGenerator(seed)
+        self.reset_state(slot0, 1)
+        logits = self.prefill(ids, slot0=slot0)
+        out = []
+        tok = torch.empty(1, dtype=torch.int32, device=self.device)
+        try:
+            for step in range(n_steps):
+                row = mask_like_reference(logits.cpu().numpy(), step, mask_below, eos_id,
+                                          min_tokens_before_eos)
+                t = int(gen.sample(row, temperature, top_p)[0])
+                if t == eos_id:
+                    break
+                out.append(t)
+                tok.fill_(t)
+                logits = self.step(tok, slot0=slot0)
+        finally:
+            gen.close()
+        return np.asarray(out, np.int64)
+
     def set_decode_graphs(self, enabled: bool = True):
         """Replay decode steps as CUDA graphs (needs a non-default stream)."""
         _lib.call("yuf_model_set_decode_graphs", self._h, 1 if enabled else 0)

@@ -44,3 +44,68 @@ def philox_uniform(seed: int, step: int, seq0: int, n: int, device="cuda"):
     _lib.call("yuf_philox_uniform", int(seed) & (2**64 - 1), int(step) & (2**64 - 1), int(seq0), n,
               out.data_ptr(), torch.cuda.current_stream(out.device).cuda_stream)
     return out
+
+
+class TorchCpuGenerator:
+    """Host generator with the reference's random stream (C ABI ``yuf_mt19937_*``):
+    the state of torch's CPU generator after ``torch.manual_seed(seed)``, which
+    the reference's generation loop samples from (yufmusicgen/training.py:23-28,
+    cli/generate.py:45-56)."""
+
+    def __init__(self, seed: int):
+        import ctypes
+
+        self._h = ctypes.c_void_p()
+        _lib.call("yuf_mt19937_create", int(seed) & (2**64 - 1), ctypes.byref(self._h))
+
+    def close(self):
+        if self._h:
+            _lib.call("yuf_mt19937_destroy", self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def next_u32(self, n: int):
+        import numpy as np
+
+        out = np.empty(n, np.uint32)
+        _lib.call("yuf_mt19937_next", self._h, out.ctypes.data, n)
+        return out
+
+    def exponential(self, n: int):
+        import numpy as np
+
+        out = np.empty(n, np.float32)
+        _lib.call("yuf_mt19937_exponential", self._h, out.ctypes.data, n)
+        return out
+
+    def sample(self, logits, temperature: float = 1.0, top_p: float = 0.95):
+        """The reference's ``sample_token`` on host logits [B, V] (or [V]); rows
+        draw one after another."""
+        import numpy as np
+
+        x = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
+        one = x.ndim == 1
+        x = x.reshape(1, -1) if one else x
+        out = np.empty(x.shape[0], np.int32)
+        _lib.call("yuf_sample_host", x.ctypes.data, x.shape[0], x.shape[1], float(temperature),
+                  float(top_p), self._h, out.ctypes.data)
+        return int(out[0]) if one else out
+
+
+def mask_like_reference(logits, step: int, mask_below: int = MIDI_OFFSET, eos_id: int = EOS,
+                        min_before_eos: int = 16):
+    """The reference loop's masking (generate.py:142-147) on host logits [B, V]:
+    ids below MIDI_OFFSET become -inf, EOS stays selectable from step 16 on."""
+    import numpy as np
+
+    x = np.array(logits, dtype=np.float32, copy=True)
+    keep_eos = x[..., eos_id].copy()
+    x[..., :mask_below] = -np.inf
+    if step >= min_before_eos:
+        x[..., eos_id] = keep_eos
+    return x
