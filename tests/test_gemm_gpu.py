@@ -1,5 +1,7 @@
 """The tcgen05 projection GEMM (yuf_gemm_bf16) against a float64 product of the
-same bf16 operands, through the C ABI, at the engine's shapes (configs 1, 3, 4
+same bf16 operands.  Shapes with at least 512 rows and columns and enough 256 x
+256 tiles run on CTA pairs (cta_group::2), the others on single CTAs; both are
+covered.  Compared through the C ABI, at the engine's shapes (configs 1, 3, 4
 and 5: R/K/V, low-rank, output, ROSA, FFN, LM head; prefill rows and decode
 batches) and at ragged ones (rows, columns and K that are not tile multiples,
 unaligned output strides).
@@ -52,6 +54,7 @@ SHAPES = [  # (M, N, K, batch): engine projections at config 3 / 4 / 5 / 1 sizes
     (4096, 640, 2560, 1), (256, 640, 640, 3), (256, 20000, 640, 1), (8192, 1024, 1024, 1),
     (512, 128, 128, 3), (512, 512, 32, 1),
     (1, 64, 32, 1), (100, 100, 40, 1), (129, 200, 72, 2), (300, 1000, 1024, 1), (777, 96, 136, 3),
+    (3000, 1300, 200, 3), (2048, 2048, 4096, 1),  # CTA-pair kernel with ragged edges; long K
 ]
 
 
@@ -65,7 +68,8 @@ def test_gemm_fp32_output_batched(M, N, K, batch):
     check(C, want, K)
 
 
-@pytest.mark.parametrize("M,N,K", [(4096, 640, 640), (4096, 640, 2560), (256, 640, 128), (33, 100, 64)])
+@pytest.mark.parametrize("M,N,K", [(4096, 640, 640), (4096, 640, 2560), (256, 640, 128), (33, 100, 64),
+                                   (4096, 1280, 640)])
 def test_gemm_accumulates_into_the_residual(M, N, K):
     A = rnd(M, K, seed=1)
     W = rnd(N, K, seed=2, scale=0.05)

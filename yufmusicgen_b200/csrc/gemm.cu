@@ -81,6 +81,93 @@ YUF_DEVICE bool gemm_wait(uint64_t* bar, uint32_t parity, volatile int* abort_fl
   return false;
 }
 
+// Epilogue of one output tile held in TMEM (lanes = rows, columns = outputs):
+// the calling warp's 32 rows, `row` this thread's, `tbase` the TMEM address of
+// the warp's lane quarter at the tile's first column; tile column block `nt` of
+// BN columns (SiLU-gate: BN / 2 output columns).  Every lane runs the TMEM loads
+// (warp-collective); only live rows store.
+template <int BN, int EPI>
+YUF_DEVICE void gemm_epilogue_tile(const GemmParams& p, uint32_t tbase, int z, int row, int nt, bool live) {
+  if constexpr (EPI == GEMM_EPI_SWIGLU) {
+    // tile columns per 128: [64 "in" rows | 64 "gate" rows] of the packed weight
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+#pragma unroll 1
+    for (int sb = 0; sb < BN / 128; ++sb)
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        float vi[32], vg[32];
+        tmem_ld_x32(tbase + sb * 128 + h * 32, vi);
+        tmem_ld_x32(tbase + sb * 128 + 64 + h * 32, vg);
+        const int col = nt * (BN / 2) + sb * 64 + h * 32;
+        if (live) {
+          if (p.vec && col + 32 <= p.n_out) {
+#pragma unroll
+            for (int c = 0; c < 32; c += 8) {
+              uint4 pk;
+              __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                b2[e] = __floats2bfloat162_rn(silu(vi[c + 2 * e]) * vg[c + 2 * e],
+                                              silu(vi[c + 2 * e + 1]) * vg[c + 2 * e + 1]);
+              *reinterpret_cast<uint4*>(out + col + c) = pk;
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(silu(vi[c]) * vg[c]);
+          }
+        }
+      }
+  } else {
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      float v[32];
+      tmem_ld_x32(tbase + c0, v);
+      const int col = nt * BN + c0;
+      if (!live || col >= p.N) continue;
+      if constexpr (EPI == GEMM_EPI_F32) {
+        float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
+        if (p.vec && col + 32 <= p.N) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 4) {
+            float4 o = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+            if (p.beta != 0.f) {
+              const float4 old = *reinterpret_cast<const float4*>(out + c);
+              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+            }
+            *reinterpret_cast<float4*>(out + c) = o;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (col + c < p.N) out[c] = p.beta != 0.f ? v[c] + out[c] : v[c];
+        }
+      } else {  // GEMM_EPI_BF16
+        if (p.tanh_batch0 && z == 0) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = tanhf(v[c]);
+        }
+        __nv_bfloat16* out =
+            static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
+        if (p.vec && col + 32 <= p.N) {
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint4 pk;
+            __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) b2[e] = __floats2bfloat162_rn(v[c + 2 * e], v[c + 2 * e + 1]);
+            *reinterpret_cast<uint4*>(out + c) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (col + c < p.N) out[c] = __float2bfloat16_rn(v[c]);
+        }
+      }
+    }
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
@@ -196,84 +283,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
       const int row = mt * G::BM + q * 32 + lane;
       const bool live = row < p.M;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      if constexpr (EPI == GEMM_EPI_SWIGLU) {
-        // tile columns per 128: [64 "in" rows | 64 "gate" rows] of the packed weight
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
-#pragma unroll 1
-        for (int sb = 0; sb < BN / 128; ++sb)
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            float vi[32], vg[32];
-            tmem_ld_x32(tbase + sb * 128 + h * 32, vi);
-            tmem_ld_x32(tbase + sb * 128 + 64 + h * 32, vg);
-            const int col = nt * (BN / 2) + sb * 64 + h * 32;
-            if (live) {
-              if (p.vec && col + 32 <= p.n_out) {
-#pragma unroll
-                for (int c = 0; c < 32; c += 8) {
-                  uint4 pk;
-                  __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-                  for (int e = 0; e < 4; ++e)
-                    b2[e] = __floats2bfloat162_rn(silu(vi[c + 2 * e]) * vg[c + 2 * e],
-                                                  silu(vi[c + 2 * e + 1]) * vg[c + 2 * e + 1]);
-                  *reinterpret_cast<uint4*>(out + col + c) = pk;
-                }
-              } else {
-#pragma unroll
-                for (int c = 0; c < 32; ++c)
-                  if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(silu(vi[c]) * vg[c]);
-              }
-            }
-          }
-      } else {
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          float v[32];
-          tmem_ld_x32(tbase + c0, v);
-          const int col = nt * BN + c0;
-          if (!live || col >= p.N) continue;
-          if constexpr (EPI == GEMM_EPI_F32) {
-            float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
-            if (p.vec && col + 32 <= p.N) {
-#pragma unroll
-              for (int c = 0; c < 32; c += 4) {
-                float4 o = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
-                if (p.beta != 0.f) {
-                  const float4 old = *reinterpret_cast<const float4*>(out + c);
-                  o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-                }
-                *reinterpret_cast<float4*>(out + c) = o;
-              }
-            } else {
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                if (col + c < p.N) out[c] = p.beta != 0.f ? v[c] + out[c] : v[c];
-            }
-          } else {  // GEMM_EPI_BF16
-            if (p.tanh_batch0 && z == 0) {
-#pragma unroll
-              for (int c = 0; c < 32; ++c) v[c] = tanhf(v[c]);
-            }
-            __nv_bfloat16* out =
-                static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
-            if (p.vec && col + 32 <= p.N) {
-#pragma unroll
-              for (int c = 0; c < 32; c += 8) {
-                uint4 pk;
-                __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) b2[e] = __floats2bfloat162_rn(v[c + 2 * e], v[c + 2 * e + 1]);
-                *reinterpret_cast<uint4*>(out + c) = pk;
-              }
-            } else {
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                if (col + c < p.N) out[c] = __float2bfloat16_rn(v[c]);
-            }
-          }
-        }
-      }
+      gemm_epilogue_tile<BN, EPI>(p, tbase, z, row, nt, live);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -287,6 +297,173 @@ __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
   if (warp == 1) {
     tc_fence_after_sync();
     tmem_dealloc(tmem, G::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- CTA pairs
+// Large problems run on CTA pairs (a 2-CTA cluster, cta_group::2): a 256 x 256
+// output tile per pair, each CTA loading 128 rows of A and 128 rows of W per K
+// block (half the W traffic of a 128 x 256 tile per SM for the same MMA work),
+// peer 0 issuing M = 256, N = 256 UMMAs over both SMs' operands, each CTA
+// draining its own 128 accumulator rows.  Both CTAs' loads complete on peer 0's
+// full barrier (peer 0 expects the bytes of both); MMA completion is committed
+// to both CTAs' empty and accumulator-full barriers (multicast commit); the
+// epilogue warps of both CTAs release an accumulator on peer 0's empty barrier
+// (8 arrivals).  No TMA multicast: each CTA loads its own boxes.
+struct GemmPairCfg {
+  static constexpr int BM = 128, BN = 256, BK = 64;  // per CTA: 128 rows of A, 128 rows of W
+  static constexpr int A_BYTES = BM * BK * 2;        // 16 KB
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KB
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr uint32_t TMEM_COLS = 512;         // two accumulators of 256 columns
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = STAGES * STAGE + BAR_BYTES + 1024;
+  static constexpr uint32_t IDESC = umma_idesc_bf16(256, BN);
+  static constexpr int THREADS = 192;
+  static_assert(STAGE % 1024 == 0, "stages stay 1024-byte aligned for the 128-byte swizzle");
+};
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmPairCfg::THREADS, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
+                          const GemmParams p) {
+  using G = GemmPairCfg;
+  extern __shared__ __align__(1024) unsigned char gemm_smem_raw[];
+  unsigned char* sm = gemm_smem_raw + ((1024u - (smem_u32(gemm_smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + G::STAGES * G::STAGE);
+  uint64_t* empty = full + G::STAGES;
+  uint64_t* tfull = empty + G::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // four epilogue warps in each CTA
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tslot, G::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before_sync();
+  cluster_sync();  // both CTAs' barriers and the pair's TMEM are ready
+  tc_fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const int npairs = gridDim.x >> 1;
+  const int total = p.m_tiles * p.n_tiles * p.batch;
+  const int kblocks = (p.K + G::BK - 1) / G::BK;
+
+  if (warp == 0) {
+    if (lane == 0) {  // ------------------------------------------ TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      for (int t = blockIdx.x >> 1; t < total; t += npairs) {
+        int z, mt, nt;
+        gemm_tile(t, p.m_tiles, p.n_tiles, z, mt, nt);
+        const int ay = (int)(z * p.a_brows) + mt * 256 + (int)rank * 128;
+        const int wy = (int)(z * p.w_brows) + nt * G::BN + (int)rank * (G::BN / 2);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!gemm_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          if (leader) mbar_expect_tx(&full[stage], 2 * G::STAGE);
+          const uint32_t bar0 = mapa_shared(smem_u32(&full[stage]), 0);
+          unsigned char* st = sm + stage * G::STAGE;
+          tma_load_2d_pair(st, &ta, bar0, kb * G::BK, ay);
+          tma_load_2d_pair(st + G::A_BYTES, &tw, bar0, kb * G::BK, wy);
+          ++issued;
+          if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+      if (*abort_flag) {
+        if (leader) {  // the phases peer 0 expected cover both CTAs' loads
+          for (int s = 0; s < G::STAGES; ++s) {
+            if (issued <= s) break;
+            mbar_wait(&full[s], s < stage ? phase : phase ^ 1u);
+          }
+        } else {  // peer 1 cannot see its loads complete: give them time to land
+          const unsigned long long t0 = global_ns();
+          while (global_ns() - t0 < 200000ull) __nanosleep(1000);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {  // ---------------------------------- MMA issuer (peer 0)
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool any = false;
+      for (int t = blockIdx.x >> 1; t < total; t += npairs) {
+        if (!gemm_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after_sync();
+        const uint32_t d = tmem + (uint32_t)(acc * G::BN);
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!gemm_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after_sync();
+          const uint32_t a0 = smem_u32(sm + stage * G::STAGE), b0 = a0 + G::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < G::BK / 16; ++kk)
+            umma_bf16_pair(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), G::IDESC,
+                           (kb | kk) != 0 ? 1u : 0u);
+          any = true;
+          umma_commit_pair_multicast(&empty[stage], 0x3);  // both CTAs' stage is free
+          if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair_multicast(&tfull[acc], 0x3);  // both halves of the tile are complete
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (any) {
+        umma_commit_pair(drain);
+        mbar_wait(drain, 0);
+      }
+    }
+  } else {  // ------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x >> 1; t < total; t += npairs) {
+      int z, mt, nt;
+      gemm_tile(t, p.m_tiles, p.n_tiles, z, mt, nt);
+      bool ok = gemm_wait(&tfull[acc], acc_phase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after_sync();
+      const int row = mt * 256 + (int)rank * 128 + q * 32 + lane;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * G::BN);
+      gemm_epilogue_tile<G::BN, EPI>(p, tbase, z, row, nt, row < p.M);
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&tempty[acc]);
+        else mbar_arrive_remote(mapa_shared(smem_u32(&tempty[acc]), 0));
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicAdd(&g_gemm_wait_timeouts, 1u);
+  tc_fence_before_sync();
+  cluster_sync();  // no CTA leaves while its peer may still read its operands or barriers
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc_pair(tmem, G::TMEM_COLS);
   }
 }
 
@@ -349,6 +526,67 @@ static yuf_status_t launch_gemm(const GemmArgs& g, GemmParams p, cudaStream_t s)
   return check_launch("gemm_bf16_kernel");
 }
 
+// CTA pairs of the pair kernel that can be resident at once on this device.
+static int pair_slots(const void* fn, int smem) {
+  static int cache[128][3] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 127;
+  const int slot = fn == (const void*)gemm_bf16_pair_kernel<GEMM_EPI_F32> ? 0
+                   : fn == (const void*)gemm_bf16_pair_kernel<GEMM_EPI_BF16> ? 1 : 2;
+  if (cache[dev][slot] == 0) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * 74, 1, 1);
+    cfg.blockDim = dim3(GemmPairCfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    cache[dev][slot] = n;
+  }
+  return cache[dev][slot];
+}
+
+template <int EPI>
+static yuf_status_t launch_gemm_pair(const GemmArgs& g, GemmParams p, cudaStream_t s) {
+  using G = GemmPairCfg;
+  static std::once_flag attr_once[128];
+  static cudaError_t attr_err[128];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 127;
+  std::call_once(attr_once[dev], [&] {
+    attr_err[dev] = cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         G::SMEM);
+  });
+  if (attr_err[dev] != cudaSuccess) {
+    set_error("gemm: cannot set %d bytes of shared memory: %s", G::SMEM, cudaGetErrorString(attr_err[dev]));
+    return YUF_ERR_CUDA;
+  }
+  CUtensorMap ta, tw;
+  if (!make_bf16_map(&ta, g.A, g.K, g.a_rows, g.lda, G::BM) ||
+      !make_bf16_map(&tw, g.W, g.K, g.w_rows, g.K, G::BN / 2)) {
+    set_error("gemm: cuTensorMapEncodeTiled failed (A rows %lld, lda %lld, W rows %lld, K %d)", g.a_rows,
+              g.lda, g.w_rows, g.K);
+    return YUF_ERR_CUDA;
+  }
+  p.m_tiles = (p.M + 255) / 256;
+  p.n_tiles = (p.N + G::BN - 1) / G::BN;
+  const long long total = (long long)p.m_tiles * p.n_tiles * p.batch;
+  const int pairs = (int)std::min<long long>(total, pair_slots((const void*)gemm_bf16_pair_kernel<EPI>, G::SMEM));
+  gemm_bf16_pair_kernel<EPI><<<2 * pairs, G::THREADS, G::SMEM, s>>>(ta, tw, p);
+  return check_launch("gemm_bf16_pair_kernel");
+}
+
 yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
   if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return YUF_OK;
   const bool a_ok = (reinterpret_cast<uintptr_t>(g.A) & 15) == 0 && g.lda % 8 == 0;
@@ -377,6 +615,13 @@ yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
           g.c_bstride % vec_elems == 0;
   const int sms = sm_count();
   auto tiles = [&](int bn) { return (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch; };
+  // enough 256 x 256 tiles to fill the pairs: the CTA-pair kernel
+  const long long pair_tiles = (long long)((g.M + 255) / 256) * ((g.N + 255) / 256) * g.batch;
+  if (g.M >= 512 && g.N >= 512 && pair_tiles >= sms / 2 && (g.epi != GEMM_EPI_SWIGLU || g.N % 256 == 0)) {
+    if (g.epi == GEMM_EPI_F32) return launch_gemm_pair<GEMM_EPI_F32>(g, p, s);
+    if (g.epi == GEMM_EPI_BF16) return launch_gemm_pair<GEMM_EPI_BF16>(g, p, s);
+    return launch_gemm_pair<GEMM_EPI_SWIGLU>(g, p, s);
+  }
   if (g.epi == GEMM_EPI_SWIGLU) {
     if (g.N % 128 != 0) {
       set_error("gemm: the SiLU-gate weight must hold whole 128-row groups (N = %d)", g.N);

@@ -24,4 +24,15 @@ YUF_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, in
       : "memory");
 }
 
+// The same load issued by either CTA of a cta_group::2 pair: the box lands in
+// the issuing CTA's shared memory and completes its bytes on the mbarrier at
+// shared::cluster address `bar_cluster` (peer 0's, from mapa_shared).
+YUF_DEVICE void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
 }  // namespace yuf
