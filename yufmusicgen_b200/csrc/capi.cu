@@ -12,6 +12,11 @@ namespace yuf {
 
 static thread_local char g_err[1024] = "";
 
+static thread_local bool g_pdl = false;
+bool pdl_enabled() { return g_pdl; }
+PdlScope::PdlScope(bool on) : prev(g_pdl) { g_pdl = on; }
+PdlScope::~PdlScope() { g_pdl = prev; }
+
 void set_error(const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);

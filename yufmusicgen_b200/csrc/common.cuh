@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/yufb200.h"
 
 #define YUF_DEVICE __device__ __forceinline__
@@ -36,6 +38,47 @@ YUF_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::);
 template <int N>
 YUF_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
+}  // namespace yuf
+
+// ---- programmatic dependent launch (PDL) ----------------------------------
+// The engine's decode step is a chain of ~15 small kernels per layer whose cost
+// is dominated by the gap between one kernel's end and the next one's start.
+// Launched with programmatic stream serialization, a kernel may be scheduled
+// while its predecessor still runs: it first waits for the predecessor grid to
+// complete with all its memory visible (pdl_wait, before touching global memory
+// the predecessor could write or read), then lets its own successor launch
+// (pdl_trigger), so at most two kernels of the chain are resident and the
+// successor's launch and set-up overlap this kernel's work.  Both are no-ops
+// for a kernel launched the ordinary way.
+namespace yuf {
+YUF_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+YUF_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// the calling host thread's launches use PDL while a PdlScope(true) is alive
+bool pdl_enabled();
+struct PdlScope {
+  explicit PdlScope(bool on);
+  ~PdlScope();
+  bool prev;
+};
+// kernel<<<grid, block, smem, s>>>(args...), with programmatic stream
+// serialization when pdl_enabled(); errors surface through check_launch.
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 }  // namespace yuf
 
 // Host-side error reporting shared by every C-ABI entry point.

@@ -336,6 +336,9 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
                             void* ws_base = nullptr) {
   const size_t rows = (size_t)B * T;
   const int d = m->d(), H = m->H(), N = m->N(), R = m->R(), lr = m->lr(), V = m->V();
+  // a decode step is a chain of small dependent kernels: launch them with
+  // programmatic dependent launch (each kernel's start overlaps its predecessor)
+  PdlScope pdl(T == 1 && !m->debug);
   // a caller-supplied workspace serves a decode step only (sized by ws_bytes(.., true))
   const bool caller_ws = ws_base != nullptr;
   if (!caller_ws) {
@@ -848,6 +851,8 @@ namespace yuf {
 __global__ void gen_record_kernel(int32_t* __restrict__ ids, int32_t* __restrict__ tokens,
                                   int32_t* __restrict__ lengths, int B, int n_steps, int s,
                                   int eos_id) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   int len = s == 0 ? n_steps : lengths[b];
@@ -900,11 +905,12 @@ yuf_status_t yuf_generate(yuf_model* m, const int32_t* prompt_ids, int B, int T,
   Y_TRY(yuf_prefill(m, prompt_ids, B, T, slot0, logits, nullptr, stream));
   const int eos_for_mask = p->eos_id >= 0 ? p->eos_id : 0;
   const float top_p = std::min(p->top_p, 1.f);  // >= 1 keeps the whole top-k
+  PdlScope pdl(true);  // sampling and recording join the decode steps' launch chain
   for (int st = 0; st < n_steps; ++st) {
     const int allow_eos = p->eos_id >= 0 && st >= p->min_tokens_before_eos;
     Y_TRY(yuf_sample(logits, B, (int)V, p->temperature, p->top_k, top_p, p->seed, (uint64_t)st,
                      p->seq0, p->mask_below, eos_for_mask, allow_eos, ids, nullptr, stream));
-    gen_record_kernel<<<(B + 127) / 128, 128, 0, s>>>(ids, tokens, lengths, B, n_steps, st, p->eos_id);
+    launch_k(gen_record_kernel, dim3((B + 127) / 128), dim3(128), 0, s, ids, tokens, lengths, B, n_steps, st, p->eos_id);
     Y_CUDA(cudaGetLastError());
     Y_TRY(yuf_step(m, ids, B, slot0, logits, stream));
   }

@@ -204,6 +204,8 @@ __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
+  pdl_wait();  // the set-up above overlaps the previous kernel of a PDL chain
+  pdl_trigger();
   const uint32_t tmem = *tslot;
   const int total = p.m_tiles * p.n_tiles * p.batch;
   const int kblocks = (p.K + G::BK - 1) / G::BK;
@@ -362,6 +364,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmPairCfg::THREADS
   tc_fence_before_sync();
   cluster_sync();  // both CTAs' barriers and the pair's TMEM are ready
   tc_fence_after_sync();
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = *tslot;
   const int npairs = gridDim.x >> 1;
   const int total = p.m_tiles * p.n_tiles * p.batch;
@@ -522,7 +526,7 @@ static yuf_status_t launch_gemm(const GemmArgs& g, GemmParams p, cudaStream_t s)
   p.n_tiles = (p.N + BN - 1) / BN;
   const long long total = (long long)p.m_tiles * p.n_tiles * p.batch;
   const int grid = (int)std::min<long long>(total, sm_count());
-  gemm_bf16_kernel<BN, EPI><<<grid, G::THREADS, G::SMEM, s>>>(ta, tw, p);
+  launch_k(gemm_bf16_kernel<BN, EPI>, dim3(grid), dim3(G::THREADS), G::SMEM, s, ta, tw, p);
   return check_launch("gemm_bf16_kernel");
 }
 
@@ -583,7 +587,7 @@ static yuf_status_t launch_gemm_pair(const GemmArgs& g, GemmParams p, cudaStream
   p.n_tiles = (p.N + G::BN - 1) / G::BN;
   const long long total = (long long)p.m_tiles * p.n_tiles * p.batch;
   const int pairs = (int)std::min<long long>(total, pair_slots((const void*)gemm_bf16_pair_kernel<EPI>, G::SMEM));
-  gemm_bf16_pair_kernel<EPI><<<2 * pairs, G::THREADS, G::SMEM, s>>>(ta, tw, p);
+  launch_k(gemm_bf16_pair_kernel<EPI>, dim3(2 * pairs), dim3(G::THREADS), G::SMEM, s, ta, tw, p);
   return check_launch("gemm_bf16_pair_kernel");
 }
 

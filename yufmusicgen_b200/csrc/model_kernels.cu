@@ -50,6 +50,8 @@ YUF_DEVICE float block_sum(float v, float* red) {
 // x[row, :] = E[ids[row], :]  (nn.Embedding, model.py:411)
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const float* __restrict__ E,
                              float* __restrict__ x, int rows, int d, int vocab, int* __restrict__ err) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   if (row >= rows) return;
   int id = ids[row];
@@ -68,6 +70,8 @@ template <typename OUT>
 __global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                  const float* __restrict__ b, const float* __restrict__ gate,
                                  OUT* __restrict__ out, int rows, int d) {
+  pdl_wait();
+  pdl_trigger();
   const int warps = blockDim.x >> 5;
   const int row = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -96,6 +100,8 @@ __global__ void __launch_bounds__(128)
     layernorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ w,
                          const float* __restrict__ b, const float* __restrict__ gate,
                          OUT* __restrict__ out, int rows, int d) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -153,6 +159,8 @@ __global__ void __launch_bounds__(1024)
     ln_row_kernel(const float* __restrict__ x, const float* __restrict__ w,
                   const float* __restrict__ b, const float* __restrict__ gate, OUT* __restrict__ out,
                   int rows, int d, float* __restrict__ xt, float* prev, const float* __restrict__ mix) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   const int row = blockIdx.x, i = threadIdx.x, d4 = d >> 2;
   const bool act = i < d4;
@@ -197,6 +205,8 @@ __global__ void __launch_bounds__(128)
     ln_mix_step_kernel(const float* __restrict__ x, const float* __restrict__ w,
                        const float* __restrict__ b, float* __restrict__ xt, float* prev,
                        const float* __restrict__ mix, OUT* __restrict__ out, int B, int d) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= B) return;
@@ -252,6 +262,8 @@ __global__ void __launch_bounds__(128)
 template <typename OUT>
 __global__ void mix_kernel(const float* __restrict__ xt, const float* __restrict__ prev,
                            const float* __restrict__ mix, OUT* __restrict__ out, int B, int T, int d) {
+  pdl_wait();
+  pdl_trigger();
   const size_t rows = (size_t)B * T;
   const size_t total = rows * d;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
@@ -278,6 +290,8 @@ __global__ void mix_kernel(const float* __restrict__ xt, const float* __restrict
 template <typename OUT>
 __global__ void tanh_kernel(const float* __restrict__ x, OUT* __restrict__ out, size_t n_tanh,
                             size_t n) {
+  pdl_wait();
+  pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     store_out(out, i, i < n_tanh ? tanhf(x[i]) : x[i]);
@@ -294,6 +308,8 @@ __global__ void timemix_post_kernel(const float* __restrict__ k, const float* __
                                     float* __restrict__ w_raw, float* __restrict__ k_adj,
                                     float* __restrict__ a_op, float* __restrict__ b_op,
                                     float* __restrict__ g_out, int rows, int H, int N) {
+  pdl_wait();
+  pdl_trigger();
   const int warps = blockDim.x >> 5;
   const size_t item = (size_t)blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -340,6 +356,8 @@ __global__ void timemix_post_kernel(const float* __restrict__ k, const float* __
 template <typename OUT>
 __global__ void silu_mul_kernel(const float* __restrict__ ig, OUT* __restrict__ out, int rows,
                                 int F) {
+  pdl_wait();
+  pdl_trigger();
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const float* in = ig + (size_t)row * 2 * F;
     const size_t o = (size_t)row * F;
@@ -356,6 +374,8 @@ __global__ void silu_mul_kernel(const float* __restrict__ ig, OUT* __restrict__ 
 
 // float -> bfloat16 copy (activations feeding a bf16-weight GEMM)
 __global__ void to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, size_t n) {
+  pdl_wait();
+  pdl_trigger();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     y[i] = __float2bfloat16_rn(x[i]);
@@ -369,13 +389,13 @@ static int grid_for(size_t n, int threads) {
 
 void launch_embed(const int32_t* ids, const float* E, float* x, int rows, int d, int vocab, int* err,
                   cudaStream_t s) {
-  embed_kernel<<<rows, 128, 0, s>>>(ids, E, x, rows, d, vocab, err);
+  launch_k(embed_kernel, dim3(rows), dim3(128), 0, s, ids, E, x, rows, d, vocab, err);
 }
 template <typename OUT>
 void launch_layernorm(const float* x, const float* w, const float* b, const float* gate, OUT* out,
                       int rows, int d, cudaStream_t s) {
   if (rows < 4 * 148 && d % 4 == 0 && d <= 4096) {  // small batch: one CTA per row
-    ln_row_kernel<OUT, false><<<rows, ((d / 4 + 31) / 32) * 32, 0, s>>>(x, w, b, gate, out, rows, d,
+    launch_k(ln_row_kernel<OUT, false>, dim3(rows), dim3(((d / 4 + 31) / 32) * 32), 0, s, x, w, b, gate, out, rows, d,
                                                                          nullptr, nullptr, nullptr);
     return;
   }
@@ -387,7 +407,7 @@ void launch_layernorm(const float* x, const float* w, const float* b, const floa
     switch (vpl) {
 #define CASE(V)                                                                                  \
   case V:                                                                                        \
-    layernorm_reg_kernel<OUT, V><<<blocks, 32 * wpb, 0, s>>>(x, w, b, gate, out, rows, d); \
+    launch_k(layernorm_reg_kernel<OUT, V>, dim3(blocks), dim3(32 * wpb), 0, s, x, w, b, gate, out, rows, d); \
     return;
       CASE(1) CASE(2) CASE(3) CASE(4) CASE(5) CASE(6) CASE(7) CASE(8)
 #undef CASE
@@ -395,14 +415,14 @@ void launch_layernorm(const float* x, const float* w, const float* b, const floa
     }
   }
   const int warps = 8;
-  layernorm_kernel<OUT><<<(rows + warps - 1) / warps, 32 * warps, 0, s>>>(x, w, b, gate, out, rows, d);
+  launch_k(layernorm_kernel<OUT>, dim3((rows + warps - 1) / warps), dim3(32 * warps), 0, s, x, w, b, gate, out, rows, d);
 }
 template <typename OUT>
 bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* xt, float* prev,
                         const float* mix, OUT* out, int B, int d, cudaStream_t s) {
   if (d % 4 != 0) return false;
   if (B < 4 * 148 && d <= 4096) {
-    ln_row_kernel<OUT, true><<<B, ((d / 4 + 31) / 32) * 32, 0, s>>>(x, w, b, nullptr, out, B, d, xt,
+    launch_k(ln_row_kernel<OUT, true>, dim3(B), dim3(((d / 4 + 31) / 32) * 32), 0, s, x, w, b, nullptr, out, B, d, xt,
                                                                      prev, mix);
     return true;
   }
@@ -412,7 +432,7 @@ bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* x
   switch ((d / 4 + 31) / 32) {
 #define CASE(V)                                                                                 \
   case V:                                                                                       \
-    ln_mix_step_kernel<OUT, V><<<blocks, 32 * wpb, 0, s>>>(x, w, b, xt, prev, mix, out, B, d); \
+    launch_k(ln_mix_step_kernel<OUT, V>, dim3(blocks), dim3(32 * wpb), 0, s, x, w, b, xt, prev, mix, out, B, d); \
     return true;
     CASE(1) CASE(2) CASE(3) CASE(4) CASE(5) CASE(6) CASE(7) CASE(8)
 #undef CASE
@@ -422,11 +442,11 @@ bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* x
 template <typename OUT>
 void launch_mix(const float* xt, const float* prev, const float* mix, OUT* out, int B, int T, int d,
                 cudaStream_t s) {
-  mix_kernel<OUT><<<grid_for((size_t)B * T * d, 256), 256, 0, s>>>(xt, prev, mix, out, B, T, d);
+  launch_k(mix_kernel<OUT>, dim3(grid_for((size_t)B * T * d, 256)), dim3(256), 0, s, xt, prev, mix, out, B, T, d);
 }
 template <typename OUT>
 void launch_tanh(const float* x, OUT* out, size_t n_tanh, size_t n, cudaStream_t s) {
-  tanh_kernel<OUT><<<grid_for(n, 256), 256, 0, s>>>(x, out, n_tanh, n);
+  launch_k(tanh_kernel<OUT>, dim3(grid_for(n, 256)), dim3(256), 0, s, x, out, n_tanh, n);
 }
 void launch_timemix_post(const float* k, const float* lw, const float* la, const float* lg,
                          const float* w0, const float* a0, const float* k_k, const float* k_a,
@@ -434,15 +454,15 @@ void launch_timemix_post(const float* k, const float* lw, const float* la, const
                          int H, int N, cudaStream_t s) {
   const int warps = 8;
   const size_t items = (size_t)rows * H;
-  timemix_post_kernel<<<(unsigned)((items + warps - 1) / warps), 32 * warps, 0, s>>>(
+  launch_k(timemix_post_kernel, dim3((unsigned)((items + warps - 1) / warps)), dim3(32 * warps), 0, s, 
       k, lw, la, lg, w0, a0, k_k, k_a, w_raw, k_adj, a_op, b_op, g, rows, H, N);
 }
 template <typename OUT>
 void launch_silu_mul(const float* ig, OUT* out, int rows, int F, cudaStream_t s) {
-  silu_mul_kernel<OUT><<<rows < 148 * 64 ? rows : 148 * 64, 256, 0, s>>>(ig, out, rows, F);
+  launch_k(silu_mul_kernel<OUT>, dim3(rows < 148 * 64 ? rows : 148 * 64), dim3(256), 0, s, ig, out, rows, F);
 }
 void launch_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) {
-  to_bf16_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
+  launch_k(to_bf16_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, x, y, n);
 }
 
 template void launch_layernorm<float>(const float*, const float*, const float*, const float*, float*,

@@ -247,6 +247,8 @@ __global__ void __launch_bounds__(1024)
                      float* m_out, int R, int ld, const float* __restrict__ bias_c,
                      const float* __restrict__ bias_w, const float* __restrict__ bias_g,
                      int raw_params, __nv_bfloat16* __restrict__ read_bf) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float scratch[32 * 2];
   __shared__ float red[2];
   const int bb = blockIdx.x, j = threadIdx.x, nwarps = blockDim.x >> 5;
@@ -347,7 +349,7 @@ yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const f
                                   const float* m0, float* read, float* m_out, int B, int T, int R,
                                   float* scratch, __nv_bfloat16* read_bf, cudaStream_t stream) {
   if (T == 1 && R <= 1024) {
-    rosa_step_kernel<true><<<B, ((R + 31) / 32) * 32, 0, stream>>>(
+    launch_k(rosa_step_kernel<true>, dim3(B), dim3(((R + 31) / 32) * 32), 0, stream, 
         cand, write, gate, decay_raw, dir_raw, m0, read, m_out, R, ld, bias_c, bias_w, bias_g, 1,
         read_bf);
     return check_launch("rosa_step_kernel");

@@ -68,6 +68,8 @@ __global__ void __launch_bounds__(SAMPLER_THREADS)
     sample_kernel(const float* __restrict__ logits, int V, float inv_temp, int top_k, float top_p,
                   uint64_t seed, uint64_t step, int seq0, int mask_below, int eos_id, int allow_eos,
                   int32_t* __restrict__ out_ids, float* __restrict__ out_u) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float srow[];                 // [V] masked scaled logits
   __shared__ float top_v[SAMPLER_MAX_K];
   __shared__ int top_i[SAMPLER_MAX_K];
@@ -282,7 +284,7 @@ extern "C" yuf_status_t yuf_sample(const float* logits, int B, int V, float temp
   }
   const float inv_temp = temperature > 0.f ? 1.f / temperature : 0.f;
   const int k = temperature > 0.f ? top_k : 1;
-  sample_kernel<<<B, SAMPLER_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
+  launch_k(sample_kernel, dim3(B), dim3(SAMPLER_THREADS), smem, static_cast<cudaStream_t>(stream), 
       logits, V, temperature > 0.f ? inv_temp : 1.f, k, top_p, seed, step, seq0, mask_below, eos_id,
       allow_eos, out_ids, out_uniform);
   return check_launch("sample_kernel");

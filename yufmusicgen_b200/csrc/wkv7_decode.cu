@@ -25,6 +25,8 @@ __global__ void __launch_bounds__(N * 4)
                        const float* __restrict__ k, const float* __restrict__ v,
                        const float* __restrict__ a, const float* __restrict__ b, const float* s0,
                        float* __restrict__ y, float* s_out, int BH) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int G = 4, C = N / G, C2 = C / 2;
   __shared__ float vec[2][5 * N];  // ret, k, a, b, r of the current and the next head
   const int tid = threadIdx.x;
@@ -126,6 +128,8 @@ __global__ void __launch_bounds__(N * 4)
                             const float* __restrict__ k, const float* __restrict__ v,
                             const float* __restrict__ a, const float* __restrict__ b,
                             const float* s0, float* __restrict__ y, float* s_out, int BH) {
+  pdl_wait();
+  pdl_trigger();
   using K = DecRing<N>;
   constexpr int G = 4, C = N / G, C2 = C / 2;
   extern __shared__ __align__(128) unsigned char dsm[];
@@ -305,12 +309,12 @@ yuf_status_t wkv7_decode_dispatch(const float* r, const float* w, const float* k
     const int per_sm = ring ? ring_blocks_per_sm<NN>() : 0;                                      \
     if (per_sm > 0) {                                                                            \
       const int grid = std::min(BH, per_sm * sm_count());                                        \
-      wkv7_decode_ring_kernel<NN><<<grid, NN * 4, DecRing<NN>::SMEM, stream>>>(                  \
+      launch_k(wkv7_decode_ring_kernel<NN>, dim3(grid), dim3(NN * 4), DecRing<NN>::SMEM, stream,                   \
           r, w, k, v, a, b, s0, y, s_out, BH);                                                   \
       return check_launch("wkv7_decode_ring_kernel");                                            \
     }                                                                                            \
     const int grid = std::min(BH, decode_blocks_per_sm<NN>() * sm_count());                     \
-    wkv7_decode_kernel<NN><<<grid, NN * 4, 0, stream>>>(r, w, k, v, a, b, s0, y, s_out, BH);    \
+    launch_k(wkv7_decode_kernel<NN>, dim3(grid), dim3(NN * 4), 0, stream, r, w, k, v, a, b, s0, y, s_out, BH);    \
     return check_launch("wkv7_decode_kernel");                                                   \
   }
     CASE(16) CASE(32) CASE(40) CASE(48) CASE(64) CASE(96) CASE(128)
