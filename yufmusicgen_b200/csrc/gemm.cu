@@ -471,6 +471,224 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmPairCfg::THREADS
   }
 }
 
+// ------------------------------------------------------- split K in a cluster
+// Few rows (a decode batch): too few output tiles to occupy the GPU, and every
+// column tile re-reads the same activation rows.  The K blocks of one output
+// tile are split over the `ks` CTAs of a cluster (ks <= 8): each CTA multiplies
+// its slice into TMEM, parks the fp32 partial tile in its own shared memory,
+// and after a cluster barrier reduces 128 / ks rows of the tile by reading all
+// ks partials through distributed shared memory, in rank order (deterministic),
+// then applies the epilogue.  One tile per cluster, no atomics.
+template <int BN>
+struct GemmSplitCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = std::min(8, (192 * 1024) / STAGE);
+  static constexpr int PSTRIDE = BN + 4;  // floats per partial row (bank spread)
+  static constexpr int P_BYTES = BM * PSTRIDE * 4;
+  static constexpr int BODY = STAGES * STAGE > P_BYTES ? STAGES * STAGE : P_BYTES;
+  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = BODY + BAR_BYTES + 1024;
+  static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
+  static constexpr int THREADS = 192;
+};
+
+// Epilogue of four consecutive output columns (col .. col+3) of one row.
+template <int EPI>
+YUF_DEVICE void store4(const GemmParams& p, int z, int row, int col, float4 v) {
+  const bool full = p.vec && col + 4 <= p.N;
+  if constexpr (EPI == GEMM_EPI_F32) {
+    float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
+    if (full) {
+      if (p.beta != 0.f) {
+        const float4 o = *reinterpret_cast<const float4*>(out);
+        v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+      }
+      *reinterpret_cast<float4*>(out) = v;
+    } else {
+      const float e[4] = {v.x, v.y, v.z, v.w};
+      for (int c = 0; c < 4; ++c)
+        if (col + c < p.N) out[c] = p.beta != 0.f ? out[c] + e[c] : e[c];
+    }
+  } else {
+    if (p.tanh_batch0 && z == 0) {
+      v.x = tanhf(v.x); v.y = tanhf(v.y); v.z = tanhf(v.z); v.w = tanhf(v.w);
+    }
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
+    if (full) {
+      uint2 pk;
+      reinterpret_cast<__nv_bfloat162*>(&pk)[0] = __floats2bfloat162_rn(v.x, v.y);
+      reinterpret_cast<__nv_bfloat162*>(&pk)[1] = __floats2bfloat162_rn(v.z, v.w);
+      *reinterpret_cast<uint2*>(out) = pk;
+    } else {
+      const float e[4] = {v.x, v.y, v.z, v.w};
+      for (int c = 0; c < 4; ++c)
+        if (col + c < p.N) out[c] = __float2bfloat16_rn(e[c]);
+    }
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(GemmSplitCfg<BN>::THREADS, 1)
+    gemm_bf16_splitk_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tw,
+                            const GemmParams p, int ks, int kb_per) {
+  using G = GemmSplitCfg<BN>;
+  extern __shared__ __align__(1024) unsigned char gemm_smem_raw[];
+  unsigned char* sm = gemm_smem_raw + ((1024u - (smem_u32(gemm_smem_raw) & 1023u)) & 1023u);
+  float* part = reinterpret_cast<float*>(sm);  // the partial tile, once the MMAs are done
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + G::BODY);
+  uint64_t* empty = full + G::STAGES;
+  uint64_t* tfull = empty + G::STAGES;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tfull + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = (int)cluster_rank();
+  const int tile = blockIdx.x / ks;
+  const int per = p.m_tiles * p.n_tiles;
+  const int z = tile / per, mt = (tile % per) / p.n_tiles, nt = tile % p.n_tiles;
+  const int kblocks = (p.K + G::BK - 1) / G::BK;
+  const int kb0 = r * kb_per, kb1 = min(kblocks, kb0 + kb_per), nkb = max(0, kb1 - kb0);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, G::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer over this CTA's K slice
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      const int ay = (int)(z * p.a_brows) + mt * G::BM, wy = (int)(z * p.w_brows) + nt * BN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!gemm_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
+        unsigned char* st = sm + stage * G::STAGE;
+        mbar_expect_tx(&full[stage], G::STAGE);
+        tma_load_2d(st, &ta, &full[stage], kb * G::BK, ay);
+        tma_load_2d(st + G::A_BYTES, &tw, &full[stage], kb * G::BK, wy);
+        ++issued;
+        if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (*abort_flag)
+        for (int s = 0; s < G::STAGES; ++s) {
+          if (issued <= s) break;
+          mbar_wait(&full[s], s < stage ? phase : phase ^ 1u);
+        }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nkb > 0) {  // MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        if (!gemm_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+        tc_fence_after_sync();
+        const uint32_t a0 = smem_u32(sm + stage * G::STAGE), b0 = a0 + G::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < G::BK / 16; ++kk)
+          umma_bf16(tmem, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), G::IDESC,
+                    (i | kk) != 0 ? 1u : 0u);
+        umma_commit(&empty[stage]);
+        if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
+      }
+      umma_commit(tfull);  // also when a wait expired: every MMA issued ends before the tile is read
+      (void)ok;
+    }
+  } else {  // epilogue warps: the partial tile into shared memory
+    const int q = warp & 3;
+    const int prow = q * 32 + lane;
+    float* dst = part + (size_t)prow * G::PSTRIDE;
+    bool ok = nkb == 0 || mbar_wait(tfull, 0);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) *abort_flag = 1;
+    if (nkb > 0 && ok) {
+      tc_fence_after_sync();
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld_x32(tbase + c0, v);
+#pragma unroll
+        for (int c = 0; c < 32; c += 4)
+          *reinterpret_cast<float4*>(dst + c0 + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+      }
+    } else {
+      for (int c = 0; c < BN; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  tc_fence_before_sync();
+  cluster_sync();  // every CTA's partial is in its shared memory
+  // reduce rows [r * 128 / ks, (r + 1) * 128 / ks) over the ks partials, in rank order
+  {
+    const int rows = G::BM / ks, r0 = r * rows;
+    const uint32_t pbase = smem_u32(part);
+    if constexpr (EPI == GEMM_EPI_SWIGLU) {
+      constexpr int QC = BN / 8;  // float4 chunks of "in" columns per row (BN / 2 columns)
+      for (int i = threadIdx.x; i < rows * QC; i += G::THREADS) {
+        const int rr = r0 + i / QC, j = (i % QC) * 4;         // j: 0 .. BN/2 - 4
+        const int cin = (j / 64) * 128 + j % 64, cgate = cin + 64;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), g = a;
+        for (int qq = 0; qq < ks; ++qq) {
+          const float4 x = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * G::PSTRIDE + cin) * 4), qq));
+          const float4 y = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * G::PSTRIDE + cgate) * 4), qq));
+          a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+          g.x += y.x; g.y += y.y; g.z += y.z; g.w += y.w;
+        }
+        const int row = mt * G::BM + rr, col = nt * (BN / 2) + j;
+        if (row < p.M) {
+          __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+          const float h[4] = {silu(a.x) * g.x, silu(a.y) * g.y, silu(a.z) * g.z, silu(a.w) * g.w};
+          if (p.vec && col + 4 <= p.n_out) {
+            uint2 pk;
+            reinterpret_cast<__nv_bfloat162*>(&pk)[0] = __floats2bfloat162_rn(h[0], h[1]);
+            reinterpret_cast<__nv_bfloat162*>(&pk)[1] = __floats2bfloat162_rn(h[2], h[3]);
+            *reinterpret_cast<uint2*>(out + col) = pk;
+          } else {
+            for (int c = 0; c < 4; ++c)
+              if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(h[c]);
+          }
+        }
+      }
+    } else {
+      constexpr int QC = BN / 4;
+      for (int i = threadIdx.x; i < rows * QC; i += G::THREADS) {
+        const int rr = r0 + i / QC, c = (i % QC) * 4;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int qq = 0; qq < ks; ++qq) {
+          const float4 x = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * G::PSTRIDE + c) * 4), qq));
+          a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+        }
+        const int row = mt * G::BM + rr, col = nt * BN + c;
+        if (row < p.M && col < p.N) store4<EPI>(p, z, row, col, a);
+      }
+    }
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicAdd(&g_gemm_wait_timeouts, 1u);
+  cluster_sync();  // no CTA leaves while a peer may still read its partial
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, G::TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------- host side
 static int sm_count() {
   static int cache[128] = {};
@@ -591,6 +809,116 @@ static yuf_status_t launch_gemm_pair(const GemmArgs& g, GemmParams p, cudaStream
   return check_launch("gemm_bf16_pair_kernel");
 }
 
+// Clusters of `ks` CTAs of the split-K kernel that can be resident at once.
+template <int BN, int EPI>
+static int splitk_slots(int ks) {
+  static int cache[128][9] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 127;
+  if (cache[dev][ks] == 0) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(ks * 16, 1, 1);
+    cfg.blockDim = dim3(GemmSplitCfg<BN>::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = GemmSplitCfg<BN>::SMEM;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = ks;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_splitk_kernel<BN, EPI>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / (2 * ks);
+    }
+    cache[dev][ks] = std::max(1, n);
+  }
+  return cache[dev][ks];
+}
+
+template <int BN, int EPI>
+static yuf_status_t launch_gemm_splitk(const GemmArgs& g, GemmParams p, int ks, cudaStream_t s) {
+  using G = GemmSplitCfg<BN>;
+  static std::once_flag attr_once[128];
+  static cudaError_t attr_err[128];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 127;
+  std::call_once(attr_once[dev], [&] {
+    attr_err[dev] = cudaFuncSetAttribute(gemm_bf16_splitk_kernel<BN, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+    if (attr_err[dev] == cudaSuccess)
+      attr_err[dev] = cudaFuncSetAttribute(gemm_bf16_splitk_kernel<BN, EPI>,
+                                           cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  });
+  if (attr_err[dev] != cudaSuccess) {
+    set_error("gemm: kernel attributes: %s", cudaGetErrorString(attr_err[dev]));
+    return YUF_ERR_CUDA;
+  }
+  CUtensorMap ta, tw;
+  if (!make_bf16_map(&ta, g.A, g.K, g.a_rows, g.lda, G::BM) || !make_bf16_map(&tw, g.W, g.K, g.w_rows, g.K, BN)) {
+    set_error("gemm: cuTensorMapEncodeTiled failed (A rows %lld, lda %lld, W rows %lld, K %d)", g.a_rows,
+              g.lda, g.w_rows, g.K);
+    return YUF_ERR_CUDA;
+  }
+  p.n_tiles = (p.N + BN - 1) / BN;
+  const int kblocks = (p.K + G::BK - 1) / G::BK;
+  const int kb_per = (kblocks + ks - 1) / ks;
+  const long long tiles = (long long)p.m_tiles * p.n_tiles * p.batch;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(tiles * ks), 1, 1);
+  cfg.blockDim = dim3(G::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = G::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (pdl_enabled()) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
+  cudaLaunchKernelEx(&cfg, gemm_bf16_splitk_kernel<BN, EPI>, ta, tw, p, ks, kb_per);
+  return check_launch("gemm_bf16_splitk_kernel");
+}
+
+// Few rows: pick the column tile and the K split whose CTAs each load the
+// fewest bytes while every cluster of the launch is resident at once.
+template <int EPI>
+static yuf_status_t dispatch_splitk(const GemmArgs& g, const GemmParams& p, cudaStream_t s) {
+  const int kblocks = (g.K + 63) / 64;
+  int best_bn = 0, best_ks = 1;
+  long long best_cost = -1;
+  for (int bn : {64, 128, 256}) {
+    if (EPI == GEMM_EPI_SWIGLU && (bn < 128 || g.N % bn != 0)) continue;
+    const long long tiles = (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch;
+    for (int ks : {8, 4, 2, 1}) {
+      if (ks > kblocks && ks > 1) continue;
+      const int slots = bn == 64 ? splitk_slots<64, EPI>(ks)
+                                 : (bn == 128 ? splitk_slots<128, EPI>(ks) : splitk_slots<256, EPI>(ks));
+      if (tiles > slots && ks > 1) continue;
+      const long long kb_per = (kblocks + ks - 1) / ks;
+      // bytes per CTA (A + W slices), then a wave count for launches that do not fit
+      const long long waves = (tiles + slots - 1) / slots;
+      const long long cost = (128 + bn) * kb_per * waves;
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        best_bn = bn;
+        best_ks = ks;
+      }
+    }
+  }
+  if (best_bn == 64) return launch_gemm_splitk<64, EPI>(g, p, best_ks, s);
+  if (best_bn == 128) return launch_gemm_splitk<128, EPI>(g, p, best_ks, s);
+  return launch_gemm_splitk<256, EPI>(g, p, best_ks, s);
+}
+
 yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
   if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return YUF_OK;
   const bool a_ok = (reinterpret_cast<uintptr_t>(g.A) & 15) == 0 && g.lda % 8 == 0;
@@ -619,6 +947,12 @@ yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
           g.c_bstride % vec_elems == 0;
   const int sms = sm_count();
   auto tiles = [&](int bn) { return (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch; };
+  // a decode batch: split K over a cluster
+  if (p.m_tiles <= 2 && (g.epi != GEMM_EPI_SWIGLU || g.N % 128 == 0)) {
+    if (g.epi == GEMM_EPI_F32) return dispatch_splitk<GEMM_EPI_F32>(g, p, s);
+    if (g.epi == GEMM_EPI_BF16) return dispatch_splitk<GEMM_EPI_BF16>(g, p, s);
+    return dispatch_splitk<GEMM_EPI_SWIGLU>(g, p, s);
+  }
   // enough 256 x 256 tiles to fill the pairs: the CTA-pair kernel
   const long long pair_tiles = (long long)((g.M + 255) / 256) * ((g.N + 255) / 256) * g.batch;
   if (g.M >= 512 && g.N >= 512 && pair_tiles >= sms / 2 && (g.epi != GEMM_EPI_SWIGLU || g.N % 256 == 0)) {
