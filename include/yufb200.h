@@ -191,12 +191,27 @@ enum {
   YUF_GEMM_F32 = 0,
   YUF_GEMM_BF16 = 1,
   YUF_GEMM_BF16_TANH0 = 2,
-  YUF_GEMM_SILU_GATE = 3
+  YUF_GEMM_SILU_GATE = 3,
+  YUF_GEMM_F32_TANH0 = 4,     /* yuf_gemm_tf32x3 only: fp32 tanh(acc) for batch 0 */
+  YUF_GEMM_SILU_GATE_F32 = 5  /* yuf_gemm_tf32x3 only: the SiLU-gate epilogue, fp32 out */
 };
 yuf_status_t yuf_gemm_bf16(const void* A, long long lda, long long a_batch_rows, const void* W,
                            long long w_batch_rows, void* C, long long ldc, long long c_batch_stride,
                            int M, int N, int K, int batch, int epilogue, int accumulate, int n_out,
                            void* stream);
+/* The same projections with fp32 operands at fp32 accuracy (the engine's fp32
+ * mode): A fp32 (row stride lda), W as two fp32 parts [N, K] each, W_hi = W
+ * with its 13 low mantissa bits cleared and W_lo = W - W_hi (yuf_tf32_split);
+ * the kernel splits A the same way and sums A_lo W_hi + A_hi W_lo + A_hi W_hi
+ * on the tensor cores (kind::tf32, "3xTF32", ~2^-20 relative per product).
+ * Epilogues YUF_GEMM_F32 (accumulate allowed), YUF_GEMM_F32_TANH0,
+ * YUF_GEMM_SILU_GATE_F32.  lda and K multiples of 4. */
+yuf_status_t yuf_gemm_tf32x3(const float* A, long long lda, long long a_batch_rows, const float* W_hi,
+                             const float* W_lo, long long w_batch_rows, float* C, long long ldc,
+                             long long c_batch_stride, int M, int N, int K, int batch, int epilogue,
+                             int accumulate, int n_out, void* stream);
+/* Host: split n fp32 weights into the two parts yuf_gemm_tf32x3 takes. */
+yuf_status_t yuf_tf32_split(const float* w, size_t n, float* hi, float* lo);
 
 /* ------------------------------------------------------------------------ *
  * Model engine: the YufMusicGen block stack (yufmusicgen/model.py:345-445) on

@@ -142,3 +142,77 @@ def test_gemm_rejects_unaligned_operands():
                              BF16, 1, 0, s) == 1  # accumulate needs the fp32 epilogue
     torch.cuda.synchronize()
     assert lib.yuf_sync_check(s) == 0
+
+
+# ---- fp32 operands at fp32 accuracy (3xTF32, yuf_gemm_tf32x3) -------------
+# Against a float64 product of the fp32 operands: the three tf32 products keep
+# about 2^-20 of each product, so the fp32 tolerance of the engine holds:
+# |got - want| <= 1e-4 sqrt(K) max|A| max|W| + 1e-5 |want|.
+F32_TANH0, SILU_GATE_F32 = 4, 5
+
+
+def split32(W):
+    w = np.ascontiguousarray(W.detach().cpu().numpy(), np.float32)
+    hi, lo = np.empty_like(w), np.empty_like(w)
+    assert _lib.load().yuf_tf32_split(w.ctypes.data, w.size, hi.ctypes.data, lo.ctypes.data) == 0
+    return torch.from_numpy(hi).to(DEV), torch.from_numpy(lo).to(DEV)
+
+
+def gemm32(A, lda, a_brows, Wh, Wl, w_brows, C, ldc, c_bstride, M, N, K, batch, epi, acc=0, n_out=0):
+    lib = _lib.load()
+    st = lib.yuf_gemm_tf32x3(A.data_ptr(), lda, a_brows, Wh.data_ptr(), Wl.data_ptr(), w_brows, C.data_ptr(),
+                             ldc, c_bstride, M, N, K, batch, epi, acc, n_out,
+                             torch.cuda.current_stream().cuda_stream)
+    assert st == 0, lib.yuf_last_error().decode()
+
+
+def check32(got, want, K, scale):
+    np.testing.assert_allclose(got.double().cpu().numpy(), want.double().cpu().numpy(), rtol=1e-5,
+                               atol=1e-4 * math.sqrt(K) * scale)
+
+
+SHAPES32 = [(4096, 640, 640, 3), (4096, 640, 2560, 1), (256, 640, 640, 3), (256, 20000, 640, 1), (256, 640, 2560, 1),
+            (1, 64, 32, 1), (100, 100, 40, 1), (129, 200, 72, 2), (777, 96, 136, 3), (2, 384, 640, 1)]
+
+
+@pytest.mark.parametrize("M,N,K,batch", SHAPES32)
+def test_gemm_tf32x3_matches_fp32(M, N, K, batch):
+    g = torch.Generator().manual_seed(M + N + K)
+    A = torch.randn(batch * M, K, generator=g).to(DEV)
+    W = (torch.randn(batch * N, K, generator=g) * 0.05).to(DEV)
+    Wh, Wl = split32(W)
+    C = torch.full((batch * M, N), float("nan"), device=DEV)
+    gemm32(A, K, M, Wh, Wl, N, C, N, M * N, M, N, K, batch, F32)
+    want = torch.cat([ref(A[z * M:(z + 1) * M], W[z * N:(z + 1) * N]) for z in range(batch)])
+    check32(C, want, K, float(A.abs().max() * W.abs().max()))
+
+
+def test_gemm_tf32x3_residual_tanh_and_silu_gate():
+    g = torch.Generator().manual_seed(5)
+    M, d, lr = 300, 640, 64
+    A = torch.randn(M, d, generator=g).to(DEV)
+    W = (torch.randn(d, d, generator=g) * 0.05).to(DEV)
+    Wh, Wl = split32(W)
+    x = torch.randn(M, d, generator=g).to(DEV)
+    C = x.clone()
+    gemm32(A, d, 0, Wh, Wl, 0, C, d, 0, M, d, d, 1, F32, acc=1)
+    check32(C, x.double() + ref(A, W), d, float(A.abs().max() * W.abs().max()))
+    # low-rank first stage: three batches, tanh on the first
+    A3 = torch.randn(3 * M, d, generator=g).to(DEV)
+    L1 = (torch.randn(3 * lr, d, generator=g) * 0.05).to(DEV)
+    Lh, Ll = split32(L1)
+    C3 = torch.empty(3 * M, lr, device=DEV)
+    gemm32(A3, d, M, Lh, Ll, lr, C3, lr, M * lr, M, lr, d, 3, F32_TANH0)
+    want = torch.cat([ref(A3[z * M:(z + 1) * M], L1[z * lr:(z + 1) * lr]) for z in range(3)])
+    want[:M] = torch.tanh(want[:M])
+    check32(C3, want, d, float(A3.abs().max() * L1.abs().max()))
+    # FFN: SiLU(in) * gate with the packed in/gate weight, fp32 out
+    F = 4 * d
+    Win, Wg = (torch.randn(F, d, generator=g) * 0.05).to(DEV), (torch.randn(F, d, generator=g) * 0.05).to(DEV)
+    Wp = pack_silu_gate(Win, Wg)
+    Ph, Pl = split32(Wp)
+    H = torch.empty(M, F, device=DEV)
+    gemm32(A, d, 0, Ph, Pl, 0, H, F, 0, M, Wp.shape[0], d, 1, SILU_GATE_F32, n_out=F)
+    hin, hg = ref(A, Win), ref(A, Wg)
+    np.testing.assert_allclose(H.double().cpu().numpy(), (hin * torch.sigmoid(hin) * hg).cpu().numpy(),
+                               rtol=1e-4, atol=1e-4)

@@ -54,6 +54,9 @@ SIGNATURES = {
     "yuf_sync_check": [P],
     "yuf_debug_wait_selftest": [ctypes.c_ulonglong, P],
     "yuf_model_set_debug": [P, I],
+    "yuf_gemm_tf32x3": [P, ctypes.c_longlong, ctypes.c_longlong, P, P, ctypes.c_longlong, P, ctypes.c_longlong,
+                        ctypes.c_longlong, I, I, I, I, I, I, I, P],
+    "yuf_tf32_split": [P, ctypes.c_size_t, P, P],
     "yuf_mt19937_create": [ctypes.c_uint64, P],
     "yuf_mt19937_destroy": [P],
     "yuf_mt19937_next": [P, P, ctypes.c_int64],

@@ -28,6 +28,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -88,7 +89,31 @@ YUF_DEVICE bool gemm_wait(uint64_t* bar, uint32_t parity, volatile int* abort_fl
 // (warp-collective); only live rows store.
 template <int BN, int EPI>
 YUF_DEVICE void gemm_epilogue_tile(const GemmParams& p, uint32_t tbase, int z, int row, int nt, bool live) {
-  if constexpr (EPI == GEMM_EPI_SWIGLU) {
+  if constexpr (EPI == GEMM_EPI_SWIGLU_F32) {
+    float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+#pragma unroll 1
+    for (int sb = 0; sb < BN / 128; ++sb)
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        float vi[32], vg[32];
+        tmem_ld_x32(tbase + sb * 128 + h * 32, vi);
+        tmem_ld_x32(tbase + sb * 128 + 64 + h * 32, vg);
+        const int col = nt * (BN / 2) + sb * 64 + h * 32;
+        if (live) {
+          if (p.vec && col + 32 <= p.n_out) {
+#pragma unroll
+            for (int c = 0; c < 32; c += 4)
+              *reinterpret_cast<float4*>(out + col + c) =
+                  make_float4(silu(vi[c]) * vg[c], silu(vi[c + 1]) * vg[c + 1], silu(vi[c + 2]) * vg[c + 2],
+                              silu(vi[c + 3]) * vg[c + 3]);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (col + c < p.n_out) out[col + c] = silu(vi[c]) * vg[c];
+          }
+        }
+      }
+  } else if constexpr (EPI == GEMM_EPI_SWIGLU) {
     // tile columns per 128: [64 "in" rows | 64 "gate" rows] of the packed weight
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
 #pragma unroll 1
@@ -126,6 +151,10 @@ YUF_DEVICE void gemm_epilogue_tile(const GemmParams& p, uint32_t tbase, int z, i
       const int col = nt * BN + c0;
       if (!live || col >= p.N) continue;
       if constexpr (EPI == GEMM_EPI_F32) {
+        if (p.tanh_batch0 && z == 0) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = tanhf(v[c]);
+        }
         float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
         if (p.vec && col + 32 <= p.N) {
 #pragma unroll
@@ -501,6 +530,9 @@ template <int EPI>
 YUF_DEVICE void store4(const GemmParams& p, int z, int row, int col, float4 v) {
   const bool full = p.vec && col + 4 <= p.N;
   if constexpr (EPI == GEMM_EPI_F32) {
+    if (p.tanh_batch0 && z == 0) {
+      v.x = tanhf(v.x); v.y = tanhf(v.y); v.z = tanhf(v.z); v.w = tanhf(v.w);
+    }
     float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
     if (full) {
       if (p.beta != 0.f) {
@@ -527,6 +559,65 @@ YUF_DEVICE void store4(const GemmParams& p, int z, int row, int col, float4 v) {
       const float e[4] = {v.x, v.y, v.z, v.w};
       for (int c = 0; c < 4; ++c)
         if (col + c < p.N) out[c] = __float2bfloat16_rn(e[c]);
+    }
+  }
+}
+
+// The reduction step of a K split over a cluster: the calling CTA (rank r of
+// ks) sums rows [r * 128 / ks, (r + 1) * 128 / ks) of the ks partial tiles
+// (fp32, row stride pstride floats, at shared address `pbase` in every CTA) in
+// rank order and applies the epilogue; all `nthreads` threads of the CTA take
+// part.
+template <int BN, int EPI>
+YUF_DEVICE void cluster_reduce_store(const GemmParams& p, uint32_t pbase, int pstride, int ks, int r, int z,
+                                     int mt, int nt, int nthreads) {
+  const int rows = 128 / ks, r0 = r * rows;
+  if constexpr (EPI == GEMM_EPI_SWIGLU || EPI == GEMM_EPI_SWIGLU_F32) {
+    constexpr int QC = BN / 8;  // float4 chunks of "in" columns per row (BN / 2 columns)
+    for (int i = threadIdx.x; i < rows * QC; i += nthreads) {
+      const int rr = r0 + i / QC, j = (i % QC) * 4;  // j: 0 .. BN/2 - 4
+      const int cin = (j / 64) * 128 + j % 64, cgate = cin + 64;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), g = a;
+      for (int qq = 0; qq < ks; ++qq) {
+        const float4 x = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + cin) * 4), qq));
+        const float4 y = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + cgate) * 4), qq));
+        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+        g.x += y.x; g.y += y.y; g.z += y.z; g.w += y.w;
+      }
+      const int row = mt * 128 + rr, col = nt * (BN / 2) + j;
+      if (row >= p.M) continue;
+      const float h[4] = {silu(a.x) * g.x, silu(a.y) * g.y, silu(a.z) * g.z, silu(a.w) * g.w};
+      const bool full = p.vec && col + 4 <= p.n_out;
+      if constexpr (EPI == GEMM_EPI_SWIGLU_F32) {
+        float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+        if (full) *reinterpret_cast<float4*>(out + col) = make_float4(h[0], h[1], h[2], h[3]);
+        else
+          for (int c = 0; c < 4; ++c)
+            if (col + c < p.n_out) out[col + c] = h[c];
+      } else {
+        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+        if (full) {
+          uint2 pk;
+          reinterpret_cast<__nv_bfloat162*>(&pk)[0] = __floats2bfloat162_rn(h[0], h[1]);
+          reinterpret_cast<__nv_bfloat162*>(&pk)[1] = __floats2bfloat162_rn(h[2], h[3]);
+          *reinterpret_cast<uint2*>(out + col) = pk;
+        } else {
+          for (int c = 0; c < 4; ++c)
+            if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(h[c]);
+        }
+      }
+    }
+  } else {
+    constexpr int QC = BN / 4;
+    for (int i = threadIdx.x; i < rows * QC; i += nthreads) {
+      const int rr = r0 + i / QC, c = (i % QC) * 4;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int qq = 0; qq < ks; ++qq) {
+        const float4 x = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + c) * 4), qq));
+        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+      }
+      const int row = mt * 128 + rr, col = nt * BN + c;
+      if (row < p.M && col < p.N) store4<EPI>(p, z, row, col, a);
     }
   }
 }
@@ -637,49 +728,186 @@ __global__ void __launch_bounds__(GemmSplitCfg<BN>::THREADS, 1)
   tc_fence_before_sync();
   cluster_sync();  // every CTA's partial is in its shared memory
   // reduce rows [r * 128 / ks, (r + 1) * 128 / ks) over the ks partials, in rank order
-  {
-    const int rows = G::BM / ks, r0 = r * rows;
-    const uint32_t pbase = smem_u32(part);
-    if constexpr (EPI == GEMM_EPI_SWIGLU) {
-      constexpr int QC = BN / 8;  // float4 chunks of "in" columns per row (BN / 2 columns)
-      for (int i = threadIdx.x; i < rows * QC; i += G::THREADS) {
-        const int rr = r0 + i / QC, j = (i % QC) * 4;         // j: 0 .. BN/2 - 4
-        const int cin = (j / 64) * 128 + j % 64, cgate = cin + 64;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), g = a;
-        for (int qq = 0; qq < ks; ++qq) {
-          const float4 x = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * G::PSTRIDE + cin) * 4), qq));
-          const float4 y = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * G::PSTRIDE + cgate) * 4), qq));
-          a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
-          g.x += y.x; g.y += y.y; g.z += y.z; g.w += y.w;
-        }
-        const int row = mt * G::BM + rr, col = nt * (BN / 2) + j;
-        if (row < p.M) {
-          __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
-          const float h[4] = {silu(a.x) * g.x, silu(a.y) * g.y, silu(a.z) * g.z, silu(a.w) * g.w};
-          if (p.vec && col + 4 <= p.n_out) {
-            uint2 pk;
-            reinterpret_cast<__nv_bfloat162*>(&pk)[0] = __floats2bfloat162_rn(h[0], h[1]);
-            reinterpret_cast<__nv_bfloat162*>(&pk)[1] = __floats2bfloat162_rn(h[2], h[3]);
-            *reinterpret_cast<uint2*>(out + col) = pk;
-          } else {
-            for (int c = 0; c < 4; ++c)
-              if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(h[c]);
-          }
-        }
+  cluster_reduce_store<BN, EPI>(p, smem_u32(part), G::PSTRIDE, ks, r, z, mt, nt, G::THREADS);
+  if (threadIdx.x == 0 && *abort_flag) atomicAdd(&g_gemm_wait_timeouts, 1u);
+  cluster_sync();  // no CTA leaves while a peer may still read its partial
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, G::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------- fp32 (3xTF32)
+// fp32 weights at fp32 accuracy: every product as three kind::tf32 UMMAs,
+// A_lo W_hi + A_hi W_lo + A_hi W_hi (the low parts' product, ~2^-20 relative,
+// is dropped).  The weight arrives already split (host, at load time); the
+// activation tile arrives as fp32 and four converter warps split it in shared
+// memory -- the high part (low 13 mantissa bits cleared) in place, the
+// remainder into a second tile of the same swizzled layout (the split is
+// elementwise, so no index changes) -- before the MMA warp may read the stage.
+// One output tile per cluster of `ks` CTAs splitting K (ks = 1 for many rows),
+// partials reduced through distributed shared memory as in the bf16 split-K
+// kernel.
+template <int BN>
+struct GemmTf32Cfg {
+  static constexpr int BM = 128, BK = 32;         // BK fp32 = one 128-byte swizzle row
+  static constexpr int A_BYTES = BM * BK * 4;     // 16 KB, the high part after the split
+  static constexpr int AL_BYTES = A_BYTES;        // the low part
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE = A_BYTES + AL_BYTES + 2 * B_BYTES;
+  static constexpr int STAGES = std::min(8, (192 * 1024) / STAGE);
+  static constexpr int PSTRIDE = BN + 4;
+  static constexpr int P_BYTES = BM * PSTRIDE * 4;
+  static constexpr int BODY = STAGES * STAGE > P_BYTES ? STAGES * STAGE : P_BYTES;
+  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM = BODY + BAR_BYTES + 1024;
+  static constexpr uint32_t IDESC = umma_idesc_tf32(BM, BN);
+  static constexpr int THREADS = 320;  // producer, MMA, 4 epilogue warps, 4 converter warps
+  static_assert(STAGE % 1024 == 0, "stages stay 1024-byte aligned for the 128-byte swizzle");
+};
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(GemmTf32Cfg<BN>::THREADS, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap twh,
+                       const __grid_constant__ CUtensorMap twl, const GemmParams p, int ks, int kb_per) {
+  using G = GemmTf32Cfg<BN>;
+  extern __shared__ __align__(1024) unsigned char gemm_smem_raw[];
+  unsigned char* sm = gemm_smem_raw + ((1024u - (smem_u32(gemm_smem_raw) & 1023u)) & 1023u);
+  float* part = reinterpret_cast<float*>(sm);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + G::BODY);
+  uint64_t* conv = full + G::STAGES;
+  uint64_t* empty = conv + G::STAGES;
+  uint64_t* tfull = empty + G::STAGES;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tfull + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = (int)cluster_rank();
+  const int tile = blockIdx.x / ks;
+  const int per = p.m_tiles * p.n_tiles;
+  const int z = tile / per, mt = (tile % per) / p.n_tiles, nt = tile % p.n_tiles;
+  const int kblocks = (p.K + G::BK - 1) / G::BK;
+  const int kb0 = r * kb_per, kb1 = min(kblocks, kb0 + kb_per), nkb = max(0, kb1 - kb0);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < G::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);  // one arrival per converter warp
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, G::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {  // TMA: the fp32 activation tile and both weight parts
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      const int ay = (int)(z * p.a_brows) + mt * G::BM, wy = (int)(z * p.w_brows) + nt * BN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!gemm_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
+        unsigned char* st = sm + stage * G::STAGE;
+        mbar_expect_tx(&full[stage], G::A_BYTES + 2 * G::B_BYTES);
+        tma_load_2d(st, &ta, &full[stage], kb * G::BK, ay);
+        tma_load_2d(st + G::A_BYTES + G::AL_BYTES, &twh, &full[stage], kb * G::BK, wy);
+        tma_load_2d(st + G::A_BYTES + G::AL_BYTES + G::B_BYTES, &twl, &full[stage], kb * G::BK, wy);
+        ++issued;
+        if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
       }
-    } else {
-      constexpr int QC = BN / 4;
-      for (int i = threadIdx.x; i < rows * QC; i += G::THREADS) {
-        const int rr = r0 + i / QC, c = (i % QC) * 4;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int qq = 0; qq < ks; ++qq) {
-          const float4 x = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * G::PSTRIDE + c) * 4), qq));
-          a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+      if (*abort_flag)
+        for (int s = 0; s < G::STAGES; ++s) {
+          if (issued <= s) break;
+          mbar_wait(&full[s], s < stage ? phase : phase ^ 1u);
         }
-        const int row = mt * G::BM + rr, col = nt * BN + c;
-        if (row < p.M && col < p.N) store4<EPI>(p, z, row, col, a);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nkb > 0) {  // MMA issuer: three tf32 products per k step
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int i = 0; i < nkb; ++i) {
+        if (!gemm_wait(&conv[stage], phase, abort_flag)) break;
+        tc_fence_after_sync();
+        const uint32_t ah = smem_u32(sm + stage * G::STAGE), al = ah + G::A_BYTES;
+        const uint32_t bh = al + G::AL_BYTES, bl = bh + G::B_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < G::BK / 8; ++kk) {
+          const uint32_t o = kk * 32;
+          umma_tf32(tmem, umma_desc_sw128(al + o), umma_desc_sw128(bh + o), G::IDESC, (i | kk) != 0 ? 1u : 0u);
+          umma_tf32(tmem, umma_desc_sw128(ah + o), umma_desc_sw128(bl + o), G::IDESC, 1u);
+          umma_tf32(tmem, umma_desc_sw128(ah + o), umma_desc_sw128(bh + o), G::IDESC, 1u);
+        }
+        umma_commit(&empty[stage]);
+        if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
+      }
+      umma_commit(tfull);
+    }
+  } else if (warp >= 6) {  // converters: split each landed activation tile
+    const int ct = threadIdx.x - 192;  // 0 .. 127
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int i = 0; i < nkb; ++i) {
+      bool ok = gemm_wait(&full[stage], phase, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      unsigned char* st = sm + stage * G::STAGE;
+#pragma unroll
+      for (int c = 0; c < G::A_BYTES / 16 / 128; ++c) {
+        const int off = (c * 128 + ct) * 16;
+        uint4 x = *reinterpret_cast<const uint4*>(st + off), hi, lo;
+        split4(*reinterpret_cast<const float4*>(&x), hi, lo);
+        *reinterpret_cast<uint4*>(st + off) = hi;
+        *reinterpret_cast<uint4*>(st + G::A_BYTES + off) = lo;
+      }
+      fence_proxy_async();  // the split tiles become visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[stage]);
+      if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
+    }
+  }
+  // epilogue warps 2-5: the tile (ks = 1) or this CTA's partial of it
+  const bool epi_warp = warp >= 2 && warp < 6;
+  if (epi_warp) {
+    const int q = warp & 3;
+    bool ok = nkb == 0 || mbar_wait(tfull, 0);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) *abort_flag = 1;
+    if (ok && nkb > 0) tc_fence_after_sync();
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    const int prow = q * 32 + lane;
+    if (ks == 1) {
+      if (ok && nkb > 0) gemm_epilogue_tile<BN, EPI>(p, tbase, z, mt * G::BM + prow, nt, mt * G::BM + prow < p.M);
+    } else {
+      float* dst = part + (size_t)prow * G::PSTRIDE;
+      if (ok && nkb > 0) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          float v[32];
+          tmem_ld_x32(tbase + c0, v);
+#pragma unroll
+          for (int c = 0; c < 32; c += 4)
+            *reinterpret_cast<float4*>(dst + c0 + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+        }
+      } else {
+        for (int c = 0; c < BN; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
+  }
+  tc_fence_before_sync();
+  if (ks > 1) {
+    cluster_sync();  // every CTA's partial is in its shared memory
+    cluster_reduce_store<BN, EPI>(p, smem_u32(part), G::PSTRIDE, ks, r, z, mt, nt, G::THREADS);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicAdd(&g_gemm_wait_timeouts, 1u);
   cluster_sync();  // no CTA leaves while a peer may still read its partial
@@ -981,6 +1209,173 @@ yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
   return launch_gemm<256, GEMM_EPI_BF16>(g, p, s);
 }
 
+// ---------------------------------------------------------------- 3xTF32 host
+void split_tf32_host(const float* w, size_t n, float* hi, float* lo) {
+  for (size_t i = 0; i < n; ++i) {
+    uint32_t u;
+    std::memcpy(&u, &w[i], 4);
+    u &= 0xffffe000u;
+    float h;
+    std::memcpy(&h, &u, 4);
+    hi[i] = h;
+    lo[i] = w[i] - h;
+  }
+}
+
+static bool make_f32_map(CUtensorMap* m, const void* base, long long inner, long long rows, long long ld,
+                         int box_rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t gdim[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)ld * 4};
+  const cuuint32_t box[2] = {32u, (cuuint32_t)box_rows};
+  const cuuint32_t estride[2] = {1u, 1u};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int EPI>
+static int tf32_slots(int ks) {
+  static int cache[128][9] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 127;
+  if (cache[dev][ks] == 0) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(ks * 16, 1, 1);
+    cfg.blockDim = dim3(GemmTf32Cfg<BN>::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = GemmTf32Cfg<BN>::SMEM;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = ks;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tf32x3_kernel<BN, EPI>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / (2 * ks);
+    }
+    cache[dev][ks] = std::max(1, n);
+  }
+  return cache[dev][ks];
+}
+
+template <int BN, int EPI>
+static yuf_status_t launch_tf32(const GemmArgs& g, const void* W_lo, GemmParams p, int ks, cudaStream_t s) {
+  using G = GemmTf32Cfg<BN>;
+  static std::once_flag attr_once[128];
+  static cudaError_t attr_err[128];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 127;
+  std::call_once(attr_once[dev], [&] {
+    attr_err[dev] = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         G::SMEM);
+  });
+  if (attr_err[dev] != cudaSuccess) {
+    set_error("gemm: kernel attributes: %s", cudaGetErrorString(attr_err[dev]));
+    return YUF_ERR_CUDA;
+  }
+  CUtensorMap ta, twh, twl;
+  if (!make_f32_map(&ta, g.A, g.K, g.a_rows, g.lda, G::BM) || !make_f32_map(&twh, g.W, g.K, g.w_rows, g.K, BN) ||
+      !make_f32_map(&twl, W_lo, g.K, g.w_rows, g.K, BN)) {
+    set_error("gemm: cuTensorMapEncodeTiled failed (fp32; A rows %lld, lda %lld, W rows %lld, K %d)", g.a_rows,
+              g.lda, g.w_rows, g.K);
+    return YUF_ERR_CUDA;
+  }
+  p.n_tiles = (p.N + BN - 1) / BN;
+  const int kblocks = (p.K + G::BK - 1) / G::BK;
+  const int kb_per = (kblocks + ks - 1) / ks;
+  const long long tiles = (long long)p.m_tiles * p.n_tiles * p.batch;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(tiles * ks), 1, 1);
+  cfg.blockDim = dim3(G::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = G::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (pdl_enabled()) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
+  cudaLaunchKernelEx(&cfg, gemm_tf32x3_kernel<BN, EPI>, ta, twh, twl, p, ks, kb_per);
+  return check_launch("gemm_tf32x3_kernel");
+}
+
+template <int EPI>
+static yuf_status_t dispatch_tf32(const GemmArgs& g, const void* W_lo, const GemmParams& p, cudaStream_t s) {
+  const int kblocks = (g.K + 31) / 32;
+  const int sms = sm_count();
+  int best_bn = 0, best_ks = 1;
+  long long best_cost = -1;
+  for (int bn : {64, 128}) {
+    if ((EPI == GEMM_EPI_SWIGLU_F32) && (bn < 128 || g.N % bn != 0)) continue;
+    const long long tiles = (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch;
+    for (int ks : {8, 4, 2, 1}) {
+      if (ks > 1 && (ks > kblocks || p.m_tiles > 2)) continue;  // the K split serves few rows
+      const int slots = bn == 64 ? tf32_slots<64, EPI>(ks) : tf32_slots<128, EPI>(ks);
+      if (ks > 1 && tiles > slots) continue;
+      const long long kb_per = (kblocks + ks - 1) / ks;
+      const long long waves = (tiles + (ks == 1 ? sms : slots) - 1) / (ks == 1 ? sms : slots);
+      const long long cost = (128 + 2 * bn) * kb_per * waves;
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        best_bn = bn;
+        best_ks = ks;
+      }
+    }
+  }
+  if (best_bn == 64) return launch_tf32<64, EPI>(g, W_lo, p, best_ks, s);
+  return launch_tf32<128, EPI>(g, W_lo, p, best_ks, s);
+}
+
+yuf_status_t gemm_tf32x3(const GemmArgs& g, const void* W_lo, cudaStream_t s) {
+  if (g.M <= 0 || g.N <= 0 || g.batch <= 0) return YUF_OK;
+  const bool ok = (reinterpret_cast<uintptr_t>(g.A) & 15) == 0 && g.lda % 4 == 0 &&
+                  (reinterpret_cast<uintptr_t>(g.W) & 15) == 0 && (reinterpret_cast<uintptr_t>(W_lo) & 15) == 0 &&
+                  g.K % 4 == 0 && g.K > 0;
+  if (!ok) {
+    set_error("gemm (fp32): operands need 16-byte aligned rows (lda %lld, K %d)", g.lda, g.K);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  if (g.epi != GEMM_EPI_F32 && g.epi != GEMM_EPI_SWIGLU_F32) {
+    set_error("gemm (fp32): epilogue %d writes bf16", g.epi);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  GemmParams p{};
+  p.C = g.C;
+  p.ldc = g.ldc;
+  p.c_bstride = g.c_bstride;
+  p.M = g.M;
+  p.N = g.N;
+  p.K = g.K;
+  p.batch = g.batch;
+  p.a_brows = g.a_brows;
+  p.w_brows = g.w_brows;
+  p.beta = g.beta;
+  p.tanh_batch0 = g.tanh_batch0;
+  p.n_out = g.epi == GEMM_EPI_SWIGLU_F32 ? g.n_out : g.N;
+  p.m_tiles = (g.M + 127) / 128;
+  p.vec = (reinterpret_cast<uintptr_t>(g.C) & 15) == 0 && g.ldc % 4 == 0 && g.c_bstride % 4 == 0;
+  if (g.epi == GEMM_EPI_SWIGLU_F32) {
+    if (g.N % 128 != 0) {
+      set_error("gemm: the SiLU-gate weight must hold whole 128-row groups (N = %d)", g.N);
+      return YUF_ERR_INVALID_ARGUMENT;
+    }
+    return dispatch_tf32<GEMM_EPI_SWIGLU_F32>(g, W_lo, p, s);
+  }
+  return dispatch_tf32<GEMM_EPI_F32>(g, W_lo, p, s);
+}
+
 unsigned int gemm_wait_timeouts() {
   unsigned int n = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&n, g_gemm_wait_timeouts, sizeof(n)) != cudaSuccess ||
@@ -1042,4 +1437,60 @@ extern "C" yuf_status_t yuf_gemm_bf16(const void* A, long long lda, long long a_
   g.tanh_batch0 = epilogue == YUF_GEMM_BF16_TANH0;
   g.n_out = n_out;
   return gemm_bf16(g, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" yuf_status_t yuf_gemm_tf32x3(const float* A, long long lda, long long a_batch_rows, const float* W_hi,
+                                        const float* W_lo, long long w_batch_rows, float* C, long long ldc,
+                                        long long c_batch_stride, int M, int N, int K, int batch, int epilogue,
+                                        int accumulate, int n_out, void* stream) {
+  if (!A || !W_hi || !W_lo || !C || M < 0 || N < 0 || K <= 0 || batch < 0 || lda < K || ldc < 1) {
+    set_error("gemm (fp32): null operand or bad sizes (M=%d N=%d K=%d batch=%d lda=%lld ldc=%lld)", M, N, K,
+              batch, lda, ldc);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  if (epilogue != YUF_GEMM_F32 && epilogue != YUF_GEMM_F32_TANH0 && epilogue != YUF_GEMM_SILU_GATE_F32) {
+    set_error("gemm (fp32): epilogue %d has no fp32 form", epilogue);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  if (accumulate && epilogue != YUF_GEMM_F32) {
+    set_error("gemm (fp32): accumulate needs the plain fp32 epilogue");
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  if (epilogue == YUF_GEMM_SILU_GATE_F32 && (n_out <= 0 || 2 * (long long)n_out > N)) {
+    set_error("gemm (fp32): the SiLU-gate epilogue needs 0 < n_out <= N / 2 (n_out=%d N=%d)", n_out, N);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  if (batch > 1 && (a_batch_rows < M || w_batch_rows < N)) {
+    set_error("gemm (fp32): batches overlap");
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  GemmArgs g{};
+  g.A = A;
+  g.lda = lda;
+  g.a_brows = batch > 1 ? a_batch_rows : 0;
+  g.a_rows = (long long)(batch > 1 ? batch - 1 : 0) * g.a_brows + M;
+  g.W = W_hi;
+  g.w_brows = batch > 1 ? w_batch_rows : 0;
+  g.w_rows = (long long)(batch > 1 ? batch - 1 : 0) * g.w_brows + N;
+  g.C = C;
+  g.ldc = ldc;
+  g.c_bstride = c_batch_stride;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.batch = batch;
+  g.epi = epilogue == YUF_GEMM_SILU_GATE_F32 ? GEMM_EPI_SWIGLU_F32 : GEMM_EPI_F32;
+  g.beta = accumulate ? 1.f : 0.f;
+  g.tanh_batch0 = epilogue == YUF_GEMM_F32_TANH0;
+  g.n_out = n_out;
+  return gemm_tf32x3(g, W_lo, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" yuf_status_t yuf_tf32_split(const float* w, size_t n, float* hi, float* lo) {
+  if ((n > 0) && (!w || !hi || !lo)) {
+    set_error("tf32_split: null buffer");
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  split_tf32_host(w, n, hi, lo);
+  return YUF_OK;
 }

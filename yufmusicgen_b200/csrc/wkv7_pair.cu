@@ -706,12 +706,6 @@ YUF_DEVICE uint32_t corr_tc_off(int r, int c) {
   return (uint32_t)((r & 7) * 16 + c * 128 + (r >> 3) * (int)CorrTcCfg<N>::SBO);
 }
 
-YUF_DEVICE void split4(const float4 x, uint4& hi, uint4& lo) {
-  split_tf32(x.x, hi.x, lo.x);
-  split_tf32(x.y, hi.y, lo.y);
-  split_tf32(x.z, hi.z, lo.z);
-  split_tf32(x.w, hi.w, lo.w);
-}
 
 template <int N>
 __global__ void __launch_bounds__(128)
