@@ -228,7 +228,7 @@ typedef struct yuf_model_config {
 } yuf_model_config;
 
 enum {
-  YUF_PRECISION_FP32 = 0,        /* fp32 weights; GEMMs with fp32 accuracy (BF16x9 emulation) */
+  YUF_PRECISION_FP32 = 0,        /* fp32 weights; GEMMs with fp32 accuracy (3xTF32 tensor cores) */
   YUF_PRECISION_BF16_WEIGHTS = 1 /* bf16 weights and GEMM inputs, fp32 accumulate and state */
 };
 

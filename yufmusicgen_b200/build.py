@@ -24,7 +24,7 @@ INCLUDE = PKG.parent / "include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", str(INCLUDE),
               "--expt-relaxed-constexpr"]
-LINK_LIBS = ["-lcublas", "-lcublasLt", "-lcudart"]
+LINK_LIBS = ["-lcudart"]
 
 
 def nvcc() -> str:

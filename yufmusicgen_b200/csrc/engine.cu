@@ -15,17 +15,14 @@
 //   x    += W_out(silu(x_f W_in^T) * (x_f W_g^T))      GEMM [8d, d], silu_mul, GEMM (beta = 1)
 // then logits = LN_final(x) E^T (tied head, model.py:389-391, 421).
 //
-// bf16-weight mode: every projection is the library's tcgen05 GEMM (gemm.cu)
-// on bf16 weights and bf16 activations with fp32 accumulation, with the work
+// Every projection is the library's tcgen05 GEMM (gemm.cu), with the work
 // around it folded into the epilogues: tanh of the w branch (lr1), the residual
 // adds of W_o / ROSA out / FFN out (accumulate into x), and SiLU(in) * gate of
-// the FFN (its weight packed in 64-row in/gate groups), so the FFN hidden
-// leaves the GEMM as bf16 and no [rows, 8d] intermediate exists.  fp32 mode
-// runs the products on cuBLAS's BF16x9 FP32 emulation (fp32-accurate products
-// on the tensor cores).  Everything else (scans, norms, activations, state)
-// stays fp32.
-
-#include <cublas_v2.h>
+// the FFN (its weight packed in 64-row in/gate groups), so no [rows, 8d]
+// intermediate exists.  bf16-weight mode: bf16 weights and bf16 activations
+// with fp32 accumulation.  fp32 mode: fp32 weights (stored as their tf32 high
+// part and remainder) and fp32 activations at fp32 accuracy (3xTF32).
+// Everything else (scans, norms, activations, state) stays fp32.
 
 #include <algorithm>
 #include <cmath>
@@ -61,24 +58,29 @@ static int reference_low_rank(int d) {
 
 using namespace yuf;
 
+// A projection weight [rows, K]: bf16 in bf16-weight mode (lo unused); in fp32
+// mode its tf32 high part and the fp32 remainder, two planes of rows * K.
+struct Wt {
+  void* hi = nullptr;
+  void* lo = nullptr;
+};
+
 struct LayerW {
   float *ln_t_w, *ln_t_b, *mix, *w0, *a0, *k_k, *k_a;
-  void *W_rkv, *W_lr1, *W_lr2, *W_o;
+  Wt W_rkv, W_lr1, W_lr2, W_o;
   float *ln_o_w, *ln_o_b, *ln_r_w, *ln_r_b, *householder, *decay, *b_rosa;
-  void *W_rosa_in, *W_rosa_out;
+  Wt W_rosa_in, W_rosa_out;
   float *ln_f_w, *ln_f_b;
-  void *W_ffn_in, *W_ffn_out;
+  Wt W_ffn_in, W_ffn_out;
 };
 
 struct yuf_model {
   yuf_model_config cfg{};
   int precision = 0;
   int device = 0;
-  cublasHandle_t blas = nullptr;
-  bool emulated_fp32 = false;
   std::vector<std::unique_ptr<DevBuf>> owned;
   float* emb = nullptr;        // [V, d] fp32
-  void* emb_gemm = nullptr;    // LM head operand (fp32 or bf16 copy)
+  Wt emb_gemm;                 // LM head operand (the tied embedding as a projection weight)
   float *fin_w = nullptr, *fin_b = nullptr;
   std::vector<LayerW> L;
   // state slots
@@ -87,7 +89,6 @@ struct yuf_model {
   // workspace
   size_t ws_rows = 0;
   std::unique_ptr<DevBuf> ws;
-  std::unique_ptr<DevBuf> blas_ws;
   int* d_err = nullptr;
   // decode-step CUDA graphs, keyed by (B, slot0, ids, logits); a workspace
   // reallocation bumps ws_gen and invalidates them
@@ -150,58 +151,28 @@ namespace yuf {
       return e_ == cudaErrorMemoryAllocation ? YUF_ERR_OUT_OF_MEMORY : YUF_ERR_CUDA; \
     }                                                                         \
   } while (0)
-#define Y_BLAS(call)                                                          \
-  do {                                                                        \
-    cublasStatus_t s_ = (call);                                               \
-    if (s_ != CUBLAS_STATUS_SUCCESS) {                                        \
-      set_error("%s failed: cuBLAS status %d", #call, (int)s_);               \
-      return YUF_ERR_CUDA;                                                    \
-    }                                                                         \
-  } while (0)
 #define Y_TRY(call)                    \
   do {                                 \
     yuf_status_t st_ = (call);         \
     if (st_ != YUF_OK) return st_;     \
   } while (0)
 
-// Row-major C[M,N] (ldc) = A[M,K] (lda) . W[N,K]^T + beta C, batched with strides.
-static yuf_status_t gemm(yuf_model* m, const void* A, int lda, long long sA, const void* W,
-                         long long sW, float* C, int ldc, long long sC, int M, int N, int K,
-                         float beta, int batch, cudaStream_t s) {
-  const float alpha = 1.f;
-  const bool bf = m->precision == YUF_PRECISION_BF16_WEIGHTS;
-  const cudaDataType ty = bf ? CUDA_R_16BF : CUDA_R_32F;
-  // fp32: the handle's math mode (CUBLAS_FP32_EMULATED_BF16X9_MATH) lets cuBLAS run
-  // the fp32 products as BF16x9 on the tensor cores with fp32-level accuracy.
-  const cublasComputeType_t ct = CUBLAS_COMPUTE_32F;
-  Y_BLAS(cublasSetStream(m->blas, s));
-  // cublasSetStream resets the handle to cuBLAS's own workspace pool; point it
-  // back at the model's preallocated workspace so no GEMM allocates.
-  Y_BLAS(cublasSetWorkspace(m->blas, m->blas_ws->p, m->blas_ws->bytes));
-  if (batch == 1) {
-    Y_BLAS(cublasGemmEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, &alpha, W, ty, K, A, ty, lda,
-                        &beta, C, CUDA_R_32F, ldc, ct, CUBLAS_GEMM_DEFAULT));
-  } else {
-    Y_BLAS(cublasGemmStridedBatchedEx(m->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, &alpha, W, ty, K, sW,
-                                      A, ty, lda, sA, &beta, C, CUDA_R_32F, ldc, sC, batch, ct,
-                                      CUBLAS_GEMM_DEFAULT));
-  }
-  return YUF_OK;
-}
-
-// bf16-weight mode: C[z] = A[z] . W[z]^T on the tcgen05 GEMM (gemm.cu).
+// C[z] = A[z] . W[z]^T on the tcgen05 GEMM (gemm.cu) in the model's precision:
+// bf16 operands (bf16-weight mode) or fp32 operands at fp32 accuracy (3xTF32).
 // a_brows / w_brows: rows between batches in A / W; c_bstride: elements
-// between batches in C.
-static yuf_status_t proj_bf16(const void* A, long long lda, long long a_brows, const void* W,
-                              long long w_brows, void* C, long long ldc, long long c_bstride, int M,
-                              int N, int K, int batch, int epi, bool accumulate, cudaStream_t s,
-                              int n_out = 0, bool tanh_batch0 = false) {
+// between batches in C.  `epi` names the bf16-mode epilogue; fp32 mode writes
+// the same results in fp32 (GEMM_EPI_BF16 -> fp32 with the same tanh,
+// GEMM_EPI_SWIGLU -> GEMM_EPI_SWIGLU_F32).
+static yuf_status_t proj(const yuf_model* m, const void* A, long long lda, long long a_brows, const Wt& W,
+                         long long w_brows, void* C, long long ldc, long long c_bstride, int M, int N, int K,
+                         int batch, int epi, bool accumulate, cudaStream_t s, int n_out = 0,
+                         bool tanh_batch0 = false) {
   GemmArgs g{};
   g.A = A;
   g.lda = lda;
   g.a_brows = a_brows;
   g.a_rows = (long long)(batch - 1) * a_brows + M;
-  g.W = W;
+  g.W = W.hi;
   g.w_brows = w_brows;
   g.w_rows = (long long)(batch - 1) * w_brows + N;
   g.C = C;
@@ -215,17 +186,19 @@ static yuf_status_t proj_bf16(const void* A, long long lda, long long a_brows, c
   g.beta = accumulate ? 1.f : 0.f;
   g.tanh_batch0 = tanh_batch0 ? 1 : 0;
   g.n_out = n_out;
-  return gemm_bf16(g, s);
+  if (m->precision == YUF_PRECISION_BF16_WEIGHTS) return gemm_bf16(g, s);
+  g.epi = epi == GEMM_EPI_SWIGLU ? GEMM_EPI_SWIGLU_F32 : GEMM_EPI_F32;
+  return gemm_tf32x3(g, W.lo, s);
 }
 
-// Rows of the packed FFN in/gate weight of bf16 mode: 64-row groups of
-// ffn_in.weight and ffn_gate.weight alternating, the hidden width padded to 64.
+// Rows of the packed FFN in/gate weight: 64-row groups of ffn_in.weight and
+// ffn_gate.weight alternating, the hidden width padded to 64.
 static int ffn_pad(int d) { return (4 * d + 63) / 64 * 64; }
 
 // Workspace for `rows` token rows (grown on demand; never shrinks).
 struct WS {
   float *x, *xt, *mixed, *rkv, *lr1, *lr2, *w_raw, *k_adj, *a_op, *b_op, *g, *y, *tmp, *rosa, *read,
-      *ig, *h, *scan;  // scan: scratch of the time-parallel scans
+      *h, *scan;  // scan: scratch of the time-parallel scans
   __nv_bfloat16* bf;  // bf16 staging of a GEMM input (largest: [rows, 4d] or [6][rows][d])
 };
 
@@ -233,7 +206,7 @@ static size_t ws_floats_per_row(const yuf_model* m) {
   const size_t d = m->d(), lr = m->lr(), R = m->R();
   return d /*x*/ + d /*xt*/ + 6 * d /*mixed*/ + 3 * d /*rkv*/ + 3 * lr /*lr1*/ + 3 * d /*lr2*/ +
          5 * d /*w_raw,k_adj,a_op,b_op,g*/ + d /*y*/ + d /*tmp*/ + 3 * R /*rosa*/ + R /*read*/ +
-         8 * d /*ig*/ + 4 * d /*h*/;
+         4 * d /*h*/;
 }
 
 // Scratch of the time-parallel scans for a forward over `rows` token rows.
@@ -298,7 +271,6 @@ static WS carve(yuf_model* m, size_t rows, void* base, bool decode_only = false)
   w.tmp = take(rows * d);
   w.rosa = take(rows * 3 * R);
   w.read = take(rows * R);
-  w.ig = take(rows * 8 * d);
   w.h = take(rows * 4 * d);
   {  // 16-byte alignment for the scans' cp.async / float4 accesses
     uintptr_t a = reinterpret_cast<uintptr_t>(p);
@@ -383,24 +355,14 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     }
     const size_t esz = m->precision == YUF_PRECISION_BF16_WEIGHTS ? 2 : 4;
     const char* mixed_hi = static_cast<const char*>(mixed) + 3 * RD * esz;  // w, a, g mixes
-    if (bf) {
-      // r, k, v; then x_{w,a,g} L1 with tanh on the w branch, written as bf16 into
-      // the lr1 buffer, which feeds L2
-      Y_TRY(proj_bf16(mixed, d, (long long)rows, Lw.W_rkv, d, w.rkv, d, RD, (int)rows, d, d, 3,
-                      GEMM_EPI_F32, false, s));
-      __nv_bfloat16* lr1b = reinterpret_cast<__nv_bfloat16*>(w.lr1);
-      Y_TRY(proj_bf16(mixed_hi, d, (long long)rows, Lw.W_lr1, lr, lr1b, lr, (long long)rows * lr,
-                      (int)rows, lr, d, 3, GEMM_EPI_BF16, false, s, 0, true));
-      Y_TRY(proj_bf16(lr1b, lr, (long long)rows, Lw.W_lr2, d, w.lr2, d, RD, (int)rows, d, lr, 3,
-                      GEMM_EPI_F32, false, s));
-    } else {
-      Y_TRY(gemm(m, mixed, d, RD, Lw.W_rkv, (long long)d * d, w.rkv, d, RD, (int)rows, d, d, 0.f, 3, s));
-      Y_TRY(gemm(m, mixed_hi, d, RD, Lw.W_lr1, (long long)lr * d, w.lr1, lr, rows * lr, (int)rows, lr, d,
-                 0.f, 3, s));
-      launch_tanh<float>(w.lr1, w.lr1, rows * lr, rows * lr, s);  // w branch: tanh(x_w W1)
-      Y_TRY(gemm(m, w.lr1, lr, rows * lr, Lw.W_lr2, (long long)d * lr, w.lr2, d, RD, (int)rows, d, lr,
-                 0.f, 3, s));
-    }
+    // r, k, v; then x_{w,a,g} L1 with tanh on the w branch (bf16 in bf16 mode),
+    // written into the lr1 buffer, which feeds L2
+    Y_TRY(proj(m, mixed, d, (long long)rows, Lw.W_rkv, d, w.rkv, d, RD, (int)rows, d, d, 3, GEMM_EPI_F32,
+               false, s));
+    Y_TRY(proj(m, mixed_hi, d, (long long)rows, Lw.W_lr1, lr, w.lr1, lr, (long long)rows * lr, (int)rows, lr,
+               d, 3, GEMM_EPI_BF16, false, s, 0, true));
+    Y_TRY(proj(m, w.lr1, lr, (long long)rows, Lw.W_lr2, d, w.lr2, d, RD, (int)rows, d, lr, 3, GEMM_EPI_F32,
+               false, s));
     launch_timemix_post(w.rkv + RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD, Lw.w0, Lw.a0, Lw.k_k, Lw.k_a,
                         w.w_raw, w.k_adj, w.a_op, w.b_op, w.g, (int)rows, H, N, s);
     if (T == 1)
@@ -425,59 +387,35 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
       dump(m, "y", li, w.y, RD, s);
     }
     // x += W_o (LN_out(y) * g)
-    if (bf)
-      Y_TRY(proj_bf16(att, d, 0, Lw.W_o, 0, w.x, d, 0, (int)rows, d, d, 1, GEMM_EPI_F32, true, s));
-    else
-      Y_TRY(gemm(m, att, d, 0, Lw.W_o, 0, w.x, d, 0, (int)rows, d, d, 1.f, 1, s));
+    Y_TRY(proj(m, att, d, 0, Lw.W_o, 0, w.x, d, 0, (int)rows, d, d, 1, GEMM_EPI_F32, true, s));
     if (m->debug) dump(m, "h1", li, w.x, RD, s);
     // --- ROSA: [cand | write | gate] = LN_rosa(x) W^T, scan, x += read W_out^T
     const void* xr = ln_in(w.x, Lw.ln_r_w, Lw.ln_r_b, nullptr);
-    if (bf)
-      Y_TRY(proj_bf16(xr, d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0, (int)rows, 3 * R, d, 1, GEMM_EPI_F32,
-                      false, s));
-    else
-      Y_TRY(gemm(m, xr, d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0, (int)rows, 3 * R, d, 0.f, 1, s));
+    Y_TRY(proj(m, xr, d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0, (int)rows, 3 * R, d, 1, GEMM_EPI_F32, false, s));
     Y_TRY(rosa_engine_dispatch(w.rosa, w.rosa + R, w.rosa + 2 * R, Lw.b_rosa, Lw.b_rosa + R,
                                Lw.b_rosa + 2 * R, 3 * R, Lw.decay, Lw.householder, mem, w.read, mem, B,
                                T, R, w.scan, bf ? w.bf : nullptr, s));
     if (m->debug) dump(m, "read", li, w.read, rows * R, s);
-    if (bf)
-      Y_TRY(proj_bf16(w.bf, R, 0, Lw.W_rosa_out, 0, w.x, d, 0, (int)rows, d, R, 1, GEMM_EPI_F32, true, s));
-    else
-      Y_TRY(gemm(m, w.read, R, 0, Lw.W_rosa_out, 0, w.x, d, 0, (int)rows, d, R, 1.f, 1, s));
+    Y_TRY(proj(m, bf ? static_cast<const void*>(w.bf) : w.read, R, 0, Lw.W_rosa_out, 0, w.x, d, 0, (int)rows,
+               d, R, 1, GEMM_EPI_F32, true, s));
     if (m->debug) dump(m, "h2", li, w.x, RD, s);
     // --- FFN: x += W_out(SiLU(x_f W_in^T) * (x_f W_g^T))
     const void* xf = ln_in(w.x, Lw.ln_f_w, Lw.ln_f_b, nullptr);
-    if (bf) {
-      // the hidden leaves the GEMM as bf16 (SiLU-gate epilogue) into the h buffer
-      __nv_bfloat16* hid = reinterpret_cast<__nv_bfloat16*>(w.h);
-      Y_TRY(proj_bf16(xf, d, 0, Lw.W_ffn_in, 0, hid, 4 * d, 0, (int)rows, 2 * ffn_pad(d), d, 1,
-                      GEMM_EPI_SWIGLU, false, s, 4 * d));
-      Y_TRY(proj_bf16(hid, 4 * d, 0, Lw.W_ffn_out, 0, w.x, d, 0, (int)rows, d, 4 * d, 1, GEMM_EPI_F32, true,
-                      s));
-    } else {
-      Y_TRY(gemm(m, xf, d, 0, Lw.W_ffn_in, 0, w.ig, 8 * d, 0, (int)rows, 8 * d, d, 0.f, 1, s));
-      launch_silu_mul<float>(w.ig, w.h, (int)rows, 4 * d, s);
-      Y_TRY(gemm(m, w.h, 4 * d, 0, Lw.W_ffn_out, 0, w.x, d, 0, (int)rows, d, 4 * d, 1.f, 1, s));
-    }
+    // the hidden leaves the GEMM through the SiLU-gate epilogue into the h buffer
+    Y_TRY(proj(m, xf, d, 0, Lw.W_ffn_in, 0, w.h, 4 * d, 0, (int)rows, 2 * ffn_pad(d), d, 1, GEMM_EPI_SWIGLU,
+               false, s, 4 * d));
+    Y_TRY(proj(m, w.h, 4 * d, 0, Lw.W_ffn_out, 0, w.x, d, 0, (int)rows, d, 4 * d, 1, GEMM_EPI_F32, true, s));
     if (m->debug) dump(m, "h3", li, w.x, RD, s);
   }
   // final norm + tied LM head
   const void* hn = ln_in(w.x, m->fin_w, m->fin_b, nullptr);
   const size_t esz = bf ? 2 : 4;
-  if (logits_all) {
-    if (bf)
-      Y_TRY(proj_bf16(hn, d, 0, m->emb_gemm, 0, logits_all, V, 0, (int)rows, V, d, 1, GEMM_EPI_F32, false, s));
-    else
-      Y_TRY(gemm(m, hn, d, 0, m->emb_gemm, 0, logits_all, V, 0, (int)rows, V, d, 0.f, 1, s));
-  }
+  if (logits_all)
+    Y_TRY(proj(m, hn, d, 0, m->emb_gemm, 0, logits_all, V, 0, (int)rows, V, d, 1, GEMM_EPI_F32, false, s));
   if (logits_last) {
     const void* last = static_cast<const char*>(hn) + (size_t)(T - 1) * d * esz;
-    if (bf)
-      Y_TRY(proj_bf16(last, (long long)T * d, 0, m->emb_gemm, 0, logits_last, V, 0, B, V, d, 1, GEMM_EPI_F32,
-                      false, s));
-    else
-      Y_TRY(gemm(m, last, T * d, 0, m->emb_gemm, 0, logits_last, V, 0, B, V, d, 0.f, 1, s));
+    Y_TRY(proj(m, last, (long long)T * d, 0, m->emb_gemm, 0, logits_last, V, 0, B, V, d, 1, GEMM_EPI_F32, false,
+               s));
     if (m->debug) dump(m, "logits", -1, logits_last, (size_t)B * V, s);
   }
   return check_launch("model forward");
@@ -502,12 +440,36 @@ static yuf_status_t upload(yuf_model* m, const std::unordered_map<std::string, H
   return YUF_OK;
 }
 
+// A packed host fp32 weight to the device in the model precision: bf16, or
+// the tf32 high part and the remainder (two planes) for fp32 mode.
+static yuf_status_t upload_weight(yuf_model* m, const std::vector<float>& host, Wt* out) {
+  const size_t total = host.size();
+  if (m->precision == YUF_PRECISION_BF16_WEIGHTS) {
+    std::vector<__nv_bfloat16> hb(total);
+    for (size_t i = 0; i < total; ++i) hb[i] = __float2bfloat16_rn(host[i]);
+    void* d = m->alloc(total * 2);
+    if (!d) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+    Y_CUDA(cudaMemcpy(d, hb.data(), total * 2, cudaMemcpyHostToDevice));
+    out->hi = d;
+    out->lo = nullptr;
+  } else {
+    std::vector<float> hl(2 * total);
+    split_tf32_host(host.data(), total, hl.data(), hl.data() + total);
+    float* d = static_cast<float*>(m->alloc(2 * total * 4));
+    if (!d) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+    Y_CUDA(cudaMemcpy(d, hl.data(), 2 * total * 4, cudaMemcpyHostToDevice));
+    out->hi = d;
+    out->lo = d + total;
+  }
+  return YUF_OK;
+}
+
 // Pack host fp32 matrices (each [rows_i, K], row-major) into one GEMM weight in
 // the model precision.  transpose: the source is [K, rows] (a Parameter used as
 // x @ P, model.py:108-112) and is transposed to [rows, K].
 static yuf_status_t pack_weight(yuf_model* m, const std::unordered_map<std::string, HostTensor>& t,
                                 const std::vector<std::string>& names, const std::vector<int>& rows,
-                                int K, bool transpose, void** out) {
+                                int K, bool transpose, Wt* out) {
   size_t total = 0;
   for (int r : rows) total += (size_t)r * K;
   std::vector<float> host(total);
@@ -526,47 +488,28 @@ static yuf_status_t pack_weight(yuf_model* m, const std::unordered_map<std::stri
     }
     off += (size_t)rows[i] * K;
   }
-  if (m->precision == YUF_PRECISION_BF16_WEIGHTS) {
-    std::vector<__nv_bfloat16> hb(total);
-    for (size_t i = 0; i < total; ++i) hb[i] = __float2bfloat16_rn(host[i]);
-    void* d = m->alloc(total * 2);
-    if (!d) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
-    Y_CUDA(cudaMemcpy(d, hb.data(), total * 2, cudaMemcpyHostToDevice));
-    *out = d;
-  } else {
-    void* d = m->alloc(total * 4);
-    if (!d) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
-    Y_CUDA(cudaMemcpy(d, host.data(), total * 4, cudaMemcpyHostToDevice));
-    *out = d;
-  }
-  return YUF_OK;
+  return upload_weight(m, host, out);
 }
 
-// bf16 mode: ffn_in.weight and ffn_gate.weight ([F, d] each) interleaved in
-// 64-row groups -- rows 128g .. 128g+63 = ffn_in rows 64g .., rows 128g+64 ..
-// 128g+127 = the same ffn_gate rows -- with F padded to a multiple of 64 by zero
-// rows, the layout the GEMM's SiLU-gate epilogue pairs columns in.
-static yuf_status_t pack_ffn_in_bf16(yuf_model* m, const std::unordered_map<std::string, HostTensor>& t,
-                                     const std::string& in_name, const std::string& gate_name, void** out) {
+// ffn_in.weight and ffn_gate.weight ([F, d] each) interleaved in 64-row groups
+// -- rows 128g .. 128g+63 = ffn_in rows 64g .., rows 128g+64 .. 128g+127 = the
+// same ffn_gate rows -- with F padded to a multiple of 64 by zero rows, the
+// layout the GEMM's SiLU-gate epilogue pairs columns in.
+static yuf_status_t pack_ffn_in(yuf_model* m, const std::unordered_map<std::string, HostTensor>& t,
+                                const std::string& in_name, const std::string& gate_name, Wt* out) {
   const int d = m->d(), F = 4 * d, Fp = ffn_pad(d);
   auto in = t.find(in_name), gate = t.find(gate_name);
   Y_REQUIRE(in != t.end() && gate != t.end(), "model: missing tensor %s or %s", in_name.c_str(),
             gate_name.c_str());
   Y_REQUIRE(in->second.n == (int64_t)F * d && gate->second.n == (int64_t)F * d,
             "model: %s / %s must hold %lld elements", in_name.c_str(), gate_name.c_str(), (long long)F * d);
-  std::vector<__nv_bfloat16> hb((size_t)2 * Fp * d, __float2bfloat16_rn(0.f));
+  std::vector<float> host((size_t)2 * Fp * d, 0.f);
   for (int r = 0; r < F; ++r) {
     const size_t dst_in = ((size_t)(r / 64) * 128 + r % 64) * d, dst_gate = dst_in + (size_t)64 * d;
-    for (int k = 0; k < d; ++k) {
-      hb[dst_in + k] = __float2bfloat16_rn(in->second.p[(size_t)r * d + k]);
-      hb[dst_gate + k] = __float2bfloat16_rn(gate->second.p[(size_t)r * d + k]);
-    }
+    std::memcpy(host.data() + dst_in, in->second.p + (size_t)r * d, (size_t)d * 4);
+    std::memcpy(host.data() + dst_gate, gate->second.p + (size_t)r * d, (size_t)d * 4);
   }
-  void* dptr = m->alloc(hb.size() * 2);
-  if (!dptr) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
-  Y_CUDA(cudaMemcpy(dptr, hb.data(), hb.size() * 2, cudaMemcpyHostToDevice));
-  *out = dptr;
-  return YUF_OK;
+  return upload_weight(m, host, out);
 }
 
 static yuf_status_t load_weights(yuf_model* m, const std::unordered_map<std::string, HostTensor>& t) {
@@ -632,10 +575,7 @@ static yuf_status_t load_weights(yuf_model* m, const std::unordered_map<std::str
     Y_TRY(pack_weight(m, t, {ro + "output.weight"}, {d}, R, false, &Lw.W_rosa_out));
     Y_TRY(upload(m, t, p + "norm_ffn.weight", d, &Lw.ln_f_w));
     Y_TRY(upload(m, t, p + "norm_ffn.bias", d, &Lw.ln_f_b));
-    if (m->precision == YUF_PRECISION_BF16_WEIGHTS)
-      Y_TRY(pack_ffn_in_bf16(m, t, p + "ffn_in.weight", p + "ffn_gate.weight", &Lw.W_ffn_in));
-    else
-      Y_TRY(pack_weight(m, t, {p + "ffn_in.weight", p + "ffn_gate.weight"}, {F, F}, d, false, &Lw.W_ffn_in));
+    Y_TRY(pack_ffn_in(m, t, p + "ffn_in.weight", p + "ffn_gate.weight", &Lw.W_ffn_in));
     Y_TRY(pack_weight(m, t, {p + "ffn_out.weight"}, {d}, F, false, &Lw.W_ffn_out));
   }
   return YUF_OK;
@@ -660,9 +600,9 @@ yuf_status_t model_create_from_map(const yuf_model_config* cfg, int precision, i
             "model: unknown precision %d", precision);
   yuf_model_config c = *cfg;
   Y_TRY(validate_cfg(&c));
-  if (precision == YUF_PRECISION_BF16_WEIGHTS && c.rosa_size % 8 != 0) {
-    set_error("model: bf16-weight mode needs rosa_size %% 8 == 0 (16-byte rows for the tensor-core "
-              "GEMM), got %d", c.rosa_size);
+  if (c.rosa_size % (precision == YUF_PRECISION_BF16_WEIGHTS ? 8 : 4) != 0) {
+    set_error("model: rosa_size %d must be a multiple of %d in this precision (16-byte rows for the "
+              "tensor-core GEMM)", c.rosa_size, precision == YUF_PRECISION_BF16_WEIGHTS ? 8 : 4);
     return YUF_ERR_UNSUPPORTED;
   }
   switch (c.head_size) {
@@ -674,25 +614,10 @@ yuf_status_t model_create_from_map(const yuf_model_config* cfg, int precision, i
   m->cfg = c;
   m->precision = precision;
   m->device = device;
-  Y_BLAS(cublasCreate(&m->blas));
-  // fp32: prefer cuBLAS's BF16x9 emulation (fp32-accurate on the tensor cores,
-  // cuBLAS >= 12.9); an older cuBLAS already loaded into the process (e.g. the
-  // one a framework ships) rejects the mode, and plain fp32 GEMMs are used.
-  m->emulated_fp32 = precision == YUF_PRECISION_FP32 &&
-                     cublasSetMathMode(m->blas, CUBLAS_FP32_EMULATED_BF16X9_MATH) == CUBLAS_STATUS_SUCCESS;
-  if (!m->emulated_fp32) Y_BLAS(cublasSetMathMode(m->blas, CUBLAS_DEFAULT_MATH));
-  m->blas_ws = std::make_unique<DevBuf>();
-  m->blas_ws->bytes = 64u << 20;
-  Y_CUDA(cudaMalloc(&m->blas_ws->p, m->blas_ws->bytes));
-  Y_BLAS(cublasSetWorkspace(m->blas, m->blas_ws->p, m->blas_ws->bytes));
   m->d_err = static_cast<int*>(m->alloc(sizeof(int)));
   if (!m->d_err) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
   Y_CUDA(cudaMemset(m->d_err, 0, sizeof(int)));
-  yuf_status_t st = load_weights(m.get(), t);
-  if (st != YUF_OK) {
-    cublasDestroy(m->blas);
-    return st;
-  }
+  Y_TRY(load_weights(m.get(), t));
   *out = m.release();
   return YUF_OK;
 }
@@ -717,7 +642,6 @@ yuf_status_t yuf_model_destroy(yuf_model* m) {
   if (!m) return YUF_OK;
   cudaSetDevice(m->device);
   m->drop_graphs();
-  if (m->blas) cublasDestroy(m->blas);
   delete m;
   return YUF_OK;
 }
@@ -1007,8 +931,8 @@ yuf_status_t yuf_debug_dump(yuf_model* m, const char* region, int layer, float* 
 // not allowed), or code living inside a process that hands it a fixed device
 // memory budget up front.  yuf_step_static serves them: its per-call working
 // memory comes from the fixed array below instead of the model's grow-on-demand
-// workspace, so a call allocates nothing (the model, its weights, its state
-// slots and the GEMM workspace were all allocated when the model was built).
+// workspace, so a call allocates nothing (the model, its weights and its state
+// slots were all allocated when the model was built).
 //
 // The array is a file-scope __device__ object: every GPU that loads this library
 // holds it (YUF_STATIC_SCRATCH_BYTES) until the process exits.  Host code cannot
