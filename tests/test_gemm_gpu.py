@@ -146,8 +146,9 @@ def test_gemm_rejects_unaligned_operands():
 
 # ---- fp32 operands at fp32 accuracy (3xTF32, yuf_gemm_tf32x3) -------------
 # Against a float64 product of the fp32 operands: the three tf32 products keep
-# about 2^-20 of each product, so the fp32 tolerance of the engine holds:
-# |got - want| <= 1e-4 sqrt(K) max|A| max|W| + 1e-5 |want|.
+# each product to about 2^-20, so |got - want| <= 4e-6 sqrt(K) max|A| max|W| +
+# 1e-5 |want| (an emulation of the scheme errs by 1e-6 .. 5e-6 absolute at
+# these shapes; dropping either low part would err by 2e-3 and fail).
 F32_TANH0, SILU_GATE_F32 = 4, 5
 
 
@@ -168,7 +169,7 @@ def gemm32(A, lda, a_brows, Wh, Wl, w_brows, C, ldc, c_bstride, M, N, K, batch, 
 
 def check32(got, want, K, scale):
     np.testing.assert_allclose(got.double().cpu().numpy(), want.double().cpu().numpy(), rtol=1e-5,
-                               atol=1e-4 * math.sqrt(K) * scale)
+                               atol=4e-6 * math.sqrt(K) * scale)
 
 
 SHAPES32 = [(4096, 640, 640, 3), (4096, 640, 2560, 1), (256, 640, 640, 3), (256, 20000, 640, 1), (256, 640, 2560, 1),

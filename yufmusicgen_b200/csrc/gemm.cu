@@ -745,9 +745,13 @@ __global__ void __launch_bounds__(GemmSplitCfg<BN>::THREADS, 1)
 // memory -- the high part (low 13 mantissa bits cleared) in place, the
 // remainder into a second tile of the same swizzled layout (the split is
 // elementwise, so no index changes) -- before the MMA warp may read the stage.
-// One output tile per cluster of `ks` CTAs splitting K (ks = 1 for many rows),
-// partials reduced through distributed shared memory as in the bf16 split-K
-// kernel.
+// The tensor core's own accumulation drops low bits once the running sum grows
+// (measured: ~1e-5 relative over K = 640 even with exact products), so each
+// 32-wide K block goes into a fresh TMEM accumulator (two, alternating) and the
+// epilogue warps add it to an fp32 register accumulator: the tensor core only
+// ever sums 96 products.  One output tile per cluster of `ks` CTAs splitting K
+// (ks = 1 for many rows), partials reduced through distributed shared memory as
+// in the bf16 split-K kernel.
 template <int BN>
 struct GemmTf32Cfg {
   static constexpr int BM = 128, BK = 32;         // BK fp32 = one 128-byte swizzle row
@@ -759,12 +763,13 @@ struct GemmTf32Cfg {
   static constexpr int PSTRIDE = BN + 4;
   static constexpr int P_BYTES = BM * PSTRIDE * 4;
   static constexpr int BODY = STAGES * STAGE > P_BYTES ? STAGES * STAGE : P_BYTES;
-  static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;   // two K-block accumulators
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = BODY + BAR_BYTES + 1024;
   static constexpr uint32_t IDESC = umma_idesc_tf32(BM, BN);
   static constexpr int THREADS = 320;  // producer, MMA, 4 epilogue warps, 4 converter warps
   static_assert(STAGE % 1024 == 0, "stages stay 1024-byte aligned for the 128-byte swizzle");
+  static_assert(BN == 64 || BN == 128, "tile width");
 };
 
 template <int BN, int EPI>
@@ -778,8 +783,10 @@ __global__ void __launch_bounds__(GemmTf32Cfg<BN>::THREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + G::BODY);
   uint64_t* conv = full + G::STAGES;
   uint64_t* empty = conv + G::STAGES;
-  uint64_t* tfull = empty + G::STAGES;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(tfull + 1);
+  uint64_t* tfull = empty + G::STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;         // [2]
+  uint64_t* drain = tempty + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -795,7 +802,11 @@ __global__ void __launch_bounds__(GemmTf32Cfg<BN>::THREADS, 1)
       mbar_init(&conv[s], 4);  // one arrival per converter warp
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tfull, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -833,25 +844,34 @@ __global__ void __launch_bounds__(GemmTf32Cfg<BN>::THREADS, 1)
         }
     }
   } else if (warp == 1) {
-    if (lane == 0 && nkb > 0) {  // MMA issuer: three tf32 products per k step
+    if (lane == 0 && nkb > 0) {  // MMA issuer: a fresh accumulator per K block
       int stage = 0;
       uint32_t phase = 0;
+      bool any = false;
       for (int i = 0; i < nkb; ++i) {
+        const int acc = i & 1;
+        if (!gemm_wait(&tempty[acc], ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_flag)) break;
         if (!gemm_wait(&conv[stage], phase, abort_flag)) break;
         tc_fence_after_sync();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
         const uint32_t ah = smem_u32(sm + stage * G::STAGE), al = ah + G::A_BYTES;
         const uint32_t bh = al + G::AL_BYTES, bl = bh + G::B_BYTES;
 #pragma unroll
         for (int kk = 0; kk < G::BK / 8; ++kk) {
           const uint32_t o = kk * 32;
-          umma_tf32(tmem, umma_desc_sw128(al + o), umma_desc_sw128(bh + o), G::IDESC, (i | kk) != 0 ? 1u : 0u);
-          umma_tf32(tmem, umma_desc_sw128(ah + o), umma_desc_sw128(bl + o), G::IDESC, 1u);
-          umma_tf32(tmem, umma_desc_sw128(ah + o), umma_desc_sw128(bh + o), G::IDESC, 1u);
+          umma_tf32(d, umma_desc_sw128(al + o), umma_desc_sw128(bh + o), G::IDESC, kk != 0 ? 1u : 0u);
+          umma_tf32(d, umma_desc_sw128(ah + o), umma_desc_sw128(bl + o), G::IDESC, 1u);
+          umma_tf32(d, umma_desc_sw128(ah + o), umma_desc_sw128(bh + o), G::IDESC, 1u);
         }
+        any = true;
         umma_commit(&empty[stage]);
+        umma_commit(&tfull[acc]);
         if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
       }
-      umma_commit(tfull);
+      if (any) {  // every MMA issued has finished before the columns are freed
+        umma_commit(drain);
+        mbar_wait(drain, 0);
+      }
     }
   } else if (warp >= 6) {  // converters: split each landed activation tile
     const int ct = threadIdx.x - 192;  // 0 .. 127
@@ -875,33 +895,64 @@ __global__ void __launch_bounds__(GemmTf32Cfg<BN>::THREADS, 1)
       if (lane == 0) mbar_arrive(&conv[stage]);
       if (++stage == G::STAGES) { stage = 0; phase ^= 1u; }
     }
-  }
-  // epilogue warps 2-5: the tile (ks = 1) or this CTA's partial of it
-  const bool epi_warp = warp >= 2 && warp < 6;
-  if (epi_warp) {
+  } else {  // epilogue warps 2-5: sum the K-block accumulators in fp32 registers
     const int q = warp & 3;
-    bool ok = nkb == 0 || mbar_wait(tfull, 0);
-    ok = __all_sync(0xffffffffu, ok);
-    if (!ok) *abort_flag = 1;
-    if (ok && nkb > 0) tc_fence_after_sync();
-    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
     const int prow = q * 32 + lane;
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    float racc[BN];
+#pragma unroll
+    for (int c = 0; c < BN; ++c) racc[c] = 0.f;
+    bool ok = true;
+    for (int i = 0; i < nkb && ok; ++i) {
+      const int acc = i & 1;
+      ok = gemm_wait(&tfull[acc], (uint32_t)(i >> 1) & 1u, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after_sync();
+#pragma unroll
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld_x32(tbase + (uint32_t)(acc * BN + c0), v);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) racc[c0 + c] += v[c];
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (!ok) *abort_flag = 1;
+    const int row = mt * G::BM + prow;
     if (ks == 1) {
-      if (ok && nkb > 0) gemm_epilogue_tile<BN, EPI>(p, tbase, z, mt * G::BM + prow, nt, mt * G::BM + prow < p.M);
+      if (ok && row < p.M) {
+        if constexpr (EPI == GEMM_EPI_SWIGLU_F32) {
+          float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+#pragma unroll
+          for (int sb = 0; sb < BN / 128; ++sb)
+#pragma unroll
+            for (int j = 0; j < 64; j += 4) {
+              const int col = nt * (BN / 2) + sb * 64 + j;
+              float h[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) h[e] = silu(racc[sb * 128 + j + e]) * racc[sb * 128 + 64 + j + e];
+              if (p.vec && col + 4 <= p.n_out) *reinterpret_cast<float4*>(out + col) = make_float4(h[0], h[1], h[2], h[3]);
+              else
+                for (int e = 0; e < 4; ++e)
+                  if (col + e < p.n_out) out[col + e] = h[e];
+            }
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN; c += 4) {
+            const int col = nt * BN + c;
+            if (col < p.N) store4<GEMM_EPI_F32>(p, z, row, col, make_float4(racc[c], racc[c + 1], racc[c + 2], racc[c + 3]));
+          }
+        }
+      }
     } else {
       float* dst = part + (size_t)prow * G::PSTRIDE;
-      if (ok && nkb > 0) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          float v[32];
-          tmem_ld_x32(tbase + c0, v);
 #pragma unroll
-          for (int c = 0; c < 32; c += 4)
-            *reinterpret_cast<float4*>(dst + c0 + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
-        }
-      } else {
-        for (int c = 0; c < BN; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+      for (int c = 0; c < BN; c += 4)
+        *reinterpret_cast<float4*>(dst + c) =
+            ok ? make_float4(racc[c], racc[c + 1], racc[c + 2], racc[c + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
   tc_fence_before_sync();
