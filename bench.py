@@ -47,7 +47,8 @@ fallback (a Python loop of einsums per token), so they are stronger baselines.
 ``--only headline`` runs just the config-2 steps (the command the profiles'
 ncu captures use); ``--only model`` just one rank's config-3 prefill and
 config-4 decode step timings (fp32 and bf16 weights); ``--only prefill`` /
-``--only decode`` just the bf16-weight config-3 prefill / config-4 decode step.
+``--only decode`` just the bf16-weight config-3 prefill / config-4 decode step;
+``--only c5`` one rank's config-5 prefill (8 sequences of 8192 tokens).
 """
 
 from __future__ import annotations
@@ -79,7 +80,7 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--only", choices=["all", "headline", "model", "prefill", "decode"], default="all")
+    p.add_argument("--only", choices=["all", "headline", "model", "prefill", "decode", "c5"], default="all")
     return p.parse_args()
 
 
@@ -436,6 +437,28 @@ def measure_sharded(dev, rank, world, barrier, max_over_ranks):
             del eng
     del w
     # config 5: this rank's 8 of the 64 sequences
+    ms = measure_c5(dev, 2, rank, timed)
+    tokens = world * C5_SEQS_PER_GPU * C5_T
+    flop = 915e6 * tokens  # about 2 x linear parameters + LM head per token
+    tflops = flop / world / (ms * 1e-3) / 1e12
+    res["prefill_c5_bf16"] = {"ms": ms, "tokens_per_s": tokens / (ms * 1e-3),
+                              "sequences": world * C5_SEQS_PER_GPU, "seq_len": C5_T,
+                              "TFLOPs_per_gpu": tflops,
+                              "tensor_frac_per_gpu": tflops / bf16_peak()}
+    return res
+
+
+def measure_c5(dev, reps, rank=0, timed=None):
+    """Config 5 on one rank: 8 sequences of T = 8192 through the 24-layer d1024
+    model (bf16 weights, fp32 state); ms per prefill (max over ranks when
+    `timed` is the sharded timer)."""
+    import torch
+
+    from yufmusicgen_b200 import config as C
+    from yufmusicgen_b200.engine import Engine
+    from yufmusicgen_b200.weights import init_weights
+    from yufmusicgen_b200.workloads import zipf_ids
+
     cfg = C.ModelConfig(**C.LONG_1K)
     w = init_weights(cfg, 2, "baseline")
     ids = torch.as_tensor(zipf_ids(C5_SEQS_PER_GPU, C5_T, seed=100 + rank, vocab=cfg.vocab_size),
@@ -448,17 +471,15 @@ def measure_sharded(dev, rank, world, barrier, max_over_ranks):
         eng.reset_state(0, C5_SEQS_PER_GPU)
         eng.prefill(ids, slot0=0, out_last=last)
 
-    ms = timed(pf, 2, torch.cuda.current_stream(dev))
+    stream = torch.cuda.current_stream(dev)
+    if timed is None:
+        ms = _time(pf, reps, dev, stream, warm=1)
+        out = {"ms": ms, "tokens_per_s": C5_SEQS_PER_GPU * C5_T / (ms * 1e-3)}
+    else:
+        out = timed(pf, reps, stream)
     eng.close()
     del eng
-    tokens = world * C5_SEQS_PER_GPU * C5_T
-    flop = 915e6 * tokens  # about 2 x linear parameters + LM head per token
-    tflops = flop / world / (ms * 1e-3) / 1e12
-    res["prefill_c5_bf16"] = {"ms": ms, "tokens_per_s": tokens / (ms * 1e-3),
-                              "sequences": world * C5_SEQS_PER_GPU, "seq_len": C5_T,
-                              "TFLOPs_per_gpu": tflops,
-                              "tensor_frac_per_gpu": tflops / bf16_peak()}
-    return res
+    return out
 
 
 def headline_keys(sh, world):
@@ -583,6 +604,9 @@ def run_ours(args):
     def step():
         cuda_ops.wkv7_forward(d["r"], d["w"], d["k"], d["v"], d["a"], d["b"], None, out=y, state_out=s)
 
+    if args.only == "c5":
+        print(json.dumps({"only": "c5", "c5": measure_c5(dev, 1)}), flush=True)
+        return
     if args.only in ("model", "prefill", "decode"):
         parts = ("prefill", "decode") if args.only == "model" else (args.only,)
         precs = ("fp32", "bf16") if args.only == "model" else ("bf16",)
