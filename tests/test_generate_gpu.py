@@ -139,5 +139,5 @@ def test_sampled_decode_with_the_references_stream(golden):
     eng = Engine(cfg, init_weights(cfg, 1, "baseline"), n_slots=1)
     toks = eng.generate_reference_stream(g["decode.prompt"], len(g["decode.tokens"]), temperature=1.0,
                                          top_p=0.95, seed=1337)
-    np.testing.assert_array_equal(toks[:safe + 1], g["decode.tokens"][:safe + 1])
+    np.testing.assert_array_equal(toks[:safe], g["decode.tokens"][:safe])
     eng.close()
