@@ -4,15 +4,16 @@
 // Forward of one block (yufmusicgen/model.py:365-378), rows = tokens:
 //   xt  = LN_time(x)                                   layernorm_kernel
 //   6 token-shift mixes of xt (prev = state)           mix_kernel
-//   r,k,v = x_{r,k,v} W^T                              one strided-batched GEMM
-//   lr1 = x_{w,a,g} L1 ; tanh on the w part ; lr2 = lr1 L2   two batched GEMMs
+//   r,k,v = x_{r,k,v} W^T                              one batched GEMM
+//   lr1 = x_{w,a,g} L1 (tanh on the w part in the epilogue) ; lr2 = lr1 L2   two batched GEMMs
 //   w_raw, k_adj, a_op, b_op, g                        timemix_post_kernel
 //   y, S  = WKV-7 scan (state slot in/out)             wkv7 kernels
-//   x    += W_o (LN_out(y) * g)                        layernorm(+gate) + GEMM (beta = 1)
+//   x    += W_o (LN_out(y) * g)                        layernorm(+gate) + GEMM accumulating into x
 //   [cand|write|gate] = LN_rosa(x) W^T                 one GEMM ([3R, d] weight)
 //   read, m = ROSA scan (+ bias, gated, state slot)    rosa scan kernel
-//   x    += read W_out^T                               GEMM (beta = 1)
-//   x    += W_out(silu(x_f W_in^T) * (x_f W_g^T))      GEMM [8d, d], silu_mul, GEMM (beta = 1)
+//   x    += read W_out^T                               GEMM accumulating into x
+//   x    += W_out(silu(x_f W_in^T) * (x_f W_g^T))      GEMM [8d, d] with a SiLU-gate epilogue,
+//                                                      GEMM accumulating into x
 // then logits = LN_final(x) E^T (tied head, model.py:389-391, 421).
 //
 // Every projection is the library's tcgen05 GEMM (gemm.cu), with the work
