@@ -29,6 +29,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <map>
 #include <mutex>
 
 #include "common.cuh"
@@ -984,6 +985,23 @@ static int sm_count() {
   return cache[dev];
 }
 
+// The dynamic shared-memory limit of a kernel, set once per (kernel, device);
+// must precede occupancy queries as well as launches.
+static cudaError_t set_smem_once(const void* fn, int smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, cudaError_t> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(fn, dev);
+  auto it = done.find(key);
+  if (it != done.end()) return it->second;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) cudaGetLastError();
+  done[key] = e;
+  return e;
+}
+
 static bool make_bf16_map(CUtensorMap* m, const void* base, long long inner, long long rows,
                           long long ld, int box_rows) {
   auto enc = tensor_map_encoder();
@@ -1000,17 +1018,9 @@ static bool make_bf16_map(CUtensorMap* m, const void* base, long long inner, lon
 template <int BN, int EPI>
 static yuf_status_t launch_gemm(const GemmArgs& g, GemmParams p, cudaStream_t s) {
   using G = GemmCfg<BN>;
-  static std::once_flag attr_once[128];
-  static cudaError_t attr_err[128];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  dev &= 127;
-  std::call_once(attr_once[dev], [&] {
-    attr_err[dev] = cudaFuncSetAttribute(gemm_bf16_kernel<BN, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
-  });
-  if (attr_err[dev] != cudaSuccess) {
-    set_error("gemm: cannot set %d bytes of shared memory: %s", G::SMEM, cudaGetErrorString(attr_err[dev]));
+  const cudaError_t attr_err = set_smem_once((const void*)gemm_bf16_kernel<BN, EPI>, G::SMEM);
+  if (attr_err != cudaSuccess) {
+    set_error("gemm: cannot set %d bytes of shared memory: %s", G::SMEM, cudaGetErrorString(attr_err));
     return YUF_ERR_CUDA;
   }
   CUtensorMap ta, tw;
@@ -1048,6 +1058,7 @@ static int pair_slots(const void* fn, int smem) {
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int n = 0;
+    set_smem_once(fn, smem);
     if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess || n <= 0) {
       cudaGetLastError();
       n = sm_count() / 2;
@@ -1060,17 +1071,9 @@ static int pair_slots(const void* fn, int smem) {
 template <int EPI>
 static yuf_status_t launch_gemm_pair(const GemmArgs& g, GemmParams p, cudaStream_t s) {
   using G = GemmPairCfg;
-  static std::once_flag attr_once[128];
-  static cudaError_t attr_err[128];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  dev &= 127;
-  std::call_once(attr_once[dev], [&] {
-    attr_err[dev] = cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         G::SMEM);
-  });
-  if (attr_err[dev] != cudaSuccess) {
-    set_error("gemm: cannot set %d bytes of shared memory: %s", G::SMEM, cudaGetErrorString(attr_err[dev]));
+  const cudaError_t attr_err = set_smem_once((const void*)gemm_bf16_pair_kernel<EPI>, G::SMEM);
+  if (attr_err != cudaSuccess) {
+    set_error("gemm: cannot set %d bytes of shared memory: %s", G::SMEM, cudaGetErrorString(attr_err));
     return YUF_ERR_CUDA;
   }
   CUtensorMap ta, tw;
@@ -1108,6 +1111,7 @@ static int splitk_slots(int ks) {
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int n = 0;
+    set_smem_once((const void*)gemm_bf16_splitk_kernel<BN, EPI>, GemmSplitCfg<BN>::SMEM);
     if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_splitk_kernel<BN, EPI>, &cfg) != cudaSuccess || n <= 0) {
       cudaGetLastError();
       n = sm_count() / (2 * ks);
@@ -1120,20 +1124,9 @@ static int splitk_slots(int ks) {
 template <int BN, int EPI>
 static yuf_status_t launch_gemm_splitk(const GemmArgs& g, GemmParams p, int ks, cudaStream_t s) {
   using G = GemmSplitCfg<BN>;
-  static std::once_flag attr_once[128];
-  static cudaError_t attr_err[128];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  dev &= 127;
-  std::call_once(attr_once[dev], [&] {
-    attr_err[dev] = cudaFuncSetAttribute(gemm_bf16_splitk_kernel<BN, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
-    if (attr_err[dev] == cudaSuccess)
-      attr_err[dev] = cudaFuncSetAttribute(gemm_bf16_splitk_kernel<BN, EPI>,
-                                           cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  });
-  if (attr_err[dev] != cudaSuccess) {
-    set_error("gemm: kernel attributes: %s", cudaGetErrorString(attr_err[dev]));
+  const cudaError_t attr_err = set_smem_once((const void*)gemm_bf16_splitk_kernel<BN, EPI>, G::SMEM);
+  if (attr_err != cudaSuccess) {
+    set_error("gemm: cannot set %d bytes of shared memory: %s", G::SMEM, cudaGetErrorString(attr_err));
     return YUF_ERR_CUDA;
   }
   CUtensorMap ta, tw;
@@ -1305,6 +1298,7 @@ static int tf32_slots(int ks) {
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int n = 0;
+    set_smem_once((const void*)gemm_tf32x3_kernel<BN, EPI>, GemmTf32Cfg<BN>::SMEM);
     if (cudaOccupancyMaxActiveClusters(&n, gemm_tf32x3_kernel<BN, EPI>, &cfg) != cudaSuccess || n <= 0) {
       cudaGetLastError();
       n = sm_count() / (2 * ks);
@@ -1317,17 +1311,9 @@ static int tf32_slots(int ks) {
 template <int BN, int EPI>
 static yuf_status_t launch_tf32(const GemmArgs& g, const void* W_lo, GemmParams p, int ks, cudaStream_t s) {
   using G = GemmTf32Cfg<BN>;
-  static std::once_flag attr_once[128];
-  static cudaError_t attr_err[128];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  dev &= 127;
-  std::call_once(attr_once[dev], [&] {
-    attr_err[dev] = cudaFuncSetAttribute(gemm_tf32x3_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         G::SMEM);
-  });
-  if (attr_err[dev] != cudaSuccess) {
-    set_error("gemm: kernel attributes: %s", cudaGetErrorString(attr_err[dev]));
+  const cudaError_t attr_err = set_smem_once((const void*)gemm_tf32x3_kernel<BN, EPI>, G::SMEM);
+  if (attr_err != cudaSuccess) {
+    set_error("gemm: cannot set %d bytes of shared memory: %s", G::SMEM, cudaGetErrorString(attr_err));
     return YUF_ERR_CUDA;
   }
   CUtensorMap ta, twh, twl;
