@@ -84,9 +84,13 @@ enum {
   YUF_WKV_PARALLEL = 3,   /* chunks scanned in parallel (about one wave of blocks), states
                              carried between them; takes stream-ordered scratch for the chunk
                              transitions from a library-owned pool that keeps its pages; T >= 256 */
-  YUF_WKV_PARALLEL_TC = 4 /* YUF_WKV_PARALLEL with the output correction y += S0 q_t on the
+  YUF_WKV_PARALLEL_TC = 4, /* YUF_WKV_PARALLEL with the output correction y += S0 q_t on the
                              tcgen05 tensor cores (TMEM accumulators, 3xTF32) for N <= 64;
                              today slower than the default mma.sync correction            */
+  YUF_WKV_ROWS = 5         /* token by token, one CTA per (sequence, head) with the state rows
+                             split over warps (4 lanes per row, decay-scaled state inside
+                             8-token groups staged by a producer warp with TMA); reads the
+                             inputs and writes y once                                     */
 };
 /* yuf_wkv7_forward with an explicit algorithm (same results to fp32 rounding). */
 yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k, const float* v,

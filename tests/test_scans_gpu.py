@@ -34,7 +34,7 @@ def close(got, want, rtol=RTOL, atol=ATOL):
 WKV_CASES = ["n40_state", "n32_zero", "n64_state", "n16_state", "n40_t1"]
 
 
-ALGOS = [cuda_ops.ALGO_SEQUENTIAL, cuda_ops.ALGO_CHUNKED]
+ALGOS = [cuda_ops.ALGO_SEQUENTIAL, cuda_ops.ALGO_CHUNKED, cuda_ops.ALGO_ROWS]
 
 
 @pytest.mark.parametrize("algo", ALGOS)
