@@ -44,19 +44,23 @@ struct RowsCfg {
   static constexpr int NWS = N / (8 * R);              // scan warps
   static constexpr int NT = 32 * (NWS + 1);            // + the producer warp
   static constexpr int TS = 8;                         // tokens per staged group
-  static constexpr int NB = 4;                         // ring slots
+  static constexpr int NR = N >= 96 ? 3 : (N >= 64 ? 4 : 6);  // raw slots: groups loaded ahead
+  static constexpr int NB = 4;                         // scaled slots
   static constexpr int CS = conflict_free_stride(C, G);
   static constexpr int VP = G * CS;                    // padded vector length
-  // slot layout (floats): raw [6][TS][N] (TMA), scaled a', b', k', r' [4][TS][VP], gamma_end [VP]
-  static constexpr int RAW = 0;
-  static constexpr int SCALED = RAW + 6 * TS * N;
-  static constexpr int GEND = SCALED + 4 * TS * VP;
-  static constexpr int SLOT = (GEND + VP + 31) / 32 * 32;  // 128-byte multiple
-  static constexpr int BAR = NB * SLOT;                     // 3 x NB mbarriers
-  static constexpr size_t BYTES = (size_t)BAR * 4 + 3 * NB * 8 + 128;
+  // raw slot (floats): [6][TS][N], the TMA destination
+  static constexpr int RAW_SLOT = 6 * TS * N;
+  // scaled slot (floats): a', b', k', r' [4][TS][VP], v [TS][N], gamma_end [VP]
+  static constexpr int SV = 4 * TS * VP;
+  static constexpr int SGEND = SV + TS * N;
+  static constexpr int SC_SLOT = (SGEND + VP + 31) / 32 * 32;  // 128-byte multiple
+  static constexpr int SCALED = NR * RAW_SLOT;
+  static constexpr int BAR = SCALED + NB * SC_SLOT;            // NR + 2 NB mbarriers
+  static constexpr size_t BYTES = (size_t)BAR * 4 + (NR + 2 * NB) * 8 + 128;
   static constexpr uint32_t TX = 6u * TS * N * 4;
   static_assert(N % 8 == 0 && C % 2 == 0 && NWS * 8 * R == N, "rows kernel: N in {16, 32, 40, 48, 64, 96, 128}");
   static_assert((TS * N * 4) % 128 == 0, "TMA boxes land on 128-byte boundaries");
+  static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
 struct RowsTmaps {
@@ -68,12 +72,12 @@ __global__ void __launch_bounds__(RowsCfg<N>::NT, 1)
     wkv7_rows_kernel(const float* __restrict__ s0, float* __restrict__ y, float* __restrict__ s_out, int T,
                      int H, const __grid_constant__ RowsTmaps tm) {
   using K = RowsCfg<N>;
-  constexpr int C = K::C, C2 = K::C2, R = K::R, TS = K::TS, NB = K::NB, CS = K::CS, VP = K::VP;
+  constexpr int C = K::C, C2 = K::C2, R = K::R, TS = K::TS, NB = K::NB, NR = K::NR, CS = K::CS, VP = K::VP;
   extern __shared__ __align__(128) float rows_smem[];
   float* sm = rows_smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + K::BAR);
-  uint64_t* ready = full + NB;
-  uint64_t* empty = ready + NB;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + K::BAR);  // [NR] raw boxes landed
+  uint64_t* ready = full + NR;                                // [NB] scaled slot filled
+  uint64_t* empty = ready + NB;                               // [NB] scaled slot consumed
   __shared__ int abort_flag;
 
   const int bh = blockIdx.x;
@@ -81,8 +85,8 @@ __global__ void __launch_bounds__(RowsCfg<N>::NT, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ngroups = (T + TS - 1) / TS;
   if (threadIdx.x == 0) {
+    for (int s = 0; s < NR; ++s) mbar_init(&full[s], 1);
     for (int s = 0; s < NB; ++s) {
-      mbar_init(&full[s], 1);
       mbar_init(&ready[s], 1);
       mbar_init(&empty[s], K::NWS);
     }
@@ -90,55 +94,71 @@ __global__ void __launch_bounds__(RowsCfg<N>::NT, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == K::NWS) {  // ------------------------------------------------- producer
     const int tx = hh * N, ty = bb * T;
-    for (int gi = 0; gi < ngroups; ++gi) {
-      const int slot = gi % NB;
-      const uint32_t ph = (uint32_t)(gi / NB) & 1u;
-      bool ok = mbar_wait(&empty[slot], ph ^ 1u);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok || *(volatile int*)&abort_flag) { abort_flag = 1; break; }
-      float* S = sm + slot * K::SLOT;
-      if (lane == 0) {
-        fence_proxy_async();  // the slot's previous contents were read through the generic proxy
-        mbar_expect_tx(&full[slot], K::TX);
+    auto issue = [&](int gi) {  // lane 0: the six boxes of group gi into raw slot gi % NR
+      float* Rw = sm + (gi % NR) * K::RAW_SLOT;
+      uint64_t* bar = &full[gi % NR];
+      mbar_expect_tx(bar, K::TX);
 #pragma unroll
-        for (int arr = 0; arr < 6; ++arr) tma_load_2d(S + K::RAW + arr * TS * N, &tm.m[arr], &full[slot], tx, ty + gi * TS);
-      }
-      ok = __all_sync(0xffffffffu, mbar_wait(&full[slot], ph));
-      if (!ok) {
-        if (lane == 0) mbar_wait(&full[slot], ph);  // let the boxes land before leaving
-        abort_flag = 1;
-        break;
-      }
-      // scaled vectors, a lane per column pair, gamma running over the group
+      for (int arr = 0; arr < 6; ++arr) tma_load_2d(Rw + arr * TS * N, &tm.m[arr], bar, tx, ty + gi * TS);
+    };
+    int issued = 0;
+    if (lane == 0)
+      for (; issued < min(NR, ngroups); ++issued) issue(issued);
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+    for (int gi = 0; gi < ngroups; ++gi) {
+      const int rs = gi % NR, ss = gi % NB;
+      bool ok = mbar_wait(&full[rs], (uint32_t)(gi / NR) & 1u) && mbar_wait(&empty[ss], ((uint32_t)(gi / NB) & 1u) ^ 1u);
+      ok = __all_sync(0xffffffffu, ok) && !*(volatile int*)&abort_flag;
+      if (!ok) { abort_flag = 1; break; }
+      const float* Rw = sm + rs * K::RAW_SLOT;
+      float* Sc = sm + K::SCALED + ss * K::SC_SLOT;
       const int Tc = min(TS, T - gi * TS);
+      // scaled vectors, a lane per column pair, gamma running over the group; v copied
       for (int jp = lane; jp < N / 2; jp += 32) {
         const int j = 2 * jp;
         const int pj = (j / C) * CS + (j % C);
         float2 gam = make_float2(1.f, 1.f), ginv = gam;
         for (int t = 0; t < Tc; ++t) {
           const int rj = t * N + j;
-          const float2 wr = *reinterpret_cast<const float2*>(S + K::RAW + 1 * TS * N + rj);
+          const float2 wr = *reinterpret_cast<const float2*>(Rw + 1 * TS * N + rj);
           const float sx = W_SCALE * sigmoidf_fast(wr.x), sy = W_SCALE * sigmoidf_fast(wr.y);
-          const float2 av = *reinterpret_cast<const float2*>(S + K::RAW + 4 * TS * N + rj);
-          const float2 bv = *reinterpret_cast<const float2*>(S + K::RAW + 5 * TS * N + rj);
-          const float2 kv = *reinterpret_cast<const float2*>(S + K::RAW + 2 * TS * N + rj);
-          const float2 rv = *reinterpret_cast<const float2*>(S + K::RAW + 0 * TS * N + rj);
-          float* d = S + K::SCALED + t * VP + pj;
+          const float2 av = *reinterpret_cast<const float2*>(Rw + 4 * TS * N + rj);
+          const float2 bv = *reinterpret_cast<const float2*>(Rw + 5 * TS * N + rj);
+          const float2 kv = *reinterpret_cast<const float2*>(Rw + 2 * TS * N + rj);
+          const float2 rv = *reinterpret_cast<const float2*>(Rw + 0 * TS * N + rj);
+          float* d = Sc + t * VP + pj;
           *reinterpret_cast<float2*>(d + 0 * TS * VP) = fmul2(av, gam);  // gamma_{t-1} a_t
           gam = fmul2(gam, make_float2(__expf(sx), __expf(sy)));
           ginv = fmul2(ginv, make_float2(__expf(-sx), __expf(-sy)));
           *reinterpret_cast<float2*>(d + 1 * TS * VP) = fmul2(bv, ginv);  // b_t / gamma_t
           *reinterpret_cast<float2*>(d + 2 * TS * VP) = fmul2(kv, ginv);  // k_t / gamma_t
           *reinterpret_cast<float2*>(d + 3 * TS * VP) = fmul2(rv, gam);   // gamma_t r_t
+          *reinterpret_cast<float2*>(Sc + K::SV + rj) = *reinterpret_cast<const float2*>(Rw + 3 * TS * N + rj);
         }
-        *reinterpret_cast<float2*>(S + K::GEND + pj) = gam;
+        *reinterpret_cast<float2*>(Sc + K::SGEND + pj) = gam;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ready[slot]);
+      if (lane == 0) {
+        mbar_arrive(&ready[ss]);
+        if (issued < ngroups) {  // the raw slot is free again: load the group NR ahead into it
+          fence_proxy_async();
+          issue(issued);
+        }
+      }
+      issued = min(issued + 1, max(issued, ngroups));
+      issued = __shfl_sync(0xffffffffu, issued, 0);
     }
+    if (lane == 0 && *(volatile int*)&abort_flag)  // let boxes still in flight land before leaving
+      for (int g2 = 0; g2 < NR; ++g2) {
+        const int gl = issued - 1 - g2;  // the last NR groups issued
+        if (gl < 0) break;
+        mbar_wait(&full[gl % NR], (uint32_t)(gl / NR) & 1u);
+      }
   } else {  // ---------------------------------------------------------- scan warps
     const int rg = lane >> 2, g = lane & 3;
     const int i0 = (warp * 8 + rg) * R, j0 = g * C;
@@ -153,16 +173,15 @@ __global__ void __launch_bounds__(RowsCfg<N>::NT, 1)
     const size_t tok_stride = (size_t)H * N;
     float* ybase = y + ((size_t)bb * T * H + hh) * N + i0;
     for (int gi = 0; gi < ngroups; ++gi) {
-      const int slot = gi % NB;
-      const uint32_t ph = (uint32_t)(gi / NB) & 1u;
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&ready[slot], ph));
+      const int ss = gi % NB;
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&ready[ss], (uint32_t)(gi / NB) & 1u));
       if (!ok || *(volatile int*)&abort_flag) { abort_flag = 1; break; }
-      const float* S = sm + slot * K::SLOT;
-      const float* Pa = S + K::SCALED + 0 * TS * VP + g * CS;
-      const float* Pb = S + K::SCALED + 1 * TS * VP + g * CS;
-      const float* Pk = S + K::SCALED + 2 * TS * VP + g * CS;
-      const float* Pr = S + K::SCALED + 3 * TS * VP + g * CS;
-      const float* Pv = S + K::RAW + 3 * TS * N + i0;
+      const float* Sc = sm + K::SCALED + ss * K::SC_SLOT;
+      const float* Pa = Sc + 0 * TS * VP + g * CS;
+      const float* Pb = Sc + 1 * TS * VP + g * CS;
+      const float* Pk = Sc + 2 * TS * VP + g * CS;
+      const float* Pr = Sc + 3 * TS * VP + g * CS;
+      const float* Pv = Sc + K::SV + i0;
       const int Tc = min(TS, T - gi * TS);
       // sa of the group's first token (the state enters the group unscaled)
       float sa[R];
@@ -239,16 +258,16 @@ __global__ void __launch_bounds__(RowsCfg<N>::NT, 1)
       {
         float2 ge[C2];
 #pragma unroll
-        for (int c = 0; c < C2; ++c) ge[c] = *reinterpret_cast<const float2*>(S + K::GEND + g * CS + 2 * c);
+        for (int c = 0; c < C2; ++c) ge[c] = *reinterpret_cast<const float2*>(Sc + K::SGEND + g * CS + 2 * c);
 #pragma unroll
         for (int p = 0; p < R; ++p)
 #pragma unroll
           for (int c = 0; c < C2; ++c) Sx[p][c] = fmul2(Sx[p][c], ge[c]);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (lane == 0) mbar_arrive(&empty[ss]);
     }
-    if (s_out && !abort_flag) {
+    if (s_out && !*(volatile int*)&abort_flag) {
 #pragma unroll
       for (int p = 0; p < R; ++p)
 #pragma unroll
