@@ -87,10 +87,15 @@ enum {
   YUF_WKV_PARALLEL_TC = 4, /* YUF_WKV_PARALLEL with the output correction y += S0 q_t on the
                              tcgen05 tensor cores (TMEM accumulators, 3xTF32) for N <= 64;
                              today slower than the default mma.sync correction            */
-  YUF_WKV_ROWS = 5         /* token by token, one CTA per (sequence, head) with the state rows
+  YUF_WKV_ROWS = 5,        /* token by token, one CTA per (sequence, head) with the state rows
                              split over warps (4 lanes per row, decay-scaled state inside
                              8-token groups staged by a producer warp with TMA); reads the
                              inputs and writes y once                                     */
+  YUF_WKV_CHUNKED_TC = 6   /* 16-token chunks, one CTA per (sequence, head), the state in
+                             tensor-core accumulators: per chunk the state products
+                             (W S^T, Q S^T, SA^T B~ + V^T K~) on mma.sync 3xTF32, the
+                             chunk-local Gram matrices and substitution on the FMA pipe by
+                             prep warps, inputs staged by TMA; N in {16, 32, 40, 48, 64}  */
 };
 /* yuf_wkv7_forward with an explicit algorithm (same results to fp32 rounding). */
 yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k, const float* v,

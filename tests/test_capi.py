@@ -129,6 +129,7 @@ def test_python_algorithm_constants_match_the_header():
 
     text = HEADER.read_text()
     enum = dict((m.group(1), int(m.group(2))) for m in re.finditer(r"YUF_WKV_([A-Z_]+) = (\d+)", text))
-    assert enum == {"AUTO": 0, "SEQUENTIAL": 1, "CHUNKED": 2, "PARALLEL": 3, "PARALLEL_TC": 4, "ROWS": 5}
+    assert enum == {"AUTO": 0, "SEQUENTIAL": 1, "CHUNKED": 2, "PARALLEL": 3, "PARALLEL_TC": 4, "ROWS": 5,
+                    "CHUNKED_TC": 6}
     for name, value in enum.items():
         assert getattr(cuda_ops, f"ALGO_{name}") == value

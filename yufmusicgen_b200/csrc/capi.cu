@@ -72,6 +72,11 @@ unsigned int wkv7_pair_wait_timeouts();
 unsigned int wkv7_decode_wait_timeouts();
 unsigned int gemm_wait_timeouts();
 unsigned int wkv7_rows_wait_timeouts();
+unsigned int wkv7_chunk_tc_wait_timeouts();
+bool wkv7_chunk_tc_supports(int N);
+yuf_status_t wkv7_chunk_tc(const float* r, const float* w, const float* k, const float* v, const float* a,
+                           const float* b, const float* s0, float* y, float* s_out, int B, int T, int H, int N,
+                           cudaStream_t st);
 yuf_status_t wkv7_rows(const float* r, const float* w, const float* k, const float* v, const float* a,
                        const float* b, const float* s0, float* y, float* s_out, int B, int T, int H, int N,
                        cudaStream_t st);
@@ -136,8 +141,9 @@ extern "C" {
 
 unsigned int yuf_wait_timeouts(void) {
   const unsigned int p = yuf::wkv7_pair_wait_timeouts(), d = yuf::wkv7_decode_wait_timeouts(),
-                     g = yuf::gemm_wait_timeouts(), r = yuf::wkv7_rows_wait_timeouts();
-  return (p == ~0u || d == ~0u || g == ~0u || r == ~0u) ? ~0u : p + d + g + r;
+                     g = yuf::gemm_wait_timeouts(), r = yuf::wkv7_rows_wait_timeouts(),
+                     c = yuf::wkv7_chunk_tc_wait_timeouts();
+  return (p == ~0u || d == ~0u || g == ~0u || r == ~0u || c == ~0u) ? ~0u : p + d + g + r + c;
 }
 
 yuf_status_t yuf_sync_check(void* stream) {
@@ -191,7 +197,7 @@ yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k,
   yuf_status_t st = check_wkv_args(in, 7, B, T, H, N);
   if (st != YUF_OK) return st;
   REQUIRE(aligned(s0, 8) && aligned(s_out, 8), "wkv7: state buffers must be 8-byte aligned");
-  REQUIRE(algo >= YUF_WKV_AUTO && algo <= YUF_WKV_ROWS, "wkv7: unknown algorithm %d", algo);
+  REQUIRE(algo >= YUF_WKV_AUTO && algo <= YUF_WKV_CHUNKED_TC, "wkv7: unknown algorithm %d", algo);
   REQUIRE((algo != YUF_WKV_PARALLEL && algo != YUF_WKV_PARALLEL_TC) || T >= 256,
           "wkv7: the time-parallel scan needs T >= 256 (T=%d)", T);
   if (B == 0 || H == 0) return YUF_OK;
@@ -200,6 +206,7 @@ yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k,
     return wkv7_decode_dispatch(r, w, k, v, a, b, s0, y, s_out, B * H, N, st_);
   if (algo == YUF_WKV_CHUNKED) return wkv7_chunk_dispatch(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, st_);
   if (algo == YUF_WKV_ROWS) return wkv7_rows(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, st_);
+  if (algo == YUF_WKV_CHUNKED_TC) return wkv7_chunk_tc(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, st_);
   if (algo == YUF_WKV_PARALLEL || algo == YUF_WKV_PARALLEL_TC ||
       (algo == YUF_WKV_AUTO && wkv7_parallel_applies(B, T, H, N))) {
     // stream-ordered scratch for the chunk transitions, released right after use

@@ -1,0 +1,674 @@
+// Chunked WKV-7 prefill with the state contractions on the tensor cores (sm_100a).
+//
+// One CTA per (sequence, head) walks the sequence in chunks of L = 16 tokens;
+// the N x N state stays in mma accumulator registers for the whole sequence.
+// Per token the recurrence is (yufmusicgen/model.py:145-165, rwkv7_clampw.cu)
+//   sa = S a,   S <- S diag(d) + sa b^T + v k^T,   y = S r,   d = exp(W_SCALE sigmoid(w)).
+// Per chunk, with gamma_t = d_0 ... d_t (per column, gamma_{-1} = 1) and the
+// scaled vectors
+//   a~_t = gamma_{t-1} a_t,  b~_t = b_t / gamma_t,  k~_t = k_t / gamma_t,  r~_t = gamma_t r_t,
+// the column-scaled state S'_t = S_t diag(1 / gamma_t) obeys
+//   S'_t = S'_{t-1} + sa_t b~_t^T + v_t k~_t^T,   sa_t = S'_{t-1} a~_t,   y_t = S'_t r~_t
+// (S'_{-1} = S, the chunk's start state).  With the chunk's Gram matrices
+//   Lab[t][s] = a~_t . b~_s,  Lak[t][s] = a~_t . k~_s   (s < t),
+//   Mrb[t][s] = r~_t . b~_s,  Mrk[t][s] = r~_t . k~_s   (s <= t),
+// forward substitution over t gives sa_t = S w_t + u_t with
+//   w_t = a~_t + sum_{s<t} Lab[t][s] w_s,      u_t = sum_{s<t} Lab[t][s] u_s + Lak[t][s] v_s,
+// and then
+//   y_t = S q_t + yu_t,   q_t = r~_t + sum_{s<=t} Mrb[t][s] w_s,
+//                         yu_t = sum_{s<=t} Mrb[t][s] u_s + Mrk[t][s] v_s,
+//   S_next = (S + sum_t sa_t b~_t^T + v_t k~_t^T) diag(gamma_15).
+// Only the three products with S depend on the previous chunk:
+//   SA^T = W S^T + U,   Y^T = Q S^T + YU   ([16 x N] x [N x N]),
+//   dS = SA^T^T B~ + V^T K~                 ([N x 16] x [16 x N]),
+// and they run on the tensor cores (mma.sync m16n8k8 tf32, 3xTF32: each fp32
+// operand split into a tf32 high part and the remainder, three products, fp32
+// accumulation -- fp32-class accuracy).  The retention bound d >= 0.545 keeps
+// 1 / gamma below 0.545^-16 ~ 1.6e4 inside a chunk, far inside fp32, and every
+// term a~_t . b~_s (s < t) carries the ratio gamma_{t-1} / gamma_s <= 1.
+//
+// Warp roles (per CTA):
+//   * NS scan warps, warp w owning state rows 16w .. 16w+15 (all N columns):
+//     per chunk SA^T and Y^T for its rows (S as the mma B operand straight from
+//     the accumulator registers, the k index permuted so that a thread's two
+//     accumulator columns are its two k slots), y stored to global, SA staged
+//     through a warp-private scratch as the A operand of dS, S updated in fp32;
+//   * NP prep warps, each preparing a whole chunk (chunks round-robin): the
+//     scaled vectors, the four Gram matrices, the substitution for W and U, and
+//     Q and YU, on the fp32 FMA pipe while the scan warps hold the tensor pipe;
+//   * one loader warp: six TMA boxes (N columns x 16 tokens, one per input) per
+//     chunk into a ring of raw slots.
+// Rings: raw slots (full: TMA bytes; empty: the prep warp's 32 lanes) and
+// prepared slots (full: the prep warp's 32 lanes; empty: every scan lane).
+// Every wait is bounded; a timed-out wait counts in g_ctc_wait_timeouts and the
+// CTA leaves after its TMA copies in flight have landed.
+// Inputs are read once, y written once, the state read and written once.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "mbarrier.cuh"
+#include "tma.cuh"
+
+namespace yuf {
+
+__device__ unsigned int g_ctc_wait_timeouts;
+
+constexpr int CTC_L = 16;
+
+// row stride (floats) of the prepared vectors: >= n and = 8 (mod 32), which
+// makes the mma fragment loads bank-conflict free
+constexpr int ctc_ld(int n) { return n + ((8 - n % 32) + 32) % 32; }
+
+template <int N>
+struct CtcCfg {
+  static constexpr int L = CTC_L;
+  static constexpr int LD = ctc_ld(N);
+  static constexpr int NS = (N + 15) / 16;     // scan warps
+  static constexpr int NP = LD <= 40 ? 4 : 2;  // prep warps
+  static constexpr int NR = NP + 1;            // raw slots
+  static constexpr int NB = NP + 1;            // prepared slots
+  static constexpr int NT = 32 * (NS + NP + 1);
+  static constexpr int NJ = N / 8;             // 8-column tiles
+  static constexpr int GL = L + 4;             // Gram row stride (= 20 mod 32: conflict-free fragments)
+  static constexpr int SLD = 24;               // SA scratch row stride (= 24 mod 32: conflict free)
+  // raw slot: r, w, k, v, a, b as [L][N] each (the TMA boxes)
+  static constexpr int RAW = 6 * L * N;
+  // prepared slot: W, Q, U, YU, B~, K~, V as [L][LD], gamma_15 as [LD]
+  static constexpr int P_W = 0, P_Q = L * LD, P_U = 2 * L * LD, P_YU = 3 * L * LD, P_B = 4 * L * LD,
+                       P_K = 5 * L * LD, P_V = 6 * L * LD, P_G = 7 * L * LD;
+  static constexpr int PREP = (P_G + LD + 31) / 32 * 32;
+  // prep warp scratch: a~, r~ as [L][LD]; Lab (then T), Lak, Mrb, Mrk, T Lak,
+  // Mrb T Lak + Mrk as [L][GL]
+  static constexpr int X_A = 0, X_R = L * LD, X_G = 2 * L * LD, X_T = X_G + 4 * L * GL;
+  static constexpr int XS = (X_T + 2 * L * GL + 31) / 32 * 32;
+  static constexpr int OFF_PREP = NR * RAW;
+  static constexpr int OFF_X = OFF_PREP + NB * PREP;
+  static constexpr int OFF_SA = OFF_X + NP * XS;
+  static constexpr int OFF_BAR = OFF_SA + NS * L * SLD;
+  static constexpr int NBAR = 2 * NR + 2 * NB;
+  static constexpr size_t BYTES = (size_t)OFF_BAR * 4 + NBAR * 8;
+  static constexpr uint32_t TX = 6u * L * N * 4;
+  static_assert(N % 8 == 0 && N <= 64, "chunked tensor-core scan: N a multiple of 8, at most 64");
+  static_assert((L * N * 4) % 128 == 0 && RAW % 32 == 0, "TMA boxes on 128-byte boundaries");
+  static_assert(OFF_BAR % 2 == 0, "mbarriers 8-byte aligned");
+  static_assert(BYTES <= 227 * 1024, "shared memory");
+};
+
+struct CtcTmaps {
+  CUtensorMap m[6];  // r, w, k, v, a, b as [B*T, H*N] fp32
+};
+
+YUF_DEVICE void split_a(const float (&x)[4], uint32_t (&h)[4], uint32_t (&l)[4]) {
+#pragma unroll
+  for (int e = 0; e < 4; ++e) split_tf32(x[e], h[e], l[e]);
+}
+YUF_DEVICE void split_b(float x0, float x1, uint32_t (&h)[2], uint32_t (&l)[2]) {
+  split_tf32(x0, h[0], l[0]);
+  split_tf32(x1, h[1], l[1]);
+}
+
+// Prep products on the tensor cores (mma.sync m16n8k8, 3xTF32), one warp:
+//   out = C + A B (+ A2 B2),   A, A2: [16][GL] row-major (t, s);  B, B2, C, out: [16][LD]
+// (16 x 16 by 16 x N; C may be null).  Fragments are loaded before any mma and
+// the outputs stored after the last, and the three terms of every product are
+// issued across the N / 8 column tiles in turn.  Not inlined: the six calls
+// per chunk share one copy of the code.
+template <int N, int LD, int GL>
+__device__ __noinline__ void prep_mma16(const float* A, const float* B, const float* A2, const float* B2,
+                                        const float* C, float* out) {
+  constexpr int NJ = N / 8;
+  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const bool two = A2 != nullptr;
+  uint32_t ah[2][2][4], al[2][2][4];  // [operand][kk]
+#pragma unroll
+  for (int o = 0; o < 2; ++o) {
+    const float* M = o ? A2 : A;
+    if (o == 1 && !two) break;
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const float x[4] = {M[g * GL + 8 * kk + q], M[(g + 8) * GL + 8 * kk + q], M[g * GL + 8 * kk + q + 4],
+                          M[(g + 8) * GL + 8 * kk + q + 4]};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) split_tf32(x[e], ah[o][kk][e], al[o][kk][e]);
+    }
+  }
+  uint32_t bh[2][2][NJ][2], bl[2][2][NJ][2];  // [operand][kk][tile]
+  float d[NJ][4];
+#pragma unroll
+  for (int nt = 0; nt < NJ; ++nt) {
+#pragma unroll
+    for (int o = 0; o < 2; ++o) {
+      const float* M = o ? B2 : B;
+      if (o == 1 && !two) break;
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        split_tf32(M[(8 * kk + q) * LD + 8 * nt + g], bh[o][kk][nt][0], bl[o][kk][nt][0]);
+        split_tf32(M[(8 * kk + q + 4) * LD + 8 * nt + g], bh[o][kk][nt][1], bl[o][kk][nt][1]);
+      }
+    }
+    if (C) {
+      const float2 c0 = *reinterpret_cast<const float2*>(C + g * LD + 8 * nt + 2 * q);
+      const float2 c1 = *reinterpret_cast<const float2*>(C + (g + 8) * LD + 8 * nt + 2 * q);
+      d[nt][0] = c0.x; d[nt][1] = c0.y; d[nt][2] = c1.x; d[nt][3] = c1.y;
+    } else {
+      d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int o = 0; o < 2; ++o) {
+    if (o == 1 && !two) break;
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+#pragma unroll
+      for (int nt = 0; nt < NJ; ++nt) mma_tf32(d[nt], al[o][kk], bh[o][kk][nt]);
+#pragma unroll
+      for (int nt = 0; nt < NJ; ++nt) mma_tf32(d[nt], ah[o][kk], bl[o][kk][nt]);
+#pragma unroll
+      for (int nt = 0; nt < NJ; ++nt) mma_tf32(d[nt], ah[o][kk], bh[o][kk][nt]);
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < NJ; ++nt) {
+    *reinterpret_cast<float2*>(out + g * LD + 8 * nt + 2 * q) = make_float2(d[nt][0], d[nt][1]);
+    *reinterpret_cast<float2*>(out + (g + 8) * LD + 8 * nt + 2 * q) = make_float2(d[nt][2], d[nt][3]);
+  }
+}
+
+// The chunk's Gram matrices on the tensor cores, one warp:
+//   [a~; r~] [b~; k~]^T  (32 x N by N x 32, 3xTF32), masked to
+//   Lab, Lak (s < t) and Mrb, Mrk (s <= t), stored row-major [t][GL] at G,
+//   G + 16 GL, G + 32 GL, G + 48 GL.
+template <int N, int LD, int GL>
+__device__ __noinline__ void prep_gram(const float* At, const float* Rt, const float* Bt, const float* Kt, float* G) {
+  constexpr int NJ = N / 8;
+  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  float d[2][4][4];  // [a~ | r~][b~ s0-7 | b~ s8-15 | k~ s0-7 | k~ s8-15]
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) d[mt][nt][e] = 0.f;
+#pragma unroll 1
+  for (int kc = 0; kc < NJ; ++kc) {
+    // k slots q / q+4 <-> columns 8kc + 2q / 8kc + 2q + 1 (float2 loads)
+    uint32_t ah[2][4], al[2][4], bh[4][2], bl[4][2];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const float* M = mt ? Rt : At;
+      const float2 x0 = *reinterpret_cast<const float2*>(M + g * LD + 8 * kc + 2 * q);
+      const float2 x1 = *reinterpret_cast<const float2*>(M + (g + 8) * LD + 8 * kc + 2 * q);
+      split_tf32(x0.x, ah[mt][0], al[mt][0]);
+      split_tf32(x1.x, ah[mt][1], al[mt][1]);
+      split_tf32(x0.y, ah[mt][2], al[mt][2]);
+      split_tf32(x1.y, ah[mt][3], al[mt][3]);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const float* M = (nt < 2 ? Bt : Kt) + (8 * (nt & 1) + g) * LD + 8 * kc + 2 * q;
+      const float2 x = *reinterpret_cast<const float2*>(M);
+      split_tf32(x.x, bh[nt][0], bl[nt][0]);
+      split_tf32(x.y, bh[nt][1], bl[nt][1]);
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_tf32(d[mt][nt], al[mt], bh[nt]);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_tf32(d[mt][nt], ah[mt], bl[nt]);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_tf32(d[mt][nt], ah[mt], bh[nt]);
+  }
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      float* M = G + (2 * mt + (nt >> 1)) * 16 * GL;  // Lab, Lak, Mrb, Mrk
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = g + 8 * (e >> 1), sidx = 8 * (nt & 1) + 2 * q + (e & 1);
+        const bool keep = mt ? sidx <= t : sidx < t;
+        M[t * GL + sidx] = keep ? d[mt][nt][e] : 0.f;
+      }
+    }
+}
+
+// p ? a : b as one select instruction: both operands are computed first, so
+// the items of an unrolled loop keep their independent dependency chains (a
+// conditional around each item's loads or math would serialise them), and a
+// non-finite value in a masked slot cannot leak through a multiply.
+YUF_DEVICE float sel(bool p, float a, float b) {
+  float r;
+  asm("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\tselp.f32 %0, %1, %2, q;\n\t}"
+      : "=f"(r)
+      : "f"(a), "f"(b), "r"((int)p));
+  return r;
+}
+
+// true once; the caller that flips the flag counts the timeout
+YUF_DEVICE void ctc_abort(int* flag) {
+  if (atomicExch(flag, 1) == 0) atomicAdd(&g_ctc_wait_timeouts, 1u);
+}
+
+template <int N>
+__global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
+    wkv7_chunk_tc_kernel(const float* __restrict__ s0, float* __restrict__ y, float* __restrict__ s_out, int T,
+                         int H, const __grid_constant__ CtcTmaps tm) {
+  using K = CtcCfg<N>;
+  constexpr int L = K::L, LD = K::LD, NS = K::NS, NP = K::NP, NR = K::NR, NB = K::NB, NJ = K::NJ;
+  constexpr int GL = K::GL, SLD = K::SLD;
+  extern __shared__ __align__(128) float ctc_smem[];
+  float* sm = ctc_smem;
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sm + K::OFF_BAR);
+  uint64_t* raw_empty = raw_full + NR;
+  uint64_t* prep_full = raw_empty + NR;
+  uint64_t* prep_empty = prep_full + NB;
+  __shared__ int abort_flag;
+
+  const int bh = blockIdx.x;
+  const int bb = bh / H, hh = bh - bb * H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nchunks = (T + L - 1) / L;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NR; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 32);
+    }
+    for (int s = 0; s < NB; ++s) {
+      mbar_init(&prep_full[s], 32);
+      mbar_init(&prep_empty[s], 32 * NS);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  volatile int* abort_v = &abort_flag;
+
+  if (warp < NS) {  // ------------------------------------------------------ scan warps
+    const int g = lane >> 2, q = lane & 3;
+    const int i0 = warp * 16;
+    const bool h1 = i0 + 16 <= N;  // the tile's second 8 rows are state rows
+    const size_t sbase = (size_t)bh * N * N;
+    float S[NJ][4];
+#pragma unroll
+    for (int c = 0; c < NJ; ++c)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = i0 + g + (e >> 1) * 8, col = 8 * c + 2 * q + (e & 1);
+        S[c][e] = (s0 && row < N) ? s0[sbase + (size_t)row * N + col] : 0.f;
+      }
+    float* SA = sm + K::OFF_SA + warp * L * SLD;
+    const size_t ystride = (size_t)H * N;
+    float* ybase = y + ((size_t)bb * T * H + hh) * N + i0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int slot = c % NB;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&prep_full[slot], (uint32_t)(c / NB) & 1u));
+      if (!ok || *abort_v) {
+        if (lane == 0) ctc_abort(&abort_flag);
+        break;
+      }
+      const float* P = sm + K::OFF_PREP + slot * K::PREP;
+      // SA^T and Y^T for this warp's rows: M = token, N = state row, K = column
+      float sa[2][4], yy[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = i0 + 8 * h + 2 * q;
+        const float2 u0 = *reinterpret_cast<const float2*>(P + K::P_U + g * LD + col);
+        const float2 u1 = *reinterpret_cast<const float2*>(P + K::P_U + (g + 8) * LD + col);
+        const float2 y0 = *reinterpret_cast<const float2*>(P + K::P_YU + g * LD + col);
+        const float2 y1 = *reinterpret_cast<const float2*>(P + K::P_YU + (g + 8) * LD + col);
+        sa[h][0] = u0.x; sa[h][1] = u0.y; sa[h][2] = u1.x; sa[h][3] = u1.y;
+        yy[h][0] = y0.x; yy[h][1] = y0.y; yy[h][2] = y1.x; yy[h][3] = y1.y;
+      }
+#pragma unroll
+      for (int kc = 0; kc < NJ; ++kc) {
+        // A: rows g, g+8 of W (and Q), k slots q / q+4 <-> columns 8kc+2q / 8kc+2q+1
+        const float2 w0 = *reinterpret_cast<const float2*>(P + K::P_W + g * LD + 8 * kc + 2 * q);
+        const float2 w1 = *reinterpret_cast<const float2*>(P + K::P_W + (g + 8) * LD + 8 * kc + 2 * q);
+        const float2 q0 = *reinterpret_cast<const float2*>(P + K::P_Q + g * LD + 8 * kc + 2 * q);
+        const float2 q1 = *reinterpret_cast<const float2*>(P + K::P_Q + (g + 8) * LD + 8 * kc + 2 * q);
+        uint32_t wh[4], wl[4], qh[4], ql[4];
+        split_a({w0.x, w1.x, w0.y, w1.y}, wh, wl);
+        split_a({q0.x, q1.x, q0.y, q1.y}, qh, ql);
+        // B: S[i0 + 8h + g][8kc + 2q (+1)], the accumulator pair of tile kc
+        uint32_t bhi[2][2], blo[2][2];
+        split_b(S[kc][0], S[kc][1], bhi[0], blo[0]);
+        split_b(S[kc][2], S[kc][3], bhi[1], blo[1]);
+        // the three terms of the four products in turn, so that consecutive
+        // mma instructions feed different accumulators
+        mma_tf32(sa[0], wl, bhi[0]);
+        mma_tf32(yy[0], ql, bhi[0]);
+        if (h1) {
+          mma_tf32(sa[1], wl, bhi[1]);
+          mma_tf32(yy[1], ql, bhi[1]);
+        }
+        mma_tf32(sa[0], wh, blo[0]);
+        mma_tf32(yy[0], qh, blo[0]);
+        if (h1) {
+          mma_tf32(sa[1], wh, blo[1]);
+          mma_tf32(yy[1], qh, blo[1]);
+        }
+        mma_tf32(sa[0], wh, bhi[0]);
+        mma_tf32(yy[0], qh, bhi[0]);
+        if (h1) {
+          mma_tf32(sa[1], wh, bhi[1]);
+          mma_tf32(yy[1], qh, bhi[1]);
+        }
+      }
+      // y rows of this chunk; SA into the warp's scratch as [token][row]
+      const int t0 = c * L + g;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = 8 * h + 2 * q;
+        const bool real = h == 0 || h1;
+        *reinterpret_cast<float2*>(SA + g * SLD + col) =
+            real ? make_float2(sa[h][0], sa[h][1]) : make_float2(0.f, 0.f);
+        *reinterpret_cast<float2*>(SA + (g + 8) * SLD + col) =
+            real ? make_float2(sa[h][2], sa[h][3]) : make_float2(0.f, 0.f);
+        if (real) {
+          if (t0 < T) *reinterpret_cast<float2*>(ybase + (size_t)t0 * ystride + col) = make_float2(yy[h][0], yy[h][1]);
+          if (t0 + 8 < T)
+            *reinterpret_cast<float2*>(ybase + (size_t)(t0 + 8) * ystride + col) = make_float2(yy[h][2], yy[h][3]);
+        }
+      }
+      __syncwarp();
+      // dS = SA^T^T B~ + V^T K~: M = state row, N = column, K = token
+      float dS[NJ][4];
+#pragma unroll
+      for (int c2 = 0; c2 < NJ; ++c2)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dS[c2][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const int ta = 8 * kk + q, tb = ta + 4;
+        uint32_t sah[4], sal[4], vh[4], val[4];
+        split_a({SA[ta * SLD + g], SA[ta * SLD + g + 8], SA[tb * SLD + g], SA[tb * SLD + g + 8]}, sah, sal);
+        const float* V = P + K::P_V + i0 + g;
+        split_a({V[ta * LD], h1 ? V[ta * LD + 8] : 0.f, V[tb * LD], h1 ? V[tb * LD + 8] : 0.f}, vh, val);
+        uint32_t bbh[NJ][2], bbl[NJ][2], kh[NJ][2], kl[NJ][2];
+#pragma unroll
+        for (int c2 = 0; c2 < NJ; ++c2) {
+          split_b(P[K::P_B + ta * LD + 8 * c2 + g], P[K::P_B + tb * LD + 8 * c2 + g], bbh[c2], bbl[c2]);
+          split_b(P[K::P_K + ta * LD + 8 * c2 + g], P[K::P_K + tb * LD + 8 * c2 + g], kh[c2], kl[c2]);
+        }
+        // term by term across the column tiles (independent accumulators back to back)
+#pragma unroll
+        for (int c2 = 0; c2 < NJ; ++c2) mma_tf32(dS[c2], sal, bbh[c2]);
+#pragma unroll
+        for (int c2 = 0; c2 < NJ; ++c2) mma_tf32(dS[c2], val, kh[c2]);
+#pragma unroll
+        for (int c2 = 0; c2 < NJ; ++c2) mma_tf32(dS[c2], sah, bbl[c2]);
+#pragma unroll
+        for (int c2 = 0; c2 < NJ; ++c2) mma_tf32(dS[c2], vh, kl[c2]);
+#pragma unroll
+        for (int c2 = 0; c2 < NJ; ++c2) mma_tf32(dS[c2], sah, bbh[c2]);
+#pragma unroll
+        for (int c2 = 0; c2 < NJ; ++c2) mma_tf32(dS[c2], vh, kh[c2]);
+      }
+#pragma unroll
+      for (int c2 = 0; c2 < NJ; ++c2) {
+        const float2 gm = *reinterpret_cast<const float2*>(P + K::P_G + 8 * c2 + 2 * q);
+        S[c2][0] = (S[c2][0] + dS[c2][0]) * gm.x;
+        S[c2][1] = (S[c2][1] + dS[c2][1]) * gm.y;
+        S[c2][2] = (S[c2][2] + dS[c2][2]) * gm.x;
+        S[c2][3] = (S[c2][3] + dS[c2][3]) * gm.y;
+      }
+      __syncwarp();
+      mbar_arrive(&prep_empty[slot]);
+    }
+    if (s_out && !*abort_v) {
+#pragma unroll
+      for (int c = 0; c < NJ; ++c)
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int row = i0 + g + 8 * hr;
+          if (row < N)
+            *reinterpret_cast<float2*>(s_out + sbase + (size_t)row * N + 8 * c + 2 * q) =
+                make_float2(S[c][2 * hr], S[c][2 * hr + 1]);
+        }
+    }
+  } else if (warp < NS + NP) {  // ------------------------------------------- prep warps
+    const int p = warp - NS;
+    float* X = sm + K::OFF_X + p * K::XS;
+    for (int c = p; c < nchunks; c += NP) {
+      const int rs = c % NR, ps = c % NB;
+      bool ok = mbar_wait(&raw_full[rs], (uint32_t)(c / NR) & 1u) &&
+                mbar_wait(&prep_empty[ps], ((uint32_t)(c / NB) & 1u) ^ 1u);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_v) {
+        if (lane == 0) ctc_abort(&abort_flag);
+        break;
+      }
+      const float* R = sm + rs * K::RAW;  // r, w, k, v, a, b: [L][N]
+      float* P = sm + K::OFF_PREP + ps * K::PREP;
+      const int Tc = min(L, T - c * L);
+      // Loads are grouped ahead of the stores of each step below: the raw,
+      // scratch and prepared regions all live in one shared array, so the
+      // compiler could not move a load above a preceding store.  Loops are
+      // kept rolled where that costs no parallelism, so that the scan and prep
+      // code together stay small in the instruction caches.
+      // (1) log retentions ls = W_SCALE sigmoid(w), an item (t, j) per lane,
+      //     into the W region (free until W is written)
+      float* Gs = P + K::P_W;
+      constexpr int ITEMS = L * N / 32;
+      {
+        float lw[ITEMS];
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) lw[it] = R[1 * L * N + lane + 32 * it];
+#pragma unroll
+        for (int it = 0; it < ITEMS; ++it) {
+          const int e = lane + 32 * it, t = e / N;
+          Gs[t * LD + (e - t * N)] = sel(t < Tc, W_SCALE * sigmoidf_fast(lw[it]), 0.f);
+        }
+      }
+      __syncwarp();
+      // (2) running sums G_t = ls_0 + ... + ls_t (gamma_t = exp(G_t)), a lane per column
+#pragma unroll 1
+      for (int j = lane; j < N; j += 32) {
+        float x[L];
+#pragma unroll
+        for (int t = 0; t < L; ++t) x[t] = Gs[t * LD + j];
+#pragma unroll
+        for (int t = 1; t < L; ++t) x[t] += x[t - 1];
+#pragma unroll
+        for (int t = 0; t < L; ++t) Gs[t * LD + j] = x[t];
+        P[K::P_G + j] = __expf(x[L - 1]);
+      }
+      __syncwarp();
+      // (3) scaled vectors, the lane's items in two unrolled halves
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        constexpr int HI = (ITEMS + 1) / 2;
+        float G[HI], Gp[HI], ra[HI], rb[HI], rk[HI], rr[HI], rv[HI];
+#pragma unroll
+        for (int u = 0; u < HI; ++u) {
+          const int it = min(hf * HI + u, ITEMS - 1);  // past the end: a repeat, not stored
+          const int e = lane + 32 * it, t = e / N, j = e - t * N;
+          const bool live = t < Tc;
+          G[u] = Gs[t * LD + j];
+          Gp[u] = t > 0 ? Gs[(t - 1) * LD + j] : 0.f;
+          rr[u] = live ? R[e] : 0.f;
+          rk[u] = live ? R[2 * L * N + e] : 0.f;
+          rv[u] = live ? R[3 * L * N + e] : 0.f;
+          ra[u] = live ? R[4 * L * N + e] : 0.f;
+          rb[u] = live ? R[5 * L * N + e] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < HI; ++u) {
+          const int it = hf * HI + u;
+          if (it >= ITEMS) break;
+          const int e = lane + 32 * it, t = e / N, j = e - t * N;
+          const float gam = __expf(G[u]), ginv = __expf(-G[u]), gprev = __expf(Gp[u]);
+          X[K::X_A + t * LD + j] = ra[u] * gprev;  // gamma_{t-1} a_t
+          P[K::P_B + t * LD + j] = rb[u] * ginv;   // b_t / gamma_t
+          P[K::P_K + t * LD + j] = rk[u] * ginv;   // k_t / gamma_t
+          X[K::X_R + t * LD + j] = rr[u] * gam;    // gamma_t r_t
+          P[K::P_V + t * LD + j] = rv[u];
+        }
+      }
+      __syncwarp();
+      mbar_arrive(&raw_empty[rs]);  // every lane is done with the raw slot
+      // (4) Gram matrices Lab, Lak, Mrb, Mrk (row-major [t][GL])
+      prep_gram<N, LD, GL>(X + K::X_A, X + K::X_R, P + K::P_B, P + K::P_K, X + K::X_G);
+      __syncwarp();
+      // (5) T = (I - Lab)^-1 (unit lower triangular), lane c < 16 solving for
+      //     column c; T replaces Lab once every lane has read it
+      {
+        float* Lab = X + K::X_G;
+        const int cidx = lane & 15;
+        float x[L];
+#pragma unroll
+        for (int t = 0; t < L; ++t) {
+          float acc = t == cidx ? 1.f : 0.f;
+#pragma unroll
+          for (int s2 = 0; s2 < t; ++s2) acc = fmaf(Lab[t * GL + s2], x[s2], acc);
+          x[t] = acc;
+        }
+        __syncwarp();
+        if (lane < 16) {
+#pragma unroll
+          for (int t = 0; t < L; ++t) Lab[t * GL + cidx] = x[t];
+        }
+      }
+      __syncwarp();
+      // (6) TLak = T Lak and M2 = Mrb TLak + Mrk (16 x 16, into the free
+      //     slots after Mrk), then W = T A~,  Q = R~ + Mrb W,  U = TLak V,
+      //     YU = M2 V  (U = T Lak V and YU = Mrb U + Mrk V regrouped)
+      {
+        const float* Tm = X + K::X_G;
+        const float* Lak = Tm + L * GL;
+        const float* Mrb = Lak + L * GL;
+        const float* Mrk = Mrb + L * GL;
+        float* TLak = X + K::X_T;
+        float* M2 = TLak + L * GL;
+        prep_mma16<16, GL, GL>(Tm, Lak, nullptr, nullptr, nullptr, TLak);
+        prep_mma16<N, LD, GL>(Tm, X + K::X_A, nullptr, nullptr, nullptr, P + K::P_W);
+        __syncwarp();
+        prep_mma16<16, GL, GL>(Mrb, TLak, nullptr, nullptr, Mrk, M2);
+        prep_mma16<N, LD, GL>(Mrb, P + K::P_W, nullptr, nullptr, X + K::X_R, P + K::P_Q);
+        prep_mma16<N, LD, GL>(TLak, P + K::P_V, nullptr, nullptr, nullptr, P + K::P_U);
+        __syncwarp();
+        prep_mma16<N, LD, GL>(M2, P + K::P_V, nullptr, nullptr, nullptr, P + K::P_YU);
+      }
+      __syncwarp();
+      mbar_arrive(&prep_full[ps]);
+    }
+  } else if (lane == 0) {  // ------------------------------------------------- loader
+    const int tx = hh * N, ty = bb * T;
+    int c = 0;
+    for (; c < nchunks; ++c) {
+      const int rs = c % NR;
+      if (!mbar_wait(&raw_empty[rs], ((uint32_t)(c / NR) & 1u) ^ 1u) || *abort_v) {
+        ctc_abort(&abort_flag);
+        break;
+      }
+      float* dst = sm + rs * K::RAW;
+      mbar_expect_tx(&raw_full[rs], K::TX);
+#pragma unroll
+      for (int arr = 0; arr < 6; ++arr) tma_load_2d(dst + arr * L * N, &tm.m[arr], &raw_full[rs], tx, ty + c * L);
+    }
+    // the copies still in flight land before the CTA may leave
+    for (int c2 = max(0, c - NR); c2 < c; ++c2) mbar_wait(&raw_full[c2 % NR], (uint32_t)(c2 / NR) & 1u);
+  }
+}
+
+// Tensor maps of the six [B*T, H*N] inputs, box = N columns x 16 tokens.
+static yuf_status_t make_ctc_tmaps(const float* const (&src)[6], long long rows, int H, int N, CtcTmaps* out) {
+  auto enc = tensor_map_encoder();
+  if (!enc) {
+    set_error("wkv7 chunked-tc: cuTensorMapEncodeTiled is unavailable");
+    return YUF_ERR_CUDA;
+  }
+  const cuuint64_t gdim[2] = {(cuuint64_t)H * N, (cuuint64_t)rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)H * N * sizeof(float)};
+  const cuuint32_t box[2] = {(cuuint32_t)N, (cuuint32_t)CTC_L};
+  const cuuint32_t estride[2] = {1u, 1u};
+  for (int i = 0; i < 6; ++i) {
+    const CUresult rc = enc(&out->m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(src[i]), gdim,
+                            gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (rc != CUDA_SUCCESS) {
+      set_error("wkv7 chunked-tc: cuTensorMapEncodeTiled failed (%d) for input %d", (int)rc, i);
+      return YUF_ERR_CUDA;
+    }
+  }
+  return YUF_OK;
+}
+
+template <int N>
+static yuf_status_t launch_ctc(const float* const (&src)[6], const float* s0, float* y, float* s_out, int B, int T,
+                               int H, cudaStream_t st) {
+  using K = CtcCfg<N>;
+  static std::once_flag once[128];
+  static cudaError_t attr[128];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 127;
+  std::call_once(once[dev], [&] {
+    attr[dev] =
+        cudaFuncSetAttribute(wkv7_chunk_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)K::BYTES);
+  });
+  if (attr[dev] != cudaSuccess) {
+    set_error("wkv7 chunked-tc: cannot set %zu bytes of shared memory: %s", K::BYTES,
+              cudaGetErrorString(attr[dev]));
+    return YUF_ERR_CUDA;
+  }
+  CtcTmaps tm;
+  const yuf_status_t rc = make_ctc_tmaps(src, (long long)B * T, H, N, &tm);
+  if (rc != YUF_OK) return rc;
+  launch_k(wkv7_chunk_tc_kernel<N>, dim3(B * H), dim3(K::NT), K::BYTES, st, s0, y, s_out, T, H, tm);
+  return check_launch("wkv7_chunk_tc_kernel");
+}
+
+bool wkv7_chunk_tc_supports(int N) { return N == 16 || N == 32 || N == 40 || N == 48 || N == 64; }
+
+// Chunked tensor-core scan of [B, T, H, N] inputs from s0 (nullable), writing y
+// and the final state (nullable).  Inputs 16-byte aligned.
+yuf_status_t wkv7_chunk_tc(const float* r, const float* w, const float* k, const float* v, const float* a,
+                           const float* b, const float* s0, float* y, float* s_out, int B, int T, int H, int N,
+                           cudaStream_t st) {
+  if (T == 0) {  // no tokens: the final state is the initial one
+    if (!s_out || s_out == s0) return YUF_OK;
+    const size_t bytes = (size_t)B * H * N * N * sizeof(float);
+    const cudaError_t e = s0 ? cudaMemcpyAsync(s_out, s0, bytes, cudaMemcpyDeviceToDevice, st)
+                             : cudaMemsetAsync(s_out, 0, bytes, st);
+    if (e != cudaSuccess) {
+      set_error("wkv7 chunked-tc: %s", cudaGetErrorString(e));
+      return YUF_ERR_CUDA;
+    }
+    return YUF_OK;
+  }
+  const float* const src[6] = {r, w, k, v, a, b};
+  switch (N) {
+    case 16: return launch_ctc<16>(src, s0, y, s_out, B, T, H, st);
+    case 32: return launch_ctc<32>(src, s0, y, s_out, B, T, H, st);
+    case 40: return launch_ctc<40>(src, s0, y, s_out, B, T, H, st);
+    case 48: return launch_ctc<48>(src, s0, y, s_out, B, T, H, st);
+    case 64: return launch_ctc<64>(src, s0, y, s_out, B, T, H, st);
+    default:
+      set_error("wkv7 chunked-tc: head size N=%d has no kernel (N in {16, 32, 40, 48, 64})", N);
+      return YUF_ERR_UNSUPPORTED;
+  }
+}
+
+unsigned int wkv7_chunk_tc_wait_timeouts() {
+  unsigned int n = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&n, g_ctc_wait_timeouts, sizeof(n)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_ctc_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess) {
+    cudaGetLastError();
+    return ~0u;
+  }
+  return n;
+}
+
+}  // namespace yuf

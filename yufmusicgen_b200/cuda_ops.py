@@ -45,7 +45,7 @@ def _validate(tensors, names=("r", "w", "k", "v", "a", "b")):
         raise ValueError("RWKV-7 CUDA inputs must be on one device")
 
 
-ALGO_AUTO, ALGO_SEQUENTIAL, ALGO_CHUNKED, ALGO_PARALLEL, ALGO_PARALLEL_TC, ALGO_ROWS = 0, 1, 2, 3, 4, 5
+ALGO_AUTO, ALGO_SEQUENTIAL, ALGO_CHUNKED, ALGO_PARALLEL, ALGO_PARALLEL_TC, ALGO_ROWS, ALGO_CHUNKED_TC = range(7)
 
 
 def wkv7_forward(r, w, k, v, a, b, state=None, out=None, state_out=None, algo=ALGO_AUTO):
