@@ -73,10 +73,6 @@ unsigned int wkv7_decode_wait_timeouts();
 unsigned int gemm_wait_timeouts();
 unsigned int wkv7_rows_wait_timeouts();
 unsigned int wkv7_chunk_tc_wait_timeouts();
-bool wkv7_chunk_tc_supports(int N);
-yuf_status_t wkv7_chunk_tc(const float* r, const float* w, const float* k, const float* v, const float* a,
-                           const float* b, const float* s0, float* y, float* s_out, int B, int T, int H, int N,
-                           cudaStream_t st);
 yuf_status_t wkv7_rows(const float* r, const float* w, const float* k, const float* v, const float* a,
                        const float* b, const float* s0, float* y, float* s_out, int B, int T, int H, int N,
                        cudaStream_t st);
@@ -206,7 +202,8 @@ yuf_status_t yuf_wkv7_forward_ex(const float* r, const float* w, const float* k,
     return wkv7_decode_dispatch(r, w, k, v, a, b, s0, y, s_out, B * H, N, st_);
   if (algo == YUF_WKV_CHUNKED) return wkv7_chunk_dispatch(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, st_);
   if (algo == YUF_WKV_ROWS) return wkv7_rows(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, st_);
-  if (algo == YUF_WKV_CHUNKED_TC) return wkv7_chunk_tc(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, st_);
+  if (algo == YUF_WKV_CHUNKED_TC || (algo == YUF_WKV_AUTO && wkv7_chunk_tc_applies(B, T, H, N)))
+    return wkv7_chunk_tc(r, w, k, v, a, b, s0, y, s_out, B, T, H, N, st_);
   if (algo == YUF_WKV_PARALLEL || algo == YUF_WKV_PARALLEL_TC ||
       (algo == YUF_WKV_AUTO && wkv7_parallel_applies(B, T, H, N))) {
     // stream-ordered scratch for the chunk transitions, released right after use

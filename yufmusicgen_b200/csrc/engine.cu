@@ -369,6 +369,8 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     if (T == 1)
       Y_TRY(wkv7_decode_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S,
                                  B * H, N, s));
+    else if (wkv7_chunk_tc_applies(B, T, H, N))
+      Y_TRY(wkv7_chunk_tc(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, B, T, H, N, s));
     else if (wkv7_parallel_applies(B, T, H, N))
       Y_TRY(wkv7_parallel(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, B, T, H,
                           N, w.scan + scan_rosa_floats(m, rows), s));

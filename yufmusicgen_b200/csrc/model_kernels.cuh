@@ -64,4 +64,11 @@ yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
                            int B, int T, int H, int N, float* scratch, cudaStream_t st,
                            bool tc_correct = false);
+// Chunked WKV-7 prefill on the tensor cores (wkv7_chunk_tc.cu): one CTA per
+// (sequence, head), no scratch; N in {16, 32, 40, 48, 64}.
+bool wkv7_chunk_tc_supports(int N);
+bool wkv7_chunk_tc_applies(int B, int T, int H, int N);
+yuf_status_t wkv7_chunk_tc(const float* r, const float* w, const float* k, const float* v, const float* a,
+                           const float* b, const float* s0, float* y, float* s_out, int B, int T, int H, int N,
+                           cudaStream_t st);
 }  // namespace yuf

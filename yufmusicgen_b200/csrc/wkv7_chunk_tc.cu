@@ -112,70 +112,77 @@ YUF_DEVICE void split_b(float x0, float x1, uint32_t (&h)[2], uint32_t (&l)[2]) 
 }
 
 // Prep products on the tensor cores (mma.sync m16n8k8, 3xTF32), one warp:
-//   out = C + A B (+ A2 B2),   A, A2: [16][GL] row-major (t, s);  B, B2, C, out: [16][LD]
-// (16 x 16 by 16 x N; C may be null).  Fragments are loaded before any mma and
-// the outputs stored after the last, and the three terms of every product are
-// issued across the N / 8 column tiles in turn.  Not inlined: the six calls
-// per chunk share one copy of the code.
-template <int N, int LD, int GL>
-__device__ __noinline__ void prep_mma16(const float* A, const float* B, const float* A2, const float* B2,
-                                        const float* C, float* out) {
+//   out_p = C_p + A_p B_p  for p < NPR independent products,
+//   A_p: [16][GL] row-major (t, s);  B_p, C_p, out_p: [16][LD] (16 x 16 by 16 x N,
+//   C_p may be null).  The products' fragments are all loaded before the first
+//   mma and the outputs stored after the last; the mma instructions of the
+//   products and column tiles are interleaved term by term, so that consecutive
+//   ones feed different accumulators.  Not inlined: the calls of a chunk share
+//   the code.
+struct PrepProd {
+  const float* A;
+  const float* B;
+  const float* C;
+  float* out;
+};
+template <int N, int LD, int GL, int NPR>
+__device__ __noinline__ void prep_mma(PrepProd p0, PrepProd p1) {
   constexpr int NJ = N / 8;
   const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-  const bool two = A2 != nullptr;
-  uint32_t ah[2][2][4], al[2][2][4];  // [operand][kk]
+  const PrepProd pr[2] = {p0, p1};
+  uint32_t ah[NPR][2][4], al[NPR][2][4];
+  uint32_t bh[NPR][2][NJ][2], bl[NPR][2][NJ][2];
+  float d[NPR][NJ][4];
 #pragma unroll
-  for (int o = 0; o < 2; ++o) {
-    const float* M = o ? A2 : A;
-    if (o == 1 && !two) break;
+  for (int o = 0; o < NPR; ++o) {
+    const float* A = pr[o].A;
+    const float* B = pr[o].B;
+    const float* C = pr[o].C;
 #pragma unroll
     for (int kk = 0; kk < 2; ++kk) {
-      const float x[4] = {M[g * GL + 8 * kk + q], M[(g + 8) * GL + 8 * kk + q], M[g * GL + 8 * kk + q + 4],
-                          M[(g + 8) * GL + 8 * kk + q + 4]};
+      const float x[4] = {A[g * GL + 8 * kk + q], A[(g + 8) * GL + 8 * kk + q], A[g * GL + 8 * kk + q + 4],
+                          A[(g + 8) * GL + 8 * kk + q + 4]};
 #pragma unroll
       for (int e = 0; e < 4; ++e) split_tf32(x[e], ah[o][kk][e], al[o][kk][e]);
-    }
-  }
-  uint32_t bh[2][2][NJ][2], bl[2][2][NJ][2];  // [operand][kk][tile]
-  float d[NJ][4];
 #pragma unroll
-  for (int nt = 0; nt < NJ; ++nt) {
-#pragma unroll
-    for (int o = 0; o < 2; ++o) {
-      const float* M = o ? B2 : B;
-      if (o == 1 && !two) break;
-#pragma unroll
-      for (int kk = 0; kk < 2; ++kk) {
-        split_tf32(M[(8 * kk + q) * LD + 8 * nt + g], bh[o][kk][nt][0], bl[o][kk][nt][0]);
-        split_tf32(M[(8 * kk + q + 4) * LD + 8 * nt + g], bh[o][kk][nt][1], bl[o][kk][nt][1]);
+      for (int nt = 0; nt < NJ; ++nt) {
+        split_tf32(B[(8 * kk + q) * LD + 8 * nt + g], bh[o][kk][nt][0], bl[o][kk][nt][0]);
+        split_tf32(B[(8 * kk + q + 4) * LD + 8 * nt + g], bh[o][kk][nt][1], bl[o][kk][nt][1]);
       }
     }
-    if (C) {
-      const float2 c0 = *reinterpret_cast<const float2*>(C + g * LD + 8 * nt + 2 * q);
-      const float2 c1 = *reinterpret_cast<const float2*>(C + (g + 8) * LD + 8 * nt + 2 * q);
-      d[nt][0] = c0.x; d[nt][1] = c0.y; d[nt][2] = c1.x; d[nt][3] = c1.y;
-    } else {
-      d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < NJ; ++nt) {
+      if (C) {
+        const float2 c0 = *reinterpret_cast<const float2*>(C + g * LD + 8 * nt + 2 * q);
+        const float2 c1 = *reinterpret_cast<const float2*>(C + (g + 8) * LD + 8 * nt + 2 * q);
+        d[o][nt][0] = c0.x; d[o][nt][1] = c0.y; d[o][nt][2] = c1.x; d[o][nt][3] = c1.y;
+      } else {
+        d[o][nt][0] = d[o][nt][1] = d[o][nt][2] = d[o][nt][3] = 0.f;
+      }
     }
   }
 #pragma unroll
-  for (int o = 0; o < 2; ++o) {
-    if (o == 1 && !two) break;
+  for (int kk = 0; kk < 2; ++kk) {
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
+    for (int o = 0; o < NPR; ++o)
 #pragma unroll
-      for (int nt = 0; nt < NJ; ++nt) mma_tf32(d[nt], al[o][kk], bh[o][kk][nt]);
+      for (int nt = 0; nt < NJ; ++nt) mma_tf32(d[o][nt], al[o][kk], bh[o][kk][nt]);
 #pragma unroll
-      for (int nt = 0; nt < NJ; ++nt) mma_tf32(d[nt], ah[o][kk], bl[o][kk][nt]);
+    for (int o = 0; o < NPR; ++o)
 #pragma unroll
-      for (int nt = 0; nt < NJ; ++nt) mma_tf32(d[nt], ah[o][kk], bh[o][kk][nt]);
+      for (int nt = 0; nt < NJ; ++nt) mma_tf32(d[o][nt], ah[o][kk], bl[o][kk][nt]);
+#pragma unroll
+    for (int o = 0; o < NPR; ++o)
+#pragma unroll
+      for (int nt = 0; nt < NJ; ++nt) mma_tf32(d[o][nt], ah[o][kk], bh[o][kk][nt]);
+  }
+#pragma unroll
+  for (int o = 0; o < NPR; ++o)
+#pragma unroll
+    for (int nt = 0; nt < NJ; ++nt) {
+      *reinterpret_cast<float2*>(pr[o].out + g * LD + 8 * nt + 2 * q) = make_float2(d[o][nt][0], d[o][nt][1]);
+      *reinterpret_cast<float2*>(pr[o].out + (g + 8) * LD + 8 * nt + 2 * q) = make_float2(d[o][nt][2], d[o][nt][3]);
     }
-  }
-#pragma unroll
-  for (int nt = 0; nt < NJ; ++nt) {
-    *reinterpret_cast<float2*>(out + g * LD + 8 * nt + 2 * q) = make_float2(d[nt][0], d[nt][1]);
-    *reinterpret_cast<float2*>(out + (g + 8) * LD + 8 * nt + 2 * q) = make_float2(d[nt][2], d[nt][3]);
-  }
 }
 
 // The chunk's Gram matrices on the tensor cores, one warp:
@@ -460,15 +467,16 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
       // (1) log retentions ls = W_SCALE sigmoid(w), an item (t, j) per lane,
       //     into the W region (free until W is written)
       float* Gs = P + K::P_W;
-      constexpr int ITEMS = L * N / 32;
-      {
-        float lw[ITEMS];
+      constexpr int ITEMS = L * N / 32;  // a multiple of 4
+#pragma unroll 1
+      for (int i0 = 0; i0 < ITEMS; i0 += 4) {
+        float lw[4];
 #pragma unroll
-        for (int it = 0; it < ITEMS; ++it) lw[it] = R[1 * L * N + lane + 32 * it];
+        for (int u = 0; u < 4; ++u) lw[u] = R[1 * L * N + lane + 32 * (i0 + u)];
 #pragma unroll
-        for (int it = 0; it < ITEMS; ++it) {
-          const int e = lane + 32 * it, t = e / N;
-          Gs[t * LD + (e - t * N)] = sel(t < Tc, W_SCALE * sigmoidf_fast(lw[it]), 0.f);
+        for (int u = 0; u < 4; ++u) {
+          const int e = lane + 32 * (i0 + u), t = e / N;
+          Gs[t * LD + (e - t * N)] = sel(t < Tc, W_SCALE * sigmoidf_fast(lw[u]), 0.f);
         }
       }
       __syncwarp();
@@ -485,29 +493,25 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         P[K::P_G + j] = __expf(x[L - 1]);
       }
       __syncwarp();
-      // (3) scaled vectors, the lane's items in two unrolled halves
+      // (3) scaled vectors, four items per lane and step
+#pragma unroll 1
+      for (int i0 = 0; i0 < ITEMS; i0 += 4) {
+        float G[4], Gp[4], ra[4], rb[4], rk[4], rr[4], rv[4];
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        constexpr int HI = (ITEMS + 1) / 2;
-        float G[HI], Gp[HI], ra[HI], rb[HI], rk[HI], rr[HI], rv[HI];
-#pragma unroll
-        for (int u = 0; u < HI; ++u) {
-          const int it = min(hf * HI + u, ITEMS - 1);  // past the end: a repeat, not stored
-          const int e = lane + 32 * it, t = e / N, j = e - t * N;
+        for (int u = 0; u < 4; ++u) {
+          const int e = lane + 32 * (i0 + u), t = e / N, j = e - t * N;
           const bool live = t < Tc;
           G[u] = Gs[t * LD + j];
-          Gp[u] = t > 0 ? Gs[(t - 1) * LD + j] : 0.f;
-          rr[u] = live ? R[e] : 0.f;
-          rk[u] = live ? R[2 * L * N + e] : 0.f;
-          rv[u] = live ? R[3 * L * N + e] : 0.f;
-          ra[u] = live ? R[4 * L * N + e] : 0.f;
-          rb[u] = live ? R[5 * L * N + e] : 0.f;
+          Gp[u] = sel(t > 0, Gs[max(t - 1, 0) * LD + j], 0.f);
+          rr[u] = sel(live, R[e], 0.f);
+          rk[u] = sel(live, R[2 * L * N + e], 0.f);
+          rv[u] = sel(live, R[3 * L * N + e], 0.f);
+          ra[u] = sel(live, R[4 * L * N + e], 0.f);
+          rb[u] = sel(live, R[5 * L * N + e], 0.f);
         }
 #pragma unroll
-        for (int u = 0; u < HI; ++u) {
-          const int it = hf * HI + u;
-          if (it >= ITEMS) break;
-          const int e = lane + 32 * it, t = e / N, j = e - t * N;
+        for (int u = 0; u < 4; ++u) {
+          const int e = lane + 32 * (i0 + u), t = e / N, j = e - t * N;
           const float gam = __expf(G[u]), ginv = __expf(-G[u]), gprev = __expf(Gp[u]);
           X[K::X_A + t * LD + j] = ra[u] * gprev;  // gamma_{t-1} a_t
           P[K::P_B + t * LD + j] = rb[u] * ginv;   // b_t / gamma_t
@@ -551,14 +555,15 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         const float* Mrk = Mrb + L * GL;
         float* TLak = X + K::X_T;
         float* M2 = TLak + L * GL;
-        prep_mma16<16, GL, GL>(Tm, Lak, nullptr, nullptr, nullptr, TLak);
-        prep_mma16<N, LD, GL>(Tm, X + K::X_A, nullptr, nullptr, nullptr, P + K::P_W);
+        const PrepProd none{nullptr, nullptr, nullptr, nullptr};
+        prep_mma<16, GL, GL, 1>({Tm, Lak, nullptr, TLak}, none);
+        prep_mma<N, LD, GL, 1>({Tm, X + K::X_A, nullptr, P + K::P_W}, none);
         __syncwarp();
-        prep_mma16<16, GL, GL>(Mrb, TLak, nullptr, nullptr, Mrk, M2);
-        prep_mma16<N, LD, GL>(Mrb, P + K::P_W, nullptr, nullptr, X + K::X_R, P + K::P_Q);
-        prep_mma16<N, LD, GL>(TLak, P + K::P_V, nullptr, nullptr, nullptr, P + K::P_U);
+        prep_mma<16, GL, GL, 1>({Mrb, TLak, Mrk, M2}, none);
+        prep_mma<N, LD, GL, 1>({Mrb, P + K::P_W, X + K::X_R, P + K::P_Q}, none);
+        prep_mma<N, LD, GL, 1>({TLak, P + K::P_V, nullptr, P + K::P_U}, none);
         __syncwarp();
-        prep_mma16<N, LD, GL>(M2, P + K::P_V, nullptr, nullptr, nullptr, P + K::P_YU);
+        prep_mma<N, LD, GL, 1>({M2, P + K::P_V, nullptr, P + K::P_YU}, none);
       }
       __syncwarp();
       mbar_arrive(&prep_full[ps]);
@@ -631,6 +636,29 @@ static yuf_status_t launch_ctc(const float* const (&src)[6], const float* s0, fl
 }
 
 bool wkv7_chunk_tc_supports(int N) { return N == 16 || N == 32 || N == 40 || N == 48 || N == 64; }
+
+// One CTA per (sequence, head) walks the whole sequence, so this kernel wins
+// once the chains fill the SMs: measured on B200 at T = 2048, N = 40 it takes
+// 0.89x the time-parallel scan's time at B*H = 128 (one 86 %-full wave) but 2x
+// at B*H = 32; at T = 8192, N = 64, B*H = 128 0.98x.  Taken for T >= 256 when
+// the waves of CTAs are at least 85 % full.
+bool wkv7_chunk_tc_applies(int B, int T, int H, int N) {
+  if (T < 256 || !wkv7_chunk_tc_supports(N)) return false;
+  static int sms[128];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dev &= 127;
+  if (sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      return false;
+    }
+    sms[dev] = n;
+  }
+  const long long bh = (long long)B * H, waves = (bh + sms[dev] - 1) / sms[dev];
+  return bh * 100 >= 85 * waves * sms[dev];
+}
 
 // Chunked tensor-core scan of [B, T, H, N] inputs from s0 (nullable), writing y
 // and the final state (nullable).  Inputs 16-byte aligned.
