@@ -16,9 +16,9 @@ NCCL only for the start/stop barrier and the max-over-ranks time).
 * ``roofline``  the scan's algorithmic bytes (6 inputs + y per (b,t,h):
               7*N*4 B; plus the final state N*N*4 per (b,h)) over the measured
               time of one step, against the measured HBM copy bandwidth.  At
-              this shape the step is the time-parallel scan: three launches,
-              wkv7_pairw_kernel<40> (chunk summaries), wkv7_carry_kernel<40>
-              (carried states) and wkv7_correct_kernel<40> (output correction).
+              this shape (B*H = 128 chains, one 86 %-full wave of CTAs) AUTO runs
+              the chunked tensor-core scan: one launch of
+              wkv7_chunk_tc_kernel<40> per step.
 * ``cpu_baseline``  the C restatement of the reference recurrence
               (oracle/scans_ref.c, OpenMP over (b,h)) on this host's cores;
               ``cpu_baseline_model`` the whole 0.1B model through the numpy port
@@ -45,7 +45,8 @@ top-level keys.  Both ports are faster than the reference's PyTorch CPU
 fallback (a Python loop of einsums per token), so they are stronger baselines.
 
 ``--only headline`` runs just the config-2 steps (the command the profiles'
-ncu captures use); ``--only model`` just one rank's config-3 prefill and
+ncu captures use); ``--only scans`` every scan algorithm once on config 2;
+``--only model`` just one rank's config-3 prefill and
 config-4 decode step timings (fp32 and bf16 weights); ``--only prefill`` /
 ``--only decode`` just the bf16-weight config-3 prefill / config-4 decode step;
 ``--only c5`` one rank's config-5 prefill (8 sequences of 8192 tokens).
@@ -71,7 +72,7 @@ ALGO_BYTES = B * T * H * 7 * N * 4 + B * H * N * N * 4
 METRIC = "wkv7_scan_prefill_tokens_per_s"
 UNIT = "tokens/s"
 WORKLOAD = "config2_wkv7_scan_op_B8_T2048_H16_N40_fp32"
-LAUNCHES_PER_STEP = 3  # time-parallel scan: chunk summaries, carry, output correction
+LAUNCHES_PER_STEP = 1  # the chunked tensor-core scan (AUTO at B*H = 128)
 
 
 def parse():
@@ -80,7 +81,8 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--only", choices=["all", "headline", "model", "prefill", "decode", "c5"], default="all")
+    p.add_argument("--only", choices=["all", "headline", "scans", "model", "prefill", "decode", "c5"],
+                   default="all")
     return p.parse_args()
 
 
@@ -107,9 +109,9 @@ def bf16_peak():
 
 
 def profiled_traffic():
-    """DRAM bytes of one headline step (all of its kernels) from the committed
-    ncu summary of the time-parallel scan on the config-2 workload."""
-    f = ROOT / "profiles" / "wkv7_time_parallel_config2.txt"
+    """DRAM bytes of one headline step from the committed ncu summary of the
+    chunked tensor-core scan on the config-2 workload."""
+    f = ROOT / "profiles" / "wkv7_chunk_tc_config2.txt"
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
@@ -225,6 +227,34 @@ def _time(fn, n, dev, stream, warm=3):
     return e0.elapsed_time(e1) / n
 
 
+SCAN_ALGOS = (("sequential", "ALGO_SEQUENTIAL"), ("chunked16", "ALGO_CHUNKED"),
+              ("time_parallel", "ALGO_PARALLEL"), ("rows", "ALGO_ROWS"), ("chunked_tc", "ALGO_CHUNKED_TC"))
+
+
+def measure_scans(dev, stream, args):
+    """Every WKV-7 scan algorithm on the headline workload (config 2), each
+    called explicitly (``--only scans``; the profiles' captures of the kernels
+    that AUTO does not pick at this shape use it)."""
+    import torch
+
+    from yufmusicgen_b200 import cuda_ops
+    from yufmusicgen_b200.workloads import wkv_op_inputs
+
+    out = {}
+    n = max(5, min(args.steps, 50))
+    ins = wkv_op_inputs(B, T, H, N, seed=0)
+    d = {k: torch.from_numpy(ins[k]).to(dev) for k in "rwkvab"}
+    y = torch.empty_like(d["r"])
+    s = torch.empty(B, H, N, N, device=dev)
+    for name, algo in SCAN_ALGOS:
+        a = getattr(cuda_ops, algo)
+        ms = _time(lambda: cuda_ops.wkv7_forward(*(d[k] for k in "rwkvab"), None, out=y, state_out=s,
+                                                 algo=a), n, dev, stream)
+        out[f"wkv7_{name}_config2"] = {"ms": ms, "GBps": ALGO_BYTES / ms / 1e6}
+    del d, y, s
+    return out
+
+
 def measure_extras(dev, stream, args):
     """Secondary kernels of the hot path, timed on rank 0 (not the headline)."""
     import torch
@@ -233,23 +263,9 @@ def measure_extras(dev, stream, args):
     from yufmusicgen_b200.workloads import rosa_op_inputs, wkv_op_inputs
 
     peak, _ = peaks()
-    out = {}
     n = max(5, min(args.steps, 50))
-    # the sequential kernel on the headline workload, for comparison
-    ins = wkv_op_inputs(B, T, H, N, seed=0)
-    d = {k: torch.from_numpy(ins[k]).to(dev) for k in "rwkvab"}
-    y = torch.empty_like(d["r"])
-    s = torch.empty(B, H, N, N, device=dev)
-    ms = _time(lambda: cuda_ops.wkv7_forward(*(d[k] for k in "rwkvab"), None, out=y, state_out=s,
-                                             algo=cuda_ops.ALGO_SEQUENTIAL), n, dev, stream)
-    out["wkv7_sequential_config2"] = {"ms": ms, "GBps": ALGO_BYTES / ms / 1e6}
-    ms = _time(lambda: cuda_ops.wkv7_forward(*(d[k] for k in "rwkvab"), None, out=y, state_out=s,
-                                             algo=cuda_ops.ALGO_CHUNKED), n, dev, stream)
-    out["wkv7_chunked16_config2"] = {"ms": ms, "GBps": ALGO_BYTES / ms / 1e6}
-    ms = _time(lambda: cuda_ops.wkv7_forward(*(d[k] for k in "rwkvab"), None, out=y, state_out=s,
-                                             algo=cuda_ops.ALGO_PARALLEL), n, dev, stream)
-    out["wkv7_time_parallel_config2"] = {"ms": ms, "GBps": ALGO_BYTES / ms / 1e6}
-    del d, y, s
+    # every scan algorithm on the headline workload, for comparison
+    out = measure_scans(dev, stream, args)
     # batched decode step: config-4 state shape (256 seqs x 16 heads x N40), T = 1
     Bd = 256
     di = wkv_op_inputs(Bd, 1, H, N, seed=1, with_state=True)
@@ -607,6 +623,9 @@ def run_ours(args):
     if args.only == "c5":
         print(json.dumps({"only": "c5", "c5": measure_c5(dev, 1)}), flush=True)
         return
+    if args.only == "scans":
+        print(json.dumps({"only": "scans", "scans": measure_scans(dev, stream, args)}), flush=True)
+        return
     if args.only in ("model", "prefill", "decode"):
         parts = ("prefill", "decode") if args.only == "model" else (args.only,)
         precs = ("fp32", "bf16") if args.only == "model" else ("bf16",)
@@ -720,9 +739,8 @@ def run_ours(args):
                                "all ranks at once); the scan overlaps it"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "wkv7 time-parallel scan (AUTO at B*H = 128): "
-                                   "wkv7_pairw_kernel<40> + wkv7_carry_kernel<40> + "
-                                   "wkv7_correct_kernel<40>",
+                         "kernel": "wkv7 chunked tensor-core scan (AUTO at B*H = 128): "
+                                   "wkv7_chunk_tc_kernel<40>",
                          "algorithmic_bytes_per_step": ALGO_BYTES},
             "gpu_launches": LAUNCHES_PER_STEP * args.steps,
             "clocks": clocks.summary(),
