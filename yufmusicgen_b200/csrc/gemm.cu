@@ -660,7 +660,10 @@ __global__ void __launch_bounds__(GemmSplitCfg<BN>::THREADS, 1)
   tc_fence_before_sync();
   __syncthreads();
   tc_fence_after_sync();
-  pdl_wait();
+  // The TMA producer thread waits for the previous kernel later, after it has
+  // requested its first weight tiles: the weights are not written by any
+  // kernel of the chain, so their HBM latency overlaps the previous kernel's tail.
+  if (warp != 0 || lane != 0) pdl_wait();
   pdl_trigger();
   const uint32_t tmem = *tslot;
 
@@ -670,7 +673,17 @@ __global__ void __launch_bounds__(GemmSplitCfg<BN>::THREADS, 1)
       uint32_t phase = 0;
       long long issued = 0;
       const int ay = (int)(z * p.a_brows) + mt * G::BM, wy = (int)(z * p.w_brows) + nt * BN;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      const int pre = min(nkb, G::STAGES);  // stages whose weight tile goes out before the wait
+      for (int i = 0; i < pre; ++i) {
+        mbar_expect_tx(&full[i], G::STAGE);
+        tma_load_2d(sm + i * G::STAGE + G::A_BYTES, &tw, &full[i], (kb0 + i) * G::BK, wy);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) tma_load_2d(sm + i * G::STAGE, &ta, &full[i], (kb0 + i) * G::BK, ay);
+      issued = pre;
+      stage = pre % G::STAGES;
+      phase = pre == G::STAGES ? 1u : 0u;
+      for (int kb = kb0 + pre; kb < kb1; ++kb) {
         if (!gemm_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
         unsigned char* st = sm + stage * G::STAGE;
         mbar_expect_tx(&full[stage], G::STAGE);
