@@ -565,59 +565,161 @@ YUF_DEVICE void store4(const GemmParams& p, int z, int row, int col, float4 v) {
 }
 
 // The reduction step of a K split over a cluster: the calling CTA (rank r of
-// ks) sums rows [r * 128 / ks, (r + 1) * 128 / ks) of the ks partial tiles
+// KS) sums rows [r * 128 / KS, (r + 1) * 128 / KS) of the KS partial tiles
 // (fp32, row stride pstride floats, at shared address `pbase` in every CTA) in
 // rank order and applies the epilogue; all `nthreads` threads of the CTA take
-// part.
-template <int BN, int EPI>
-YUF_DEVICE void cluster_reduce_store(const GemmParams& p, uint32_t pbase, int pstride, int ks, int r, int z,
-                                     int mt, int nt, int nthreads) {
+// part.  KS is a template argument so that a thread's KS distributed-shared-
+// memory loads of one element group are all in flight at once (a remote load
+// costs hundreds of cycles; issued one after another they made the reduction
+// the longest phase of a decode-batch GEMM).
+template <int BN, int EPI, int KS, int LOADS>
+YUF_DEVICE void cluster_reduce_store_ks(const GemmParams& p, uint32_t pbase, int pstride, int r, int z, int mt,
+                                        int nt, int nthreads) {
+  constexpr int ks = KS;
   const int rows = 128 / ks, r0 = r * rows;
   if constexpr (EPI == GEMM_EPI_SWIGLU || EPI == GEMM_EPI_SWIGLU_F32) {
     constexpr int QC = BN / 8;  // float4 chunks of "in" columns per row (BN / 2 columns)
-    for (int i = threadIdx.x; i < rows * QC; i += nthreads) {
-      const int rr = r0 + i / QC, j = (i % QC) * 4;  // j: 0 .. BN/2 - 4
-      const int cin = (j / 64) * 128 + j % 64, cgate = cin + 64;
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), g = a;
-      for (int qq = 0; qq < ks; ++qq) {
-        const float4 x = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + cin) * 4), qq));
-        const float4 y = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + cgate) * 4), qq));
-        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
-        g.x += y.x; g.y += y.y; g.z += y.z; g.w += y.w;
+    constexpr int U = 2 * KS >= LOADS ? 1 : LOADS / (2 * KS);  // groups per thread and step (2 U KS loads)
+    const int total = rows * QC;
+    for (int i0 = threadIdx.x; i0 < total; i0 += nthreads * U) {
+      float4 xs[U][KS], ys[U][KS];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = min(i0 + u * nthreads, total - 1);
+        const int rr = r0 + i / QC, j = (i % QC) * 4;
+        const int cin = (j / 64) * 128 + j % 64, cgate = cin + 64;
+#pragma unroll
+        for (int qq = 0; qq < KS; ++qq) {
+          xs[u][qq] = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + cin) * 4), qq));
+          ys[u][qq] = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + cgate) * 4), qq));
+        }
       }
-      const int row = mt * 128 + rr, col = nt * (BN / 2) + j;
-      if (row >= p.M) continue;
-      const float h[4] = {silu(a.x) * g.x, silu(a.y) * g.y, silu(a.z) * g.z, silu(a.w) * g.w};
-      const bool full = p.vec && col + 4 <= p.n_out;
-      if constexpr (EPI == GEMM_EPI_SWIGLU_F32) {
-        float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
-        if (full) *reinterpret_cast<float4*>(out + col) = make_float4(h[0], h[1], h[2], h[3]);
-        else
-          for (int c = 0; c < 4; ++c)
-            if (col + c < p.n_out) out[col + c] = h[c];
-      } else {
-        __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
-        if (full) {
-          uint2 pk;
-          reinterpret_cast<__nv_bfloat162*>(&pk)[0] = __floats2bfloat162_rn(h[0], h[1]);
-          reinterpret_cast<__nv_bfloat162*>(&pk)[1] = __floats2bfloat162_rn(h[2], h[3]);
-          *reinterpret_cast<uint2*>(out + col) = pk;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * nthreads;
+        if (i >= total) break;
+        const int rr = r0 + i / QC, j = (i % QC) * 4;  // j: 0 .. BN/2 - 4
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), g = a;
+#pragma unroll
+        for (int qq = 0; qq < KS; ++qq) {
+          a.x += xs[u][qq].x; a.y += xs[u][qq].y; a.z += xs[u][qq].z; a.w += xs[u][qq].w;
+          g.x += ys[u][qq].x; g.y += ys[u][qq].y; g.z += ys[u][qq].z; g.w += ys[u][qq].w;
+        }
+        const int row = mt * 128 + rr, col = nt * (BN / 2) + j;
+        if (row >= p.M) continue;
+        const float h[4] = {silu(a.x) * g.x, silu(a.y) * g.y, silu(a.z) * g.z, silu(a.w) * g.w};
+        const bool full = p.vec && col + 4 <= p.n_out;
+        if constexpr (EPI == GEMM_EPI_SWIGLU_F32) {
+          float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+          if (full) *reinterpret_cast<float4*>(out + col) = make_float4(h[0], h[1], h[2], h[3]);
+          else
+            for (int c = 0; c < 4; ++c)
+              if (col + c < p.n_out) out[col + c] = h[c];
         } else {
-          for (int c = 0; c < 4; ++c)
-            if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(h[c]);
+          __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+          if (full) {
+            uint2 pk;
+            reinterpret_cast<__nv_bfloat162*>(&pk)[0] = __floats2bfloat162_rn(h[0], h[1]);
+            reinterpret_cast<__nv_bfloat162*>(&pk)[1] = __floats2bfloat162_rn(h[2], h[3]);
+            *reinterpret_cast<uint2*>(out + col) = pk;
+          } else {
+            for (int c = 0; c < 4; ++c)
+              if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(h[c]);
+          }
         }
       }
     }
   } else {
     constexpr int QC = BN / 4;
+    constexpr int U = KS >= LOADS ? 1 : LOADS / KS;  // groups per thread and step (U KS loads in flight)
+    const int total = rows * QC;
+    for (int i0 = threadIdx.x; i0 < total; i0 += nthreads * U) {
+      float4 xs[U][KS];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = min(i0 + u * nthreads, total - 1);
+        const int rr = r0 + i / QC, c = (i % QC) * 4;
+#pragma unroll
+        for (int qq = 0; qq < KS; ++qq)
+          xs[u][qq] = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + c) * 4), qq));
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * nthreads;
+        if (i >= total) break;
+        const int rr = r0 + i / QC, c = (i % QC) * 4;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int qq = 0; qq < KS; ++qq) {
+          a.x += xs[u][qq].x; a.y += xs[u][qq].y; a.z += xs[u][qq].z; a.w += xs[u][qq].w;
+        }
+        const int row = mt * 128 + rr, col = nt * BN + c;
+        if (row < p.M && col < p.N) store4<EPI>(p, z, row, col, a);
+      }
+    }
+  }
+}
+
+// LOADS: distributed-shared-memory loads a thread keeps in flight (fewer for
+// register-heavy callers).
+template <int BN, int EPI, int LOADS = 8>
+YUF_DEVICE void cluster_reduce_store(const GemmParams& p, uint32_t pbase, int pstride, int ks, int r, int z,
+                                     int mt, int nt, int nthreads) {
+  switch (ks) {
+    case 1: cluster_reduce_store_ks<BN, EPI, 1, LOADS>(p, pbase, pstride, r, z, mt, nt, nthreads); break;
+    case 2: cluster_reduce_store_ks<BN, EPI, 2, LOADS>(p, pbase, pstride, r, z, mt, nt, nthreads); break;
+    case 4: cluster_reduce_store_ks<BN, EPI, 4, LOADS>(p, pbase, pstride, r, z, mt, nt, nthreads); break;
+    default: cluster_reduce_store_ks<BN, EPI, 8, LOADS>(p, pbase, pstride, r, z, mt, nt, nthreads); break;
+  }
+}
+
+// The epilogue from this CTA's own shared memory: `recv` holds ks slices of
+// 128 / ks rows (slice q at q * (128 / ks) rows, rows of pstride floats), summed
+// in slice order -- the order of cluster_reduce_store -- for rows
+// [r * 128 / ks, ...) of the tile.  With ks = 1 (no K split) it is the whole
+// tile straight from the partial, without distributed-shared-memory loads or
+// cluster barriers.
+template <int BN, int EPI>
+YUF_DEVICE void local_reduce_store(const GemmParams& p, const float* recv, int pstride, int ks, int r, int z,
+                                   int mt, int nt, int nthreads) {
+  const int rows = 128 / ks, r0 = r * rows;
+  const int slice = rows * pstride;
+  if constexpr (EPI == GEMM_EPI_SWIGLU) {
+    constexpr int QC = BN / 8;
     for (int i = threadIdx.x; i < rows * QC; i += nthreads) {
-      const int rr = r0 + i / QC, c = (i % QC) * 4;
+      const int lr = i / QC, j = (i % QC) * 4;
+      const int cin = (j / 64) * 128 + j % 64, cgate = cin + 64;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), g = a;
+      for (int qq = 0; qq < ks; ++qq) {
+        const float4 x = *reinterpret_cast<const float4*>(recv + qq * slice + lr * pstride + cin);
+        const float4 y = *reinterpret_cast<const float4*>(recv + qq * slice + lr * pstride + cgate);
+        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+        g.x += y.x; g.y += y.y; g.z += y.z; g.w += y.w;
+      }
+      const int row = mt * 128 + r0 + lr, col = nt * (BN / 2) + j;
+      if (row >= p.M) continue;
+      const float h[4] = {silu(a.x) * g.x, silu(a.y) * g.y, silu(a.z) * g.z, silu(a.w) * g.w};
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
+      if (p.vec && col + 4 <= p.n_out) {
+        uint2 pk;
+        reinterpret_cast<__nv_bfloat162*>(&pk)[0] = __floats2bfloat162_rn(h[0], h[1]);
+        reinterpret_cast<__nv_bfloat162*>(&pk)[1] = __floats2bfloat162_rn(h[2], h[3]);
+        *reinterpret_cast<uint2*>(out + col) = pk;
+      } else {
+        for (int c = 0; c < 4; ++c)
+          if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(h[c]);
+      }
+    }
+  } else {
+    constexpr int QC = BN / 4;
+    for (int i = threadIdx.x; i < rows * QC; i += nthreads) {
+      const int lr = i / QC, c = (i % QC) * 4;
       float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int qq = 0; qq < ks; ++qq) {
-        const float4 x = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + c) * 4), qq));
+        const float4 x = *reinterpret_cast<const float4*>(recv + qq * slice + lr * pstride + c);
         a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
       }
-      const int row = mt * 128 + rr, col = nt * BN + c;
+      const int row = mt * 128 + r0 + lr, col = nt * BN + c;
       if (row < p.M && col < p.N) store4<EPI>(p, z, row, col, a);
     }
   }
@@ -740,11 +842,16 @@ __global__ void __launch_bounds__(GemmSplitCfg<BN>::THREADS, 1)
     }
   }
   tc_fence_before_sync();
-  cluster_sync();  // every CTA's partial is in its shared memory
-  // reduce rows [r * 128 / ks, (r + 1) * 128 / ks) over the ks partials, in rank order
-  cluster_reduce_store<BN, EPI>(p, smem_u32(part), G::PSTRIDE, ks, r, z, mt, nt, G::THREADS);
+  if (ks > 1) {
+    cluster_sync();  // every CTA's partial is in its shared memory
+    // reduce rows [r * 128 / ks, (r + 1) * 128 / ks) over the ks partials, in rank order
+    cluster_reduce_store<BN, EPI>(p, smem_u32(part), G::PSTRIDE, ks, r, z, mt, nt, G::THREADS);
+    cluster_sync();  // no CTA leaves while a peer may still read its partial
+  } else {
+    __syncthreads();  // no split: the whole tile from this CTA's own shared memory
+    local_reduce_store<BN, EPI>(p, part, G::PSTRIDE, 1, 0, z, mt, nt, G::THREADS);
+  }
   if (threadIdx.x == 0 && *abort_flag) atomicAdd(&g_gemm_wait_timeouts, 1u);
-  cluster_sync();  // no CTA leaves while a peer may still read its partial
   if (warp == 1) {
     tc_fence_after_sync();
     tmem_dealloc(tmem, G::TMEM_COLS);
@@ -972,7 +1079,7 @@ __global__ void __launch_bounds__(GemmTf32Cfg<BN>::THREADS, 1)
   tc_fence_before_sync();
   if (ks > 1) {
     cluster_sync();  // every CTA's partial is in its shared memory
-    cluster_reduce_store<BN, EPI>(p, smem_u32(part), G::PSTRIDE, ks, r, z, mt, nt, G::THREADS);
+    cluster_reduce_store<BN, EPI, 2>(p, smem_u32(part), G::PSTRIDE, ks, r, z, mt, nt, G::THREADS);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicAdd(&g_gemm_wait_timeouts, 1u);
   cluster_sync();  // no CTA leaves while a peer may still read its partial

@@ -123,6 +123,7 @@ YUF_DEVICE float4 ld_shared_cluster_f4(uint32_t cluster_addr) {
 YUF_DEVICE void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+
 // TMEM of the pair: one warp with the same warp index in each CTA
 YUF_DEVICE void tmem_alloc_pair(uint32_t* slot, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
