@@ -34,12 +34,13 @@
 //     accumulator columns are its two k slots), y stored to global, SA staged
 //     through a warp-private scratch as the A operand of dS, S updated in fp32;
 //   * NP prep warps, each preparing a whole chunk (chunks round-robin): the
-//     scaled vectors, the four Gram matrices, the substitution for W and U, and
-//     Q and YU, on the fp32 FMA pipe while the scan warps hold the tensor pipe;
-//   * one loader warp: six TMA boxes (N columns x 16 tokens, one per input) per
-//     chunk into a ring of raw slots.
-// Rings: raw slots (full: TMA bytes; empty: the prep warp's 32 lanes) and
-// prepared slots (full: the prep warp's 32 lanes; empty: every scan lane).
+//     scaled vectors in place of the staged inputs, the four Gram matrices and
+//     the products W, Q, U, YU on mma.sync (3xTF32), T by forward substitution;
+//   * one loader warp: six TMA boxes (LD columns x 16 tokens, one per input) per
+//     chunk straight into the chunk's slot.
+// One ring of NB chunk slots: tma_full (the boxes' bytes), prep_full (the prep
+// warp's 32 lanes), slot_empty (every scan lane).  A slot is loaded, prepared
+// in place and scanned, so one chunk in flight costs one slot.
 // Every wait is bounded; a timed-out wait counts in g_ctc_wait_timeouts and the
 // CTA leaves after its TMA copies in flight have landed.
 // Inputs are read once, y written once, the state read and written once.
@@ -68,32 +69,31 @@ struct CtcCfg {
   static constexpr int L = CTC_L;
   static constexpr int LD = ctc_ld(N);
   static constexpr int NS = (N + 15) / 16;     // scan warps
-  static constexpr int NP = LD <= 40 ? 4 : 2;  // prep warps
-  static constexpr int NR = NP + 1;            // raw slots
-  static constexpr int NB = NP + 1;            // prepared slots
+  static constexpr int NP = LD <= 40 ? 5 : 3;  // prep warps
+  static constexpr int NB = LD <= 40 ? NP + 2 : NP + 1;  // chunk slots: NP in prep, one scanned (+ one loading)
   static constexpr int NT = 32 * (NS + NP + 1);
   static constexpr int NJ = N / 8;             // 8-column tiles
   static constexpr int GL = L + 4;             // Gram row stride (= 20 mod 32: conflict-free fragments)
   static constexpr int SLD = 24;               // SA scratch row stride (= 24 mod 32: conflict free)
-  // raw slot: r, w, k, v, a, b as [L][N] each (the TMA boxes)
-  static constexpr int RAW = 6 * L * N;
-  // prepared slot: W, Q, U, YU, B~, K~, V as [L][LD], gamma_15 as [LD]
-  static constexpr int P_W = 0, P_Q = L * LD, P_U = 2 * L * LD, P_YU = 3 * L * LD, P_B = 4 * L * LD,
-                       P_K = 5 * L * LD, P_V = 6 * L * LD, P_G = 7 * L * LD;
-  static constexpr int PREP = (P_G + LD + 31) / 32 * 32;
-  // prep warp scratch: a~, r~ as [L][LD]; Lab (then T), Lak, Mrb, Mrk, T Lak,
-  // Mrb T Lak + Mrk as [L][GL]
-  static constexpr int X_A = 0, X_R = L * LD, X_G = 2 * L * LD, X_T = X_G + 4 * L * GL;
-  static constexpr int XS = (X_T + 2 * L * GL + 31) / 32 * 32;
-  static constexpr int OFF_PREP = NR * RAW;
-  static constexpr int OFF_X = OFF_PREP + NB * PREP;
+  // A chunk slot, rows of LD floats: the six TMA boxes (LD columns x L tokens:
+  // r, w, k, v, a, b), transformed in place into r~, the log-decay running sums,
+  // k~, v, a~, b~; then W, Q, U, YU; gamma_15.
+  static constexpr int S_R = 0, S_W = L * LD, S_K = 2 * L * LD, S_V = 3 * L * LD, S_A = 4 * L * LD,
+                       S_B = 5 * L * LD, P_W = 6 * L * LD, P_Q = 7 * L * LD, P_U = 8 * L * LD,
+                       P_YU = 9 * L * LD, P_G = 10 * L * LD;
+  static constexpr int SLOT = (P_G + LD + 31) / 32 * 32;
+  // prep warp scratch: Lab (then T), Lak, Mrb, Mrk, T Lak, Mrb T Lak + Mrk as [L][GL]
+  static constexpr int X_G = 0, X_T = 4 * L * GL;
+  static constexpr int XS = (6 * L * GL + 31) / 32 * 32;
+  static constexpr int OFF_X = NB * SLOT;
   static constexpr int OFF_SA = OFF_X + NP * XS;
   static constexpr int OFF_BAR = OFF_SA + NS * L * SLD;
-  static constexpr int NBAR = 2 * NR + 2 * NB;
+  static constexpr int NBAR = 3 * NB;
   static constexpr size_t BYTES = (size_t)OFF_BAR * 4 + NBAR * 8;
-  static constexpr uint32_t TX = 6u * L * N * 4;
+  static constexpr uint32_t TX = 6u * L * LD * 4;
   static_assert(N % 8 == 0 && N <= 64, "chunked tensor-core scan: N a multiple of 8, at most 64");
-  static_assert((L * N * 4) % 128 == 0 && RAW % 32 == 0, "TMA boxes on 128-byte boundaries");
+  static_assert((L * LD * 4) % 128 == 0 && SLOT % 32 == 0, "TMA boxes on 128-byte boundaries");
+  static_assert(LD <= 256 && (LD * 4) % 16 == 0, "TMA box width");
   static_assert(OFF_BAR % 2 == 0, "mbarriers 8-byte aligned");
   static_assert(BYTES <= 227 * 1024, "shared memory");
 };
@@ -270,14 +270,13 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
     wkv7_chunk_tc_kernel(const float* __restrict__ s0, float* __restrict__ y, float* __restrict__ s_out, int T,
                          int H, const __grid_constant__ CtcTmaps tm) {
   using K = CtcCfg<N>;
-  constexpr int L = K::L, LD = K::LD, NS = K::NS, NP = K::NP, NR = K::NR, NB = K::NB, NJ = K::NJ;
+  constexpr int L = K::L, LD = K::LD, NS = K::NS, NP = K::NP, NB = K::NB, NJ = K::NJ;
   constexpr int GL = K::GL, SLD = K::SLD;
   extern __shared__ __align__(128) float ctc_smem[];
   float* sm = ctc_smem;
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(sm + K::OFF_BAR);
-  uint64_t* raw_empty = raw_full + NR;
-  uint64_t* prep_full = raw_empty + NR;
-  uint64_t* prep_empty = prep_full + NB;
+  uint64_t* tma_full = reinterpret_cast<uint64_t*>(sm + K::OFF_BAR);  // [NB] the slot's boxes landed
+  uint64_t* prep_full = tma_full + NB;                                 // [NB] the slot is prepared
+  uint64_t* slot_empty = prep_full + NB;                               // [NB] the scan is done with it
   __shared__ int abort_flag;
 
   const int bh = blockIdx.x;
@@ -285,13 +284,10 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nchunks = (T + L - 1) / L;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NR; ++s) {
-      mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 32);
-    }
     for (int s = 0; s < NB; ++s) {
+      mbar_init(&tma_full[s], 1);
       mbar_init(&prep_full[s], 32);
-      mbar_init(&prep_empty[s], 32 * NS);
+      mbar_init(&slot_empty[s], 32 * NS);
     }
     abort_flag = 0;
     fence_mbar_init();
@@ -324,7 +320,7 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         if (lane == 0) ctc_abort(&abort_flag);
         break;
       }
-      const float* P = sm + K::OFF_PREP + slot * K::PREP;
+      const float* P = sm + slot * K::SLOT;
       // SA^T and Y^T for this warp's rows: M = token, N = state row, K = column
       float sa[2][4], yy[2][4];
 #pragma unroll
@@ -400,13 +396,13 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         const int ta = 8 * kk + q, tb = ta + 4;
         uint32_t sah[4], sal[4], vh[4], val[4];
         split_a({SA[ta * SLD + g], SA[ta * SLD + g + 8], SA[tb * SLD + g], SA[tb * SLD + g + 8]}, sah, sal);
-        const float* V = P + K::P_V + i0 + g;
+        const float* V = P + K::S_V + i0 + g;
         split_a({V[ta * LD], h1 ? V[ta * LD + 8] : 0.f, V[tb * LD], h1 ? V[tb * LD + 8] : 0.f}, vh, val);
         uint32_t bbh[NJ][2], bbl[NJ][2], kh[NJ][2], kl[NJ][2];
 #pragma unroll
         for (int c2 = 0; c2 < NJ; ++c2) {
-          split_b(P[K::P_B + ta * LD + 8 * c2 + g], P[K::P_B + tb * LD + 8 * c2 + g], bbh[c2], bbl[c2]);
-          split_b(P[K::P_K + ta * LD + 8 * c2 + g], P[K::P_K + tb * LD + 8 * c2 + g], kh[c2], kl[c2]);
+          split_b(P[K::S_B + ta * LD + 8 * c2 + g], P[K::S_B + tb * LD + 8 * c2 + g], bbh[c2], bbl[c2]);
+          split_b(P[K::S_K + ta * LD + 8 * c2 + g], P[K::S_K + tb * LD + 8 * c2 + g], kh[c2], kl[c2]);
         }
         // term by term across the column tiles (independent accumulators back to back)
 #pragma unroll
@@ -431,7 +427,7 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         S[c2][3] = (S[c2][3] + dS[c2][3]) * gm.y;
       }
       __syncwarp();
-      mbar_arrive(&prep_empty[slot]);
+      mbar_arrive(&slot_empty[slot]);
     }
     if (s_out && !*abort_v) {
 #pragma unroll
@@ -448,31 +444,33 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
     const int p = warp - NS;
     float* X = sm + K::OFF_X + p * K::XS;
     for (int c = p; c < nchunks; c += NP) {
-      const int rs = c % NR, ps = c % NB;
-      bool ok = mbar_wait(&raw_full[rs], (uint32_t)(c / NR) & 1u) &&
-                mbar_wait(&prep_empty[ps], ((uint32_t)(c / NB) & 1u) ^ 1u);
-      ok = __all_sync(0xffffffffu, ok);
+      const int ps = c % NB;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tma_full[ps], (uint32_t)(c / NB) & 1u));
       if (!ok || *abort_v) {
         if (lane == 0) ctc_abort(&abort_flag);
         break;
       }
-      const float* R = sm + rs * K::RAW;  // r, w, k, v, a, b: [L][N]
-      float* P = sm + K::OFF_PREP + ps * K::PREP;
+      float* P = sm + ps * K::SLOT;  // the boxes r, w, k, v, a, b as [L][LD], transformed in place
       const int Tc = min(L, T - c * L);
-      // Loads are grouped ahead of the stores of each step below: the raw,
-      // scratch and prepared regions all live in one shared array, so the
-      // compiler could not move a load above a preceding store.  Loops are
-      // kept rolled where that costs no parallelism, so that the scan and prep
-      // code together stay small in the instruction caches.
+      // Loads are grouped ahead of the stores of each step below: the slot and
+      // the scratch live in one shared array, so the compiler could not move a
+      // load above a preceding store.  Loops are kept rolled where that costs
+      // no parallelism, so that the scan and prep code together stay small in
+      // the instruction caches.  Every step below touches item (t, j) of the
+      // slot from the same lane that reads it, so the in-place transforms are
+      // race free.
       // (1) log retentions ls = W_SCALE sigmoid(w), an item (t, j) per lane,
-      //     into the W region (free until W is written)
-      float* Gs = P + K::P_W;
+      //     in place of w
+      float* Gs = P + K::S_W;
       constexpr int ITEMS = L * N / 32;  // a multiple of 4
 #pragma unroll 1
       for (int i0 = 0; i0 < ITEMS; i0 += 4) {
         float lw[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) lw[u] = R[1 * L * N + lane + 32 * (i0 + u)];
+        for (int u = 0; u < 4; ++u) {
+          const int e = lane + 32 * (i0 + u), t = e / N;
+          lw[u] = Gs[t * LD + (e - t * N)];
+        }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int e = lane + 32 * (i0 + u), t = e / N;
@@ -493,37 +491,37 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         P[K::P_G + j] = __expf(x[L - 1]);
       }
       __syncwarp();
-      // (3) scaled vectors, four items per lane and step
+      // (3) scaled vectors in place, four items per lane and step (tokens past
+      //     the sequence's end become zeros)
 #pragma unroll 1
       for (int i0 = 0; i0 < ITEMS; i0 += 4) {
         float G[4], Gp[4], ra[4], rb[4], rk[4], rr[4], rv[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int e = lane + 32 * (i0 + u), t = e / N, j = e - t * N;
+          const int e = lane + 32 * (i0 + u), t = e / N, o = t * LD + (e - t * N);
           const bool live = t < Tc;
-          G[u] = Gs[t * LD + j];
-          Gp[u] = sel(t > 0, Gs[max(t - 1, 0) * LD + j], 0.f);
-          rr[u] = sel(live, R[e], 0.f);
-          rk[u] = sel(live, R[2 * L * N + e], 0.f);
-          rv[u] = sel(live, R[3 * L * N + e], 0.f);
-          ra[u] = sel(live, R[4 * L * N + e], 0.f);
-          rb[u] = sel(live, R[5 * L * N + e], 0.f);
+          G[u] = Gs[o];
+          Gp[u] = sel(t > 0, Gs[o - (t > 0 ? LD : 0)], 0.f);
+          rr[u] = sel(live, P[K::S_R + o], 0.f);
+          rk[u] = sel(live, P[K::S_K + o], 0.f);
+          rv[u] = sel(live, P[K::S_V + o], 0.f);
+          ra[u] = sel(live, P[K::S_A + o], 0.f);
+          rb[u] = sel(live, P[K::S_B + o], 0.f);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int e = lane + 32 * (i0 + u), t = e / N, j = e - t * N;
+          const int e = lane + 32 * (i0 + u), t = e / N, o = t * LD + (e - t * N);
           const float gam = __expf(G[u]), ginv = __expf(-G[u]), gprev = __expf(Gp[u]);
-          X[K::X_A + t * LD + j] = ra[u] * gprev;  // gamma_{t-1} a_t
-          P[K::P_B + t * LD + j] = rb[u] * ginv;   // b_t / gamma_t
-          P[K::P_K + t * LD + j] = rk[u] * ginv;   // k_t / gamma_t
-          X[K::X_R + t * LD + j] = rr[u] * gam;    // gamma_t r_t
-          P[K::P_V + t * LD + j] = rv[u];
+          P[K::S_A + o] = ra[u] * gprev;  // gamma_{t-1} a_t
+          P[K::S_B + o] = rb[u] * ginv;   // b_t / gamma_t
+          P[K::S_K + o] = rk[u] * ginv;   // k_t / gamma_t
+          P[K::S_R + o] = rr[u] * gam;    // gamma_t r_t
+          P[K::S_V + o] = rv[u];
         }
       }
       __syncwarp();
-      mbar_arrive(&raw_empty[rs]);  // every lane is done with the raw slot
       // (4) Gram matrices Lab, Lak, Mrb, Mrk (row-major [t][GL])
-      prep_gram<N, LD, GL>(X + K::X_A, X + K::X_R, P + K::P_B, P + K::P_K, X + K::X_G);
+      prep_gram<N, LD, GL>(P + K::S_A, P + K::S_R, P + K::S_B, P + K::S_K, X + K::X_G);
       __syncwarp();
       // (5) T = (I - Lab)^-1 (unit lower triangular), lane c < 16 solving for
       //     column c; T replaces Lab once every lane has read it
@@ -557,13 +555,13 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         float* M2 = TLak + L * GL;
         const PrepProd none{nullptr, nullptr, nullptr, nullptr};
         prep_mma<16, GL, GL, 1>({Tm, Lak, nullptr, TLak}, none);
-        prep_mma<N, LD, GL, 1>({Tm, X + K::X_A, nullptr, P + K::P_W}, none);
+        prep_mma<N, LD, GL, 1>({Tm, P + K::S_A, nullptr, P + K::P_W}, none);
         __syncwarp();
         prep_mma<16, GL, GL, 1>({Mrb, TLak, Mrk, M2}, none);
-        prep_mma<N, LD, GL, 1>({Mrb, P + K::P_W, X + K::X_R, P + K::P_Q}, none);
-        prep_mma<N, LD, GL, 1>({TLak, P + K::P_V, nullptr, P + K::P_U}, none);
+        prep_mma<N, LD, GL, 1>({Mrb, P + K::P_W, P + K::S_R, P + K::P_Q}, none);
+        prep_mma<N, LD, GL, 1>({TLak, P + K::S_V, nullptr, P + K::P_U}, none);
         __syncwarp();
-        prep_mma<N, LD, GL, 1>({M2, P + K::P_V, nullptr, P + K::P_YU}, none);
+        prep_mma<N, LD, GL, 1>({M2, P + K::S_V, nullptr, P + K::P_YU}, none);
       }
       __syncwarp();
       mbar_arrive(&prep_full[ps]);
@@ -572,23 +570,26 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
     const int tx = hh * N, ty = bb * T;
     int c = 0;
     for (; c < nchunks; ++c) {
-      const int rs = c % NR;
-      if (!mbar_wait(&raw_empty[rs], ((uint32_t)(c / NR) & 1u) ^ 1u) || *abort_v) {
+      const int ps = c % NB;
+      if (!mbar_wait(&slot_empty[ps], ((uint32_t)(c / NB) & 1u) ^ 1u) || *abort_v) {
         ctc_abort(&abort_flag);
         break;
       }
-      float* dst = sm + rs * K::RAW;
-      mbar_expect_tx(&raw_full[rs], K::TX);
+      float* dst = sm + ps * K::SLOT;
+      mbar_expect_tx(&tma_full[ps], K::TX);
 #pragma unroll
-      for (int arr = 0; arr < 6; ++arr) tma_load_2d(dst + arr * L * N, &tm.m[arr], &raw_full[rs], tx, ty + c * L);
+      for (int arr = 0; arr < 6; ++arr) tma_load_2d(dst + arr * L * LD, &tm.m[arr], &tma_full[ps], tx, ty + c * L);
     }
     // the copies still in flight land before the CTA may leave
-    for (int c2 = max(0, c - NR); c2 < c; ++c2) mbar_wait(&raw_full[c2 % NR], (uint32_t)(c2 / NR) & 1u);
+    for (int c2 = max(0, c - NB); c2 < c; ++c2) mbar_wait(&tma_full[c2 % NB], (uint32_t)(c2 / NB) & 1u);
   }
 }
 
-// Tensor maps of the six [B*T, H*N] inputs, box = N columns x 16 tokens.
-static yuf_status_t make_ctc_tmaps(const float* const (&src)[6], long long rows, int H, int N, CtcTmaps* out) {
+// Tensor maps of the six [B*T, H*N] inputs, box = `width` columns x 16 tokens
+// (the slot's row stride: columns past the head's N are the next head's, or
+// zero fill past the last head, and are never used).
+static yuf_status_t make_ctc_tmaps(const float* const (&src)[6], long long rows, int H, int N, int width,
+                                   CtcTmaps* out) {
   auto enc = tensor_map_encoder();
   if (!enc) {
     set_error("wkv7 chunked-tc: cuTensorMapEncodeTiled is unavailable");
@@ -596,7 +597,7 @@ static yuf_status_t make_ctc_tmaps(const float* const (&src)[6], long long rows,
   }
   const cuuint64_t gdim[2] = {(cuuint64_t)H * N, (cuuint64_t)rows};
   const cuuint64_t gstride[1] = {(cuuint64_t)H * N * sizeof(float)};
-  const cuuint32_t box[2] = {(cuuint32_t)N, (cuuint32_t)CTC_L};
+  const cuuint32_t box[2] = {(cuuint32_t)width, (cuuint32_t)CTC_L};
   const cuuint32_t estride[2] = {1u, 1u};
   for (int i = 0; i < 6; ++i) {
     const CUresult rc = enc(&out->m[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(src[i]), gdim,
@@ -629,7 +630,7 @@ static yuf_status_t launch_ctc(const float* const (&src)[6], const float* s0, fl
     return YUF_ERR_CUDA;
   }
   CtcTmaps tm;
-  const yuf_status_t rc = make_ctc_tmaps(src, (long long)B * T, H, N, &tm);
+  const yuf_status_t rc = make_ctc_tmaps(src, (long long)B * T, H, N, K::LD, &tm);
   if (rc != YUF_OK) return rc;
   launch_k(wkv7_chunk_tc_kernel<N>, dim3(B * H), dim3(K::NT), K::BYTES, st, s0, y, s_out, T, H, tm);
   return check_launch("wkv7_chunk_tc_kernel");
@@ -639,9 +640,9 @@ bool wkv7_chunk_tc_supports(int N) { return N == 16 || N == 32 || N == 40 || N =
 
 // One CTA per (sequence, head) walks the whole sequence, so this kernel wins
 // once the chains fill the SMs: measured on B200 at T = 2048, N = 40 it takes
-// 0.89x the time-parallel scan's time at B*H = 128 (one 86 %-full wave) but 2x
-// at B*H = 32; at T = 8192, N = 64, B*H = 128 0.98x.  Taken for T >= 256 when
-// the waves of CTAs are at least 85 % full.
+// 0.86x the time-parallel scan's time at B*H = 128 (one 86 %-full wave) and
+// 0.81x at B*H = 1024, but 1.9x at B*H = 32; at T = 8192, N = 64, B*H = 128
+// 0.75x.  Taken for T >= 256 when the waves of CTAs are at least 85 % full.
 bool wkv7_chunk_tc_applies(int B, int T, int H, int N) {
   if (T < 256 || !wkv7_chunk_tc_supports(N)) return false;
   static int sms[128];
