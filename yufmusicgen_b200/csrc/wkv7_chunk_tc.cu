@@ -445,7 +445,13 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
     float* X = sm + K::OFF_X + p * K::XS;
     for (int c = p; c < nchunks; c += NP) {
       const int ps = c % NB;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tma_full[ps], (uint32_t)(c / NB) & 1u));
+      // The slot's previous chunk is scanned first (its slot_empty phase), so
+      // that this warp never waits on tma_full two phases ahead: the loads of
+      // chunks c - NB and c may complete out of order, and a parity wait that
+      // far ahead would see chunk c - 2 NB's completed phase.
+      bool ok = mbar_wait(&slot_empty[ps], ((uint32_t)(c / NB) & 1u) ^ 1u) &&
+                mbar_wait(&tma_full[ps], (uint32_t)(c / NB) & 1u);
+      ok = __all_sync(0xffffffffu, ok);
       if (!ok || *abort_v) {
         if (lane == 0) ctc_abort(&abort_flag);
         break;
