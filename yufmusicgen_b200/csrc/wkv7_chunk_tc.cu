@@ -35,7 +35,9 @@
 //     through a warp-private scratch as the A operand of dS, S updated in fp32;
 //   * NP prep warps, each preparing a whole chunk (chunks round-robin): the
 //     scaled vectors in place of the staged inputs, the four Gram matrices and
-//     the products W, Q, U, YU on mma.sync (3xTF32), T by forward substitution;
+//     the products W, U (and Q, YU for N <= 40; for wider heads the scan warps
+//     add Y^T's in-chunk terms Mrb SA^T + Mrk V themselves) on mma.sync
+//     (3xTF32), T by forward substitution;
 //   * one loader warp: six TMA boxes (LD columns x 16 tokens, one per input) per
 //     chunk straight into the chunk's slot.
 // One ring of NB chunk slots: tma_full (the boxes' bytes), prep_full (the prep
@@ -69,22 +71,32 @@ struct CtcCfg {
   static constexpr int L = CTC_L;
   static constexpr int LD = ctc_ld(N);
   static constexpr int NS = (N + 15) / 16;     // scan warps
-  static constexpr int NP = LD <= 40 ? 5 : 3;  // prep warps
-  static constexpr int NB = LD <= 40 ? NP + 2 : NP + 1;  // chunk slots: NP in prep, one scanned (+ one loading)
-  static constexpr int NT = 32 * (NS + NP + 1);
   static constexpr int NJ = N / 8;             // 8-column tiles
   static constexpr int GL = L + 4;             // Gram row stride (= 20 mod 32: conflict-free fragments)
   static constexpr int SLD = 24;               // SA scratch row stride (= 24 mod 32: conflict free)
+  // Where Y^T's in-chunk terms are formed.  YS: the scan warps form
+  // Y^T = R~ S^T + Mrb SA^T + Mrk V themselves (wide heads, where the prep is
+  // the longer side: N = 64 prep 1270 us against scan 755 us per B*H = 128
+  // step when the prep made Q and YU); otherwise the prep makes
+  // Q = R~ + Mrb W and YU = (Mrb T Lak + Mrk) V and the scan forms
+  // Y^T = Q S^T + YU (N = 40: the other way round the scan became the longer
+  // side, 185 against 124 us).
+  static constexpr bool YS = LD > 40;
+  static constexpr int NP = YS ? 4 : 5;        // prep warps
+  static constexpr int NB = YS ? NP + 1 : NP + 2;  // chunk slots: NP in prep, one scanned (+ one loading)
+  static constexpr int NT = 32 * (NS + NP + 1);
   // A chunk slot, rows of LD floats: the six TMA boxes (LD columns x L tokens:
   // r, w, k, v, a, b), transformed in place into r~, the log-decay running sums,
-  // k~, v, a~, b~; then W, Q, U, YU; gamma_15.
+  // k~, v, a~, b~; then W, U, gamma_15 and either Mrb and Mrk ([L][GL] each,
+  // YS) or Q and YU.
   static constexpr int S_R = 0, S_W = L * LD, S_K = 2 * L * LD, S_V = 3 * L * LD, S_A = 4 * L * LD,
-                       S_B = 5 * L * LD, P_W = 6 * L * LD, P_Q = 7 * L * LD, P_U = 8 * L * LD,
-                       P_YU = 9 * L * LD, P_G = 10 * L * LD;
+                       S_B = 5 * L * LD, P_W = 6 * L * LD, P_U = 7 * L * LD, P_M = 8 * L * LD,
+                       P_Q = 8 * L * LD, P_YU = 9 * L * LD, P_G = (YS ? 9 : 10) * L * LD;
   static constexpr int SLOT = (P_G + LD + 31) / 32 * 32;
-  // prep warp scratch: Lab (then T), Lak, Mrb, Mrk, T Lak, Mrb T Lak + Mrk as [L][GL]
-  static constexpr int X_G = 0, X_T = 4 * L * GL;
-  static constexpr int XS = (6 * L * GL + 31) / 32 * 32;
+  // prep warp scratch as [L][GL]: Lab (then T), Lak, T Lak; without YS also
+  // Mrb, Mrk and Mrb T Lak + Mrk
+  static constexpr int X_G = 0, X_T = 2 * L * GL, X_RB = 3 * L * GL, X_M2 = 5 * L * GL;
+  static constexpr int XS = ((YS ? 3 : 6) * L * GL + 31) / 32 * 32;
   static constexpr int OFF_X = NB * SLOT;
   static constexpr int OFF_SA = OFF_X + NP * XS;
   static constexpr int OFF_BAR = OFF_SA + NS * L * SLD;
@@ -95,6 +107,7 @@ struct CtcCfg {
   static_assert((L * LD * 4) % 128 == 0 && SLOT % 32 == 0, "TMA boxes on 128-byte boundaries");
   static_assert(LD <= 256 && (LD * 4) % 16 == 0, "TMA box width");
   static_assert(OFF_BAR % 2 == 0, "mbarriers 8-byte aligned");
+  static_assert(2 * L * GL <= L * LD, "Mrb and Mrk fit their slot region");
   static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
@@ -187,10 +200,11 @@ __device__ __noinline__ void prep_mma(PrepProd p0, PrepProd p1) {
 
 // The chunk's Gram matrices on the tensor cores, one warp:
 //   [a~; r~] [b~; k~]^T  (32 x N by N x 32, 3xTF32), masked to
-//   Lab, Lak (s < t) and Mrb, Mrk (s <= t), stored row-major [t][GL] at G,
-//   G + 16 GL, G + 32 GL, G + 48 GL.
+//   Lab, Lak (s < t), stored row-major [t][GL] at Gab and Gab + 16 GL, and
+//   Mrb, Mrk (s <= t) at Grb and Grb + 16 GL.
 template <int N, int LD, int GL>
-__device__ __noinline__ void prep_gram(const float* At, const float* Rt, const float* Bt, const float* Kt, float* G) {
+__device__ __noinline__ void prep_gram(const float* At, const float* Rt, const float* Bt, const float* Kt, float* Gab,
+                                       float* Grb) {
   constexpr int NJ = N / 8;
   const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   float d[2][4][4];  // [a~ | r~][b~ s0-7 | b~ s8-15 | k~ s0-7 | k~ s8-15]
@@ -238,7 +252,7 @@ __device__ __noinline__ void prep_gram(const float* At, const float* Rt, const f
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
-      float* M = G + (2 * mt + (nt >> 1)) * 16 * GL;  // Lab, Lak, Mrb, Mrk
+      float* M = (mt ? Grb : Gab) + (nt >> 1) * 16 * GL;  // Lab, Lak / Mrb, Mrk
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int t = g + 8 * (e >> 1), sidx = 8 * (nt & 1) + 2 * q + (e & 1);
@@ -321,25 +335,31 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         break;
       }
       const float* P = sm + slot * K::SLOT;
-      // SA^T and Y^T for this warp's rows: M = token, N = state row, K = column
+      // SA^T = W S^T + U and Y^T = Q S^T + YU (or, YS, its first term R~ S^T)
+      // for this warp's rows: M = token, N = state row, K = column
       float sa[2][4], yy[2][4];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int col = i0 + 8 * h + 2 * q;
         const float2 u0 = *reinterpret_cast<const float2*>(P + K::P_U + g * LD + col);
         const float2 u1 = *reinterpret_cast<const float2*>(P + K::P_U + (g + 8) * LD + col);
-        const float2 y0 = *reinterpret_cast<const float2*>(P + K::P_YU + g * LD + col);
-        const float2 y1 = *reinterpret_cast<const float2*>(P + K::P_YU + (g + 8) * LD + col);
         sa[h][0] = u0.x; sa[h][1] = u0.y; sa[h][2] = u1.x; sa[h][3] = u1.y;
-        yy[h][0] = y0.x; yy[h][1] = y0.y; yy[h][2] = y1.x; yy[h][3] = y1.y;
+        if constexpr (K::YS) {
+          yy[h][0] = yy[h][1] = yy[h][2] = yy[h][3] = 0.f;
+        } else {
+          const float2 y0 = *reinterpret_cast<const float2*>(P + K::P_YU + g * LD + col);
+          const float2 y1 = *reinterpret_cast<const float2*>(P + K::P_YU + (g + 8) * LD + col);
+          yy[h][0] = y0.x; yy[h][1] = y0.y; yy[h][2] = y1.x; yy[h][3] = y1.y;
+        }
       }
+      const float* QA = P + (K::YS ? K::S_R : K::P_Q);
 #pragma unroll
       for (int kc = 0; kc < NJ; ++kc) {
-        // A: rows g, g+8 of W (and Q), k slots q / q+4 <-> columns 8kc+2q / 8kc+2q+1
+        // A: rows g, g+8 of W (and Q or R~), k slots q / q+4 <-> columns 8kc+2q / 8kc+2q+1
         const float2 w0 = *reinterpret_cast<const float2*>(P + K::P_W + g * LD + 8 * kc + 2 * q);
         const float2 w1 = *reinterpret_cast<const float2*>(P + K::P_W + (g + 8) * LD + 8 * kc + 2 * q);
-        const float2 q0 = *reinterpret_cast<const float2*>(P + K::P_Q + g * LD + 8 * kc + 2 * q);
-        const float2 q1 = *reinterpret_cast<const float2*>(P + K::P_Q + (g + 8) * LD + 8 * kc + 2 * q);
+        const float2 q0 = *reinterpret_cast<const float2*>(QA + g * LD + 8 * kc + 2 * q);
+        const float2 q1 = *reinterpret_cast<const float2*>(QA + (g + 8) * LD + 8 * kc + 2 * q);
         uint32_t wh[4], wl[4], qh[4], ql[4];
         split_a({w0.x, w1.x, w0.y, w1.y}, wh, wl);
         split_a({q0.x, q1.x, q0.y, q1.y}, qh, ql);
@@ -368,8 +388,7 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
           mma_tf32(yy[1], qh, bhi[1]);
         }
       }
-      // y rows of this chunk; SA into the warp's scratch as [token][row]
-      const int t0 = c * L + g;
+      // SA into the warp's scratch as [token][row]
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int col = 8 * h + 2 * q;
@@ -378,13 +397,57 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
             real ? make_float2(sa[h][0], sa[h][1]) : make_float2(0.f, 0.f);
         *reinterpret_cast<float2*>(SA + (g + 8) * SLD + col) =
             real ? make_float2(sa[h][2], sa[h][3]) : make_float2(0.f, 0.f);
-        if (real) {
+      }
+      __syncwarp();
+      // YS: Y^T += Mrb SA^T + Mrk V: M = token, N = state row, K = token
+      if constexpr (K::YS) {
+        const float* Mb = P + K::P_M;
+        const float* Mk = Mb + L * GL;
+        const float* V = P + K::S_V + i0 + g;
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const int sa0 = 8 * kk + q, sb0 = sa0 + 4;
+          uint32_t mbh[4], mbl[4], mkh[4], mkl[4];
+          split_a({Mb[g * GL + sa0], Mb[(g + 8) * GL + sa0], Mb[g * GL + sb0], Mb[(g + 8) * GL + sb0]}, mbh, mbl);
+          split_a({Mk[g * GL + sa0], Mk[(g + 8) * GL + sa0], Mk[g * GL + sb0], Mk[(g + 8) * GL + sb0]}, mkh, mkl);
+          uint32_t bsh[2][2], bsl[2][2], bvh[2][2], bvl[2][2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            split_b(SA[sa0 * SLD + 8 * h + g], SA[sb0 * SLD + 8 * h + g], bsh[h], bsl[h]);
+            split_b(h == 0 || h1 ? V[sa0 * LD + 8 * h] : 0.f, h == 0 || h1 ? V[sb0 * LD + 8 * h] : 0.f, bvh[h],
+                    bvl[h]);
+          }
+          mma_tf32(yy[0], mbl, bsh[0]);
+          mma_tf32(yy[0], mkl, bvh[0]);
+          if (h1) {
+            mma_tf32(yy[1], mbl, bsh[1]);
+            mma_tf32(yy[1], mkl, bvh[1]);
+          }
+          mma_tf32(yy[0], mbh, bsl[0]);
+          mma_tf32(yy[0], mkh, bvl[0]);
+          if (h1) {
+            mma_tf32(yy[1], mbh, bsl[1]);
+            mma_tf32(yy[1], mkh, bvl[1]);
+          }
+          mma_tf32(yy[0], mbh, bsh[0]);
+          mma_tf32(yy[0], mkh, bvh[0]);
+          if (h1) {
+            mma_tf32(yy[1], mbh, bsh[1]);
+            mma_tf32(yy[1], mkh, bvh[1]);
+          }
+        }
+      }
+      // y rows of this chunk
+      const int t0 = c * L + g;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int col = 8 * h + 2 * q;
+        if (h == 0 || h1) {
           if (t0 < T) *reinterpret_cast<float2*>(ybase + (size_t)t0 * ystride + col) = make_float2(yy[h][0], yy[h][1]);
           if (t0 + 8 < T)
             *reinterpret_cast<float2*>(ybase + (size_t)(t0 + 8) * ystride + col) = make_float2(yy[h][2], yy[h][3]);
         }
       }
-      __syncwarp();
       // dS = SA^T^T B~ + V^T K~: M = state row, N = column, K = token
       float dS[NJ][4];
 #pragma unroll
@@ -527,7 +590,8 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
       }
       __syncwarp();
       // (4) Gram matrices Lab, Lak, Mrb, Mrk (row-major [t][GL])
-      prep_gram<N, LD, GL>(P + K::S_A, P + K::S_R, P + K::S_B, P + K::S_K, X + K::X_G);
+      prep_gram<N, LD, GL>(P + K::S_A, P + K::S_R, P + K::S_B, P + K::S_K, X + K::X_G,
+                           K::YS ? P + K::P_M : X + K::X_RB);
       __syncwarp();
       // (5) T = (I - Lab)^-1 (unit lower triangular), lane c < 16 solving for
       //     column c; T replaces Lab once every lane has read it
@@ -549,25 +613,29 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         }
       }
       __syncwarp();
-      // (6) TLak = T Lak and M2 = Mrb TLak + Mrk (16 x 16, into the free
-      //     slots after Mrk), then W = T A~,  Q = R~ + Mrb W,  U = TLak V,
-      //     YU = M2 V  (U = T Lak V and YU = Mrb U + Mrk V regrouped)
+      // (6) TLak = T Lak (16 x 16), then W = T A~ and U = TLak V (U = T Lak V
+      //     regrouped); without YS also M2 = Mrb TLak + Mrk, Q = R~ + Mrb W and
+      //     YU = M2 V (YU = Mrb U + Mrk V regrouped).
       {
         const float* Tm = X + K::X_G;
         const float* Lak = Tm + L * GL;
-        const float* Mrb = Lak + L * GL;
-        const float* Mrk = Mrb + L * GL;
         float* TLak = X + K::X_T;
-        float* M2 = TLak + L * GL;
         const PrepProd none{nullptr, nullptr, nullptr, nullptr};
         prep_mma<16, GL, GL, 1>({Tm, Lak, nullptr, TLak}, none);
         prep_mma<N, LD, GL, 1>({Tm, P + K::S_A, nullptr, P + K::P_W}, none);
         __syncwarp();
-        prep_mma<16, GL, GL, 1>({Mrb, TLak, Mrk, M2}, none);
-        prep_mma<N, LD, GL, 1>({Mrb, P + K::P_W, P + K::S_R, P + K::P_Q}, none);
-        prep_mma<N, LD, GL, 1>({TLak, P + K::S_V, nullptr, P + K::P_U}, none);
-        __syncwarp();
-        prep_mma<N, LD, GL, 1>({M2, P + K::S_V, nullptr, P + K::P_YU}, none);
+        if constexpr (!K::YS) {
+          const float* Mrb = X + K::X_RB;
+          const float* Mrk = Mrb + L * GL;
+          float* M2 = X + K::X_M2;
+          prep_mma<16, GL, GL, 1>({Mrb, TLak, Mrk, M2}, none);
+          prep_mma<N, LD, GL, 1>({Mrb, P + K::P_W, P + K::S_R, P + K::P_Q}, none);
+          prep_mma<N, LD, GL, 1>({TLak, P + K::S_V, nullptr, P + K::P_U}, none);
+          __syncwarp();
+          prep_mma<N, LD, GL, 1>({M2, P + K::S_V, nullptr, P + K::P_YU}, none);
+        } else {
+          prep_mma<N, LD, GL, 1>({TLak, P + K::S_V, nullptr, P + K::P_U}, none);
+        }
       }
       __syncwarp();
       mbar_arrive(&prep_full[ps]);
@@ -648,7 +716,7 @@ bool wkv7_chunk_tc_supports(int N) { return N == 16 || N == 32 || N == 40 || N =
 // once the chains fill the SMs: measured on B200 at T = 2048, N = 40 it takes
 // 0.86x the time-parallel scan's time at B*H = 128 (one 86 %-full wave) and
 // 0.81x at B*H = 1024, but 1.9x at B*H = 32; at T = 8192, N = 64, B*H = 128
-// 0.75x.  Taken for T >= 256 when the waves of CTAs are at least 85 % full.
+// 0.57x.  Taken for T >= 256 when the waves of CTAs are at least 85 % full.
 bool wkv7_chunk_tc_applies(int B, int T, int H, int N) {
   if (T < 256 || !wkv7_chunk_tc_supports(N)) return false;
   static int sms[128];
