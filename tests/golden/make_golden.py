@@ -15,6 +15,10 @@ Every fixture is produced by the reference's own PyTorch fp32 CPU code:
 * gradients of both recurrences by torch autograd through the reference's
   CPU code (``grads_cases.npz``), the oracle of the training backward ops.
 
+``python tests/golden/make_golden.py dropin`` writes only the fixture of the
+reference op wrapper's own padding (``yufmusicgen/cuda_ops.py`` ``_pad_inputs``:
+T padded to a multiple of 16 with w_raw = -80 and zeros) with the CPU
+recurrence's output for the unpadded inputs (``dropin_pad_cases.npz``);
 ``python tests/golden/make_golden.py grads`` writes only the gradient fixture,
 ``... greedy256`` only the 256-step greedy decode of the 0.1B model, ``... long``
 only the benchmark-size prefills (config 3 in full, config-5 geometry), ``...
@@ -426,6 +430,29 @@ def greedy256_case():
         meta_keys=np.array(["seed", "recipe", "steps"]), meta_vals=np.array(["1", "baseline", str(n)]))
 
 
+def dropin_case():
+    """What the reference op wrapper hands its CUDA op: ``_pad_inputs`` of
+    yufmusicgen/cuda_ops.py:160-186 on T not a multiple of 16, and the CPU
+    recurrence's y and final state for the unpadded inputs (zero state)."""
+    from yufmusicgen import cuda_ops as ref_ops
+
+    out = {}
+    for name, B, T, H, N, seed in (("n40_t21", 2, 21, 3, 40, 31), ("n64_t5", 1, 5, 2, 64, 32),
+                                   ("n16_t37", 2, 37, 2, 16, 33)):
+        ins = wkv_op_inputs(B, T, H, N, seed=seed)
+        args = [t(ins[k]) for k in ("r", "w", "k", "v", "a", "b")]
+        padded, length = ref_ops._pad_inputs(*args)
+        assert length == T
+        y, sT = RWKV7TimeMix._torch_recurrence(*args, torch.zeros(B, H, N, N))
+        for k, x in zip(("r", "w", "k", "v", "a", "b"), padded):
+            out[f"{name}.{k}_padded"] = x.numpy()
+            out[f"{name}.{k}"] = ins[k]
+        out[f"{name}.length"] = np.array(length)
+        out[f"{name}.y"] = y.numpy()
+        out[f"{name}.sT"] = sT.numpy()
+    np.savez_compressed(HERE / "dropin_pad_cases.npz", **out)
+
+
 def main():
     wkv_cases()
     rosa_cases()
@@ -453,9 +480,12 @@ if __name__ == "__main__":
         sampler_cases()
     elif sys.argv[1:] == ["greedy256"]:
         greedy256_case()
+    elif sys.argv[1:] == ["dropin"]:
+        dropin_case()
     else:
         main()
         grad_cases()
         greedy256_case()
         long_cases()
+        dropin_case()
         sampler_cases()
