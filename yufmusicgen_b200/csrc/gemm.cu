@@ -42,6 +42,12 @@ namespace yuf {
 
 __device__ unsigned int g_gemm_wait_timeouts;
 
+// Per-warp staging of the epilogue: 32 rows x 32 columns of fp32 with a row
+// stride of 36 floats (16-byte rows apart by 4 banks: conflict-free float4
+// writes by row and float4 reads by column group).
+constexpr int GEMM_STG_LD = 36;
+constexpr int GEMM_STG_FLOATS = 32 * GEMM_STG_LD;
+
 template <int BN>
 struct GemmCfg {
   static constexpr int BM = 128, BK = 64;           // BK bf16 = one 128-byte swizzle row
@@ -50,8 +56,9 @@ struct GemmCfg {
   static constexpr int STAGE = A_BYTES + B_BYTES;   // multiple of 1024
   static constexpr int STAGES = std::min(8, (192 * 1024) / STAGE);
   static constexpr uint32_t TMEM_COLS = 2 * BN;     // two fp32 accumulators of BN columns
+  static constexpr int STG_BYTES = 4 * GEMM_STG_FLOATS * 4;  // the epilogue warps' staging
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = STAGES * STAGE + BAR_BYTES + 1024;  // + alignment slack
+  static constexpr int SMEM = STAGES * STAGE + STG_BYTES + BAR_BYTES + 1024;  // + alignment slack
   static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
   static constexpr int THREADS = 192;
   static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
@@ -83,40 +90,82 @@ YUF_DEVICE bool gemm_wait(uint64_t* bar, uint32_t parity, volatile int* abort_fl
   return false;
 }
 
+// One 32 x 32 block of the calling warp's fp32 outputs (added to C when
+// p.beta != 0): lane l holds row l's 32 values in v; they go through the warp's
+// staging area so that each store instruction writes four whole 128-byte row
+// segments instead of 16 bytes in each of 32 rows (for an fp32 tile that cut
+// the [65536 x 3072] R/K/V projection from 449 to 362 us).  `rows` rows of the
+// block are live; columns from `col` on, up to `ncols` of them.
+YUF_DEVICE void gemm_store_block_f32(const GemmParams& p, float* stg, const float (&v)[32], int z, int row0,
+                                     int rows, int col, int ncols) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    *reinterpret_cast<float4*>(stg + lane * GEMM_STG_LD + 4 * k) =
+        make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  __syncwarp();
+  const int c4 = 4 * (lane & 7);
+  const bool full = p.vec && c4 + 4 <= ncols;
+  float* base = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row0 * p.ldc + col + c4;
+  float4 x[8], old[8];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    x[it] = *reinterpret_cast<const float4*>(stg + (it * 4 + (lane >> 3)) * GEMM_STG_LD + c4);
+    old[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncwarp();  // the staging area is free for the next block
+  if (p.beta != 0.f && full) {  // the residual's old values, all loads before the first store
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int r = it * 4 + (lane >> 3);
+      if (r < rows) old[it] = *reinterpret_cast<const float4*>(base + (size_t)r * p.ldc);
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    if (r >= rows) continue;
+    float* out = base + (size_t)r * p.ldc;
+    if (full) {
+      *reinterpret_cast<float4*>(out) =
+          make_float4(x[it].x + old[it].x, x[it].y + old[it].y, x[it].z + old[it].z, x[it].w + old[it].w);
+    } else {
+      const float e[4] = {x[it].x, x[it].y, x[it].z, x[it].w};
+      for (int c = 0; c < 4; ++c)
+        if (c4 + c < ncols) out[c] = p.beta != 0.f ? e[c] + out[c] : e[c];
+    }
+  }
+}
+
+// bf16 outputs from one thread's row: 32 values as four 16-byte stores.
+YUF_DEVICE void gemm_store_row_bf16(const GemmParams& p, const float (&v)[32], int z, int row, int col,
+                                    int ncols) {
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
+  if (p.vec && ncols >= 32) {
+#pragma unroll
+    for (int c = 0; c < 32; c += 8) {
+      uint4 pk;
+      __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) b2[e] = __floats2bfloat162_rn(v[c + 2 * e], v[c + 2 * e + 1]);
+      *reinterpret_cast<uint4*>(out + c) = pk;
+    }
+  } else {
+    for (int c = 0; c < 32; ++c)
+      if (c < ncols) out[c] = __float2bfloat16_rn(v[c]);
+  }
+}
+
 // Epilogue of one output tile held in TMEM (lanes = rows, columns = outputs):
-// the calling warp's 32 rows, `row` this thread's, `tbase` the TMEM address of
-// the warp's lane quarter at the tile's first column; tile column block `nt` of
-// BN columns (SiLU-gate: BN / 2 output columns).  Every lane runs the TMEM loads
-// (warp-collective); only live rows store.
+// the calling warp's 32 rows starting at `row0` (`rows` of them live), `tbase`
+// the TMEM address of the warp's lane quarter at the tile's first column; tile
+// column block `nt` of BN columns (SiLU-gate: BN / 2 output columns).  Every
+// lane runs the TMEM loads (warp-collective); `stg` is the warp's staging area.
 template <int BN, int EPI>
-YUF_DEVICE void gemm_epilogue_tile(const GemmParams& p, uint32_t tbase, int z, int row, int nt, bool live) {
-  if constexpr (EPI == GEMM_EPI_SWIGLU_F32) {
-    float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
-#pragma unroll 1
-    for (int sb = 0; sb < BN / 128; ++sb)
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        float vi[32], vg[32];
-        tmem_ld_x32(tbase + sb * 128 + h * 32, vi);
-        tmem_ld_x32(tbase + sb * 128 + 64 + h * 32, vg);
-        const int col = nt * (BN / 2) + sb * 64 + h * 32;
-        if (live) {
-          if (p.vec && col + 32 <= p.n_out) {
-#pragma unroll
-            for (int c = 0; c < 32; c += 4)
-              *reinterpret_cast<float4*>(out + col + c) =
-                  make_float4(silu(vi[c]) * vg[c], silu(vi[c + 1]) * vg[c + 1], silu(vi[c + 2]) * vg[c + 2],
-                              silu(vi[c + 3]) * vg[c + 3]);
-          } else {
-#pragma unroll
-            for (int c = 0; c < 32; ++c)
-              if (col + c < p.n_out) out[col + c] = silu(vi[c]) * vg[c];
-          }
-        }
-      }
-  } else if constexpr (EPI == GEMM_EPI_SWIGLU) {
+YUF_DEVICE void gemm_epilogue_tile(const GemmParams& p, uint32_t tbase, int z, int row0, int rows, int nt,
+                                   float* stg) {
+  if constexpr (EPI == GEMM_EPI_SWIGLU_F32 || EPI == GEMM_EPI_SWIGLU) {
     // tile columns per 128: [64 "in" rows | 64 "gate" rows] of the packed weight
-    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc;
 #pragma unroll 1
     for (int sb = 0; sb < BN / 128; ++sb)
 #pragma unroll 1
@@ -125,23 +174,13 @@ YUF_DEVICE void gemm_epilogue_tile(const GemmParams& p, uint32_t tbase, int z, i
         tmem_ld_x32(tbase + sb * 128 + h * 32, vi);
         tmem_ld_x32(tbase + sb * 128 + 64 + h * 32, vg);
         const int col = nt * (BN / 2) + sb * 64 + h * 32;
-        if (live) {
-          if (p.vec && col + 32 <= p.n_out) {
+        if (rows <= 0 || col >= p.n_out) continue;
 #pragma unroll
-            for (int c = 0; c < 32; c += 8) {
-              uint4 pk;
-              __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                b2[e] = __floats2bfloat162_rn(silu(vi[c + 2 * e]) * vg[c + 2 * e],
-                                              silu(vi[c + 2 * e + 1]) * vg[c + 2 * e + 1]);
-              *reinterpret_cast<uint4*>(out + col + c) = pk;
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < 32; ++c)
-              if (col + c < p.n_out) out[col + c] = __float2bfloat16_rn(silu(vi[c]) * vg[c]);
-          }
+        for (int c = 0; c < 32; ++c) vi[c] = silu(vi[c]) * vg[c];
+        if constexpr (EPI == GEMM_EPI_SWIGLU) {
+          if ((threadIdx.x & 31) < rows) gemm_store_row_bf16(p, vi, z, row0 + (threadIdx.x & 31), col, p.n_out - col);
+        } else {
+          gemm_store_block_f32(p, stg, vi, z, row0, rows, col, min(32, p.n_out - col));
         }
       }
   } else {
@@ -150,49 +189,15 @@ YUF_DEVICE void gemm_epilogue_tile(const GemmParams& p, uint32_t tbase, int z, i
       float v[32];
       tmem_ld_x32(tbase + c0, v);
       const int col = nt * BN + c0;
-      if (!live || col >= p.N) continue;
-      if constexpr (EPI == GEMM_EPI_F32) {
-        if (p.tanh_batch0 && z == 0) {
+      if (rows <= 0 || col >= p.N) continue;
+      if (p.tanh_batch0 && z == 0) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] = tanhf(v[c]);
-        }
-        float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
-        if (p.vec && col + 32 <= p.N) {
-#pragma unroll
-          for (int c = 0; c < 32; c += 4) {
-            float4 o = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
-            if (p.beta != 0.f) {
-              const float4 old = *reinterpret_cast<const float4*>(out + c);
-              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-            }
-            *reinterpret_cast<float4*>(out + c) = o;
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (col + c < p.N) out[c] = p.beta != 0.f ? v[c] + out[c] : v[c];
-        }
-      } else {  // GEMM_EPI_BF16
-        if (p.tanh_batch0 && z == 0) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] = tanhf(v[c]);
-        }
-        __nv_bfloat16* out =
-            static_cast<__nv_bfloat16*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
-        if (p.vec && col + 32 <= p.N) {
-#pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            uint4 pk;
-            __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) b2[e] = __floats2bfloat162_rn(v[c + 2 * e], v[c + 2 * e + 1]);
-            *reinterpret_cast<uint4*>(out + c) = pk;
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (col + c < p.N) out[c] = __float2bfloat16_rn(v[c]);
-        }
+        for (int c = 0; c < 32; ++c) v[c] = tanhf(v[c]);
+      }
+      if constexpr (EPI == GEMM_EPI_BF16) {
+        if ((threadIdx.x & 31) < rows) gemm_store_row_bf16(p, v, z, row0 + (threadIdx.x & 31), col, p.N - col);
+      } else {
+        gemm_store_block_f32(p, stg, v, z, row0, rows, col, min(32, p.N - col));
       }
     }
   }
@@ -205,7 +210,8 @@ __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
   using G = GemmCfg<BN>;
   extern __shared__ __align__(1024) unsigned char gemm_smem_raw[];
   unsigned char* sm = gemm_smem_raw + ((1024u - (smem_u32(gemm_smem_raw) & 1023u)) & 1023u);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + G::STAGES * G::STAGE);
+  float* stg_all = reinterpret_cast<float*>(sm + G::STAGES * G::STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + G::STAGES * G::STAGE + G::STG_BYTES);
   uint64_t* empty = full + G::STAGES;
   uint64_t* tfull = empty + G::STAGES;   // [2] accumulator ready for the epilogue
   uint64_t* tempty = tfull + 2;          // [2] accumulator drained by the epilogue
@@ -312,10 +318,9 @@ __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after_sync();
-      const int row = mt * G::BM + q * 32 + lane;
-      const bool live = row < p.M;
+      const int row0 = mt * G::BM + q * 32;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-      gemm_epilogue_tile<BN, EPI>(p, tbase, z, row, nt, live);
+      gemm_epilogue_tile<BN, EPI>(p, tbase, z, row0, min(32, p.M - row0), nt, stg_all + q * GEMM_STG_FLOATS);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -349,8 +354,9 @@ struct GemmPairCfg {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int STAGES = 6;
   static constexpr uint32_t TMEM_COLS = 512;         // two accumulators of 256 columns
+  static constexpr int STG_BYTES = 4 * GEMM_STG_FLOATS * 4;  // the epilogue warps' staging
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = STAGES * STAGE + BAR_BYTES + 1024;
+  static constexpr int SMEM = STAGES * STAGE + STG_BYTES + BAR_BYTES + 1024;
   static constexpr uint32_t IDESC = umma_idesc_bf16(256, BN);
   static constexpr int THREADS = 192;
   static_assert(STAGE % 1024 == 0, "stages stay 1024-byte aligned for the 128-byte swizzle");
@@ -363,7 +369,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmPairCfg::THREADS
   using G = GemmPairCfg;
   extern __shared__ __align__(1024) unsigned char gemm_smem_raw[];
   unsigned char* sm = gemm_smem_raw + ((1024u - (smem_u32(gemm_smem_raw) & 1023u)) & 1023u);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + G::STAGES * G::STAGE);
+  float* stg_all = reinterpret_cast<float*>(sm + G::STAGES * G::STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + G::STAGES * G::STAGE + G::STG_BYTES);
   uint64_t* empty = full + G::STAGES;
   uint64_t* tfull = empty + G::STAGES;
   uint64_t* tempty = tfull + 2;
@@ -479,9 +486,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GemmPairCfg::THREADS
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after_sync();
-      const int row = mt * 256 + (int)rank * 128 + q * 32 + lane;
+      const int row0 = mt * 256 + (int)rank * 128 + q * 32;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * G::BN);
-      gemm_epilogue_tile<G::BN, EPI>(p, tbase, z, row, nt, row < p.M);
+      gemm_epilogue_tile<G::BN, EPI>(p, tbase, z, row0, min(32, p.M - row0), nt,
+                                     stg_all + q * GEMM_STG_FLOATS);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) {
