@@ -1291,13 +1291,41 @@ static yuf_status_t launch_gemm_splitk(const GemmArgs& g, GemmParams p, int ks, 
   return check_launch("gemm_bf16_splitk_kernel");
 }
 
-// Few rows: pick the column tile and the K split whose CTAs each load the
-// fewest bytes while every cluster of the launch is resident at once.
+// Launch plans are compared in one cost unit: rows of A and W tiles that a
+// CTA streams per 64-wide K block, times the K blocks it covers, times the
+// rounds (persistent kernel) or waves (split-K kernel) the tiles take, plus a
+// fixed per-launch cost.  Fitted to B200 timings of both kernels at K = 640 to
+// 2560 and 128 to 4096 rows, one unit is about 1.6 ns; the fixed costs are
+// 6.3 us for the persistent kernel and 8 us for a split-K launch (its cluster
+// reduction).  A split-K launch whose clusters do not all fit at once pays
+// half again for the waves after the first, whose epilogues do not overlap.
+constexpr long long GEMM_COST_PERSISTENT = 3900, GEMM_COST_SPLITK = 5000;
+
+struct GemmPlan {
+  long long cost = -1;
+  int bn = 128, ks = 1;
+};
+
+// Persistent one-CTA kernel: the column tile whose rounds of tiles cost least.
+static GemmPlan plan_persistent(const GemmArgs& g, const GemmParams& p, int sms) {
+  const long long kblocks = (g.K + 63) / 64;
+  GemmPlan best;
+  for (int bn : {256, 128, 64}) {
+    if (g.epi == GEMM_EPI_SWIGLU && (bn < 128 || g.N % bn != 0)) continue;
+    const long long tiles = (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch;
+    const long long rounds = (tiles + sms - 1) / sms;
+    const long long cost = GEMM_COST_PERSISTENT + rounds * kblocks * (128 + bn);
+    if (best.cost < 0 || cost < best.cost) best = {cost, bn, 1};
+  }
+  return best;
+}
+
+// Split-K clusters: the column tile and the K split whose CTAs each load the
+// fewest bytes, with every cluster resident at once when K is split.
 template <int EPI>
-static yuf_status_t dispatch_splitk(const GemmArgs& g, const GemmParams& p, cudaStream_t s) {
+static GemmPlan plan_splitk(const GemmArgs& g, const GemmParams& p) {
   const int kblocks = (g.K + 63) / 64;
-  int best_bn = 0, best_ks = 1;
-  long long best_cost = -1;
+  GemmPlan best;
   for (int bn : {64, 128, 256}) {
     if (EPI == GEMM_EPI_SWIGLU && (bn < 128 || g.N % bn != 0)) continue;
     const long long tiles = (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch;
@@ -1307,19 +1335,20 @@ static yuf_status_t dispatch_splitk(const GemmArgs& g, const GemmParams& p, cuda
                                  : (bn == 128 ? splitk_slots<128, EPI>(ks) : splitk_slots<256, EPI>(ks));
       if (tiles > slots && ks > 1) continue;
       const long long kb_per = (kblocks + ks - 1) / ks;
-      // bytes per CTA (A + W slices), then a wave count for launches that do not fit
       const long long waves = (tiles + slots - 1) / slots;
-      const long long cost = (128 + bn) * kb_per * waves;
-      if (best_cost < 0 || cost < best_cost) {
-        best_cost = cost;
-        best_bn = bn;
-        best_ks = ks;
-      }
+      const long long cost = GEMM_COST_SPLITK + (128 + bn) * kb_per * (2 * waves - 1 + waves) / 2;
+      if (best.cost < 0 || cost < best.cost) best = {cost, bn, ks};
     }
   }
-  if (best_bn == 64) return launch_gemm_splitk<64, EPI>(g, p, best_ks, s);
-  if (best_bn == 128) return launch_gemm_splitk<128, EPI>(g, p, best_ks, s);
-  return launch_gemm_splitk<256, EPI>(g, p, best_ks, s);
+  return best;
+}
+
+template <int EPI>
+static yuf_status_t launch_splitk_plan(const GemmArgs& g, const GemmParams& p, const GemmPlan& plan,
+                                       cudaStream_t s) {
+  if (plan.bn == 64) return launch_gemm_splitk<64, EPI>(g, p, plan.ks, s);
+  if (plan.bn == 128) return launch_gemm_splitk<128, EPI>(g, p, plan.ks, s);
+  return launch_gemm_splitk<256, EPI>(g, p, plan.ks, s);
 }
 
 yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
@@ -1349,12 +1378,19 @@ yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
   p.vec = (reinterpret_cast<uintptr_t>(g.C) & 15) == 0 && g.ldc % vec_elems == 0 &&
           g.c_bstride % vec_elems == 0;
   const int sms = sm_count();
-  auto tiles = [&](int bn) { return (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch; };
-  // a decode batch: split K over a cluster
+  const GemmPlan persistent = plan_persistent(g, p, sms);
+  // a decode batch: split K over a cluster, unless the persistent kernel's
+  // rounds of whole-K tiles cost less (short K, many columns)
   if (p.m_tiles <= 2 && (g.epi != GEMM_EPI_SWIGLU || g.N % 128 == 0)) {
-    if (g.epi == GEMM_EPI_F32) return dispatch_splitk<GEMM_EPI_F32>(g, p, s);
-    if (g.epi == GEMM_EPI_BF16) return dispatch_splitk<GEMM_EPI_BF16>(g, p, s);
-    return dispatch_splitk<GEMM_EPI_SWIGLU>(g, p, s);
+    GemmPlan split;
+    if (g.epi == GEMM_EPI_F32) split = plan_splitk<GEMM_EPI_F32>(g, p);
+    else if (g.epi == GEMM_EPI_BF16) split = plan_splitk<GEMM_EPI_BF16>(g, p);
+    else split = plan_splitk<GEMM_EPI_SWIGLU>(g, p);
+    if (split.cost <= persistent.cost) {
+      if (g.epi == GEMM_EPI_F32) return launch_splitk_plan<GEMM_EPI_F32>(g, p, split, s);
+      if (g.epi == GEMM_EPI_BF16) return launch_splitk_plan<GEMM_EPI_BF16>(g, p, split, s);
+      return launch_splitk_plan<GEMM_EPI_SWIGLU>(g, p, split, s);
+    }
   }
   // enough 256 x 256 tiles to fill the pairs: the CTA-pair kernel
   const long long pair_tiles = (long long)((g.M + 255) / 256) * ((g.N + 255) / 256) * g.batch;
@@ -1368,12 +1404,10 @@ yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
       set_error("gemm: the SiLU-gate weight must hold whole 128-row groups (N = %d)", g.N);
       return YUF_ERR_INVALID_ARGUMENT;
     }
-    return tiles(256) >= sms && g.N % 256 == 0 ? launch_gemm<256, GEMM_EPI_SWIGLU>(g, p, s)
-                                               : launch_gemm<128, GEMM_EPI_SWIGLU>(g, p, s);
+    return persistent.bn == 256 ? launch_gemm<256, GEMM_EPI_SWIGLU>(g, p, s)
+                                : launch_gemm<128, GEMM_EPI_SWIGLU>(g, p, s);
   }
-  int bn = 128;
-  if (g.N <= 64 || tiles(128) < sms) bn = 64;
-  else if (g.N % 256 == 0 || g.N >= 4096) bn = 256;
+  const int bn = persistent.bn;
   if (g.epi == GEMM_EPI_F32) {
     if (bn == 64) return launch_gemm<64, GEMM_EPI_F32>(g, p, s);
     if (bn == 128) return launch_gemm<128, GEMM_EPI_F32>(g, p, s);

@@ -339,7 +339,7 @@ __global__ void timemix_post_kernel(const float* __restrict__ k, const float* __
     const float2 lwv = *reinterpret_cast<const float2*>(lw + i);
     const float2 lav = *reinterpret_cast<const float2*>(la + i);
     const float2 lgv = *reinterpret_cast<const float2*>(lg + i);
-    const float ax = 1.f / (1.f + expf(-(a0p.x + lav.x))), ay = 1.f / (1.f + expf(-(a0p.y + lav.y)));
+    const float ax = sigmoidf_fast(a0p.x + lav.x), ay = sigmoidf_fast(a0p.y + lav.y);
     const float kkx = kv.x * kkp.x * inv, kky = kv.y * kkp.y * inv;
     *reinterpret_cast<float2*>(w_raw + i) = make_float2(w0p.x + lwv.x, w0p.y + lwv.y);
     *reinterpret_cast<float2*>(a_op + i) = make_float2(-kkx, -kky);
@@ -347,7 +347,7 @@ __global__ void timemix_post_kernel(const float* __restrict__ k, const float* __
     *reinterpret_cast<float2*>(k_adj + i) =
         make_float2(kv.x * (1.f + (ax - 1.f) * kap.x), kv.y * (1.f + (ay - 1.f) * kap.y));
     *reinterpret_cast<float2*>(g_out + i) =
-        make_float2(1.f / (1.f + expf(-lgv.x)), 1.f / (1.f + expf(-lgv.y)));
+        make_float2(sigmoidf_fast(lgv.x), sigmoidf_fast(lgv.y));
   }
 }
 
