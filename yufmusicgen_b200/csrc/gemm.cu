@@ -538,8 +538,10 @@ struct GemmSplitCfg {
 };
 
 // Epilogue of four consecutive output columns (col .. col+3) of one row.
+// `old`: the four outputs' previous values when the caller loaded them ahead
+// (p.beta != 0, whole float4 groups), else null.
 template <int EPI>
-YUF_DEVICE void store4(const GemmParams& p, int z, int row, int col, float4 v) {
+YUF_DEVICE void store4(const GemmParams& p, int z, int row, int col, float4 v, const float4* old = nullptr) {
   const bool full = p.vec && col + 4 <= p.N;
   if constexpr (EPI == GEMM_EPI_F32) {
     if (p.tanh_batch0 && z == 0) {
@@ -548,7 +550,7 @@ YUF_DEVICE void store4(const GemmParams& p, int z, int row, int col, float4 v) {
     float* out = static_cast<float*>(p.C) + (size_t)z * p.c_bstride + (size_t)row * p.ldc + col;
     if (full) {
       if (p.beta != 0.f) {
-        const float4 o = *reinterpret_cast<const float4*>(out);
+        const float4 o = old ? *old : *reinterpret_cast<const float4*>(out);
         v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
       }
       *reinterpret_cast<float4*>(out) = v;
@@ -644,8 +646,10 @@ YUF_DEVICE void cluster_reduce_store_ks(const GemmParams& p, uint32_t pbase, int
     constexpr int QC = BN / 4;
     constexpr int U = KS >= LOADS ? 1 : LOADS / KS;  // groups per thread and step (U KS loads in flight)
     const int total = rows * QC;
+    // the residual (p.beta != 0) is loaded with the partials, not behind them
+    const bool pre = EPI == GEMM_EPI_F32 && p.beta != 0.f && p.vec;
     for (int i0 = threadIdx.x; i0 < total; i0 += nthreads * U) {
-      float4 xs[U][KS];
+      float4 xs[U][KS], old[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int i = min(i0 + u * nthreads, total - 1);
@@ -653,6 +657,11 @@ YUF_DEVICE void cluster_reduce_store_ks(const GemmParams& p, uint32_t pbase, int
 #pragma unroll
         for (int qq = 0; qq < KS; ++qq)
           xs[u][qq] = ld_shared_cluster_f4(mapa_shared(pbase + (uint32_t)((rr * pstride + c) * 4), qq));
+        const int row = mt * 128 + rr, col = nt * BN + c;
+        old[u] = pre && row < p.M && col + 4 <= p.N
+                     ? *reinterpret_cast<const float4*>(static_cast<const float*>(p.C) + (size_t)z * p.c_bstride +
+                                                        (size_t)row * p.ldc + col)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -665,7 +674,7 @@ YUF_DEVICE void cluster_reduce_store_ks(const GemmParams& p, uint32_t pbase, int
           a.x += xs[u][qq].x; a.y += xs[u][qq].y; a.z += xs[u][qq].z; a.w += xs[u][qq].w;
         }
         const int row = mt * 128 + rr, col = nt * BN + c;
-        if (row < p.M && col < p.N) store4<EPI>(p, z, row, col, a);
+        if (row < p.M && col < p.N) store4<EPI>(p, z, row, col, a, pre ? &old[u] : nullptr);
       }
     }
   }
@@ -673,7 +682,10 @@ YUF_DEVICE void cluster_reduce_store_ks(const GemmParams& p, uint32_t pbase, int
 
 // LOADS: distributed-shared-memory loads a thread keeps in flight (fewer for
 // register-heavy callers).
-template <int BN, int EPI, int LOADS = 8>
+#ifndef GEMM_SPLIT_LOADS
+#define GEMM_SPLIT_LOADS 8
+#endif
+template <int BN, int EPI, int LOADS = GEMM_SPLIT_LOADS>
 YUF_DEVICE void cluster_reduce_store(const GemmParams& p, uint32_t pbase, int pstride, int ks, int r, int z,
                                      int mt, int nt, int nthreads) {
   switch (ks) {
@@ -722,16 +734,34 @@ YUF_DEVICE void local_reduce_store(const GemmParams& p, const float* recv, int p
       }
     }
   } else {
-    constexpr int QC = BN / 4;
-    for (int i = threadIdx.x; i < rows * QC; i += nthreads) {
-      const int lr = i / QC, c = (i % QC) * 4;
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int qq = 0; qq < ks; ++qq) {
-        const float4 x = *reinterpret_cast<const float4*>(recv + qq * slice + lr * pstride + c);
-        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+    constexpr int QC = BN / 4, U = 8;
+    // the residual (p.beta != 0) of U groups is loaded before their sums
+    const bool pre = EPI == GEMM_EPI_F32 && p.beta != 0.f && p.vec;
+    const int total = rows * QC;
+    for (int i0 = threadIdx.x; i0 < total; i0 += U * nthreads) {
+      float4 old[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * nthreads;
+        const int row = mt * 128 + r0 + i / QC, col = nt * BN + (i % QC) * 4;
+        old[u] = pre && i < total && row < p.M && col + 4 <= p.N
+                     ? *reinterpret_cast<const float4*>(static_cast<const float*>(p.C) + (size_t)z * p.c_bstride +
+                                                        (size_t)row * p.ldc + col)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      const int row = mt * 128 + r0 + lr, col = nt * BN + c;
-      if (row < p.M && col < p.N) store4<EPI>(p, z, row, col, a);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = i0 + u * nthreads;
+        if (i >= total) break;
+        const int lr = i / QC, c = (i % QC) * 4;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int qq = 0; qq < ks; ++qq) {
+          const float4 x = *reinterpret_cast<const float4*>(recv + qq * slice + lr * pstride + c);
+          a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+        }
+        const int row = mt * 128 + r0 + lr, col = nt * BN + c;
+        if (row < p.M && col < p.N) store4<EPI>(p, z, row, col, a, pre ? &old[u] : nullptr);
+      }
     }
   }
 }
@@ -1291,19 +1321,13 @@ static yuf_status_t launch_gemm_splitk(const GemmArgs& g, GemmParams p, int ks, 
   return check_launch("gemm_bf16_splitk_kernel");
 }
 
-// Launch plans are compared in one cost unit: rows of A and W tiles that a
-// CTA streams per 64-wide K block, times the K blocks it covers, times the
-// rounds (persistent kernel) or waves (split-K kernel) the tiles take, plus a
-// fixed per-launch cost.  Fitted to B200 timings of both kernels at K = 640 to
-// 2560 and 128 to 4096 rows, one unit is about 1.6 ns; the fixed costs are
-// 6.3 us for the persistent kernel and 8 us for a split-K launch (its cluster
-// reduction).  A split-K launch whose clusters do not all fit at once pays
-// half again for the waves after the first, whose epilogues do not overlap.
-constexpr long long GEMM_COST_PERSISTENT = 3900, GEMM_COST_SPLITK = 5000;
-
+// Launch plans of the persistent kernel are compared in one cost unit: rows
+// of A and W tiles that a CTA streams per 64-wide K block, times the K blocks
+// it covers, times the rounds its tiles take.
 struct GemmPlan {
-  long long cost = -1;
+  double cost = -1;
   int bn = 128, ks = 1;
+  bool split = false;
 };
 
 // Persistent one-CTA kernel: the column tile whose rounds of tiles cost least.
@@ -1314,30 +1338,45 @@ static GemmPlan plan_persistent(const GemmArgs& g, const GemmParams& p, int sms)
     if (g.epi == GEMM_EPI_SWIGLU && (bn < 128 || g.N % bn != 0)) continue;
     const long long tiles = (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch;
     const long long rounds = (tiles + sms - 1) / sms;
-    const long long cost = GEMM_COST_PERSISTENT + rounds * kblocks * (128 + bn);
-    if (best.cost < 0 || cost < best.cost) best = {cost, bn, 1};
+    const double cost = (double)rounds * kblocks * (128 + bn);
+    if (best.cost < 0 || cost < best.cost) best = {cost, bn, 1, false};
   }
   return best;
 }
 
-// Split-K clusters: the column tile and the K split whose CTAs each load the
-// fewest bytes, with every cluster resident at once when K is split.
+// Few rows (a decode batch, at most two 128-row tiles): every plan of the
+// persistent kernel and of the split-K kernel (K split over a cluster, partial
+// tiles reduced through distributed shared memory) was timed on B200 as a
+// chain of dependent launches (graph replay with programmatic dependent
+// launch) over 13 projection shapes of 64-256 rows, and the times fitted, in
+// microseconds, with kb the 64-wide K blocks a CTA covers:
+//   persistent:           3.64 + 1.515e-3 kb (128 + BN) rounds
+//   split-K, ks = 1:      5.99 + 1.515e-3 kb (128 + BN) waves  (+ 2.2 with a residual)
+//   split-K, ks > 1:      4.65 + 1.515e-3 kb (128 + BN) + 1.64e-2 BN (ks - 1) / ks
+// The last term is the reduction's distributed-shared-memory traffic.  A K
+// split is taken only when its clusters fill at most 3/4 of the resident
+// cluster slots: fuller launches of 8-CTA clusters ran as two waves.
 template <int EPI>
-static GemmPlan plan_splitk(const GemmArgs& g, const GemmParams& p) {
+static GemmPlan plan_few_rows(const GemmArgs& g, const GemmParams& p, int sms) {
   const int kblocks = (g.K + 63) / 64;
   GemmPlan best;
   for (int bn : {64, 128, 256}) {
     if (EPI == GEMM_EPI_SWIGLU && (bn < 128 || g.N % bn != 0)) continue;
     const long long tiles = (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch;
-    for (int ks : {8, 4, 2, 1}) {
+    const long long rounds = (tiles + sms - 1) / sms;
+    const double per_kb = 1.515e-3 * (128 + bn);
+    GemmPlan cand{3.64 + per_kb * kblocks * rounds, bn, 1, false};
+    if (best.cost < 0 || cand.cost < best.cost) best = cand;
+    for (int ks : {1, 2, 4, 8}) {
       if (ks > kblocks && ks > 1) continue;
       const int slots = bn == 64 ? splitk_slots<64, EPI>(ks)
                                  : (bn == 128 ? splitk_slots<128, EPI>(ks) : splitk_slots<256, EPI>(ks));
-      if (tiles > slots && ks > 1) continue;
+      if (ks > 1 && 4 * tiles > 3LL * slots) continue;
       const long long kb_per = (kblocks + ks - 1) / ks;
       const long long waves = (tiles + slots - 1) / slots;
-      const long long cost = GEMM_COST_SPLITK + (128 + bn) * kb_per * (2 * waves - 1 + waves) / 2;
-      if (best.cost < 0 || cost < best.cost) best = {cost, bn, ks};
+      const double cost = ks == 1 ? 5.99 + per_kb * kb_per * waves + (g.beta != 0.f ? 2.2 : 0.0)
+                                  : 4.65 + per_kb * kb_per + 1.64e-2 * bn * (ks - 1) / ks;
+      if (cost < best.cost) best = {cost, bn, ks, true};
     }
   }
   return best;
@@ -1378,19 +1417,20 @@ yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
   p.vec = (reinterpret_cast<uintptr_t>(g.C) & 15) == 0 && g.ldc % vec_elems == 0 &&
           g.c_bstride % vec_elems == 0;
   const int sms = sm_count();
-  const GemmPlan persistent = plan_persistent(g, p, sms);
-  // a decode batch: split K over a cluster, unless the persistent kernel's
-  // rounds of whole-K tiles cost less (short K, many columns)
+  GemmPlan persistent = plan_persistent(g, p, sms);
+  // a decode batch: the K split over a cluster or the persistent kernel,
+  // whichever the timed model prefers
   if (p.m_tiles <= 2 && (g.epi != GEMM_EPI_SWIGLU || g.N % 128 == 0)) {
-    GemmPlan split;
-    if (g.epi == GEMM_EPI_F32) split = plan_splitk<GEMM_EPI_F32>(g, p);
-    else if (g.epi == GEMM_EPI_BF16) split = plan_splitk<GEMM_EPI_BF16>(g, p);
-    else split = plan_splitk<GEMM_EPI_SWIGLU>(g, p);
-    if (split.cost <= persistent.cost) {
-      if (g.epi == GEMM_EPI_F32) return launch_splitk_plan<GEMM_EPI_F32>(g, p, split, s);
-      if (g.epi == GEMM_EPI_BF16) return launch_splitk_plan<GEMM_EPI_BF16>(g, p, split, s);
-      return launch_splitk_plan<GEMM_EPI_SWIGLU>(g, p, split, s);
+    GemmPlan few;
+    if (g.epi == GEMM_EPI_F32) few = plan_few_rows<GEMM_EPI_F32>(g, p, sms);
+    else if (g.epi == GEMM_EPI_BF16) few = plan_few_rows<GEMM_EPI_BF16>(g, p, sms);
+    else few = plan_few_rows<GEMM_EPI_SWIGLU>(g, p, sms);
+    if (few.split) {
+      if (g.epi == GEMM_EPI_F32) return launch_splitk_plan<GEMM_EPI_F32>(g, p, few, s);
+      if (g.epi == GEMM_EPI_BF16) return launch_splitk_plan<GEMM_EPI_BF16>(g, p, few, s);
+      return launch_splitk_plan<GEMM_EPI_SWIGLU>(g, p, few, s);
     }
+    persistent = few;
   }
   // enough 256 x 256 tiles to fill the pairs: the CTA-pair kernel
   const long long pair_tiles = (long long)((g.M + 255) / 256) * ((g.N + 255) / 256) * g.batch;
