@@ -101,6 +101,16 @@ struct yuf_model {
     cudaGraphExec_t exec;
   };
   bool decode_graphs = false;
+  // a decode step runs the low-rank projections (x_{w,a,g} L1, then L2) on a
+  // second stream beside the r/k/v projection: both read the mixes, and the
+  // time-mix epilogue joins them
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  ~yuf_model() {
+    if (ev_join) cudaEventDestroy(ev_join);
+    if (ev_fork) cudaEventDestroy(ev_fork);
+    if (side) cudaStreamDestroy(side);
+  }
   size_t ws_gen = 0;
   std::vector<DecodeGraph> graphs;
   void drop_graphs() {
@@ -357,13 +367,24 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     const size_t esz = m->precision == YUF_PRECISION_BF16_WEIGHTS ? 2 : 4;
     const char* mixed_hi = static_cast<const char*>(mixed) + 3 * RD * esz;  // w, a, g mixes
     // r, k, v; then x_{w,a,g} L1 with tanh on the w branch (bf16 in bf16 mode),
-    // written into the lr1 buffer, which feeds L2
+    // written into the lr1 buffer, which feeds L2.  A decode step runs the two
+    // low-rank projections on the side stream, concurrently with r, k, v.
+    const bool fork = T == 1 && m->side != nullptr;
+    cudaStream_t s_lr = fork ? m->side : s;
+    if (fork) {
+      Y_CUDA(cudaEventRecord(m->ev_fork, s));
+      Y_CUDA(cudaStreamWaitEvent(m->side, m->ev_fork, 0));
+    }
+    Y_TRY(proj(m, mixed_hi, d, (long long)rows, Lw.W_lr1, lr, w.lr1, lr, (long long)rows * lr, (int)rows, lr,
+               d, 3, GEMM_EPI_BF16, false, s_lr, 0, true));
+    Y_TRY(proj(m, w.lr1, lr, (long long)rows, Lw.W_lr2, d, w.lr2, d, RD, (int)rows, d, lr, 3, GEMM_EPI_F32,
+               false, s_lr));
     Y_TRY(proj(m, mixed, d, (long long)rows, Lw.W_rkv, d, w.rkv, d, RD, (int)rows, d, d, 3, GEMM_EPI_F32,
                false, s));
-    Y_TRY(proj(m, mixed_hi, d, (long long)rows, Lw.W_lr1, lr, w.lr1, lr, (long long)rows * lr, (int)rows, lr,
-               d, 3, GEMM_EPI_BF16, false, s, 0, true));
-    Y_TRY(proj(m, w.lr1, lr, (long long)rows, Lw.W_lr2, d, w.lr2, d, RD, (int)rows, d, lr, 3, GEMM_EPI_F32,
-               false, s));
+    if (fork) {
+      Y_CUDA(cudaEventRecord(m->ev_join, m->side));
+      Y_CUDA(cudaStreamWaitEvent(s, m->ev_join, 0));
+    }
     launch_timemix_post(w.rkv + RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD, Lw.w0, Lw.a0, Lw.k_k, Lw.k_a,
                         w.w_raw, w.k_adj, w.a_op, w.b_op, w.g, (int)rows, H, N, s);
     if (T == 1)
@@ -620,6 +641,9 @@ yuf_status_t model_create_from_map(const yuf_model_config* cfg, int precision, i
   m->d_err = static_cast<int*>(m->alloc(sizeof(int)));
   if (!m->d_err) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
   Y_CUDA(cudaMemset(m->d_err, 0, sizeof(int)));
+  Y_CUDA(cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking));
+  Y_CUDA(cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming));
+  Y_CUDA(cudaEventCreateWithFlags(&m->ev_join, cudaEventDisableTiming));
   Y_TRY(load_weights(m.get(), t));
   *out = m.release();
   return YUF_OK;
