@@ -385,19 +385,30 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
       Y_CUDA(cudaEventRecord(m->ev_join, m->side));
       Y_CUDA(cudaStreamWaitEvent(s, m->ev_join, 0));
     }
-    launch_timemix_post(w.rkv + RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD, Lw.w0, Lw.a0, Lw.k_k, Lw.k_a,
-                        w.w_raw, w.k_adj, w.a_op, w.b_op, w.g, (int)rows, H, N, s);
-    if (T == 1)
-      Y_TRY(wkv7_decode_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S,
-                                 B * H, N, s));
-    else if (wkv7_chunk_tc_applies(B, T, H, N))
-      Y_TRY(wkv7_chunk_tc(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, B, T, H, N, s));
-    else if (wkv7_parallel_applies(B, T, H, N))
-      Y_TRY(wkv7_parallel(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, B, T, H,
-                          N, w.scan + scan_rosa_floats(m, rows), s));
-    else
-      Y_TRY(wkv7_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, nullptr,
-                          nullptr, B, T, H, N, false, s));
+    // a decode step folds the time-mix epilogue into the WKV step (one launch);
+    // debug runs keep it separate, so that its outputs can be dumped
+    yuf_status_t tm_st = YUF_ERR_UNSUPPORTED;
+    if (T == 1 && !m->debug)
+      tm_st = wkv7_decode_tm_dispatch(w.rkv, w.rkv + RD, w.rkv + 2 * RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD, Lw.w0,
+                                      Lw.a0, Lw.k_k, Lw.k_a, w.g, S, w.y, S, B * H, H, N, s);
+    if (tm_st != YUF_ERR_UNSUPPORTED) {
+      Y_TRY(tm_st);
+    } else {
+      launch_timemix_post(w.rkv + RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD, Lw.w0, Lw.a0, Lw.k_k, Lw.k_a,
+                          w.w_raw, w.k_adj, w.a_op, w.b_op, w.g, (int)rows, H, N, s);
+      if (T == 1)
+        Y_TRY(wkv7_decode_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S,
+                                   B * H, N, s));
+      else if (wkv7_chunk_tc_applies(B, T, H, N))
+        Y_TRY(wkv7_chunk_tc(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, B, T, H, N,
+                            s));
+      else if (wkv7_parallel_applies(B, T, H, N))
+        Y_TRY(wkv7_parallel(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, B, T, H,
+                            N, w.scan + scan_rosa_floats(m, rows), s));
+      else
+        Y_TRY(wkv7_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, nullptr,
+                            nullptr, B, T, H, N, false, s));
+    }
     const void* att = ln_in(w.y, Lw.ln_o_w, Lw.ln_o_b, w.g);
     if (m->debug) {
       dump(m, "ln0", li, w.xt, RD, s);

@@ -37,6 +37,10 @@ yuf_status_t wkv7_dispatch(const float* r, const float* w, const float* k, const
                            cudaStream_t stream);
 // one-time setup of the decode kernels for head size N (outside graph capture)
 void wkv7_decode_prepare(int N);
+yuf_status_t wkv7_decode_tm_dispatch(const float* r, const float* k, const float* v, const float* lw,
+                                     const float* la, const float* lg, const float* w0, const float* a0,
+                                     const float* k_k, const float* k_a, float* g, const float* s0, float* y,
+                                     float* s_out, int BH, int H, int N, cudaStream_t stream);
 yuf_status_t wkv7_decode_dispatch(const float* r, const float* w, const float* k, const float* v,
                                   const float* a, const float* b, const float* s0, float* y,
                                   float* s_out, int BH, int N, cudaStream_t stream);

@@ -116,25 +116,40 @@ struct DecRing {
   static constexpr int VEC_BYTES = N * 4;
   static constexpr int SLOT = STATE_BYTES + 6 * VEC_BYTES;  // state, r, w, k, v, a, b
   static constexpr int STAGES = SLOT * 4 <= 96 * 1024 ? 4 : (SLOT * 3 <= 128 * 1024 ? 3 : 2);
-  static constexpr int SMEM = STAGES * SLOT + N * 4 + STAGES * 8;  // slots, retention, barriers
+  static constexpr int EXTRA = (6 * N + 16) * 4;  // retention; the time-mix scratch (TM)
+  static constexpr int SMEM = STAGES * SLOT + EXTRA + STAGES * 8;  // slots, scratch, barriers
   static_assert(SLOT % 16 == 0 && VEC_BYTES % 16 == 0, "bulk copies need 16-byte multiples");
+  static_assert(N % 8 == 0, "N * 4 threads in whole warps");
 };
 
 __device__ unsigned int g_decode_wait_timeouts;
 
-template <int N>
+// The time-mix epilogue of the head, folded in (TM): the slot's vectors are
+// then r, the w / a / g low-rank outputs, k and v as the projections left them,
+// and each head first forms (yufmusicgen/model.py:113-125)
+//   w = w0 + lw,  kk = normalize(k * k_k),  alpha = sigmoid(a0 + la),
+//   a = -kk,  b = kk * alpha,  k' = k * (1 + (alpha - 1) * k_a),  g = sigmoid(lg)
+// (g to global for the output gate), the arithmetic of timemix_post_kernel.
+struct DecTm {
+  const float *w0, *a0, *k_k, *k_a;  // [H * N] per-channel parameters
+  float* g;                          // [BH * N] output gate
+  int H;
+};
+
+template <int N, bool TM>
 __global__ void __launch_bounds__(N * 4)
     wkv7_decode_ring_kernel(const float* __restrict__ r, const float* __restrict__ w,
                             const float* __restrict__ k, const float* __restrict__ v,
                             const float* __restrict__ a, const float* __restrict__ b,
-                            const float* s0, float* __restrict__ y, float* s_out, int BH) {
+                            const float* s0, float* __restrict__ y, float* s_out, int BH, const DecTm tm) {
   pdl_wait();
   pdl_trigger();
   using K = DecRing<N>;
   constexpr int G = 4, C = N / G, C2 = C / 2;
   extern __shared__ __align__(128) unsigned char dsm[];
   float* ret = reinterpret_cast<float*>(dsm + K::STAGES * K::SLOT);
-  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + K::STAGES * K::SLOT + N * 4);
+  float* tmv = ret + N;                 // TM: a, b, k', kk, alpha (N each), the warps' partial norms
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + K::STAGES * K::SLOT + K::EXTRA);
   const int tid = threadIdx.x;
   const int row = tid / G, g = tid - row * G, j0 = g * C;
   const int first = blockIdx.x, stride = gridDim.x;
@@ -174,13 +189,49 @@ __global__ void __launch_bounds__(N * 4)
       return;
     }
     float* St = reinterpret_cast<float*>(dsm + sl * K::SLOT);
-    const float* vec = St + N * N;  // r, w, k, v, a, b
-    if (tid < N) ret[tid] = __expf(W_SCALE * sigmoidf_fast(vec[N + tid]));
-    __syncthreads();
-    const float* W_ = ret + j0;
+    const float* vec = St + N * N;  // r, w, k, v, a, b (TM: r, lw, k, v, la, lg)
     const float* K_ = vec + 2 * N + j0;
     const float* A_ = vec + 4 * N + j0;
     const float* B_ = vec + 5 * N + j0;
+    if constexpr (TM) {
+      const int bh = first + j * stride;
+      const int h = bh % tm.H;
+      float kk2 = 0.f;  // this column's |kk|^2 term; 0 past the N columns
+      if (tid < N) {
+        const int c = h * N + tid;
+        const float kv = vec[2 * N + tid];
+        const float kk = kv * tm.k_k[c];
+        const float alpha = sigmoidf_fast(tm.a0[c] + vec[4 * N + tid]);
+        ret[tid] = __expf(W_SCALE * sigmoidf_fast(tm.w0[c] + vec[N + tid]));
+        tmv[2 * N + tid] = kv * (1.f + (alpha - 1.f) * tm.k_a[c]);  // k'
+        tmv[3 * N + tid] = kk;                                      // kk before the norm
+        tmv[4 * N + tid] = alpha;
+        tm.g[(size_t)bh * N + tid] = sigmoidf_fast(vec[5 * N + tid]);
+        kk2 = kk * kk;
+      }
+      // every thread of the CTA in the butterfly (no branch around it), one
+      // partial per warp
+      kk2 = group_sum<32>(kk2);
+      if ((tid & 31) == 0) tmv[5 * N + (tid >> 5)] = kk2;
+      __syncthreads();
+      if (tid < N) {
+        float sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < N / 8; ++q) sum += tmv[5 * N + q];  // the N * 4 / 32 warps' partials
+        const float inv = 1.f / fmaxf(sqrtf(sum), 1e-12f);  // F.normalize eps (model.py:116)
+        const float kk = tmv[3 * N + tid] * inv;
+        tmv[tid] = -kk;                         // a
+        tmv[N + tid] = kk * tmv[4 * N + tid];  // b
+      }
+      __syncthreads();
+      K_ = tmv + 2 * N + j0;
+      A_ = tmv + j0;
+      B_ = tmv + N + j0;
+    } else {
+      if (tid < N) ret[tid] = __expf(W_SCALE * sigmoidf_fast(vec[N + tid]));
+      __syncthreads();
+    }
+    const float* W_ = ret + j0;
     const float* R_ = vec + j0;
     const float vi = vec[3 * N + row];
     float* Srow = St + row * N + j0;
@@ -231,7 +282,7 @@ unsigned int wkv7_decode_wait_timeouts() {
 
 // Resident ring CTAs per SM for head size N on the current device (0: the ring
 // cannot run); sets the kernel's shared-memory limit on first use per device.
-template <int N>
+template <int N, bool TM>
 static int ring_blocks_per_sm() {
   static int cache[64];  // per device: blocks + 1, 0 = not yet known
   int dev = 0;
@@ -241,9 +292,9 @@ static int ring_blocks_per_sm() {
   }
   if (cache[dev]) return cache[dev] - 1;
   int v = 0;
-  if (cudaFuncSetAttribute(wkv7_decode_ring_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(wkv7_decode_ring_kernel<N, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            DecRing<N>::SMEM) != cudaSuccess ||
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, wkv7_decode_ring_kernel<N>, N * 4,
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, wkv7_decode_ring_kernel<N, TM>, N * 4,
                                                     DecRing<N>::SMEM) != cudaSuccess) {
     cudaGetLastError();
     v = 0;
@@ -280,13 +331,13 @@ static int sm_count() {
 // size N; the engine calls this before capturing decode graphs.
 void wkv7_decode_prepare(int N) {
   switch (N) {
-    case 16: ring_blocks_per_sm<16>(); break;
-    case 32: ring_blocks_per_sm<32>(); break;
-    case 40: ring_blocks_per_sm<40>(); break;
-    case 48: ring_blocks_per_sm<48>(); break;
-    case 64: ring_blocks_per_sm<64>(); break;
-    case 96: ring_blocks_per_sm<96>(); break;
-    case 128: ring_blocks_per_sm<128>(); break;
+    case 16: ring_blocks_per_sm<16, false>(); ring_blocks_per_sm<16, true>(); break;
+    case 32: ring_blocks_per_sm<32, false>(); ring_blocks_per_sm<32, true>(); break;
+    case 40: ring_blocks_per_sm<40, false>(); ring_blocks_per_sm<40, true>(); break;
+    case 48: ring_blocks_per_sm<48, false>(); ring_blocks_per_sm<48, true>(); break;
+    case 64: ring_blocks_per_sm<64, false>(); ring_blocks_per_sm<64, true>(); break;
+    case 96: ring_blocks_per_sm<96, false>(); ring_blocks_per_sm<96, true>(); break;
+    case 128: ring_blocks_per_sm<128, false>(); ring_blocks_per_sm<128, true>(); break;
     default: break;
   }
   sm_count();
@@ -306,11 +357,11 @@ yuf_status_t wkv7_decode_dispatch(const float* r, const float* w, const float* k
   switch (N) {
 #define CASE(NN)                                                                                 \
   case NN: {                                                                                     \
-    const int per_sm = ring ? ring_blocks_per_sm<NN>() : 0;                                      \
+    const int per_sm = ring ? ring_blocks_per_sm<NN, false>() : 0;                               \
     if (per_sm > 0) {                                                                            \
       const int grid = std::min(BH, per_sm * sm_count());                                        \
-      launch_k(wkv7_decode_ring_kernel<NN>, dim3(grid), dim3(NN * 4), DecRing<NN>::SMEM, stream,                   \
-          r, w, k, v, a, b, s0, y, s_out, BH);                                                   \
+      launch_k(wkv7_decode_ring_kernel<NN, false>, dim3(grid), dim3(NN * 4), DecRing<NN>::SMEM, stream,            \
+          r, w, k, v, a, b, s0, y, s_out, BH, DecTm{});                                          \
       return check_launch("wkv7_decode_ring_kernel");                                            \
     }                                                                                            \
     const int grid = std::min(BH, decode_blocks_per_sm<NN>() * sm_count());                     \
@@ -321,6 +372,38 @@ yuf_status_t wkv7_decode_dispatch(const float* r, const float* w, const float* k
 #undef CASE
     default:
       set_error("wkv7: head size N=%d has no kernel (supported: 16, 32, 40, 48, 64, 96, 128)", N);
+      return YUF_ERR_UNSUPPORTED;
+  }
+}
+
+// The decode step with the time-mix epilogue folded in: r, k, v and the w / a /
+// g low-rank outputs as the projections left them ([BH, N] rows), the layer's
+// per-channel w0, a0, k_k, k_a ([H * N]); writes y, the state and the output
+// gate g.  YUF_ERR_UNSUPPORTED when the bulk-copy ring cannot run (a buffer off
+// a 16-byte boundary, no state, no occupancy): the caller then takes the
+// separate epilogue kernel and wkv7_decode_dispatch.
+yuf_status_t wkv7_decode_tm_dispatch(const float* r, const float* k, const float* v, const float* lw,
+                                     const float* la, const float* lg, const float* w0, const float* a0,
+                                     const float* k_k, const float* k_a, float* g, const float* s0, float* y,
+                                     float* s_out, int BH, int H, int N, cudaStream_t stream) {
+  if (BH <= 0) return YUF_OK;
+  const bool ring = s0 && s_out && H > 0 && BH % H == 0 && aligned16(s0) && aligned16(s_out) && aligned16(r) &&
+                    aligned16(k) && aligned16(v) && aligned16(lw) && aligned16(la) && aligned16(lg);
+  if (!ring) return YUF_ERR_UNSUPPORTED;
+  const DecTm tm{w0, a0, k_k, k_a, g, H};
+  switch (N) {
+#define CASE(NN)                                                                                 \
+  case NN: {                                                                                     \
+    const int per_sm = ring_blocks_per_sm<NN, true>();                                           \
+    if (per_sm <= 0) return YUF_ERR_UNSUPPORTED;                                                 \
+    const int grid = std::min(BH, per_sm * sm_count());                                          \
+    launch_k(wkv7_decode_ring_kernel<NN, true>, dim3(grid), dim3(NN * 4), DecRing<NN>::SMEM, stream, r, lw, k, v, \
+             la, lg, s0, y, s_out, BH, tm);                                                      \
+    return check_launch("wkv7_decode_ring_kernel (time-mix)");                                   \
+  }
+    CASE(16) CASE(32) CASE(40) CASE(48) CASE(64) CASE(96) CASE(128)
+#undef CASE
+    default:
       return YUF_ERR_UNSUPPORTED;
   }
 }
