@@ -110,13 +110,16 @@ __global__ void __launch_bounds__(N * 4)
 // back with a bulk store.  STAGES-1 heads are in flight while one is computed,
 // and the copies move whole contiguous blocks, so the kernel streams at close
 // to copy bandwidth instead of waiting on per-thread load latency.
-template <int N>
+template <int N, bool TM = false>
 struct DecRing {
   static constexpr int STATE_BYTES = N * N * 4;
   static constexpr int VEC_BYTES = N * 4;
-  static constexpr int SLOT = STATE_BYTES + 6 * VEC_BYTES;  // state, r, w, k, v, a, b
+  // state, r, w, k, v, a, b; TM: state, r, lw, k, v, la, lg, then the head's
+  // w0, a0, k_k, k_a
+  static constexpr int NVEC = TM ? 10 : 6;
+  static constexpr int SLOT = STATE_BYTES + NVEC * VEC_BYTES;
   static constexpr int STAGES = SLOT * 4 <= 96 * 1024 ? 4 : (SLOT * 3 <= 128 * 1024 ? 3 : 2);
-  static constexpr int EXTRA = (6 * N + 16) * 4;  // retention; the time-mix scratch (TM)
+  static constexpr int EXTRA = (TM ? 6 * N + 16 : N) * 4;  // retention; the time-mix scratch
   static constexpr int SMEM = STAGES * SLOT + EXTRA + STAGES * 8;  // slots, scratch, barriers
   static_assert(SLOT % 16 == 0 && VEC_BYTES % 16 == 0, "bulk copies need 16-byte multiples");
   static_assert(N % 8 == 0, "N * 4 threads in whole warps");
@@ -144,7 +147,7 @@ __global__ void __launch_bounds__(N * 4)
                             const float* s0, float* __restrict__ y, float* s_out, int BH, const DecTm tm) {
   pdl_wait();
   pdl_trigger();
-  using K = DecRing<N>;
+  using K = DecRing<N, TM>;
   constexpr int G = 4, C = N / G, C2 = C / 2;
   extern __shared__ __align__(128) unsigned char dsm[];
   float* ret = reinterpret_cast<float*>(dsm + K::STAGES * K::SLOT);
@@ -166,6 +169,13 @@ __global__ void __launch_bounds__(N * 4)
 #pragma unroll
     for (int q = 0; q < 6; ++q)
       bulk_load(slot + K::STATE_BYTES + q * K::VEC_BYTES, vsrc[q] + bh * N, K::VEC_BYTES, &full[sl]);
+    if constexpr (TM) {
+      const size_t c0 = (size_t)((int)bh % tm.H) * N;
+      const float* psrc[4] = {tm.w0, tm.a0, tm.k_k, tm.k_a};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        bulk_load(slot + K::STATE_BYTES + (6 + q) * K::VEC_BYTES, psrc[q] + c0, K::VEC_BYTES, &full[sl]);
+    }
   };
   if (tid == 0) {
     for (int sl = 0; sl < K::STAGES; ++sl) mbar_init(&full[sl], 1);
@@ -195,15 +205,14 @@ __global__ void __launch_bounds__(N * 4)
     const float* B_ = vec + 5 * N + j0;
     if constexpr (TM) {
       const int bh = first + j * stride;
-      const int h = bh % tm.H;
+      const float* prm = vec + 6 * N;  // the head's w0, a0, k_k, k_a
       float kk2 = 0.f;  // this column's |kk|^2 term; 0 past the N columns
       if (tid < N) {
-        const int c = h * N + tid;
         const float kv = vec[2 * N + tid];
-        const float kk = kv * tm.k_k[c];
-        const float alpha = sigmoidf_fast(tm.a0[c] + vec[4 * N + tid]);
-        ret[tid] = __expf(W_SCALE * sigmoidf_fast(tm.w0[c] + vec[N + tid]));
-        tmv[2 * N + tid] = kv * (1.f + (alpha - 1.f) * tm.k_a[c]);  // k'
+        const float kk = kv * prm[2 * N + tid];
+        const float alpha = sigmoidf_fast(prm[N + tid] + vec[4 * N + tid]);
+        ret[tid] = __expf(W_SCALE * sigmoidf_fast(prm[tid] + vec[N + tid]));
+        tmv[2 * N + tid] = kv * (1.f + (alpha - 1.f) * prm[3 * N + tid]);  // k'
         tmv[3 * N + tid] = kk;                                      // kk before the norm
         tmv[4 * N + tid] = alpha;
         tm.g[(size_t)bh * N + tid] = sigmoidf_fast(vec[5 * N + tid]);
@@ -293,9 +302,9 @@ static int ring_blocks_per_sm() {
   if (cache[dev]) return cache[dev] - 1;
   int v = 0;
   if (cudaFuncSetAttribute(wkv7_decode_ring_kernel<N, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           DecRing<N>::SMEM) != cudaSuccess ||
+                           DecRing<N, TM>::SMEM) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, wkv7_decode_ring_kernel<N, TM>, N * 4,
-                                                    DecRing<N>::SMEM) != cudaSuccess) {
+                                                    DecRing<N, TM>::SMEM) != cudaSuccess) {
     cudaGetLastError();
     v = 0;
   }
@@ -388,7 +397,8 @@ yuf_status_t wkv7_decode_tm_dispatch(const float* r, const float* k, const float
                                      float* s_out, int BH, int H, int N, cudaStream_t stream) {
   if (BH <= 0) return YUF_OK;
   const bool ring = s0 && s_out && H > 0 && BH % H == 0 && aligned16(s0) && aligned16(s_out) && aligned16(r) &&
-                    aligned16(k) && aligned16(v) && aligned16(lw) && aligned16(la) && aligned16(lg);
+                    aligned16(k) && aligned16(v) && aligned16(lw) && aligned16(la) && aligned16(lg) &&
+                    aligned16(w0) && aligned16(a0) && aligned16(k_k) && aligned16(k_a);
   if (!ring) return YUF_ERR_UNSUPPORTED;
   const DecTm tm{w0, a0, k_k, k_a, g, H};
   switch (N) {
@@ -397,7 +407,7 @@ yuf_status_t wkv7_decode_tm_dispatch(const float* r, const float* k, const float
     const int per_sm = ring_blocks_per_sm<NN, true>();                                           \
     if (per_sm <= 0) return YUF_ERR_UNSUPPORTED;                                                 \
     const int grid = std::min(BH, per_sm * sm_count());                                          \
-    launch_k(wkv7_decode_ring_kernel<NN, true>, dim3(grid), dim3(NN * 4), DecRing<NN>::SMEM, stream, r, lw, k, v, \
+    launch_k(wkv7_decode_ring_kernel<NN, true>, dim3(grid), dim3(NN * 4), DecRing<NN, true>::SMEM, stream, r, lw, k, v, \
              la, lg, s0, y, s_out, BH, tm);                                                      \
     return check_launch("wkv7_decode_ring_kernel (time-mix)");                                   \
   }
