@@ -299,3 +299,32 @@ def test_benchmark_size_prefill_bf16_weights_per_layer(golden, fixture, cfgd, se
     bad = {k: v for k, v in rel.items() if v[0] > BF_REGION_MAX or v[1] > BF_REGION_RMS}
     assert not bad, bad
     eng.close()
+
+
+@pytest.mark.parametrize("cfgd,precision,T", [
+    (C.BASE_0P1B, "fp32", 256),
+    (C.BASE_0P1B, "fp32", 300),
+    (C.BASE_0P1B, "bf16", 256),
+    (dict(C.LONG_1K, n_layers=2), "fp32", 256),
+])
+def test_chunked_prefill_with_the_time_mix_folded_in_matches_the_separate_epilogue(cfgd, precision, T):
+    """B*H = 128, T >= 256 (T = 300: a ragged last chunk): the prefill takes the chunked tensor-core WKV scan with
+    the time-mix epilogue folded into its prep (and the output norm applying
+    sigmoid to the gate's pre-activation).  Debug runs keep timemix_post in front
+    of the same scan; every position's logits and the next decode step agree
+    (fp32: 1e-4 abs + 1e-4 rel, the two differ only in the order of the |kk|
+    sums; bf16 weights: the stated bf16 tolerance)."""
+    cfg, w, eng = make(cfgd, 3, "perturbed", precision=precision, n_slots=8)
+    ids = torch.as_tensor(zipf_ids(8, T, seed=5, vocab=cfg.vocab_size), dtype=torch.int32, device="cuda")
+    nxt = torch.as_tensor(zipf_ids(8, 1, seed=6, vocab=cfg.vocab_size), dtype=torch.int32, device="cuda")
+    outs = []
+    for debug in (False, True):
+        eng.reset_state()
+        if debug:
+            eng.set_debug(True, regions=["logits"])
+        _, allv = eng.prefill(ids, all_logits=True)
+        step = eng.step(nxt.reshape(-1))
+        outs.append((allv.cpu().numpy(), step.cpu().numpy()))
+    rtol, atol = (1e-4, 1e-4) if precision == "fp32" else (BF_RTOL, BF_ATOL)
+    np.testing.assert_allclose(outs[0][0], outs[1][0], rtol=rtol, atol=atol)
+    np.testing.assert_allclose(outs[0][1], outs[1][1], rtol=rtol, atol=atol)

@@ -334,12 +334,13 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
   // bf16-weight mode: the producers of GEMM inputs (mixes, layer norms, the FFN
   // gate) write bf16 straight into the staging buffer instead of fp32 plus a copy
   const bool bf = m->precision == YUF_PRECISION_BF16_WEIGHTS;
-  auto ln_in = [&](const float* x, const float* lw, const float* lb, const float* gate) -> const void* {
+  auto ln_in = [&](const float* x, const float* lw, const float* lb, const float* gate,
+                   bool gate_sig = false) -> const void* {
     if (bf) {
-      launch_layernorm<__nv_bfloat16>(x, lw, lb, gate, w.bf, (int)rows, d, s);
+      launch_layernorm<__nv_bfloat16>(x, lw, lb, gate, w.bf, (int)rows, d, s, gate_sig);
       return w.bf;
     }
-    launch_layernorm<float>(x, lw, lb, gate, w.tmp, (int)rows, d, s);
+    launch_layernorm<float>(x, lw, lb, gate, w.tmp, (int)rows, d, s, gate_sig);
     return w.tmp;
   };
   for (int li = 0; li < m->cfg.n_layers; ++li) {
@@ -385,12 +386,27 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
       Y_CUDA(cudaEventRecord(m->ev_join, m->side));
       Y_CUDA(cudaStreamWaitEvent(s, m->ev_join, 0));
     }
-    // a decode step folds the time-mix epilogue into the WKV step (one launch);
-    // debug runs keep it separate, so that its outputs can be dumped
+    // The decode step and the chunked tensor-core prefill scan fold the time-mix
+    // epilogue into the WKV kernel (no separate pass over the projections'
+    // outputs); the prefill scan leaves the output gate to the output norm,
+    // which takes sigmoid(lg) itself.  Debug runs keep the epilogue separate, so
+    // that its outputs can be dumped.
     yuf_status_t tm_st = YUF_ERR_UNSUPPORTED;
-    if (T == 1 && !m->debug)
-      tm_st = wkv7_decode_tm_dispatch(w.rkv, w.rkv + RD, w.rkv + 2 * RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD, Lw.w0,
-                                      Lw.a0, Lw.k_k, Lw.k_a, w.g, S, w.y, S, B * H, H, N, s);
+    const float* out_gate = w.g;
+    bool out_gate_sig = false;
+    if (!m->debug) {
+      if (T == 1) {
+        tm_st = wkv7_decode_tm_dispatch(w.rkv, w.rkv + RD, w.rkv + 2 * RD, w.lr2, w.lr2 + RD, w.lr2 + 2 * RD,
+                                        Lw.w0, Lw.a0, Lw.k_k, Lw.k_a, w.g, S, w.y, S, B * H, H, N, s);
+      } else if (wkv7_chunk_tc_applies(B, T, H, N)) {
+        tm_st = wkv7_chunk_tc_tm(w.rkv, w.rkv + RD, w.rkv + 2 * RD, w.lr2, w.lr2 + RD, Lw.w0, Lw.a0, Lw.k_k,
+                                 Lw.k_a, S, w.y, S, B, T, H, N, s);
+        if (tm_st != YUF_ERR_UNSUPPORTED) {
+          out_gate = w.lr2 + 2 * RD;
+          out_gate_sig = true;
+        }
+      }
+    }
     if (tm_st != YUF_ERR_UNSUPPORTED) {
       Y_TRY(tm_st);
     } else {
@@ -409,7 +425,7 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
         Y_TRY(wkv7_dispatch(w.rkv, w.w_raw, w.k_adj, w.rkv + 2 * RD, w.a_op, w.b_op, S, w.y, S, nullptr,
                             nullptr, B, T, H, N, false, s));
     }
-    const void* att = ln_in(w.y, Lw.ln_o_w, Lw.ln_o_b, w.g);
+    const void* att = ln_in(w.y, Lw.ln_o_w, Lw.ln_o_b, out_gate, out_gate_sig);
     if (m->debug) {
       dump(m, "ln0", li, w.xt, RD, s);
       dump(m, "r", li, w.rkv, RD, s);

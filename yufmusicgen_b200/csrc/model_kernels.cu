@@ -65,11 +65,13 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const float* __res
 }
 
 // LayerNorm over d (eps 1e-5, biased variance: nn.LayerNorm).  One warp per row.
-// Optionally multiplies by gate[row, :] after the affine (out_norm(y) * g).
+// Optionally multiplies by gate[row, :] after the affine (out_norm(y) * g), or
+// by sigmoid(gate[row, :]) when gate_sig (the gate's pre-activation, as the
+// low-rank projection left it).
 template <typename OUT>
 __global__ void layernorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                  const float* __restrict__ b, const float* __restrict__ gate,
-                                 OUT* __restrict__ out, int rows, int d) {
+                                 OUT* __restrict__ out, int rows, int d, int gate_sig) {
   pdl_wait();
   pdl_trigger();
   const int warps = blockDim.x >> 5;
@@ -88,7 +90,10 @@ __global__ void layernorm_kernel(const float* __restrict__ x, const float* __res
   const float rstd = rsqrtf(warp_sum(q) / d + 1e-5f);
   for (int i = lane; i < d; i += 32) {
     float v = (xr[i] - mean) * rstd * w[i] + b[i];
-    if (gate) v *= gate[(size_t)row * d + i];
+    if (gate) {
+      const float gv = gate[(size_t)row * d + i];
+      v *= gate_sig ? sigmoidf_fast(gv) : gv;
+    }
     store_out(out, (size_t)row * d + i, v);
   }
 }
@@ -99,7 +104,7 @@ template <typename OUT, int VPL>
 __global__ void __launch_bounds__(128)
     layernorm_reg_kernel(const float* __restrict__ x, const float* __restrict__ w,
                          const float* __restrict__ b, const float* __restrict__ gate,
-                         OUT* __restrict__ out, int rows, int d) {
+                         OUT* __restrict__ out, int rows, int d, int gate_sig) {
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -136,7 +141,8 @@ __global__ void __launch_bounds__(128)
       float4 o = make_float4((v[u].x - mean) * rstd * ww.x + bb.x, (v[u].y - mean) * rstd * ww.y + bb.y,
                              (v[u].z - mean) * rstd * ww.z + bb.z, (v[u].w - mean) * rstd * ww.w + bb.w);
       if (g4) {
-        const float4 gg = g4[i];
+        float4 gg = g4[i];
+        if (gate_sig) gg = make_float4(sigmoidf_fast(gg.x), sigmoidf_fast(gg.y), sigmoidf_fast(gg.z), sigmoidf_fast(gg.w));
         o.x *= gg.x; o.y *= gg.y; o.z *= gg.z; o.w *= gg.w;
       }
       store4(out, (size_t)row * d + 4 * i, o);
@@ -158,7 +164,8 @@ template <typename OUT, bool MIX>
 __global__ void __launch_bounds__(1024)
     ln_row_kernel(const float* __restrict__ x, const float* __restrict__ w,
                   const float* __restrict__ b, const float* __restrict__ gate, OUT* __restrict__ out,
-                  int rows, int d, float* __restrict__ xt, float* prev, const float* __restrict__ mix) {
+                  int rows, int d, float* __restrict__ xt, float* prev, const float* __restrict__ mix,
+                  int gate_sig) {
   pdl_wait();
   pdl_trigger();
   __shared__ float red[32];
@@ -168,7 +175,10 @@ __global__ void __launch_bounds__(1024)
   const float4 v = act ? *reinterpret_cast<const float4*>(x + base) : make_float4(0.f, 0.f, 0.f, 0.f);
   float4 pv = make_float4(0.f, 0.f, 0.f, 0.f), gv = make_float4(1.f, 1.f, 1.f, 1.f);
   if (act && MIX) pv = *reinterpret_cast<const float4*>(prev + base);
-  if (act && !MIX && gate) gv = *reinterpret_cast<const float4*>(gate + base);
+  if (act && !MIX && gate) {
+    gv = *reinterpret_cast<const float4*>(gate + base);
+    if (gate_sig) gv = make_float4(sigmoidf_fast(gv.x), sigmoidf_fast(gv.y), sigmoidf_fast(gv.z), sigmoidf_fast(gv.w));
+  }
   const float mean = block_sum((v.x + v.y) + (v.z + v.w), red) / d;
   const float cx = v.x - mean, cy = v.y - mean, cz = v.z - mean, cw = v.w - mean;
   const float q = act ? fmaf(cx, cx, fmaf(cy, cy, fmaf(cz, cz, cw * cw))) : 0.f;
@@ -393,10 +403,11 @@ void launch_embed(const int32_t* ids, const float* E, float* x, int rows, int d,
 }
 template <typename OUT>
 void launch_layernorm(const float* x, const float* w, const float* b, const float* gate, OUT* out,
-                      int rows, int d, cudaStream_t s) {
+                      int rows, int d, cudaStream_t s, bool gate_sigmoid) {
+  const int gs = gate_sigmoid ? 1 : 0;
   if (rows < 4 * 148 && d % 4 == 0 && d <= 4096) {  // small batch: one CTA per row
     launch_k(ln_row_kernel<OUT, false>, dim3(rows), dim3(((d / 4 + 31) / 32) * 32), 0, s, x, w, b, gate, out, rows, d,
-                                                                         nullptr, nullptr, nullptr);
+                                                                         nullptr, nullptr, nullptr, gs);
     return;
   }
   // one row per warp, four warps per block
@@ -407,7 +418,7 @@ void launch_layernorm(const float* x, const float* w, const float* b, const floa
     switch (vpl) {
 #define CASE(V)                                                                                  \
   case V:                                                                                        \
-    launch_k(layernorm_reg_kernel<OUT, V>, dim3(blocks), dim3(32 * wpb), 0, s, x, w, b, gate, out, rows, d); \
+    launch_k(layernorm_reg_kernel<OUT, V>, dim3(blocks), dim3(32 * wpb), 0, s, x, w, b, gate, out, rows, d, gs); \
     return;
       CASE(1) CASE(2) CASE(3) CASE(4) CASE(5) CASE(6) CASE(7) CASE(8)
 #undef CASE
@@ -415,7 +426,8 @@ void launch_layernorm(const float* x, const float* w, const float* b, const floa
     }
   }
   const int warps = 8;
-  launch_k(layernorm_kernel<OUT>, dim3((rows + warps - 1) / warps), dim3(32 * warps), 0, s, x, w, b, gate, out, rows, d);
+  launch_k(layernorm_kernel<OUT>, dim3((rows + warps - 1) / warps), dim3(32 * warps), 0, s, x, w, b, gate, out, rows, d,
+           gs);
 }
 template <typename OUT>
 bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* xt, float* prev,
@@ -423,7 +435,7 @@ bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* x
   if (d % 4 != 0) return false;
   if (B < 4 * 148 && d <= 4096) {
     launch_k(ln_row_kernel<OUT, true>, dim3(B), dim3(((d / 4 + 31) / 32) * 32), 0, s, x, w, b, nullptr, out, B, d, xt,
-                                                                     prev, mix);
+                                                                     prev, mix, 0);
     return true;
   }
   if (d > 8 * 128) return false;
@@ -466,9 +478,9 @@ void launch_to_bf16(const float* x, __nv_bfloat16* y, size_t n, cudaStream_t s) 
 }
 
 template void launch_layernorm<float>(const float*, const float*, const float*, const float*, float*,
-                                      int, int, cudaStream_t);
+                                      int, int, cudaStream_t, bool);
 template void launch_layernorm<__nv_bfloat16>(const float*, const float*, const float*, const float*,
-                                              __nv_bfloat16*, int, int, cudaStream_t);
+                                              __nv_bfloat16*, int, int, cudaStream_t, bool);
 template bool launch_ln_mix_step<float>(const float*, const float*, const float*, float*, float*,
                                          const float*, float*, int, int, cudaStream_t);
 template bool launch_ln_mix_step<__nv_bfloat16>(const float*, const float*, const float*, float*,

@@ -9,9 +9,10 @@ namespace yuf {
 
 void launch_embed(const int32_t* ids, const float* E, float* x, int rows, int d, int vocab, int* err,
                   cudaStream_t s);
+// gate (nullable) multiplies the normalised row; gate_sigmoid: sigmoid(gate) does
 template <typename OUT>
 void launch_layernorm(const float* x, const float* w, const float* b, const float* gate, OUT* out,
-                      int rows, int d, cudaStream_t s);
+                      int rows, int d, cudaStream_t s, bool gate_sigmoid = false);
 template <typename OUT>
 void launch_mix(const float* xt, const float* prev, const float* mix, OUT* out, int B, int T, int d,
                 cudaStream_t s);
@@ -75,4 +76,10 @@ bool wkv7_chunk_tc_applies(int B, int T, int H, int N);
 yuf_status_t wkv7_chunk_tc(const float* r, const float* w, const float* k, const float* v, const float* a,
                            const float* b, const float* s0, float* y, float* s_out, int B, int T, int H, int N,
                            cudaStream_t st);
+// the same with the time-mix epilogue folded in: r, k, v, lw, la as the projections
+// left them, the layer's w0, a0, k_k, k_a
+yuf_status_t wkv7_chunk_tc_tm(const float* r, const float* k, const float* v, const float* lw, const float* la,
+                              const float* w0, const float* a0, const float* k_k, const float* k_a,
+                              const float* s0, float* y, float* s_out, int B, int T, int H, int N,
+                              cudaStream_t st);
 }  // namespace yuf

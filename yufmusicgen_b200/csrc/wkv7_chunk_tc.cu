@@ -99,10 +99,12 @@ struct CtcCfg {
   static constexpr int XS = ((YS ? 3 : 6) * L * GL + 31) / 32 * 32;
   static constexpr int OFF_X = NB * SLOT;
   static constexpr int OFF_SA = OFF_X + NP * XS;
-  static constexpr int OFF_BAR = OFF_SA + NS * L * SLD;
+  static constexpr int OFF_PRM = OFF_SA + NS * L * SLD;  // the head's w0, a0, k_k, k_a ([4][LD], TM)
+  static constexpr int OFF_BAR = OFF_PRM + 4 * LD;
   static constexpr int NBAR = 3 * NB;
   static constexpr size_t BYTES = (size_t)OFF_BAR * 4 + NBAR * 8;
   static constexpr uint32_t TX = 6u * L * LD * 4;
+  static constexpr uint32_t TX_TM = 5u * L * LD * 4;  // TM: no b box
   static_assert(N % 8 == 0 && N <= 64, "chunked tensor-core scan: N a multiple of 8, at most 64");
   static_assert((L * LD * 4) % 128 == 0 && SLOT % 32 == 0, "TMA boxes on 128-byte boundaries");
   static_assert(LD <= 256 && (LD * 4) % 16 == 0, "TMA box width");
@@ -113,6 +115,16 @@ struct CtcCfg {
 
 struct CtcTmaps {
   CUtensorMap m[6];  // r, w, k, v, a, b as [B*T, H*N] fp32
+};
+
+// The time-mix epilogue folded into the prep (TM): the boxes are then r, the w
+// and a low-rank outputs, k and v as the projections left them, and the prep
+// forms (yufmusicgen/model.py:113-125), per token and column,
+//   w = w0 + lw,  kk = normalize(k * k_k) over the head,  alpha = sigmoid(a0 + la),
+//   a = -kk,  b = kk * alpha,  k' = k * (1 + (alpha - 1) * k_a)
+// -- the arithmetic of timemix_post_kernel -- before it scales them.
+struct CtcTm {
+  const float *w0, *a0, *k_k, *k_a;  // [H * N] per-channel parameters of the layer
 };
 
 YUF_DEVICE void split_a(const float (&x)[4], uint32_t (&h)[4], uint32_t (&l)[4]) {
@@ -279,10 +291,10 @@ YUF_DEVICE void ctc_abort(int* flag) {
   if (atomicExch(flag, 1) == 0) atomicAdd(&g_ctc_wait_timeouts, 1u);
 }
 
-template <int N>
+template <int N, bool TM>
 __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
     wkv7_chunk_tc_kernel(const float* __restrict__ s0, float* __restrict__ y, float* __restrict__ s_out, int T,
-                         int H, const __grid_constant__ CtcTmaps tm) {
+                         int H, const __grid_constant__ CtcTmaps tm, const CtcTm prm) {
   using K = CtcCfg<N>;
   constexpr int L = K::L, LD = K::LD, NS = K::NS, NP = K::NP, NB = K::NB, NJ = K::NJ;
   constexpr int GL = K::GL, SLD = K::SLD;
@@ -305,6 +317,14 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
     }
     abort_flag = 0;
     fence_mbar_init();
+  }
+  if constexpr (TM) {  // the head's time-mix parameters (weights: no kernel of the chain writes them)
+    float* pr = sm + K::OFF_PRM;
+    for (int i = threadIdx.x; i < 4 * N; i += blockDim.x) {
+      const int which = i / N, j = i - which * N;
+      const float* src = which == 0 ? prm.w0 : (which == 1 ? prm.a0 : (which == 2 ? prm.k_k : prm.k_a));
+      pr[which * LD + j] = src[hh * N + j];
+    }
   }
   __syncthreads();
   pdl_wait();
@@ -528,8 +548,23 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
       // the instruction caches.  Every step below touches item (t, j) of the
       // slot from the same lane that reads it, so the in-place transforms are
       // race free.
+      const float* pw0 = sm + K::OFF_PRM;  // TM: w0, a0, k_k, k_a, LD apart
+      // (0) TM: 1 / |k * k_k| per token, lanes 2t and 2t+1 summing half the
+      //     columns each (F.normalize eps, model.py:116)
+      float inv_n = 0.f;
+      if constexpr (TM) {
+        const int t = lane >> 1, j0 = (lane & 1) * (N / 2);
+        float ss = 0.f;
+#pragma unroll 4
+        for (int j = j0; j < j0 + N / 2; ++j) {
+          const float kk = P[K::S_K + t * LD + j] * pw0[2 * LD + j];
+          ss = fmaf(kk, kk, ss);
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        inv_n = 1.f / fmaxf(sqrtf(ss), 1e-12f);
+      }
       // (1) log retentions ls = W_SCALE sigmoid(w), an item (t, j) per lane,
-      //     in place of w
+      //     in place of w (TM: w = w0 + lw)
       float* Gs = P + K::S_W;
       constexpr int ITEMS = L * N / 32;  // a multiple of 4
 #pragma unroll 1
@@ -539,6 +574,7 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         for (int u = 0; u < 4; ++u) {
           const int e = lane + 32 * (i0 + u), t = e / N;
           lw[u] = Gs[t * LD + (e - t * N)];
+          if constexpr (TM) lw[u] += pw0[e - t * N];
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -567,15 +603,25 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         float G[4], Gp[4], ra[4], rb[4], rk[4], rr[4], rv[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int e = lane + 32 * (i0 + u), t = e / N, o = t * LD + (e - t * N);
+          const int e = lane + 32 * (i0 + u), t = e / N, j = e - t * N, o = t * LD + j;
           const bool live = t < Tc;
           G[u] = Gs[o];
           Gp[u] = sel(t > 0, Gs[o - (t > 0 ? LD : 0)], 0.f);
           rr[u] = sel(live, P[K::S_R + o], 0.f);
           rk[u] = sel(live, P[K::S_K + o], 0.f);
           rv[u] = sel(live, P[K::S_V + o], 0.f);
-          ra[u] = sel(live, P[K::S_A + o], 0.f);
-          rb[u] = sel(live, P[K::S_B + o], 0.f);
+          if constexpr (TM) {
+            // a = -kk, b = kk alpha, k' = k (1 + (alpha - 1) k_a) from the raw k and la
+            const float inv = __shfl_sync(0xffffffffu, inv_n, 2 * t);
+            const float kk = rk[u] * pw0[2 * LD + j] * inv;
+            const float alpha = sigmoidf_fast(pw0[LD + j] + sel(live, P[K::S_A + o], 0.f));
+            ra[u] = -kk;
+            rb[u] = kk * alpha;
+            rk[u] = rk[u] * (1.f + (alpha - 1.f) * pw0[3 * LD + j]);
+          } else {
+            ra[u] = sel(live, P[K::S_A + o], 0.f);
+            rb[u] = sel(live, P[K::S_B + o], 0.f);
+          }
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -650,9 +696,10 @@ __global__ void __launch_bounds__(CtcCfg<N>::NT, 1)
         break;
       }
       float* dst = sm + ps * K::SLOT;
-      mbar_expect_tx(&tma_full[ps], K::TX);
+      mbar_expect_tx(&tma_full[ps], TM ? K::TX_TM : K::TX);
 #pragma unroll
-      for (int arr = 0; arr < 6; ++arr) tma_load_2d(dst + arr * L * LD, &tm.m[arr], &tma_full[ps], tx, ty + c * L);
+      for (int arr = 0; arr < (TM ? 5 : 6); ++arr)
+        tma_load_2d(dst + arr * L * LD, &tm.m[arr], &tma_full[ps], tx, ty + c * L);
     }
     // the copies still in flight land before the CTA may leave
     for (int c2 = max(0, c - NB); c2 < c; ++c2) mbar_wait(&tma_full[c2 % NB], (uint32_t)(c2 / NB) & 1u);
@@ -685,9 +732,9 @@ static yuf_status_t make_ctc_tmaps(const float* const (&src)[6], long long rows,
   return YUF_OK;
 }
 
-template <int N>
+template <int N, bool TM>
 static yuf_status_t launch_ctc(const float* const (&src)[6], const float* s0, float* y, float* s_out, int B, int T,
-                               int H, cudaStream_t st) {
+                               int H, const CtcTm& prm, cudaStream_t st) {
   using K = CtcCfg<N>;
   static std::once_flag once[128];
   static cudaError_t attr[128];
@@ -696,7 +743,7 @@ static yuf_status_t launch_ctc(const float* const (&src)[6], const float* s0, fl
   dev &= 127;
   std::call_once(once[dev], [&] {
     attr[dev] =
-        cudaFuncSetAttribute(wkv7_chunk_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)K::BYTES);
+        cudaFuncSetAttribute(wkv7_chunk_tc_kernel<N, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)K::BYTES);
   });
   if (attr[dev] != cudaSuccess) {
     set_error("wkv7 chunked-tc: cannot set %zu bytes of shared memory: %s", K::BYTES,
@@ -706,8 +753,8 @@ static yuf_status_t launch_ctc(const float* const (&src)[6], const float* s0, fl
   CtcTmaps tm;
   const yuf_status_t rc = make_ctc_tmaps(src, (long long)B * T, H, N, K::LD, &tm);
   if (rc != YUF_OK) return rc;
-  launch_k(wkv7_chunk_tc_kernel<N>, dim3(B * H), dim3(K::NT), K::BYTES, st, s0, y, s_out, T, H, tm);
-  return check_launch("wkv7_chunk_tc_kernel");
+  launch_k(wkv7_chunk_tc_kernel<N, TM>, dim3(B * H), dim3(K::NT), K::BYTES, st, s0, y, s_out, T, H, tm, prm);
+  return check_launch(TM ? "wkv7_chunk_tc_kernel (time-mix)" : "wkv7_chunk_tc_kernel");
 }
 
 bool wkv7_chunk_tc_supports(int N) { return N == 16 || N == 32 || N == 40 || N == 48 || N == 64; }
@@ -752,14 +799,41 @@ yuf_status_t wkv7_chunk_tc(const float* r, const float* w, const float* k, const
     return YUF_OK;
   }
   const float* const src[6] = {r, w, k, v, a, b};
+  const CtcTm none{nullptr, nullptr, nullptr, nullptr};
   switch (N) {
-    case 16: return launch_ctc<16>(src, s0, y, s_out, B, T, H, st);
-    case 32: return launch_ctc<32>(src, s0, y, s_out, B, T, H, st);
-    case 40: return launch_ctc<40>(src, s0, y, s_out, B, T, H, st);
-    case 48: return launch_ctc<48>(src, s0, y, s_out, B, T, H, st);
-    case 64: return launch_ctc<64>(src, s0, y, s_out, B, T, H, st);
+    case 16: return launch_ctc<16, false>(src, s0, y, s_out, B, T, H, none, st);
+    case 32: return launch_ctc<32, false>(src, s0, y, s_out, B, T, H, none, st);
+    case 40: return launch_ctc<40, false>(src, s0, y, s_out, B, T, H, none, st);
+    case 48: return launch_ctc<48, false>(src, s0, y, s_out, B, T, H, none, st);
+    case 64: return launch_ctc<64, false>(src, s0, y, s_out, B, T, H, none, st);
     default:
       set_error("wkv7 chunked-tc: head size N=%d has no kernel (N in {16, 32, 40, 48, 64})", N);
+      return YUF_ERR_UNSUPPORTED;
+  }
+}
+
+// The same scan from the projections' raw outputs with the time-mix epilogue
+// folded into its prep (CtcTm): r, k, v and the w / a low-rank outputs lw, la
+// as [B, T, H, N]; w0, a0, k_k, k_a the layer's [H * N] parameters.  T >= 1.
+yuf_status_t wkv7_chunk_tc_tm(const float* r, const float* k, const float* v, const float* lw, const float* la,
+                              const float* w0, const float* a0, const float* k_k, const float* k_a,
+                              const float* s0, float* y, float* s_out, int B, int T, int H, int N,
+                              cudaStream_t st) {
+  if (T <= 0) {
+    set_error("wkv7 chunked-tc (time-mix): T = %d", T);
+    return YUF_ERR_INVALID_ARGUMENT;
+  }
+  // the sixth tensor map is never loaded from in this mode (any valid tensor)
+  const float* const src[6] = {r, lw, k, v, la, la};
+  const CtcTm prm{w0, a0, k_k, k_a};
+  switch (N) {
+    case 16: return launch_ctc<16, true>(src, s0, y, s_out, B, T, H, prm, st);
+    case 32: return launch_ctc<32, true>(src, s0, y, s_out, B, T, H, prm, st);
+    case 40: return launch_ctc<40, true>(src, s0, y, s_out, B, T, H, prm, st);
+    case 48: return launch_ctc<48, true>(src, s0, y, s_out, B, T, H, prm, st);
+    case 64: return launch_ctc<64, true>(src, s0, y, s_out, B, T, H, prm, st);
+    default:
+      set_error("wkv7 chunked-tc (time-mix): head size N=%d has no kernel", N);
       return YUF_ERR_UNSUPPORTED;
   }
 }
