@@ -330,10 +330,10 @@ def test_wkv7_time_parallel_full_config2_and_inplace_state(algo):
 
 
 @pytest.mark.parametrize("B,T,R", [(1, 1024, 128), (2, 2048, 128), (3, 512, 100), (4, 256, 32), (3, 512, 64), (2, 384, 12),
-                                   (2, 512, 256), (8, 1024, 256), (1, 2048, 200)])
+                                   (2, 512, 256), (8, 1024, 256), (1, 2048, 200), (8, 8192, 256)])
 def test_rosa_time_parallel_matches_oracle(B, T, R):
     ins = rosa_op_inputs(B, T, R, seed=B * 1000 + T + R, with_state=True)
-    if R == 128:
+    if R >= 128:
         ins["decay"][:8] = 0.9999  # slow channels stress the carried state
     args = [cu(ins[k]) for k in ("cand", "write", "read_gate", "decay", "direction", "m0")]
     read, m = rosa_cuda.rosa_scan(*args, gated=True)

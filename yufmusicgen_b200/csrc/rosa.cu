@@ -621,6 +621,74 @@ __global__ void __launch_bounds__(256)
   if (on && m_out) m_out[(size_t)b * R + i] = m;
 }
 
+// The low-rank carry for R = 256, K = 64 with both factors in registers: the
+// thread (s, q) = (tid / 4, tid % 4) holds M[s, j] for the channels j = q (mod 4)
+// (64 values) and forms p_s with its three partners by two shuffles; the thread
+// i holds row i of W (64 values) and applies D^K m - 2 W p + z for channel i.
+// Each step reads m and p from shared memory (p as broadcast float4s) and
+// needs two barriers.  Every thread copies its own channel's chunk end state z
+// into an 8-deep shared ring by cp.async, seven chunks ahead, and waits only
+// for its own copies.
+__global__ void __launch_bounds__(256)
+    rosa_carry_lowrank_reg_kernel(const float* __restrict__ Wt, const float* __restrict__ Mt,
+                                  const float* __restrict__ DK, const float* __restrict__ z,
+                                  const float* m0, float* __restrict__ m_start, float* m_out, int C) {
+  constexpr int R = 256, K = 64, ZR = 8;
+  __shared__ __align__(16) float mv[R];
+  __shared__ __align__(16) float pv[K];
+  __shared__ float zs[ZR][R];
+  const int b = blockIdx.x, i = threadIdx.x;
+  const int s = i >> 2, q = i & 3;
+  float Mr[R / 4], Wc[K];
+#pragma unroll
+  for (int jj = 0; jj < R / 4; ++jj) Mr[jj] = Mt[(size_t)(4 * jj + q) * K + s];
+#pragma unroll
+  for (int ss = 0; ss < K; ++ss) Wc[ss] = Wt[(size_t)ss * R + i];
+  const float dk = DK[i];
+  float m = m0 ? m0[(size_t)b * R + i] : 0.f;
+  const float* zb = z + (size_t)b * C * R + i;
+  auto fetch = [&](int c) {  // this thread's z of chunk c into its ring slot; always commits
+    if (c < C) {
+      const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(&zs[c % ZR][i]));
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(zb + (size_t)c * R));
+    }
+    cp_async_commit();
+  };
+  for (int c = 0; c < ZR - 1; ++c) fetch(c);
+  for (int c = 0; c < C; ++c) {
+    fetch(c + ZR - 1);
+    m_start[((size_t)b * C + c) * R + i] = m;
+    mv[i] = m;
+    __syncthreads();
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < R / 4; jj += 4) {
+      a0 = fmaf(Mr[jj + 0], mv[4 * (jj + 0) + q], a0);
+      a1 = fmaf(Mr[jj + 1], mv[4 * (jj + 1) + q], a1);
+      a2 = fmaf(Mr[jj + 2], mv[4 * (jj + 2) + q], a2);
+      a3 = fmaf(Mr[jj + 3], mv[4 * (jj + 3) + q], a3);
+    }
+    float p = (a0 + a1) + (a2 + a3);
+    p += __shfl_xor_sync(0xffffffffu, p, 1);
+    p += __shfl_xor_sync(0xffffffffu, p, 2);
+    if (q == 0) pv[s] = p;
+    __syncthreads();
+    float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f;
+#pragma unroll
+    for (int ss = 0; ss < K; ss += 4) {
+      const float4 pp = *reinterpret_cast<const float4*>(pv + ss);
+      w0 = fmaf(Wc[ss + 0], pp.x, w0);
+      w1 = fmaf(Wc[ss + 1], pp.y, w1);
+      w2 = fmaf(Wc[ss + 2], pp.z, w2);
+      w3 = fmaf(Wc[ss + 3], pp.w, w3);
+    }
+    cp_async_wait<ZR - 1>();  // this thread's copy of chunk c has landed
+    m = fmaf(dk, m, zs[c % ZR][i]) - 2.f * ((w0 + w1) + (w2 + w3));
+  }
+  cp_async_wait<0>();
+  if (m_out) m_out[(size_t)b * R + i] = m;
+}
+
 template <bool GATED, int MODE>
 static void launch_mode(const float* cand, const float* write, const float* gate,
                         const float* bias_c, const float* bias_w, const float* bias_g, int ld,
@@ -689,14 +757,18 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
     float* Mt = Wt + (size_t)K * R;    // [R][K]
     float* DK = Mt + (size_t)R * K;    // [R]
     rosa_lowrank_kernel<<<1, threads, 0, s>>>(decay, dir, raw, Wt, Mt, DK, K, R);
-    const size_t sm = ((size_t)K * R + (size_t)R * K + R + K) * sizeof(float);
-    cudaError_t e = cudaFuncSetAttribute(rosa_carry_lowrank_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    if (e != cudaSuccess) {
-      set_error("rosa: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
-      return YUF_ERR_CUDA;
+    if (R == 256 && K == 64) {
+      rosa_carry_lowrank_reg_kernel<<<B, 256, 0, s>>>(Wt, Mt, DK, z, m0, m_start, m_out, C);
+    } else {
+      const size_t sm = ((size_t)K * R + (size_t)R * K + R + K) * sizeof(float);
+      cudaError_t e = cudaFuncSetAttribute(rosa_carry_lowrank_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      if (e != cudaSuccess) {
+        set_error("rosa: cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+        return YUF_ERR_CUDA;
+      }
+      rosa_carry_lowrank_kernel<<<B, threads, sm, s>>>(Wt, Mt, DK, z, m0, m_start, m_out, C, K, R);
     }
-    rosa_carry_lowrank_kernel<<<B, threads, sm, s>>>(Wt, Mt, DK, z, m0, m_start, m_out, C, K, R);
   }
   // 4. rescan every chunk from its true start state
   if (gated)
