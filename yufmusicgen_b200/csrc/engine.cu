@@ -356,11 +356,20 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
                       : launch_ln_mix_step<float>(w.x, Lw.ln_t_w, Lw.ln_t_b, w.xt, prev, Lw.mix,
                                                   w.mixed, B, d, s));
     if (!fused_mix) {
-      launch_layernorm<float>(w.x, Lw.ln_t_w, Lw.ln_t_b, nullptr, w.xt, (int)rows, d, s);
-      if (bf)
-        launch_mix<__nv_bfloat16>(w.xt, prev, Lw.mix, w.bf, B, T, d, s);
-      else
-        launch_mix<float>(w.xt, prev, Lw.mix, w.mixed, B, T, d, s);
+      // one pass for the norm, the shift and the lerps; debug runs keep the
+      // separate norm so that every row's xt can be dumped
+      const bool fused_rows =
+          !m->debug && (bf ? launch_ln_mix_rows<__nv_bfloat16>(w.x, Lw.ln_t_w, Lw.ln_t_b, w.xt, prev, Lw.mix,
+                                                               w.bf, B, T, d, s)
+                           : launch_ln_mix_rows<float>(w.x, Lw.ln_t_w, Lw.ln_t_b, w.xt, prev, Lw.mix, w.mixed,
+                                                       B, T, d, s));
+      if (!fused_rows) {
+        launch_layernorm<float>(w.x, Lw.ln_t_w, Lw.ln_t_b, nullptr, w.xt, (int)rows, d, s);
+        if (bf)
+          launch_mix<__nv_bfloat16>(w.xt, prev, Lw.mix, w.bf, B, T, d, s);
+        else
+          launch_mix<float>(w.xt, prev, Lw.mix, w.mixed, B, T, d, s);
+      }
       Y_CUDA(cudaMemcpy2DAsync(prev, d * sizeof(float), w.xt + (size_t)(T - 1) * d,
                                (size_t)T * d * sizeof(float), d * sizeof(float), B,
                                cudaMemcpyDeviceToDevice, s));

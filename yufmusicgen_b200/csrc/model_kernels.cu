@@ -269,6 +269,98 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// The TimeMix layer norm of one row into registers (VPL float4 per lane, the
+// arithmetic of layernorm_reg_kernel): two-pass mean and variance, then the affine.
+template <int VPL>
+YUF_DEVICE void ln_row_regs(const float* __restrict__ xrow, const float4* __restrict__ w4,
+                            const float4* __restrict__ b4, int d, int lane, float4 (&o)[VPL]) {
+  const int d4 = d >> 2;
+  const float4* xr = reinterpret_cast<const float4*>(xrow);
+  float4 v[VPL];
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    const int i = lane + 32 * u;
+    v[u] = i < d4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[u].x + v[u].y) + (v[u].z + v[u].w);
+  }
+  const float mean = warp_sum(s) / d;
+  float q = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    if (lane + 32 * u < d4) {
+      const float cx = v[u].x - mean, cy = v[u].y - mean, cz = v[u].z - mean, cw = v[u].w - mean;
+      q = fmaf(cx, cx, fmaf(cy, cy, fmaf(cz, cz, fmaf(cw, cw, q))));
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / d + 1e-5f);
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    const int i = lane + 32 * u;
+    if (i < d4) {
+      const float4 ww = w4[i], bb = b4[i];
+      o[u] = make_float4((v[u].x - mean) * rstd * ww.x + bb.x, (v[u].y - mean) * rstd * ww.y + bb.y,
+                         (v[u].z - mean) * rstd * ww.z + bb.z, (v[u].w - mean) * rstd * ww.w + bb.w);
+    } else {
+      o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+}
+
+// Prefill: the TimeMix layer norm, the token shift and the six lerps in one
+// pass (model.py:98-105).  One warp per row (b, t): the row's norm and, for
+// t > 0, the previous row's norm recomputed (its x is read again, mostly from
+// L2) -- for t = 0 the shift source is prev[b], the previous call's last norm.
+// xt receives only each sequence's last row (the caller copies it into prev
+// after this kernel, so prev is only read here); out [6][rows][d] in the order
+// r, k, v, w, a, g.
+template <typename OUT, int VPL>
+__global__ void __launch_bounds__(128)
+    ln_mix_rows_kernel(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ b,
+                       float* __restrict__ xt, const float* __restrict__ prev, const float* __restrict__ mix,
+                       OUT* __restrict__ out, int B, int T, int d) {
+  pdl_wait();
+  pdl_trigger();
+  const int rows = B * T;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int bb = row / T, t = row - bb * T;
+  const int d4 = d >> 2;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  float4 o[VPL], sh[VPL];
+  ln_row_regs<VPL>(x + (size_t)row * d, w4, b4, d, lane, o);
+  if (t > 0) {
+    ln_row_regs<VPL>(x + (size_t)(row - 1) * d, w4, b4, d, lane, sh);
+  } else {
+    const float4* p4 = reinterpret_cast<const float4*>(prev + (size_t)bb * d);
+#pragma unroll
+    for (int u = 0; u < VPL; ++u) {
+      const int i = lane + 32 * u;
+      sh[u] = i < d4 ? p4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  const size_t total = (size_t)rows * d;
+  const float4* m4 = reinterpret_cast<const float4*>(mix);
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    const int i = lane + 32 * u;
+    if (i < d4) {
+      const size_t oi = (size_t)row * d + 4 * i;
+      if (t == T - 1) *reinterpret_cast<float4*>(xt + oi) = o[u];
+      const float4 delta = make_float4(o[u].x - sh[u].x, o[u].y - sh[u].y, o[u].z - sh[u].z, o[u].w - sh[u].w);
+      // mix rows in the reference order r, w, k, v, a, g; outputs in r, k, v, w, a, g
+      store4(out, 0 * total + oi, f4_lerp(o[u], delta, m4[0 * d4 + i]));
+      store4(out, 3 * total + oi, f4_lerp(o[u], delta, m4[1 * d4 + i]));
+      store4(out, 1 * total + oi, f4_lerp(o[u], delta, m4[2 * d4 + i]));
+      store4(out, 2 * total + oi, f4_lerp(o[u], delta, m4[3 * d4 + i]));
+      store4(out, 4 * total + oi, f4_lerp(o[u], delta, m4[4 * d4 + i]));
+      store4(out, 5 * total + oi, f4_lerp(o[u], delta, m4[5 * d4 + i]));
+    }
+  }
+}
+
 template <typename OUT>
 __global__ void mix_kernel(const float* __restrict__ xt, const float* __restrict__ prev,
                            const float* __restrict__ mix, OUT* __restrict__ out, int B, int T, int d) {
@@ -452,6 +544,22 @@ bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* x
   }
 }
 template <typename OUT>
+bool launch_ln_mix_rows(const float* x, const float* w, const float* b, float* xt, const float* prev,
+                        const float* mix, OUT* out, int B, int T, int d, cudaStream_t s) {
+  if (d % 4 != 0 || d > 8 * 128 || (long long)B * T > 0x7fffffffLL) return false;
+  const int wpb = 4;
+  const int blocks = (int)(((long long)B * T + wpb - 1) / wpb);
+  switch ((d / 4 + 31) / 32) {
+#define CASE(V)                                                                                 \
+  case V:                                                                                       \
+    launch_k(ln_mix_rows_kernel<OUT, V>, dim3(blocks), dim3(32 * wpb), 0, s, x, w, b, xt, prev, mix, out, B, T, d); \
+    return true;
+    CASE(1) CASE(2) CASE(3) CASE(4) CASE(5) CASE(6) CASE(7) CASE(8)
+#undef CASE
+    default: return false;
+  }
+}
+template <typename OUT>
 void launch_mix(const float* xt, const float* prev, const float* mix, OUT* out, int B, int T, int d,
                 cudaStream_t s) {
   launch_k(mix_kernel<OUT>, dim3(grid_for((size_t)B * T * d, 256)), dim3(256), 0, s, xt, prev, mix, out, B, T, d);
@@ -486,6 +594,10 @@ template bool launch_ln_mix_step<float>(const float*, const float*, const float*
 template bool launch_ln_mix_step<__nv_bfloat16>(const float*, const float*, const float*, float*,
                                                 float*, const float*, __nv_bfloat16*, int, int,
                                                 cudaStream_t);
+template bool launch_ln_mix_rows<float>(const float*, const float*, const float*, float*, const float*,
+                                         const float*, float*, int, int, int, cudaStream_t);
+template bool launch_ln_mix_rows<__nv_bfloat16>(const float*, const float*, const float*, float*, const float*,
+                                                 const float*, __nv_bfloat16*, int, int, int, cudaStream_t);
 template void launch_mix<float>(const float*, const float*, const float*, float*, int, int, int,
                                 cudaStream_t);
 template void launch_mix<__nv_bfloat16>(const float*, const float*, const float*, __nv_bfloat16*,

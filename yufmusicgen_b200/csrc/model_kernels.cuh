@@ -21,6 +21,12 @@ void launch_mix(const float* xt, const float* prev, const float* mix, OUT* out, 
 template <typename OUT>
 bool launch_ln_mix_step(const float* x, const float* w, const float* b, float* xt, float* prev,
                         const float* mix, OUT* out, int B, int d, cudaStream_t s);
+// B sequences x T tokens (prefill): layer norm + token shift + six lerps in one
+// launch, xt written for each sequence's last row only; false (nothing
+// launched) when d is not a multiple of 4 or above 1024
+template <typename OUT>
+bool launch_ln_mix_rows(const float* x, const float* w, const float* b, float* xt, const float* prev,
+                        const float* mix, OUT* out, int B, int T, int d, cudaStream_t s);
 // tanh of the first n_tanh elements, plain copy (conversion) of the rest up to n
 template <typename OUT>
 void launch_tanh(const float* x, OUT* out, size_t n_tanh, size_t n, cudaStream_t s);
