@@ -106,8 +106,14 @@ __global__ void __launch_bounds__(1024)
 // output).  MODE 2: transition -- batch row bb starts from the unit vector e_bb
 // with zero input for T steps, so m_out row bb = A^T e_bb, i.e. column bb of
 // A^T (A the one-step transition, A^T its T-th power).
-template <bool GATED, bool COMPAT, int MAXT, int MODE = 0>
-__global__ void __launch_bounds__(MAXT)
+// LEAN: the register-light form for launches of many more blocks than the SMs
+// hold at once (the chunk passes of a long time-parallel scan): p_t formed once
+// per block in shared memory instead of by every thread, u_t formed inside the
+// EMA, the next gate requested after the read stage, three 256-thread blocks
+// per SM.  The default form keeps all of that in registers, which is faster
+// where each block's chain of chunks is the critical path.
+template <bool GATED, bool COMPAT, int MAXT, int MODE = 0, bool LEAN = false>
+__global__ void __launch_bounds__(MAXT, LEAN ? 3 : 1)
     rosa_scan_kernel(const float* __restrict__ cand, const float* __restrict__ write,
                      const float* __restrict__ gate, const float* __restrict__ decay,
                      const float* __restrict__ dir, const float* m0, float* __restrict__ read,
@@ -122,6 +128,7 @@ __global__ void __launch_bounds__(MAXT)
   __shared__ float s_sum[L + 1];
   __shared__ float q[L + 1];
   __shared__ float c_sum[L + 1];
+  __shared__ float p_sm[L + 1];
 
   const int bb = blockIdx.x;
   const int j = threadIdx.x;
@@ -133,8 +140,11 @@ __global__ void __launch_bounds__(MAXT)
   if (coef != nullptr) {
     d = act ? coef[ROSA_COEF_D + j] : 0.f;
     dec = act ? coef[ROSA_COEF_D + R + j] : 0.f;
+    if (j <= L) q[j] = coef[j];  // read after the first block reduction's barriers
+    if constexpr (!LEAN) {
 #pragma unroll
-    for (int n = 0; n <= L; ++n) qr[n] = coef[n];
+      for (int n = 0; n <= L; ++n) qr[n] = coef[n];
+    }
   } else {
     rosa_setup(j, R, nwarps, decay, dir, raw_params, scratch, c_sum, q, d, dec, qr);
   }
@@ -149,27 +159,34 @@ __global__ void __launch_bounds__(MAXT)
   if (COMPAT && act) mem_saved[(size_t)bb * (T + 1) * R + j] = m;
 
   float cc[L], ww[L], gg[L];
-  auto load = [&](int t0, float (&c_)[L], float (&w_)[L], float (&g_)[L]) {
+  auto load_cw = [&](int t0) {
 #pragma unroll
     for (int t = 0; t < L; ++t) {
       const bool ok = act && (t0 + t < T) && MODE != 2;
       const size_t o = base_in + (size_t)(t0 + t) * ld;
-      c_[t] = ok ? cand[o] + bc : 0.f;
-      w_[t] = ok ? write[o] + bw : 0.f;
-      g_[t] = (ok && (GATED || COMPAT)) ? gate[o] + bg : 0.f;
+      cc[t] = ok ? cand[o] + bc : 0.f;
+      ww[t] = ok ? write[o] + bw : 0.f;
     }
   };
-  if (T > 0) load(0, cc, ww, gg);
+  auto load_g = [&](int t0) {
+#pragma unroll
+    for (int t = 0; t < L; ++t) {
+      const bool ok = act && (t0 + t < T) && MODE != 2;
+      gg[t] = (ok && (GATED || COMPAT)) ? gate[base_in + (size_t)(t0 + t) * ld] + bg : 0.f;
+    }
+  };
+  if (T > 0) {
+    load_cw(0);
+    load_g(0);
+  }
 
   for (int t0 = 0; t0 < T; t0 += L) {
     const int Lc = min(L, T - t0);
-    float u[L];
-#pragma unroll
-    for (int t = 0; t < L; ++t) u[t] = sigmoidf_fast(ww[t]) * tanhf(cc[t]);
-    float gcur[L];
-#pragma unroll
-    for (int t = 0; t < L; ++t) gcur[t] = gg[t];
-    float ccur[L], wcur[L];
+    // LEAN: the gate is only read in step 4, so the next chunk's gate is
+    // requested after it; otherwise (and for COMPAT's saved tensors) the
+    // chunk's raw inputs are copied before the next chunk's are requested
+    float gcur[(COMPAT || !LEAN) ? L : 1], ccur[COMPAT ? L : 1], wcur[COMPAT ? L : 1];
+    float u[LEAN ? 1 : L];
     if constexpr (COMPAT) {
 #pragma unroll
       for (int t = 0; t < L; ++t) {
@@ -177,38 +194,89 @@ __global__ void __launch_bounds__(MAXT)
         wcur[t] = ww[t];
       }
     }
-    if (t0 + L < T) load(t0 + L, cc, ww, gg);  // prefetch the next chunk
+    if constexpr (COMPAT || !LEAN) {
+#pragma unroll
+      for (int t = 0; t < L; ++t) gcur[t] = gg[t];
+    }
+    if constexpr (!LEAN) {
+#pragma unroll
+      for (int t = 0; t < L; ++t) u[t] = sigmoidf_fast(ww[t]) * tanhf(cc[t]);
+      if (t0 + L < T) {  // prefetch the next chunk
+        load_cw(t0 + L);
+        load_g(t0 + L);
+      }
+    }
 
     // 1. per-channel EMA from the true chunk-start memory.
-    float e[L + 1], x[L + 1];
+    float e[L + 1];
     e[0] = m;
-    x[0] = d * m;
 #pragma unroll
     for (int t = 0; t < L; ++t) {
-      e[t + 1] = (t < Lc) ? fmaf(dec, e[t], u[t]) : e[t];
-      x[t + 1] = d * e[t + 1];
+      float ut;
+      if constexpr (LEAN) ut = sigmoidf_fast(ww[t]) * tanhf(cc[t]);
+      else ut = u[t];
+      e[t + 1] = (t < Lc) ? fmaf(dec, e[t], ut) : e[t];
     }
-    // 2. all L+1 projections s_t = d . e_t in one block reduction.
-    block_sum_array<L + 1>(x, scratch, s_sum, nwarps);
-    // 3. p_{t+1} = sum_{tau <= t} q_{t-tau} s_tau  (p index shifted by one).
-    float p[L + 1], sv[L + 1];
-#pragma unroll
-    for (int t = 0; t <= L; ++t) sv[t] = s_sum[t];
-#pragma unroll
-    for (int t = 0; t <= L; ++t) {
-      float acc = 0.f;
-#pragma unroll
-      for (int tau = 0; tau <= t; ++tau) acc = fmaf(qr[t - tau], sv[tau], acc);
-      p[t] = acc;
+    if constexpr (LEAN) {
+      if (t0 + L < T) {  // prefetch the next chunk
+        load_cw(t0 + L);
+        if constexpr (COMPAT) load_g(t0 + L);
+      }
     }
+    // 2. all L+1 projections s_t = d . e_t in one block reduction (the steps of
+    //    block_sum_array, with d e_t formed in place).
+    {
+      const int lane = j & 31, warp = j >> 5;
+#pragma unroll
+      for (int i = 0; i <= L; ++i) {
+        float sv = d * e[i];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sv += __shfl_xor_sync(0xffffffffu, sv, o);
+        if (lane == 0) scratch[warp * (L + 1) + i] = sv;
+      }
+      __syncthreads();
+      if (j <= L) {
+        float sv = 0.f;
+        for (int wi = 0; wi < nwarps; ++wi) sv += scratch[wi * (L + 1) + j];
+        s_sum[j] = sv;
+      }
+      __syncthreads();
+    }
+    // 3. p_{t+1} = sum_{tau <= t} q_{t-tau} s_tau  (p index shifted by one): by
+    //    every thread into registers, or (LEAN) once per block, thread t forming
+    //    p_t into shared memory.
+    float p[LEAN ? 1 : L + 1];
+    if constexpr (LEAN) {
+      if (j <= L) {
+        float acc = 0.f;
+        for (int tau = 0; tau <= j; ++tau) acc = fmaf(q[j - tau], s_sum[tau], acc);
+        p_sm[j] = acc;
+      }
+      __syncthreads();
+    } else {
+      float sv[L + 1];
+#pragma unroll
+      for (int t = 0; t <= L; ++t) sv[t] = s_sum[t];
+#pragma unroll
+      for (int t = 0; t <= L; ++t) {
+        float acc = 0.f;
+#pragma unroll
+        for (int tau = 0; tau <= t; ++tau) acc = fmaf(qr[t - tau], sv[tau], acc);
+        p[t] = acc;
+      }
+    }
+    auto P = [&](int t) -> float {
+      if constexpr (LEAN) return p_sm[t];
+      else return p[t];
+    };
     // 4. correction, memory and read.
     float gc = 0.f;
 #pragma unroll
     for (int t = 0; t < L; ++t) {
       if (t < Lc) {
-        gc = dec * fmaf(p[t], d, gc);
+        gc = dec * fmaf(P(t), d, gc);
         const float mt = fmaf(-2.f, gc, e[t + 1]);
-        const float rd = fmaf(-2.f * p[t + 1], d, mt);
+        const float rd = fmaf(-2.f * P(t + 1), d, mt);
         if (act && MODE == 0) {
           const size_t o = base + (size_t)(t0 + t) * R;
           if constexpr (COMPAT) {
@@ -220,7 +288,10 @@ __global__ void __launch_bounds__(MAXT)
             decay_saved[o] = dec;
             mem_saved[(size_t)bb * (T + 1) * R + (size_t)(t0 + t + 1) * R + j] = mt;
           } else if constexpr (GATED) {
-            read[o] = rd * sigmoidf_fast(gcur[t]);
+            float gv;
+            if constexpr (LEAN) gv = gg[t];
+            else gv = gcur[t];
+            read[o] = rd * sigmoidf_fast(gv);
           } else {
             read[o] = rd;
           }
@@ -228,7 +299,9 @@ __global__ void __launch_bounds__(MAXT)
         if (t == Lc - 1) m = mt;
       }
     }
-    __syncthreads();  // s_sum / scratch are rewritten by the next chunk
+    if constexpr (LEAN && !COMPAT)
+      if (t0 + L < T) load_g(t0 + L);
+    __syncthreads();  // s_sum / scratch / p_sm are rewritten by the next chunk
   }
   if (act && m_out != nullptr) m_out[(size_t)bb * R + j] = m;
 }
@@ -689,15 +762,31 @@ __global__ void __launch_bounds__(256)
   if (m_out) m_out[(size_t)b * R + i] = m;
 }
 
+static int sm_count_rosa() {
+  static int n = [] {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      cudaGetLastError();
+    return v > 0 ? v : 148;
+  }();
+  return n;
+}
+
 template <bool GATED, int MODE>
 static void launch_mode(const float* cand, const float* write, const float* gate,
                         const float* bias_c, const float* bias_w, const float* bias_g, int ld,
                         const float* decay, const float* dir, int raw, const float* m0, float* read,
                         float* m_out, int B, int T, int R, const float* coef, cudaStream_t s) {
   const int threads = ((R + 31) / 32) * 32;
-  rosa_scan_kernel<GATED, false, 256, MODE><<<B, threads, 0, s>>>(
-      cand, write, gate, decay, dir, m0, read, m_out, nullptr, nullptr, nullptr, nullptr, nullptr,
-      nullptr, T, R, ld, bias_c, bias_w, bias_g, raw, coef);
+  // more blocks than two per SM: the register-light form, three blocks per SM
+  if (B > 2 * sm_count_rosa())
+    rosa_scan_kernel<GATED, false, 256, MODE, true><<<B, threads, 0, s>>>(
+        cand, write, gate, decay, dir, m0, read, m_out, nullptr, nullptr, nullptr, nullptr, nullptr,
+        nullptr, T, R, ld, bias_c, bias_w, bias_g, raw, coef);
+  else
+    rosa_scan_kernel<GATED, false, 256, MODE><<<B, threads, 0, s>>>(
+        cand, write, gate, decay, dir, m0, read, m_out, nullptr, nullptr, nullptr, nullptr, nullptr,
+        nullptr, T, R, ld, bias_c, bias_w, bias_g, raw, coef);
 }
 
 size_t rosa_parallel_scratch_floats(int B, int T, int R) {
