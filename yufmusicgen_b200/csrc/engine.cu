@@ -70,6 +70,7 @@ struct LayerW {
   float *ln_t_w, *ln_t_b, *mix, *w0, *a0, *k_k, *k_a;
   Wt W_rkv, W_lr1, W_lr2, W_o;
   float *ln_o_w, *ln_o_b, *ln_r_w, *ln_r_b, *householder, *decay, *b_rosa;
+  float* rosa_factors = nullptr;  // the time-parallel ROSA scan's layer constants, built at load
   Wt W_rosa_in, W_rosa_out;
   float *ln_f_w, *ln_f_b;
   Wt W_ffn_in, W_ffn_out;
@@ -454,7 +455,7 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
     Y_TRY(proj(m, xr, d, 0, Lw.W_rosa_in, 0, w.rosa, 3 * R, 0, (int)rows, 3 * R, d, 1, GEMM_EPI_F32, false, s));
     Y_TRY(rosa_engine_dispatch(w.rosa, w.rosa + R, w.rosa + 2 * R, Lw.b_rosa, Lw.b_rosa + R,
                                Lw.b_rosa + 2 * R, 3 * R, Lw.decay, Lw.householder, mem, w.read, mem, B,
-                               T, R, w.scan, bf ? w.bf : nullptr, s));
+                               T, R, w.scan, bf ? w.bf : nullptr, s, Lw.rosa_factors));
     if (m->debug) dump(m, "read", li, w.read, rows * R, s);
     Y_TRY(proj(m, bf ? static_cast<const void*>(w.bf) : w.read, R, 0, Lw.W_rosa_out, 0, w.x, d, 0, (int)rows,
                d, R, 1, GEMM_EPI_F32, true, s));
@@ -618,6 +619,12 @@ static yuf_status_t load_weights(yuf_model* m, const std::unordered_map<std::str
     Y_TRY(upload(m, t, p + "norm_rosa.bias", d, &Lw.ln_r_b));
     Y_TRY(upload(m, t, ro + "householder", R, &Lw.householder));
     Y_TRY(upload(m, t, ro + "decay", R, &Lw.decay));
+    if (R <= 256) {  // the time-parallel scan's constants depend on these two parameters only
+      Lw.rosa_factors = static_cast<float*>(m->alloc(rosa_factor_floats(R) * sizeof(float)));
+      if (!Lw.rosa_factors) { set_error("model: out of device memory"); return YUF_ERR_OUT_OF_MEMORY; }
+      Y_TRY(rosa_prepare_factors(Lw.decay, Lw.householder, 1, R, Lw.rosa_factors, nullptr));
+      Y_CUDA(cudaStreamSynchronize(nullptr));
+    }
     Y_TRY(pack_weight(m, t, {ro + "input.weight", ro + "write_gate.weight", ro + "read_gate.weight"},
                       {R, R, R}, d, false, &Lw.W_rosa_in));
     {

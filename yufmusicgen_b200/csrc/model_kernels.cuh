@@ -57,9 +57,15 @@ yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const f
                                   const float* bias_c, const float* bias_w, const float* bias_g,
                                   int ld, const float* decay_raw, const float* dir_raw,
                                   const float* m0, float* read, float* m_out, int B, int T, int R,
-                                  float* scratch, __nv_bfloat16* read_bf, cudaStream_t stream);
+                                  float* scratch, __nv_bfloat16* read_bf, cudaStream_t stream,
+                                  const float* factors = nullptr);
 // floats of scratch the time-parallel ROSA scan needs (0 if it does not apply)
 size_t rosa_parallel_scratch_floats(int B, int T, int R);
+// a layer's time-parallel ROSA constants (coefficients, A^K or its low-rank
+// factors): floats, and the launches that build them from the raw parameters
+size_t rosa_factor_floats(int R);
+yuf_status_t rosa_prepare_factors(const float* decay, const float* dir, int raw, int R, float* out,
+                                  cudaStream_t s);
 bool rosa_parallel_applies(int B, int T, int R);
 
 }  // namespace yuf

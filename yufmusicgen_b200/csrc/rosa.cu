@@ -35,7 +35,7 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
                            const float* bias_c, const float* bias_w, const float* bias_g, int ld,
                            const float* decay, const float* dir, int raw, const float* m0,
                            float* read, float* m_out, int B, int T, int R, bool gated,
-                           float* scratch, cudaStream_t s);
+                           float* scratch, cudaStream_t s, const float* factors = nullptr);
 
 // Per-layer constants of the scan for channel j of a block of `nwarps` warps:
 // the unit direction d_j and post-sigmoid decay dec_j (from the raw parameters
@@ -414,13 +414,14 @@ static yuf_status_t rosa_engine_scan(const float* cand, const float* write, cons
                                      const float* bias_c, const float* bias_w, const float* bias_g,
                                      int ld, const float* decay_raw, const float* dir_raw,
                                      const float* m0, float* read, float* m_out, int B, int T, int R,
-                                     float* scratch, cudaStream_t stream);
+                                     float* scratch, const float* factors, cudaStream_t stream);
 
 yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const float* gate,
                                   const float* bias_c, const float* bias_w, const float* bias_g,
                                   int ld, const float* decay_raw, const float* dir_raw,
                                   const float* m0, float* read, float* m_out, int B, int T, int R,
-                                  float* scratch, __nv_bfloat16* read_bf, cudaStream_t stream) {
+                                  float* scratch, __nv_bfloat16* read_bf, cudaStream_t stream,
+                                  const float* factors) {
   if (T == 1 && R <= 1024) {
     launch_k(rosa_step_kernel<true>, dim3(B), dim3(((R + 31) / 32) * 32), 0, stream, 
         cand, write, gate, decay_raw, dir_raw, m0, read, m_out, R, ld, bias_c, bias_w, bias_g, 1,
@@ -428,7 +429,7 @@ yuf_status_t rosa_engine_dispatch(const float* cand, const float* write, const f
     return check_launch("rosa_step_kernel");
   }
   yuf_status_t st = rosa_engine_scan(cand, write, gate, bias_c, bias_w, bias_g, ld, decay_raw, dir_raw,
-                                     m0, read, m_out, B, T, R, scratch, stream);
+                                     m0, read, m_out, B, T, R, scratch, factors, stream);
   if (st == YUF_OK && read_bf) {
     launch_to_bf16(read, read_bf, (size_t)B * T * R, stream);
     return check_launch("to_bf16_kernel");
@@ -442,10 +443,10 @@ static yuf_status_t rosa_engine_scan(const float* cand, const float* write, cons
                                      const float* bias_c, const float* bias_w, const float* bias_g,
                                      int ld, const float* decay_raw, const float* dir_raw,
                                      const float* m0, float* read, float* m_out, int B, int T, int R,
-                                     float* scratch, cudaStream_t stream) {
+                                     float* scratch, const float* factors, cudaStream_t stream) {
   if (scratch && rosa_parallel_applies(B, T, R))
     return rosa_parallel(cand, write, gate, bias_c, bias_w, bias_g, ld, decay_raw, dir_raw, 1, m0,
-                         read, m_out, B, T, R, true, scratch, stream);
+                         read, m_out, B, T, R, true, scratch, stream, factors);
   const int threads = ((R + 31) / 32) * 32;
   if (threads <= 256)
     rosa_scan_kernel<true, false, 256><<<B, threads, 0, stream>>>(
@@ -803,26 +804,69 @@ bool rosa_parallel_applies(int B, int T, int R) {
   return R <= 256 && T % K == 0 && T >= 4 * K && (long long)B * (T / K) >= 16;
 }
 
+size_t rosa_factor_floats(int R) {
+  const size_t K = rosa_par_k(R);
+  return ROSA_COEF_D + 2 * (size_t)R + (R <= 128 ? (size_t)R * R : 2 * K * R + R);
+}
+
+// The layer constants of the time-parallel scan, from the raw parameters
+// (raw != 0: decay = sigmoid(param), direction = normalize(householder)) or
+// the post-activation ones: the coefficient block [q | d | decay]
+// (ROSA_COEF_D + 2R floats), then A^K transposed (R <= 128) or the factors
+// W^T [K][R], M^T [R][K] and D^K [R] of its low-rank form.  They depend on the
+// layer's parameters only, so the engine builds them once per layer.
+yuf_status_t rosa_prepare_factors(const float* decay, const float* dir, int raw, int R, float* out,
+                                  cudaStream_t s) {
+  if (R < 1 || R > 256) {
+    set_error("rosa: time-parallel factors need 1 <= R <= 256 (R = %d)", R);
+    return YUF_ERR_UNSUPPORTED;
+  }
+  const int K = rosa_par_k(R);
+  float* coef = out;
+  float* ak = out + ROSA_COEF_D + 2 * R;
+  const int threads = ((R + 31) / 32) * 32;
+  rosa_coef_kernel<<<1, threads, 0, s>>>(decay, dir, raw, R, coef);
+  if (R <= 128) {
+    // A^K from R unit vectors (inputs unused in MODE 2)
+    launch_mode<false, 2>(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, R, decay, dir, raw, nullptr,
+                          nullptr, ak, R, K, R, coef, s);
+  } else {
+    rosa_lowrank_kernel<<<1, threads, 0, s>>>(decay, dir, raw, ak, ak + (size_t)K * R, ak + 2 * (size_t)K * R, K,
+                                              R);
+  }
+  return check_launch("rosa factors");
+}
+
 // The caller guarantees rosa_parallel_applies(); scratch holds
-// rosa_parallel_scratch_floats() floats.
+// rosa_parallel_scratch_floats() floats.  factors (nullable): the layer's
+// rosa_prepare_factors() output for these parameters, which then are not
+// rebuilt here.
 yuf_status_t rosa_parallel(const float* cand, const float* write, const float* gate,
                            const float* bias_c, const float* bias_w, const float* bias_g, int ld,
                            const float* decay, const float* dir, int raw, const float* m0,
                            float* read, float* m_out, int B, int T, int R, bool gated,
-                           float* scratch, cudaStream_t s) {
+                           float* scratch, cudaStream_t s, const float* factors) {
   const int K = rosa_par_k(R);
   const int C = T / K;
-  float* AKt = scratch;
-  float* z = AKt + (size_t)R * R;
+  float* AKt_s = scratch;
+  float* z = AKt_s + (size_t)R * R;
   float* m_start = z + (size_t)B * C * R;
-  float* coef = m_start + (size_t)B * C * R;  // q, d, dec of this layer
+  float* coef_s = m_start + (size_t)B * C * R;  // q, d, dec of this layer
+  if (!factors) {
+    // build the layer constants into the scratch: coefficient block, then A^K
+    // (or its low-rank factors) where the scratch keeps A^K
+    const int threads = ((R + 31) / 32) * 32;
+    rosa_coef_kernel<<<1, threads, 0, s>>>(decay, dir, raw, R, coef_s);
+    if (R <= 128)
+      launch_mode<false, 2>(cand, write, gate, nullptr, nullptr, nullptr, ld, decay, dir, raw, nullptr,
+                            nullptr, AKt_s, R, K, R, coef_s, s);
+    else
+      rosa_lowrank_kernel<<<1, threads, 0, s>>>(decay, dir, raw, AKt_s, AKt_s + (size_t)K * R,
+                                                AKt_s + 2 * (size_t)K * R, K, R);
+  }
+  const float* coef = factors ? factors : coef_s;
+  const float* AKt = factors ? factors + ROSA_COEF_D + 2 * R : AKt_s;
   const int threads = ((R + 31) / 32) * 32;
-  rosa_coef_kernel<<<1, threads, 0, s>>>(decay, dir, raw, R, coef);
-  // 1. A^K from R unit vectors (inputs unused in MODE 2); its low-rank form
-  //    for R > 128 is built in step 3
-  if (R <= 128)
-    launch_mode<false, 2>(cand, write, gate, nullptr, nullptr, nullptr, ld, decay, dir, raw, nullptr,
-                          nullptr, AKt, R, K, R, coef, s);
   // 2. chunk end states from zero: chunks are the batch, K tokens each
   launch_mode<false, 1>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, nullptr,
                         nullptr, z, B * C, K, R, coef, s);
@@ -842,10 +886,9 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
     }
     rosa_carry_kernel<<<B, threads, sm, s>>>(AKt, z, m0, m_start, m_out, C, R);
   } else {
-    float* Wt = AKt;                   // [K][R]
-    float* Mt = Wt + (size_t)K * R;    // [R][K]
-    float* DK = Mt + (size_t)R * K;    // [R]
-    rosa_lowrank_kernel<<<1, threads, 0, s>>>(decay, dir, raw, Wt, Mt, DK, K, R);
+    const float* Wt = AKt;                   // [K][R]
+    const float* Mt = Wt + (size_t)K * R;    // [R][K]
+    const float* DK = Mt + (size_t)R * K;    // [R]
     if (R == 256 && K == 64) {
       rosa_carry_lowrank_reg_kernel<<<B, 256, 0, s>>>(Wt, Mt, DK, z, m0, m_start, m_out, C);
     } else {
