@@ -301,22 +301,26 @@ def test_benchmark_size_prefill_bf16_weights_per_layer(golden, fixture, cfgd, se
     eng.close()
 
 
-@pytest.mark.parametrize("cfgd,precision,T", [
-    (C.BASE_0P1B, "fp32", 256),
-    (C.BASE_0P1B, "fp32", 300),
-    (C.BASE_0P1B, "bf16", 256),
-    (dict(C.LONG_1K, n_layers=2), "fp32", 256),
+@pytest.mark.parametrize("cfgd,precision,B,T", [
+    (C.BASE_0P1B, "fp32", 8, 256),
+    (C.BASE_0P1B, "fp32", 8, 300),
+    (C.BASE_0P1B, "bf16", 8, 256),
+    (dict(C.LONG_1K, n_layers=2), "fp32", 8, 256),
+    (C.BASE_0P1B, "fp32", 2, 1024),
+    (C.BASE_0P1B, "bf16", 2, 1024),
+    (dict(C.LONG_1K, n_layers=2), "fp32", 2, 512),
 ])
-def test_chunked_prefill_with_the_time_mix_folded_in_matches_the_separate_epilogue(cfgd, precision, T):
-    """B*H = 128, T >= 256 (T = 300: a ragged last chunk): the prefill takes the chunked tensor-core WKV scan with
-    the time-mix epilogue folded into its prep (and the output norm applying
-    sigmoid to the gate's pre-activation).  Debug runs keep timemix_post in front
-    of the same scan; every position's logits and the next decode step agree
-    (fp32: 1e-4 abs + 1e-4 rel, the two differ only in the order of the |kk|
-    sums; bf16 weights: the stated bf16 tolerance)."""
+def test_prefill_with_the_time_mix_folded_in_matches_the_separate_epilogue(cfgd, precision, B, T):
+    """B*H = 128, T >= 256 (T = 300: a ragged last chunk): the prefill takes the
+    chunked tensor-core WKV scan with the time-mix epilogue folded into its prep;
+    B*H = 32: the time-parallel scan with it folded into its first pass (both
+    with the output norm applying sigmoid to the gate's pre-activation).  Debug
+    runs keep timemix_post in front of the same scans; every position's logits
+    and the next decode step agree (fp32: 1e-4 abs + 1e-4 rel, the two differ
+    only in the order of the |kk| sums; bf16 weights: the stated bf16 tolerance)."""
     cfg, w, eng = make(cfgd, 3, "perturbed", precision=precision, n_slots=8)
-    ids = torch.as_tensor(zipf_ids(8, T, seed=5, vocab=cfg.vocab_size), dtype=torch.int32, device="cuda")
-    nxt = torch.as_tensor(zipf_ids(8, 1, seed=6, vocab=cfg.vocab_size), dtype=torch.int32, device="cuda")
+    ids = torch.as_tensor(zipf_ids(B, T, seed=5, vocab=cfg.vocab_size), dtype=torch.int32, device="cuda")
+    nxt = torch.as_tensor(zipf_ids(B, 1, seed=6, vocab=cfg.vocab_size), dtype=torch.int32, device="cuda")
     outs = []
     for debug in (False, True):
         eng.reset_state()

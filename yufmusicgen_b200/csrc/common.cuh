@@ -81,6 +81,15 @@ inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
 }
 }  // namespace yuf
 
+// The time-mix epilogue's per-channel parameters of one layer ([H * N] each),
+// for the WKV kernels that fold it in: w = w0 + lw, kk = normalize(k * k_k),
+// alpha = sigmoid(a0 + la), a = -kk, b = kk * alpha, k' = k * (1 + (alpha - 1) * k_a).
+namespace yuf {
+struct WkvTm {
+  const float *w0, *a0, *k_k, *k_a;
+};
+}  // namespace yuf
+
 // Host-side error reporting shared by every C-ABI entry point.
 namespace yuf {
 void set_error(const char* fmt, ...);

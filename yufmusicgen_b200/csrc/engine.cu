@@ -396,10 +396,10 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
       Y_CUDA(cudaEventRecord(m->ev_join, m->side));
       Y_CUDA(cudaStreamWaitEvent(s, m->ev_join, 0));
     }
-    // The decode step and the chunked tensor-core prefill scan fold the time-mix
-    // epilogue into the WKV kernel (no separate pass over the projections'
-    // outputs); the prefill scan leaves the output gate to the output norm,
-    // which takes sigmoid(lg) itself.  Debug runs keep the epilogue separate, so
+    // The decode step and the prefill scans (chunked tensor-core, and the first
+    // pass of the time-parallel one) fold the time-mix epilogue into the WKV
+    // kernel (no separate pass over the projections' outputs); a prefill leaves
+    // the output gate to the output norm, which takes sigmoid(lg) itself.  Debug runs keep the epilogue separate, so
     // that its outputs can be dumped.
     yuf_status_t tm_st = YUF_ERR_UNSUPPORTED;
     const float* out_gate = w.g;
@@ -411,10 +411,14 @@ static yuf_status_t forward(yuf_model* m, const int32_t* ids, int B, int T, int 
       } else if (wkv7_chunk_tc_applies(B, T, H, N)) {
         tm_st = wkv7_chunk_tc_tm(w.rkv, w.rkv + RD, w.rkv + 2 * RD, w.lr2, w.lr2 + RD, Lw.w0, Lw.a0, Lw.k_k,
                                  Lw.k_a, S, w.y, S, B, T, H, N, s);
-        if (tm_st != YUF_ERR_UNSUPPORTED) {
-          out_gate = w.lr2 + 2 * RD;
-          out_gate_sig = true;
-        }
+      } else if (wkv7_parallel_applies(B, T, H, N)) {
+        const WkvTm prm{Lw.w0, Lw.a0, Lw.k_k, Lw.k_a};
+        tm_st = wkv7_parallel(w.rkv, w.lr2, w.rkv + RD, w.rkv + 2 * RD, w.lr2 + RD, w.lr2 + RD, S, w.y, S, B, T,
+                              H, N, w.scan + scan_rosa_floats(m, rows), s, false, &prm);
+      }
+      if (T > 1 && tm_st != YUF_ERR_UNSUPPORTED) {
+        out_gate = w.lr2 + 2 * RD;
+        out_gate_sig = true;
       }
     }
     if (tm_st != YUF_ERR_UNSUPPORTED) {

@@ -77,10 +77,13 @@ namespace yuf {
 bool wkv7_parallel_applies(int B, int T, int H, int N);
 size_t wkv7_parallel_scratch_floats(int B, int T, int H, int N);
 size_t wkv7_parallel_scratch_bound(size_t rows, int H, int N);
+// tm (nullable): the time-mix epilogue folded into the first pass -- r, lw, k,
+// v, la as the projections left them in place of r, w, k, v, a (b unused);
+// YUF_ERR_UNSUPPORTED (nothing launched) for head sizes above 64.
 yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
                            int B, int T, int H, int N, float* scratch, cudaStream_t st,
-                           bool tc_correct = false);
+                           bool tc_correct = false, const WkvTm* tm = nullptr);
 // Chunked WKV-7 prefill on the tensor cores (wkv7_chunk_tc.cu): one CTA per
 // (sequence, head), no scratch; N in {16, 32, 40, 48, 64}.
 bool wkv7_chunk_tc_supports(int N);

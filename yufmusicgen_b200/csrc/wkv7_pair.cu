@@ -275,10 +275,13 @@ struct PairWCfg {
   static constexpr int PAD = RAW + 6 * TS * N;    // [4][TS][VP] scaled a, b, k, r in lane layout
   static constexpr int GEND = PAD + 4 * TS * VP;  // [VP] gamma at the group end
   static constexpr int VV = GEND + VP;            // [TS][N] values
-  static constexpr int MBAR = (VV + TS * N + 1) / 2 * 2;  // one 8-byte mbarrier
+  static constexpr int PRM = VV + TS * N;         // [4][N] the head's w0, a0, k_k, k_a (time-mix folded in)
+  static constexpr int NRM = PRM + 4 * N;         // [TS] 1 / |k k_k| per token (time-mix folded in)
+  static constexpr int MBAR = (NRM + TS + 1) / 2 * 2;  // one 8-byte mbarrier
   static constexpr int TOTAL = MBAR + 2;
   static constexpr size_t BYTES = (size_t)TOTAL * sizeof(float);
   static constexpr uint32_t TX_BYTES = 6u * TS * N * sizeof(float);  // six full boxes per group
+  static constexpr uint32_t TX_BYTES_TM = 5u * TS * N * sizeof(float);  // time-mix folded in: no b box
   static_assert(N % 8 == 0 && C % 2 == 0 && N <= 64 && NW * 8 * R == N,
                 "warp pair kernel: N in {16, 32, 40, 48, 64}");
   static_assert((TS * N * sizeof(float)) % 128 == 0, "TMA boxes land on 128-byte boundaries");
@@ -313,14 +316,18 @@ YUF_DEVICE void load_cols(float2 (&dst)[C / 2], const float* p) {
 #ifndef YUF_PAIRW_MINB
 #define YUF_PAIRW_MINB 1  // minimum resident blocks per SM the register budget is set for
 #endif
-template <int N>
+// TM: the time-mix epilogue folded in (WkvTm): the boxes are r, the w and a
+// low-rank outputs, k and v as the projections left them, and the scaled
+// vectors are formed from them (timemix_post_kernel's arithmetic) with the
+// head's 1 / |k k_k| per token from a first pass over the group.
+template <int N, bool TM = false>
 __global__ void __launch_bounds__(PairWCfg<N>::NT, YUF_PAIRW_MINB)
     wkv7_pairw_kernel(const float* __restrict__ r, const float* __restrict__ w,
                       const float* __restrict__ k, const float* __restrict__ v,
                       const float* __restrict__ a, const float* __restrict__ b,
                       float* __restrict__ y, float* __restrict__ Q, float* __restrict__ U_out,
                       float* __restrict__ P_out, int K_, int H, int Tstride, int Cper,
-                      const __grid_constant__ PairTmaps tm) {
+                      const __grid_constant__ PairTmaps tm, const WkvTm prm) {
   using K = PairWCfg<N>;
   constexpr int R = K::R, C = K::C, C2 = K::C2, CS = K::CS, VP = K::VP, TS = K::TS;
   constexpr int RH = (R + 1) / 2;  // outputs kept by the even lane of a pair after reduce-scatter
@@ -353,10 +360,10 @@ __global__ void __launch_bounds__(PairWCfg<N>::NT, YUF_PAIRW_MINB)
   // TMA coordinates of this item's first token: column hh*N, row s*Tstride + c*K
   const int tx = hh * N;
   const int ty = (bb / Cper) * Tstride + (bb % Cper) * K_;
-  auto stage = [&](int t0) {  // one thread: the six 8-token boxes of a group
-    mbar_expect_tx(bar, K::TX_BYTES);
+  auto stage = [&](int t0) {  // one thread: the six (TM: five) 8-token boxes of a group
+    mbar_expect_tx(bar, TM ? K::TX_BYTES_TM : K::TX_BYTES);
 #pragma unroll
-    for (int arr = 0; arr < 6; ++arr)
+    for (int arr = 0; arr < (TM ? 5 : 6); ++arr)
       tma_load_2d(sm + K::RAW + arr * TS * N, &tm.m[arr], bar, tx, ty + t0);
   };
 
@@ -364,6 +371,13 @@ __global__ void __launch_bounds__(PairWCfg<N>::NT, YUF_PAIRW_MINB)
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
+  }
+  if constexpr (TM) {  // the head's parameters (weights: no kernel of the chain writes them)
+    for (int i = tid; i < 4 * N; i += NT) {
+      const int which = i / N, jj = i - which * N;
+      const float* src = which == 0 ? prm.w0 : (which == 1 ? prm.a0 : (which == 2 ? prm.k_k : prm.k_a));
+      sm[K::PRM + i] = src[hh * N + jj];
+    }
   }
   block_sync<K::NW>();
   if (tid == 0 && ngroups > 0) stage(0);
@@ -392,18 +406,54 @@ __global__ void __launch_bounds__(PairWCfg<N>::NT, YUF_PAIRW_MINB)
       }
       return;
     }
+    if constexpr (TM) {  // 1 / |k k_k| of each token: warp 0, four lanes a token
+      if (wp == 0) {
+        const int t = lane >> 2, q4 = lane & 3;
+        float ss = 0.f;
+        if (t < Tc) {
+          for (int jj = q4 * (N / 4); jj < (q4 + 1) * (N / 4); ++jj) {
+            const float kk = sm[K::RAW + 2 * TS * N + t * N + jj] * sm[K::PRM + 2 * N + jj];
+            ss = fmaf(kk, kk, ss);
+          }
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        if (q4 == 0) sm[K::NRM + t] = 1.f / fmaxf(sqrtf(ss), 1e-12f);  // F.normalize eps (model.py:116)
+      }
+      block_sync<K::NW>();
+    }
     // scaled vectors: a thread per column pair, running gamma over the group's tokens
     if (tid < N / 2) {
       const int j = 2 * tid;
       const int pj = (j / C) * CS + (j % C);  // lane-layout offset of the pair
       float2 gam = make_float2(1.f, 1.f), ginv = gam;
+      float2 pw0, pa0, pkk, pka;
+      if constexpr (TM) {
+        pw0 = *reinterpret_cast<const float2*>(sm + K::PRM + j);
+        pa0 = *reinterpret_cast<const float2*>(sm + K::PRM + N + j);
+        pkk = *reinterpret_cast<const float2*>(sm + K::PRM + 2 * N + j);
+        pka = *reinterpret_cast<const float2*>(sm + K::PRM + 3 * N + j);
+      }
       for (int t = 0; t < Tc; ++t) {
         const int rj = t * N + j;
-        const float2 wr = *reinterpret_cast<const float2*>(sm + K::RAW + 1 * TS * N + rj);
+        float2 wr = *reinterpret_cast<const float2*>(sm + K::RAW + 1 * TS * N + rj);
+        if constexpr (TM) wr = make_float2(pw0.x + wr.x, pw0.y + wr.y);
         const float sx = W_SCALE * sigmoidf_fast(wr.x), sy = W_SCALE * sigmoidf_fast(wr.y);
-        const float2 av = *reinterpret_cast<const float2*>(sm + K::RAW + 4 * TS * N + rj);
-        const float2 bv = *reinterpret_cast<const float2*>(sm + K::RAW + 5 * TS * N + rj);
-        const float2 kv = *reinterpret_cast<const float2*>(sm + K::RAW + 2 * TS * N + rj);
+        float2 av, bv, kv;
+        if constexpr (TM) {
+          const float2 kr = *reinterpret_cast<const float2*>(sm + K::RAW + 2 * TS * N + rj);
+          const float2 la = *reinterpret_cast<const float2*>(sm + K::RAW + 4 * TS * N + rj);
+          const float inv = sm[K::NRM + t];
+          const float kkx = kr.x * pkk.x * inv, kky = kr.y * pkk.y * inv;
+          const float alx = sigmoidf_fast(pa0.x + la.x), aly = sigmoidf_fast(pa0.y + la.y);
+          av = make_float2(-kkx, -kky);
+          bv = make_float2(kkx * alx, kky * aly);
+          kv = make_float2(kr.x * (1.f + (alx - 1.f) * pka.x), kr.y * (1.f + (aly - 1.f) * pka.y));
+        } else {
+          av = *reinterpret_cast<const float2*>(sm + K::RAW + 4 * TS * N + rj);
+          bv = *reinterpret_cast<const float2*>(sm + K::RAW + 5 * TS * N + rj);
+          kv = *reinterpret_cast<const float2*>(sm + K::RAW + 2 * TS * N + rj);
+        }
         const float2 rv = *reinterpret_cast<const float2*>(sm + K::RAW + 0 * TS * N + rj);
         float* d = sm + K::PAD + t * VP + pj;
         *reinterpret_cast<float2*>(d + 0 * TS * VP) = fmul2(av, gam);  // gamma_{t-1} a_t
@@ -937,9 +987,14 @@ unsigned int wkv7_pair_wait_timeouts() {
   return n;
 }
 
+// prm (nullable): the time-mix epilogue folded in (r, lw, k, v, la as the
+// projections left them in place of r, w, k, v, a; b unused); head sizes up to
+// 64 only -- YUF_ERR_UNSUPPORTED above.
 yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, const float* v,
                                 const float* a, const float* b, float* y, float* Q, float* U, float* P,
-                                int items, int K, int H, int N, int Tstride, int Cper, cudaStream_t st) {
+                                int items, int K, int H, int N, int Tstride, int Cper, cudaStream_t st,
+                                const WkvTm* prm) {
+  if (prm && N > 64) return YUF_ERR_UNSUPPORTED;
   PairTmaps tm;
   if (N <= 64) {
     const float* const src[6] = {r, w, k, v, a, b};
@@ -950,7 +1005,7 @@ yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, 
 #define CASEW(NN)                                                                                \
   case NN: {                                                                                     \
     using Kc = PairWCfg<NN>;                                                                     \
-    auto kern = wkv7_pairw_kernel<NN>;                                                           \
+    auto kern = prm ? wkv7_pairw_kernel<NN, true> : wkv7_pairw_kernel<NN, false>;               \
     if (Kc::BYTES > 48 * 1024 &&                                                                 \
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Kc::BYTES) != \
             cudaSuccess) {                                                                       \
@@ -958,7 +1013,7 @@ yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, 
       return YUF_ERR_CUDA;                                                                       \
     }                                                                                            \
     kern<<<items * H, Kc::NT, Kc::BYTES, st>>>(r, w, k, v, a, b, y, Q, U, P, K, H, Tstride, Cper, \
-                                                tm);                                             \
+                                                tm, prm ? *prm : WkvTm{});                       \
     return check_launch("wkv7_pairw_kernel");                                                    \
   }
 #define CASE(NN)                                                                                 \

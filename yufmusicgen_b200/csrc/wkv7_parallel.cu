@@ -36,7 +36,8 @@ constexpr int WKV_PAR_CMAX = YUF_WKV_PAR_CMAX;  // the carry is sequential over 
 
 yuf_status_t wkv7_pair_dispatch(const float* r, const float* w, const float* k, const float* v,
                                 const float* a, const float* b, float* y, float* Q, float* U, float* P,
-                                int items, int K, int H, int N, int Tstride, int Cper, cudaStream_t st);
+                                int items, int K, int H, int N, int Tstride, int Cper, cudaStream_t st,
+                                const WkvTm* prm = nullptr);
 yuf_status_t wkv7_correct_dispatch(const float* S0, const float* Q, float* y, int items, int K, int H,
                                    int N, int Tstride, int Cper, bool skip_first, bool tc, cudaStream_t st);
 int wkv7_pair_slots(int N);
@@ -237,7 +238,8 @@ size_t wkv7_parallel_scratch_bound(size_t rows, int H, int N) {
 
 yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const float* v,
                            const float* a, const float* b, const float* s0, float* y, float* s_out,
-                           int B, int T, int H, int N, float* scratch, cudaStream_t st, bool tc_correct) {
+                           int B, int T, int H, int N, float* scratch, cudaStream_t st, bool tc_correct,
+                           const WkvTm* tm) {
   int C = 0, K = 0;
   wkv7_parallel_plan(B, T, H, N, &C, &K);
   const size_t per = (size_t)B * C * H * N * N;
@@ -246,7 +248,7 @@ yuf_status_t wkv7_parallel(const float* r, const float* w, const float* k, const
   float* S_start = P + per;
   float* Qm = S_start + per;  // [B*C, H, K, N]
   // 1. one pass: y from a zero start (into y), Q, U, P
-  yuf_status_t rc = wkv7_pair_dispatch(r, w, k, v, a, b, y, Qm, U, P, B * C, K, H, N, T, C, st);
+  yuf_status_t rc = wkv7_pair_dispatch(r, w, k, v, a, b, y, Qm, U, P, B * C, K, H, N, T, C, st, tm);
   if (rc != YUF_OK) return rc;
   // 2. chunk start states and the final state
   switch (N) {
