@@ -55,6 +55,7 @@ SHAPES = [  # (M, N, K, batch): engine projections at config 3 / 4 / 5 / 1 sizes
     (512, 128, 128, 3), (512, 512, 32, 1),
     (1, 64, 32, 1), (100, 100, 40, 1), (129, 200, 72, 2), (300, 1000, 1024, 1), (777, 96, 136, 3),
     (3000, 1300, 200, 3), (2048, 2048, 4096, 1),  # CTA-pair kernel with ragged edges; long K
+    (4096, 600, 256, 1),  # 160-column tiles, the last one 120 wide
 ]
 
 

@@ -10,7 +10,7 @@
 //   warp 0   one thread issues the TMA loads: per 64-wide K block the A box
 //            (128 x 64) and the W box (BN x 64), 128-byte swizzled, into a ring
 //            of shared-memory stages guarded by full/empty mbarriers;
-//   warp 1   allocates 2*BN TMEM columns (two accumulators), and one thread
+//   warp 1   allocates two accumulators of BN columns in TMEM, and one thread
 //            issues the kind::f16 UMMAs (M = 128, N = BN, K = 16; four per
 //            stage), committing each stage back to its empty barrier and each
 //            finished tile to the accumulator's full barrier;
@@ -55,13 +55,16 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;   // multiple of 1024
   static constexpr int STAGES = std::min(8, (192 * 1024) / STAGE);
-  static constexpr uint32_t TMEM_COLS = 2 * BN;     // two fp32 accumulators of BN columns
+  // two fp32 accumulators of BN columns, ACC columns apart (a power of two, so
+  // that each starts on an aligned column); TMEM_COLS a power of two as well
+  static constexpr uint32_t ACC = BN <= 64 ? 64 : (BN <= 128 ? 128 : 256);
+  static constexpr uint32_t TMEM_COLS = 2 * ACC;
   static constexpr int STG_BYTES = 4 * GEMM_STG_FLOATS * 4;  // the epilogue warps' staging
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = STAGES * STAGE + STG_BYTES + BAR_BYTES + 1024;  // + alignment slack
   static constexpr uint32_t IDESC = umma_idesc_bf16(BM, BN);
   static constexpr int THREADS = 192;
-  static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
+  static_assert(BN == 64 || BN == 128 || BN == 160 || BN == 256, "tile width");
   static_assert(STAGE % 1024 == 0, "stages stay 1024-byte aligned for the 128-byte swizzle");
   static_assert(2 * STAGES * 8 + 4 * 8 + 8 + 8 <= BAR_BYTES, "barrier block");
 };
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
       for (int t = blockIdx.x; t < total; t += gridDim.x) {
         if (!gemm_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after_sync();
-        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        const uint32_t d = tmem + (uint32_t)acc * G::ACC;
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!gemm_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
@@ -322,7 +325,7 @@ __global__ void __launch_bounds__(GemmCfg<BN>::THREADS, 1)
       if (!ok) break;
       tc_fence_after_sync();
       const int row0 = mt * G::BM + q * 32;
-      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)acc * G::ACC;
       gemm_epilogue_tile<BN, EPI>(p, tbase, z, row0, min(32, p.M - row0), nt, stg_all + q * GEMM_STG_FLOATS);
       tc_fence_before_sync();
       __syncwarp();
@@ -1334,8 +1337,8 @@ struct GemmPlan {
 static GemmPlan plan_persistent(const GemmArgs& g, const GemmParams& p, int sms) {
   const long long kblocks = (g.K + 63) / 64;
   GemmPlan best;
-  for (int bn : {256, 128, 64}) {
-    if (g.epi == GEMM_EPI_SWIGLU && (bn < 128 || g.N % bn != 0)) continue;
+  for (int bn : {256, 160, 128, 64}) {
+    if (g.epi == GEMM_EPI_SWIGLU && (bn == 160 || bn < 128 || g.N % bn != 0)) continue;
     const long long tiles = (long long)p.m_tiles * ((g.N + bn - 1) / bn) * g.batch;
     const long long rounds = (tiles + sms - 1) / sms;
     const double cost = (double)rounds * kblocks * (128 + bn);
@@ -1451,10 +1454,12 @@ yuf_status_t gemm_bf16(const GemmArgs& g, cudaStream_t s) {
   if (g.epi == GEMM_EPI_F32) {
     if (bn == 64) return launch_gemm<64, GEMM_EPI_F32>(g, p, s);
     if (bn == 128) return launch_gemm<128, GEMM_EPI_F32>(g, p, s);
+    if (bn == 160) return launch_gemm<160, GEMM_EPI_F32>(g, p, s);
     return launch_gemm<256, GEMM_EPI_F32>(g, p, s);
   }
   if (bn == 64) return launch_gemm<64, GEMM_EPI_BF16>(g, p, s);
   if (bn == 128) return launch_gemm<128, GEMM_EPI_BF16>(g, p, s);
+  if (bn == 160) return launch_gemm<160, GEMM_EPI_BF16>(g, p, s);
   return launch_gemm<256, GEMM_EPI_BF16>(g, p, s);
 }
 
