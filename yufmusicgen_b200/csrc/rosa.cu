@@ -804,17 +804,22 @@ bool rosa_parallel_applies(int B, int T, int R) {
   return R <= 256 && T % K == 0 && T >= 4 * K && (long long)B * (T / K) >= 16;
 }
 
+// chunks per group of the two-level carry (R <= 128)
+constexpr int ROSA_CARRY_G = 8;
+
 size_t rosa_factor_floats(int R) {
   const size_t K = rosa_par_k(R);
-  return ROSA_COEF_D + 2 * (size_t)R + (R <= 128 ? (size_t)R * R : 2 * K * R + R);
+  // R <= 128: A^K and A^(K G), both transposed
+  return ROSA_COEF_D + 2 * (size_t)R + (R <= 128 ? 2 * (size_t)R * R : 2 * K * R + R);
 }
 
 // The layer constants of the time-parallel scan, from the raw parameters
 // (raw != 0: decay = sigmoid(param), direction = normalize(householder)) or
 // the post-activation ones: the coefficient block [q | d | decay]
-// (ROSA_COEF_D + 2R floats), then A^K transposed (R <= 128) or the factors
-// W^T [K][R], M^T [R][K] and D^K [R] of its low-rank form.  They depend on the
-// layer's parameters only, so the engine builds them once per layer.
+// (ROSA_COEF_D + 2R floats), then A^K and A^(K G) transposed (R <= 128; the
+// second for the two-level carry) or the factors W^T [K][R], M^T [R][K] and
+// D^K [R] of A^K's low-rank form.  They depend on the layer's parameters only,
+// so the engine builds them once per layer.
 yuf_status_t rosa_prepare_factors(const float* decay, const float* dir, int raw, int R, float* out,
                                   cudaStream_t s) {
   if (R < 1 || R > 256) {
@@ -827,9 +832,11 @@ yuf_status_t rosa_prepare_factors(const float* decay, const float* dir, int raw,
   const int threads = ((R + 31) / 32) * 32;
   rosa_coef_kernel<<<1, threads, 0, s>>>(decay, dir, raw, R, coef);
   if (R <= 128) {
-    // A^K from R unit vectors (inputs unused in MODE 2)
+    // A^K and A^(K G) from R unit vectors (inputs unused in MODE 2)
     launch_mode<false, 2>(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, R, decay, dir, raw, nullptr,
                           nullptr, ak, R, K, R, coef, s);
+    launch_mode<false, 2>(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, R, decay, dir, raw, nullptr,
+                          nullptr, ak + (size_t)R * R, R, K * ROSA_CARRY_G, R, coef, s);
   } else {
     rosa_lowrank_kernel<<<1, threads, 0, s>>>(decay, dir, raw, ak, ak + (size_t)K * R, ak + 2 * (size_t)K * R, K,
                                               R);
@@ -871,7 +878,27 @@ yuf_status_t rosa_parallel(const float* cand, const float* write, const float* g
   launch_mode<false, 1>(cand, write, gate, bias_c, bias_w, bias_g, ld, decay, dir, raw, nullptr,
                         nullptr, z, B * C, K, R, coef, s);
   // 3. carry across chunks
-  if (R == 32 || R == 64 || R == 128) {
+  constexpr int G = ROSA_CARRY_G;
+  const int NG = C / G;
+  if ((R == 32 || R == 64 || R == 128) && factors && C % G == 0 && NG >= 4 &&
+      2LL * B * NG <= (long long)R) {
+    // Two levels, depth 2 G + C / G instead of C: (a) every group of G chunks
+    // from a zero state (its end state Zg), (b) per sequence the group start
+    // states M_g+1 = A^(K G) M_g + Zg, (c) every group again from its true start,
+    // writing the chunk start states.  Zg and M_g use the scratch's A^K area.
+    const float* AKGt = AKt + (size_t)R * R;
+    float* Zg = AKt_s;
+    float* Mg = Zg + (size_t)B * NG * R;
+    auto carry = [&](const float* A, const float* zz, const float* start, float* starts, float* end, int blocks,
+                     int steps) {
+      if (R == 32) rosa_carry_reg_kernel<32><<<blocks, 64, 0, s>>>(A, zz, start, starts, end, steps);
+      else if (R == 64) rosa_carry_reg_kernel<64><<<blocks, 128, 0, s>>>(A, zz, start, starts, end, steps);
+      else rosa_carry_reg_kernel<128><<<blocks, 256, 0, s>>>(A, zz, start, starts, end, steps);
+    };
+    carry(AKt, z, nullptr, m_start, Zg, B * NG, G);  // (a): the chunk starts written here are replaced in (c)
+    carry(AKGt, Zg, m0, Mg, m_out, B, NG);           // (b)
+    carry(AKt, z, Mg, m_start, nullptr, B * NG, G);  // (c)
+  } else if (R == 32 || R == 64 || R == 128) {
     if (R == 32) rosa_carry_reg_kernel<32><<<B, 64, 0, s>>>(AKt, z, m0, m_start, m_out, C);
     else if (R == 64) rosa_carry_reg_kernel<64><<<B, 128, 0, s>>>(AKt, z, m0, m_start, m_out, C);
     else rosa_carry_reg_kernel<128><<<B, 256, 0, s>>>(AKt, z, m0, m_start, m_out, C);
